@@ -1,0 +1,216 @@
+"""Model and engine configuration.
+
+``ModelConfig`` covers the decoder families the engine runs: Llama (SmolLM2),
+Qwen2 (qkv bias), Qwen3 (qk-norm) and Qwen3-MoE (softmax top-k router).  It is
+built from GGUF metadata the same way the reference derives its
+``model.Config`` (internal/model/config.go:374-605, internal/ggufload/gguf_config.go)
+or from one of the named presets used by the benchmarks.
+
+``EngineConfig`` is the single typed place for runtime knobs; every field can
+be overridden by a ``FAK_*`` environment variable (the reference scatters
+~100 such knobs across packages, e.g. FAK_CUDA_GRAPH, FAK_PAGED_KV_BLOCK_TOKENS,
+FAK_NATIVE_MAX_RUNNING, FAK_INKERNEL_RADIX_BUDGET).
+"""
+from __future__ import annotations
+
+import dataclasses
+import os
+from typing import Any
+
+
+@dataclasses.dataclass(frozen=True)
+class ModelConfig:
+    arch: str  # "llama" | "qwen2" | "qwen3" | "qwen3moe"
+    n_layers: int
+    d_model: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn_dim: int
+    vocab_size: int
+    rms_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    tie_embeddings: bool = False
+    qkv_bias: bool = False
+    qk_norm: bool = False
+    n_experts: int = 0
+    n_experts_used: int = 0
+    expert_ffn_dim: int = 0
+    norm_topk_prob: bool = True
+    max_context: int = 32768
+    bos_token_id: int = 1
+    eos_token_id: int = 2
+    name: str = ""
+
+    @property
+    def q_dim(self) -> int:
+        return self.n_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    @property
+    def gqa_group(self) -> int:
+        return self.n_heads // self.n_kv_heads
+
+    @property
+    def is_moe(self) -> bool:
+        return self.n_experts > 0
+
+    def validate(self) -> None:
+        if self.n_heads % self.n_kv_heads:
+            raise ValueError(f"n_heads {self.n_heads} not a multiple of n_kv_heads {self.n_kv_heads}")
+        if self.head_dim % 2:
+            raise ValueError("head_dim must be even for RoPE")
+        if self.is_moe and not (0 < self.n_experts_used <= self.n_experts):
+            raise ValueError("MoE config needs 0 < n_experts_used <= n_experts")
+
+    def param_count(self) -> int:
+        d, L = self.d_model, self.n_layers
+        attn = d * self.q_dim + 2 * d * self.kv_dim + self.q_dim * d
+        if self.is_moe:
+            ffn = self.n_experts * 3 * d * self.expert_ffn_dim + d * self.n_experts
+        else:
+            ffn = 3 * d * self.ffn_dim
+        emb = self.vocab_size * d * (1 if self.tie_embeddings else 2)
+        return L * (attn + ffn) + emb
+
+    def replace(self, **kw: Any) -> "ModelConfig":
+        return dataclasses.replace(self, **kw)
+
+
+PRESETS: dict[str, ModelConfig] = {
+    # SmolLM2-135M (HF config): 30 layers, 576 wide, 9/3 heads of 64, FFN 1536, tied, theta 1e4
+    "smollm2-135m": ModelConfig("llama", 30, 576, 9, 3, 64, 1536, 49152, 1e-5, 10000.0, tie_embeddings=True,
+                                max_context=8192, bos_token_id=1, eos_token_id=2, name="smollm2-135m"),
+    # Qwen2.5-7B: 28 layers, 3584 wide, 28/4 heads of 128, FFN 18944, qkv bias, theta 1e6
+    "qwen2.5-7b": ModelConfig("qwen2", 28, 3584, 28, 4, 128, 18944, 152064, 1e-6, 1e6, qkv_bias=True,
+                              max_context=32768, bos_token_id=151643, eos_token_id=151645, name="qwen2.5-7b"),
+    # Qwen2.5-32B: 64 layers, 5120 wide, 40/8 heads of 128, FFN 27648
+    "qwen2.5-32b": ModelConfig("qwen2", 64, 5120, 40, 8, 128, 27648, 152064, 1e-6, 1e6, qkv_bias=True,
+                               max_context=32768, bos_token_id=151643, eos_token_id=151645, name="qwen2.5-32b"),
+    # Qwen3-30B-A3B: 48 layers, 2048 wide, 32/4 heads of 128, 128 experts top-8, expert FFN 768, qk-norm
+    "qwen3-30b-a3b": ModelConfig("qwen3moe", 48, 2048, 32, 4, 128, 6144, 151936, 1e-6, 1e6, qk_norm=True,
+                                 n_experts=128, n_experts_used=8, expert_ffn_dim=768, norm_topk_prob=True,
+                                 max_context=32768, bos_token_id=151643, eos_token_id=151645,
+                                 name="qwen3-30b-a3b"),
+    # small shapes for tests (same structure, few layers)
+    "tiny-llama": ModelConfig("llama", 2, 256, 4, 2, 64, 512, 512, 1e-5, 10000.0, tie_embeddings=True,
+                              max_context=1024, name="tiny-llama"),
+    "tiny-qwen2": ModelConfig("qwen2", 2, 512, 8, 2, 64, 1024, 1024, 1e-6, 1e6, qkv_bias=True,
+                              max_context=2048, name="tiny-qwen2"),
+    "tiny-qwen3moe": ModelConfig("qwen3moe", 2, 512, 8, 2, 64, 1024, 1024, 1e-6, 1e6, qk_norm=True,
+                                 n_experts=8, n_experts_used=2, expert_ffn_dim=256, max_context=2048,
+                                 name="tiny-qwen3moe"),
+}
+
+
+def preset(name: str) -> ModelConfig:
+    try:
+        return PRESETS[name]
+    except KeyError as e:
+        raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}") from e
+
+
+def config_from_gguf_metadata(meta: dict[str, Any], tensor_shapes: dict[str, tuple[int, ...]] | None = None
+                              ) -> ModelConfig:
+    """Derive a ModelConfig from GGUF metadata (keys ``{arch}.*`` as written by llama.cpp)."""
+    arch = meta.get("general.architecture")
+    if arch not in ("llama", "qwen2", "qwen3", "qwen3moe", "mistral"):
+        raise ValueError(f"unsupported GGUF architecture {arch!r}")
+
+    def g(key: str, default: Any = None) -> Any:
+        return meta.get(f"{arch}.{key}", default)
+
+    d = int(g("embedding_length"))
+    nh = int(g("attention.head_count"))
+    nkv = int(g("attention.head_count_kv", nh))
+    hd = int(g("attention.key_length", d // nh))
+    vocab = g("vocab_size")
+    shapes = tensor_shapes or {}
+    if vocab is None:
+        toks = meta.get("tokenizer.ggml.tokens")
+        vocab = len(toks) if toks else shapes.get("token_embd.weight", (0,))[0]
+    tied = "output.weight" not in shapes if shapes else bool(meta.get("fak.tie_embeddings", False))
+    qkv_bias = "blk.0.attn_q.bias" in shapes if shapes else arch == "qwen2"
+    qk_norm = "blk.0.attn_q_norm.weight" in shapes if shapes else arch.startswith("qwen3")
+    n_exp = int(g("expert_count", 0) or 0)
+    cfg = ModelConfig(
+        arch="llama" if arch == "mistral" else arch,
+        n_layers=int(g("block_count")),
+        d_model=d,
+        n_heads=nh,
+        n_kv_heads=nkv,
+        head_dim=hd,
+        ffn_dim=int(g("feed_forward_length", 0) or 0),
+        vocab_size=int(vocab),
+        rms_eps=float(f"{float(g('attention.layer_norm_rms_epsilon', 1e-5)):.6g}"),
+        rope_theta=float(f"{float(g('rope.freq_base', 10000.0)):.7g}"),
+        tie_embeddings=tied,
+        qkv_bias=qkv_bias,
+        qk_norm=qk_norm,
+        n_experts=n_exp,
+        n_experts_used=int(g("expert_used_count", 0) or 0),
+        expert_ffn_dim=int(g("expert_feed_forward_length", 0) or 0),
+        norm_topk_prob=bool(g("expert_weights_norm", True)),
+        max_context=int(g("context_length", 4096)),
+        bos_token_id=int(meta.get("tokenizer.ggml.bos_token_id", 1)),
+        eos_token_id=int(meta.get("tokenizer.ggml.eos_token_id", 2)),
+        name=str(meta.get("general.name", "")),
+    )
+    cfg.validate()
+    return cfg
+
+
+def _env(name: str, default: Any, typ: type) -> Any:
+    v = os.environ.get(name)
+    if v is None or v == "":
+        return default
+    if typ is bool:
+        return v.lower() in ("1", "true", "yes", "on")
+    return typ(v)
+
+
+@dataclasses.dataclass
+class EngineConfig:
+    """Runtime knobs (each one overridable by the FAK_* variable named in ENV_KEYS)."""
+    page_size: int = 16                 # tokens per KV page
+    kv_pages: int = 0                   # 0: size from free memory * kv_mem_fraction
+    kv_mem_fraction: float = 0.5
+    max_batch: int = 64                 # max running decode lanes
+    max_prefill_tokens: int = 4096      # chunked-prefill chunk
+    cuda_graph: bool = True
+    graph_batch_buckets: tuple[int, ...] = (1, 2, 4, 8, 16, 32, 64)
+    radix_cache: bool = True
+    radix_budget_pages: int = 0         # 0: unlimited (evict only under KV pressure)
+    tp: int = 1
+    ep: int = 1
+    fused_collectives: bool = True      # in-kernel P2P collectives; False = NCCL baseline
+    prefill_bf16_weights: bool = True   # keep a bf16 copy of each quantized weight for prefill GEMMs
+    seed: int = 0
+
+    ENV_KEYS = {
+        "page_size": ("FAK_PAGED_KV_BLOCK_TOKENS", int),
+        "kv_pages": ("FAK_KV_PAGES", int),
+        "kv_mem_fraction": ("FAK_KV_MEM_FRACTION", float),
+        "max_batch": ("FAK_NATIVE_MAX_RUNNING", int),
+        "max_prefill_tokens": ("FAK_MAX_PREFILL_TOKENS", int),
+        "cuda_graph": ("FAK_CUDA_GRAPH", bool),
+        "radix_cache": ("FAK_INKERNEL_RADIX", bool),
+        "radix_budget_pages": ("FAK_INKERNEL_RADIX_BUDGET", int),
+        "tp": ("FAK_TENSOR_PARALLEL", int),
+        "ep": ("FAK_EXPERT_PARALLEL", int),
+        "fused_collectives": ("FAK_FUSED_COLLECTIVES", bool),
+        "prefill_bf16_weights": ("FAK_PREFILL_BF16", bool),
+        "seed": ("FAK_SEED", int),
+    }
+
+    @classmethod
+    def from_env(cls, **overrides: Any) -> "EngineConfig":
+        cfg = cls(**overrides)
+        for fname, (env, typ) in cls.ENV_KEYS.items():
+            if fname in overrides:
+                continue
+            setattr(cfg, fname, _env(env, getattr(cfg, fname), typ))
+        return cfg

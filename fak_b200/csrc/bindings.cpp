@@ -1,0 +1,43 @@
+// Python bindings for the sm_100a kernels (module fak_b200._C).
+#include <torch/extension.h>
+
+torch::Tensor quantize_blocks(torch::Tensor x, int64_t qtype);
+torch::Tensor dequantize_rows(torch::Tensor w, int64_t qtype, int64_t rows, int64_t cols, int64_t pitch,
+                              c10::ScalarType out_dtype);
+void quant_act(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx, torch::Tensor ds);
+void qgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, torch::Tensor qx, torch::Tensor ds,
+           int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi);
+void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                      torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
+                      c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
+                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace);
+void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                       torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
+                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out);
+void embed(torch::Tensor table, int64_t qtype, int64_t pitch, int64_t V, int64_t d, torch::Tensor ids,
+           c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> out_bf16,
+           c10::optional<torch::Tensor> err);
+void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Tensor cos_t, torch::Tensor sin_t,
+             int64_t H, int64_t Hkv, c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double eps,
+             c10::optional<torch::Tensor> q_f32, c10::optional<torch::Tensor> q_bf16, torch::Tensor k_cache,
+             torch::Tensor v_cache);
+void rmsnorm_bf16(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor y);
+void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out);
+void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias, int64_t epi,
+               c10::optional<torch::Tensor> err);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "fak_b200 sm_100a kernels";
+  m.def("quantize_blocks", &quantize_blocks);
+  m.def("dequantize_rows", &dequantize_rows);
+  m.def("quant_act", &quant_act);
+  m.def("qgemv", &qgemv);
+  m.def("decode_attention", &decode_attention);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("embed", &embed);
+  m.def("rope_kv", &rope_kv);
+  m.def("rmsnorm_bf16", &rmsnorm_bf16);
+  m.def("argmax_rows", &argmax_rows);
+  m.def("gemm_bf16", &gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"),
+        pybind11::arg("bias") = pybind11::none(), pybind11::arg("epi") = 0, pybind11::arg("err") = pybind11::none());
+}

@@ -1,0 +1,555 @@
+// Paged attention over the block KV cache.
+//
+// KV layout: k_cache / v_cache [num_pages, Hkv, PAGE=16, D] bf16 -- one (page, kv-head) is one
+// contiguous 16 x D tile, so a page streams with 16-byte async copies and its rows feed ldmatrix.
+// Pages are shared between sequences through the radix prefix cache, so every sequence reads
+// through its own block table.
+//
+// decode  (one query token per sequence): the query heads of one KV group are packed into the
+//         M=16 rows of an m16n8k16 MMA (GQA groups <= 16), 16 tokens of one page are the N side;
+//         the context is split across CTAs (flash-decode) and across the 4 warps of a CTA, with
+//         an online softmax per warp and a log-sum-exp merge at the end.  The final merge writes
+//         the output already quantized (int8 + per-32 scale/sum) for the o_proj GEMV.
+//         Reference: k_flash_attention (internal/compute/cuda_kernels.cu:701-759), one block per
+//         head over a contiguous f32 cache.
+// prefill (a chunk of new tokens per sequence, after their K/V were appended): FlashAttention-2
+//         style, 64 queries x one head per CTA, 64-token K/V tiles double-buffered in shared
+//         memory, causal mask against absolute positions so a chunk attends to the whole cached
+//         prefix plus itself.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include "mma.cuh"
+
+using namespace fak;
+
+namespace {
+
+constexpr int PAGE = 16;
+constexpr float NEG_INF = -INFINITY;
+
+FAK_DEV float quad_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  return v;
+}
+FAK_DEV float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  return v;
+}
+
+// quantize one 32-wide block held one value per lane; writes int8 codes and (scale, sum)
+FAK_DEV void warp_quant_store(float v, int8_t* qdst, float2* dsdst, int lane) {
+  float amax = warp_max(fabsf(v));
+  float s = warp_sum(v);
+  float d = amax / 127.f;
+  qdst[lane] = (int8_t)(d > 0.f ? rintf(v / d) : 0.f);
+  if (lane == 0) *dsdst = make_float2(d, s);
+}
+
+// =============================================================================================
+// decode
+// =============================================================================================
+template <int D>
+struct DecodeSmem {
+  __nv_bfloat16 k[4][2][PAGE][D + 8];
+  __nv_bfloat16 v[4][2][PAGE][D + 8];
+};
+
+template <int D>
+__global__ void __launch_bounds__(128)
+k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc,
+              const int* __restrict__ block_table, int bt_stride, const int* __restrict__ ctx_len, int H, int Hkv,
+              int n_split, int pages_per_split, float scale_log2, float* __restrict__ part_o,
+              float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
+              float2* __restrict__ ds) {
+  constexpr int KS = D / 16;   // k-steps over the head dim
+  constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  DecodeSmem<D>& sm = *reinterpret_cast<DecodeSmem<D>*>(smem_raw);
+
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int G = H / Hkv;
+  pdl_wait();
+  const int ctx = ctx_len[b];
+  const int n_pages = (ctx + PAGE - 1) / PAGE;
+  // pages per split follow the live context so every split gets an even share of the pages
+  const int pps = max(pages_per_split, (n_pages + n_split - 1) / n_split);
+  const int p_begin = split * pps;
+  const int p_end = min(n_pages, p_begin + pps);
+
+  // Q fragments (rows = query heads of this group, zero beyond G)
+  uint32_t qa[KS][4];
+  {
+    const int h0 = kvh * G + gq, h1 = kvh * G + gq + 8;
+    const float* q0 = q + ((int64_t)b * H + h0) * D;
+    const float* q1 = q + ((int64_t)b * H + h1) * D;
+    const bool v0 = gq < G, v1 = gq + 8 < G;
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+      int c = ks * 16 + 2 * tq;
+      float2 a0 = v0 ? *reinterpret_cast<const float2*>(q0 + c) : make_float2(0.f, 0.f);
+      float2 a1 = v1 ? *reinterpret_cast<const float2*>(q1 + c) : make_float2(0.f, 0.f);
+      float2 a2 = v0 ? *reinterpret_cast<const float2*>(q0 + c + 8) : make_float2(0.f, 0.f);
+      float2 a3 = v1 ? *reinterpret_cast<const float2*>(q1 + c + 8) : make_float2(0.f, 0.f);
+      qa[ks][0] = pack_bf16(a0.x, a0.y);
+      qa[ks][1] = pack_bf16(a1.x, a1.y);
+      qa[ks][2] = pack_bf16(a2.x, a2.y);
+      qa[ks][3] = pack_bf16(a3.x, a3.y);
+    }
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
+
+  const int* bt = block_table + (int64_t)b * bt_stride;
+  auto issue_page = [&](int p, int buf) {
+    const int pid = bt[p];
+    const __nv_bfloat16* ks = kc + ((int64_t)pid * Hkv + kvh) * PAGE * D;
+    const __nv_bfloat16* vs = vc + ((int64_t)pid * Hkv + kvh) * PAGE * D;
+    constexpr int CHUNKS = PAGE * D / 8;  // 16-byte chunks per tile
+#pragma unroll
+    for (int c = lane; c < CHUNKS; c += 32) {
+      int tok = c / (D / 8), part = c % (D / 8);
+      cp_async16(smem_u32(&sm.k[warp][buf][tok][part * 8]), ks + tok * D + part * 8);
+      cp_async16(smem_u32(&sm.v[warp][buf][tok][part * 8]), vs + tok * D + part * 8);
+    }
+    cp_async_commit();
+  };
+
+  int p = p_begin + warp;
+  int buf = 0;
+  if (p < p_end) issue_page(p, 0);
+  for (; p < p_end; p += 4) {
+    const int pn = p + 4;
+    if (pn < p_end) {
+      issue_page(pn, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    // S = Q K^T for 16 tokens
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int jj = mi >> 1, hh = mi & 1;
+#pragma unroll
+      for (int ks = 0; ks < KS; ks++) {
+        uint32_t r0, r1, r2, r3;
+        ldmatrix_x4(smem_u32(&sm.k[warp][buf][8 * jj + ri][16 * ks + 8 * hh]), r0, r1, r2, r3);
+        mma_bf16_16816(s[0], qa[ks], r0, r1);
+        mma_bf16_16816(s[1], qa[ks], r2, r3);
+      }
+    }
+    const int valid = min(PAGE, ctx - p * PAGE);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        int tok = 8 * j + 2 * tq + (e & 1);
+        s[j][e] = tok < valid ? s[j][e] * scale_log2 : NEG_INF;
+      }
+    }
+    float mx0 = quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1])));
+    float mx1 = quad_max(fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3])));
+    float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    float base0 = mn0 == NEG_INF ? 0.f : mn0, base1 = mn1 == NEG_INF ? 0.f : mn1;
+    float c0 = exp2f(m0 - base0), c1 = exp2f(m1 - base1);
+    m0 = mn0; m1 = mn1;
+    float pr[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      pr[j][0] = exp2f(s[j][0] - base0);
+      pr[j][1] = exp2f(s[j][1] - base0);
+      pr[j][2] = exp2f(s[j][2] - base1);
+      pr[j][3] = exp2f(s[j][3] - base1);
+    }
+    l0 = l0 * c0 + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
+    l1 = l1 * c1 + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
+#pragma unroll
+    for (int i = 0; i < NT; i++) {
+      o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1;
+    }
+    uint32_t pa[4] = {pack_bf16(pr[0][0], pr[0][1]), pack_bf16(pr[0][2], pr[0][3]), pack_bf16(pr[1][0], pr[1][1]),
+                      pack_bf16(pr[1][2], pr[1][3])};
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int tok = (mi & 1) * 8 + ri, dsel = (mi >> 1) * 8;
+#pragma unroll
+      for (int d = 0; d < NT; d += 2) {
+        uint32_t r0, r1, r2, r3;
+        ldmatrix_x4_trans(smem_u32(&sm.v[warp][buf][tok][8 * d + dsel]), r0, r1, r2, r3);
+        mma_bf16_16816(o[d], pa, r0, r1);
+        mma_bf16_16816(o[d + 1], pa, r2, r3);
+      }
+    }
+    __syncwarp();
+    buf ^= 1;
+  }
+  l0 = quad_sum(l0);
+  l1 = quad_sum(l1);
+
+  // merge the 4 warps through shared memory (reuses the K/V staging area)
+  __syncthreads();
+  float* so = reinterpret_cast<float*>(smem_raw);   // [4][16][D]
+  float* sml = so + 4 * 16 * D;                      // [4][16][2]
+#pragma unroll
+  for (int i = 0; i < NT; i++) {
+    int c = 8 * i + 2 * tq;
+    so[(warp * 16 + gq) * D + c] = o[i][0];
+    so[(warp * 16 + gq) * D + c + 1] = o[i][1];
+    so[(warp * 16 + gq + 8) * D + c] = o[i][2];
+    so[(warp * 16 + gq + 8) * D + c + 1] = o[i][3];
+  }
+  if (tq == 0) {
+    sml[(warp * 16 + gq) * 2] = m0;
+    sml[(warp * 16 + gq) * 2 + 1] = l0;
+    sml[(warp * 16 + gq + 8) * 2] = m1;
+    sml[(warp * 16 + gq + 8) * 2 + 1] = l1;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  // each warp finalizes dims [32*warp, 32*warp+32) (D=128) or warps 0-1 (D=64) for every head
+  for (int r = 0; r < G; r++) {
+    float mstar = NEG_INF;
+#pragma unroll
+    for (int w = 0; w < 4; w++) mstar = fmaxf(mstar, sml[(w * 16 + r) * 2]);
+    float base = mstar == NEG_INF ? 0.f : mstar;
+    float L = 0.f, f[4];
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      f[w] = exp2f(sml[(w * 16 + r) * 2] - base);
+      L += f[w] * sml[(w * 16 + r) * 2 + 1];
+    }
+    const int h = kvh * G + r;
+    for (int dd = threadIdx.x; dd < D; dd += 128) {
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; w++) acc += f[w] * so[(w * 16 + r) * D + dd];
+      if (n_split == 1) {
+        float v = L > 0.f ? acc / L : 0.f;
+        int64_t oi = ((int64_t)b * H + h) * D + dd;
+        if (out) out[oi] = v;
+        if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), lane);
+      } else {
+        int64_t pi = (((int64_t)b * H + h) * n_split + split);
+        part_o[pi * D + dd] = acc;
+        if (dd == 0) part_ml[pi] = make_float2(mstar, L);
+      }
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D)
+k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int H, int n_split,
+                 float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds) {
+  pdl_wait();
+  const int b = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
+  const int64_t base = ((int64_t)b * H + h) * n_split;
+  float mstar = NEG_INF;
+  for (int s = 0; s < n_split; s++) mstar = fmaxf(mstar, part_ml[base + s].x);
+  float mb = mstar == NEG_INF ? 0.f : mstar;
+  float L = 0.f, acc = 0.f;
+  for (int s = 0; s < n_split; s++) {
+    float2 ml = part_ml[base + s];
+    float f = exp2f(ml.x - mb);
+    L += f * ml.y;
+    acc += f * part_o[(base + s) * D + dd];
+  }
+  pdl_launch_dependents();
+  float v = L > 0.f ? acc / L : 0.f;
+  int64_t oi = ((int64_t)b * H + h) * D + dd;
+  if (out) out[oi] = v;
+  if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), dd & 31);
+}
+
+// =============================================================================================
+// prefill
+// =============================================================================================
+constexpr int PF_Q = 64;   // queries per CTA (4 warps x 16)
+constexpr int PF_KV = 64;  // keys per tile
+
+template <int D>
+struct PrefillSmem {
+  __nv_bfloat16 k[2][PF_KV][D + 8];
+  __nv_bfloat16 v[2][PF_KV][D + 8];
+};
+
+template <int D>
+__global__ void __launch_bounds__(128)
+k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv_bfloat16* __restrict__ kc,
+               const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_table, int bt_stride,
+               const int* __restrict__ tile_seq, const int* __restrict__ tile_q0, const int* __restrict__ seq_qoff,
+               const int* __restrict__ seq_qlen, const int* __restrict__ seq_pos0, int H, int Hkv, float scale_log2,
+               __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+  constexpr int KS = D / 16;
+  constexpr int NT = D / 8;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  PrefillSmem<D>& sm = *reinterpret_cast<PrefillSmem<D>*>(smem_raw);
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int G = H / Hkv, kvh = h / G;
+  pdl_wait();
+  const int sq = tile_seq[tile];
+  const int q0 = tile_q0[tile];
+  const int qoff = seq_qoff[sq], qlen = seq_qlen[sq], pos0 = seq_pos0[sq];
+  const int* bt = block_table + (int64_t)sq * bt_stride;
+
+  const int r0 = q0 + warp * 16 + gq, r1 = r0 + 8;  // local query indices of this thread's rows
+  const bool v0 = r0 < qlen, v1 = r1 < qlen;
+  uint32_t qa[KS][4];
+  {
+    const __nv_bfloat16* qp0 = q + (int64_t)(qoff + r0) * q_stride + (int64_t)h * D;
+    const __nv_bfloat16* qp1 = q + (int64_t)(qoff + r1) * q_stride + (int64_t)h * D;
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+      int c = ks * 16 + 2 * tq;
+      qa[ks][0] = v0 ? *reinterpret_cast<const uint32_t*>(qp0 + c) : 0u;
+      qa[ks][1] = v1 ? *reinterpret_cast<const uint32_t*>(qp1 + c) : 0u;
+      qa[ks][2] = v0 ? *reinterpret_cast<const uint32_t*>(qp0 + c + 8) : 0u;
+      qa[ks][3] = v1 ? *reinterpret_cast<const uint32_t*>(qp1 + c + 8) : 0u;
+    }
+  }
+  const int qpos0 = pos0 + r0, qpos1 = pos0 + r1;
+  const int kv_end = pos0 + min(q0 + PF_Q, qlen);  // exclusive bound on keys any row of this tile sees
+  const int n_kv_tiles = (kv_end + PF_KV - 1) / PF_KV;
+
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
+
+  auto issue_tile = [&](int kt, int buf) {
+    constexpr int CPR = D / 8;  // 16-byte chunks per token row
+    for (int c = threadIdx.x; c < PF_KV * CPR; c += 128) {
+      int tok = c / CPR, part = c % CPR;
+      int kp = kt * PF_KV + tok;
+      bool ok = kp < kv_end;
+      int pid = ok ? bt[kp / PAGE] : 0;
+      int64_t off = (((int64_t)pid * Hkv + kvh) * PAGE + (kp % PAGE)) * D + part * 8;
+      cp_async16_zfill(smem_u32(&sm.k[buf][tok][part * 8]), kc + (ok ? off : 0), ok);
+      cp_async16_zfill(smem_u32(&sm.v[buf][tok][part * 8]), vc + (ok ? off : 0), ok);
+    }
+    cp_async_commit();
+  };
+
+  if (n_kv_tiles > 0) issue_tile(0, 0);
+  for (int kt = 0; kt < n_kv_tiles; kt++) {
+    const int buf = kt & 1;
+    if (kt + 1 < n_kv_tiles) {
+      issue_tile(kt + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int jj = mi >> 1, hh = mi & 1;
+#pragma unroll
+      for (int ks = 0; ks < KS; ks++) {
+#pragma unroll
+        for (int jp = 0; jp < 4; jp++) {  // pairs of n-tiles (16 keys)
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(smem_u32(&sm.k[buf][16 * jp + 8 * jj + ri][16 * ks + 8 * hh]), b0, b1, b2, b3);
+          mma_bf16_16816(s[2 * jp], qa[ks], b0, b1);
+          mma_bf16_16816(s[2 * jp + 1], qa[ks], b2, b3);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        int kp = kt * PF_KV + 8 * j + 2 * tq + (e & 1);
+        int qp = (e < 2) ? qpos0 : qpos1;
+        s[j][e] = (kp <= qp && kp < kv_end) ? s[j][e] * scale_log2 : NEG_INF;
+      }
+    }
+    float mx0 = NEG_INF, mx1 = NEG_INF;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = quad_max(mx0);
+    mx1 = quad_max(mx1);
+    float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    float base0 = mn0 == NEG_INF ? 0.f : mn0, base1 = mn1 == NEG_INF ? 0.f : mn1;
+    float c0 = exp2f(m0 - base0), c1 = exp2f(m1 - base1);
+    m0 = mn0; m1 = mn1;
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      s[j][0] = exp2f(s[j][0] - base0);
+      s[j][1] = exp2f(s[j][1] - base0);
+      s[j][2] = exp2f(s[j][2] - base1);
+      s[j][3] = exp2f(s[j][3] - base1);
+      rs0 += s[j][0] + s[j][1];
+      rs1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * c0 + rs0;
+    l1 = l1 * c1 + rs1;
+#pragma unroll
+    for (int i = 0; i < NT; i++) {
+      o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1;
+    }
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int tsel = (mi & 1) * 8 + ri, dsel = (mi >> 1) * 8;
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        uint32_t pa[4] = {pack_bf16(s[2 * kk][0], s[2 * kk][1]), pack_bf16(s[2 * kk][2], s[2 * kk][3]),
+                          pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]), pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+#pragma unroll
+        for (int d = 0; d < NT; d += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(smem_u32(&sm.v[buf][16 * kk + tsel][8 * d + dsel]), b0, b1, b2, b3);
+          mma_bf16_16816(o[d], pa, b0, b1);
+          mma_bf16_16816(o[d + 1], pa, b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  pdl_launch_dependents();
+  l0 = quad_sum(l0);
+  l1 = quad_sum(l1);
+  float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  __nv_bfloat16* op0 = out + (int64_t)(qoff + r0) * out_stride + (int64_t)h * D;
+  __nv_bfloat16* op1 = out + (int64_t)(qoff + r1) * out_stride + (int64_t)h * D;
+#pragma unroll
+  for (int i = 0; i < NT; i++) {
+    int c = 8 * i + 2 * tq;
+    if (v0) *reinterpret_cast<uint32_t*>(op0 + c) = pack_bf16(o[i][0] * inv0, o[i][1] * inv0);
+    if (v1) *reinterpret_cast<uint32_t*>(op1 + c) = pack_bf16(o[i][2] * inv1, o[i][3] * inv1);
+  }
+}
+
+cudaLaunchAttribute g_pdl_attr[1];
+
+void set_pdl(cudaLaunchConfig_t& cfg) {
+  g_pdl_attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  g_pdl_attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = g_pdl_attr;
+  cfg.numAttrs = 1;
+}
+
+}  // namespace
+
+// q [B,H,D] f32; caches [P,Hkv,16,D] bf16; block_table [B, *] int32; ctx_len [B] int32.
+// Writes out [B,H*D] f32 (optional) and/or the int8 quantized output (qx [B,H*D], ds [B,H*D/32,2]).
+// workspace: f32 buffer of at least B*H*n_split*(D+2) floats when n_split > 1.
+void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                      torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
+                      c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
+                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
+  TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
+  TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(), "v_cache");
+  TORCH_CHECK(k_cache.size(2) == PAGE, "page size must be 16");
+  int B = (int)q.size(0), H = (int)q.size(1), D = (int)q.size(2), Hkv = (int)k_cache.size(1);
+  TORCH_CHECK(k_cache.size(3) == D && (D == 64 || D == 128), "head dim must be 64 or 128");
+  TORCH_CHECK(H % Hkv == 0 && H / Hkv <= 16, "GQA group must be <= 16");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && block_table.dim() == 2 && block_table.stride(1) == 1, "bt");
+  TORCH_CHECK(ctx_len.scalar_type() == torch::kInt32 && ctx_len.numel() >= B, "ctx_len");
+  TORCH_CHECK(n_split >= 1 && pages_per_split >= 1, "split");
+  if (B == 0) return;
+  float* op = out.has_value() ? out->data_ptr<float>() : nullptr;
+  int8_t* qp = qx.has_value() ? qx->data_ptr<int8_t>() : nullptr;
+  float2* dp = ds.has_value() ? reinterpret_cast<float2*>(ds->data_ptr<float>()) : nullptr;
+  if (qp) TORCH_CHECK(dp && qx->numel() >= (int64_t)B * H * D && ds->numel() >= (int64_t)B * H * D / 16, "qx/ds size");
+  if (op) TORCH_CHECK(out->numel() >= (int64_t)B * H * D && out->is_contiguous(), "out");
+  float* pw = nullptr;
+  if (n_split > 1) {
+    TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == torch::kFloat32 &&
+                    workspace->numel() >= (int64_t)B * H * n_split * (D + 2),
+                "decode_attention: workspace too small");
+    pw = workspace->data_ptr<float>();
+  }
+  float2* pml = pw ? reinterpret_cast<float2*>(pw + (int64_t)B * H * n_split * D) : nullptr;
+  float scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(Hkv, B, (unsigned)n_split);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  set_pdl(cfg);
+  int bts = (int)block_table.stride(0);
+  if (D == 128) {
+    size_t smem = std::max(sizeof(DecodeSmem<128>), (size_t)(4 * 16 * 128 + 4 * 16 * 2) * 4);
+    cfg.dynamicSmemBytes = smem;
+    FAK_CUDA_CHECK(cudaFuncSetAttribute(k_decode_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<128>, (const float*)q.data_ptr<float>(),
+                                      (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
+                                      (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp));
+  } else {
+    size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
+    cfg.dynamicSmemBytes = smem;
+    FAK_CUDA_CHECK(cudaFuncSetAttribute(k_decode_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<64>, (const float*)q.data_ptr<float>(),
+                                      (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
+                                      (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp));
+  }
+  if (n_split > 1) {
+    cudaLaunchConfig_t c2 = {};
+    c2.gridDim = dim3(B, H);
+    c2.blockDim = dim3(D);
+    c2.stream = stream;
+    set_pdl(c2);
+    if (D == 128)
+      FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H,
+                                        (int)n_split, op, qp, dp));
+    else
+      FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H,
+                                        (int)n_split, op, qp, dp));
+  }
+}
+
+// q [T,H,D] bf16 (row stride q_stride elements); out [T, H*D] bf16 (row stride out_stride).
+// Per-tile metadata (int32, device): tile_seq, tile_q0; per-sequence: seq_qoff, seq_qlen, seq_pos0.
+void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                       torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
+                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.stride(2) == 1, "q [T,H,D] bf16");
+  TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
+  int H = (int)q.size(1), D = (int)q.size(2), Hkv = (int)k_cache.size(1);
+  TORCH_CHECK(q.stride(1) == D, "q heads must be contiguous");
+  TORCH_CHECK(D == 64 || D == 128, "head dim must be 64 or 128");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "out [T,H*D] bf16");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && block_table.stride(1) == 1, "block_table");
+  if (n_tiles == 0) return;
+  float scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)n_tiles, H);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  set_pdl(cfg);
+  auto args = [&](auto kern, size_t smem) {
+    cfg.dynamicSmemBytes = smem;
+    FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(
+        &cfg, kern, (const __nv_bfloat16*)q.data_ptr(), (int64_t)q.stride(0), (const __nv_bfloat16*)k_cache.data_ptr(),
+        (const __nv_bfloat16*)v_cache.data_ptr(), (const int*)block_table.data_ptr<int>(), (int)block_table.stride(0),
+        (const int*)tile_seq.data_ptr<int>(), (const int*)tile_q0.data_ptr<int>(), (const int*)seq_qoff.data_ptr<int>(),
+        (const int*)seq_qlen.data_ptr<int>(), (const int*)seq_pos0.data_ptr<int>(), H, Hkv, scale_log2,
+        (__nv_bfloat16*)out.data_ptr(), (int64_t)out.stride(0)));
+  };
+  if (D == 128) args(k_prefill_attn<128>, sizeof(PrefillSmem<128>));
+  else args(k_prefill_attn<64>, sizeof(PrefillSmem<64>));
+}

@@ -1,0 +1,78 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define FAK_DEV __device__ __forceinline__
+
+namespace fak {
+
+constexpr int QK_K = 256;
+enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q8_0 = 8, QT_Q4_K = 12, QT_Q6_K = 14, QT_BF16 = 30 };
+
+FAK_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+FAK_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+FAK_DEV float half_bits_to_float(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Little-endian unaligned reads from byte pointers (weights keep GGML block layout).
+FAK_DEV uint16_t ld_u16(const uint8_t* p) { return (uint16_t)p[0] | ((uint16_t)p[1] << 8); }
+
+// Streaming global loads for weights: read-only path, do not pollute L1.
+FAK_DEV uint4 ldg_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+FAK_DEV uint32_t ldg_stream4(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+FAK_DEV uint2 ldg_stream8(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// independent prologue (weight prefetch) while this one drains, and wait for
+// the previous kernel's results only where they are first read.
+FAK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+FAK_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+FAK_DEV int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+FAK_DEV float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+FAK_DEV float bf16_bits_lo(uint32_t v) { return __uint_as_float(v << 16); }
+FAK_DEV float bf16_bits_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Device-side error word: kernels never trap; they record a code and return.
+// Codes: 1 = bounded wait expired, 2 = index out of range, 3 = bad argument.
+FAK_DEV void report_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+}  // namespace fak
+
+#define FAK_CUDA_CHECK(expr)                                                                  \
+  do {                                                                                        \
+    cudaError_t _e = (expr);                                                                  \
+    if (_e != cudaSuccess) {                                                                  \
+      throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(_e) + " at " + \
+                               __FILE__ + ":" + std::to_string(__LINE__));                    \
+    }                                                                                         \
+  } while (0)

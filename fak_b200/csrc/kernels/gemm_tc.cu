@@ -1,0 +1,234 @@
+// bf16 GEMM on the 5th-generation tensor cores: C[M, N] (op)= A[M, K] . B[N, K]^T (+ bias).
+//
+// A = activations (K-major), B = weights (K-major, the dequantized copy of a GGUF matrix).
+// One CTA computes a 128 x BN tile; warp roles:
+//   warp 0     TMA producer: 128 x 64 A box and BN x 64 B box per k-block (128-byte swizzle)
+//              into a STAGES-deep shared-memory ring, completion tracked by mbarriers;
+//   warp 1     allocates BN TMEM columns, then one thread issues tcgen05.mma (M=128, N=BN,
+//              K=16 per instruction, 4 per k-block) and tcgen05.commit frees each stage;
+//   warps 2-5  epilogue: tcgen05.ld the fp32 accumulator (warp w reads TMEM lanes
+//              32*(w%4)..+31 = tile rows), fused bias / residual add / SwiGLU, global store.
+// No TMA multicast is used, so the kernel is safe on multi-GPU runs.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cudaTypedefs.h>
+
+#include "tc.cuh"
+
+using namespace fak;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int GEMM_THREADS = 192;
+
+enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2 };
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  alignas(1024) __nv_bfloat16 a[STAGES][BM * BK];
+  alignas(1024) __nv_bfloat16 b[STAGES][BN * BK];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t accum_full;
+  uint32_t tmem_base;
+};
+
+template <typename OutT>
+FAK_DEV void store_val(OutT* p, float v);
+template <>
+FAK_DEV void store_val<float>(float* p, float v) { *p = v; }
+template <>
+FAK_DEV void store_val<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <int BN, int STAGES, typename OutT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M, int N,
+            int K, OutT* __restrict__ out, int64_t ldo, const float* __restrict__ bias, int epi, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  GemmSmem<BN, STAGES>& sm = *reinterpret_cast<GemmSmem<BN, STAGES>*>(base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const int nkb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      tc::mbar_init(&sm.full[s], 1);
+      tc::mbar_init(&sm.empty[s], 1);
+    }
+    tc::mbar_init(&sm.accum_full, 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmap_a);
+    tc::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sm.tmem_base, BN);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  // the A operand is produced by the previous kernel
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; kb++) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        tc::mbar_wait(&sm.empty[s], ph ^ 1, err);
+        tc::mbar_arrive_expect_tx(&sm.full[s], (BM + BN) * BK * 2);
+        tc::tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * BK, m0);
+        tc::tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * BK, n0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+      for (int kb = 0; kb < nkb; kb++) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        tc::mbar_wait(&sm.full[s], ph, err);
+        tc::tc_fence_after();
+        const uint64_t ad = tc::smem_desc_sw128(sm.a[s]);
+        const uint64_t bd = tc::smem_desc_sw128(sm.b[s]);
+#pragma unroll
+        for (int k = 0; k < BK / 16; k++) {
+          // advance 16 bf16 = 32 bytes along K inside the swizzle row (encoded >> 4)
+          tc::mma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        }
+        tc::mma_commit(&sm.empty[s]);
+      }
+      tc::mma_commit(&sm.accum_full);
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    tc::mbar_wait(&sm.accum_full, 0, err);
+    tc::tc_fence_after();
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tc::tmem_ld16(lane_addr + c, r);
+      tc::tmem_ld_wait();
+      if (row >= M) continue;
+      const int col0 = n0 + c;
+      if (epi == G_SWIGLU) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          int col = col0 + j;
+          if (col + 1 < N) {
+            float g = __uint_as_float(r[j]), u = __uint_as_float(r[j + 1]);
+            if (bias) { g += bias[col]; u += bias[col + 1]; }
+            store_val(out + (int64_t)row * ldo + (col >> 1), silu(g) * u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          int col = col0 + j;
+          if (col < N) {
+            float v = __uint_as_float(r[j]);
+            if (bias) v += bias[col];
+            OutT* p = out + (int64_t)row * ldo + col;
+            if (epi == G_ADD) v += (float)*p;
+            store_val(p, v);
+          }
+        }
+      }
+    }
+  }
+  pdl_launch_dependents();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, BN);
+  }
+}
+
+// ---- host: tensor maps through the driver entry point (no link-time libcuda dependency) ----
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    FAK_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+CUtensorMap make_map_bf16_kmajor(const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_elems * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+template <int BN, int STAGES, typename OutT>
+void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* bias, int epi,
+                 int* err) {
+  const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
+  CUtensorMap ma = make_map_bf16_kmajor(a.data_ptr(), M, K, a.stride(0), BM);
+  CUtensorMap mb = make_map_bf16_kmajor(b.data_ptr(), N, K, b.stride(0), BN);
+  size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
+  auto kern = k_gemm_bf16<BN, STAGES, OutT>;
+  FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((M + BM - 1) / BM, (N + BN - 1) / BN);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, reinterpret_cast<OutT*>(out.data_ptr()),
+                                    (int64_t)out.stride(0), bias, epi, err));
+}
+
+}  // namespace
+
+// out (op)= a[M,K] . b[N,K]^T ; a, b bf16 K-major (row stride multiple of 8 elements, 16B-aligned base).
+// epi: 0 store, 1 add into out, 2 SwiGLU over interleaved (gate, up) columns -> out[:, N/2].
+void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias, int64_t epi,
+               c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == torch::kBFloat16 && a.dim() == 2 && a.stride(1) == 1, "a: [M,K] bf16");
+  TORCH_CHECK(b.scalar_type() == torch::kBFloat16 && b.dim() == 2 && b.stride(1) == 1, "b: [N,K] bf16");
+  TORCH_CHECK(a.size(1) == b.size(1), "K mismatch");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "row strides must be multiples of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0,
+              "operands must be 16-byte aligned");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out: [M, *] row-major");
+  const int64_t M = a.size(0), N = b.size(0);
+  TORCH_CHECK(out.size(0) >= M && out.size(1) >= (epi == G_SWIGLU ? N / 2 : N), "out too small");
+  if (epi == G_SWIGLU) TORCH_CHECK(N % 2 == 0, "SwiGLU needs an even N");
+  if (M == 0 || N == 0) return;
+  const float* bp = nullptr;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "bias");
+    bp = bias->data_ptr<float>();
+  }
+  int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
+  if (out.scalar_type() == torch::kFloat32)
+    launch_gemm<256, 4, float>(a, b, out, bp, (int)epi, ep);
+  else if (out.scalar_type() == torch::kBFloat16)
+    launch_gemm<256, 4, __nv_bfloat16>(a, b, out, bp, (int)epi, ep);
+  else
+    TORCH_CHECK(false, "out must be float32 or bfloat16");
+}

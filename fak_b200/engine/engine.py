@@ -1,0 +1,338 @@
+"""The serving engine: requests, KV pages, radix prefix reuse, continuous batching.
+
+One ``Engine`` owns one model replica (one GPU, or one tensor-parallel group where every
+rank runs the same scheduler deterministically).  ``step()`` is one scheduler iteration:
+
+1. admit waiting requests while KV pages last: look the prompt up in the radix cache
+   (whole 16-token pages), take references on the matched pages and allocate pages for
+   the rest;
+2. prefill the admitted prompt suffixes as one packed ragged chunk (bounded by
+   ``max_prefill_tokens``; longer prompts continue in the next iteration);
+3. decode one token for every running request in one batched forward (CUDA graph);
+4. retire finished requests: their whole pages go into the radix tree for later requests,
+   their references are dropped.
+
+Reference behaviour: NativeScheduler (internal/modelengine/nativesched.go:42-227) for the
+waiting/running loop, InKernelPlanner.generateReusedContextWithBias
+(internal/agent/inkernel_planner.go:1046-1164) for lookup -> clone -> prefill suffix ->
+insert -> decode, and KV-block preemption (nativesched_preempt.go) when pages run out.
+The reference's device path never reuses prefixes (inkernel_planner.go:1054); this one
+always does.
+"""
+from __future__ import annotations
+
+import dataclasses
+import itertools
+import math
+import time
+from typing import Callable
+
+import numpy as np
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..kv import OutOfPages, PagePool, RadixCache
+from ..models.runner import KVCache, ModelRunner, PrefillMeta
+from ..models.weights import ModelWeights, gguf_source, load_weights, synthetic_source
+from .sampling import SamplingParams, sample
+
+
+@dataclasses.dataclass
+class Request:
+    rid: int
+    prompt: list[int]
+    max_new_tokens: int
+    sampling: SamplingParams
+    stop_ids: frozenset[int] = frozenset()
+    arrival: float = dataclasses.field(default_factory=time.perf_counter)
+    # state
+    tokens: list[int] = dataclasses.field(default_factory=list)  # prompt + generated
+    output: list[int] = dataclasses.field(default_factory=list)
+    pages: list[int] = dataclasses.field(default_factory=list)
+    n_kv: int = 0            # tokens whose K/V are in ``pages``
+    n_cached_hit: int = 0    # prompt tokens served by the radix cache
+    first_token_time: float | None = None
+    finish_time: float | None = None
+    finished: bool = False
+    finish_reason: str = ""
+    on_token: Callable[[int], None] | None = None
+
+    @property
+    def ttft(self) -> float | None:
+        return None if self.first_token_time is None else self.first_token_time - self.arrival
+
+
+class Engine:
+    def __init__(self, weights: ModelWeights, ecfg: EngineConfig | None = None, device: str | torch.device = "cuda",
+                 collectives=None, n_pages: int | None = None, max_context: int | None = None, tp_group=None):
+        self.ecfg = ecfg or EngineConfig.from_env()
+        self.cfg: ModelConfig = weights.cfg
+        self.device = torch.device(device)
+        self.weights = weights
+        ps = self.ecfg.page_size
+        if ps != 16:
+            raise ValueError("the attention kernels are built for 16-token pages")
+        self.max_context = max_context or self.cfg.max_context
+        if n_pages is None:
+            n_pages = self.ecfg.kv_pages or self._pages_from_memory()
+        self.kv = KVCache.allocate(self.cfg.n_layers, n_pages, weights.n_kv_local, self.cfg.head_dim, self.device)
+        self.pool = PagePool(n_pages, reserve=1)
+        self.radix = RadixCache(self.pool, ps) if self.ecfg.radix_cache else None
+        if collectives is None and tp_group is not None and weights.tp_size > 1:
+            from ..parallel.tp import NcclTP
+            collectives = NcclTP(tp_group, weights, self.ecfg.max_batch, self.device)
+        self.tp_group = tp_group
+        self.runner = ModelRunner(weights, self.kv, max_batch=self.ecfg.max_batch,
+                                  max_prefill_tokens=self.ecfg.max_prefill_tokens, max_context=self.max_context,
+                                  collectives=collectives)
+        self.bt_width = math.ceil(self.max_context / ps)
+        self.waiting: list[Request] = []
+        self.prefilling: list[Request] = []
+        self.running: list[Request] = []
+        self._rid = itertools.count()
+        self.stats = {"prefill_tokens": 0, "prefill_tokens_avoided": 0, "decode_tokens": 0, "steps": 0,
+                      "preemptions": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+        self._graphs_ready = False
+
+    # ------------------------------------------------------------------------------------
+    @staticmethod
+    def _tp(tp_group) -> tuple[int, int]:
+        if tp_group is None:
+            return 0, 1
+        import torch.distributed as dist
+        return dist.get_rank(tp_group), dist.get_world_size(tp_group)
+
+    @classmethod
+    def from_gguf(cls, path: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None, **kw) -> "Engine":
+        r, n = cls._tp(tp_group)
+        w = load_weights(gguf_source(path), device, tp_rank=r, tp_size=n,
+                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
+        return cls(w, ecfg, device, tp_group=tp_group, **kw)
+
+    @classmethod
+    def synthetic(cls, cfg: ModelConfig, mix: str = "q4_k_m", seed: int = 0, ecfg: EngineConfig | None = None,
+                  device="cuda", tp_group=None, **kw) -> "Engine":
+        r, n = cls._tp(tp_group)
+        w = load_weights(synthetic_source(cfg, mix, seed, device=str(device)), device, tp_rank=r, tp_size=n,
+                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
+        return cls(w, ecfg, device, tp_group=tp_group, **kw)
+
+    def shutdown(self) -> None:
+        """Release CUDA graphs (they may hold collectives) before the process group goes away."""
+        self.runner._graphs.clear()
+        self._graphs_ready = False
+        torch.cuda.synchronize(self.device)
+
+    def _pages_from_memory(self) -> int:
+        free, _ = torch.cuda.mem_get_info(self.device)
+        per = KVCache.bytes_per_page(self.cfg.n_layers, self.weights.n_kv_local, self.cfg.head_dim)
+        return max(64, int(free * self.ecfg.kv_mem_fraction) // per)
+
+    def warmup_graphs(self, buckets: tuple[int, ...] | None = None) -> None:
+        if not self.ecfg.cuda_graph:
+            return
+        for b in buckets or self.ecfg.graph_batch_buckets:
+            if b <= self.ecfg.max_batch:
+                self.runner.capture(b, self.bt_width)
+        self._graphs_ready = True
+
+    # ------------------------------------------------------------------------------------
+    def add_request(self, prompt: list[int], max_new_tokens: int = 128, sampling: SamplingParams | None = None,
+                    stop_ids=(), on_token=None) -> Request:
+        if not prompt:
+            raise ValueError("empty prompt")
+        if len(prompt) + max_new_tokens > self.max_context:
+            raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds context {self.max_context}")
+        r = Request(next(self._rid), list(prompt), max_new_tokens, sampling or SamplingParams(),
+                    frozenset(stop_ids), on_token=on_token)
+        r.tokens = list(prompt)
+        self.waiting.append(r)
+        return r
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.prefilling or self.running)
+
+    def _alloc(self, n: int) -> list[int]:
+        if n <= 0:
+            return []
+        if self.pool.n_free() < n and self.radix is not None:
+            self.radix.evict(n - self.pool.n_free())
+        return self.pool.alloc(n)
+
+    def _admit(self) -> None:
+        ps = self.ecfg.page_size
+        while self.waiting and len(self.running) + len(self.prefilling) < self.ecfg.max_batch:
+            r = self.waiting[0]
+            hit, pages = 0, []
+            if self.radix is not None:
+                # keep at least one prompt token to prefill: its logits give the first output token
+                hit, pages = self.radix.lookup(r.prompt, max_tokens=len(r.prompt) - 1)
+            need = math.ceil(len(r.prompt) / ps) - len(pages)
+            try:
+                new = self._alloc(need)
+            except OutOfPages:
+                self.pool.release(pages)
+                if not self.running and not self.prefilling:
+                    raise
+                break
+            self.waiting.pop(0)
+            r.pages = pages + new
+            r.n_kv = hit
+            r.n_cached_hit = hit
+            self.stats["prefill_tokens_avoided"] += hit
+            self.prefilling.append(r)
+
+    # ------------------------------------------------------------------------------------
+    def _run_prefill(self) -> None:
+        budget = self.ecfg.max_prefill_tokens
+        chunk: list[tuple[Request, int, int]] = []
+        for r in self.prefilling:
+            if budget <= 0:
+                break
+            n = min(len(r.prompt) - r.n_kv, budget)
+            chunk.append((r, r.n_kv, n))
+            budget -= n
+        if not chunk:
+            return
+        ps = self.ecfg.page_size
+        ids, pos, slot, qlens, pos0s, last = [], [], [], [], [], []
+        W = max(len(r.pages) for r, s, n in chunk)
+        bt = np.zeros((len(chunk), max(W, 1)), dtype=np.int32)
+        t = 0
+        for k, (r, s, n) in enumerate(chunk):
+            ids.extend(r.prompt[s:s + n])
+            p = np.arange(s, s + n)
+            pos.extend(p.tolist())
+            pg = np.asarray(r.pages, dtype=np.int64)
+            slot.extend((pg[p // ps] * ps + p % ps).tolist())
+            bt[k, :len(r.pages)] = r.pages
+            qlens.append(n)
+            pos0s.append(s)
+            t += n
+            last.append(t - 1)
+        dev = self.device
+        to = lambda a: torch.tensor(a, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        meta = PrefillMeta.build(qlens, pos0s, dev)
+        self.stats["h2d_bytes"] += 4 * (3 * len(ids) + len(last) + bt.size + 3 * len(qlens) + 2 * meta.n_tiles)
+        logits = self.runner.prefill(to(ids), to(pos), to(slot), torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True),
+                                     meta, to(last))
+        self.stats["prefill_tokens"] += t
+        done = []
+        for k, (r, s, n) in enumerate(chunk):
+            r.n_kv = s + n
+            if r.n_kv == len(r.prompt):
+                done.append((k, r))
+        if done:
+            rows = torch.tensor([k for k, _ in done], device=dev)
+            toks = sample(logits.index_select(0, rows), [r.sampling for _, r in done], [r for _, r in done])
+            self.stats["d2h_bytes"] += 8 * len(done)
+            now = time.perf_counter()
+            for (k, r), tok in zip(done, toks):
+                self.prefilling.remove(r)
+                r.first_token_time = now
+                self._emit(r, tok)
+                if not r.finished:
+                    self.running.append(r)
+
+    def _emit(self, r: Request, tok: int) -> None:
+        r.output.append(tok)
+        r.tokens.append(tok)
+        if r.on_token is not None:
+            r.on_token(tok)
+        if tok in r.stop_ids:
+            self._finish(r, "stop")
+        elif len(r.output) >= r.max_new_tokens:
+            self._finish(r, "length")
+
+    def _finish(self, r: Request, reason: str) -> None:
+        r.finished = True
+        r.finish_reason = reason
+        r.finish_time = time.perf_counter()
+        if self.radix is not None:
+            # the K/V of tokens[:n_kv] is in the pages; the last sampled token was never fed
+            self.radix.insert(r.tokens[:r.n_kv], r.pages)
+        self.pool.release(r.pages)
+        r.pages = []
+
+    def _run_decode(self) -> None:
+        if not self.running:
+            return
+        ps = self.ecfg.page_size
+        lanes = []
+        for r in list(self.running):
+            p = r.n_kv  # position of the token being fed (the last sampled one)
+            if p // ps >= len(r.pages):
+                try:
+                    r.pages.extend(self._alloc(1))
+                except OutOfPages:
+                    self._preempt(r)
+                    continue
+            lanes.append(r)
+        if not lanes:
+            return
+        B = len(lanes)
+        W = self.bt_width
+        ids = np.empty(B, np.int32)
+        pos = np.empty(B, np.int32)
+        slot = np.empty(B, np.int32)
+        ctx = np.empty(B, np.int32)
+        bt = np.zeros((B, W), np.int32)
+        for k, r in enumerate(lanes):
+            p = r.n_kv
+            ids[k] = r.tokens[-1]
+            pos[k] = p
+            slot[k] = r.pages[p // ps] * ps + p % ps
+            ctx[k] = p + 1
+            bt[k, :len(r.pages)] = r.pages
+        dev = self.device
+        h = torch.from_numpy(np.concatenate([ids, pos, slot, ctx])).pin_memory()
+        d = h.to(dev, non_blocking=True)
+        btd = torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True)
+        greedy = all(r.sampling.greedy for r in lanes)
+        out = self.runner.decode(d[0:B], d[B:2 * B], d[2 * B:3 * B], btd, d[3 * B:4 * B], B,
+                                 use_graph=self._graphs_ready)
+        self.stats["h2d_bytes"] += h.numel() * 4 + bt.size * 4
+        if greedy:
+            toks = out.cpu().tolist()
+            self.stats["d2h_bytes"] += 4 * B
+        else:
+            toks = sample(self.runner.logits[:B], [r.sampling for r in lanes], lanes)
+            self.stats["d2h_bytes"] += 8 * B
+        self.stats["decode_tokens"] += B
+        for r, tok in zip(lanes, toks):
+            r.n_kv += 1
+            self._emit(r, tok)
+        self.running = [r for r in self.running if not r.finished]
+
+    def _preempt(self, r: Request) -> None:
+        """Out of pages: give this request's pages back and recompute it later (recompute
+        preemption; its finished prefix goes to the radix cache so the recompute is cheap)."""
+        self.stats["preemptions"] += 1
+        self.running.remove(r)
+        if self.radix is not None:
+            self.radix.insert(r.tokens[:r.n_kv], r.pages)
+        self.pool.release(r.pages)
+        r.pages = []
+        r.prompt = list(r.tokens)
+        r.max_new_tokens -= len(r.output)
+        r.output_before_preempt = list(r.output)
+        r.n_kv = 0
+        self.waiting.insert(0, r)
+
+    def step(self) -> None:
+        self._admit()
+        self._run_prefill()
+        self._run_decode()
+        self.stats["steps"] += 1
+
+    def run_until_done(self, reqs: list[Request] | None = None) -> None:
+        while self.has_work():
+            self.step()
+            if reqs is not None and all(r.finished for r in reqs):
+                break
+
+    def generate(self, prompts: list[list[int]], max_new_tokens: int = 32, sampling: SamplingParams | None = None,
+                 stop_ids=()) -> list[list[int]]:
+        reqs = [self.add_request(p, max_new_tokens, sampling, stop_ids) for p in prompts]
+        self.run_until_done(reqs)
+        return [r.output for r in reqs]

@@ -1,0 +1,175 @@
+"""Plain-PyTorch fp32 forward of the supported decoder families: the numerics oracle.
+
+This is the framework's equivalent of the reference's cpu-ref backend and
+cacheless ``Model.Forward`` (internal/compute/cpuref.go:38-290,
+internal/model/forward.go:45-434): every CUDA kernel and every engine path
+is tested against it.  Semantics kept identical to the reference:
+
+* RMSNorm ``x * rsqrt(mean(x^2) + eps) * w`` (cuda_kernels.cu:529-548).
+* HF rotate_half RoPE with the angle computed in float64 (cuda_kernels.cu:551-567).
+* SiLU-gated FFN; qkv bias (Qwen2); per-head q/k RMSNorm before RoPE (Qwen3).
+* MoE router: softmax over all experts, then top-k, renormalised when
+  ``norm_topk_prob`` (internal/model/moe.go:279-311).
+* Causal attention with GQA head groups.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from ..config import ModelConfig
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return xf * inv * w.float()
+
+
+def rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin tables [T, head_dim/2] with angles evaluated in float64."""
+    half = head_dim // 2
+    j = torch.arange(half, dtype=torch.float64)
+    inv = 1.0 / torch.pow(torch.tensor(theta, dtype=torch.float64), 2.0 * j / head_dim)
+    ang = positions.to(torch.float64)[:, None].cpu() * inv[None, :]
+    return torch.cos(ang).float().to(positions.device), torch.sin(ang).float().to(positions.device)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [T, H, D]; rotate_half pairs (j, j + D/2)."""
+    half = x.shape[-1] // 2
+    x0, x1 = x[..., :half], x[..., half:]
+    c, s = cos[:, None, :], sin[:, None, :]
+    return torch.cat([x0 * c - x1 * s, x1 * c + x0 * s], dim=-1)
+
+
+def moe_route(logits: torch.Tensor, k: int, norm_topk: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Softmax-then-top-k router. Returns (weights [T,k], expert ids [T,k])."""
+    p = torch.softmax(logits.float(), dim=-1)
+    w, idx = torch.topk(p, k, dim=-1)
+    if norm_topk:
+        w = w / w.sum(-1, keepdim=True)
+    return w, idx
+
+
+class ReferenceModel:
+    """fp32 forward over canonical GGUF-named tensors (already dequantized, HF row order)."""
+
+    def __init__(self, cfg: ModelConfig, tensors: dict[str, torch.Tensor], device: str | torch.device = "cpu"):
+        cfg.validate()
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.t = {k: v.to(self.device, torch.float32) for k, v in tensors.items()}
+
+    @classmethod
+    def from_gguf(cls, path_or_file, device: str | torch.device = "cpu") -> "ReferenceModel":
+        from .loader import load_reference_tensors
+        cfg, tensors = load_reference_tensors(path_or_file)
+        return cls(cfg, tensors, device)
+
+    def w(self, name: str) -> torch.Tensor:
+        return self.t[name]
+
+    def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        return self.t["token_embd.weight"][ids.to(self.device)]
+
+    def lm_head(self, h: torch.Tensor) -> torch.Tensor:
+        W = self.t["token_embd.weight"] if self.cfg.tie_embeddings else self.t["output.weight"]
+        return h @ W.T
+
+    def _ffn(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        cfg, p = self.cfg, f"blk.{i}."
+        if not cfg.is_moe:
+            g = x @ self.w(p + "ffn_gate.weight").T
+            u = x @ self.w(p + "ffn_up.weight").T
+            return (torch.nn.functional.silu(g) * u) @ self.w(p + "ffn_down.weight").T
+        wts, idx = moe_route(x @ self.w(p + "ffn_gate_inp.weight").T, cfg.n_experts_used, cfg.norm_topk_prob)
+        G, U, D = self.w(p + "ffn_gate_exps.weight"), self.w(p + "ffn_up_exps.weight"), self.w(p + "ffn_down_exps.weight")
+        out = torch.zeros_like(x)
+        for t in range(x.shape[0]):
+            for j in range(cfg.n_experts_used):
+                e = int(idx[t, j])
+                h = torch.nn.functional.silu(G[e] @ x[t]) * (U[e] @ x[t])
+                out[t] += wts[t, j] * (D[e] @ h)
+        return out
+
+    def forward(self, ids: torch.Tensor, start_pos: int = 0,
+                kv: list[tuple[torch.Tensor, torch.Tensor]] | None = None,
+                hidden_only: bool = False) -> torch.Tensor:
+        """Run T tokens at absolute positions start_pos.. ; ``kv`` (per layer [Tctx,Hkv,D]) is extended in place."""
+        cfg = self.cfg
+        ids = torch.as_tensor(ids, dtype=torch.long, device=self.device).reshape(-1)
+        T = ids.numel()
+        x = self.embed(ids)
+        pos = torch.arange(start_pos, start_pos + T, device=self.device)
+        cos, sin = rope_cos_sin(pos, cfg.head_dim, cfg.rope_theta)
+        H, Hk, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        for i in range(cfg.n_layers):
+            p = f"blk.{i}."
+            h = rmsnorm(x, self.w(p + "attn_norm.weight"), cfg.rms_eps)
+            q = h @ self.w(p + "attn_q.weight").T
+            k = h @ self.w(p + "attn_k.weight").T
+            v = h @ self.w(p + "attn_v.weight").T
+            if cfg.qkv_bias:
+                q = q + self.w(p + "attn_q.bias")
+                k = k + self.w(p + "attn_k.bias")
+                v = v + self.w(p + "attn_v.bias")
+            q = q.view(T, H, D)
+            k = k.view(T, Hk, D)
+            v = v.view(T, Hk, D)
+            if cfg.qk_norm:
+                q = rmsnorm(q, self.w(p + "attn_q_norm.weight"), cfg.rms_eps)
+                k = rmsnorm(k, self.w(p + "attn_k_norm.weight"), cfg.rms_eps)
+            q = apply_rope(q, cos, sin)
+            k = apply_rope(k, cos, sin)
+            if kv is not None:
+                if len(kv) <= i:
+                    kv.append((k, v))
+                else:
+                    kv[i] = (torch.cat([kv[i][0], k]), torch.cat([kv[i][1], v]))
+                K, V = kv[i]
+            else:
+                K, V = k, v
+            a = attention(q, K, V, start_pos)
+            x = x + a.reshape(T, H * D) @ self.w(p + "attn_output.weight").T
+            h = rmsnorm(x, self.w(p + "ffn_norm.weight"), cfg.rms_eps)
+            x = x + self._ffn(i, h)
+        x = rmsnorm(x, self.t["output_norm.weight"], cfg.rms_eps)
+        return x if hidden_only else self.lm_head(x)
+
+    @torch.no_grad()
+    def generate_greedy(self, prompt: list[int], n_new: int) -> list[int]:
+        kv: list = []
+        logits = self.forward(torch.tensor(prompt), 0, kv)
+        out = []
+        nxt = int(torch.argmax(logits[-1]))
+        pos = len(prompt)
+        for _ in range(n_new):
+            out.append(nxt)
+            logits = self.forward(torch.tensor([nxt]), pos, kv)
+            pos += 1
+            nxt = int(torch.argmax(logits[-1]))
+        return out
+
+
+def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int) -> torch.Tensor:
+    """q [T,H,D] at positions start_pos..; K,V [Tctx,Hk,D] covering positions 0..Tctx-1 (causal)."""
+    T, H, D = q.shape
+    Tc, Hk, _ = K.shape
+    g = H // Hk
+    Kx = K.repeat_interleave(g, dim=1)
+    Vx = V.repeat_interleave(g, dim=1)
+    s = torch.einsum("thd,chd->htc", q.float(), Kx.float()) / math.sqrt(D)
+    qpos = torch.arange(start_pos, start_pos + T, device=q.device)[:, None]
+    kpos = torch.arange(Tc, device=q.device)[None, :]
+    s = s.masked_fill((kpos > qpos)[None], float("-inf"))
+    pr = torch.softmax(s, dim=-1)
+    return torch.einsum("htc,chd->thd", pr, Vx.float())
+
+
+def numpy_seeded_ids(n: int, vocab: int, seed: int) -> list[int]:
+    """Seeded uniform token ids (the benchmarks' synthetic prompts)."""
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, vocab, size=n).tolist()

@@ -1,0 +1,278 @@
+"""Forward passes of the dense Llama/Qwen2/Qwen3 and Qwen3-MoE decoders on the GPU.
+
+Two entry points, both over the paged KV cache:
+
+``decode``   B sequences advance one token.  Per layer: RMSNorm+int8 activation quant,
+             q/k/v GEMV (+bias), RoPE (+q/k norm) with the K/V append into the pages,
+             split-KV paged attention whose merge writes the o_proj input already
+             quantized, o_proj GEMV accumulating into the fp32 residual, RMSNorm+quant,
+             gate/up GEMV with a SwiGLU epilogue, quant, down GEMV accumulating into the
+             residual.  The whole step is captured as one CUDA graph per batch bucket.
+``prefill``  a packed chunk of new tokens from several sequences (ragged), each attending
+             to its cached prefix + itself; bf16 activations through tensor-core GEMMs.
+
+The reference runs the same per-token sequence of ops one kernel per op on one stream
+(internal/model/hal.go:269-439, tokenHALOutput) and prefills with a per-token loop
+(hal.go:522-534); batched decode shares one weight stream across lanes
+(internal/model/batch_step.go:7).  With tensor parallelism the ``collectives`` object
+supplies the gathers/reductions between the GEMVs (parallel/tp.py).
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import torch
+
+from ..config import ModelConfig
+from ..ops import kernels as K
+from .weights import ModelWeights
+
+
+def rope_tables(max_pos: int, head_dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    half = head_dim // 2
+    j = torch.arange(half, dtype=torch.float64)
+    inv = 1.0 / torch.pow(torch.tensor(theta, dtype=torch.float64), 2.0 * j / head_dim)
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cos(ang).float().to(device).contiguous(), torch.sin(ang).float().to(device).contiguous()
+
+
+@dataclasses.dataclass
+class KVCache:
+    k: torch.Tensor  # [L, P, Hkv_local, 16, D] bf16
+    v: torch.Tensor
+
+    @classmethod
+    def allocate(cls, n_layers: int, n_pages: int, n_kv: int, head_dim: int, device, page_size: int = 16
+                 ) -> "KVCache":
+        shape = (n_layers, n_pages, n_kv, page_size, head_dim)
+        return cls(torch.zeros(shape, dtype=torch.bfloat16, device=device),
+                   torch.zeros(shape, dtype=torch.bfloat16, device=device))
+
+    @property
+    def n_pages(self) -> int:
+        return self.k.shape[1]
+
+    @staticmethod
+    def bytes_per_page(n_layers: int, n_kv: int, head_dim: int, page_size: int = 16) -> int:
+        return 2 * n_layers * n_kv * page_size * head_dim * 2
+
+
+@dataclasses.dataclass
+class PrefillMeta:
+    """Packed ragged chunk description (all int32 device tensors)."""
+    tile_seq: torch.Tensor
+    tile_q0: torch.Tensor
+    seq_qoff: torch.Tensor
+    seq_qlen: torch.Tensor
+    seq_pos0: torch.Tensor
+    n_tiles: int
+
+    @classmethod
+    def build(cls, qlens: list[int], pos0s: list[int], device) -> "PrefillMeta":
+        tile_seq, tile_q0, off, offs = [], [], 0, []
+        for s, ql in enumerate(qlens):
+            offs.append(off)
+            for q0 in range(0, ql, 64):
+                tile_seq.append(s)
+                tile_q0.append(q0)
+            off += ql
+        mk = lambda a: torch.tensor(a, dtype=torch.int32).to(device, non_blocking=True)
+        return cls(mk(tile_seq), mk(tile_q0), mk(offs), mk(qlens), mk(pos0s), len(tile_seq))
+
+
+class ModelRunner:
+    def __init__(self, weights: ModelWeights, kv: KVCache, max_batch: int = 64, max_prefill_tokens: int = 4096,
+                 max_context: int | None = None, collectives=None):
+        self.w = weights
+        self.cfg: ModelConfig = weights.cfg
+        self.kv = kv
+        self.coll = collectives
+        cfg = self.cfg
+        dev = kv.k.device
+        self.device = dev
+        self.max_batch = max_batch
+        self.max_prefill = max_prefill_tokens
+        self.max_context = max_context or cfg.max_context
+        self.Hq = weights.n_q_local
+        self.Hkv = weights.n_kv_local
+        self.D = cfg.head_dim
+        self.qkv_dim = (self.Hq + 2 * self.Hkv) * self.D
+        f0, f1 = weights.ffn_slice
+        self.ffn_local = (f1 - f0) if not cfg.is_moe else cfg.expert_ffn_dim
+        self.cos, self.sin = rope_tables(self.max_context, self.D, cfg.rope_theta, dev)
+        B, d = max_batch, cfg.d_model
+        # decode buffers (static: CUDA graphs capture their addresses)
+        self.x = torch.zeros(B, d, dtype=torch.float32, device=dev)
+        self.qkv = torch.zeros(B, self.qkv_dim, dtype=torch.float32, device=dev)
+        self.q = torch.zeros(B, self.Hq, self.D, dtype=torch.float32, device=dev)
+        self.h = torch.zeros(B, max(self.ffn_local, 32), dtype=torch.float32, device=dev)
+        self.act_d = K.ActQ(B, d, dev)
+        self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
+        self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
+        self.logits = torch.zeros(B, weights.lm_head.rows, dtype=torch.float32, device=dev)
+        self.next_ids = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.max_split = 64
+        self.attn_ws = torch.zeros(B * self.Hq * self.max_split * (self.D + 2), dtype=torch.float32, device=dev)
+        self._graphs: dict[int, tuple[torch.cuda.CUDAGraph, dict]] = {}
+        self._graph_kernels: dict[int, int] = {}
+
+    # ------------------------------------------------------------------------------------
+    def n_split_for(self, B: int) -> int:
+        """Context splits of the decode attention.  Independent of B on purpose: a sequence's
+        attention then reduces in the same order whatever batch it runs in, so batched decode
+        is bit-identical to serial decode.  The kernel spreads the live pages evenly over the
+        splits, so short contexts just leave some splits empty."""
+        return 32
+
+    def _layer_decode(self, i: int, B: int, pos, slot, bt, ctx, n_split: int) -> None:
+        cfg, L, kv = self.cfg, self.w.layers[i], self.kv
+        x = self.x[:B]
+        K.quant_act(x, self.act_d, L.attn_norm, cfg.rms_eps)
+        for seg, off in L.qkv:
+            bias = L.qkv_bias[off:off + seg.rows] if L.qkv_bias is not None else None
+            K.gemv(seg, self.act_d, B, self.qkv[:B, off:off + seg.rows], bias, K.EPI_STORE)
+        K.rope_kv(self.qkv[:B], pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
+                  self.q[:B], None, kv.k[i], kv.v[i])
+        if self.coll is None:
+            K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_attn,
+                               workspace=self.attn_ws)
+            K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD)
+        else:
+            self.coll.decode_attn_o(self, i, B, bt, ctx, n_split)
+        K.quant_act(x, self.act_d, L.ffn_norm, cfg.rms_eps)
+        if cfg.is_moe:
+            from .moe import moe_decode
+            moe_decode(self, i, B)
+            return
+        K.gemv(L.gate_up, self.act_d, B, self.h[:B], None, K.EPI_SWIGLU)
+        K.quant_act(self.h[:B, :self.ffn_local], self.act_ffn)
+        if self.coll is None:
+            K.gemv(L.down, self.act_ffn, B, x, None, K.EPI_ADD)
+        else:
+            self.coll.decode_down(self, i, B)
+
+    def decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True) -> None:
+        """One decode step for B sequences; results in self.logits[:B] / self.next_ids[:B]."""
+        cfg = self.cfg
+        n_split = self.n_split_for(B)
+        K.embed(self.w.embed, ids, self.x[:B], None, self.err)
+        for i in range(cfg.n_layers):
+            self._layer_decode(i, B, pos, slot, bt, ctx, n_split)
+        K.quant_act(self.x[:B], self.act_d, self.w.final_norm, cfg.rms_eps)
+        self._lm_head(B)
+        if greedy:
+            K.argmax(self.logits[:B], self.logits.shape[1], self.next_ids[:B])
+
+    def _lm_head(self, B: int) -> None:
+        if self.coll is None:
+            K.gemv(self.w.lm_head, self.act_d, B, self.logits[:B], None, K.EPI_STORE)
+        else:
+            self.coll.lm_head(self, B)
+
+    # ------------------------------------------------------------------------------------
+    # CUDA graph per batch bucket
+    # ------------------------------------------------------------------------------------
+    def _static_inputs(self, B: int, bt_width: int) -> dict:
+        dev = self.device
+        return {
+            "ids": torch.zeros(B, dtype=torch.int32, device=dev),
+            "pos": torch.zeros(B, dtype=torch.int32, device=dev),
+            "slot": torch.zeros(B, dtype=torch.int32, device=dev),
+            "bt": torch.zeros(B, bt_width, dtype=torch.int32, device=dev),
+            "ctx": torch.ones(B, dtype=torch.int32, device=dev),
+        }
+
+    def capture(self, B: int, bt_width: int) -> None:
+        st = self._static_inputs(B, bt_width)
+        # warm up (also triggers lazy cudaFuncSetAttribute) on a side stream, then capture
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        before = K.launches()
+        with torch.cuda.graph(g):
+            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B)
+        self._graph_kernels[B] = K.launches() - before
+        K._launches[0] = before
+        self._graphs[B] = (g, st)
+
+    def graph_bucket(self, B: int) -> int | None:
+        cands = [b for b in self._graphs if b >= B]
+        return min(cands) if cands else None
+
+    def decode(self, ids, pos, slot, bt, ctx, B: int, use_graph: bool = True) -> torch.Tensor:
+        """Decode one token for B sequences; returns next ids (device int32 [B])."""
+        bucket = self.graph_bucket(B) if use_graph else None
+        if bucket is None:
+            self.decode_eager(ids, pos, slot, bt, ctx, B)
+            return self.next_ids[:B]
+        g, st = self._graphs[bucket]
+        st["ids"][:B].copy_(ids)
+        st["pos"][:B].copy_(pos)
+        st["slot"][:B].copy_(slot)
+        w = min(bt.shape[1], st["bt"].shape[1])
+        st["bt"][:B, :w].copy_(bt[:, :w])
+        st["ctx"][:B].copy_(ctx)
+        if bucket > B:  # padding lanes: a 1-token context on page 0 of their own slot
+            st["ctx"][B:].fill_(1)
+            st["slot"][B:].fill_(-1)
+        g.replay()
+        K.count(self._graph_kernels[bucket])
+        return self.next_ids[:B]
+
+    # ------------------------------------------------------------------------------------
+    # prefill
+    # ------------------------------------------------------------------------------------
+    def prefill(self, ids, pos, slot, bt, meta: PrefillMeta, last_idx: torch.Tensor) -> torch.Tensor:
+        """Run a packed chunk; returns logits [S, V] for each sequence's last token (and next ids)."""
+        cfg, dev = self.cfg, self.device
+        T = ids.numel()
+        d = cfg.d_model
+        x = torch.empty(T, d, dtype=torch.float32, device=dev)
+        hb = torch.empty(T, d, dtype=torch.bfloat16, device=dev)
+        qkv = torch.empty(T, self.qkv_dim, dtype=torch.float32, device=dev)
+        qb = torch.empty(T, self.Hq, self.D, dtype=torch.bfloat16, device=dev)
+        ab = torch.empty(T, self.Hq * self.D, dtype=torch.bfloat16, device=dev)
+        K.embed(self.w.embed, ids, x, None, self.err)
+        for i in range(cfg.n_layers):
+            L = self.w.layers[i]
+            K.rmsnorm_bf16(x, L.attn_norm, cfg.rms_eps, hb)
+            for seg, off in L.qkv:
+                bias = L.qkv_bias[off:off + seg.rows] if L.qkv_bias is not None else None
+                K.gemm(hb, seg, qkv[:, off:off + seg.rows], K.EPI_STORE, bias)
+            K.rope_kv(qkv, pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
+                      None, qb, self.kv.k[i], self.kv.v[i])
+            K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab)
+            if self.coll is None:
+                K.gemm(ab, L.o, x, K.EPI_ADD)
+            else:
+                self.coll.prefill_attn_o(self, i, ab, x)
+            K.rmsnorm_bf16(x, L.ffn_norm, cfg.rms_eps, hb)
+            if cfg.is_moe:
+                from .moe import moe_prefill
+                moe_prefill(self, i, hb, x)
+                continue
+            hf = torch.empty(T, self.ffn_local, dtype=torch.float32, device=dev)
+            K.gemm(hb, L.gate_up, hf, K.EPI_SWIGLU)
+            hb2 = hf.to(torch.bfloat16)
+            if self.coll is None:
+                K.gemm(hb2, L.down, x, K.EPI_ADD)
+            else:
+                self.coll.prefill_down(self, i, hb2, x)
+        S = last_idx.numel()
+        xl = x.index_select(0, last_idx.long())
+        logits = torch.empty(S, self.w.lm_head.rows, dtype=torch.float32, device=dev)
+        for s0 in range(0, S, self.max_batch):
+            s1 = min(S, s0 + self.max_batch)
+            n = s1 - s0
+            K.quant_act(xl[s0:s1], self.act_d, self.w.final_norm, cfg.rms_eps)
+            if self.coll is None:
+                K.gemv(self.w.lm_head, self.act_d, n, logits[s0:s1], None, K.EPI_STORE)
+            else:
+                self.coll.lm_head_to(self, n, logits[s0:s1])
+        return logits

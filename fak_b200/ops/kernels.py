@@ -1,0 +1,89 @@
+"""Thin typed wrappers over the sm_100a extension, plus the GEMM dispatch used by prefill."""
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext
+
+EPI_STORE, EPI_ADD, EPI_SWIGLU = 0, 1, 2
+GEMV_MAX_B = 8
+
+# kernel-launch accounting (the benchmark reports how many of this package's kernels ran)
+_launches = [0]
+
+
+def count(n: int = 1) -> None:
+    _launches[0] += n
+
+
+def launches() -> int:
+    return _launches[0]
+
+
+def reset_launches() -> None:
+    _launches[0] = 0
+
+
+class ActQ:
+    """int8-quantized activations: codes [B, K] and per-32 (scale, sum) [B, K/32, 2]."""
+
+    def __init__(self, B: int, K: int, device):
+        self.K = K
+        self.q = torch.zeros(B, K, dtype=torch.int8, device=device)
+        self.ds = torch.zeros(B, K // 32, 2, dtype=torch.float32, device=device)
+
+
+def quant_act(x: torch.Tensor, act: ActQ, gamma: torch.Tensor | None = None, eps: float = 1e-6) -> None:
+    ext().quant_act(x, gamma, eps, act.q, act.ds)
+    count()
+
+
+def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None, epi: int = EPI_STORE) -> None:
+    """y[:B] (op)= W . x for B <= 8 tokens (w: models.weights.QuantWeight)."""
+    C = ext()
+    for b0 in range(0, B, GEMV_MAX_B):
+        nb = min(GEMV_MAX_B, B - b0)
+        q = act.q[b0:b0 + nb]
+        d = act.ds[b0:b0 + nb]
+        C.qgemv(w.buf, w.qtype, w.rows, w.cols, w.pitch, q, d, nb, y[b0:b0 + nb], bias, epi)
+        count()
+
+
+def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
+                     workspace=None) -> None:
+    ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
+                           act.q if act is not None else None, act.ds if act is not None else None, workspace)
+    count(2 if n_split > 1 else 1)
+
+
+def prefill_attention(q, k_cache, v_cache, block_table, meta, out) -> None:
+    ext().prefill_attention(q, k_cache, v_cache, block_table, meta.tile_seq, meta.tile_q0, meta.seq_qoff,
+                            meta.seq_qlen, meta.seq_pos0, meta.n_tiles, out)
+    count()
+
+
+def embed(w, ids: torch.Tensor, out_f32=None, out_bf16=None, err=None) -> None:
+    ext().embed(w.buf, w.qtype, w.pitch, w.rows, w.cols, ids, out_f32, out_bf16, err)
+    count()
+
+
+def rope_kv(qkv, pos, slot, cos, sin, H, Hkv, q_norm, k_norm, eps, q_f32, q_bf16, k_cache, v_cache) -> None:
+    ext().rope_kv(qkv, pos, slot, cos, sin, H, Hkv, q_norm, k_norm, eps, q_f32, q_bf16, k_cache, v_cache)
+    count()
+
+
+def rmsnorm_bf16(x, w, eps, y) -> None:
+    ext().rmsnorm_bf16(x, w, eps, y)
+    count()
+
+
+def argmax(logits: torch.Tensor, V: int, out: torch.Tensor) -> None:
+    ext().argmax_rows(logits, V, out)
+    count()
+
+
+def gemm(a: torch.Tensor, w, out: torch.Tensor, epi: int = EPI_STORE, bias: torch.Tensor | None = None,
+         err: torch.Tensor | None = None) -> None:
+    """out (op)= a[M,K] (bf16) . W^T on the tcgen05 tensor cores (W: QuantWeight -> its dense bf16 copy)."""
+    ext().gemm_bf16(a, w.dense() if not isinstance(w, torch.Tensor) else w, out, bias, epi, err)
+    count()

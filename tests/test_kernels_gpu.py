@@ -1,0 +1,238 @@
+"""Numerics of the sm_100a kernels against plain fp32 PyTorch references (GPU only)."""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from fak_b200.gguf import quants as Q
+from fak_b200.gguf.constants import GGMLType
+
+pytestmark = pytest.mark.gpu
+
+QTYPES = [(GGMLType.Q8_0, 32), (GGMLType.Q4_K, 256), (GGMLType.Q6_K, 256)]
+
+
+def _ext():
+    from fak_b200.ops._ext import ext
+    return ext()
+
+
+@pytest.mark.parametrize("qt,blk", QTYPES)
+def test_quantize_matches_numpy_bitexact(qt, blk):
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal((64, 4 * 256)) * 0.02).astype(np.float32)
+    ref = Q.quantize(x, qt)
+    got = _ext().quantize_blocks(torch.from_numpy(x).cuda().reshape(-1), int(qt)).cpu().numpy()
+    assert got.shape == ref.shape
+    match = (got == ref).mean()
+    np.save(f"gpurun_out/quant_{int(qt)}_got.npy", got) if os.path.isdir("gpurun_out") else None
+    # same format, same decoded values up to one quantization step
+    dg, dr = Q.dequantize(got, qt), Q.dequantize(ref, qt)
+    step = np.abs(x).max() / (127 if qt == GGMLType.Q8_0 else 15)
+    assert np.abs(dg - dr).max() <= step, match
+    assert match > 0.9, match
+
+
+@pytest.mark.parametrize("qt,blk", QTYPES)
+def test_dequantize_rows(qt, blk):
+    from fak_b200.ops import quant as dq
+    rng = np.random.default_rng(2)
+    rows, cols = 48, 3 * 256
+    x = (rng.standard_normal((rows, cols)) * 0.05).astype(np.float32)
+    raw = Q.quantize(x, qt).reshape(rows, -1)
+    from fak_b200.models.weights import QuantWeight
+    w = QuantWeight.from_rows(torch.from_numpy(raw), int(qt), cols, torch.device("cuda"))
+    ref = Q.dequantize(raw.reshape(-1), qt).reshape(rows, cols)
+    got = w.dense(torch.float32, cache=False).cpu().numpy()
+    np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6)
+    gotb = w.dense(torch.bfloat16, cache=False).float().cpu().numpy()
+    np.testing.assert_allclose(gotb, ref, rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("B", [1, 3, 5, 8])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_qgemv(qt, blk, B, epi):
+    from fak_b200.models.weights import QuantWeight
+    from fak_b200.ops import kernels as K
+    torch.manual_seed(0)
+    N, Kd = 512 + 64, 1024 if qt != GGMLType.Q8_0 else 576
+    rng = np.random.default_rng(3)
+    Wf = (rng.standard_normal((N, Kd)) * 0.05).astype(np.float32)
+    raw = Q.quantize(Wf, qt).reshape(N, -1)
+    w = QuantWeight.from_rows(torch.from_numpy(raw), int(qt), Kd, torch.device("cuda"))
+    Wd = torch.from_numpy(Q.dequantize(raw.reshape(-1), qt).reshape(N, Kd)).cuda()
+    x = torch.randn(B, Kd, device="cuda")
+    act = K.ActQ(8, Kd, "cuda")
+    K.quant_act(x, act)
+    bias = torch.randn(N, device="cuda") * 0.1
+    ref = x @ Wd.T + bias
+    if epi == K.EPI_SWIGLU:
+        ref = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+        y = torch.zeros(B, N // 2, device="cuda")
+    else:
+        y = torch.randn(B, N, device="cuda")
+        if epi == K.EPI_ADD:
+            ref = ref + y
+    K.gemv(w, act, B, y, bias, epi)
+    torch.cuda.synchronize()
+    err = (y - ref).abs().max().item() / ref.abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
+    # SwiGLU multiplies two int8-activation dot products, which roughly doubles the relative error
+    tol_cos, tol_err = (0.999, 0.06) if epi == K.EPI_SWIGLU else (0.9995, 0.03)
+    assert cos > tol_cos and err < tol_err, (cos, err)
+
+
+def test_quant_act_rmsnorm():
+    from fak_b200.ops import kernels as K
+    x = torch.randn(4, 512, device="cuda") * 3
+    g = torch.rand(512, device="cuda") + 0.5
+    act = K.ActQ(4, 512, "cuda")
+    K.quant_act(x, act, g, 1e-6)
+    xn = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * g
+    deq = act.q.float().view(4, 16, 32) * act.ds[:, :, 0:1]
+    assert torch.allclose(deq.view(4, 512), xn, atol=xn.abs().max().item() / 127 * 0.51 + 1e-6)
+    assert torch.allclose(act.ds[:, :, 1], xn.view(4, 16, 32).sum(-1), atol=1e-4)
+
+
+def _paged_cache(ctx_lens, Hkv, D, n_pages=256, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kc = torch.randn(n_pages, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+    vc = torch.randn(n_pages, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+    perm = torch.randperm(n_pages - 1, generator=torch.Generator().manual_seed(seed)) + 1
+    bts, used = [], 0
+    for L in ctx_lens:
+        n = math.ceil(L / 16)
+        bts.append(perm[used:used + n].tolist())
+        used += n
+    W = max(len(b) for b in bts)
+    bt = torch.zeros(len(ctx_lens), W, dtype=torch.int32)
+    for i, b in enumerate(bts):
+        bt[i, :len(b)] = torch.tensor(b)
+    return kc, vc, bt.cuda()
+
+
+def _gather(kc, bt_row, L):
+    pages = kc[bt_row.long()]  # [n, Hkv, 16, D]
+    return pages.permute(0, 2, 1, 3).reshape(-1, kc.shape[1], kc.shape[3])[:L].float()
+
+
+@pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3), (128, 8, 8)])
+@pytest.mark.parametrize("n_split", [1, 7])
+def test_decode_attention(D, H, Hkv, n_split):
+    from fak_b200.ops import kernels as K
+    ctx = [1, 17, 100, 333, 1000]
+    B = len(ctx)
+    kc, vc, bt = _paged_cache(ctx, Hkv, D)
+    q = torch.randn(B, H, D, device="cuda")
+    out = torch.zeros(B, H * D, device="cuda")
+    act = K.ActQ(B, H * D, "cuda")
+    ws = torch.zeros(B * H * n_split * (D + 2), device="cuda")
+    K.decode_attention(q, kc, vc, bt, torch.tensor(ctx, dtype=torch.int32, device="cuda"), n_split, out=out, act=act,
+                       workspace=ws)
+    torch.cuda.synchronize()
+    G = H // Hkv
+    for b, L in enumerate(ctx):
+        Kb, Vb = _gather(kc, bt[b], L), _gather(vc, bt[b], L)
+        qb = q[b].bfloat16().float()
+        s = torch.einsum("hd,thd->ht", qb, Kb.repeat_interleave(G, 1)) / math.sqrt(D)
+        ref = torch.einsum("ht,thd->hd", torch.softmax(s, -1), Vb.repeat_interleave(G, 1)).reshape(-1)
+        assert torch.allclose(out[b], ref, atol=2e-2, rtol=2e-2), (b, (out[b] - ref).abs().max())
+    deq = act.q.float().view(B, -1, 32) * act.ds[:, :, 0:1]
+    assert torch.allclose(deq.view(B, -1), out, atol=out.abs().max().item() / 127 + 1e-5)
+
+
+@pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3)])
+def test_prefill_attention(D, H, Hkv):
+    from fak_b200.models.runner import PrefillMeta
+    from fak_b200.ops import kernels as K
+    qlens, pos0s = [70, 5, 130], [0, 40, 300]
+    ctx = [p + q for p, q in zip(pos0s, qlens)]
+    kc, vc, bt = _paged_cache(ctx, Hkv, D, seed=3)
+    T = sum(qlens)
+    q = torch.randn(T, H, D, device="cuda").bfloat16()
+    out = torch.zeros(T, H * D, device="cuda", dtype=torch.bfloat16)
+    meta = PrefillMeta.build(qlens, pos0s, "cuda")
+    K.prefill_attention(q, kc, vc, bt, meta, out)
+    torch.cuda.synchronize()
+    G = H // Hkv
+    off = 0
+    for s, (ql, p0) in enumerate(zip(qlens, pos0s)):
+        Kb = _gather(kc, bt[s], p0 + ql).repeat_interleave(G, 1)
+        Vb = _gather(vc, bt[s], p0 + ql).repeat_interleave(G, 1)
+        qs = q[off:off + ql].float()
+        sc = torch.einsum("qhd,thd->hqt", qs, Kb) / math.sqrt(D)
+        qpos = torch.arange(p0, p0 + ql, device="cuda")[:, None]
+        kpos = torch.arange(p0 + ql, device="cuda")[None, :]
+        sc = sc.masked_fill((kpos > qpos)[None], float("-inf"))
+        ref = torch.einsum("hqt,thd->qhd", torch.softmax(sc, -1), Vb).reshape(ql, -1)
+        got = out[off:off + ql].float()
+        assert torch.allclose(got, ref, atol=3e-2, rtol=3e-2), (s, (got - ref).abs().max())
+        off += ql
+
+
+@pytest.mark.parametrize("D,qk_norm", [(128, False), (64, True)])
+def test_rope_kv(D, qk_norm):
+    from fak_b200.models.reference import apply_rope, rmsnorm, rope_cos_sin
+    from fak_b200.models.runner import rope_tables
+    from fak_b200.ops import kernels as K
+    H, Hkv, T = 6, 2, 9
+    qkv = torch.randn(T, (H + 2 * Hkv) * D, device="cuda")
+    pos = torch.tensor([0, 1, 2, 5, 17, 100, 1000, 4095, 33], dtype=torch.int32, device="cuda")
+    slot = torch.arange(T, dtype=torch.int32, device="cuda") + 16 * 3
+    cos, sin = rope_tables(4096, D, 1e6, "cuda")
+    kc = torch.zeros(8, Hkv, 16, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    qn = torch.rand(D, device="cuda") + 0.5 if qk_norm else None
+    kn = torch.rand(D, device="cuda") + 0.5 if qk_norm else None
+    qo = torch.zeros(T, H, D, device="cuda")
+    K.rope_kv(qkv, pos, slot, cos, sin, H, Hkv, qn, kn, 1e-6, qo, None, kc, vc)
+    torch.cuda.synchronize()
+    q = qkv[:, :H * D].view(T, H, D)
+    k = qkv[:, H * D:(H + Hkv) * D].view(T, Hkv, D)
+    v = qkv[:, (H + Hkv) * D:].view(T, Hkv, D)
+    if qk_norm:
+        q, k = rmsnorm(q, qn, 1e-6), rmsnorm(k, kn, 1e-6)
+    c, s = rope_cos_sin(pos.cpu().long(), D, 1e6)
+    qr, kr = apply_rope(q.cpu(), c, s), apply_rope(k.cpu(), c, s)
+    assert torch.allclose(qo.cpu(), qr, atol=1e-4)
+    kk = kc[3].permute(1, 0, 2)[:T].float().cpu()
+    vv = vc[3].permute(1, 0, 2)[:T].float().cpu()
+    assert torch.allclose(kk, kr, atol=2e-2)
+    assert torch.allclose(vv, v.cpu(), atol=2e-2)
+
+
+def test_argmax_first_index():
+    from fak_b200.ops import kernels as K
+    x = torch.randn(3, 50000, device="cuda")
+    x[1, 7] = 100.0
+    x[1, 9] = 100.0
+    out = torch.zeros(3, dtype=torch.int32, device="cuda")
+    K.argmax(x, 50000, out)
+    assert out.tolist() == torch.argmax(x, -1).tolist()
+    assert out[1].item() == 7
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 256, 128), (200, 512, 576), (1280, 4608, 3584), (77, 250, 1536)])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_tcgen05(M, N, K, epi):
+    from fak_b200.ops import kernels as Kn
+    torch.manual_seed(M + N + K)
+    a = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    bias = torch.randn(N, device="cuda") * 0.1
+    ref = a.float() @ b.float().T + bias
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    if epi == 2:
+        ref = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+        out = torch.zeros(M, N // 2, device="cuda")
+    else:
+        out = torch.randn(M, N, device="cuda")
+        if epi == 1:
+            ref = ref + out
+    Kn.gemm(a, b, out, epi, bias, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert torch.allclose(out, ref, atol=2e-3 * math.sqrt(K), rtol=1e-2), (out - ref).abs().max()
