@@ -1,0 +1,61 @@
+"""Bandwidth of the quantized decode GEMV kernels on one weight matrix (CUDA events, L2 > working set).
+
+    python -m fak_b200.benchmarks.gemvbench --rows 37888 --cols 3584 --qtype 12 --batch 5
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--rows", type=int, default=37888)
+    ap.add_argument("--cols", type=int, default=3584)
+    ap.add_argument("--qtype", type=int, default=12)
+    ap.add_argument("--batch", type=int, default=5)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--kernel", default="qmmv", choices=["qmmv", "qgemv"])
+    ap.add_argument("--flags", type=int, default=0)
+    args = ap.parse_args(argv)
+    from fak_b200.models.weights import QuantWeight
+    from fak_b200.ops import kernels as K
+    from fak_b200.ops import quant as dq
+    from fak_b200.ops._ext import ext
+    dev = torch.device("cuda", 0)
+    # several copies so consecutive launches stream from DRAM, not L2 (126 MB)
+    n_copies = max(2, int(400e6 // (args.rows * dq.row_bytes(args.qtype, args.cols))) + 1)
+    ws = []
+    for i in range(n_copies):
+        raw = dq.synth_quantized((args.rows, args.cols), args.qtype, 1234 + i, 0.02, device="cuda")
+        ws.append(QuantWeight.from_rows(raw.view(args.rows, -1), args.qtype, args.cols, dev))
+    act = K.ActQ(8, args.cols, dev)
+    K.quant_act(torch.randn(args.batch, args.cols, device=dev), act)
+    y = torch.zeros(8, args.rows, device=dev)
+    C = ext()
+
+    def run(w):
+        if args.kernel == "qmmv":
+            C.qmmv(w.buf, w.qtype, w.rows, w.cols, w.pitch, act.q, act.ds, args.batch, y, None, 0, args.flags)
+        else:
+            C.qgemv(w.buf, w.qtype, w.rows, w.cols, w.pitch, act.q, act.ds, args.batch, y, None, 0)
+    for i in range(3):
+        run(ws[i % n_copies])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.iters):
+        run(ws[i % n_copies])
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000 / args.iters
+    nbytes = ws[0].nbytes
+    print(json.dumps({"kernel": args.kernel, "rows": args.rows, "cols": args.cols, "qtype": args.qtype,
+                      "batch": args.batch, "flags": args.flags, "us": round(us, 2),
+                      "tb_s": round(nbytes / us / 1e6, 3)}))
+
+
+if __name__ == "__main__":
+    main()

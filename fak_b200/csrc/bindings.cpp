@@ -23,6 +23,10 @@ void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Te
              torch::Tensor v_cache);
 void rmsnorm_bf16(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor y);
 void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out);
+void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, torch::Tensor qx, torch::Tensor ds,
+          int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, int64_t flags);
+void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx,
+                    torch::Tensor ds);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias, int64_t epi,
                c10::optional<torch::Tensor> err);
 
@@ -38,6 +42,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv", &rope_kv);
   m.def("rmsnorm_bf16", &rmsnorm_bf16);
   m.def("argmax_rows", &argmax_rows);
+  m.def("qmmv", &qmmv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
+        pybind11::arg("pitch"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"),
+        pybind11::arg("bias"), pybind11::arg("epi"), pybind11::arg("flags") = 0);
+  m.def("quant_act_wide", &quant_act_wide);
   m.def("gemm_bf16", &gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"),
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("epi") = 0, pybind11::arg("err") = pybind11::none());
 }

@@ -55,6 +55,11 @@ FAK_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_depen
 
 FAK_DEV int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// Exact int -> float for |c| < 2^22 without the (low-throughput) conversion pipe: adding c to
+// the bit pattern of 1.5 * 2^23 gives the float 1.5 * 2^23 + c (one ulp = 1 in that binade), and
+// subtracting 1.5 * 2^23 is exact.  Two full-rate ALU/FMA-pipe ops instead of one I2F.
+FAK_DEV float i2f_exact22(int c) { return __int_as_float(c + 0x4B400000) - 12582912.0f; }
+
 FAK_DEV float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 FAK_DEV float bf16_bits_lo(uint32_t v) { return __uint_as_float(v << 16); }

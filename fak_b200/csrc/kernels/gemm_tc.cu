@@ -120,13 +120,14 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       if (row >= M) continue;
       const int col0 = n0 + c;
       if (epi == G_SWIGLU) {
+        // columns [col0, col0+8) are gate rows of outputs col0/2 + j, [col0+8, col0+16) the up rows
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) {
+        for (int j = 0; j < 8; j++) {
           int col = col0 + j;
-          if (col + 1 < N) {
-            float g = __uint_as_float(r[j]), u = __uint_as_float(r[j + 1]);
-            if (bias) { g += bias[col]; u += bias[col + 1]; }
-            store_val(out + (int64_t)row * ldo + (col >> 1), silu(g) * u);
+          if (col + 8 < N) {
+            float g = __uint_as_float(r[j]), u = __uint_as_float(r[j + 8]);
+            if (bias) { g += bias[col]; u += bias[col + 8]; }
+            store_val(out + (int64_t)row * ldo + (col0 >> 1) + j, silu(g) * u);
           }
         }
       } else {
@@ -205,7 +206,7 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& 
 }  // namespace
 
 // out (op)= a[M,K] . b[N,K]^T ; a, b bf16 K-major (row stride multiple of 8 elements, 16B-aligned base).
-// epi: 0 store, 1 add into out, 2 SwiGLU over interleaved (gate, up) columns -> out[:, N/2].
+// epi: 0 store, 1 add into out, 2 SwiGLU over 8-column interleaved (gate x8, up x8) blocks -> out[:, N/2].
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias, int64_t epi,
                c10::optional<torch::Tensor> err) {
   TORCH_CHECK(a.is_cuda() && a.scalar_type() == torch::kBFloat16 && a.dim() == 2 && a.stride(1) == 1, "a: [M,K] bf16");
@@ -217,7 +218,7 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out: [M, *] row-major");
   const int64_t M = a.size(0), N = b.size(0);
   TORCH_CHECK(out.size(0) >= M && out.size(1) >= (epi == G_SWIGLU ? N / 2 : N), "out too small");
-  if (epi == G_SWIGLU) TORCH_CHECK(N % 2 == 0, "SwiGLU needs an even N");
+  if (epi == G_SWIGLU) TORCH_CHECK(N % 16 == 0, "SwiGLU needs 8-column interleaved gate/up blocks");
   if (M == 0 || N == 0) return;
   const float* bp = nullptr;
   if (bias.has_value()) {

@@ -94,7 +94,7 @@ FAK_DEV float dot_q4k(const WUnitQ4K& wu, const XUnit& xu) {
     s0 = dp4a((int)wu.q[i], xu.w[i], s0);
     s1 = dp4a((int)wu.q[8 + i], xu.w[8 + i], s1);
   }
-  return wu.ds0 * xu.ds.x * (float)s0 + wu.ds1 * xu.ds.z * (float)s1 - wu.mn0 * xu.ds.y - wu.mn1 * xu.ds.w;
+  return wu.ds0 * xu.ds.x * i2f_exact22(s0) + wu.ds1 * xu.ds.z * i2f_exact22(s1) - wu.mn0 * xu.ds.y - wu.mn1 * xu.ds.w;
 }
 
 struct WUnitQ8 {
@@ -122,7 +122,7 @@ FAK_DEV float dot_q8(const WUnitQ8& wu, const XUnit& xu) {
     s0 = dp4a((int)wu.q[i], xu.w[i], s0);
     s1 = dp4a((int)wu.q[8 + i], xu.w[8 + i], s1);
   }
-  return wu.d0 * xu.ds.x * (float)s0 + wu.d1 * xu.ds.z * (float)s1;
+  return wu.d0 * xu.ds.x * i2f_exact22(s0) + wu.d1 * xu.ds.z * i2f_exact22(s1);
 }
 
 struct WUnitQ6K {
@@ -185,8 +185,8 @@ FAK_DEV float dot_q6k(const WUnitQ6K& wu, const XUnit& xu) {
     b0 = dp4a((int)wu.q[8 + i], xu.w[8 + i], b0);
     b1 = dp4a((int)wu.q[12 + i], xu.w[12 + i], b1);
   }
-  return xu.ds.x * (wu.sc[0] * (float)a0 + wu.sc[1] * (float)a1) +
-         xu.ds.z * (wu.sc[2] * (float)b0 + wu.sc[3] * (float)b1);
+  return xu.ds.x * (wu.sc[0] * i2f_exact22(a0) + wu.sc[1] * i2f_exact22(a1)) +
+         xu.ds.z * (wu.sc[2] * i2f_exact22(b0) + wu.sc[3] * i2f_exact22(b1));
 }
 
 // x-block offsets (in elements, relative to the row start of x) of the two 32-blocks a unit covers
@@ -345,7 +345,7 @@ void qgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, 
     TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "qgemv: bias");
     bp = bias->data_ptr<float>();
   }
-  if (epi == EPI_SWIGLU) TORCH_CHECK(N % 2 == 0, "qgemv: SwiGLU needs interleaved (gate, up) rows");
+  TORCH_CHECK(epi != EPI_SWIGLU, "qgemv: the SwiGLU epilogue lives in qmmv (8-row interleaved gate/up tiles)");
   auto stream = at::cuda::getCurrentCUDAStream();
   // rows per warp: 4 when that still gives ~2 CTAs per SM, else 2
   int RW = (N / (4 * GEMV_WARPS) >= 296) ? 4 : 2;

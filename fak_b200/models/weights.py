@@ -5,8 +5,8 @@ pitch (``ops.quant.row_pitch``) so every row starts on a 16-byte boundary for wi
 asynchronous loads.  Row permutations are exact on quantized rows, which the loader uses to
 
 * fuse q/k/v into one matrix when their block types match (one GEMV launch);
-* interleave gate/up rows (row 2i = gate_i, row 2i+1 = up_i) so the GEMV epilogue can apply
-  SwiGLU without a second pass (reference fused-op boundary: SwiGLUMatMulAddInPlace,
+* interleave gate/up rows in blocks of 8 (``interleave_gate_up``) so the GEMV/GEMM epilogues
+  can apply SwiGLU without a second pass (reference fused-op boundary: SwiGLUMatMulAddInPlace,
   internal/model/hal.go:204-255);
 * restore HF rotary row order for GGML "llama" checkpoints (done in ``models.loader``).
 
@@ -48,7 +48,8 @@ class QuantWeight:
         if rows_u8.shape[1] != packed:
             raise ValueError(f"row bytes {rows_u8.shape[1]} != expected {packed} for {GGMLType(qtype).name}x{cols}")
         pitch = dq.row_pitch(qtype, cols)
-        buf = torch.zeros(rows * pitch + 64, dtype=torch.uint8, device=device)
+        # slack: tile copies may read up to one pitch past the last row
+        buf = torch.zeros(rows * pitch + pitch + 256, dtype=torch.uint8, device=device)
         src = rows_u8.to(device, non_blocking=False)
         buf[: rows * pitch].view(rows, pitch)[:, :packed].copy_(src)
         return cls(buf, int(qtype), rows, int(cols), pitch)
@@ -216,6 +217,20 @@ def ffn_assignment(ffn: int, tp_rank: int, tp_size: int, granule: int) -> tuple[
     return start * granule, (start + n) * granule
 
 
+def interleave_gate_up(g_rows: torch.Tensor, u_rows: torch.Tensor, block: int = 8) -> torch.Tensor:
+    """Rows [16i, 16i+8) = gate rows [8i, 8i+8), rows [16i+8, 16i+16) = up rows [8i, 8i+8).
+
+    The GEMV and GEMM SwiGLU epilogues rely on this layout: a 16-row MMA tile (or a
+    16-column accumulator chunk) then holds matching gate and up values in the same thread.
+    """
+    n = g_rows.shape[0]
+    if n % block or u_rows.shape[0] != n:
+        raise ValueError(f"gate/up rows ({n}) must be a multiple of {block}")
+    g = g_rows.reshape(n // block, block, -1)
+    u = u_rows.reshape(n // block, block, -1)
+    return torch.stack([g, u], dim=1).reshape(2 * n, -1)
+
+
 def _rows_of(raw: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
     return raw.index_select(0, idx.to(raw.device))
 
@@ -301,8 +316,7 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
             us, ut, uraw = quant(p + "ffn_up.weight")
             if gt != ut:
                 raise ValueError(f"layer {i}: gate ({gt}) and up ({ut}) block types differ")
-            g_rows, u_rows = graw[f0:f1], uraw[f0:f1]
-            inter = torch.stack([g_rows, u_rows], dim=1).reshape(2 * (f1 - f0), -1)
+            inter = interleave_gate_up(graw[f0:f1], uraw[f0:f1])
             L.gate_up = QuantWeight.from_rows(inter, gt, cfg.d_model, device)
             ds_, dt, draw = quant(p + "ffn_down.weight")
             if tp_size > 1:
@@ -341,6 +355,6 @@ def _load_moe_layer(cfg, get, quant, p, L: LayerWeights, device, expert_filter) 
     draw = draw.view(E, d, -1)
     L.experts_gate_up, L.experts_down, L.expert_ids = [], [], keep
     for e in keep:
-        inter = torch.stack([graw[e], uraw[e]], dim=1).reshape(2 * f, -1)
+        inter = interleave_gate_up(graw[e], uraw[e])
         L.experts_gate_up.append(QuantWeight.from_rows(inter, gt, d, device))
         L.experts_down.append(QuantWeight.from_rows(draw[e].contiguous(), dt, f, device))

@@ -34,18 +34,25 @@ class ActQ:
 
 
 def quant_act(x: torch.Tensor, act: ActQ, gamma: torch.Tensor | None = None, eps: float = 1e-6) -> None:
-    ext().quant_act(x, gamma, eps, act.q, act.ds)
+    ext().quant_act_wide(x, gamma, eps, act.q, act.ds)
     count()
 
 
+# below this many tokens the CUDA-core dp4a GEMV is cheaper than the int8 MMA tile kernel
+DP4A_MAX_B = 1
+
+
 def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None, epi: int = EPI_STORE) -> None:
-    """y[:B] (op)= W . x for B <= 8 tokens (w: models.weights.QuantWeight)."""
+    """y[:B] (op)= W . x for a decode batch (w: models.weights.QuantWeight); chunks of 8 tokens."""
     C = ext()
     for b0 in range(0, B, GEMV_MAX_B):
         nb = min(GEMV_MAX_B, B - b0)
         q = act.q[b0:b0 + nb]
         d = act.ds[b0:b0 + nb]
-        C.qgemv(w.buf, w.qtype, w.rows, w.cols, w.pitch, q, d, nb, y[b0:b0 + nb], bias, epi)
+        if nb <= DP4A_MAX_B and epi != EPI_SWIGLU:
+            C.qgemv(w.buf, w.qtype, w.rows, w.cols, w.pitch, q, d, nb, y[b0:b0 + nb], bias, epi)
+        else:
+            C.qmmv(w.buf, w.qtype, w.rows, w.cols, w.pitch, q, d, nb, y[b0:b0 + nb], bias, epi)
         count()
 
 

@@ -18,8 +18,13 @@ def row_bytes(qtype: int, cols: int) -> int:
 
 
 def row_pitch(qtype: int, cols: int) -> int:
-    """Row stride on the device: the packed row rounded up to 16 bytes (blocks stay unchanged)."""
-    return (row_bytes(qtype, cols) + 15) // 16 * 16
+    """Row stride on the device (blocks stay unchanged): the packed row rounded up to 16 bytes and
+    then to 16 mod 128, so a 16-row tile copied as one contiguous span lands in shared memory with
+    consecutive rows on different banks."""
+    p = (row_bytes(qtype, cols) + 15) // 16 * 16
+    while p % 128 != 16:
+        p += 16
+    return p
 
 
 def quantize_blocks(x: torch.Tensor, qtype: int) -> torch.Tensor:

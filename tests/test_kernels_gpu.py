@@ -19,6 +19,13 @@ def _ext():
     return ext()
 
 
+def _swiglu_ref(y):
+    """SwiGLU over 8-row interleaved (gate x8, up x8) blocks of the output dim."""
+    M, N = y.shape
+    blocks = y.view(M, N // 16, 2, 8)
+    return (torch.nn.functional.silu(blocks[:, :, 0]) * blocks[:, :, 1]).reshape(M, N // 2)
+
+
 @pytest.mark.parametrize("qt,blk", QTYPES)
 def test_quantize_matches_numpy_bitexact(qt, blk):
     rng = np.random.default_rng(1)
@@ -70,7 +77,7 @@ def test_qgemv(qt, blk, B, epi):
     bias = torch.randn(N, device="cuda") * 0.1
     ref = x @ Wd.T + bias
     if epi == K.EPI_SWIGLU:
-        ref = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+        ref = _swiglu_ref(ref)
         y = torch.zeros(B, N // 2, device="cuda")
     else:
         y = torch.randn(B, N, device="cuda")
@@ -215,7 +222,7 @@ def test_argmax_first_index():
     assert out[1].item() == 7
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 256, 128), (200, 512, 576), (1280, 4608, 3584), (77, 250, 1536)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 256, 128), (200, 512, 576), (1280, 4608, 3584), (77, 240, 1536)])
 @pytest.mark.parametrize("epi", [0, 1, 2])
 def test_gemm_tcgen05(M, N, K, epi):
     from fak_b200.ops import kernels as Kn
@@ -226,7 +233,7 @@ def test_gemm_tcgen05(M, N, K, epi):
     ref = a.float() @ b.float().T + bias
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     if epi == 2:
-        ref = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+        ref = _swiglu_ref(ref)
         out = torch.zeros(M, N // 2, device="cuda")
     else:
         out = torch.randn(M, N, device="cuda")
