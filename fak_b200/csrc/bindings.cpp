@@ -10,7 +10,7 @@ void qgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, 
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
-                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace);
+                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo);
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
                        torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out);
@@ -27,6 +27,14 @@ void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, t
           int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, int64_t flags);
 void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx,
                     torch::Tensor ds);
+void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
+                        int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
+                        torch::Tensor counters, torch::Tensor err, int64_t ctas);
+void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, int64_t n, int64_t flags_off,
+                       int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas);
+void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
+                torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
+                torch::Tensor err);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias, int64_t epi,
                c10::optional<torch::Tensor> err);
 
@@ -36,12 +44,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequantize_rows", &dequantize_rows);
   m.def("quant_act", &quant_act);
   m.def("qgemv", &qgemv);
-  m.def("decode_attention", &decode_attention);
+  m.def("decode_attention", &decode_attention, pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"),
+        pybind11::arg("block_table"), pybind11::arg("ctx_len"), pybind11::arg("n_split"),
+        pybind11::arg("pages_per_split"), pybind11::arg("out"), pybind11::arg("qx"), pybind11::arg("ds"),
+        pybind11::arg("workspace"), pybind11::arg("ldo") = 0);
   m.def("prefill_attention", &prefill_attention);
   m.def("embed", &embed);
   m.def("rope_kv", &rope_kv);
   m.def("rmsnorm_bf16", &rmsnorm_bf16);
   m.def("argmax_rows", &argmax_rows);
+  m.def("p2p_allgather_cols", &p2p_allgather_cols);
+  m.def("p2p_allreduce_add", &p2p_allreduce_add);
+  m.def("p2p_argmax", &p2p_argmax);
   m.def("qmmv", &qmmv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
         pybind11::arg("pitch"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"),
         pybind11::arg("bias"), pybind11::arg("epi"), pybind11::arg("flags") = 0);

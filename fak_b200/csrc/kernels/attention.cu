@@ -63,7 +63,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
               const int* __restrict__ block_table, int bt_stride, const int* __restrict__ ctx_len, int H, int Hkv,
               int n_split, int pages_per_split, float scale_log2, float* __restrict__ part_o,
               float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
-              float2* __restrict__ ds) {
+              float2* __restrict__ ds, int ldo) {
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -235,7 +235,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
       for (int w = 0; w < 4; w++) acc += f[w] * so[(w * 16 + r) * D + dd];
       if (n_split == 1) {
         float v = L > 0.f ? acc / L : 0.f;
-        int64_t oi = ((int64_t)b * H + h) * D + dd;
+        int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
         if (out) out[oi] = v;
         if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), lane);
       } else {
@@ -250,7 +250,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
 template <int D>
 __global__ void __launch_bounds__(D)
 k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int H, int n_split,
-                 float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds) {
+                 float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds, int ldo) {
   pdl_wait();
   const int b = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
   const int64_t base = ((int64_t)b * H + h) * n_split;
@@ -266,7 +266,7 @@ k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ pa
   }
   pdl_launch_dependents();
   float v = L > 0.f ? acc / L : 0.f;
-  int64_t oi = ((int64_t)b * H + h) * D + dd;
+  int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
   if (out) out[oi] = v;
   if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), dd & 31);
 }
@@ -455,7 +455,7 @@ void set_pdl(cudaLaunchConfig_t& cfg) {
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
-                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace) {
+                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
   TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
   TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(), "v_cache");
@@ -470,8 +470,11 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   float* op = out.has_value() ? out->data_ptr<float>() : nullptr;
   int8_t* qp = qx.has_value() ? qx->data_ptr<int8_t>() : nullptr;
   float2* dp = ds.has_value() ? reinterpret_cast<float2*>(ds->data_ptr<float>()) : nullptr;
-  if (qp) TORCH_CHECK(dp && qx->numel() >= (int64_t)B * H * D && ds->numel() >= (int64_t)B * H * D / 16, "qx/ds size");
-  if (op) TORCH_CHECK(out->numel() >= (int64_t)B * H * D && out->is_contiguous(), "out");
+  if (ldo <= 0) ldo = (int64_t)H * D;  // elements per token row of out / qx
+  TORCH_CHECK(ldo >= (int64_t)H * D && ldo % 32 == 0, "decode_attention: output row stride");
+  const int64_t need = (int64_t)(B - 1) * ldo + (int64_t)H * D;  // last element written + 1
+  if (qp) TORCH_CHECK(dp && qx->numel() >= need && ds->numel() >= need / 16, "qx/ds size");
+  if (op) TORCH_CHECK(out->numel() >= need && out->is_contiguous(), "out");
   float* pw = nullptr;
   if (n_split > 1) {
     TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == torch::kFloat32 &&
@@ -495,7 +498,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<128>, (const float*)q.data_ptr<float>(),
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp));
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo));
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -503,7 +506,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<64>, (const float*)q.data_ptr<float>(),
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp));
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo));
   }
   if (n_split > 1) {
     cudaLaunchConfig_t c2 = {};
@@ -513,10 +516,10 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     set_pdl(c2);
     if (D == 128)
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H,
-                                        (int)n_split, op, qp, dp));
+                                        (int)n_split, op, qp, dp, (int)ldo));
     else
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H,
-                                        (int)n_split, op, qp, dp));
+                                        (int)n_split, op, qp, dp, (int)ldo));
   }
 }
 

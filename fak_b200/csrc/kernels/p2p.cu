@@ -1,0 +1,232 @@
+// In-kernel collectives over NVLink/NVSwitch peer memory for tensor-parallel decode.
+//
+// Every rank owns one symmetric buffer (same size and layout on all ranks, mapped into every
+// peer's address space); kernels get the device array of the W peer base pointers.  Data moves
+// with plain stores/loads to peer addresses; completion is signalled with flags in the same
+// buffers:
+//
+//   flags region: uint32 [n_sites][MAX_CTAS][W]   (slot [site][cta][src] on the receiving rank)
+//   a rank's CTA c publishes epoch e for site s by storing e (release, system scope) into
+//   flags[s][c][me] of every peer, then waits (acquire, system scope) until its own
+//   flags[s][c][r] >= e for every r.  Epochs come from a per-(site, cta) counter in local
+//   memory, incremented by the kernel itself, so the kernels replay correctly inside CUDA graphs.
+//
+// Every wait is bounded: after kSpinLimit polls the kernel records error code 1 in `err` and
+// continues, so a missing peer produces an error status on the host instead of a hung GPU.
+// No TMA or multicast loads are used here; peer memory is only touched by ordinary ld/st.
+//
+// Reference counterpart: the NCCL AllReduce/AllGather of internal/compute/cuda_nccl.cu:72-134 and
+// the host-staged collective bridge internal/model/collective_bridge.go:103-120.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include "common.cuh"
+
+using namespace fak;
+
+namespace {
+
+constexpr int MAX_W = 8;
+constexpr int MAX_CTAS = 64;
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+FAK_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+FAK_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct Peers {
+  uint8_t* base[MAX_W];  // symmetric buffer base of every rank
+};
+
+// Cross-rank barrier for CTA `cta` at `site`: all threads of the CTA call it; prior writes of the
+// CTA (to any rank) are visible to the peers once they pass it.
+FAK_DEV void rank_barrier(const Peers& P, int64_t flags_off, int site, int cta, int me, int W, uint32_t* counters,
+                          int* err) {
+  __syncthreads();
+  __shared__ uint32_t epoch_s;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    epoch_s = counters[site * MAX_CTAS + cta] + 1;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_s;
+  const int64_t slot = ((int64_t)site * MAX_CTAS + cta) * MAX_W;
+  if (threadIdx.x < W) {
+    uint32_t* peer_flag = reinterpret_cast<uint32_t*>(P.base[threadIdx.x] + flags_off) + slot + me;
+    st_release_sys(peer_flag, epoch);
+  }
+  if (threadIdx.x < W) {
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(P.base[me] + flags_off) + slot + threadIdx.x;
+    uint32_t i = 0;
+    while (ld_acquire_sys(mine) < epoch) {
+      if (++i > kSpinLimit) {
+        report_error(err, 1);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) counters[site * MAX_CTAS + cta] = epoch;
+}
+
+// ---- all-gather of per-rank column blocks of a [B, row_bytes] byte matrix ------------------
+// Rank `me` owns bytes [col0, col0 + ncols) of every row (in both the source and destination
+// layout); it copies them from its local source into the same position of every rank's buffer.
+__global__ void k_p2p_allgather_cols(Peers P, const uint8_t* __restrict__ src, int64_t src_ld, int64_t dst_off,
+                                     int64_t dst_ld, int64_t col0, int64_t ncols, int B, int64_t flags_off, int site,
+                                     int me, int W, uint32_t* counters, int* err) {
+  pdl_wait();
+  const int64_t chunks = ncols >> 4;  // 16-byte chunks per row
+  const int64_t total = (int64_t)B * chunks;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / chunks, c = i - b * chunks;
+    const uint4 v = *reinterpret_cast<const uint4*>(src + b * src_ld + col0 + 16 * c);
+    for (int r = 0; r < W; r++)
+      *reinterpret_cast<uint4*>(P.base[r] + dst_off + b * dst_ld + col0 + 16 * c) = v;
+  }
+  rank_barrier(P, flags_off, site, blockIdx.x, me, W, counters, err);
+  pdl_launch_dependents();
+}
+
+// ---- one-shot all-reduce of fp32 partials, added into x ------------------------------------
+// Every rank wrote its partial [n] into its own buffer at part_off; each element of x gets
+// sum_r part_r (summed in rank order, so every rank computes bit-identical values).
+__global__ void k_p2p_allreduce_add(Peers P, int64_t part_off, float* __restrict__ x, int64_t n, int64_t flags_off,
+                                    int site, int me, int W, uint32_t* counters, int* err) {
+  pdl_wait();
+  rank_barrier(P, flags_off, site, blockIdx.x, me, W, counters, err);
+  const int64_t n4 = n >> 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < W; r++) {
+      const float4 v = *reinterpret_cast<const float4*>(P.base[r] + part_off + 16 * i);
+      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    }
+    float4 xv = reinterpret_cast<float4*>(x)[i];
+    xv.x += s.x; xv.y += s.y; xv.z += s.z; xv.w += s.w;
+    reinterpret_cast<float4*>(x)[i] = xv;
+  }
+  pdl_launch_dependents();
+}
+
+// ---- greedy sampling over vocab-sharded logits ---------------------------------------------
+// CTA b: first-index argmax of row b of the local logits slice, published as (value, global id)
+// to every rank; after the barrier every rank reduces the W candidates in rank order.
+__global__ void k_p2p_argmax(Peers P, const float* __restrict__ logits, int64_t ld, int Vl, int64_t v_off,
+                             int64_t cand_off, int* __restrict__ out, int64_t flags_off, int site, int me, int W,
+                             uint32_t* counters, int* err) {
+  pdl_wait();
+  const int b = blockIdx.x;
+  const float* x = logits + (int64_t)b * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < Vl; i += blockDim.x) {
+    float v = x[i];
+    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nw = blockDim.x >> 5;
+    for (int w = 1; w < nw; w++)
+      if (sv[w] > sv[0] || (sv[w] == sv[0] && si[w] < si[0])) { sv[0] = sv[w]; si[0] = si[w]; }
+    const int64_t gid = si[0] == 0x7fffffff ? 0x7fffffff : (int64_t)si[0] + v_off;
+    for (int r = 0; r < W; r++) {
+      float2* cand = reinterpret_cast<float2*>(P.base[r] + cand_off) + (int64_t)b * MAX_W + me;
+      *cand = make_float2(sv[0], __int_as_float((int)gid));
+    }
+  }
+  rank_barrier(P, flags_off, site, b, me, W, counters, err);
+  if (threadIdx.x == 0) {
+    const float2* cand = reinterpret_cast<const float2*>(P.base[me] + cand_off) + (int64_t)b * MAX_W;
+    float bv = -INFINITY;
+    int bidx = 0x7fffffff;
+    for (int r = 0; r < W; r++) {
+      const float2 c = cand[r];
+      const int ci = __float_as_int(c.y);
+      if (c.x > bv || (c.x == bv && ci < bidx)) { bv = c.x; bidx = ci; }
+    }
+    out[b] = bidx == 0x7fffffff ? 0 : bidx;
+  }
+  pdl_launch_dependents();
+}
+
+Peers make_peers(torch::Tensor ptrs) {
+  TORCH_CHECK(ptrs.scalar_type() == torch::kInt64 && ptrs.numel() <= MAX_W, "peer pointer table");
+  auto h = ptrs.cpu();
+  Peers P{};
+  for (int i = 0; i < ptrs.numel(); i++) P.base[i] = reinterpret_cast<uint8_t*>(h.data_ptr<int64_t>()[i]);
+  return P;
+}
+
+cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+}  // namespace
+
+// peers: int64 [W] host tensor of symmetric buffer bases; counters: int32 [n_sites*64] local
+// device tensor (zero-initialised once); err: int32 [1] device.
+void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
+                        int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
+                        torch::Tensor counters, torch::Tensor err, int64_t ctas) {
+  const int W = (int)peers.numel();
+  TORCH_CHECK(ncols % 16 == 0 && col0 % 16 == 0 && src_ld % 16 == 0 && dst_ld % 16 == 0 && dst_off % 16 == 0,
+              "allgather: 16-byte granularity");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allgather: 1..64 CTAs");
+  Peers P = make_peers(peers);
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_allgather_cols, P, (const uint8_t*)src.data_ptr(), src_ld, dst_off,
+                                    dst_ld, col0, ncols, (int)B, flags_off, (int)site, (int)me, W,
+                                    (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>()));
+}
+
+void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, int64_t n, int64_t flags_off,
+                       int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas) {
+  const int W = (int)peers.numel();
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.numel() >= n && n % 4 == 0, "x");
+  TORCH_CHECK(part_off % 16 == 0, "partials must be 16-byte aligned");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allreduce: 1..64 CTAs");
+  Peers P = make_peers(peers);
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_allreduce_add, P, part_off, x.data_ptr<float>(), n, flags_off,
+                                    (int)site, (int)me, W, (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>()));
+}
+
+void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
+                torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
+                torch::Tensor err) {
+  const int W = (int)peers.numel();
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.stride(1) == 1, "logits");
+  TORCH_CHECK(B >= 1 && B <= MAX_CTAS, "argmax: batch 1..64");
+  Peers P = make_peers(peers);
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_cfg(dim3((unsigned)B), dim3(1024), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_argmax, P, (const float*)logits.data_ptr<float>(),
+                                    (int64_t)logits.stride(0), (int)Vl, v_off, cand_off, out.data_ptr<int>(),
+                                    flags_off, (int)site, (int)me, W, (uint32_t*)counters.data_ptr<int>(),
+                                    err.data_ptr<int>()));
+}

@@ -79,8 +79,12 @@ class Engine:
         self.pool = PagePool(n_pages, reserve=1)
         self.radix = RadixCache(self.pool, ps) if self.ecfg.radix_cache else None
         if collectives is None and tp_group is not None and weights.tp_size > 1:
-            from ..parallel.tp import NcclTP
-            collectives = NcclTP(tp_group, weights, self.ecfg.max_batch, self.device)
+            if self.ecfg.fused_collectives:
+                from ..parallel.p2p import P2PTP
+                collectives = P2PTP(tp_group, weights, self.ecfg.max_batch, self.device)
+            else:
+                from ..parallel.tp import NcclTP
+                collectives = NcclTP(tp_group, weights, self.ecfg.max_batch, self.device)
         self.tp_group = tp_group
         self.runner = ModelRunner(weights, self.kv, max_batch=self.ecfg.max_batch,
                                   max_prefill_tokens=self.ecfg.max_prefill_tokens, max_context=self.max_context,
@@ -111,9 +115,9 @@ class Engine:
 
     @classmethod
     def synthetic(cls, cfg: ModelConfig, mix: str = "q4_k_m", seed: int = 0, ecfg: EngineConfig | None = None,
-                  device="cuda", tp_group=None, **kw) -> "Engine":
+                  device="cuda", tp_group=None, std: float = 0.02, **kw) -> "Engine":
         r, n = cls._tp(tp_group)
-        w = load_weights(synthetic_source(cfg, mix, seed, device=str(device)), device, tp_rank=r, tp_size=n,
+        w = load_weights(synthetic_source(cfg, mix, seed, std=std, device=str(device)), device, tp_rank=r, tp_size=n,
                          prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 

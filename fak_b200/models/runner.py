@@ -110,7 +110,7 @@ class ModelRunner:
         self.act_d = K.ActQ(B, d, dev)
         self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
-        self.logits = torch.zeros(B, weights.lm_head.rows, dtype=torch.float32, device=dev)
+        self.logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
         self.next_ids = torch.zeros(B, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.max_split = 64
@@ -161,6 +161,9 @@ class ModelRunner:
         for i in range(cfg.n_layers):
             self._layer_decode(i, B, pos, slot, bt, ctx, n_split)
         K.quant_act(self.x[:B], self.act_d, self.w.final_norm, cfg.rms_eps)
+        if greedy and self.coll is not None and hasattr(self.coll, "lm_head_greedy"):
+            self.coll.lm_head_greedy(self, B)  # sharded logits -> distributed argmax, no logits gather
+            return
         self._lm_head(B)
         if greedy:
             K.argmax(self.logits[:B], self.logits.shape[1], self.next_ids[:B])
@@ -266,7 +269,7 @@ class ModelRunner:
                 self.coll.prefill_down(self, i, hb2, x)
         S = last_idx.numel()
         xl = x.index_select(0, last_idx.long())
-        logits = torch.empty(S, self.w.lm_head.rows, dtype=torch.float32, device=dev)
+        logits = torch.empty(S, cfg.vocab_size, dtype=torch.float32, device=dev)
         for s0 in range(0, S, self.max_batch):
             s1 = min(S, s0 + self.max_batch)
             n = s1 - s0

@@ -208,6 +208,11 @@ def head_assignment(cfg: ModelConfig, tp_rank: int, tp_size: int) -> tuple[list[
     return [k * G + start + i for i in range(n)], [k]
 
 
+def vocab_slice(V: int, tp_rank: int, tp_size: int) -> tuple[int, int]:
+    per = -(-V // tp_size)
+    return min(V, tp_rank * per), min(V, (tp_rank + 1) * per)
+
+
 def ffn_assignment(ffn: int, tp_rank: int, tp_size: int, granule: int) -> tuple[int, int]:
     """[start, end) of the FFN dim on a rank, in whole ``granule`` units (a K-quant super-block)."""
     units = ffn // granule
@@ -331,14 +336,13 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
                 L.down.dense()
         layers.append(L)
     final_norm = _vec(get, "output_norm.weight", device)
-    if cfg.tie_embeddings:
+    # lm_head: split by vocab rows under TP (ceil(V/T) rows per rank, the last rank may hold fewer)
+    v0, v1 = vocab_slice(cfg.vocab_size, tp_rank, tp_size)
+    if cfg.tie_embeddings and tp_size == 1 and emb_t in dq.DEVICE_QTYPES:
         lm_head = embed
-        if emb_t not in dq.DEVICE_QTYPES:
-            shape, t, raw = quant("token_embd.weight")
-            lm_head = QuantWeight.from_rows(raw, t, shape[1], device)
     else:
-        shape, t, raw = quant("output.weight")
-        lm_head = QuantWeight.from_rows(raw, t, shape[1], device)
+        shape, t, raw = quant("token_embd.weight" if cfg.tie_embeddings else "output.weight")
+        lm_head = QuantWeight.from_rows(raw[v0:v1].contiguous(), t, shape[1], device)
     close()
     return ModelWeights(cfg, embed, layers, final_norm, lm_head, q_heads, kv_heads, (f0, f1), tp_rank, tp_size)
 

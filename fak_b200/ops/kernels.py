@@ -57,9 +57,10 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 
 
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
-                     workspace=None) -> None:
+                     workspace=None, ldo: int = 0) -> None:
+    """ldo: elements per token row of the output (default: heads x head_dim)."""
     ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
-                           act.q if act is not None else None, act.ds if act is not None else None, workspace)
+                           act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo)
     count(2 if n_split > 1 else 1)
 
 

@@ -47,21 +47,25 @@ class NcclTP:
         self.Hq_local = len(owners[self.rank])
         B = max_batch
         self.act_local = K.ActQ(B, self.maxHq * D, device)
-        self.recv_q = torch.zeros(self.world, B, self.maxHq * D, dtype=torch.int8, device=device)
-        self.recv_ds = torch.zeros(self.world, B, self.maxHq * D // 32, 2, dtype=torch.float32, device=device)
+        # gather targets are flat: [world, b, ...] views of their first world*b rows stay contiguous
+        self.recv_q = torch.zeros(self.world * B * self.maxHq * D, dtype=torch.int8, device=device)
+        self.recv_ds = torch.zeros(self.world * B * self.maxHq * D // 16, dtype=torch.float32, device=device)
         self.tmp = torch.zeros(B, cfg.d_model, dtype=torch.float32, device=device)
-        self.Vl = weights.lm_head.rows
-        self.logits_local = torch.zeros(B, self.Vl, dtype=torch.float32, device=device)
-        self.logits_all = torch.zeros(self.world, B, self.Vl, dtype=torch.float32, device=device)
+        # every rank gathers ceil(V/T) logits (ranks with fewer real rows pad with -inf)
+        self.Vl = -(-cfg.vocab_size // self.world)
+        self.Vl_real = weights.lm_head.rows
+        self.logits_local = torch.full((B, self.Vl), float("-inf"), dtype=torch.float32, device=device)
+        self.logits_all = torch.zeros(self.world * B * self.Vl, dtype=torch.float32, device=device)
 
     # ---------------------------------------------------------------------------------
     def _gather_heads_q(self, B: int, act_dst) -> None:
-        D, H = self.D, self.cfg.n_heads
-        dist.all_gather_into_tensor(self.recv_q[:, :B].reshape(-1), self.act_local.q[:B].reshape(-1), group=self.group)
-        dist.all_gather_into_tensor(self.recv_ds[:, :B].reshape(-1), self.act_local.ds[:B].reshape(-1),
-                                    group=self.group)
-        q = self.recv_q[:, :B].view(self.world, B, self.maxHq, D).permute(1, 0, 2, 3).reshape(B, -1, D)
-        ds = self.recv_ds[:, :B].view(self.world, B, self.maxHq, D // 32, 2).permute(1, 0, 2, 3, 4)
+        D, H, Wd = self.D, self.cfg.n_heads, self.world
+        rq = self.recv_q[:Wd * B * self.maxHq * D]
+        rd = self.recv_ds[:Wd * B * self.maxHq * D // 16]
+        dist.all_gather_into_tensor(rq, self.act_local.q[:B].reshape(-1), group=self.group)
+        dist.all_gather_into_tensor(rd, self.act_local.ds[:B].reshape(-1), group=self.group)
+        q = rq.view(Wd, B, self.maxHq, D).permute(1, 0, 2, 3).reshape(B, -1, D)
+        ds = rd.view(Wd, B, self.maxHq, D // 32, 2).permute(1, 0, 2, 3, 4)
         ds = ds.reshape(B, -1, D // 32, 2)
         act_dst.q[:B].view(B, H, D).copy_(q.index_select(1, self.head_slot))
         act_dst.ds[:B].view(B, H, D // 32, 2).copy_(ds.index_select(1, self.head_slot))
@@ -71,7 +75,8 @@ class NcclTP:
         if self.Hq_local < self.maxHq:  # pad slots of ranks with fewer heads stay zero
             self.act_local.q[:B].zero_()
             self.act_local.ds[:B].zero_()
-        K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_local, workspace=rn.attn_ws)
+        K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_local, workspace=rn.attn_ws,
+                           ldo=self.maxHq * self.D)
         self._gather_heads_q(B, rn.act_attn)
         K.gemv(rn.w.layers[i].o, rn.act_attn, B, rn.x[:B], None, K.EPI_ADD)
 
@@ -82,18 +87,18 @@ class NcclTP:
         rn.x[:B].add_(t)
 
     def _gather_logits(self, B: int, out: torch.Tensor) -> None:
-        dist.all_gather_into_tensor(self.logits_all[:, :B].reshape(-1), self.logits_local[:B].reshape(-1),
-                                    group=self.group)
+        la = self.logits_all[:self.world * B * self.Vl]
+        dist.all_gather_into_tensor(la, self.logits_local[:B].reshape(-1), group=self.group)
         V = out.shape[1]
-        full = self.logits_all[:, :B].permute(1, 0, 2).reshape(B, -1)
+        full = la.view(self.world, B, self.Vl).permute(1, 0, 2).reshape(B, -1)
         out[:B].copy_(full[:, :V])
 
     def lm_head(self, rn, B: int) -> None:
-        K.gemv(rn.w.lm_head, rn.act_d, B, self.logits_local[:B], None, K.EPI_STORE)
+        K.gemv(rn.w.lm_head, rn.act_d, B, self.logits_local[:B, :self.Vl_real], None, K.EPI_STORE)
         self._gather_logits(B, rn.logits)
 
     def lm_head_to(self, rn, n: int, out: torch.Tensor) -> None:
-        K.gemv(rn.w.lm_head, rn.act_d, n, self.logits_local[:n], None, K.EPI_STORE)
+        K.gemv(rn.w.lm_head, rn.act_d, n, self.logits_local[:n, :self.Vl_real], None, K.EPI_STORE)
         self._gather_logits(n, out)
 
     # ---------------------------------------------------------------------------------

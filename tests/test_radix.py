@@ -58,3 +58,25 @@ def test_radix_does_not_evict_live_pages():
     assert rc.evict(10) == 0
     pool.release(pg)
     assert rc.evict(10) == 2
+
+
+def test_tp_head_and_ffn_assignment():
+    from fak_b200.config import preset
+    from fak_b200.models.weights import ffn_assignment, head_assignment, vocab_slice
+    cfg = preset("qwen2.5-7b")
+    for T in (1, 2, 4, 8):
+        qs, kvs = [], []
+        for r in range(T):
+            q, kv = head_assignment(cfg, r, T)
+            qs += q
+            kvs.append(kv)
+            assert all(h // cfg.gqa_group in kv for h in q)  # a rank owns the KV head of each of its q heads
+        assert sorted(qs) == list(range(cfg.n_heads))
+        spans = [ffn_assignment(cfg.ffn_dim, r, T, 256) for r in range(T)]
+        assert spans[0][0] == 0 and spans[-1][1] == cfg.ffn_dim
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        assert all((b - a) % 256 == 0 for a, b in spans)
+        vs = [vocab_slice(cfg.vocab_size, r, T) for r in range(T)]
+        assert vs[-1][1] == cfg.vocab_size and sum(b - a for a, b in vs) == cfg.vocab_size
+    # TP=8 on 28 q heads / 4 KV heads: groups of 7 split 4 + 3
+    assert [len(head_assignment(cfg, r, 8)[0]) for r in range(8)] == [4, 3] * 4

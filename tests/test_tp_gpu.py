@@ -1,0 +1,27 @@
+"""Tensor-parallel decode/prefill agreement with TP=1 (needs >= 2 GPUs)."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("model", ["tiny-qwen2", "tiny-llama"])
+@pytest.mark.parametrize("fused", [1, 0])
+def test_tp2_matches_tp1(model, fused):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", "-m", "fak_b200.benchmarks.tpcheck",
+           "--model", model, "--mix", "q8_0" if model == "tiny-llama" else "q4_k_m", "--fused", str(fused)]
+    p = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
+    assert p.returncode == 0, p.stderr[-3000:]
+    line = [l for l in p.stdout.splitlines() if l.startswith("{")][-1]
+    res = json.loads(line)
+    assert res["ok"], res
