@@ -19,7 +19,7 @@ import torch
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="tiny-qwen2")
-    ap.add_argument("--mix", default="q4_k_m")
+    ap.add_argument("--mix", default="q4_k_m", help="q4_k_m, q8_0 (MoE checkpoints use q8_0)")
     ap.add_argument("--new", type=int, default=12)
     ap.add_argument("--graphs", type=int, default=1)
     ap.add_argument("--fused", type=int, default=1, help="1: in-kernel P2P collectives, 0: NCCL")

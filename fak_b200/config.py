@@ -189,6 +189,8 @@ class EngineConfig:
     fused_collectives: bool = True      # in-kernel P2P collectives; False = NCCL baseline
     prefill_bf16_weights: bool = True   # keep a bf16 copy of each quantized weight for prefill GEMMs
     seed: int = 0
+    spec_k: int = 0                     # draft tokens per verify step (0: no speculation)
+    spec_draft_layers: int = 4          # self-speculation: the draft is the first N layers + LM head
 
     ENV_KEYS = {
         "page_size": ("FAK_PAGED_KV_BLOCK_TOKENS", int),
@@ -204,6 +206,8 @@ class EngineConfig:
         "fused_collectives": ("FAK_FUSED_COLLECTIVES", bool),
         "prefill_bf16_weights": ("FAK_PREFILL_BF16", bool),
         "seed": ("FAK_SEED", int),
+        "spec_k": ("FAK_SPEC_K", int),
+        "spec_draft_layers": ("FAK_SPEC_DRAFT_LAYERS", int),
     }
 
     @classmethod

@@ -35,6 +35,15 @@ void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, i
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
                 torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
                 torch::Tensor err);
+void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor wr, int64_t k, bool norm_topk,
+               torch::Tensor ids, torch::Tensor wts);
+void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_t max_chunks, torch::Tensor chunk_expert,
+               torch::Tensor chunk_pairs, torch::Tensor n_chunks);
+void moe_qmmv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, int64_t pitch, torch::Tensor qx,
+              torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
+              torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err);
+void moe_combine(torch::Tensor out, torch::Tensor ids, torch::Tensor wts, int64_t k, int64_t e0, int64_t E_local,
+                 torch::Tensor x);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias, int64_t epi,
                c10::optional<torch::Tensor> err);
 
@@ -56,6 +65,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_allgather_cols", &p2p_allgather_cols);
   m.def("p2p_allreduce_add", &p2p_allreduce_add);
   m.def("p2p_argmax", &p2p_argmax);
+  m.def("moe_route", &moe_route);
+  m.def("moe_group", &moe_group);
+  m.def("moe_qmmv", &moe_qmmv);
+  m.def("moe_combine", &moe_combine);
   m.def("qmmv", &qmmv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
         pybind11::arg("pitch"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"),
         pybind11::arg("bias"), pybind11::arg("epi"), pybind11::arg("flags") = 0);

@@ -138,7 +138,12 @@ class Engine:
         for b in buckets or self.ecfg.graph_batch_buckets:
             if b <= self.ecfg.max_batch:
                 self.runner.capture(b, self.bt_width)
+                if self.ecfg.spec_k > 0:
+                    self.runner.capture(b, self.bt_width, n_layers=self._draft_layers())
         self._graphs_ready = True
+
+    def _draft_layers(self) -> int:
+        return max(1, min(self.ecfg.spec_draft_layers, self.cfg.n_layers))
 
     # ------------------------------------------------------------------------------------
     def add_request(self, prompt: list[int], max_new_tokens: int = 128, sampling: SamplingParams | None = None,
@@ -258,10 +263,27 @@ class Engine:
         self.pool.release(r.pages)
         r.pages = []
 
+    def _ensure_pages(self, r: Request, last_pos: int) -> bool:
+        need = last_pos // self.ecfg.page_size + 1 - len(r.pages)
+        if need > 0:
+            try:
+                r.pages.extend(self._alloc(need))
+            except OutOfPages:
+                self._preempt(r)
+                return False
+        return True
+
     def _run_decode(self) -> None:
         if not self.running:
             return
         ps = self.ecfg.page_size
+        k = self.ecfg.spec_k
+        if k > 0 and all(r.sampling.greedy for r in self.running):
+            lanes = [r for r in list(self.running)
+                     if self._ensure_pages(r, min(r.n_kv + k, self.max_context - 1))]
+            if lanes:
+                self._run_decode_spec(lanes, k)
+            return
         lanes = []
         for r in list(self.running):
             p = r.n_kv  # position of the token being fed (the last sampled one)
@@ -306,6 +328,63 @@ class Engine:
         for r, tok in zip(lanes, toks):
             r.n_kv += 1
             self._emit(r, tok)
+        self.running = [r for r in self.running if not r.finished]
+
+    def _run_decode_spec(self, lanes: list[Request], k: int) -> None:
+        """Greedy self-speculative decode (reference: spec.SpeculativeGreedy, internal/spec/spec.go:214-300).
+
+        The draft (first layers + LM head, sharing the target's KV pages) proposes k tokens per
+        lane; the target verifies all k+1 positions in one forward, each position running as its
+        own attention lane with a causal context length; the longest agreeing prefix plus the
+        target's next token are kept, and the KV of rejected positions is dropped by truncating
+        the lane's KV length (its pages are simply overwritten later)."""
+        ps, dev, B, W = self.ecfg.page_size, self.device, len(lanes), self.bt_width
+        bt = np.zeros((B, W), np.int32)
+        p0 = np.array([r.n_kv for r in lanes], np.int64)
+        for b, r in enumerate(lanes):
+            bt[b, :len(r.pages)] = r.pages
+        pages = [np.asarray(r.pages, np.int64) for r in lanes]
+
+        def slots(pos):
+            return np.array([pages[b][pos[b] // ps] * ps + pos[b] % ps for b in range(B)], np.int32)
+
+        btd = torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True)
+        cur = torch.tensor([r.tokens[-1] for r in lanes], dtype=torch.int32).to(dev)
+        feed = [cur]
+        Ld = self._draft_layers()
+        for j in range(k):
+            pos = np.minimum(p0 + j, self.max_context - 1)
+            h = torch.from_numpy(np.concatenate([pos.astype(np.int32), slots(pos), (pos + 1).astype(np.int32)]))
+            d = h.pin_memory().to(dev, non_blocking=True)
+            out = self.runner.decode(feed[-1], d[0:B], d[B:2 * B], btd, d[2 * B:3 * B], B,
+                                     use_graph=self._graphs_ready, n_layers=Ld)
+            feed.append(out.clone())
+        toks = torch.stack(feed, 1).reshape(-1)                # lane (b, j): token fed at p0 + j
+        V = B * (k + 1)
+        vpos = (p0[:, None] + np.arange(k + 1)[None, :]).reshape(-1)
+        vpos = np.minimum(vpos, self.max_context - 1)
+        vslot = np.array([pages[i // (k + 1)][vpos[i] // ps] * ps + vpos[i] % ps for i in range(V)], np.int32)
+        h = torch.from_numpy(np.concatenate([vpos.astype(np.int32), vslot, (vpos + 1).astype(np.int32)]))
+        d = h.pin_memory().to(dev, non_blocking=True)
+        vbt = btd.repeat_interleave(k + 1, dim=0)
+        tgt = self.runner.decode(toks, d[0:V], d[V:2 * V], vbt, d[2 * V:3 * V], V, use_graph=self._graphs_ready)
+        t_host = tgt.view(B, k + 1).cpu().numpy()
+        d_host = toks.view(B, k + 1).cpu().numpy()[:, 1:]
+        self.stats["h2d_bytes"] += bt.size * 4 + (k + 1) * 12 * B + 12 * V
+        self.stats["d2h_bytes"] += 8 * V
+        for b, r in enumerate(lanes):
+            acc = 0
+            while acc < k and d_host[b, acc] == t_host[b, acc]:
+                acc += 1
+            self.stats["spec_proposed"] = self.stats.get("spec_proposed", 0) + k
+            self.stats["spec_accepted"] = self.stats.get("spec_accepted", 0) + acc
+            emitted = list(d_host[b, :acc]) + [t_host[b, acc]]
+            for t in emitted:
+                if r.finished:
+                    break
+                r.n_kv += 1
+                self._emit(r, int(t))
+        self.stats["decode_tokens"] += B
         self.running = [r for r in self.running if not r.finished]
 
     def _preempt(self, r: Request) -> None:

@@ -153,12 +153,15 @@ class ModelRunner:
         else:
             self.coll.decode_down(self, i, B)
 
-    def decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True) -> None:
-        """One decode step for B sequences; results in self.logits[:B] / self.next_ids[:B]."""
+    def decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True, n_layers: int | None = None) -> None:
+        """One decode step for B lanes; results in self.logits[:B] / self.next_ids[:B].
+
+        ``n_layers`` < cfg.n_layers runs only the first layers before the final norm and LM head:
+        the early-exit draft model of self-speculative decoding (its KV pages are the target's)."""
         cfg = self.cfg
         n_split = self.n_split_for(B)
         K.embed(self.w.embed, ids, self.x[:B], None, self.err)
-        for i in range(cfg.n_layers):
+        for i in range(cfg.n_layers if n_layers is None else n_layers):
             self._layer_decode(i, B, pos, slot, bt, ctx, n_split)
         K.quant_act(self.x[:B], self.act_d, self.w.final_norm, cfg.rms_eps)
         if greedy and self.coll is not None and hasattr(self.coll, "lm_head_greedy"):
@@ -187,34 +190,36 @@ class ModelRunner:
             "ctx": torch.ones(B, dtype=torch.int32, device=dev),
         }
 
-    def capture(self, B: int, bt_width: int) -> None:
+    def capture(self, B: int, bt_width: int, n_layers: int | None = None) -> None:
         st = self._static_inputs(B, bt_width)
         # warm up (also triggers lazy cudaFuncSetAttribute) on a side stream, then capture
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B)
+            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         before = K.launches()
         with torch.cuda.graph(g):
-            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B)
-        self._graph_kernels[B] = K.launches() - before
+            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers)
+        key = (B, n_layers)
+        self._graph_kernels[key] = K.launches() - before
         K._launches[0] = before
-        self._graphs[B] = (g, st)
+        self._graphs[key] = (g, st)
 
-    def graph_bucket(self, B: int) -> int | None:
-        cands = [b for b in self._graphs if b >= B]
+    def graph_bucket(self, B: int, n_layers: int | None = None) -> int | None:
+        cands = [b for b, nl in self._graphs if b >= B and nl == n_layers]
         return min(cands) if cands else None
 
-    def decode(self, ids, pos, slot, bt, ctx, B: int, use_graph: bool = True) -> torch.Tensor:
-        """Decode one token for B sequences; returns next ids (device int32 [B])."""
-        bucket = self.graph_bucket(B) if use_graph else None
+    def decode(self, ids, pos, slot, bt, ctx, B: int, use_graph: bool = True, n_layers: int | None = None
+               ) -> torch.Tensor:
+        """Decode one token for B lanes; returns next ids (device int32 [B])."""
+        bucket = self.graph_bucket(B, n_layers) if use_graph else None
         if bucket is None:
-            self.decode_eager(ids, pos, slot, bt, ctx, B)
+            self.decode_eager(ids, pos, slot, bt, ctx, B, n_layers=n_layers)
             return self.next_ids[:B]
-        g, st = self._graphs[bucket]
+        g, st = self._graphs[(bucket, n_layers)]
         st["ids"][:B].copy_(ids)
         st["pos"][:B].copy_(pos)
         st["slot"][:B].copy_(slot)
@@ -225,7 +230,7 @@ class ModelRunner:
             st["ctx"][B:].fill_(1)
             st["slot"][B:].fill_(-1)
         g.replay()
-        K.count(self._graph_kernels[bucket])
+        K.count(self._graph_kernels[(bucket, n_layers)])
         return self.next_ids[:B]
 
     # ------------------------------------------------------------------------------------

@@ -80,8 +80,8 @@ class LayerWeights:
     gate_up: QuantWeight | None          # interleaved rows (dense FFN)
     down: QuantWeight | None
     router: torch.Tensor | None = None   # [E, d] f32 (MoE)
-    experts_gate_up: list[QuantWeight] | None = None  # per local expert, interleaved rows
-    experts_down: list[QuantWeight] | None = None
+    experts_gate_up: QuantWeight | None = None  # local experts stacked, 8-row interleaved gate/up
+    experts_down: QuantWeight | None = None
     expert_ids: list[int] | None = None  # global ids of the experts held here
 
 
@@ -112,8 +112,8 @@ class ModelWeights:
             n += sum(s.nbytes for s, _ in L.qkv) + L.o.nbytes
             if L.gate_up is not None:
                 n += L.gate_up.nbytes + L.down.nbytes
-            if L.experts_gate_up:
-                n += sum(w.nbytes for w in L.experts_gate_up) + sum(w.nbytes for w in L.experts_down)
+            if L.experts_gate_up is not None:
+                n += L.experts_gate_up.nbytes + L.experts_down.nbytes
         return n
 
 
@@ -250,7 +250,7 @@ def _col_block_slice(raw: torch.Tensor, t: int, cols: int, c0: int, c1: int) -> 
 
 
 def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], device: str | torch.device = "cuda",
-                 tp_rank: int = 0, tp_size: int = 1, expert_filter: Callable[[int], bool] | None = None,
+                 tp_rank: int = 0, tp_size: int = 1, expert_filter: tuple[int, int] | None = None,
                  prefill_dense: bool = False) -> ModelWeights:
     cfg, get, close = source
     device = torch.device(device)
@@ -315,7 +315,9 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
             qkv=segs, qkv_bias=bias, q_norm=qn, k_norm=kn, o=o, gate_up=None, down=None,
         )
         if cfg.is_moe:
-            _load_moe_layer(cfg, get, quant, p, L, device, expert_filter)
+            # expert parallelism rides on the tensor-parallel group: rank r owns a band of experts
+            band = expert_filter if expert_filter is not None else expert_slice(cfg.n_experts, tp_rank, tp_size)
+            _load_moe_layer(cfg, get, quant, p, L, device, band)
         else:
             gs, gt, graw = quant(p + "ffn_gate.weight")
             us, ut, uraw = quant(p + "ffn_up.weight")
@@ -347,18 +349,25 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
     return ModelWeights(cfg, embed, layers, final_norm, lm_head, q_heads, kv_heads, (f0, f1), tp_rank, tp_size)
 
 
+def expert_slice(E: int, rank: int, size: int) -> tuple[int, int]:
+    """Contiguous band of experts owned by an expert-parallel rank (reference: ExpertParallelPlan,
+    internal/model/expert_parallel.go:68-83)."""
+    per = -(-E // size)
+    return min(E, rank * per), min(E, (rank + 1) * per)
+
+
 def _load_moe_layer(cfg, get, quant, p, L: LayerWeights, device, expert_filter) -> None:
     E, f, d = cfg.n_experts, cfg.expert_ffn_dim, cfg.d_model
     L.router = _vec(get, p + "ffn_gate_inp.weight", device).view(E, d).contiguous()
-    keep = [e for e in range(E) if expert_filter is None or expert_filter(e)]
+    e0, e1 = expert_filter if expert_filter is not None else (0, E)
     gs, gt, graw = quant(p + "ffn_gate_exps.weight")
     us, ut, uraw = quant(p + "ffn_up_exps.weight")
     ds_, dt, draw = quant(p + "ffn_down_exps.weight")
     graw = graw.view(E, f, -1)
     uraw = uraw.view(E, f, -1)
     draw = draw.view(E, d, -1)
-    L.experts_gate_up, L.experts_down, L.expert_ids = [], [], keep
-    for e in keep:
-        inter = interleave_gate_up(graw[e], uraw[e])
-        L.experts_gate_up.append(QuantWeight.from_rows(inter, gt, d, device))
-        L.experts_down.append(QuantWeight.from_rows(draw[e].contiguous(), dt, f, device))
+    # experts stored back to back in one buffer (rows of expert e start at e * rows_per_expert)
+    gu = torch.cat([interleave_gate_up(graw[e], uraw[e]) for e in range(e0, e1)])
+    L.experts_gate_up = QuantWeight.from_rows(gu, gt, d, device)
+    L.experts_down = QuantWeight.from_rows(draw[e0:e1].reshape((e1 - e0) * d, -1).contiguous(), dt, f, device)
+    L.expert_ids = list(range(e0, e1))

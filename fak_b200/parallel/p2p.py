@@ -119,3 +119,13 @@ class P2PTP(NcclTP):
         ext().p2p_argmax(self.peers, self.logits_local[:B], self.Vl_real, self.v_off, self.cand_off,
                          rn.next_ids[:B], B, self.flags_off, 3 * self.cfg.n_layers, self.me, self.counters, self.err)
         K.count()
+
+    def reduce_partial(self, rn, i: int, B: int, fill) -> None:
+        """x += sum over ranks of the partial fill() writes (MoE expert bands), via the P2P all-reduce."""
+        d = self.cfg.d_model
+        part_off = self.parts_off + i * self.B * d * 4
+        part = self.buf[part_off:part_off + B * d * 4].view(torch.float32).view(B, d)
+        fill(part)
+        ext().p2p_allreduce_add(self.peers, part_off, rn.x[:B], B * d, self.flags_off, 3 * i + 2, self.me,
+                                self.counters, self.err, AR_CTAS)
+        K.count(2)

@@ -118,3 +118,15 @@ class NcclTP:
         K.gemm(hb2, rn.w.layers[i].down, t, K.EPI_STORE)
         dist.all_reduce(t, group=self.group)
         x.add_(t)
+
+    # ---------------------------------------------------------------------------------
+    def reduce_partial(self, rn, i: int, B: int, fill) -> None:
+        """x += all-reduce(partial), where fill(partial) writes this rank's contribution."""
+        t = self.tmp[:B]
+        fill(t)
+        dist.all_reduce(t, group=self.group)
+        rn.x[:B].add_(t)
+
+    def prefill_reduce(self, part: torch.Tensor, x: torch.Tensor) -> None:
+        dist.all_reduce(part, group=self.group)
+        x.add_(part)

@@ -39,8 +39,8 @@ if cpu_sources:
         CppExtension(
             "fak_b200._cpu",
             cpu_sources,
-            extra_compile_args={"cxx": CXX_FLAGS + ["-fopenmp", "-march=x86-64-v3"]},
-            extra_link_args=["-fopenmp"],
+            extra_compile_args={"cxx": CXX_FLAGS + ["-march=x86-64-v3", "-pthread"]},
+            extra_link_args=["-pthread"],
         )
     )
 

@@ -81,3 +81,38 @@ def test_radix_reuse_and_batched_equals_serial(model_file):
     assert eng.stats["prefill_tokens_avoided"] >= 64  # b reused a's prefix pages
     both = eng.generate([a, b], 8)
     assert both == solo
+
+
+def test_moe_generation_matches_reference(tmp_path):
+    from fak_b200.models.reference import ReferenceModel
+    path = str(tmp_path / "moe.gguf")
+    write_synthetic_gguf(path, preset("tiny-qwen3moe"), "q8_0", seed=9, std=0.05)
+    ref = ReferenceModel.from_gguf(path, "cuda")
+    eng = _engine(path, graphs=True)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, eng.cfg.vocab_size, n).tolist() for n in (30, 12, 50, 7)]
+    outs = eng.generate(prompts, max_new_tokens=8)
+    agree = []
+    for p, o in zip(prompts, outs):
+        want = ref.generate_greedy(p, 8)
+        k = 0
+        while k < len(o) and o[k] == want[k]:
+            k += 1
+        agree.append(k)
+    assert min(agree) >= 3, (agree, outs)
+
+
+def test_self_speculative_decode_matches_greedy(model_file):
+    from fak_b200.engine import Engine
+    base = _engine(model_file, graphs=True)
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, base.cfg.vocab_size, n).tolist() for n in (25, 40)]
+    want = base.generate(prompts, max_new_tokens=16)
+    for k in (1, 4):
+        ecfg = EngineConfig(max_batch=16, kv_pages=512, cuda_graph=True, graph_batch_buckets=(1, 2, 4, 8, 16),
+                            spec_k=k, spec_draft_layers=1)
+        eng = Engine.from_gguf(model_file, ecfg, "cuda", max_context=1024)
+        eng.warmup_graphs()
+        got = eng.generate(prompts, max_new_tokens=16)
+        assert got == want, (k, got, want)
+        assert eng.stats["spec_proposed"] > 0

@@ -25,3 +25,15 @@ def test_tp2_matches_tp1(model, fused):
     line = [l for l in p.stdout.splitlines() if l.startswith("{")][-1]
     res = json.loads(line)
     assert res["ok"], res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep2_moe_matches_ep1():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29534", "-m", "fak_b200.benchmarks.tpcheck",
+           "--model", "tiny-qwen3moe", "--mix", "q8_0"]
+    p = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
+    assert p.returncode == 0, p.stderr[-3000:]
+    res = json.loads([l for l in p.stdout.splitlines() if l.startswith("{")][-1])
+    assert res["ok"], res
