@@ -19,6 +19,9 @@
 #include <torch/extension.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <cstdio>
+#include <mutex>
+
 #include "mma.cuh"
 
 using namespace fak;
@@ -555,4 +558,139 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
   };
   if (D == 128) args(k_prefill_attn<128>, sizeof(PrefillSmem<128>));
   else args(k_prefill_attn<64>, sizeof(PrefillSmem<64>));
+}
+
+// =============================================================================================
+// fak_decode_attention_noalloc: the split-KV decode attention above, as one C entry point that
+// allocates nothing.  This entry point has no counterpart in the reference.
+//
+// Who needs it: a caller that links this library through its C ABI without PyTorch (a C/C++
+// host runtime, or Python through ctypes) has no caching allocator that can hand it a split-KV
+// workspace, and a cudaMalloc/cudaFree pair per call would both cost more than the kernel and,
+// through cudaFree, wait for the whole device.  A server that sizes its memory once at start-up
+// (the KV page pool takes nearly all of HBM) also wants no allocation inside its decode loop,
+// where an out-of-memory error could only surface long after admission.  So the partial results
+// of the split-KV pass live in one statically sized device array of this file, and the call
+// touches no allocator: no cudaMalloc, no cudaFree, no torch tensor.
+//
+// Limit: B * H * n_split <= kNoAllocSlots (4096) (sequence, head, split) slots with head_dim <= 128,
+// i.e. 4096 * 130 floats = 2,129,920 bytes of scratch.  Larger calls are rejected with an error
+// message and launch nothing.  n_split == 1 uses no scratch and has no size limit.
+//
+// Set-up: the first call on a device (that device current) looks the scratch array up with
+// cudaGetSymbolAddress and caches the pointer for that device; make that first call before any
+// stream capture begins.  Nothing in the scratch must start at zero -- the attention kernel writes
+// every (sequence, head, split) slot, an empty split included, before the merge kernel reads it --
+// so nothing is cleared.
+//
+// Concurrency: there is one scratch array per device, so two calls in flight on the same device at
+// the same time (different streams, or different host threads without ordering) race on it and
+// corrupt each other's results.  Issue them on one stream or order them yourself.
+//
+// Returns 0 on success; 1 for an invalid argument, 2 for a call beyond the scratch limit, 3 for a
+// CUDA error.  On failure a message is written to err (err_len bytes, may be null).
+// =============================================================================================
+namespace {
+constexpr int64_t kNoAllocSlots = 4096;
+constexpr int kNoAllocMaxD = 128;
+constexpr int kNoAllocMaxDevices = 64;
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocSlots * (kNoAllocMaxD + 2)];
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+template <typename... A>
+int noalloc_fail(char* err, size_t err_len, int code, const char* fmt, A... a) {
+  if (err && err_len) {
+    if constexpr (sizeof...(A) == 0) snprintf(err, err_len, "%s", fmt);
+    else snprintf(err, err_len, fmt, a...);
+  }
+  return code;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noalloc(
+    const float* q, const void* k_cache, const void* v_cache, const int* block_table, int bt_stride,
+    const int* ctx_len, int B, int H, int Hkv, int D, int n_split, int pages_per_split, float* out, int8_t* qx,
+    float* ds, int ldo, void* stream, char* err, size_t err_len) {
+  if (err && err_len) err[0] = 0;
+  if (!q || !k_cache || !v_cache || !block_table || !ctx_len)
+    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: null input pointer");
+  if (!out && !qx) return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: no output (out or qx)");
+  if (qx && !ds) return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: qx given without ds");
+  if (D != 64 && D != 128)
+    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: head dim %d (must be 64 or 128)", D);
+  if (B < 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0 || H / Hkv > 16)
+    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: heads %d / kv heads %d (GQA group <= 16)", H,
+                        Hkv);
+  if (n_split < 1 || pages_per_split < 1 || bt_stride < 1)
+    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: n_split, pages_per_split, bt_stride >= 1");
+  if (ldo <= 0) ldo = H * D;
+  if (ldo < H * D || ldo % 32 != 0)
+    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: output row stride %d", ldo);
+  const int64_t slots = (int64_t)B * H * n_split;
+  if (n_split > 1 && slots > kNoAllocSlots)
+    return noalloc_fail(err, err_len, 2,
+                        "fak_decode_attention_noalloc: B*H*n_split = %lld exceeds the static scratch limit of %lld "
+                        "slots (%lld bytes); use fewer splits or the allocating entry point",
+                        (long long)slots, (long long)kNoAllocSlots,
+                        (long long)(kNoAllocSlots * (kNoAllocMaxD + 2) * sizeof(float)));
+  if (B == 0) return 0;
+
+  float* pw = nullptr;
+  if (n_split > 1) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+      return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    pw = g_noalloc_ptr[dev];
+  }
+  // partial outputs [slots, D] then (max, sum) pairs [slots] -- the layout the allocating path uses
+  float2* pml = pw ? reinterpret_cast<float2*>(pw + slots * D) : nullptr;
+  float2* dp = reinterpret_cast<float2*>(ds);
+  const float scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(Hkv, B, (unsigned)n_split);
+  cfg.blockDim = dim3(128);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(k_cache);
+  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(v_cache);
+  if (D == 128) {
+    size_t smem = std::max(sizeof(DecodeSmem<128>), (size_t)(4 * 16 * 128 + 4 * 16 * 2) * 4);
+    cfg.dynamicSmemBytes = smem;
+    e = cudaFuncSetAttribute(k_decode_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+      e = cudaLaunchKernelEx(&cfg, k_decode_attn<128>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo);
+  } else {
+    size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
+    cfg.dynamicSmemBytes = smem;
+    e = cudaFuncSetAttribute(k_decode_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+      e = cudaLaunchKernelEx(&cfg, k_decode_attn<64>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo);
+  }
+  if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode attention launch: %s", cudaGetErrorString(e));
+  if (n_split > 1) {
+    cudaLaunchConfig_t c2 = {};
+    c2.gridDim = dim3(B, H);
+    c2.blockDim = dim3(D);
+    c2.stream = static_cast<cudaStream_t>(stream);
+    if (D == 128)
+      e = cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
+                             dp, ldo);
+    else
+      e = cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
+                             dp, ldo);
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode combine launch: %s", cudaGetErrorString(e));
+  }
+  return 0;
 }
