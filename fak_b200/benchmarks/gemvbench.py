@@ -1,4 +1,4 @@
-"""Bandwidth of the quantized decode GEMV kernels on one weight matrix (CUDA events, L2 > working set).
+"""Bandwidth of the quantized decode GEMV kernels (tile-packed tgemv, row-major qmmv / qgemv) on one weight matrix (CUDA events, L2 > working set).
 
     python -m fak_b200.benchmarks.gemvbench --rows 37888 --cols 3584 --qtype 12 --batch 5
 """
@@ -17,7 +17,7 @@ def main(argv=None):
     ap.add_argument("--qtype", type=int, default=12)
     ap.add_argument("--batch", type=int, default=5)
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--kernel", default="qmmv", choices=["qmmv", "qgemv"])
+    ap.add_argument("--kernel", default="tgemv", choices=["tgemv", "qmmv", "qgemv"])
     ap.add_argument("--flags", type=int, default=0)
     args = ap.parse_args(argv)
     from fak_b200.models.weights import QuantWeight
@@ -30,14 +30,22 @@ def main(argv=None):
     ws = []
     for i in range(n_copies):
         raw = dq.synth_quantized((args.rows, args.cols), args.qtype, 1234 + i, 0.02, device="cuda")
-        ws.append(QuantWeight.from_rows(raw.view(args.rows, -1), args.qtype, args.cols, dev))
+        w = QuantWeight.from_rows(raw.view(args.rows, -1), args.qtype, args.cols, dev)
+        if args.kernel == "tgemv":
+            w.pack()
+            w.buf = None  # only the tile-packed copy is streamed
+        ws.append(w)
     act = K.ActQ(8, args.cols, dev)
     K.quant_act(torch.randn(args.batch, args.cols, device=dev), act)
     y = torch.zeros(8, args.rows, device=dev)
     C = ext()
 
+    part, cnt = K.tgemv_workspace(dev)
+
     def run(w):
-        if args.kernel == "qmmv":
+        if args.kernel == "tgemv":
+            C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q, act.ds, args.batch, y, None, 0, part, cnt, None, args.flags)
+        elif args.kernel == "qmmv":
             C.qmmv(w.buf, w.qtype, w.rows, w.cols, w.pitch, act.q, act.ds, args.batch, y, None, 0, args.flags)
         else:
             C.qgemv(w.buf, w.qtype, w.rows, w.cols, w.pitch, act.q, act.ds, args.batch, y, None, 0)
@@ -52,7 +60,11 @@ def main(argv=None):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000 / args.iters
     nbytes = ws[0].nbytes
-    print(json.dumps({"kernel": args.kernel, "rows": args.rows, "cols": args.cols, "qtype": args.qtype,
+    info = {}
+    if args.kernel == "tgemv":
+        S, ticket, slices, W, R, smem = C.tgemv_workspace(args.qtype, args.rows, args.cols, 0)
+        info = {"slices": slices, "warps": W, "depth": R, "smem": smem}
+    print(json.dumps({"kernel": args.kernel, **info, "rows": args.rows, "cols": args.cols, "qtype": args.qtype,
                       "batch": args.batch, "flags": args.flags, "us": round(us, 2),
                       "tb_s": round(nbytes / us / 1e6, 3)}))
 

@@ -39,6 +39,11 @@ void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor w
                torch::Tensor ids, torch::Tensor wts);
 void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_t max_chunks, torch::Tensor chunk_expert,
                torch::Tensor chunk_pairs, torch::Tensor n_chunks);
+void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, torch::Tensor qx, torch::Tensor ds, int64_t B,
+           torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part, torch::Tensor cnt,
+           c10::optional<torch::Tensor> err, int64_t flags);
+std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device);
+int64_t tgemv_unit_bytes(int64_t qtype);
 void moe_qmmv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, int64_t pitch, torch::Tensor qx,
               torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
               torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err);
@@ -73,6 +78,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("pitch"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"),
         pybind11::arg("bias"), pybind11::arg("epi"), pybind11::arg("flags") = 0);
   m.def("quant_act_wide", &quant_act_wide);
+  m.def("tgemv", &tgemv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
+        pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"), pybind11::arg("bias"),
+        pybind11::arg("epi"), pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
+        pybind11::arg("flags") = 0);
+  m.def("tgemv_workspace", &tgemv_workspace);
+  m.def("tgemv_unit_bytes", &tgemv_unit_bytes);
   m.def("gemm_bf16", &gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"),
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("epi") = 0, pybind11::arg("err") = pybind11::none());
 }

@@ -1,0 +1,515 @@
+// Decode GEMV over tile-packed GGML blocks on the integer tensor cores (B <= 8 tokens).
+//
+// Weight layout ("tile-packed").  Rows are grouped in tiles of 16 and each row's blocks in
+// 256-weight super units; the 16 rows x 1 unit of a tile ("unit tile") are stored contiguously,
+// split into planes so that every field a thread needs is an aligned, bank-conflict-free shared
+// load once the unit tile sits in shared memory:
+//   Q4_K  2304 B: hdr [16][16] (d, dmin, 12 scale bytes) | qs [16][128]
+//   Q6_K  3360 B: ql [16][128] | qh [16][64] | scales [16][16] | d [16][2]
+//   Q8_0  4352 B: qs [16][256] (8 blocks x 32) | d [16][8][2]
+// Plane row ("slot") s holds tile row (s >> 1) + 8 (s & 1), so the two rows an MMA thread owns
+// (g and g + 8) are adjacent slots; the 16-byte chunks of the quant planes are XOR-swizzled by slot
+// (Q4_K/Q8_0 qs: chunk ^ (s & 6); Q6_K ql: chunk ^ ((s >> 1) & 7), qh: chunk ^ ((s >> 1) & 3)).
+// The block bytes themselves are unchanged; only their placement differs from the GGUF rows.
+//
+// Work decomposition.  A work item is one tile x one K slice and belongs to ONE warp: the warp
+// streams its unit tiles through a private ring of shared-memory slots (1-D TMA bulk copies
+// completing on per-slot mbarriers, lane 0 as producer), so no CTA-wide barrier sits in the main
+// loop.  All warps of a CTA work on the same K slice, whose activations (int8 codes, per-32
+// (scale, sum) pairs) are staged once per CTA.  When the matrix has too few tiles to occupy every
+// warp, K is split into slices; the slice partials meet in a global scratch and the last warp to
+// finish a tile (atomic ticket) sums them in slice order, so results are deterministic and
+// independent of the batch size.
+//
+// Per 32-element sub-block and thread (rows g, g+8; tokens 2t, 2t+1): one m16n8k32 integer MMA
+// whose accumulator starts at the float-conversion constant 0x4B400000, so the int32 result read
+// as a float is 12582912 + dot exactly (|dot| < 2^22), then
+//   Q4_K  acc += (d*sc) * dx * dot - (dmin*m) * sum(x)     (nibbles via u8 x s8; high nibbles
+//                                                           in place, scale pre-divided by 16)
+//   Q6_K  acc += (d*sc) * dx * dot16                        (m16n8k16 per 16-element sub-block;
+//                                                           the -32 offset enters through the
+//                                                           accumulator start: -32 * sum(qx))
+//   Q8_0  acc += d * dx * dot
+// The per-(row, sub-block) float scales of a unit tile are decoded once per warp into a small
+// shared table (each lane decodes 4-8 of them) instead of by every thread that uses them.
+// Reference: the per-op GEMV kernels of internal/compute/cuda_kernels.cu (k_q8_matvec and the
+// Q4_K/Q6_K dequant paths), which read one row per warp from the GGUF rows.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include "tc.cuh"
+
+using namespace fak;
+
+namespace {
+
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+constexpr int MAXB = 8;
+constexpr int MAGIC_I = 0x4B400000;
+constexpr float MAGIC_F = 12582912.0f;
+
+template <int QT> struct Tile;
+template <> struct Tile<QT_Q4_K> { static constexpr int UT = 2304; static constexpr int TABF = 16 * 8 * 2; };
+template <> struct Tile<QT_Q6_K> { static constexpr int UT = 3360; static constexpr int TABF = 16 * 16; };
+template <> struct Tile<QT_Q8_0> { static constexpr int UT = 4352; static constexpr int TABF = 16 * 8; };
+
+FAK_DEV void mma_u8s8_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c0, int c1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+FAK_DEV void mma_s8s8_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c0, int c1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+FAK_DEV void mma_u8s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0, int c0, int c1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%7,%8};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(c0), "r"(c1));
+}
+FAK_DEV float magic_f(int c) { return __int_as_float(c) - MAGIC_F; }
+// byte i of w as a float (exact), without the XU pipe
+FAK_DEV float ubyte_f(uint32_t w, int i) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650 + i) ) - 8388608.0f;
+}
+
+FAK_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          tc::smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(tc::smem_addr(bar))
+      : "memory");
+}
+
+struct TGeo {
+  int T;        // 16-row tiles
+  int U;        // 256-weight units per row
+  int S;        // K slices
+  int Us;       // units per slice (last slice may hold fewer)
+  int P;        // CTAs per slice
+  int xstride;  // shared bytes per token row of activation codes
+  int dstride;  // float2 per token row of the staged (scale, sum) pairs
+};
+
+// Shared-memory carve-up (byte offsets), identical on host and device.
+struct TSmem {
+  int ring, xs, dsr, dsT, czT, tab, bars, total;
+};
+__host__ __device__ inline TSmem tsmem(int qt, int W, int R, const TGeo& g) {
+  const int UT = qt == QT_Q4_K ? 2304 : (qt == QT_Q6_K ? 3360 : 4352);
+  const int TABF = qt == QT_Q4_K ? 256 : (qt == QT_Q6_K ? 256 : 128);
+  TSmem s;
+  s.ring = 0;
+  s.xs = W * R * UT;
+  s.dsr = s.xs + MAXB * g.xstride;
+  s.dsT = s.dsr + MAXB * g.dstride * 8;
+  s.czT = s.dsT + g.Us * 8 * MAXB * 8;
+  s.tab = s.czT + (qt == QT_Q6_K ? g.Us * 16 * MAXB * 4 : 0);
+  s.bars = s.tab + W * TABF * 4;
+  s.total = s.bars + (W * R + 1) * 8;
+  return s;
+}
+
+// ---- one unit tile -------------------------------------------------------------------------
+// wt: the unit tile in shared memory; tab: this warp's scale table; xr: token g's codes at this
+// unit; dsT: (scale, sum) at this unit's first block, [block][token]; czT (Q6_K): accumulator
+// starts at this unit's first 16-block, [k16][token].
+template <int QT>
+FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, const int8_t* __restrict__ xr,
+                       const float2* __restrict__ dsT, const int* __restrict__ czT, int lane, float (&acc)[4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const int sA = 2 * g, sB = 2 * g + 1;
+  if constexpr (QT == QT_Q4_K) {
+    {  // scale table: lane -> slot lane>>1, sub-blocks 4*(lane&1) .. +3
+      const int s = lane >> 1, jh = lane & 1;
+      const uint4 h = *reinterpret_cast<const uint4*>(wt + 16 * s);
+      const float d = __half2float(__ushort_as_half((uint16_t)(h.x & 0xffff)));
+      const float dm = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+      // 6-bit (scale, min) of sub-blocks 0-3 are the low 6 bits of bytes 0-3 / 4-7; those of
+      // sub-blocks 4-7 combine the nibbles of bytes 8-11 with the top 2 bits of bytes 0-7
+      const uint32_t scw = jh ? ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u)) : (h.y & 0x3F3F3F3Fu);
+      const uint32_t mw = jh ? (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3F3F3F3Fu);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int j = 4 * jh + i;
+        const float a = d * ubyte_f(scw, i) * ((j & 1) ? 0.0625f : 1.0f);  // odd j: high nibbles x16
+        reinterpret_cast<float2*>(tab)[j * 16 + s] = make_float2(a, dm * ubyte_f(mw, i));
+      }
+    }
+    __syncwarp();
+    const uint8_t* qs = wt + 256;
+    const uint8_t* rA = qs + 128 * sA + 8 * (t & 1);
+    const uint8_t* rB = qs + 128 * sB + 8 * (t & 1);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int q = 2 * c + (t >> 1);
+      const uint2 qa = *reinterpret_cast<const uint2*>(rA + 16 * (q ^ (sA & 6)));
+      const uint2 qb = *reinterpret_cast<const uint2*>(rB + 16 * (q ^ (sB & 6)));
+#pragma unroll
+      for (int hi = 0; hi < 2; hi++) {
+        const int j = 2 * c + hi;
+        const uint32_t m = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+        const uint32_t a[4] = {qa.x & m, qb.x & m, qa.y & m, qb.y & m};
+        const uint2 xb = *reinterpret_cast<const uint2*>(xr + 32 * j + 8 * t);
+        int cc[4];
+        mma_u8s8_k32(cc, a, xb.x, xb.y, MAGIC_I, MAGIC_I);
+        const float4 am = *reinterpret_cast<const float4*>(tab + 2 * (j * 16 + sA));  // A_g, M_g, A_g8, M_g8
+        const float4 dx = *reinterpret_cast<const float4*>(dsT + j * MAXB + 2 * t);  // d0, s0, d1, s1
+        acc[0] = fmaf(am.x * dx.x, magic_f(cc[0]), fmaf(-am.y, dx.y, acc[0]));
+        acc[1] = fmaf(am.x * dx.z, magic_f(cc[1]), fmaf(-am.y, dx.w, acc[1]));
+        acc[2] = fmaf(am.z * dx.x, magic_f(cc[2]), fmaf(-am.w, dx.y, acc[2]));
+        acc[3] = fmaf(am.z * dx.z, magic_f(cc[3]), fmaf(-am.w, dx.w, acc[3]));
+      }
+    }
+  } else if constexpr (QT == QT_Q6_K) {
+    {  // scale table: lane -> slot lane>>1, sub-blocks 8*(lane&1) .. +7
+      const int s = lane >> 1, sh = lane & 1;
+      const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(wt + 3328 + 2 * s)));
+      const uint2 sc = *reinterpret_cast<const uint2*>(wt + 3072 + 16 * s + 8 * sh);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const uint32_t w = i < 4 ? sc.x : sc.y;
+        const int v = (int)(int8_t)((w >> (8 * (i & 3))) & 0xff);
+        tab[(8 * sh + i) * 16 + s] = d * i2f_exact22(v);
+      }
+    }
+    __syncwarp();
+    const uint8_t* ql = wt;
+    const uint8_t* qh = wt + 2048;
+    const int f8 = g, f4 = g & 3;  // swizzle keys of slots 2g and 2g+1
+#pragma unroll
+    for (int n = 0; n < 2; n++) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int c1 = 4 * n + h, c2 = 4 * n + 2 + h, ch = 2 * n + h;
+        const uint32_t la0 = *reinterpret_cast<const uint32_t*>(ql + 128 * sA + 16 * (c1 ^ f8) + 4 * t);
+        const uint32_t la1 = *reinterpret_cast<const uint32_t*>(ql + 128 * sA + 16 * (c2 ^ f8) + 4 * t);
+        const uint32_t lb0 = *reinterpret_cast<const uint32_t*>(ql + 128 * sB + 16 * (c1 ^ f8) + 4 * t);
+        const uint32_t lb1 = *reinterpret_cast<const uint32_t*>(ql + 128 * sB + 16 * (c2 ^ f8) + 4 * t);
+        const uint32_t ha = *reinterpret_cast<const uint32_t*>(qh + 64 * sA + 16 * (ch ^ f4) + 4 * t);
+        const uint32_t hb = *reinterpret_cast<const uint32_t*>(qh + 64 * sB + 16 * (ch ^ f4) + 4 * t);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const uint32_t la = (kk & 1) ? la1 : la0, lb = (kk & 1) ? lb1 : lb0;
+          const int ls = (kk >> 1) * 4, hs = 2 * kk;
+          const uint32_t a0 = ((la >> ls) & 0x0F0F0F0Fu) | (((ha >> hs) & 0x03030303u) << 4);
+          const uint32_t a1 = ((lb >> ls) & 0x0F0F0F0Fu) | (((hb >> hs) & 0x03030303u) << 4);
+          const int e0 = 128 * n + 32 * kk + 16 * h;  // first weight of this 16-block
+          const uint32_t xv = *reinterpret_cast<const uint32_t*>(xr + e0 + 4 * t);
+          const int2 cz = *reinterpret_cast<const int2*>(czT + (e0 >> 4) * MAXB + 2 * t);
+          int cc[4];
+          mma_u8s8_k16(cc, a0, a1, xv, cz.x, cz.y);
+          const float2 A = *reinterpret_cast<const float2*>(tab + (e0 >> 4) * 16 + sA);
+          const float4 dx = *reinterpret_cast<const float4*>(dsT + (e0 >> 5) * MAXB + 2 * t);
+          acc[0] = fmaf(A.x * dx.x, magic_f(cc[0]), acc[0]);
+          acc[1] = fmaf(A.x * dx.z, magic_f(cc[1]), acc[1]);
+          acc[2] = fmaf(A.y * dx.x, magic_f(cc[2]), acc[2]);
+          acc[3] = fmaf(A.y * dx.z, magic_f(cc[3]), acc[3]);
+        }
+      }
+    }
+  } else {  // Q8_0
+    {
+      const int s = lane >> 1, bh = lane & 1;
+      const uint2 dd = *reinterpret_cast<const uint2*>(wt + 4096 + 16 * s + 8 * bh);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t w = i < 2 ? dd.x : dd.y;
+        tab[(4 * bh + i) * 16 + s] = __half2float(__ushort_as_half((uint16_t)(w >> (16 * (i & 1)))));
+      }
+    }
+    __syncwarp();
+    const uint8_t* rA = wt + 256 * sA + 8 * (t & 1);
+    const uint8_t* rB = wt + 256 * sB + 8 * (t & 1);
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+      const int q = 2 * b + (t >> 1);
+      const uint2 qa = *reinterpret_cast<const uint2*>(rA + 16 * (q ^ (sA & 6)));
+      const uint2 qb = *reinterpret_cast<const uint2*>(rB + 16 * (q ^ (sB & 6)));
+      const uint32_t a[4] = {qa.x, qb.x, qa.y, qb.y};
+      const uint2 xb = *reinterpret_cast<const uint2*>(xr + 32 * b + 8 * t);
+      int cc[4];
+      mma_s8s8_k32(cc, a, xb.x, xb.y, MAGIC_I, MAGIC_I);
+      const float2 D = *reinterpret_cast<const float2*>(tab + b * 16 + sA);
+      const float4 dx = *reinterpret_cast<const float4*>(dsT + b * MAXB + 2 * t);
+      acc[0] = fmaf(D.x * dx.x, magic_f(cc[0]), acc[0]);
+      acc[1] = fmaf(D.x * dx.z, magic_f(cc[1]), acc[1]);
+      acc[2] = fmaf(D.y * dx.x, magic_f(cc[2]), acc[2]);
+      acc[3] = fmaf(D.y * dx.z, magic_f(cc[3]), acc[3]);
+    }
+  }
+  __syncwarp();  // table and slot reads done before the next unit overwrites them
+}
+
+FAK_DEV void epilogue(int tile, const float (&v)[4], int lane, int N, int B, float* __restrict__ y, int64_t ldy,
+                      const float* __restrict__ bias, int epi) {
+  const int g = lane >> 2, t = lane & 3;
+  const int r0 = tile * 16, tok0 = 2 * t, tok1 = 2 * t + 1;
+  const int rowa = r0 + g, rowb = r0 + g + 8;
+  if (epi == EPI_SWIGLU) {
+    // rows [r0, r0+8) are the gate rows of outputs [r0/2, r0/2+8), rows [r0+8, r0+16) the up rows
+    if (rowb < N) {
+      const int o = (r0 >> 1) + g;
+      const float bg = bias ? bias[rowa] : 0.f, bu = bias ? bias[rowb] : 0.f;
+      if (tok0 < B) y[(int64_t)tok0 * ldy + o] = silu(v[0] + bg) * (v[2] + bu);
+      if (tok1 < B) y[(int64_t)tok1 * ldy + o] = silu(v[1] + bg) * (v[3] + bu);
+    }
+    return;
+  }
+#pragma unroll
+  for (int half = 0; half < 2; half++) {
+    const int row = half ? rowb : rowa;
+    if (row >= N) continue;
+    const float bv = bias ? bias[row] : 0.f;
+    const float v0 = v[2 * half] + bv, v1 = v[2 * half + 1] + bv;
+    if (tok0 < B) {
+      float* p = y + (int64_t)tok0 * ldy + row;
+      *p = epi == EPI_ADD ? *p + v0 : v0;
+    }
+    if (tok1 < B) {
+      float* p = y + (int64_t)tok1 * ldy + row;
+      *p = epi == EPI_ADD ? *p + v1 : v1;
+    }
+  }
+}
+
+template <int QT, int W, int R>
+__global__ void __launch_bounds__(W * 32, 1)
+k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
+        int B, float* __restrict__ y, int64_t ldy, const float* __restrict__ bias, int epi,
+        float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo) {
+  constexpr int UT = Tile<QT>::UT;
+  constexpr int TABF = Tile<QT>::TABF;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const TSmem L = tsmem(QT, W, R, geo);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slice = blockIdx.x % geo.S, cta = blockIdx.x / geo.S;
+  const int u0 = slice * geo.Us;
+  const int nu = min(geo.Us, geo.U - u0);          // units of this slice
+  const int k0 = u0 * 256;
+  const int kb = min(nu * 256, K - k0);            // valid activation columns of the slice
+  int8_t* xs = reinterpret_cast<int8_t*>(sm + L.xs);
+  float2* dsr = reinterpret_cast<float2*>(sm + L.dsr);
+  float2* dsT = reinterpret_cast<float2*>(sm + L.dsT);
+  int* czT = reinterpret_cast<int*>(sm + L.czT);
+  float* tab = reinterpret_cast<float*>(sm + L.tab) + warp * TABF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
+  uint64_t* bar = bars + warp * R;
+  uint64_t* act_bar = bars + W * R;
+  uint8_t* ring = sm + L.ring + (size_t)warp * R * UT;
+
+  const int wg = cta * W + warp, wstride = geo.P * W;
+  const int n_my = wg < geo.T ? (geo.T - 1 - wg) / wstride + 1 : 0;
+  const int Q = n_my * nu;
+
+  if (lane == 0) {
+    for (int i = 0; i < R; i++) tc::mbar_init(&bar[i], 1);
+    if (warp == 0) tc::mbar_init(act_bar, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int q) {
+    if (q >= Q) return;
+    const int tile = wg + (q / nu) * wstride;
+    const int u = u0 + q % nu;
+    uint64_t* b = &bar[q % R];
+    tc::mbar_arrive_expect_tx(b, UT);
+    bulk_g2s(ring + (q % R) * UT, Wt + ((int64_t)tile * geo.U + u) * UT, UT, b);
+  };
+  // weights do not depend on the previous kernel: their first copies go out before the wait
+  if (lane == 0)
+    for (int q = 0; q < R - 1; q++) issue(q);
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    const uint32_t dsb = (uint32_t)(kb / 4);  // (scale, sum) bytes of the slice per token
+    tc::mbar_arrive_expect_tx(act_bar, (uint32_t)B * ((uint32_t)kb + dsb));
+    for (int b = 0; b < B; b++) {
+      bulk_g2s(xs + b * geo.xstride, qx + (int64_t)b * K + k0, (uint32_t)kb, act_bar);
+      bulk_g2s(dsr + b * geo.dstride, ds + (int64_t)b * (K / 32) + k0 / 32, dsb, act_bar);
+    }
+  }
+  // zero the activation columns no copy writes (missing tokens, padding past K)
+  for (int i = threadIdx.x; i < MAXB * (nu * 256 / 16); i += W * 32) {
+    const int b = i / (nu * 16), c = (i % (nu * 16)) * 16;
+    if (b >= B || c >= kb) *reinterpret_cast<uint4*>(xs + b * geo.xstride + c) = make_uint4(0, 0, 0, 0);
+  }
+  tc::mbar_wait(act_bar, 0, err);
+  for (int i = threadIdx.x; i < nu * 8 * MAXB; i += W * 32) {
+    const int blk = i / MAXB, b = i % MAXB;
+    dsT[i] = (b < B && blk * 32 < kb) ? dsr[b * geo.dstride + blk] : make_float2(0.f, 0.f);
+  }
+  if constexpr (QT == QT_Q6_K) {
+    for (int i = threadIdx.x; i < nu * 16 * MAXB; i += W * 32) {
+      const int k16 = i / MAXB, b = i % MAXB;
+      const int4 v = *reinterpret_cast<const int4*>(xs + b * geo.xstride + 16 * k16);
+      int s = __dp4a(v.x, 0x01010101, 0);
+      s = __dp4a(v.y, 0x01010101, s);
+      s = __dp4a(v.z, 0x01010101, s);
+      s = __dp4a(v.w, 0x01010101, s);
+      czT[i] = MAGIC_I - 32 * s;
+    }
+  }
+  __syncthreads();
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int g = lane >> 2;
+  for (int q = 0; q < Q; q++) {
+    if (lane == 0) issue(q + R - 1);  // into the slot released at the end of iteration q-1
+    tc::mbar_wait(&bar[q % R], (uint32_t)((q / R) & 1), err);
+    const int ul = q % nu;
+    unit_tile<QT>(ring + (q % R) * UT, tab, xs + g * geo.xstride + ul * 256, dsT + ul * 8 * MAXB,
+                  QT == QT_Q6_K ? czT + ul * 16 * MAXB : nullptr, lane, acc);
+    if (ul != nu - 1) continue;
+    const int tile = wg + (q / nu) * wstride;
+    if (geo.S == 1) {
+      epilogue(tile, acc, lane, N, B, y, ldy, bias, epi);
+    } else {
+      float4* mine = reinterpret_cast<float4*>(part + ((size_t)slice * geo.T + tile) * 128) + lane;
+      *mine = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      __threadfence();
+      __syncwarp();
+      int old = 0;
+      if (lane == 0) old = atomicAdd(&cnt[tile], 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == geo.S - 1) {  // last slice of this tile: reduce in slice order
+        __threadfence();
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s = 0; s < geo.S; s++) {
+          const float4 p = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)s * geo.T + tile) * 128) + lane);
+          v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
+        }
+        epilogue(tile, v, lane, N, B, y, ldy, bias, epi);
+        if (lane == 0) cnt[tile] = 0;  // ready for the next launch
+      }
+    }
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+  }
+  pdl_launch_dependents();
+}
+
+struct Plan {
+  int W, R;
+  TGeo geo;
+  int smem;
+};
+
+int tile_bytes(int qt) { return qt == QT_Q4_K ? 2304 : (qt == QT_Q6_K ? 3360 : 4352); }
+
+// Choose (warps per CTA, ring depth) and the K split.  Depends only on the matrix shape and the
+// GPU, never on the batch size, so batched and serial decoding reduce in the same order.
+Plan make_plan(int qt, int64_t N, int64_t K, int n_sm, int max_smem, int force_w, int force_r, int force_s) {
+  const int T = (int)((N + 15) / 16);
+  const int U = (int)((K + 255) / 256);
+  static const int cand[][2] = {{16, 3}, {16, 2}, {8, 4}, {8, 3}, {8, 2}};
+  for (auto& c : cand) {
+    const int W = force_w ? force_w : c[0], R = force_r ? force_r : c[1];
+    // enough (tile, slice) items to give every warp of the GPU work
+    int S = force_s ? force_s : (int)std::min<int64_t>(U, std::max<int64_t>(1, ((int64_t)n_sm * W + T - 1) / T));
+    S = std::min(S, n_sm);
+    int Us = (U + S - 1) / S;
+    S = (U + Us - 1) / Us;
+    TGeo g;
+    g.T = T;
+    g.U = U;
+    g.S = S;
+    g.Us = Us;
+    g.P = std::max(1, n_sm / S);
+    g.xstride = ((Us * 256 + 127) / 128) * 128 + 32;
+    g.dstride = Us * 8;
+    const TSmem L = tsmem(qt, W, R, g);
+    if (L.total <= max_smem) return Plan{W, R, g, L.total};
+    if (force_w && force_r) break;
+  }
+  TORCH_CHECK(false, "tgemv: no launch configuration fits in shared memory for K=", K);
+  return Plan{};
+}
+
+}  // namespace
+
+int64_t tgemv_unit_bytes(int64_t qtype) { return tile_bytes((int)qtype); }
+
+// Scratch floats / counters the split-K reduction of this shape needs.
+std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device) {
+  int n_sm = 0, max_smem = 0;
+  FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, (int)device));
+  FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, (int)device));
+  Plan p = make_plan((int)qtype, N, K, n_sm, max_smem, 0, 0, 0);
+  return {p.geo.S > 1 ? (int64_t)p.geo.S * p.geo.T * 128 : 0, p.geo.S > 1 ? (int64_t)p.geo.T : 0, p.geo.S, p.W,
+          p.R, p.smem};
+}
+
+// w: tile-packed weights (uint8, ceil(N/16) * ceil(K/256) unit tiles); qx [B, K] int8; ds [B, K/32, 2];
+// y [B, *] f32 (row stride y.stride(0)); part/cnt: split-K scratch (cnt zero-initialised; every
+// launch leaves it zero again).  flags: bits 0-4 warps, 5-8 ring depth, 9-16 K slices (overrides).
+void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, torch::Tensor qx, torch::Tensor ds, int64_t B,
+           torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part, torch::Tensor cnt,
+           c10::optional<torch::Tensor> err, int64_t flags) {
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "tgemv: w cuda uint8");
+  TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "tgemv: qtype");
+  TORCH_CHECK(K % 64 == 0 && (qtype == QT_Q8_0 || K % 256 == 0), "tgemv: K must be a multiple of 256 (64 for Q8_0)");
+  const int64_t T = (N + 15) / 16, U = (K + 255) / 256;
+  TORCH_CHECK(w.numel() >= T * U * tile_bytes((int)qtype), "tgemv: weight buffer smaller than the tile-packed size");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "tgemv: weight alignment");
+  TORCH_CHECK(qx.scalar_type() == torch::kInt8 && qx.is_contiguous() && qx.numel() >= B * K, "tgemv: qx");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(qx.data_ptr()) % 16 == 0, "tgemv: qx alignment");
+  TORCH_CHECK(ds.scalar_type() == torch::kFloat32 && ds.is_contiguous() && ds.numel() >= B * K / 16, "tgemv: ds");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ds.data_ptr()) % 16 == 0, "tgemv: ds alignment");
+  TORCH_CHECK(y.scalar_type() == torch::kFloat32 && y.dim() == 2 && y.stride(1) == 1, "tgemv: y [B, *] f32");
+  TORCH_CHECK(B >= 1 && B <= MAXB, "tgemv: 1 <= B <= 8");
+  if (epi == EPI_SWIGLU) TORCH_CHECK(N % 16 == 0, "tgemv: SwiGLU needs 8-row interleaved gate/up blocks");
+  TORCH_CHECK(y.size(0) >= B && y.size(1) >= (epi == EPI_SWIGLU ? N / 2 : N), "tgemv: y too small");
+  const float* bp = nullptr;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "tgemv: bias");
+    bp = bias->data_ptr<float>();
+  }
+  static int n_sm = 0, max_smem = 0;
+  if (!n_sm) {
+    FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, w.get_device()));
+    FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, w.get_device()));
+  }
+  Plan p = make_plan((int)qtype, N, K, n_sm, max_smem, (int)(flags & 31), (int)((flags >> 5) & 15),
+                     (int)((flags >> 9) & 255));
+  if (p.geo.S > 1) {
+    TORCH_CHECK(part.scalar_type() == torch::kFloat32 && part.numel() >= (int64_t)p.geo.S * p.geo.T * 128,
+                "tgemv: split-K scratch too small");
+    TORCH_CHECK(cnt.scalar_type() == torch::kInt32 && cnt.numel() >= p.geo.T, "tgemv: split-K counters too small");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(p.W * 32);
+  cfg.gridDim = dim3(p.geo.P * p.geo.S);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
+  auto go = [&](auto kern) {
+    FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.data_ptr<uint8_t>(), (int)N, (int)K,
+                                      (const int8_t*)qx.data_ptr<int8_t>(),
+                                      reinterpret_cast<const float2*>(ds.data_ptr<float>()), (int)B,
+                                      y.data_ptr<float>(), (int64_t)y.stride(0), bp, (int)epi,
+                                      p.geo.S > 1 ? part.data_ptr<float>() : nullptr,
+                                      p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo));
+  };
+#define FAK_TG(QTV)                                                       \
+  {                                                                       \
+    if (p.W == 16 && p.R == 3) go(k_tgemv<QTV, 16, 3>);                   \
+    else if (p.W == 16 && p.R == 2) go(k_tgemv<QTV, 16, 2>);              \
+    else if (p.W == 8 && p.R == 4) go(k_tgemv<QTV, 8, 4>);                \
+    else if (p.W == 8 && p.R == 3) go(k_tgemv<QTV, 8, 3>);                \
+    else if (p.W == 8 && p.R == 2) go(k_tgemv<QTV, 8, 2>);                \
+    else TORCH_CHECK(false, "tgemv: unsupported (warps, depth) ", p.W, ",", p.R); \
+  }
+  if (qtype == QT_Q4_K) FAK_TG(QT_Q4_K)
+  else if (qtype == QT_Q6_K) FAK_TG(QT_Q6_K)
+  else FAK_TG(QT_Q8_0)
+#undef FAK_TG
+}

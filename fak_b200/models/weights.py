@@ -40,6 +40,7 @@ class QuantWeight:
     cols: int
     pitch: int
     _dense: torch.Tensor | None = None
+    tp: torch.Tensor | None = None  # tile-packed copy for the decode GEMV (``ops.quant.tile_pack``)
 
     @classmethod
     def from_rows(cls, rows_u8: torch.Tensor, qtype: int, cols: int, device: torch.device) -> "QuantWeight":
@@ -62,6 +63,12 @@ class QuantWeight:
         if cache:
             self._dense = d
         return d
+
+    def pack(self) -> "QuantWeight":
+        """Build the tile-packed copy the decode GEMV reads (Q4_K / Q6_K / Q8_0 matrices)."""
+        if self.tp is None and self.qtype in dq.TILE_UNIT_BYTES and self.buf.is_cuda:
+            self.tp = dq.tile_pack(self.buf, self.qtype, self.rows, self.cols, self.pitch)
+        return self
 
     @property
     def nbytes(self) -> int:
@@ -329,6 +336,12 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
             if tp_size > 1:
                 draw = _col_block_slice(draw, dt, ds_[1], f0, f1)
             L.down = QuantWeight.from_rows(draw, dt, f1 - f0, device)
+        for s, _ in L.qkv:
+            s.pack()
+        L.o.pack()
+        if L.gate_up is not None:
+            L.gate_up.pack()
+            L.down.pack()
         if prefill_dense:
             for s, _ in L.qkv:
                 s.dense()
@@ -345,6 +358,7 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
     else:
         shape, t, raw = quant("token_embd.weight" if cfg.tie_embeddings else "output.weight")
         lm_head = QuantWeight.from_rows(raw[v0:v1].contiguous(), t, shape[1], device)
+    lm_head.pack()
     close()
     return ModelWeights(cfg, embed, layers, final_norm, lm_head, q_heads, kv_heads, (f0, f1), tp_rank, tp_size)
 

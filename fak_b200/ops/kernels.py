@@ -42,9 +42,38 @@ def quant_act(x: torch.Tensor, act: ActQ, gamma: torch.Tensor | None = None, eps
 DP4A_MAX_B = 1
 
 
-def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None, epi: int = EPI_STORE) -> None:
-    """y[:B] (op)= W . x for a decode batch (w: models.weights.QuantWeight); chunks of 8 tokens."""
+# split-K scratch of the tile-packed GEMV, one per device: partial sums and per-tile tickets.
+# Launches on one stream reuse it in turn; the kernel leaves the tickets at zero.
+_TG_PART_FLOATS = 1 << 21
+_TG_TICKETS = 1 << 16
+_tg_ws: dict = {}
+
+
+def tgemv_workspace(device) -> tuple[torch.Tensor, torch.Tensor]:
+    key = torch.device(device)
+    ws = _tg_ws.get(key)
+    if ws is None:
+        ws = (torch.zeros(_TG_PART_FLOATS, dtype=torch.float32, device=key),
+              torch.zeros(_TG_TICKETS, dtype=torch.int32, device=key))
+        _tg_ws[key] = ws
+    return ws
+
+
+def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None, epi: int = EPI_STORE,
+         flags: int = 0) -> None:
+    """y[:B] (op)= W . x for a decode batch (w: models.weights.QuantWeight); chunks of 8 tokens.
+
+    Matrices with a tile-packed copy (``QuantWeight.pack``) run the tile-packed tensor-core GEMV;
+    others the row-major kernels."""
     C = ext()
+    if w.tp is not None:
+        part, cnt = tgemv_workspace(w.tp.device)
+        for b0 in range(0, B, GEMV_MAX_B):
+            nb = min(GEMV_MAX_B, B - b0)
+            C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q[b0:b0 + nb], act.ds[b0:b0 + nb], nb, y[b0:b0 + nb], bias,
+                    epi, part, cnt, None, flags)
+            count()
+        return
     for b0 in range(0, B, GEMV_MAX_B):
         nb = min(GEMV_MAX_B, B - b0)
         q = act.q[b0:b0 + nb]

@@ -57,3 +57,55 @@ def synth_quantized(shape: tuple[int, ...], ggml_type: int, seed: int, std: floa
     if t == QT_BF16:
         return x.bfloat16().view(torch.uint8)
     return quantize_blocks(x, t)
+
+
+# ---- tile-packed layout of the decode GEMV ----------------------------------------------------
+# Rows in tiles of 16, each row's blocks in 256-weight units; one (tile, unit) is a contiguous
+# "unit tile" whose fields are split into planes.  Plane row ("slot") s holds tile row
+# (s >> 1) + 8 (s & 1); 16-byte chunks of the quant planes are XOR-swizzled by slot.  The block
+# bytes are unchanged, only placed differently.
+TILE_UNIT_BYTES = {QT_Q4_K: 2304, QT_Q6_K: 3360, QT_Q8_0: 4352}
+SLOT_ROWS = [(s >> 1) + 8 * (s & 1) for s in range(16)]
+
+
+def _swizzle(plane: torch.Tensor, key) -> torch.Tensor:
+    """plane [..., 16 slots, C chunks, 16]: chunk position p of slot s holds chunk p ^ key(s)."""
+    C = plane.shape[-2]
+    idx = torch.tensor([[p ^ key(s) for p in range(C)] for s in range(16)], device=plane.device)
+    return plane[..., torch.arange(16, device=plane.device)[:, None], idx, :]
+
+
+def tile_pack(buf: torch.Tensor, qtype: int, rows: int, cols: int, pitch: int) -> torch.Tensor:
+    """Row-pitched GGML rows -> tile-packed bytes [ceil(rows/16), ceil(cols/256), unit bytes]."""
+    qtype = int(qtype)
+    if qtype not in TILE_UNIT_BYTES:
+        raise ValueError(f"tile_pack: unsupported block type {qtype}")
+    T, U = -(-rows // 16), -(-cols // 256)
+    rb = row_bytes(qtype, cols)
+    m = buf[: rows * pitch].view(rows, pitch)[:, :rb]
+    if qtype == QT_Q8_0:
+        nblk = cols // 32
+        blocks = torch.zeros(T * 16, U * 8, 34, dtype=torch.uint8, device=buf.device)
+        blocks[:rows, :nblk] = m.reshape(rows, nblk, 34)
+        x = blocks.view(T, 16, U, 8, 34).permute(0, 2, 1, 3, 4)[:, :, SLOT_ROWS]  # [T,U,16,8,34]
+        d = x[..., :2].reshape(T, U, 16 * 16)
+        qs = _swizzle(x[..., 2:].reshape(T, U, 16, 16, 16), lambda s: s & 6).reshape(T, U, 4096)
+        planes = [qs, d]
+    else:
+        ub = 144 if qtype == QT_Q4_K else 210
+        full = torch.zeros(T * 16, U * ub, dtype=torch.uint8, device=buf.device)
+        full[:rows] = m
+        x = full.view(T, 16, U, ub).permute(0, 2, 1, 3)[:, :, SLOT_ROWS]  # [T,U,16,ub]
+        if qtype == QT_Q4_K:
+            hdr = x[..., :16].reshape(T, U, 256)
+            qs = _swizzle(x[..., 16:144].reshape(T, U, 16, 8, 16), lambda s: s & 6).reshape(T, U, 2048)
+            planes = [hdr, qs]
+        else:
+            ql = _swizzle(x[..., :128].reshape(T, U, 16, 8, 16), lambda s: (s >> 1) & 7).reshape(T, U, 2048)
+            qh = _swizzle(x[..., 128:192].reshape(T, U, 16, 4, 16), lambda s: (s >> 1) & 3).reshape(T, U, 1024)
+            sc = x[..., 192:208].reshape(T, U, 256)
+            d = x[..., 208:210].reshape(T, U, 32)
+            planes = [ql, qh, sc, d]
+    out = torch.cat(planes, dim=-1).contiguous()
+    assert out.shape[-1] == TILE_UNIT_BYTES[qtype]
+    return out

@@ -243,3 +243,65 @@ def test_gemm_tcgen05(M, N, K, epi):
     torch.cuda.synchronize()
     assert err.item() == 0
     assert torch.allclose(out, ref, atol=2e-3 * math.sqrt(K), rtol=1e-2), (out - ref).abs().max()
+
+
+def _tg_case(qt, N, Kd, B, seed=3):
+    from fak_b200.models.weights import QuantWeight
+    from fak_b200.ops import kernels as K
+    rng = np.random.default_rng(seed)
+    Wf = (rng.standard_normal((N, Kd)) * 0.05).astype(np.float32)
+    raw = Q.quantize(Wf, qt).reshape(N, -1)
+    w = QuantWeight.from_rows(torch.from_numpy(raw), int(qt), Kd, torch.device("cuda")).pack()
+    Wd = torch.from_numpy(Q.dequantize(raw.reshape(-1), qt).reshape(N, Kd)).cuda()
+    x = torch.randn(B, Kd, device="cuda", generator=torch.Generator("cuda").manual_seed(seed))
+    act = K.ActQ(8, Kd, "cuda")
+    K.quant_act(x, act)
+    return w, Wd, x, act
+
+
+@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("B", [1, 5, 8])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("N", [576, 16 * 2400])
+def test_tgemv_tile_packed(qt, blk, B, epi, N):
+    """Tile-packed tensor-core GEMV vs an fp32 reference; N=576 runs split-K, the tall matrix one
+    slice per tile."""
+    from fak_b200.ops import kernels as K
+    Kd = 1024 if qt != GGMLType.Q8_0 else 576
+    w, Wd, x, act = _tg_case(qt, N, Kd, B)
+    bias = torch.randn(N, device="cuda") * 0.1
+    ref = x @ Wd.T + bias
+    if epi == K.EPI_SWIGLU:
+        ref = _swiglu_ref(ref)
+        y = torch.zeros(B, N // 2, device="cuda")
+    else:
+        y = torch.randn(B, N, device="cuda")
+        if epi == K.EPI_ADD:
+            ref = ref + y
+    K.gemv(w, act, B, y, bias, epi)
+    torch.cuda.synchronize()
+    err = (y - ref).abs().max().item() / ref.abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
+    tol_cos, tol_err = (0.999, 0.06) if epi == K.EPI_SWIGLU else (0.9995, 0.03)
+    assert cos > tol_cos and err < tol_err, (cos, err)
+
+
+@pytest.mark.parametrize("qt,blk", QTYPES)
+def test_tgemv_batch_invariant_and_repeatable(qt, blk):
+    """Each token's output is bit-identical whether it runs alone or in a batch of 8, and the
+    split-K tickets are left at zero so a second launch gives the same bits."""
+    from fak_b200.ops import kernels as K
+    Kd = 3584 if qt != GGMLType.Q8_0 else 576
+    w, Wd, x, act = _tg_case(qt, 512, Kd, 8, seed=7)
+    y8 = torch.zeros(8, 512, device="cuda")
+    K.gemv(w, act, 8, y8)
+    again = torch.zeros_like(y8)
+    K.gemv(w, act, 8, again)
+    assert torch.equal(y8, again)
+    for b in range(8):
+        solo = K.ActQ(8, Kd, "cuda")
+        K.quant_act(x[b:b + 1], solo)
+        y1 = torch.zeros(1, 512, device="cuda")
+        K.gemv(w, solo, 1, y1)
+        assert torch.equal(y1[0], y8[b]), b
+    assert not K.tgemv_workspace("cuda")[1].any()
