@@ -426,6 +426,8 @@ class CpuModel {
   int n_ctx = 0;
 };
 
+void register_radix(py::module& m);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fak_b200 C++ CPU runtime: GGUF-block decoder forward (oracle + CPU serving path)";
   py::class_<CpuModel>(m, "CpuModel")
@@ -436,4 +438,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("step", &CpuModel::step, py::call_guard<py::gil_scoped_release>())
       .def("generate", &CpuModel::generate, py::call_guard<py::gil_scoped_release>())
       .def("threads", &CpuModel::threads);
+  register_radix(m);
 }

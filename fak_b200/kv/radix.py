@@ -14,11 +14,13 @@ Insert :211, split :149, LRU evictToBudget :252).  Differences by design:
   (the reference clones the matched KV into the new session, kv.go:14);
 * eviction is LRU over leaves not referenced by any live sequence.
 
-A C++ implementation with the same interface (``fak_b200._cpu.RadixCache``) is used when
-the native extension is built; this module is its executable specification and fallback.
+A C++ implementation with the same interface (``fak_b200._cpu.PagePool`` / ``RadixCache``,
+csrc/cpu/radix.cpp) replaces these classes when the native extension is built (set
+``FAK_PY_RADIX=1`` to keep the Python ones); this module is its executable specification.
 """
 from __future__ import annotations
 
+import os
 import time
 
 
@@ -195,3 +197,13 @@ class RadixCache:
         return {"cached_pages": self.n_cached_pages, "hit_tokens": self.hits_tokens,
                 "lookup_tokens": self.lookup_tokens,
                 "hit_rate": self.hits_tokens / self.lookup_tokens if self.lookup_tokens else 0.0}
+
+
+# native implementation (same interface) when the C++ extension is built
+PyPagePool, PyRadixCache = PagePool, RadixCache
+if not os.environ.get("FAK_PY_RADIX"):
+    try:
+        import torch  # noqa: F401  (loads the libraries the extension links against)
+        from .._cpu import PagePool, RadixCache  # noqa: F811
+    except ImportError:
+        pass

@@ -1,10 +1,25 @@
-"""Paged KV pool and radix prefix cache (CPU)."""
+"""Paged KV pool and radix prefix cache (CPU): the Python specification and the C++ implementation."""
+import numpy as np
 import pytest
 
-from fak_b200.kv import OutOfPages, PagePool, RadixCache
+from fak_b200.kv import radix as R
+from fak_b200.kv import OutOfPages
+
+IMPLS = [pytest.param((R.PyPagePool, R.PyRadixCache), id="python")]
+try:
+    from fak_b200 import _cpu
+    IMPLS.append(pytest.param((_cpu.PagePool, _cpu.RadixCache), id="native"))
+except ImportError:
+    pass
 
 
-def test_pool_refcounts():
+@pytest.fixture(params=IMPLS)
+def impl(request):
+    return request.param
+
+
+def test_pool_refcounts(impl):
+    PagePool, _ = impl
     p = PagePool(8, reserve=1)
     a = p.alloc(3)
     assert 0 not in a and p.n_free() == 4
@@ -19,7 +34,8 @@ def test_pool_refcounts():
         p.release(a[:1])
 
 
-def test_radix_match_insert_split_evict():
+def test_radix_match_insert_split_evict(impl):
+    PagePool, RadixCache = impl
     pool = PagePool(64, reserve=1)
     rc = RadixCache(pool, page_size=4)
     t1 = list(range(12))
@@ -48,7 +64,8 @@ def test_radix_match_insert_split_evict():
     assert st["hit_tokens"] > 0 and 0 < st["hit_rate"] <= 1
 
 
-def test_radix_does_not_evict_live_pages():
+def test_radix_does_not_evict_live_pages(impl):
+    PagePool, RadixCache = impl
     pool = PagePool(16, reserve=1)
     rc = RadixCache(pool, page_size=4)
     t = list(range(8))
@@ -80,3 +97,32 @@ def test_tp_head_and_ffn_assignment():
         assert vs[-1][1] == cfg.vocab_size and sum(b - a for a, b in vs) == cfg.vocab_size
     # TP=8 on 28 q heads / 4 KV heads: groups of 7 split 4 + 3
     assert [len(head_assignment(cfg, r, 8)[0]) for r in range(8)] == [4, 3] * 4
+
+
+def test_native_radix_matches_python_on_agent_turns():
+    """Randomised multi-agent turns: both implementations return the same hits, pages and stats."""
+    if len(IMPLS) < 2:
+        pytest.skip("native extension not built")
+    rng = np.random.default_rng(3)
+    sims = []
+    for PagePool, RadixCache in ((R.PyPagePool, R.PyRadixCache), (_cpu.PagePool, _cpu.RadixCache)):
+        pool = PagePool(600, reserve=1)
+        rc = RadixCache(pool, 16)
+        r2 = np.random.default_rng(3)
+        prefix = r2.integers(0, 1000, 512).tolist()
+        hist = [list(prefix) for _ in range(4)]
+        log = []
+        for turn in range(6):
+            for a in range(4):
+                hist[a] += r2.integers(0, 1000, int(r2.integers(1, 60))).tolist()
+                n, pages = rc.lookup(hist[a], max_tokens=len(hist[a]) - 1)
+                need = -(-(len(hist[a]) + 20) // 16) - len(pages)
+                if pool.n_free() < need:
+                    rc.evict(need - pool.n_free())
+                allp = pages + pool.alloc(need)
+                hist[a] += r2.integers(0, 1000, 20).tolist()
+                rc.insert(hist[a], allp)
+                pool.release(allp)
+                log.append((n, list(pages), pool.n_free()))
+        sims.append((log, rc.stats(), rc.n_cached_pages))
+    assert sims[0] == sims[1]
