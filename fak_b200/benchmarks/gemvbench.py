@@ -44,7 +44,8 @@ def main(argv=None):
 
     def run(w):
         if args.kernel == "tgemv":
-            C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q, act.ds, args.batch, y, None, 0, part, cnt, None, args.flags)
+            C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q, act.ds, None, None, 0.0, args.batch, y, None, 0, part, cnt,
+                    None, args.flags)
         elif args.kernel == "qmmv":
             C.qmmv(w.buf, w.qtype, w.rows, w.cols, w.pitch, act.q, act.ds, args.batch, y, None, 0, args.flags)
         else:

@@ -10,7 +10,8 @@ void qgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, 
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
-                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo);
+                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
+                      c10::optional<torch::Tensor> tickets);
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
                        torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out);
@@ -22,7 +23,8 @@ void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Te
              c10::optional<torch::Tensor> q_f32, c10::optional<torch::Tensor> q_bf16, torch::Tensor k_cache,
              torch::Tensor v_cache);
 void rmsnorm_bf16(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor y);
-void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out);
+void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out, c10::optional<torch::Tensor> keys,
+                 c10::optional<torch::Tensor> tickets);
 void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, torch::Tensor qx, torch::Tensor ds,
           int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, int64_t flags);
 void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx,
@@ -39,9 +41,10 @@ void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor w
                torch::Tensor ids, torch::Tensor wts);
 void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_t max_chunks, torch::Tensor chunk_expert,
                torch::Tensor chunk_pairs, torch::Tensor n_chunks);
-void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, torch::Tensor qx, torch::Tensor ds, int64_t B,
-           torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part, torch::Tensor cnt,
-           c10::optional<torch::Tensor> err, int64_t flags);
+void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<torch::Tensor> qx,
+           c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
+           double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
+           torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags);
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device);
 int64_t tgemv_unit_bytes(int64_t qtype);
 void moe_qmmv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, int64_t pitch, torch::Tensor qx,
@@ -61,12 +64,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &decode_attention, pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"),
         pybind11::arg("block_table"), pybind11::arg("ctx_len"), pybind11::arg("n_split"),
         pybind11::arg("pages_per_split"), pybind11::arg("out"), pybind11::arg("qx"), pybind11::arg("ds"),
-        pybind11::arg("workspace"), pybind11::arg("ldo") = 0);
+        pybind11::arg("workspace"), pybind11::arg("ldo") = 0, pybind11::arg("tickets") = pybind11::none());
   m.def("prefill_attention", &prefill_attention);
   m.def("embed", &embed);
   m.def("rope_kv", &rope_kv);
   m.def("rmsnorm_bf16", &rmsnorm_bf16);
-  m.def("argmax_rows", &argmax_rows);
+  m.def("argmax_rows", &argmax_rows, pybind11::arg("logits"), pybind11::arg("V"), pybind11::arg("out"),
+        pybind11::arg("keys") = pybind11::none(), pybind11::arg("tickets") = pybind11::none());
   m.def("p2p_allgather_cols", &p2p_allgather_cols);
   m.def("p2p_allreduce_add", &p2p_allreduce_add);
   m.def("p2p_argmax", &p2p_argmax);
@@ -79,7 +83,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("bias"), pybind11::arg("epi"), pybind11::arg("flags") = 0);
   m.def("quant_act_wide", &quant_act_wide);
   m.def("tgemv", &tgemv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
-        pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"), pybind11::arg("bias"),
+        pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
+        pybind11::arg("B"), pybind11::arg("y"), pybind11::arg("bias"),
         pybind11::arg("epi"), pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
         pybind11::arg("flags") = 0);
   m.def("tgemv_workspace", &tgemv_workspace);

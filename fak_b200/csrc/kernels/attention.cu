@@ -54,10 +54,11 @@ FAK_DEV void warp_quant_store(float v, int8_t* qdst, float2* dsdst, int lane) {
 // =============================================================================================
 // decode
 // =============================================================================================
+constexpr int DEC_STAGES = 3;  // pages in flight per warp (ring depth)
 template <int D>
 struct DecodeSmem {
-  __nv_bfloat16 k[4][2][PAGE][D + 8];
-  __nv_bfloat16 v[4][2][PAGE][D + 8];
+  __nv_bfloat16 k[4][DEC_STAGES][PAGE][D + 8];
+  __nv_bfloat16 v[4][DEC_STAGES][PAGE][D + 8];
 };
 
 template <int D>
@@ -66,7 +67,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
               const int* __restrict__ block_table, int bt_stride, const int* __restrict__ ctx_len, int H, int Hkv,
               int n_split, int pages_per_split, float scale_log2, float* __restrict__ part_o,
               float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
-              float2* __restrict__ ds, int ldo) {
+              float2* __restrict__ ds, int ldo, int* __restrict__ tickets) {
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -124,17 +125,21 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
     cp_async_commit();
   };
 
-  int p = p_begin + warp;
+  // warp w takes pages p_begin + w, + 4, ...; DEC_STAGES - 1 of them stay in flight while it
+  // computes on one (an empty commit group keeps the group count uniform past the end)
+  const int p0 = p_begin + warp;
+#pragma unroll
+  for (int i = 0; i < DEC_STAGES - 1; i++) {
+    if (p0 + 4 * i < p_end) issue_page(p0 + 4 * i, i);
+    else cp_async_commit();
+  }
   int buf = 0;
-  if (p < p_end) issue_page(p, 0);
-  for (; p < p_end; p += 4) {
-    const int pn = p + 4;
-    if (pn < p_end) {
-      issue_page(pn, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+  for (int p = p0, it = 0; p < p_end; p += 4, it++) {
+    const int pn = p + 4 * (DEC_STAGES - 1);
+    if (pn < p_end) issue_page(pn, (it + DEC_STAGES - 1) % DEC_STAGES);
+    else cp_async_commit();
+    cp_async_wait<DEC_STAGES - 1>();
+    buf = it % DEC_STAGES;
     __syncwarp();
     // S = Q K^T for 16 tokens
     float s[2][4];
@@ -194,8 +199,8 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
       }
     }
     __syncwarp();
-    buf ^= 1;
   }
+  cp_async_wait<0>();
   l0 = quad_sum(l0);
   l1 = quad_sum(l1);
 
@@ -248,6 +253,38 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
       }
     }
   }
+  if (n_split == 1 || tickets == nullptr) return;
+  // the last split CTA of this (sequence, KV group) merges all splits (same order and arithmetic
+  // as k_decode_combine) and leaves its ticket at zero for the next launch
+  __shared__ int s_ticket;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_ticket = atomicAdd(&tickets[b * Hkv + kvh], 1);
+  __syncthreads();
+  if (s_ticket != n_split - 1) return;
+  __threadfence();
+  for (int r = warp; r < G; r += 4) {
+    const int h = kvh * G + r;
+    const int64_t base = ((int64_t)b * H + h) * n_split;
+    float mstar = NEG_INF;
+    for (int s = 0; s < n_split; s++) mstar = fmaxf(mstar, __ldcg(&part_ml[base + s].x));
+    const float mb = mstar == NEG_INF ? 0.f : mstar;
+    for (int d0 = 0; d0 < D; d0 += 32) {
+      const int dd = d0 + lane;
+      float L = 0.f, acc = 0.f;
+      for (int s = 0; s < n_split; s++) {
+        const float2 ml = __ldcg(&part_ml[base + s]);
+        const float f = exp2f(ml.x - mb);
+        L += f * ml.y;
+        acc += f * __ldcg(&part_o[(base + s) * D + dd]);
+      }
+      const float v = L > 0.f ? acc / L : 0.f;
+      const int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
+      if (out) out[oi] = v;
+      if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), lane);
+    }
+  }
+  if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
 }
 
 template <int D>
@@ -458,7 +495,8 @@ void set_pdl(cudaLaunchConfig_t& cfg) {
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
-                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo) {
+                      c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
+                      c10::optional<torch::Tensor> tickets) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
   TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
   TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(), "v_cache");
@@ -486,6 +524,12 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     pw = workspace->data_ptr<float>();
   }
   float2* pml = pw ? reinterpret_cast<float2*>(pw + (int64_t)B * H * n_split * D) : nullptr;
+  int* tk = nullptr;  // given: the last split CTA merges (no combine launch)
+  if (n_split > 1 && tickets.has_value()) {
+    TORCH_CHECK(tickets->scalar_type() == torch::kInt32 && tickets->numel() >= (int64_t)B * Hkv,
+                "decode_attention: tickets [B * Hkv] int32");
+    tk = tickets->data_ptr<int>();
+  }
   float scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
   auto stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchConfig_t cfg = {};
@@ -501,7 +545,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<128>, (const float*)q.data_ptr<float>(),
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo));
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk));
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -509,9 +553,9 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<64>, (const float*)q.data_ptr<float>(),
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo));
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk));
   }
-  if (n_split > 1) {
+  if (n_split > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
     c2.gridDim = dim3(B, H);
     c2.blockDim = dim3(D);
@@ -669,14 +713,14 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     e = cudaFuncSetAttribute(k_decode_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<128>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr);
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
     e = cudaFuncSetAttribute(k_decode_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<64>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr);
   }
   if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode attention launch: %s", cudaGetErrorString(e));
   if (n_split > 1) {

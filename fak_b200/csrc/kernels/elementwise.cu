@@ -81,7 +81,8 @@ __global__ void k_rope_kv(const float* __restrict__ qkv, int64_t ld, const int* 
   const int sl = slot[t];
   const int page = sl / PAGE, off = sl % PAGE;
   const float* row = qkv + (int64_t)t * ld;
-  for (int hh = warp; hh < H + 2 * Hkv; hh += nw) {
+  // grid.y spreads the heads of a token over several CTAs (decode has only a few tokens)
+  for (int hh = blockIdx.y * nw + warp; hh < H + 2 * Hkv; hh += nw * gridDim.y) {
     const bool is_q = hh < H, is_k = !is_q && hh < H + Hkv;
     const float* src = row + (int64_t)hh * D;
     float v[PER];
@@ -187,6 +188,51 @@ __global__ void k_argmax(const float* __restrict__ logits, int64_t ld, int V, in
   pdl_launch_dependents();
 }
 
+// Multi-CTA first-index argmax: grid (rows, chunks).  Each CTA folds its chunk into one packed
+// 64-bit key per row -- order-preserving float bits in the high word, the complemented index in
+// the low word, so atomicMax keeps the largest value and, among equal values, the lowest index --
+// and the last CTA of a row (ticket) writes the index and resets the key and ticket to zero.
+FAK_DEV unsigned long long argmax_key(float v, int i) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+}
+__global__ void k_argmax_chunks(const float* __restrict__ logits, int64_t ld, int V, int chunk,
+                                unsigned long long* __restrict__ keys, int* __restrict__ tickets, int* __restrict__ out) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const float* x = logits + (int64_t)r * ld;
+  const int i0 = blockIdx.y * chunk, i1 = min(V, i0 + chunk);
+  unsigned long long best = 0ull;
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const unsigned long long k = argmax_key(x[i], i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
+  }
+  __shared__ unsigned long long sk[32];
+  __shared__ int s_last;
+  if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = sk[w] > best ? sk[w] : best;
+    atomicMax(&keys[r], best);
+    __threadfence();
+    s_last = atomicAdd(&tickets[r], 1) == (int)gridDim.y - 1;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0 && s_last) {
+    __threadfence();
+    const unsigned long long k = atomicExch(&keys[r], 0ull);
+    out[r] = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+    tickets[r] = 0;
+  }
+}
+
 cudaLaunchAttribute g_attr[1];
 cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem = 0) {
   cudaLaunchConfig_t cfg = {};
@@ -237,7 +283,8 @@ void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Te
   const float* kn = k_norm.has_value() ? k_norm->data_ptr<float>() : nullptr;
   float* qf = q_f32.has_value() ? q_f32->data_ptr<float>() : nullptr;
   __nv_bfloat16* qb = q_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(q_bf16->data_ptr()) : nullptr;
-  auto cfg = make_cfg(dim3(T), dim3(256));
+  const int heads = (int)(H + 2 * Hkv);
+  auto cfg = make_cfg(dim3(T, T >= 64 ? 1 : (heads + 3) / 4), dim3(T >= 64 ? 256 : 128));
   int n_pages = (int)k_cache.size(0);
   auto launch = [&](auto kern) {
     FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const float*)qkv.data_ptr<float>(), (int64_t)qkv.stride(0),
@@ -262,11 +309,24 @@ void rmsnorm_bf16(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor y)
                                     (__nv_bfloat16*)y.data_ptr(), (int64_t)y.stride(0)));
 }
 
-void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out) {
+void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out, c10::optional<torch::Tensor> keys,
+                 c10::optional<torch::Tensor> tickets) {
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2 && logits.stride(1) == 1, "logits");
   TORCH_CHECK(out.scalar_type() == torch::kInt32, "out int32");
   int R = (int)logits.size(0);
   if (R == 0) return;
+  if (keys.has_value()) {
+    TORCH_CHECK(keys->scalar_type() == torch::kInt64 && keys->numel() >= R, "argmax: keys [R] int64");
+    TORCH_CHECK(tickets.has_value() && tickets->scalar_type() == torch::kInt32 && tickets->numel() >= R,
+                "argmax: tickets [R] int32");
+    const int chunk = 8192;
+    auto cfg = make_cfg(dim3(R, (unsigned)((V + chunk - 1) / chunk)), dim3(256));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_argmax_chunks, (const float*)logits.data_ptr<float>(),
+                                      (int64_t)logits.stride(0), (int)V, chunk,
+                                      reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>()),
+                                      tickets->data_ptr<int>(), out.data_ptr<int>()));
+    return;
+  }
   auto cfg = make_cfg(dim3(R), dim3(1024));
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_argmax, (const float*)logits.data_ptr<float>(), (int64_t)logits.stride(0),
                                     (int)V, out.data_ptr<int>()));

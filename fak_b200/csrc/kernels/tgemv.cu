@@ -5,11 +5,12 @@
 // split into planes so that every field a thread needs is an aligned, bank-conflict-free shared
 // load once the unit tile sits in shared memory:
 //   Q4_K  2304 B: hdr [16][16] (d, dmin, 12 scale bytes) | qs [16][128]
-//   Q6_K  3360 B: ql [16][128] | qh [16][64] | scales [16][16] | d [16][2]
+//   Q6_K  3360 B: ql [16][128] | qh [16][64] (tile-row order) | scales [16][16] | d [16][2]
 //   Q8_0  4352 B: qs [16][256] (8 blocks x 32) | d [16][8][2]
 // Plane row ("slot") s holds tile row (s >> 1) + 8 (s & 1), so the two rows an MMA thread owns
 // (g and g + 8) are adjacent slots; the 16-byte chunks of the quant planes are XOR-swizzled by slot
-// (Q4_K/Q8_0 qs: chunk ^ (s & 6); Q6_K ql: chunk ^ ((s >> 1) & 7), qh: chunk ^ ((s >> 1) & 3)).
+// (Q4_K/Q8_0 qs: chunk ^ (s & 6); Q6_K ql: chunk ^ ((s >> 1) & 7)).  The Q6_K qh plane keeps tile-row
+// order (row r at 64 r bytes, so rows g and g+1 sit in opposite halves of the banks) with chunk ^ ((r >> 1) & 3).
 // The block bytes themselves are unchanged; only their placement differs from the GGUF rows.
 //
 // Work decomposition.  A work item is one tile x one K slice and belongs to ONE warp: the warp
@@ -180,7 +181,7 @@ FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, 
     __syncwarp();
     const uint8_t* ql = wt;
     const uint8_t* qh = wt + 2048;
-    const int f8 = g, f4 = g & 3;  // swizzle keys of slots 2g and 2g+1
+    const int f8 = g, f4 = (g >> 1) & 3;  // swizzle keys of ql (slots 2g, 2g+1) and qh (rows g, g+8)
 #pragma unroll
     for (int n = 0; n < 2; n++) {
 #pragma unroll
@@ -190,8 +191,8 @@ FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, 
         const uint32_t la1 = *reinterpret_cast<const uint32_t*>(ql + 128 * sA + 16 * (c2 ^ f8) + 4 * t);
         const uint32_t lb0 = *reinterpret_cast<const uint32_t*>(ql + 128 * sB + 16 * (c1 ^ f8) + 4 * t);
         const uint32_t lb1 = *reinterpret_cast<const uint32_t*>(ql + 128 * sB + 16 * (c2 ^ f8) + 4 * t);
-        const uint32_t ha = *reinterpret_cast<const uint32_t*>(qh + 64 * sA + 16 * (ch ^ f4) + 4 * t);
-        const uint32_t hb = *reinterpret_cast<const uint32_t*>(qh + 64 * sB + 16 * (ch ^ f4) + 4 * t);
+        const uint32_t ha = *reinterpret_cast<const uint32_t*>(qh + 64 * g + 16 * (ch ^ f4) + 4 * t);
+        const uint32_t hb = *reinterpret_cast<const uint32_t*>(qh + 64 * (g + 8) + 16 * (ch ^ f4) + 4 * t);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
           const uint32_t la = (kk & 1) ? la1 : la0, lb = (kk & 1) ? lb1 : lb0;
@@ -280,6 +281,7 @@ FAK_DEV void epilogue(int tile, const float (&v)[4], int lane, int N, int B, flo
 template <int QT, int W, int R>
 __global__ void __launch_bounds__(W * 32, 1)
 k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
+        const float* __restrict__ xf, int64_t ldx, const float* __restrict__ gamma, float eps,
         int B, float* __restrict__ y, int64_t ldy, const float* __restrict__ bias, int epi,
         float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo) {
   constexpr int UT = Tile<QT>::UT;
@@ -312,59 +314,133 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
     tc::fence_mbar_init();
   }
   __syncthreads();
-  auto issue = [&](int q) {
-    if (q >= Q) return;
-    const int tile = wg + (q / nu) * wstride;
-    const int u = u0 + q % nu;
-    uint64_t* b = &bar[q % R];
-    tc::mbar_arrive_expect_tx(b, UT);
-    bulk_g2s(ring + (q % R) * UT, Wt + ((int64_t)tile * geo.U + u) * UT, UT, b);
+  // producer state (lane 0): unit tiles are issued in consumption order, R-1 ahead
+  int pq = 0, pslot = 0, pu = 0;
+  const uint8_t* psrc = Wt + ((int64_t)wg * geo.U + u0) * UT;
+  const int64_t next_tile = ((int64_t)wstride * geo.U - nu) * UT;
+  auto issue_next = [&]() {
+    if (pq >= Q) return;
+    tc::mbar_arrive_expect_tx(&bar[pslot], UT);
+    bulk_g2s(ring + pslot * UT, psrc, UT, &bar[pslot]);
+    pq++;
+    pslot = pslot + 1 == R ? 0 : pslot + 1;
+    psrc += UT;
+    if (++pu == nu) {
+      pu = 0;
+      psrc += next_tile;
+    }
   };
   // weights do not depend on the previous kernel: their first copies go out before the wait
   if (lane == 0)
-    for (int q = 0; q < R - 1; q++) issue(q);
+    for (int i = 0; i < R - 1; i++) issue_next();
   pdl_wait();
-  if (threadIdx.x == 0) {
-    const uint32_t dsb = (uint32_t)(kb / 4);  // (scale, sum) bytes of the slice per token
-    tc::mbar_arrive_expect_tx(act_bar, (uint32_t)B * ((uint32_t)kb + dsb));
-    for (int b = 0; b < B; b++) {
-      bulk_g2s(xs + b * geo.xstride, qx + (int64_t)b * K + k0, (uint32_t)kb, act_bar);
-      bulk_g2s(dsr + b * geo.dstride, ds + (int64_t)b * (K / 32) + k0 / 32, dsb, act_bar);
+  if (xf != nullptr) {
+    // fp32 activations: optional RMSNorm (statistics over the whole row), then int8 per 32-block
+    // with (scale, exact sum) -- the activation quantizer, done while the weight copies fly
+    __shared__ float s_inv[MAXB];
+    if (gamma != nullptr) {
+      for (int b = warp; b < B; b += W) {
+        const float* xr = xf + (int64_t)b * ldx;
+        float ss = 0.f;
+        for (int i = lane * 4; i < K; i += 128) {
+          const float4 v = *reinterpret_cast<const float4*>(xr + i);
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s_inv[b] = rsqrtf(ss / (float)K + eps);
+      }
+      __syncthreads();
+    }
+    const int nblk = nu * 8;
+    for (int i = threadIdx.x; i < MAXB * nblk; i += W * 32) {
+      const int b = i / nblk, blk = i - b * nblk;
+      const int kk = blk * 32;
+      uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      float2 dsv = make_float2(0.f, 0.f);
+      if (b < B && kk < kb) {
+        const float* src = xf + (int64_t)b * ldx + k0 + kk;
+        const float inv = gamma != nullptr ? s_inv[b] : 1.f;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float4 f = *reinterpret_cast<const float4*>(src + 4 * j);
+          float4 gm = make_float4(1.f, 1.f, 1.f, 1.f);
+          if (gamma != nullptr) gm = *reinterpret_cast<const float4*>(gamma + k0 + kk + 4 * j);
+          v[4 * j] = f.x * inv * gm.x;
+          v[4 * j + 1] = f.y * inv * gm.y;
+          v[4 * j + 2] = f.z * inv * gm.z;
+          v[4 * j + 3] = f.w * inv * gm.w;
+        }
+        float amax = 0.f, sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          amax = fmaxf(amax, fabsf(v[j]));
+          sum += v[j];
+        }
+        const float d = amax / 127.f;
+        const float id = d > 0.f ? 1.f / d : 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const uint32_t c = (uint32_t)(int)rintf(v[j] * id) & 0xffu;
+          w[j >> 2] |= c << (8 * (j & 3));
+        }
+        dsv = make_float2(d, sum);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(xs + b * geo.xstride + kk);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      dsT[blk * MAXB + b] = dsv;
+    }
+  } else {
+    if (threadIdx.x == 0) {
+      const uint32_t dsb = (uint32_t)(kb / 4);  // (scale, sum) bytes of the slice per token
+      tc::mbar_arrive_expect_tx(act_bar, (uint32_t)B * ((uint32_t)kb + dsb));
+      for (int b = 0; b < B; b++) {
+        bulk_g2s(xs + b * geo.xstride, qx + (int64_t)b * K + k0, (uint32_t)kb, act_bar);
+        bulk_g2s(dsr + b * geo.dstride, ds + (int64_t)b * (K / 32) + k0 / 32, dsb, act_bar);
+      }
+    }
+    // zero the activation columns no copy writes (missing tokens, padding past K)
+    for (int i = threadIdx.x; i < MAXB * (nu * 256 / 16); i += W * 32) {
+      const int b = i / (nu * 16), c = (i % (nu * 16)) * 16;
+      if (b >= B || c >= kb) *reinterpret_cast<uint4*>(xs + b * geo.xstride + c) = make_uint4(0, 0, 0, 0);
+    }
+    tc::mbar_wait(act_bar, 0, err);
+    for (int i = threadIdx.x; i < nu * 8 * MAXB; i += W * 32) {
+      const int blk = i / MAXB, b = i % MAXB;
+      dsT[i] = (b < B && blk * 32 < kb) ? dsr[b * geo.dstride + blk] : make_float2(0.f, 0.f);
     }
   }
-  // zero the activation columns no copy writes (missing tokens, padding past K)
-  for (int i = threadIdx.x; i < MAXB * (nu * 256 / 16); i += W * 32) {
-    const int b = i / (nu * 16), c = (i % (nu * 16)) * 16;
-    if (b >= B || c >= kb) *reinterpret_cast<uint4*>(xs + b * geo.xstride + c) = make_uint4(0, 0, 0, 0);
-  }
-  tc::mbar_wait(act_bar, 0, err);
-  for (int i = threadIdx.x; i < nu * 8 * MAXB; i += W * 32) {
-    const int blk = i / MAXB, b = i % MAXB;
-    dsT[i] = (b < B && blk * 32 < kb) ? dsr[b * geo.dstride + blk] : make_float2(0.f, 0.f);
-  }
   if constexpr (QT == QT_Q6_K) {
+    __syncthreads();
     for (int i = threadIdx.x; i < nu * 16 * MAXB; i += W * 32) {
       const int k16 = i / MAXB, b = i % MAXB;
       const int4 v = *reinterpret_cast<const int4*>(xs + b * geo.xstride + 16 * k16);
-      int s = __dp4a(v.x, 0x01010101, 0);
-      s = __dp4a(v.y, 0x01010101, s);
-      s = __dp4a(v.z, 0x01010101, s);
-      s = __dp4a(v.w, 0x01010101, s);
-      czT[i] = MAGIC_I - 32 * s;
+      int sm4 = __dp4a(v.x, 0x01010101, 0);
+      sm4 = __dp4a(v.y, 0x01010101, sm4);
+      sm4 = __dp4a(v.z, 0x01010101, sm4);
+      sm4 = __dp4a(v.w, 0x01010101, sm4);
+      czT[i] = MAGIC_I - 32 * sm4;
     }
   }
   __syncthreads();
 
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   const int g = lane >> 2;
+  const int8_t* xg = xs + g * geo.xstride;
+  int cslot = 0, ul = 0, tile = wg;
+  uint32_t phase = 0;
   for (int q = 0; q < Q; q++) {
-    if (lane == 0) issue(q + R - 1);  // into the slot released at the end of iteration q-1
-    tc::mbar_wait(&bar[q % R], (uint32_t)((q / R) & 1), err);
-    const int ul = q % nu;
-    unit_tile<QT>(ring + (q % R) * UT, tab, xs + g * geo.xstride + ul * 256, dsT + ul * 8 * MAXB,
+    if (lane == 0) issue_next();  // into the slot released at the end of the previous iteration
+    tc::mbar_wait(&bar[cslot], phase, err);
+    unit_tile<QT>(ring + cslot * UT, tab, xg + ul * 256, dsT + ul * 8 * MAXB,
                   QT == QT_Q6_K ? czT + ul * 16 * MAXB : nullptr, lane, acc);
-    if (ul != nu - 1) continue;
-    const int tile = wg + (q / nu) * wstride;
+    if (++cslot == R) {
+      cslot = 0;
+      phase ^= 1u;
+    }
+    if (++ul < nu) continue;
+    ul = 0;
     if (geo.S == 1) {
       epilogue(tile, acc, lane, N, B, y, ldy, bias, epi);
     } else {
@@ -387,6 +463,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       }
     }
     acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    tile += wstride;
   }
   pdl_launch_dependents();
 }
@@ -399,29 +476,43 @@ struct Plan {
 
 int tile_bytes(int qt) { return qt == QT_Q4_K ? 2304 : (qt == QT_Q6_K ? 3360 : 4352); }
 
-// Choose (warps per CTA, ring depth) and the K split.  Depends only on the matrix shape and the
-// GPU, never on the batch size, so batched and serial decoding reduce in the same order.
+// Choose (warps per CTA, ring depth) and the K split.  The split minimises the unit tiles on
+// the busiest warp (rounds of tiles x units per slice, plus the split-K reduction), among splits
+// whose activation staging fits in shared memory.  Depends only on the matrix shape and the GPU,
+// never on the batch size, so batched and serial decoding reduce in the same order.
 Plan make_plan(int qt, int64_t N, int64_t K, int n_sm, int max_smem, int force_w, int force_r, int force_s) {
   const int T = (int)((N + 15) / 16);
   const int U = (int)((K + 255) / 256);
+  // activation rows 32 mod 128 bytes apart (8-byte loads, Q4_K/Q8_0) or 16 mod 128 (4-byte, Q6_K)
+  const int xpad = qt == QT_Q6_K ? 16 : 32;
   static const int cand[][2] = {{16, 3}, {16, 2}, {8, 4}, {8, 3}, {8, 2}};
   for (auto& c : cand) {
     const int W = force_w ? force_w : c[0], R = force_r ? force_r : c[1];
-    // enough (tile, slice) items to give every warp of the GPU work
-    int S = force_s ? force_s : (int)std::min<int64_t>(U, std::max<int64_t>(1, ((int64_t)n_sm * W + T - 1) / T));
-    S = std::min(S, n_sm);
-    int Us = (U + S - 1) / S;
-    S = (U + Us - 1) / Us;
-    TGeo g;
-    g.T = T;
-    g.U = U;
-    g.S = S;
-    g.Us = Us;
-    g.P = std::max(1, n_sm / S);
-    g.xstride = ((Us * 256 + 127) / 128) * 128 + 32;
-    g.dstride = Us * 8;
-    const TSmem L = tsmem(qt, W, R, g);
-    if (L.total <= max_smem) return Plan{W, R, g, L.total};
+    Plan best{};
+    double best_cost = 1e30;
+    for (int s0 = force_s ? force_s : 1; s0 <= (force_s ? force_s : std::min(U, n_sm)); s0++) {
+      const int Us = (U + s0 - 1) / s0;
+      const int S = (U + Us - 1) / Us;
+      if (S != s0 && !force_s) continue;  // same split as a smaller s0
+      TGeo g;
+      g.T = T;
+      g.U = U;
+      g.S = S;
+      g.Us = Us;
+      g.P = std::max(1, n_sm / S);
+      g.xstride = ((Us * 256 + 127) / 128) * 128 + xpad;
+      g.dstride = Us * 8;
+      const TSmem L = tsmem(qt, W, R, g);
+      if (L.total > max_smem) continue;
+      const int64_t warps = (int64_t)W * g.P;
+      const int64_t rounds = (T + warps - 1) / warps;
+      const double cost = (double)rounds * (Us + (S > 1 ? 1.0 : 0.3));
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = Plan{W, R, g, L.total};
+      }
+    }
+    if (best_cost < 1e30) return best;
     if (force_w && force_r) break;
   }
   TORCH_CHECK(false, "tgemv: no launch configuration fits in shared memory for K=", K);
@@ -442,22 +533,45 @@ std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_
           p.R, p.smem};
 }
 
-// w: tile-packed weights (uint8, ceil(N/16) * ceil(K/256) unit tiles); qx [B, K] int8; ds [B, K/32, 2];
+// w: tile-packed weights (uint8, ceil(N/16) * ceil(K/256) unit tiles); activations either quantized
+// (qx [B, K] int8, ds [B, K/32, 2]) or fp32 x [B, K] (optionally RMSNorm'd with gamma, eps);
 // y [B, *] f32 (row stride y.stride(0)); part/cnt: split-K scratch (cnt zero-initialised; every
 // launch leaves it zero again).  flags: bits 0-4 warps, 5-8 ring depth, 9-16 K slices (overrides).
-void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, torch::Tensor qx, torch::Tensor ds, int64_t B,
-           torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part, torch::Tensor cnt,
-           c10::optional<torch::Tensor> err, int64_t flags) {
+void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<torch::Tensor> qx,
+           c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
+           double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
+           torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "tgemv: w cuda uint8");
   TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "tgemv: qtype");
   TORCH_CHECK(K % 64 == 0 && (qtype == QT_Q8_0 || K % 256 == 0), "tgemv: K must be a multiple of 256 (64 for Q8_0)");
   const int64_t T = (N + 15) / 16, U = (K + 255) / 256;
   TORCH_CHECK(w.numel() >= T * U * tile_bytes((int)qtype), "tgemv: weight buffer smaller than the tile-packed size");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "tgemv: weight alignment");
-  TORCH_CHECK(qx.scalar_type() == torch::kInt8 && qx.is_contiguous() && qx.numel() >= B * K, "tgemv: qx");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(qx.data_ptr()) % 16 == 0, "tgemv: qx alignment");
-  TORCH_CHECK(ds.scalar_type() == torch::kFloat32 && ds.is_contiguous() && ds.numel() >= B * K / 16, "tgemv: ds");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(ds.data_ptr()) % 16 == 0, "tgemv: ds alignment");
+  const int8_t* qp = nullptr;
+  const float2* dp = nullptr;
+  const float* xp = nullptr;
+  const float* gp = nullptr;
+  int64_t ldx = 0;
+  if (x.has_value()) {  // fp32 activations, normalised (gamma) and quantized inside the kernel
+    TORCH_CHECK(x->scalar_type() == torch::kFloat32 && x->dim() == 2 && x->stride(1) == 1 && x->size(0) >= B &&
+                    x->size(1) >= K && x->stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(x->data_ptr()) % 16 == 0,
+                "tgemv: x [B, >=K] f32, 16-byte aligned rows");
+    xp = x->data_ptr<float>();
+    ldx = x->stride(0);
+    if (gamma.has_value()) {
+      TORCH_CHECK(gamma->scalar_type() == torch::kFloat32 && gamma->numel() >= K &&
+                      reinterpret_cast<uintptr_t>(gamma->data_ptr()) % 16 == 0, "tgemv: gamma");
+      gp = gamma->data_ptr<float>();
+    }
+  } else {
+    TORCH_CHECK(qx.has_value() && ds.has_value(), "tgemv: give x or (qx, ds)");
+    TORCH_CHECK(qx->scalar_type() == torch::kInt8 && qx->is_contiguous() && qx->numel() >= B * K, "tgemv: qx");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(qx->data_ptr()) % 16 == 0, "tgemv: qx alignment");
+    TORCH_CHECK(ds->scalar_type() == torch::kFloat32 && ds->is_contiguous() && ds->numel() >= B * K / 16, "tgemv: ds");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(ds->data_ptr()) % 16 == 0, "tgemv: ds alignment");
+    qp = qx->data_ptr<int8_t>();
+    dp = reinterpret_cast<const float2*>(ds->data_ptr<float>());
+  }
   TORCH_CHECK(y.scalar_type() == torch::kFloat32 && y.dim() == 2 && y.stride(1) == 1, "tgemv: y [B, *] f32");
   TORCH_CHECK(B >= 1 && B <= MAXB, "tgemv: 1 <= B <= 8");
   if (epi == EPI_SWIGLU) TORCH_CHECK(N % 16 == 0, "tgemv: SwiGLU needs 8-row interleaved gate/up blocks");
@@ -492,9 +606,8 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, torch::Tensor q
   int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
   auto go = [&](auto kern) {
     FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem));
-    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.data_ptr<uint8_t>(), (int)N, (int)K,
-                                      (const int8_t*)qx.data_ptr<int8_t>(),
-                                      reinterpret_cast<const float2*>(ds.data_ptr<float>()), (int)B,
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.data_ptr<uint8_t>(), (int)N, (int)K, qp, dp,
+                                      xp, ldx, gp, (float)eps, (int)B,
                                       y.data_ptr<float>(), (int64_t)y.stride(0), bp, (int)epi,
                                       p.geo.S > 1 ? part.data_ptr<float>() : nullptr,
                                       p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo));

@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import dataclasses
 import math
+import os
 
 import torch
 
@@ -110,11 +111,24 @@ class ModelRunner:
         self.act_d = K.ActQ(B, d, dev)
         self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
+        # decode GEMV inputs: activations quantized by a separate kernel (default), or fp32 sources
+        # the GEMV normalises and quantizes itself (FAK_FUSED_ACT=1: fewer launches, but every CTA
+        # repeats the row's quantization; measured 0.14 ms/step slower on Qwen2.5-7B B=5).
+        # FAK_ATTN_MERGE=1 merges the attention splits in the last split's CTA instead of a combine
+        # kernel (one CTA then reads all 32 partials of its heads: a long tail, 0.7 ms/step slower).
+        self.fused_act = os.environ.get("FAK_FUSED_ACT", "0") == "1"
+        self.attn_merge = os.environ.get("FAK_ATTN_MERGE", "0") == "1"
+        self.ffn_in = K.FAct(self.h) if self.fused_act else self.act_ffn   # SwiGLU output -> down projection
+        self.lm_in = K.FAct(self.x) if self.fused_act else self.act_d      # final norm -> LM head
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
         self.next_ids = torch.zeros(B, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.max_split = 64
         self.attn_ws = torch.zeros(B * self.Hq * self.max_split * (self.D + 2), dtype=torch.float32, device=dev)
+        self.attn_tickets = torch.zeros(B * self.Hkv, dtype=torch.int32, device=dev)  # split-merge tickets
+        # per-device kernel scratch, allocated here so no graph capture allocates it
+        K.tgemv_workspace(dev)
+        K.argmax_workspace(dev, B)
         self._graphs: dict[int, tuple[torch.cuda.CUDAGraph, dict]] = {}
         self._graph_kernels: dict[int, int] = {}
 
@@ -129,27 +143,35 @@ class ModelRunner:
     def _layer_decode(self, i: int, B: int, pos, slot, bt, ctx, n_split: int) -> None:
         cfg, L, kv = self.cfg, self.w.layers[i], self.kv
         x = self.x[:B]
-        K.quant_act(x, self.act_d, L.attn_norm, cfg.rms_eps)
+        if self.fused_act:
+            xin = K.FAct(x, L.attn_norm, cfg.rms_eps)  # RMSNorm + quantization inside the GEMV
+        else:
+            K.quant_act(x, self.act_d, L.attn_norm, cfg.rms_eps)
+            xin = self.act_d
         for seg, off in L.qkv:
             bias = L.qkv_bias[off:off + seg.rows] if L.qkv_bias is not None else None
-            K.gemv(seg, self.act_d, B, self.qkv[:B, off:off + seg.rows], bias, K.EPI_STORE)
+            K.gemv(seg, xin, B, self.qkv[:B, off:off + seg.rows], bias, K.EPI_STORE)
         K.rope_kv(self.qkv[:B], pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
                   self.q[:B], None, kv.k[i], kv.v[i])
         if self.coll is None:
             K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_attn,
-                               workspace=self.attn_ws)
+                               workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None)
             K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD)
         else:
             self.coll.decode_attn_o(self, i, B, bt, ctx, n_split)
-        K.quant_act(x, self.act_d, L.ffn_norm, cfg.rms_eps)
         if cfg.is_moe:
+            K.quant_act(x, self.act_d, L.ffn_norm, cfg.rms_eps)
             from .moe import moe_decode
             moe_decode(self, i, B)
             return
-        K.gemv(L.gate_up, self.act_d, B, self.h[:B], None, K.EPI_SWIGLU)
-        K.quant_act(self.h[:B, :self.ffn_local], self.act_ffn)
+        if self.fused_act:
+            K.gemv(L.gate_up, K.FAct(x, L.ffn_norm, cfg.rms_eps), B, self.h[:B], None, K.EPI_SWIGLU)
+        else:
+            K.quant_act(x, self.act_d, L.ffn_norm, cfg.rms_eps)
+            K.gemv(L.gate_up, self.act_d, B, self.h[:B], None, K.EPI_SWIGLU)
+            K.quant_act(self.h[:B, :self.ffn_local], self.act_ffn)
         if self.coll is None:
-            K.gemv(L.down, self.act_ffn, B, x, None, K.EPI_ADD)
+            K.gemv(L.down, self.ffn_in, B, x, None, K.EPI_ADD)
         else:
             self.coll.decode_down(self, i, B)
 
@@ -163,7 +185,11 @@ class ModelRunner:
         K.embed(self.w.embed, ids, self.x[:B], None, self.err)
         for i in range(cfg.n_layers if n_layers is None else n_layers):
             self._layer_decode(i, B, pos, slot, bt, ctx, n_split)
-        K.quant_act(self.x[:B], self.act_d, self.w.final_norm, cfg.rms_eps)
+        if self.fused_act:
+            self.lm_in = K.FAct(self.x, self.w.final_norm, cfg.rms_eps)
+        else:
+            K.quant_act(self.x[:B], self.act_d, self.w.final_norm, cfg.rms_eps)
+            self.lm_in = self.act_d
         if greedy and self.coll is not None and hasattr(self.coll, "lm_head_greedy"):
             self.coll.lm_head_greedy(self, B)  # sharded logits -> distributed argmax, no logits gather
             return
@@ -173,7 +199,7 @@ class ModelRunner:
 
     def _lm_head(self, B: int) -> None:
         if self.coll is None:
-            K.gemv(self.w.lm_head, self.act_d, B, self.logits[:B], None, K.EPI_STORE)
+            K.gemv(self.w.lm_head, self.lm_in, B, self.logits[:B], None, K.EPI_STORE)
         else:
             self.coll.lm_head(self, B)
 
@@ -278,9 +304,9 @@ class ModelRunner:
         for s0 in range(0, S, self.max_batch):
             s1 = min(S, s0 + self.max_batch)
             n = s1 - s0
-            K.quant_act(xl[s0:s1], self.act_d, self.w.final_norm, cfg.rms_eps)
+            self.lm_in = K.FAct(xl[s0:s1], self.w.final_norm, cfg.rms_eps)
             if self.coll is None:
-                K.gemv(self.w.lm_head, self.act_d, n, logits[s0:s1], None, K.EPI_STORE)
+                K.gemv(self.w.lm_head, self.lm_in, n, logits[s0:s1], None, K.EPI_STORE)
             else:
                 self.coll.lm_head_to(self, n, logits[s0:s1])
         return logits

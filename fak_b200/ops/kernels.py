@@ -33,6 +33,15 @@ class ActQ:
         self.ds = torch.zeros(B, K // 32, 2, dtype=torch.float32, device=device)
 
 
+class FAct:
+    """fp32 activations [B, >=K] that the tile-packed GEMV normalises (RMSNorm with ``gamma``, when
+    given) and quantizes itself while its weight copies are in flight -- no separate quantizer
+    launch.  The matrix's column count is K."""
+
+    def __init__(self, x: torch.Tensor, gamma: torch.Tensor | None = None, eps: float = 1e-6):
+        self.x, self.gamma, self.eps = x, gamma, float(eps)
+
+
 def quant_act(x: torch.Tensor, act: ActQ, gamma: torch.Tensor | None = None, eps: float = 1e-6) -> None:
     ext().quant_act_wide(x, gamma, eps, act.q, act.ds)
     count()
@@ -50,6 +59,7 @@ _tg_ws: dict = {}
 
 
 def tgemv_workspace(device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Allocate before any CUDA-graph capture: its addresses are baked into graphs."""
     key = torch.device(device)
     ws = _tg_ws.get(key)
     if ws is None:
@@ -70,10 +80,16 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
         part, cnt = tgemv_workspace(w.tp.device)
         for b0 in range(0, B, GEMV_MAX_B):
             nb = min(GEMV_MAX_B, B - b0)
-            C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q[b0:b0 + nb], act.ds[b0:b0 + nb], nb, y[b0:b0 + nb], bias,
-                    epi, part, cnt, None, flags)
+            if isinstance(act, FAct):
+                C.tgemv(w.tp, w.qtype, w.rows, w.cols, None, None, act.x[b0:b0 + nb], act.gamma, act.eps, nb,
+                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags)
+            else:
+                C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q[b0:b0 + nb], act.ds[b0:b0 + nb], None, None, 0.0, nb,
+                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags)
             count()
         return
+    if isinstance(act, FAct):
+        raise RuntimeError("fp32 activations need the tile-packed weights (QuantWeight.pack)")
     for b0 in range(0, B, GEMV_MAX_B):
         nb = min(GEMV_MAX_B, B - b0)
         q = act.q[b0:b0 + nb]
@@ -86,11 +102,14 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 
 
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
-                     workspace=None, ldo: int = 0) -> None:
-    """ldo: elements per token row of the output (default: heads x head_dim)."""
+                     workspace=None, ldo: int = 0, tickets=None) -> None:
+    """ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
+    [B * kv heads]; when given, the last split of each (sequence, KV group) merges the splits in the
+    same kernel instead of a separate combine launch (the kernel leaves the tickets at zero)."""
     ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
-                           act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo)
-    count(2 if n_split > 1 else 1)
+                           act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo,
+                           tickets)
+    count(2 if n_split > 1 and tickets is None else 1)
 
 
 def prefill_attention(q, k_cache, v_cache, block_table, meta, out) -> None:
@@ -114,8 +133,25 @@ def rmsnorm_bf16(x, w, eps, y) -> None:
     count()
 
 
+_argmax_ws: dict = {}
+
+
+def argmax_workspace(device, rows: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-device scratch of the multi-CTA argmax (packed keys, tickets; left at zero by every
+    launch).  Allocate it before any CUDA-graph capture: its addresses are baked into graphs."""
+    key = torch.device(device)
+    ws = _argmax_ws.get(key)
+    if ws is None or ws[0].numel() < rows:
+        n = max(rows, 256)
+        ws = (torch.zeros(n, dtype=torch.int64, device=key), torch.zeros(n, dtype=torch.int32, device=key))
+        _argmax_ws[key] = ws
+    return ws
+
+
 def argmax(logits: torch.Tensor, V: int, out: torch.Tensor) -> None:
-    ext().argmax_rows(logits, V, out)
+    """First-index argmax of each row over the first V columns."""
+    keys, tickets = argmax_workspace(logits.device, logits.shape[0])
+    ext().argmax_rows(logits, V, out, keys, tickets)
     count()
 
 

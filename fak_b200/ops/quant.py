@@ -62,8 +62,8 @@ def synth_quantized(shape: tuple[int, ...], ggml_type: int, seed: int, std: floa
 # ---- tile-packed layout of the decode GEMV ----------------------------------------------------
 # Rows in tiles of 16, each row's blocks in 256-weight units; one (tile, unit) is a contiguous
 # "unit tile" whose fields are split into planes.  Plane row ("slot") s holds tile row
-# (s >> 1) + 8 (s & 1); 16-byte chunks of the quant planes are XOR-swizzled by slot.  The block
-# bytes are unchanged, only placed differently.
+# (s >> 1) + 8 (s & 1) (except the Q6_K qh plane, kept in tile-row order); 16-byte chunks of the
+# quant planes are XOR-swizzled.  The block bytes are unchanged, only placed differently.
 TILE_UNIT_BYTES = {QT_Q4_K: 2304, QT_Q6_K: 3360, QT_Q8_0: 4352}
 SLOT_ROWS = [(s >> 1) + 8 * (s & 1) for s in range(16)]
 
@@ -102,7 +102,9 @@ def tile_pack(buf: torch.Tensor, qtype: int, rows: int, cols: int, pitch: int) -
             planes = [hdr, qs]
         else:
             ql = _swizzle(x[..., :128].reshape(T, U, 16, 8, 16), lambda s: (s >> 1) & 7).reshape(T, U, 2048)
-            qh = _swizzle(x[..., 128:192].reshape(T, U, 16, 4, 16), lambda s: (s >> 1) & 3).reshape(T, U, 1024)
+            # qh rows in tile-row order (plane row r = tile row r), chunks swizzled by (r >> 1) & 3
+            qh_rows = x[..., 128:192][:, :, [SLOT_ROWS.index(r) for r in range(16)]]
+            qh = _swizzle(qh_rows.reshape(T, U, 16, 4, 16), lambda r: (r >> 1) & 3).reshape(T, U, 1024)
             sc = x[..., 192:208].reshape(T, U, 256)
             d = x[..., 208:210].reshape(T, U, 32)
             planes = [ql, qh, sc, d]

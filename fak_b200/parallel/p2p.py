@@ -95,7 +95,7 @@ class P2PTP(NcclTP):
     def decode_attn_o(self, rn, i: int, B: int, bt, ctx, n_split: int) -> None:
         C, kv, D, H = ext(), rn.kv, self.D, self.cfg.n_heads
         K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_mine, workspace=rn.attn_ws,
-                           ldo=H * D)
+                           tickets=rn.attn_tickets, ldo=H * D)
         C.p2p_allgather_cols(self.peers, self.buf[self.q_off:], H * D, self.q_off, H * D, self.h0 * D, self.nh * D,
                              B, self.flags_off, 3 * i, self.me, self.counters, self.err, AG_CTAS)
         C.p2p_allgather_cols(self.peers, self.buf[self.ds_off:], H * D // 4, self.ds_off, H * D // 4,
@@ -108,14 +108,14 @@ class P2PTP(NcclTP):
         d = self.cfg.d_model
         part_off = self.parts_off + i * self.B * d * 4
         part = self.buf[part_off:part_off + B * d * 4].view(torch.float32).view(B, d)
-        K.gemv(rn.w.layers[i].down, rn.act_ffn, B, part, None, K.EPI_STORE)
+        K.gemv(rn.w.layers[i].down, rn.ffn_in, B, part, None, K.EPI_STORE)
         ext().p2p_allreduce_add(self.peers, part_off, rn.x[:B], B * d, self.flags_off, 3 * i + 2, self.me,
                                 self.counters, self.err, AR_CTAS)
         K.count()
 
     def lm_head_greedy(self, rn, B: int) -> None:
         """Local vocab-shard logits, then the distributed first-index argmax into rn.next_ids."""
-        K.gemv(rn.w.lm_head, rn.act_d, B, self.logits_local[:B, :self.Vl_real], None, K.EPI_STORE)
+        K.gemv(rn.w.lm_head, rn.lm_in, B, self.logits_local[:B, :self.Vl_real], None, K.EPI_STORE)
         ext().p2p_argmax(self.peers, self.logits_local[:B], self.Vl_real, self.v_off, self.cand_off,
                          rn.next_ids[:B], B, self.flags_off, 3 * self.cfg.n_layers, self.me, self.counters, self.err)
         K.count()

@@ -76,13 +76,13 @@ class NcclTP:
             self.act_local.q[:B].zero_()
             self.act_local.ds[:B].zero_()
         K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_local, workspace=rn.attn_ws,
-                           ldo=self.maxHq * self.D)
+                           tickets=rn.attn_tickets, ldo=self.maxHq * self.D)
         self._gather_heads_q(B, rn.act_attn)
         K.gemv(rn.w.layers[i].o, rn.act_attn, B, rn.x[:B], None, K.EPI_ADD)
 
     def decode_down(self, rn, i: int, B: int) -> None:
         t = self.tmp[:B]
-        K.gemv(rn.w.layers[i].down, rn.act_ffn, B, t, None, K.EPI_STORE)
+        K.gemv(rn.w.layers[i].down, rn.ffn_in, B, t, None, K.EPI_STORE)
         dist.all_reduce(t, group=self.group)
         rn.x[:B].add_(t)
 
@@ -94,11 +94,11 @@ class NcclTP:
         out[:B].copy_(full[:, :V])
 
     def lm_head(self, rn, B: int) -> None:
-        K.gemv(rn.w.lm_head, rn.act_d, B, self.logits_local[:B, :self.Vl_real], None, K.EPI_STORE)
+        K.gemv(rn.w.lm_head, rn.lm_in, B, self.logits_local[:B, :self.Vl_real], None, K.EPI_STORE)
         self._gather_logits(B, rn.logits)
 
     def lm_head_to(self, rn, n: int, out: torch.Tensor) -> None:
-        K.gemv(rn.w.lm_head, rn.act_d, n, self.logits_local[:n, :self.Vl_real], None, K.EPI_STORE)
+        K.gemv(rn.w.lm_head, rn.lm_in, n, self.logits_local[:n, :self.Vl_real], None, K.EPI_STORE)
         self._gather_logits(n, out)
 
     # ---------------------------------------------------------------------------------

@@ -305,3 +305,54 @@ def test_tgemv_batch_invariant_and_repeatable(qt, blk):
         K.gemv(w, solo, 1, y1)
         assert torch.equal(y1[0], y8[b]), b
     assert not K.tgemv_workspace("cuda")[1].any()
+
+
+@pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3)])
+def test_decode_attention_fused_merge_bitexact(D, H, Hkv):
+    """The in-kernel split merge (tickets) gives the same bits as the separate combine kernel and
+    leaves the tickets at zero."""
+    from fak_b200.ops import kernels as K
+    ctx = [1, 17, 100, 333, 1000, 4100]
+    B = len(ctx)
+    kc, vc, bt = _paged_cache(ctx, Hkv, D, n_pages=512)
+    q = torch.randn(B, H, D, device="cuda")
+    cl = torch.tensor(ctx, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(B * H * 32 * (D + 2), device="cuda")
+    outs = []
+    for tickets in (None, torch.zeros(B * Hkv, dtype=torch.int32, device="cuda")):
+        for _ in range(2):
+            out = torch.zeros(B, H * D, device="cuda")
+            act = K.ActQ(B, H * D, "cuda")
+            K.decode_attention(q, kc, vc, bt, cl, 32, out=out, act=act, workspace=ws, tickets=tickets)
+            torch.cuda.synchronize()
+            outs.append((out, act.q.clone(), act.ds.clone()))
+        if tickets is not None:
+            assert not tickets.any()
+    for o in outs[1:]:
+        assert torch.equal(o[0], outs[0][0]) and torch.equal(o[1], outs[0][1]) and torch.equal(o[2], outs[0][2])
+
+
+@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("norm", [False, True])
+@pytest.mark.parametrize("N", [576, 16 * 2400])
+def test_tgemv_fp32_input_fused_norm(qt, blk, norm, N):
+    """fp32 activations normalised and quantized inside the GEMV match the fp32 reference and the
+    separately quantized path; a token's result does not depend on the batch."""
+    from fak_b200.ops import kernels as K
+    Kd = 1024 if qt != GGMLType.Q8_0 else 576
+    B = 5
+    w, Wd, x, act = _tg_case(qt, N, Kd, B, seed=11)
+    x = x * 3
+    gamma = (torch.rand(Kd, device="cuda") + 0.5) if norm else None
+    xn = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * gamma if norm else x
+    ref = xn @ Wd.T
+    y = torch.zeros(B, N, device="cuda")
+    K.gemv(w, K.FAct(x, gamma, 1e-6), B, y)
+    torch.cuda.synchronize()
+    err = (y - ref).abs().max().item() / ref.abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
+    assert cos > 0.9995 and err < 0.03, (cos, err)
+    for b in (0, 3):
+        y1 = torch.zeros(1, N, device="cuda")
+        K.gemv(w, K.FAct(x[b:b + 1], gamma, 1e-6), 1, y1)
+        assert torch.equal(y1[0], y[b]), b

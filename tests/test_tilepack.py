@@ -67,7 +67,8 @@ def kernel_view(tp: np.ndarray, qtype: int) -> np.ndarray:
                                     c1, c2, ch = 4 * n + h, 4 * n + 2 + h, 2 * n + h
                                     la0 = wt[128 * s + 16 * (c1 ^ f8) + 4 * t:][:4]
                                     la1 = wt[128 * s + 16 * (c2 ^ f8) + 4 * t:][:4]
-                                    ha = wt[2048 + 64 * s + 16 * (ch ^ f4) + 4 * t:][:4]
+                                    r = g + 8 * row_half  # qh plane: tile-row order
+                                    ha = wt[2048 + 64 * r + 16 * (ch ^ ((r >> 1) & 3)) + 4 * t:][:4]
                                     for kk in range(4):
                                         la = la1 if kk & 1 else la0
                                         q = ((la >> (4 * (kk >> 1))) & 0xF) | (((ha >> (2 * kk)) & 3) << 4)
