@@ -128,9 +128,16 @@ class Engine:
         torch.cuda.synchronize(self.device)
 
     def _pages_from_memory(self) -> int:
+        """KV pages from the free device memory after the weights; fails closed (FitError) when not
+        even one sequence of max_context tokens would fit."""
+        from ..capacity import FitError, MemoryPlan
         free, _ = torch.cuda.mem_get_info(self.device)
         per = KVCache.bytes_per_page(self.cfg.n_layers, self.weights.n_kv_local, self.cfg.head_dim)
-        return max(64, int(free * self.ecfg.kv_mem_fraction) // per)
+        pages = int(free * self.ecfg.kv_mem_fraction) // per
+        need = -(-self.max_context // self.ecfg.page_size) + 1
+        if pages < need:
+            raise FitError(MemoryPlan(kv=need * per, kv_pages=need), int(free * self.ecfg.kv_mem_fraction))
+        return pages
 
     def warmup_graphs(self, buckets: tuple[int, ...] | None = None) -> None:
         if not self.ecfg.cuda_graph:
@@ -369,6 +376,7 @@ class Engine:
         vbt = btd.repeat_interleave(k + 1, dim=0)
         tgt = self.runner.decode(toks, d[0:V], d[V:2 * V], vbt, d[2 * V:3 * V], V, use_graph=self._graphs_ready)
         t_host = tgt.view(B, k + 1).cpu().numpy()
+        self.stats["spec_steps"] = self.stats.get("spec_steps", 0) + 1
         d_host = toks.view(B, k + 1).cpu().numpy()[:, 1:]
         self.stats["h2d_bytes"] += bt.size * 4 + (k + 1) * 12 * B + 12 * V
         self.stats["d2h_bytes"] += 8 * V
