@@ -35,12 +35,12 @@ def main(argv=None):
             w.pack()
             w.buf = None  # only the tile-packed copy is streamed
         ws.append(w)
-    act = K.ActQ(8, args.cols, dev)
+    act = K.ActQ(max(8, args.batch), args.cols, dev)
     K.quant_act(torch.randn(args.batch, args.cols, device=dev), act)
-    y = torch.zeros(8, args.rows, device=dev)
+    y = torch.zeros(max(8, args.batch), args.rows, device=dev)
     C = ext()
 
-    part, cnt = K.tgemv_workspace(dev)
+    part, cnt = K.tgemv_workspace(dev, ws)
 
     def run(w):
         if args.kernel == "tgemv":

@@ -24,7 +24,8 @@ def main(argv=None):
     ap.add_argument("--ctx", type=int, default=9000)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--prefill", type=int, default=1280, help="tokens in the timed prefill chunk")
+    ap.add_argument("--prefill", type=int, default=1280, help="tokens per sequence in the timed prefill chunk")
+    ap.add_argument("--prefill-seqs", type=int, default=1, help="sequences in the timed prefill chunk")
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (one launch per op)")
     ap.add_argument("--decode-only", action="store_true")
     args = ap.parse_args(argv)
@@ -38,9 +39,10 @@ def main(argv=None):
     torch.cuda.set_device(dev)
     cfg = preset(args.model)
     B = args.batch
-    max_ctx = (args.ctx + args.steps + args.warmup + 64 + 15) // 16 * 16
+    # the RoPE tables and block tables cover both the decode contexts and the timed prefill
+    max_ctx = (max(args.ctx + args.steps + args.warmup + 64, args.prefill) + 15) // 16 * 16
     ecfg = EngineConfig(max_batch=max(B, 8), cuda_graph=not args.eager, graph_batch_buckets=(B,),
-                        max_prefill_tokens=max(4096, args.prefill))
+                        max_prefill_tokens=max(4096, args.prefill * args.prefill_seqs))
     eng = Engine.synthetic(cfg, args.mix, 0, ecfg, dev, max_context=max_ctx)
     if not args.eager:
         eng.warmup_graphs()
@@ -72,15 +74,19 @@ def main(argv=None):
            "launches_per_step": (K.launches() - l0) / args.steps,
            "weight_bytes": eng.weights.nbytes()}
     if not args.decode_only:
-        T = args.prefill
+        # --prefill-seqs independent sequences of --prefill tokens in one chunk
+        L, S = args.prefill, args.prefill_seqs
+        T = L * S
         ids = torch.from_numpy(rng.integers(0, cfg.vocab_size, T).astype(np.int32)).to(dev)
-        pages = eng.pool.alloc((T + 15) // 16)
-        pos = torch.arange(T, dtype=torch.int32, device=dev)
-        pg = torch.tensor(pages, dtype=torch.int64, device=dev)
-        slot = (pg[pos.long() // 16] * 16 + pos.long() % 16).int()
-        bt = torch.tensor([pages], dtype=torch.int32, device=dev)
-        meta = PrefillMeta.build([T], [0], dev)
-        last = torch.tensor([T - 1], dtype=torch.int32, device=dev)
+        npg = (L + 15) // 16
+        pages = [eng.pool.alloc(npg) for _ in range(S)]
+        pos = torch.arange(L, dtype=torch.int32, device=dev).repeat(S)
+        pg = torch.tensor(pages, dtype=torch.int64, device=dev)                 # [S, npg]
+        seq = torch.arange(S, device=dev).repeat_interleave(L)
+        slot = (pg[seq, pos.long() // 16] * 16 + pos.long() % 16).int()
+        bt = pg.int()
+        meta = PrefillMeta.build([L] * S, [0] * S, dev)
+        last = (torch.arange(S, dtype=torch.int32, device=dev) + 1) * L - 1
         for _ in range(2):
             eng.runner.prefill(ids, pos, slot, bt, meta, last)
         torch.cuda.synchronize()
@@ -94,7 +100,7 @@ def main(argv=None):
         torch.cuda.synchronize()
         pms = e0.elapsed_time(e1) / n
         flops = 2.0 * T * (cfg.param_count() - cfg.vocab_size * cfg.d_model)
-        out.update({"prefill_tokens": T, "prefill_ms": round(pms, 3), "prefill_tok_s": round(T * 1000 / pms, 1),
+        out.update({"prefill_seqs": S, "prefill_tokens": T, "prefill_ms": round(pms, 3), "prefill_tok_s": round(T * 1000 / pms, 1),
                     "prefill_linear_tflops": round(flops / pms / 1e9, 1)})
     print(json.dumps(out), flush=True)
 

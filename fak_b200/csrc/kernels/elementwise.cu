@@ -70,14 +70,16 @@ __global__ void k_rope_kv(const float* __restrict__ qkv, int64_t ld, const int* 
                           const int* __restrict__ slot, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                           int H, int Hkv, const float* __restrict__ qn, const float* __restrict__ kn, float eps,
                           float* __restrict__ q_f32, __nv_bfloat16* __restrict__ q_bf16,
-                          __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int n_pages) {
+                          __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int n_pages, int n_pos) {
   constexpr int PER = D / 32;  // values per lane
   constexpr int HALF = D / 2;
   pdl_wait();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
-  const int p = pos[t];
+  // positions past the RoPE table are clamped (the engine never issues them; the clamp keeps a
+  // bad position from reading outside the table)
+  const int p = min(max(pos[t], 0), n_pos - 1);
   const int sl = slot[t];
   const int page = sl / PAGE, off = sl % PAGE;
   const float* row = qkv + (int64_t)t * ld;
@@ -277,7 +279,8 @@ void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Te
               "cache layout");
   TORCH_CHECK(qkv.size(1) >= (H + 2 * Hkv) * D, "qkv width");
   TORCH_CHECK(pos.scalar_type() == torch::kInt32 && slot.scalar_type() == torch::kInt32, "pos/slot int32");
-  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.size(1) == D / 2, "cos table");
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.size(1) == D / 2 && cos_t.size(0) >= 1 &&
+                  sin_t.sizes() == cos_t.sizes(), "cos/sin table");
   if (T == 0) return;
   const float* qn = q_norm.has_value() ? q_norm->data_ptr<float>() : nullptr;
   const float* kn = k_norm.has_value() ? k_norm->data_ptr<float>() : nullptr;
@@ -291,7 +294,8 @@ void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Te
                                       (const int*)pos.data_ptr<int>(), (const int*)slot.data_ptr<int>(),
                                       (const float*)cos_t.data_ptr<float>(), (const float*)sin_t.data_ptr<float>(),
                                       (int)H, (int)Hkv, qn, kn, (float)eps, qf, qb,
-                                      (__nv_bfloat16*)k_cache.data_ptr(), (__nv_bfloat16*)v_cache.data_ptr(), n_pages));
+                                      (__nv_bfloat16*)k_cache.data_ptr(), (__nv_bfloat16*)v_cache.data_ptr(), n_pages,
+                                      (int)cos_t.size(0)));
   };
   if (D == 128) launch(k_rope_kv<128>);
   else if (D == 64) launch(k_rope_kv<64>);

@@ -45,7 +45,7 @@ using namespace fak;
 namespace {
 
 enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
-constexpr int MAXB = 8;
+constexpr int MAXNT = 4;  // n8 token tiles per launch: up to 32 tokens
 constexpr int MAGIC_I = 0x4B400000;
 constexpr float MAGIC_F = 12582912.0f;
 
@@ -100,16 +100,17 @@ struct TGeo {
 struct TSmem {
   int ring, xs, dsr, dsT, czT, tab, bars, total;
 };
-__host__ __device__ inline TSmem tsmem(int qt, int W, int R, const TGeo& g) {
+__host__ __device__ inline TSmem tsmem(int qt, int W, int R, int NT, const TGeo& g) {
   const int UT = qt == QT_Q4_K ? 2304 : (qt == QT_Q6_K ? 3360 : 4352);
   const int TABF = qt == QT_Q4_K ? 256 : (qt == QT_Q6_K ? 256 : 128);
+  const int MB = 8 * NT;  // token rows staged
   TSmem s;
   s.ring = 0;
   s.xs = W * R * UT;
-  s.dsr = s.xs + MAXB * g.xstride;
-  s.dsT = s.dsr + MAXB * g.dstride * 8;
-  s.czT = s.dsT + g.Us * 8 * MAXB * 8;
-  s.tab = s.czT + (qt == QT_Q6_K ? g.Us * 16 * MAXB * 4 : 0);
+  s.dsr = s.xs + MB * g.xstride;
+  s.dsT = s.dsr + MB * g.dstride * 8;
+  s.czT = s.dsT + g.Us * 8 * MB * 8;
+  s.tab = s.czT + (qt == QT_Q6_K ? g.Us * 16 * MB * 4 : 0);
   s.bars = s.tab + W * TABF * 4;
   s.total = s.bars + (W * R + 1) * 8;
   return s;
@@ -117,11 +118,14 @@ __host__ __device__ inline TSmem tsmem(int qt, int W, int R, const TGeo& g) {
 
 // ---- one unit tile -------------------------------------------------------------------------
 // wt: the unit tile in shared memory; tab: this warp's scale table; xr: token g's codes at this
-// unit; dsT: (scale, sum) at this unit's first block, [block][token]; czT (Q6_K): accumulator
-// starts at this unit's first 16-block, [k16][token].
-template <int QT>
+// unit (token 8 nt + g at xr + 8 nt * xstride); dsT: (scale, sum) at this unit's first block,
+// [block][token]; czT (Q6_K): accumulator starts at this unit's first 16-block, [k16][token].
+// The weight fragments and scales of a sub-block are unpacked once and reused for every n8 tile.
+template <int QT, int NT>
 FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, const int8_t* __restrict__ xr,
-                       const float2* __restrict__ dsT, const int* __restrict__ czT, int lane, float (&acc)[4]) {
+                       int xstride, const float2* __restrict__ dsT, const int* __restrict__ czT, int lane,
+                       float (&acc)[NT][4]) {
+  constexpr int MB = 8 * NT;
   const int g = lane >> 2, t = lane & 3;
   const int sA = 2 * g, sB = 2 * g + 1;
   if constexpr (QT == QT_Q4_K) {
@@ -155,15 +159,18 @@ FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, 
         const int j = 2 * c + hi;
         const uint32_t m = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
         const uint32_t a[4] = {qa.x & m, qb.x & m, qa.y & m, qb.y & m};
-        const uint2 xb = *reinterpret_cast<const uint2*>(xr + 32 * j + 8 * t);
-        int cc[4];
-        mma_u8s8_k32(cc, a, xb.x, xb.y, MAGIC_I, MAGIC_I);
         const float4 am = *reinterpret_cast<const float4*>(tab + 2 * (j * 16 + sA));  // A_g, M_g, A_g8, M_g8
-        const float4 dx = *reinterpret_cast<const float4*>(dsT + j * MAXB + 2 * t);  // d0, s0, d1, s1
-        acc[0] = fmaf(am.x * dx.x, magic_f(cc[0]), fmaf(-am.y, dx.y, acc[0]));
-        acc[1] = fmaf(am.x * dx.z, magic_f(cc[1]), fmaf(-am.y, dx.w, acc[1]));
-        acc[2] = fmaf(am.z * dx.x, magic_f(cc[2]), fmaf(-am.w, dx.y, acc[2]));
-        acc[3] = fmaf(am.z * dx.z, magic_f(cc[3]), fmaf(-am.w, dx.w, acc[3]));
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+          const uint2 xb = *reinterpret_cast<const uint2*>(xr + nt * 8 * xstride + 32 * j + 8 * t);
+          int cc[4];
+          mma_u8s8_k32(cc, a, xb.x, xb.y, MAGIC_I, MAGIC_I);
+          const float4 dx = *reinterpret_cast<const float4*>(dsT + j * MB + nt * 8 + 2 * t);  // d0, s0, d1, s1
+          acc[nt][0] = fmaf(am.x * dx.x, magic_f(cc[0]), fmaf(-am.y, dx.y, acc[nt][0]));
+          acc[nt][1] = fmaf(am.x * dx.z, magic_f(cc[1]), fmaf(-am.y, dx.w, acc[nt][1]));
+          acc[nt][2] = fmaf(am.z * dx.x, magic_f(cc[2]), fmaf(-am.w, dx.y, acc[nt][2]));
+          acc[nt][3] = fmaf(am.z * dx.z, magic_f(cc[3]), fmaf(-am.w, dx.w, acc[nt][3]));
+        }
       }
     }
   } else if constexpr (QT == QT_Q6_K) {
@@ -200,16 +207,19 @@ FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, 
           const uint32_t a0 = ((la >> ls) & 0x0F0F0F0Fu) | (((ha >> hs) & 0x03030303u) << 4);
           const uint32_t a1 = ((lb >> ls) & 0x0F0F0F0Fu) | (((hb >> hs) & 0x03030303u) << 4);
           const int e0 = 128 * n + 32 * kk + 16 * h;  // first weight of this 16-block
-          const uint32_t xv = *reinterpret_cast<const uint32_t*>(xr + e0 + 4 * t);
-          const int2 cz = *reinterpret_cast<const int2*>(czT + (e0 >> 4) * MAXB + 2 * t);
-          int cc[4];
-          mma_u8s8_k16(cc, a0, a1, xv, cz.x, cz.y);
           const float2 A = *reinterpret_cast<const float2*>(tab + (e0 >> 4) * 16 + sA);
-          const float4 dx = *reinterpret_cast<const float4*>(dsT + (e0 >> 5) * MAXB + 2 * t);
-          acc[0] = fmaf(A.x * dx.x, magic_f(cc[0]), acc[0]);
-          acc[1] = fmaf(A.x * dx.z, magic_f(cc[1]), acc[1]);
-          acc[2] = fmaf(A.y * dx.x, magic_f(cc[2]), acc[2]);
-          acc[3] = fmaf(A.y * dx.z, magic_f(cc[3]), acc[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) {
+            const uint32_t xv = *reinterpret_cast<const uint32_t*>(xr + nt * 8 * xstride + e0 + 4 * t);
+            const int2 cz = *reinterpret_cast<const int2*>(czT + (e0 >> 4) * MB + nt * 8 + 2 * t);
+            int cc[4];
+            mma_u8s8_k16(cc, a0, a1, xv, cz.x, cz.y);
+            const float4 dx = *reinterpret_cast<const float4*>(dsT + (e0 >> 5) * MB + nt * 8 + 2 * t);
+            acc[nt][0] = fmaf(A.x * dx.x, magic_f(cc[0]), acc[nt][0]);
+            acc[nt][1] = fmaf(A.x * dx.z, magic_f(cc[1]), acc[nt][1]);
+            acc[nt][2] = fmaf(A.y * dx.x, magic_f(cc[2]), acc[nt][2]);
+            acc[nt][3] = fmaf(A.y * dx.z, magic_f(cc[3]), acc[nt][3]);
+          }
         }
       }
     }
@@ -232,24 +242,27 @@ FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, 
       const uint2 qa = *reinterpret_cast<const uint2*>(rA + 16 * (q ^ (sA & 6)));
       const uint2 qb = *reinterpret_cast<const uint2*>(rB + 16 * (q ^ (sB & 6)));
       const uint32_t a[4] = {qa.x, qb.x, qa.y, qb.y};
-      const uint2 xb = *reinterpret_cast<const uint2*>(xr + 32 * b + 8 * t);
-      int cc[4];
-      mma_s8s8_k32(cc, a, xb.x, xb.y, MAGIC_I, MAGIC_I);
       const float2 D = *reinterpret_cast<const float2*>(tab + b * 16 + sA);
-      const float4 dx = *reinterpret_cast<const float4*>(dsT + b * MAXB + 2 * t);
-      acc[0] = fmaf(D.x * dx.x, magic_f(cc[0]), acc[0]);
-      acc[1] = fmaf(D.x * dx.z, magic_f(cc[1]), acc[1]);
-      acc[2] = fmaf(D.y * dx.x, magic_f(cc[2]), acc[2]);
-      acc[3] = fmaf(D.y * dx.z, magic_f(cc[3]), acc[3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        const uint2 xb = *reinterpret_cast<const uint2*>(xr + nt * 8 * xstride + 32 * b + 8 * t);
+        int cc[4];
+        mma_s8s8_k32(cc, a, xb.x, xb.y, MAGIC_I, MAGIC_I);
+        const float4 dx = *reinterpret_cast<const float4*>(dsT + b * MB + nt * 8 + 2 * t);
+        acc[nt][0] = fmaf(D.x * dx.x, magic_f(cc[0]), acc[nt][0]);
+        acc[nt][1] = fmaf(D.x * dx.z, magic_f(cc[1]), acc[nt][1]);
+        acc[nt][2] = fmaf(D.y * dx.x, magic_f(cc[2]), acc[nt][2]);
+        acc[nt][3] = fmaf(D.y * dx.z, magic_f(cc[3]), acc[nt][3]);
+      }
     }
   }
   __syncwarp();  // table and slot reads done before the next unit overwrites them
 }
 
-FAK_DEV void epilogue(int tile, const float (&v)[4], int lane, int N, int B, float* __restrict__ y, int64_t ldy,
-                      const float* __restrict__ bias, int epi) {
+FAK_DEV void epilogue(int tile, const float (&v)[4], int tokb, int lane, int N, int B, float* __restrict__ y,
+                      int64_t ldy, const float* __restrict__ bias, int epi) {
   const int g = lane >> 2, t = lane & 3;
-  const int r0 = tile * 16, tok0 = 2 * t, tok1 = 2 * t + 1;
+  const int r0 = tile * 16, tok0 = tokb + 2 * t, tok1 = tokb + 2 * t + 1;
   const int rowa = r0 + g, rowb = r0 + g + 8;
   if (epi == EPI_SWIGLU) {
     // rows [r0, r0+8) are the gate rows of outputs [r0/2, r0/2+8), rows [r0+8, r0+16) the up rows
@@ -278,7 +291,7 @@ FAK_DEV void epilogue(int tile, const float (&v)[4], int lane, int N, int B, flo
   }
 }
 
-template <int QT, int W, int R>
+template <int QT, int W, int R, int NT>
 __global__ void __launch_bounds__(W * 32, 1)
 k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
         const float* __restrict__ xf, int64_t ldx, const float* __restrict__ gamma, float eps,
@@ -286,8 +299,9 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
         float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo) {
   constexpr int UT = Tile<QT>::UT;
   constexpr int TABF = Tile<QT>::TABF;
+  constexpr int MB = 8 * NT;  // token rows staged
   extern __shared__ __align__(128) uint8_t sm[];
-  const TSmem L = tsmem(QT, W, R, geo);
+  const TSmem L = tsmem(QT, W, R, NT, geo);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slice = blockIdx.x % geo.S, cta = blockIdx.x / geo.S;
   const int u0 = slice * geo.Us;
@@ -337,7 +351,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   if (xf != nullptr) {
     // fp32 activations: optional RMSNorm (statistics over the whole row), then int8 per 32-block
     // with (scale, exact sum) -- the activation quantizer, done while the weight copies fly
-    __shared__ float s_inv[MAXB];
+    __shared__ float s_inv[8 * MAXNT];
     if (gamma != nullptr) {
       for (int b = warp; b < B; b += W) {
         const float* xr = xf + (int64_t)b * ldx;
@@ -352,7 +366,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       __syncthreads();
     }
     const int nblk = nu * 8;
-    for (int i = threadIdx.x; i < MAXB * nblk; i += W * 32) {
+    for (int i = threadIdx.x; i < MB * nblk; i += W * 32) {
       const int b = i / nblk, blk = i - b * nblk;
       const int kk = blk * 32;
       uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
@@ -389,7 +403,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       uint4* dst = reinterpret_cast<uint4*>(xs + b * geo.xstride + kk);
       dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
       dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      dsT[blk * MAXB + b] = dsv;
+      dsT[blk * MB + b] = dsv;
     }
   } else {
     if (threadIdx.x == 0) {
@@ -401,20 +415,20 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       }
     }
     // zero the activation columns no copy writes (missing tokens, padding past K)
-    for (int i = threadIdx.x; i < MAXB * (nu * 256 / 16); i += W * 32) {
+    for (int i = threadIdx.x; i < MB * (nu * 256 / 16); i += W * 32) {
       const int b = i / (nu * 16), c = (i % (nu * 16)) * 16;
       if (b >= B || c >= kb) *reinterpret_cast<uint4*>(xs + b * geo.xstride + c) = make_uint4(0, 0, 0, 0);
     }
     tc::mbar_wait(act_bar, 0, err);
-    for (int i = threadIdx.x; i < nu * 8 * MAXB; i += W * 32) {
-      const int blk = i / MAXB, b = i % MAXB;
+    for (int i = threadIdx.x; i < nu * 8 * MB; i += W * 32) {
+      const int blk = i / MB, b = i % MB;
       dsT[i] = (b < B && blk * 32 < kb) ? dsr[b * geo.dstride + blk] : make_float2(0.f, 0.f);
     }
   }
   if constexpr (QT == QT_Q6_K) {
     __syncthreads();
-    for (int i = threadIdx.x; i < nu * 16 * MAXB; i += W * 32) {
-      const int k16 = i / MAXB, b = i % MAXB;
+    for (int i = threadIdx.x; i < nu * 16 * MB; i += W * 32) {
+      const int k16 = i / MB, b = i % MB;
       const int4 v = *reinterpret_cast<const int4*>(xs + b * geo.xstride + 16 * k16);
       int sm4 = __dp4a(v.x, 0x01010101, 0);
       sm4 = __dp4a(v.y, 0x01010101, sm4);
@@ -425,7 +439,9 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   }
   __syncthreads();
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
   const int g = lane >> 2;
   const int8_t* xg = xs + g * geo.xstride;
   int cslot = 0, ul = 0, tile = wg;
@@ -433,8 +449,8 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   for (int q = 0; q < Q; q++) {
     if (lane == 0) issue_next();  // into the slot released at the end of the previous iteration
     tc::mbar_wait(&bar[cslot], phase, err);
-    unit_tile<QT>(ring + cslot * UT, tab, xg + ul * 256, dsT + ul * 8 * MAXB,
-                  QT == QT_Q6_K ? czT + ul * 16 * MAXB : nullptr, lane, acc);
+    unit_tile<QT, NT>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
+                      QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
     if (++cslot == R) {
       cslot = 0;
       phase ^= 1u;
@@ -442,10 +458,13 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
     if (++ul < nu) continue;
     ul = 0;
     if (geo.S == 1) {
-      epilogue(tile, acc, lane, N, B, y, ldy, bias, epi);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) epilogue(tile, acc[nt], 8 * nt, lane, N, B, y, ldy, bias, epi);
     } else {
-      float4* mine = reinterpret_cast<float4*>(part + ((size_t)slice * geo.T + tile) * 128) + lane;
-      *mine = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      // partials [slice][tile][n8 tile][lane] float4
+      float4* mine = reinterpret_cast<float4*>(part + ((size_t)slice * geo.T + tile) * 128 * NT) + lane;
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) mine[32 * nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
       __threadfence();
       __syncwarp();
       int old = 0;
@@ -453,67 +472,87 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       old = __shfl_sync(0xffffffffu, old, 0);
       if (old == geo.S - 1) {  // last slice of this tile: reduce in slice order
         __threadfence();
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int s = 0; s < geo.S; s++) {
-          const float4 p = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)s * geo.T + tile) * 128) + lane);
-          v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int s = 0; s < geo.S; s++) {
+            const float4 p =
+                __ldcg(reinterpret_cast<const float4*>(part + ((size_t)s * geo.T + tile) * 128 * NT) + 32 * nt + lane);
+            v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
+          }
+          epilogue(tile, v, 8 * nt, lane, N, B, y, ldy, bias, epi);
         }
-        epilogue(tile, v, lane, N, B, y, ldy, bias, epi);
         if (lane == 0) cnt[tile] = 0;  // ready for the next launch
       }
     }
-    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     tile += wstride;
   }
   pdl_launch_dependents();
 }
 
 struct Plan {
-  int W, R;
+  int W, R, NT;
   TGeo geo;
   int smem;
 };
 
 int tile_bytes(int qt) { return qt == QT_Q4_K ? 2304 : (qt == QT_Q6_K ? 3360 : 4352); }
 
-// Choose (warps per CTA, ring depth) and the K split.  The split minimises the unit tiles on
-// the busiest warp (rounds of tiles x units per slice, plus the split-K reduction), among splits
-// whose activation staging fits in shared memory.  Depends only on the matrix shape and the GPU,
-// never on the batch size, so batched and serial decoding reduce in the same order.
-Plan make_plan(int qt, int64_t N, int64_t K, int n_sm, int max_smem, int force_w, int force_r, int force_s) {
+// Choose the K split, then (warps per CTA, ring depth) and the token tile width.  The split
+// minimises the unit tiles on the busiest warp (rounds of tiles x units per slice, plus the split-K
+// reduction) among splits whose 8-token staging fits in shared memory; it depends only on the
+// matrix shape and the GPU -- never on the batch -- so a token reduces in the same order whatever
+// batch it runs in.  Wider token tiles (16 / 32 tokens per launch) are used when their staging fits
+// with that split; otherwise the batch runs as several launches of the widest tile that fits.
+static const int kCand[][2] = {{16, 3}, {16, 2}, {8, 3}};
+
+TGeo make_geo(int qt, int T, int U, int S0, int n_sm) {
+  const int Us = (U + S0 - 1) / S0;
+  TGeo g;
+  g.T = T;
+  g.U = U;
+  g.S = (U + Us - 1) / Us;
+  g.Us = Us;
+  g.P = std::max(1, n_sm / g.S);
+  // activation rows 32 mod 128 bytes apart (8-byte loads, Q4_K/Q8_0) or 16 mod 128 (4-byte, Q6_K)
+  g.xstride = ((Us * 256 + 127) / 128) * 128 + (qt == QT_Q6_K ? 16 : 32);
+  g.dstride = Us * 8;
+  return g;
+}
+
+Plan make_plan(int qt, int64_t N, int64_t K, int NT, int n_sm, int max_smem, int force_w, int force_r,
+               int force_s) {
   const int T = (int)((N + 15) / 16);
   const int U = (int)((K + 255) / 256);
-  // activation rows 32 mod 128 bytes apart (8-byte loads, Q4_K/Q8_0) or 16 mod 128 (4-byte, Q6_K)
-  const int xpad = qt == QT_Q6_K ? 16 : 32;
-  static const int cand[][2] = {{16, 3}, {16, 2}, {8, 4}, {8, 3}, {8, 2}};
-  for (auto& c : cand) {
-    const int W = force_w ? force_w : c[0], R = force_r ? force_r : c[1];
-    Plan best{};
+  int S = force_s;
+  if (!S) {
+    // over every (warps, depth) candidate and split; ties keep the fewer slices / wider CTA
     double best_cost = 1e30;
-    for (int s0 = force_s ? force_s : 1; s0 <= (force_s ? force_s : std::min(U, n_sm)); s0++) {
-      const int Us = (U + s0 - 1) / s0;
-      const int S = (U + Us - 1) / Us;
-      if (S != s0 && !force_s) continue;  // same split as a smaller s0
-      TGeo g;
-      g.T = T;
-      g.U = U;
-      g.S = S;
-      g.Us = Us;
-      g.P = std::max(1, n_sm / S);
-      g.xstride = ((Us * 256 + 127) / 128) * 128 + xpad;
-      g.dstride = Us * 8;
-      const TSmem L = tsmem(qt, W, R, g);
-      if (L.total > max_smem) continue;
-      const int64_t warps = (int64_t)W * g.P;
-      const int64_t rounds = (T + warps - 1) / warps;
-      const double cost = (double)rounds * (Us + (S > 1 ? 1.0 : 0.3));
-      if (cost < best_cost) {
-        best_cost = cost;
-        best = Plan{W, R, g, L.total};
+    for (auto& c : kCand) {
+      for (int s0 = 1; s0 <= std::min(U, n_sm); s0++) {
+        const TGeo g = make_geo(qt, T, U, s0, n_sm);
+        if (g.S != s0) continue;  // same split as a smaller s0
+        if (tsmem(qt, c[0], c[1], 1, g).total > max_smem) continue;
+        const int64_t warps = (int64_t)c[0] * g.P;
+        const int64_t rounds = (T + warps - 1) / warps;
+        const double cost = (double)rounds * (g.Us + (g.S > 1 ? 1.0 : 0.3));
+        if (cost < best_cost - 1e-9) {
+          best_cost = cost;
+          S = g.S;
+        }
       }
     }
-    if (best_cost < 1e30) return best;
-    if (force_w && force_r) break;
+    TORCH_CHECK(S, "tgemv: no K split fits in shared memory for K=", K);
+  }
+  const TGeo g = make_geo(qt, T, U, S, n_sm);
+  for (int nt = NT; nt >= 1; nt >>= 1) {
+    for (auto& c : kCand) {
+      const int W = force_w ? force_w : c[0], R = force_r ? force_r : c[1];
+      const TSmem L = tsmem(qt, W, R, nt, g);
+      if (L.total <= max_smem) return Plan{W, R, nt, g, L.total};
+    }
   }
   TORCH_CHECK(false, "tgemv: no launch configuration fits in shared memory for K=", K);
   return Plan{};
@@ -528,9 +567,9 @@ std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_
   int n_sm = 0, max_smem = 0;
   FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, (int)device));
   FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, (int)device));
-  Plan p = make_plan((int)qtype, N, K, n_sm, max_smem, 0, 0, 0);
-  return {p.geo.S > 1 ? (int64_t)p.geo.S * p.geo.T * 128 : 0, p.geo.S > 1 ? (int64_t)p.geo.T : 0, p.geo.S, p.W,
-          p.R, p.smem};
+  Plan p = make_plan((int)qtype, N, K, 1, n_sm, max_smem, 0, 0, 0);
+  return {p.geo.S > 1 ? (int64_t)p.geo.S * p.geo.T * 128 * MAXNT : 0, p.geo.S > 1 ? (int64_t)p.geo.T : 0, p.geo.S,
+          p.W, p.R, p.smem};
 }
 
 // w: tile-packed weights (uint8, ceil(N/16) * ceil(K/256) unit tiles); activations either quantized
@@ -573,7 +612,8 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     dp = reinterpret_cast<const float2*>(ds->data_ptr<float>());
   }
   TORCH_CHECK(y.scalar_type() == torch::kFloat32 && y.dim() == 2 && y.stride(1) == 1, "tgemv: y [B, *] f32");
-  TORCH_CHECK(B >= 1 && B <= MAXB, "tgemv: 1 <= B <= 8");
+  TORCH_CHECK(B >= 1 && B <= 8 * MAXNT, "tgemv: 1 <= B <= 32");
+  const int NT = (int)((B + 7) / 8) <= 1 ? 1 : ((B + 7) / 8 <= 2 ? 2 : 4);
   if (epi == EPI_SWIGLU) TORCH_CHECK(N % 16 == 0, "tgemv: SwiGLU needs 8-row interleaved gate/up blocks");
   TORCH_CHECK(y.size(0) >= B && y.size(1) >= (epi == EPI_SWIGLU ? N / 2 : N), "tgemv: y too small");
   const float* bp = nullptr;
@@ -586,10 +626,10 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, w.get_device()));
     FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, w.get_device()));
   }
-  Plan p = make_plan((int)qtype, N, K, n_sm, max_smem, (int)(flags & 31), (int)((flags >> 5) & 15),
+  Plan p = make_plan((int)qtype, N, K, NT, n_sm, max_smem, (int)(flags & 31), (int)((flags >> 5) & 15),
                      (int)((flags >> 9) & 255));
   if (p.geo.S > 1) {
-    TORCH_CHECK(part.scalar_type() == torch::kFloat32 && part.numel() >= (int64_t)p.geo.S * p.geo.T * 128,
+    TORCH_CHECK(part.scalar_type() == torch::kFloat32 && part.numel() >= (int64_t)p.geo.S * p.geo.T * 128 * p.NT,
                 "tgemv: split-K scratch too small");
     TORCH_CHECK(cnt.scalar_type() == torch::kInt32 && cnt.numel() >= p.geo.T, "tgemv: split-K counters too small");
   }
@@ -604,25 +644,37 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
+  // the batch runs as launches of up to 8 * p.NT tokens (one launch unless the wide staging did
+  // not fit); each token's arithmetic is the same in every launch shape
+  const int chunk = 8 * p.NT;
   auto go = [&](auto kern) {
     FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem));
-    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.data_ptr<uint8_t>(), (int)N, (int)K, qp, dp,
-                                      xp, ldx, gp, (float)eps, (int)B,
-                                      y.data_ptr<float>(), (int64_t)y.stride(0), bp, (int)epi,
-                                      p.geo.S > 1 ? part.data_ptr<float>() : nullptr,
-                                      p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo));
+    for (int64_t b0 = 0; b0 < B; b0 += chunk) {
+      const int nb = (int)std::min<int64_t>(chunk, B - b0);
+      FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.data_ptr<uint8_t>(), (int)N, (int)K,
+                                        qp ? qp + b0 * K : nullptr, dp ? dp + b0 * (K / 32) : nullptr,
+                                        xp ? xp + b0 * ldx : nullptr, ldx, gp, (float)eps, nb,
+                                        y.data_ptr<float>() + b0 * y.stride(0), (int64_t)y.stride(0), bp, (int)epi,
+                                        p.geo.S > 1 ? part.data_ptr<float>() : nullptr,
+                                        p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo));
+    }
   };
-#define FAK_TG(QTV)                                                       \
-  {                                                                       \
-    if (p.W == 16 && p.R == 3) go(k_tgemv<QTV, 16, 3>);                   \
-    else if (p.W == 16 && p.R == 2) go(k_tgemv<QTV, 16, 2>);              \
-    else if (p.W == 8 && p.R == 4) go(k_tgemv<QTV, 8, 4>);                \
-    else if (p.W == 8 && p.R == 3) go(k_tgemv<QTV, 8, 3>);                \
-    else if (p.W == 8 && p.R == 2) go(k_tgemv<QTV, 8, 2>);                \
+#define FAK_TG_NT(QTV, NTV)                                              \
+  {                                                                      \
+    if (p.W == 16 && p.R == 3) go(k_tgemv<QTV, 16, 3, NTV>);             \
+    else if (p.W == 16 && p.R == 2) go(k_tgemv<QTV, 16, 2, NTV>);        \
+    else if (p.W == 8 && p.R == 3) go(k_tgemv<QTV, 8, 3, NTV>);          \
     else TORCH_CHECK(false, "tgemv: unsupported (warps, depth) ", p.W, ",", p.R); \
+  }
+#define FAK_TG(QTV)                     \
+  {                                     \
+    if (p.NT == 1) FAK_TG_NT(QTV, 1)      \
+    else if (p.NT == 2) FAK_TG_NT(QTV, 2) \
+    else FAK_TG_NT(QTV, 4)                \
   }
   if (qtype == QT_Q4_K) FAK_TG(QT_Q4_K)
   else if (qtype == QT_Q6_K) FAK_TG(QT_Q6_K)
   else FAK_TG(QT_Q8_0)
 #undef FAK_TG
+#undef FAK_TG_NT
 }

@@ -10,6 +10,8 @@ import dataclasses
 
 import torch
 
+from .constraints import LogitMask, apply_constraint, guided_decode_enabled
+
 
 @dataclasses.dataclass
 class SamplingParams:
@@ -20,18 +22,18 @@ class SamplingParams:
     presence_penalty: float = 0.0
     logit_bias: dict[int, float] | None = None
     seed: int | None = None
+    mask: LogitMask | None = None  # structural constraint; active only with guided decoding on
 
     @property
     def greedy(self) -> bool:
+        """Plain argmax (the device-side greedy path): no bias, penalties or active mask."""
         return (self.temperature <= 0.0 and not self.logit_bias and self.frequency_penalty == 0.0
-                and self.presence_penalty == 0.0)
+                and self.presence_penalty == 0.0 and not (self.mask is not None and guided_decode_enabled()))
 
 
 def _apply_penalties(row: torch.Tensor, sp: SamplingParams, generated: list[int]) -> torch.Tensor:
-    if sp.logit_bias:
-        idx = torch.tensor(list(sp.logit_bias.keys()), device=row.device, dtype=torch.long)
-        row = row.clone()
-        row[idx] += torch.tensor(list(sp.logit_bias.values()), device=row.device, dtype=row.dtype)
+    # mask (hard) then clamped logit bias (soft), then repetition penalties
+    row = apply_constraint(row, sp.mask, sp.logit_bias, generated)
     if (sp.frequency_penalty or sp.presence_penalty) and generated:
         ids = torch.tensor(generated, device=row.device, dtype=torch.long)
         counts = torch.bincount(ids, minlength=row.numel()).to(row.dtype)

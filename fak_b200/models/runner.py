@@ -127,7 +127,9 @@ class ModelRunner:
         self.attn_ws = torch.zeros(B * self.Hq * self.max_split * (self.D + 2), dtype=torch.float32, device=dev)
         self.attn_tickets = torch.zeros(B * self.Hkv, dtype=torch.int32, device=dev)  # split-merge tickets
         # per-device kernel scratch, allocated here so no graph capture allocates it
-        K.tgemv_workspace(dev)
+        mats = [weights.lm_head] + [m for L in weights.layers
+                                    for m in [s for s, _ in L.qkv] + [L.o, L.gate_up, L.down]]
+        K.tgemv_workspace(dev, mats)
         K.argmax_workspace(dev, B)
         self._graphs: dict[int, tuple[torch.cuda.CUDAGraph, dict]] = {}
         self._graph_kernels: dict[int, int] = {}

@@ -6,7 +6,8 @@ import torch
 from ._ext import ext
 
 EPI_STORE, EPI_ADD, EPI_SWIGLU = 0, 1, 2
-GEMV_MAX_B = 8
+GEMV_MAX_B = 8      # tokens per launch of the row-major kernels
+TGEMV_MAX_B = 32    # tokens per launch of the tile-packed GEMV (4 MMA column tiles)
 
 # kernel-launch accounting (the benchmark reports how many of this package's kernels ran)
 _launches = [0]
@@ -58,13 +59,18 @@ _TG_TICKETS = 1 << 16
 _tg_ws: dict = {}
 
 
-def tgemv_workspace(device) -> tuple[torch.Tensor, torch.Tensor]:
-    """Allocate before any CUDA-graph capture: its addresses are baked into graphs."""
+def tgemv_workspace(device, weights=()) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split-K scratch sized for every matrix in ``weights`` (QuantWeights with a tile-packed copy).
+    Allocate before any CUDA-graph capture: its addresses are baked into graphs."""
     key = torch.device(device)
+    need_p, need_t = _TG_PART_FLOATS, _TG_TICKETS
+    for w in weights:
+        if w is not None and w.tp is not None:
+            p, t = ext().tgemv_workspace(w.qtype, w.rows, w.cols, key.index or 0)[:2]
+            need_p, need_t = max(need_p, p), max(need_t, t)
     ws = _tg_ws.get(key)
-    if ws is None:
-        ws = (torch.zeros(_TG_PART_FLOATS, dtype=torch.float32, device=key),
-              torch.zeros(_TG_TICKETS, dtype=torch.int32, device=key))
+    if ws is None or ws[0].numel() < need_p or ws[1].numel() < need_t:
+        ws = (torch.zeros(need_p, dtype=torch.float32, device=key), torch.zeros(need_t, dtype=torch.int32, device=key))
         _tg_ws[key] = ws
     return ws
 
@@ -78,8 +84,16 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
     C = ext()
     if w.tp is not None:
         part, cnt = tgemv_workspace(w.tp.device)
-        for b0 in range(0, B, GEMV_MAX_B):
-            nb = min(GEMV_MAX_B, B - b0)
+        need = getattr(w, "_tg_need", None)
+        if need is None:
+            need = w._tg_need = tuple(ext().tgemv_workspace(w.qtype, w.rows, w.cols, w.tp.device.index or 0)[:2])
+        if part.numel() < need[0] or cnt.numel() < need[1]:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("tgemv scratch too small inside a graph capture: size it beforehand "
+                                   "(ops.kernels.tgemv_workspace(device, weights))")
+            part, cnt = tgemv_workspace(w.tp.device, (w,))
+        for b0 in range(0, B, TGEMV_MAX_B):
+            nb = min(TGEMV_MAX_B, B - b0)
             if isinstance(act, FAct):
                 C.tgemv(w.tp, w.qtype, w.rows, w.cols, None, None, act.x[b0:b0 + nb], act.gamma, act.eps, nb,
                         y[b0:b0 + nb], bias, epi, part, cnt, None, flags)

@@ -32,8 +32,13 @@ from .backend import UpstreamBackend
 from .chat import extract_tool_calls, render_chatml
 
 
-def _sampling(body: dict) -> SamplingParams:
-    return SamplingParams(temperature=float(body.get("temperature", 0.0) or 0.0),
+def _sampling(body: dict, json_mask=None) -> SamplingParams:
+    """Request sampling fields; ``response_format: {"type": "json_object"}`` adds the JSON mask
+    (active when guided decoding is switched on, FAK_NATIVE_GUIDED_DECODE=1)."""
+    rf = body.get("response_format") or {}
+    mask = json_mask() if json_mask is not None and isinstance(rf, dict) and rf.get("type") in (
+        "json_object", "json_schema") else None
+    return SamplingParams(mask=mask, temperature=float(body.get("temperature", 0.0) or 0.0),
                           top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
                           frequency_penalty=float(body.get("frequency_penalty", 0.0) or 0.0),
                           presence_penalty=float(body.get("presence_penalty", 0.0) or 0.0),
@@ -65,6 +70,7 @@ class Gateway:
         self.default_max_tokens = default_max_tokens
         self.metrics = Metrics()
         self.tok = getattr(backend, "tok", None)
+        self._json = None
 
     # ------------------------------------------------------------------ generation core
     def _stop_ids(self) -> set[int]:
@@ -133,6 +139,15 @@ class Gateway:
                              + (f" ({v.claim})" if v.claim else ""))
         return allowed, notes
 
+    def _json_mask(self):
+        """JSON-prefix token mask over this tokenizer's vocabulary (built once)."""
+        if self.tok is None:
+            return None
+        if self._json is None:
+            from ..engine.constraints import JsonMask
+            self._json = JsonMask(lambda t: self.tok.decode([t]), self.tok.vocab_size, self.tok.eos_id)
+        return self._json
+
     # ------------------------------------------------------------------ OpenAI
     def chat_completion(self, body: dict) -> dict:
         rid = "chatcmpl-" + uuid.uuid4().hex[:24]
@@ -156,7 +171,7 @@ class Gateway:
         stop = body.get("stop")
         stop = [stop] if isinstance(stop, str) else stop
         for piece, inf in self.stream_text(prompt, int(body.get("max_tokens") or body.get("max_completion_tokens")
-                                                       or self.default_max_tokens), _sampling(body), stop):
+                                                       or self.default_max_tokens), _sampling(body, self._json_mask), stop):
             text += piece
             info = inf or info
         plain, calls = extract_tool_calls(text)
@@ -187,7 +202,7 @@ class Gateway:
         prompt = render_chatml(body.get("messages", []), body.get("tools"))
         text, info, held = "", {}, ""
         for piece, inf in self.stream_text(prompt, int(body.get("max_tokens") or self.default_max_tokens),
-                                           _sampling(body), None):
+                                           _sampling(body, self._json_mask), None):
             info = inf or info
             if not piece:
                 continue
@@ -226,7 +241,7 @@ class Gateway:
         text, info = "", {}
         stop = body.get("stop")
         stop = [stop] if isinstance(stop, str) else stop
-        for piece, inf in self.stream_text(prompt, int(body.get("max_tokens") or 16), _sampling(body), stop):
+        for piece, inf in self.stream_text(prompt, int(body.get("max_tokens") or 16), _sampling(body, self._json_mask), stop):
             text += piece
             info = inf or info
         return {"id": "cmpl-" + uuid.uuid4().hex[:24], "object": "text_completion", "created": int(time.time()),
@@ -243,7 +258,7 @@ class Gateway:
         mid = "msg_" + uuid.uuid4().hex[:24]
         text, info = "", {}
         for piece, inf in self.stream_text(self._anthropic_prompt(body), int(body.get("max_tokens") or 256),
-                                           _sampling(body), body.get("stop_sequences")):
+                                           _sampling(body, self._json_mask), body.get("stop_sequences")):
             text += piece
             info = inf or info
         plain, calls = extract_tool_calls(text)

@@ -254,13 +254,13 @@ def _tg_case(qt, N, Kd, B, seed=3):
     w = QuantWeight.from_rows(torch.from_numpy(raw), int(qt), Kd, torch.device("cuda")).pack()
     Wd = torch.from_numpy(Q.dequantize(raw.reshape(-1), qt).reshape(N, Kd)).cuda()
     x = torch.randn(B, Kd, device="cuda", generator=torch.Generator("cuda").manual_seed(seed))
-    act = K.ActQ(8, Kd, "cuda")
+    act = K.ActQ(max(8, B), Kd, "cuda")
     K.quant_act(x, act)
     return w, Wd, x, act
 
 
 @pytest.mark.parametrize("qt,blk", QTYPES)
-@pytest.mark.parametrize("B", [1, 5, 8])
+@pytest.mark.parametrize("B", [1, 5, 8, 13, 32])
 @pytest.mark.parametrize("epi", [0, 1, 2])
 @pytest.mark.parametrize("N", [576, 16 * 2400])
 def test_tgemv_tile_packed(qt, blk, B, epi, N):
@@ -288,22 +288,25 @@ def test_tgemv_tile_packed(qt, blk, B, epi, N):
 
 @pytest.mark.parametrize("qt,blk", QTYPES)
 def test_tgemv_batch_invariant_and_repeatable(qt, blk):
-    """Each token's output is bit-identical whether it runs alone or in a batch of 8, and the
+    """Each token's output is bit-identical whether it runs alone or in a batch of 8 or 32, and the
     split-K tickets are left at zero so a second launch gives the same bits."""
     from fak_b200.ops import kernels as K
     Kd = 3584 if qt != GGMLType.Q8_0 else 576
-    w, Wd, x, act = _tg_case(qt, 512, Kd, 8, seed=7)
+    w, Wd, x, act = _tg_case(qt, 512, Kd, 32, seed=7)
+    y32 = torch.zeros(32, 512, device="cuda")
+    K.gemv(w, act, 32, y32)           # four n8 token tiles per launch
     y8 = torch.zeros(8, 512, device="cuda")
-    K.gemv(w, act, 8, y8)
+    K.gemv(w, act, 8, y8)             # one tile
+    assert torch.equal(y8, y32[:8])
     again = torch.zeros_like(y8)
     K.gemv(w, act, 8, again)
     assert torch.equal(y8, again)
-    for b in range(8):
+    for b in (0, 3, 7, 21, 31):
         solo = K.ActQ(8, Kd, "cuda")
         K.quant_act(x[b:b + 1], solo)
         y1 = torch.zeros(1, 512, device="cuda")
         K.gemv(w, solo, 1, y1)
-        assert torch.equal(y1[0], y8[b]), b
+        assert torch.equal(y1[0], y32[b]), b
     assert not K.tgemv_workspace("cuda")[1].any()
 
 
