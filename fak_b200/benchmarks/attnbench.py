@@ -1,0 +1,76 @@
+"""Paged decode-attention benchmark: B sequences x ctx tokens over 16-token pages (CUDA events).
+
+Builds ``--layers`` independent KV caches (so consecutive launches stream from DRAM rather than
+L2), optionally sharing the first ``--shared`` tokens' pages between all sequences as the radix
+cache does, and times split-KV decode attention plus its combine.  Reports the KV bytes each launch
+must read (shared pages counted once) and the effective bandwidth.
+
+    python -m fak_b200.benchmarks.attnbench --batch 5 --ctx 9000 --shared 8192
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=5)
+    ap.add_argument("--ctx", type=int, default=9000)
+    ap.add_argument("--shared", type=int, default=8192, help="leading tokens whose pages all sequences share")
+    ap.add_argument("--heads", type=int, default=28)
+    ap.add_argument("--kv-heads", type=int, default=4)
+    ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--split", type=int, default=32)
+    args = ap.parse_args(argv)
+    from fak_b200.ops import kernels as K
+
+    dev = torch.device("cuda", 0)
+    B, H, Hkv, D, ctx = args.batch, args.heads, args.kv_heads, args.head_dim, args.ctx
+    n_sh = min(args.shared, ctx) // 16
+    per_seq = math.ceil(ctx / 16)
+    n_pages = n_sh + B * (per_seq - n_sh) + 1
+    g = torch.Generator(device=dev).manual_seed(0)
+    caches = [(torch.randn(n_pages, Hkv, 16, D, device=dev, generator=g).bfloat16(),
+               torch.randn(n_pages, Hkv, 16, D, device=dev, generator=g).bfloat16()) for _ in range(args.layers)]
+    bt = torch.zeros(B, per_seq, dtype=torch.int32)
+    nxt = 1 + n_sh
+    for b in range(B):
+        bt[b, :n_sh] = torch.arange(1, 1 + n_sh)
+        bt[b, n_sh:] = torch.arange(nxt, nxt + per_seq - n_sh)
+        nxt += per_seq - n_sh
+    bt = bt.to(dev)
+    ctx_t = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(B, H, D, device=dev)
+    act = K.ActQ(B, H * D, dev)
+    ws = torch.zeros(B * H * args.split * (D + 2), device=dev)
+
+    def run(i):
+        kc, vc = caches[i % args.layers]
+        K.decode_attention(q, kc, vc, bt, ctx_t, args.split, act=act, workspace=ws)
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.iters):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000 / args.iters
+    page_bytes = 2 * Hkv * 16 * D * 2
+    unique = (n_sh + B * (per_seq - n_sh)) * page_bytes
+    print(json.dumps({"kernel": "decode_attention+combine", "batch": B, "ctx": ctx, "shared": n_sh * 16,
+                      "heads": H, "kv_heads": Hkv, "head_dim": D, "splits": args.split, "us": round(us, 2),
+                      "unique_kv_bytes": unique, "tb_s_unique": round(unique / us / 1e6, 3),
+                      "tb_s_streamed": round(B * per_seq * page_bytes / us / 1e6, 3)}))
+
+
+if __name__ == "__main__":
+    main()
