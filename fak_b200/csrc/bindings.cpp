@@ -31,7 +31,8 @@ void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double 
                     torch::Tensor ds);
 void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
                         int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
-                        torch::Tensor counters, torch::Tensor err, int64_t ctas);
+                        torch::Tensor counters, torch::Tensor err, int64_t ctas, c10::optional<torch::Tensor> src2,
+                        int64_t src2_ld, int64_t dst2_off, int64_t dst2_ld, int64_t col2, int64_t ncols2);
 void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, int64_t n, int64_t flags_off,
                        int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas);
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
@@ -44,7 +45,8 @@ void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_
 void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<torch::Tensor> qx,
            c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
-           torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags);
+           torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
+           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs);
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device);
 int64_t tgemv_unit_bytes(int64_t qtype);
 void moe_qmmv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, int64_t pitch, torch::Tensor qx,
@@ -71,7 +73,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bf16", &rmsnorm_bf16);
   m.def("argmax_rows", &argmax_rows, pybind11::arg("logits"), pybind11::arg("V"), pybind11::arg("out"),
         pybind11::arg("keys") = pybind11::none(), pybind11::arg("tickets") = pybind11::none());
-  m.def("p2p_allgather_cols", &p2p_allgather_cols);
+  m.def("p2p_allgather_cols", &p2p_allgather_cols, pybind11::arg("peers"), pybind11::arg("src"), pybind11::arg("src_ld"),
+        pybind11::arg("dst_off"), pybind11::arg("dst_ld"), pybind11::arg("col0"), pybind11::arg("ncols"), pybind11::arg("B"),
+        pybind11::arg("flags_off"), pybind11::arg("site"), pybind11::arg("me"), pybind11::arg("counters"),
+        pybind11::arg("err"), pybind11::arg("ctas"), pybind11::arg("src2") = pybind11::none(), pybind11::arg("src2_ld") = 0,
+        pybind11::arg("dst2_off") = 0, pybind11::arg("dst2_ld") = 0, pybind11::arg("col2") = 0, pybind11::arg("ncols2") = 0);
   m.def("p2p_allreduce_add", &p2p_allreduce_add);
   m.def("p2p_argmax", &p2p_argmax);
   m.def("moe_route", &moe_route);
@@ -86,7 +92,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
         pybind11::arg("B"), pybind11::arg("y"), pybind11::arg("bias"),
         pybind11::arg("epi"), pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
-        pybind11::arg("flags") = 0);
+        pybind11::arg("flags") = 0, pybind11::arg("ar_peers") = pybind11::none(), pybind11::arg("ar_me") = 0,
+        pybind11::arg("ar_parts_off") = 0, pybind11::arg("ar_flags_off") = 0, pybind11::arg("ar_epochs") = pybind11::none());
   m.def("tgemv_workspace", &tgemv_workspace);
   m.def("tgemv_unit_bytes", &tgemv_unit_bytes);
   m.def("gemm_bf16", &gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"),

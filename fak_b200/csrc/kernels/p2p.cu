@@ -74,20 +74,28 @@ FAK_DEV void rank_barrier(const Peers& P, int64_t flags_off, int site, int cta, 
   if (threadIdx.x == 0) counters[site * MAX_CTAS + cta] = epoch;
 }
 
-// ---- all-gather of per-rank column blocks of a [B, row_bytes] byte matrix ------------------
+// ---- all-gather of per-rank column blocks of [B, row_bytes] byte matrices -------------------
+// Up to two matrices (e.g. int8 codes and their (scale, sum) pairs) in one launch and one barrier.
 // Rank `me` owns bytes [col0, col0 + ncols) of every row (in both the source and destination
 // layout); it copies them from its local source into the same position of every rank's buffer.
-__global__ void k_p2p_allgather_cols(Peers P, const uint8_t* __restrict__ src, int64_t src_ld, int64_t dst_off,
-                                     int64_t dst_ld, int64_t col0, int64_t ncols, int B, int64_t flags_off, int site,
+struct AgSeg {
+  const uint8_t* src;
+  int64_t src_ld, dst_off, dst_ld, col0, ncols;
+};
+
+__global__ void k_p2p_allgather_cols(Peers P, AgSeg s0, AgSeg s1, int nseg, int B, int64_t flags_off, int site,
                                      int me, int W, uint32_t* counters, int* err) {
   pdl_wait();
-  const int64_t chunks = ncols >> 4;  // 16-byte chunks per row
-  const int64_t total = (int64_t)B * chunks;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t b = i / chunks, c = i - b * chunks;
-    const uint4 v = *reinterpret_cast<const uint4*>(src + b * src_ld + col0 + 16 * c);
-    for (int r = 0; r < W; r++)
-      *reinterpret_cast<uint4*>(P.base[r] + dst_off + b * dst_ld + col0 + 16 * c) = v;
+  for (int k = 0; k < nseg; k++) {
+    const AgSeg& g = k == 0 ? s0 : s1;
+    const int64_t chunks = g.ncols >> 4;  // 16-byte chunks per row
+    const int64_t total = (int64_t)B * chunks;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t b = i / chunks, c = i - b * chunks;
+      const uint4 v = *reinterpret_cast<const uint4*>(g.src + b * g.src_ld + g.col0 + 16 * c);
+      for (int r = 0; r < W; r++)
+        *reinterpret_cast<uint4*>(P.base[r] + g.dst_off + b * g.dst_ld + g.col0 + 16 * c) = v;
+    }
   }
   rank_barrier(P, flags_off, site, blockIdx.x, me, W, counters, err);
   pdl_launch_dependents();
@@ -188,19 +196,31 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaLaunchAttribute* attr) {
 
 // peers: int64 [W] host tensor of symmetric buffer bases; counters: int32 [n_sites*64] local
 // device tensor (zero-initialised once); err: int32 [1] device.
+// Segments: one or two (src, src_ld, dst_off, dst_ld, col0, ncols) column blocks gathered in one launch.
 void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
                         int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
-                        torch::Tensor counters, torch::Tensor err, int64_t ctas) {
+                        torch::Tensor counters, torch::Tensor err, int64_t ctas, c10::optional<torch::Tensor> src2,
+                        int64_t src2_ld, int64_t dst2_off, int64_t dst2_ld, int64_t col2, int64_t ncols2) {
   const int W = (int)peers.numel();
-  TORCH_CHECK(ncols % 16 == 0 && col0 % 16 == 0 && src_ld % 16 == 0 && dst_ld % 16 == 0 && dst_off % 16 == 0,
-              "allgather: 16-byte granularity");
+  auto check = [](int64_t n, int64_t c, int64_t sl, int64_t dl, int64_t off) {
+    TORCH_CHECK(n % 16 == 0 && c % 16 == 0 && sl % 16 == 0 && dl % 16 == 0 && off % 16 == 0,
+                "allgather: 16-byte granularity");
+  };
+  check(ncols, col0, src_ld, dst_ld, dst_off);
   TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allgather: 1..64 CTAs");
+  AgSeg s0{(const uint8_t*)src.data_ptr(), src_ld, dst_off, dst_ld, col0, ncols};
+  AgSeg s1 = s0;
+  int nseg = 1;
+  if (src2.has_value()) {
+    check(ncols2, col2, src2_ld, dst2_ld, dst2_off);
+    s1 = AgSeg{(const uint8_t*)src2->data_ptr(), src2_ld, dst2_off, dst2_ld, col2, ncols2};
+    nseg = 2;
+  }
   Peers P = make_peers(peers);
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
-  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_allgather_cols, P, (const uint8_t*)src.data_ptr(), src_ld, dst_off,
-                                    dst_ld, col0, ncols, (int)B, flags_off, (int)site, (int)me, W,
-                                    (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>()));
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_allgather_cols, P, s0, s1, nseg, (int)B, flags_off, (int)site,
+                                    (int)me, W, (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>()));
 }
 
 void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, int64_t n, int64_t flags_off,

@@ -291,12 +291,77 @@ FAK_DEV void epilogue(int tile, const float (&v)[4], int tokb, int lane, int N, 
   }
 }
 
+// Tensor-parallel all-reduce fused into the epilogue (K-split row-parallel layers such as the
+// down projection): the warp that finishes a tile pushes its partial into slot [me][tile] of every
+// rank's symmetric buffer with plain stores, publishes a per-tile epoch flag on every rank (release,
+// system scope), waits (acquire, bounded) for all ranks' flags of that tile, and sums the W slots of
+// its own buffer in rank order -- every rank computes bit-identical values -- before the residual
+// add.  Epochs count launches per tile in local memory, so the kernel replays inside CUDA graphs.
+// No multicast, no TMA from peer memory: peer memory is touched by ordinary stores only.
+constexpr int AR_MAX_W = 8;
+constexpr uint32_t kArSpinLimit = 1u << 24;
+struct ArPeers {
+  uint8_t* base[AR_MAX_W];  // symmetric buffer base of every rank (W = 0: no all-reduce)
+  int W, me;
+  int64_t parts_off, flags_off;
+  uint32_t* epochs;         // local [T]
+};
+
+FAK_DEV void ar_st_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+FAK_DEV uint32_t ar_ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int NT>
+FAK_DEV void ar_tile(const ArPeers& ar, int T, int tile, int lane, float (&v)[NT][4], int* err) {
+  // push this rank's partial of the tile to every rank
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    const float4 val = make_float4(v[nt][0], v[nt][1], v[nt][2], v[nt][3]);
+    const int64_t slot = (((int64_t)ar.me * T + tile) * NT + nt) * 32 + lane;
+    for (int r = 0; r < ar.W; r++) reinterpret_cast<float4*>(ar.base[r] + ar.parts_off)[slot] = val;
+  }
+  __syncwarp();
+  uint32_t ep = 0;
+  if (lane == 0) ep = ar.epochs[tile] + 1;
+  ep = __shfl_sync(0xffffffffu, ep, 0);
+  if (lane < ar.W) {
+    __threadfence_system();
+    ar_st_release(reinterpret_cast<uint32_t*>(ar.base[lane] + ar.flags_off) + (int64_t)tile * AR_MAX_W + ar.me, ep);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(ar.base[ar.me] + ar.flags_off) +
+                           (int64_t)tile * AR_MAX_W + lane;
+    uint32_t i = 0;
+    while (ar_ld_acquire(mine) < ep) {
+      if (++i > kArSpinLimit) {
+        report_error(err, 2);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < ar.W; r++) {
+      const int64_t slot = (((int64_t)r * T + tile) * NT + nt) * 32 + lane;
+      const float4 p = __ldcg(reinterpret_cast<const float4*>(ar.base[ar.me] + ar.parts_off) + slot);
+      s[0] += p.x; s[1] += p.y; s[2] += p.z; s[3] += p.w;
+    }
+    v[nt][0] = s[0]; v[nt][1] = s[1]; v[nt][2] = s[2]; v[nt][3] = s[3];
+  }
+  if (lane == 0) ar.epochs[tile] = ep;
+}
+
 template <int QT, int W, int R, int NT>
 __global__ void __launch_bounds__(W * 32, 1)
 k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
         const float* __restrict__ xf, int64_t ldx, const float* __restrict__ gamma, float eps,
         int B, float* __restrict__ y, int64_t ldy, const float* __restrict__ bias, int epi,
-        float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo) {
+        float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo, ArPeers ar) {
   constexpr int UT = Tile<QT>::UT;
   constexpr int TABF = Tile<QT>::TABF;
   constexpr int MB = 8 * NT;  // token rows staged
@@ -457,10 +522,8 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
     }
     if (++ul < nu) continue;
     ul = 0;
-    if (geo.S == 1) {
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) epilogue(tile, acc[nt], 8 * nt, lane, N, B, y, ldy, bias, epi);
-    } else {
+    bool have = true;  // this warp holds the tile's final (rank-local) value in acc
+    if (geo.S > 1) {
       // partials [slice][tile][n8 tile][lane] float4
       float4* mine = reinterpret_cast<float4*>(part + ((size_t)slice * geo.T + tile) * 128 * NT) + lane;
 #pragma unroll
@@ -470,7 +533,8 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       int old = 0;
       if (lane == 0) old = atomicAdd(&cnt[tile], 1);
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == geo.S - 1) {  // last slice of this tile: reduce in slice order
+      have = old == geo.S - 1;
+      if (have) {  // last slice of this tile: reduce in slice order
         __threadfence();
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
@@ -480,10 +544,15 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
                 __ldcg(reinterpret_cast<const float4*>(part + ((size_t)s * geo.T + tile) * 128 * NT) + 32 * nt + lane);
             v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
           }
-          epilogue(tile, v, 8 * nt, lane, N, B, y, ldy, bias, epi);
+          acc[nt][0] = v[0]; acc[nt][1] = v[1]; acc[nt][2] = v[2]; acc[nt][3] = v[3];
         }
         if (lane == 0) cnt[tile] = 0;  // ready for the next launch
       }
+    }
+    if (have) {
+      if (ar.W > 0) ar_tile<NT>(ar, geo.T, tile, lane, acc, err);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) epilogue(tile, acc[nt], 8 * nt, lane, N, B, y, ldy, bias, epi);
     }
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
@@ -579,8 +648,23 @@ std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_
 void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<torch::Tensor> qx,
            c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
-           torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags) {
+           torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
+           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "tgemv: w cuda uint8");
+  ArPeers ar{};
+  if (ar_peers.has_value()) {  // fused all-reduce over the ranks' symmetric buffers, then residual add
+    auto h = ar_peers->cpu();
+    TORCH_CHECK(h.scalar_type() == torch::kInt64 && h.numel() >= 1 && h.numel() <= AR_MAX_W, "tgemv: peers");
+    TORCH_CHECK(ar_epochs.has_value() && ar_epochs->scalar_type() == torch::kInt32 &&
+                    ar_epochs->numel() >= (N + 15) / 16, "tgemv: all-reduce epochs [tiles] int32");
+    TORCH_CHECK(epi == EPI_ADD && ar_parts_off % 16 == 0 && ar_flags_off % 4 == 0, "tgemv: all-reduce layout");
+    ar.W = (int)h.numel();
+    ar.me = (int)ar_me;
+    for (int r = 0; r < ar.W; r++) ar.base[r] = reinterpret_cast<uint8_t*>(h.data_ptr<int64_t>()[r]);
+    ar.parts_off = ar_parts_off;
+    ar.flags_off = ar_flags_off;
+    ar.epochs = reinterpret_cast<uint32_t*>(ar_epochs->data_ptr<int>());
+  }
   TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "tgemv: qtype");
   TORCH_CHECK(K % 64 == 0 && (qtype == QT_Q8_0 || K % 256 == 0), "tgemv: K must be a multiple of 256 (64 for Q8_0)");
   const int64_t T = (N + 15) / 16, U = (K + 255) / 256;
@@ -647,6 +731,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   // the batch runs as launches of up to 8 * p.NT tokens (one launch unless the wide staging did
   // not fit); each token's arithmetic is the same in every launch shape
   const int chunk = 8 * p.NT;
+  TORCH_CHECK(ar.W == 0 || B <= chunk, "tgemv: the fused all-reduce takes one launch of at most ", chunk, " tokens");
   auto go = [&](auto kern) {
     FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem));
     for (int64_t b0 = 0; b0 < B; b0 += chunk) {
@@ -656,7 +741,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
                                         xp ? xp + b0 * ldx : nullptr, ldx, gp, (float)eps, nb,
                                         y.data_ptr<float>() + b0 * y.stride(0), (int64_t)y.stride(0), bp, (int)epi,
                                         p.geo.S > 1 ? part.data_ptr<float>() : nullptr,
-                                        p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo));
+                                        p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo, ar));
     }
   };
 #define FAK_TG_NT(QTV, NTV)                                              \

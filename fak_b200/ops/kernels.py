@@ -76,11 +76,12 @@ def tgemv_workspace(device, weights=()) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None, epi: int = EPI_STORE,
-         flags: int = 0) -> None:
+         flags: int = 0, ar: tuple | None = None) -> None:
     """y[:B] (op)= W . x for a decode batch (w: models.weights.QuantWeight); chunks of 8 tokens.
 
     Matrices with a tile-packed copy (``QuantWeight.pack``) run the tile-packed tensor-core GEMV;
-    others the row-major kernels."""
+    others the row-major kernels.  ``ar`` = (peer bases, rank, parts offset, flags offset, epochs)
+    fuses a tensor-parallel all-reduce of the result into the GEMV (EPI_ADD, one launch, B <= 32)."""
     C = ext()
     if w.tp is not None:
         part, cnt = tgemv_workspace(w.tp.device)
@@ -94,12 +95,16 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
             part, cnt = tgemv_workspace(w.tp.device, (w,))
         for b0 in range(0, B, TGEMV_MAX_B):
             nb = min(TGEMV_MAX_B, B - b0)
+            if ar is not None and B > TGEMV_MAX_B:
+                raise ValueError("the fused all-reduce GEMV takes at most 32 tokens")
+            arkw = {} if ar is None else dict(ar_peers=ar[0], ar_me=ar[1], ar_parts_off=ar[2], ar_flags_off=ar[3],
+                                              ar_epochs=ar[4])
             if isinstance(act, FAct):
                 C.tgemv(w.tp, w.qtype, w.rows, w.cols, None, None, act.x[b0:b0 + nb], act.gamma, act.eps, nb,
-                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags)
+                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags, **arkw)
             else:
                 C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q[b0:b0 + nb], act.ds[b0:b0 + nb], None, None, 0.0, nb,
-                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags)
+                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags, **arkw)
             count()
         return
     if isinstance(act, FAct):

@@ -10,8 +10,11 @@ each rank's buffer mapped into every peer's address space over NVLink/NVSwitch) 
 
 Per decode layer the attention kernel writes its heads' quantized output straight into this
 rank's ``act`` columns, one all-gather kernel pushes those columns into every peer's ``act``,
-the o_proj GEMV reads the full ``act`` locally; the down GEMV writes its partial into ``parts``
-and one all-reduce kernel sums the W partials (peer loads, rank order) into the residual.
+the o_proj GEMV reads the full ``act`` locally; the down-projection GEMV all-reduces in its own
+epilogue: the warp that finishes a 16-row tile pushes the tile's partial to every rank, waits
+for the other ranks' partials of that tile and adds their rank-order sum to the residual (one
+kernel, the transfer of each tile overlapping the GEMV of the others).  Batches above 32 tokens
+fall back to the GEMV + all-reduce kernel pair.
 Greedy decoding ends with a distributed argmax instead of gathering 152k logits.  Prefill keeps
 the NCCL collectives of ``NcclTP`` (large messages, bandwidth-bound).
 """
@@ -62,6 +65,12 @@ class P2PTP(NcclTP):
         off = _align(off + L * B * d * 4)
         self.cand_off = off
         off = _align(off + B * MAX_W * 8)
+        # fused down-projection all-reduce: per-tile partial slots [src][tile][<=32 tokens] and flags
+        self.ar_tiles = (d + 15) // 16
+        self.arparts_off = off
+        off = _align(off + MAX_W * self.ar_tiles * 4 * 128 * 4)
+        self.arflags_off = off
+        off = _align(off + self.ar_tiles * MAX_W * 4)
         self.nbytes = off
         self.buf = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=device)
         self.buf.zero_()
@@ -69,6 +78,7 @@ class P2PTP(NcclTP):
         self.peers = torch.tensor(list(self.hdl.buffer_ptrs), dtype=torch.int64)
         self.me = self.hdl.rank
         self.counters = torch.zeros(self.n_sites * MAX_CTAS, dtype=torch.int32, device=device)
+        self.ar_epochs = torch.zeros(self.ar_tiles, dtype=torch.int32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
@@ -96,16 +106,22 @@ class P2PTP(NcclTP):
         C, kv, D, H = ext(), rn.kv, self.D, self.cfg.n_heads
         K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_mine, workspace=rn.attn_ws,
                            tickets=rn.attn_tickets, ldo=H * D)
+        # codes and (scale, sum) pairs of this rank's heads, pushed to every rank in one launch
         C.p2p_allgather_cols(self.peers, self.buf[self.q_off:], H * D, self.q_off, H * D, self.h0 * D, self.nh * D,
-                             B, self.flags_off, 3 * i, self.me, self.counters, self.err, AG_CTAS)
-        C.p2p_allgather_cols(self.peers, self.buf[self.ds_off:], H * D // 4, self.ds_off, H * D // 4,
-                             self.h0 * D // 4, self.nh * D // 4, B, self.flags_off, 3 * i + 1, self.me, self.counters,
-                             self.err, AG_CTAS)
-        K.count(2)
+                             B, self.flags_off, 3 * i, self.me, self.counters, self.err, AG_CTAS,
+                             self.buf[self.ds_off:], H * D // 4, self.ds_off, H * D // 4, self.h0 * D // 4,
+                             self.nh * D // 4)
+        K.count(1)
         K.gemv(rn.w.layers[i].o, self.act_full, B, rn.x[:B], None, K.EPI_ADD)
 
     def decode_down(self, rn, i: int, B: int) -> None:
         d = self.cfg.d_model
+        w = rn.w.layers[i].down
+        if w.tp is not None and B <= K.TGEMV_MAX_B:
+            # one kernel: local K-split GEMV, per-tile push to every rank, rank-order sum, residual add
+            K.gemv(w, rn.ffn_in, B, rn.x[:B], None, K.EPI_ADD,
+                   ar=(self.peers, self.me, self.arparts_off, self.arflags_off, self.ar_epochs))
+            return
         part_off = self.parts_off + i * self.B * d * 4
         part = self.buf[part_off:part_off + B * d * 4].view(torch.float32).view(B, d)
         K.gemv(rn.w.layers[i].down, rn.ffn_in, B, part, None, K.EPI_STORE)
