@@ -8,10 +8,14 @@
 //              K=16 per instruction, 4 per k-block) and tcgen05.commit frees each stage;
 //   warps 2-5  epilogue: tcgen05.ld the fp32 accumulator (warp w reads TMEM lanes
 //              32*(w%4)..+31 = tile rows), fused bias / residual add / SwiGLU, global store.
-// No TMA multicast is used, so the kernel is safe on multi-GPU runs.
+// No TMA multicast is used, so the kernel is safe on multi-GPU runs.  The persistent variant
+// (default) keeps two TMEM accumulators so each CTA's epilogue overlaps its next tile's MMAs.
 #include <torch/extension.h>
 #include <c10/cuda/CUDAStream.h>
 #include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <type_traits>
 
 #include "tc.cuh"
 
@@ -154,6 +158,172 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   }
 }
 
+// ---- persistent variant -----------------------------------------------------------------------
+// One CTA per SM walks output tiles t = blockIdx.x, + gridDim.x, ... (m fastest, so the CTAs of a
+// wave share weight column blocks through L2).  TMEM holds TWO 128 x BN fp32 accumulators (all 512
+// columns at BN = 256): the MMA thread fills one while the epilogue warps drain the other, so the
+// epilogue of tile i runs under the MMAs of tile i+1.  The producer streams k-blocks of successive
+// tiles through the same smem ring without draining it between tiles.
+template <int BN, int STAGES>
+struct GemmSmemP {
+  alignas(1024) __nv_bfloat16 a[STAGES][BM * BK];
+  alignas(1024) __nv_bfloat16 b[STAGES][BN * BK];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+template <typename OutT>
+FAK_DEV void store16(OutT* p, const float (&v)[16], bool add, int n_valid);
+template <>
+FAK_DEV void store16<float>(float* p, const float (&v)[16], bool add, int n_valid) {
+  if (n_valid == 16 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      if (add) {
+        const float4 c = reinterpret_cast<const float4*>(p)[q];
+        o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+      }
+      reinterpret_cast<float4*>(p)[q] = o;
+    }
+    return;
+  }
+  for (int j = 0; j < n_valid; j++) p[j] = add ? p[j] + v[j] : v[j];
+}
+template <>
+FAK_DEV void store16<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[16], bool add, int n_valid) {
+  for (int j = 0; j < n_valid; j++) p[j] = __float2bfloat16_rn(add ? __bfloat162float(p[j]) + v[j] : v[j]);
+}
+
+template <int BN, int STAGES, typename OutT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       int M, int N, int K, OutT* __restrict__ out, int64_t ldo, const float* __restrict__ bias,
+                       int epi, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  GemmSmemP<BN, STAGES>& sm = *reinterpret_cast<GemmSmemP<BN, STAGES>*>(base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = (K + BK - 1) / BK;
+  const int n_m = (M + BM - 1) / BM, n_n = (N + BN - 1) / BN;
+  const int n_tiles = n_m * n_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      tc::mbar_init(&sm.full[s], 1);
+      tc::mbar_init(&sm.empty[s], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      tc::mbar_init(&sm.acc_full[i], 1);
+      tc::mbar_init(&sm.acc_empty[i], 4);  // one arrival per epilogue warp
+    }
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmap_a);
+    tc::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sm.tmem_base, 2 * BN);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;  // k-blocks issued across tiles
+      for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+        const int m0 = (t % n_m) * BM, n0 = (t / n_m) * BN;
+        for (int kb = 0; kb < nkb; kb++, g++) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          tc::mbar_wait(&sm.empty[s], ph ^ 1, err);
+          tc::mbar_arrive_expect_tx(&sm.full[s], (BM + BN) * BK * 2);
+          tc::tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * BK, m0);
+          tc::tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * BK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(BM, BN);
+      int g = 0, i = 0;
+      for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, i++) {
+        const int buf = i & 1, use = i >> 1;
+        tc::mbar_wait(&sm.acc_empty[buf], (uint32_t)((use & 1) ^ 1), err);  // epilogue drained this buffer
+        tc::tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < nkb; kb++, g++) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          tc::mbar_wait(&sm.full[s], ph, err);
+          tc::tc_fence_after();
+          const uint64_t ad = tc::smem_desc_sw128(sm.a[s]);
+          const uint64_t bd = tc::smem_desc_sw128(sm.b[s]);
+#pragma unroll
+          for (int k = 0; k < BK / 16; k++) tc::mma_bf16(acc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          tc::mma_commit(&sm.empty[s]);
+        }
+        tc::mma_commit(&sm.acc_full[buf]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, i++) {
+      const int buf = i & 1, use = i >> 1;
+      const int m0 = (t % n_m) * BM, n0 = (t / n_m) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      tc::mbar_wait(&sm.acc_full[buf], (uint32_t)(use & 1), err);
+      tc::tc_fence_after();
+      const uint32_t lane_addr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tc::tmem_ld16(lane_addr + c, r);
+        tc::tmem_ld_wait();
+        const int col0 = n0 + c;
+        if (row >= M || col0 >= N) continue;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]) + ((bias && col0 + j < N) ? bias[col0 + j] : 0.f);
+        if (epi == G_SWIGLU) {
+          // columns [col0, col0+8) gate rows of outputs col0/2 + j, [col0+8, col0+16) the up rows
+          float o[16];
+#pragma unroll
+          for (int j = 0; j < 8; j++) o[j] = silu(v[j]) * v[j + 8];
+          OutT* p = out + (int64_t)row * ldo + (col0 >> 1);
+          if (col0 + 16 <= N && std::is_same<OutT, float>::value && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+            float* pf = reinterpret_cast<float*>(p);
+            reinterpret_cast<float4*>(pf)[0] = make_float4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<float4*>(pf)[1] = make_float4(o[4], o[5], o[6], o[7]);
+          } else {
+            for (int j = 0; j < 8; j++)
+              if (col0 + j + 8 < N) store_val(p + j, o[j]);
+          }
+        } else {
+          store16<OutT>(out + (int64_t)row * ldo + col0, v, epi == G_ADD, min(16, N - col0));
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&sm.acc_empty[buf]);
+    }
+  }
+  pdl_launch_dependents();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
 // ---- host: tensor maps through the driver entry point (no link-time libcuda dependency) ----
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -182,15 +352,18 @@ CUtensorMap make_map_bf16_kmajor(const void* ptr, int64_t rows, int64_t cols, in
 
 template <int BN, int STAGES, typename OutT>
 void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* bias, int epi,
-                 int* err) {
+                 int* err, bool persistent) {
   const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
   CUtensorMap ma = make_map_bf16_kmajor(a.data_ptr(), M, K, a.stride(0), BM);
   CUtensorMap mb = make_map_bf16_kmajor(b.data_ptr(), N, K, b.stride(0), BN);
-  size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
-  auto kern = k_gemm_bf16<BN, STAGES, OutT>;
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  static int n_sm = 0;
+  if (!n_sm) FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, a.get_device()));
+  size_t smem = persistent ? sizeof(GemmSmemP<BN, STAGES>) + 1024 : sizeof(GemmSmem<BN, STAGES>) + 1024;
+  auto kern = persistent ? k_gemm_bf16_persistent<BN, STAGES, OutT> : k_gemm_bf16<BN, STAGES, OutT>;
   FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((M + BM - 1) / BM, (N + BN - 1) / BN);
+  cfg.gridDim = persistent ? dim3((unsigned)std::min(tiles, n_sm)) : dim3((M + BM - 1) / BM, (N + BN - 1) / BN);
   cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = at::cuda::getCurrentCUDAStream();
@@ -226,10 +399,15 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
     bp = bias->data_ptr<float>();
   }
   int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
+  // persistent double-buffered-TMEM kernel by default; FAK_GEMM_PERSISTENT=0 selects one tile per CTA
+  static const bool persistent = []() {
+    const char* e = std::getenv("FAK_GEMM_PERSISTENT");
+    return !(e && e[0] == '0');
+  }();
   if (out.scalar_type() == torch::kFloat32)
-    launch_gemm<256, 4, float>(a, b, out, bp, (int)epi, ep);
+    launch_gemm<256, 4, float>(a, b, out, bp, (int)epi, ep, persistent);
   else if (out.scalar_type() == torch::kBFloat16)
-    launch_gemm<256, 4, __nv_bfloat16>(a, b, out, bp, (int)epi, ep);
+    launch_gemm<256, 4, __nv_bfloat16>(a, b, out, bp, (int)epi, ep, persistent);
   else
     TORCH_CHECK(false, "out must be float32 or bfloat16");
 }

@@ -561,6 +561,137 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   pdl_launch_dependents();
 }
 
+// ---- grouped expert GEMV (MoE decode) ------------------------------------------------------
+// The experts of a layer are stacked row-wise and tile-packed (expert e owns tiles
+// [e * Te, (e + 1) * Te)).  A CTA takes one chunk of <= 8 (token, expert) pairs of one expert
+// (from the deterministic grouping kernel), gathers their activation rows once, and its warps stream
+// every tile of that expert through their private rings (whole K: no split).  Outputs go to the
+// pair's row of y: SwiGLU over 8-row interleaved gate/up rows for gate/up, plain store for down.
+template <int QT, int W, int R>
+__global__ void __launch_bounds__(W * 32, 1)
+k_tgemv_moe(const uint8_t* __restrict__ Wt, int Te, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
+            int topk, int act_by_token, const int* __restrict__ chunk_expert, const int* __restrict__ chunk_pairs,
+            const int* __restrict__ n_chunks, float* __restrict__ y, int64_t ldy, int epi, int* __restrict__ err,
+            TGeo geo) {
+  constexpr int UT = Tile<QT>::UT;
+  constexpr int TABF = Tile<QT>::TABF;
+  constexpr int MB = 8;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const TSmem L = tsmem(QT, W, R, 1, geo);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunk = blockIdx.x;
+  pdl_wait();
+  if (chunk >= n_chunks[0]) return;
+  const int e = chunk_expert[chunk];
+  int pr[MB];
+#pragma unroll
+  for (int s = 0; s < MB; s++) pr[s] = chunk_pairs[chunk * MB + s];
+  const int nu = geo.U, kb = K;
+  int8_t* xs = reinterpret_cast<int8_t*>(sm + L.xs);
+  float2* dsr = reinterpret_cast<float2*>(sm + L.dsr);
+  float2* dsT = reinterpret_cast<float2*>(sm + L.dsT);
+  int* czT = reinterpret_cast<int*>(sm + L.czT);
+  float* tab = reinterpret_cast<float*>(sm + L.tab) + warp * TABF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
+  uint64_t* bar = bars + warp * R;
+  uint64_t* act_bar = bars + W * R;
+  uint8_t* ring = sm + L.ring + (size_t)warp * R * UT;
+  const int n_my = warp < Te ? (Te - 1 - warp) / W + 1 : 0;
+  const int Q = n_my * nu;
+  if (lane == 0) {
+    for (int i = 0; i < R; i++) tc::mbar_init(&bar[i], 1);
+    if (warp == 0) tc::mbar_init(act_bar, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  int pq = 0, pslot = 0, pu = 0;
+  const uint8_t* psrc = Wt + ((int64_t)e * Te + warp) * nu * UT;
+  const int64_t next_tile = ((int64_t)W * nu - nu) * UT;
+  auto issue_next = [&]() {
+    if (pq >= Q) return;
+    tc::mbar_arrive_expect_tx(&bar[pslot], UT);
+    bulk_g2s(ring + pslot * UT, psrc, UT, &bar[pslot]);
+    pq++;
+    pslot = pslot + 1 == R ? 0 : pslot + 1;
+    psrc += UT;
+    if (++pu == nu) {
+      pu = 0;
+      psrc += next_tile;
+    }
+  };
+  if (lane == 0)
+    for (int i = 0; i < R - 1; i++) issue_next();
+  if (threadIdx.x == 0) {
+    uint32_t nv = 0;
+    for (int s = 0; s < MB; s++) nv += pr[s] >= 0;
+    tc::mbar_arrive_expect_tx(act_bar, nv * ((uint32_t)K + (uint32_t)K / 4));
+    for (int s = 0; s < MB; s++) {
+      if (pr[s] < 0) continue;
+      const int64_t row = act_by_token ? pr[s] / topk : pr[s];
+      bulk_g2s(xs + s * geo.xstride, qx + row * K, (uint32_t)K, act_bar);
+      bulk_g2s(dsr + s * geo.dstride, ds + row * (K / 32), (uint32_t)(K / 4), act_bar);
+    }
+  }
+  for (int i = threadIdx.x; i < MB * (nu * 256 / 16); i += W * 32) {
+    const int b = i / (nu * 16), c = (i % (nu * 16)) * 16;
+    if (pr[b] < 0 || c >= kb) *reinterpret_cast<uint4*>(xs + b * geo.xstride + c) = make_uint4(0, 0, 0, 0);
+  }
+  tc::mbar_wait(act_bar, 0, err);
+  for (int i = threadIdx.x; i < nu * 8 * MB; i += W * 32) {
+    const int blk = i / MB, b = i % MB;
+    dsT[i] = (pr[b] >= 0 && blk * 32 < kb) ? dsr[b * geo.dstride + blk] : make_float2(0.f, 0.f);
+  }
+  if constexpr (QT == QT_Q6_K) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < nu * 16 * MB; i += W * 32) {
+      const int k16 = i / MB, b = i % MB;
+      const int4 v = *reinterpret_cast<const int4*>(xs + b * geo.xstride + 16 * k16);
+      int sm4 = __dp4a(v.x, 0x01010101, 0);
+      sm4 = __dp4a(v.y, 0x01010101, sm4);
+      sm4 = __dp4a(v.z, 0x01010101, sm4);
+      sm4 = __dp4a(v.w, 0x01010101, sm4);
+      czT[i] = MAGIC_I - 32 * sm4;
+    }
+  }
+  __syncthreads();
+  float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+  const int g = lane >> 2, t = lane & 3;
+  const int8_t* xg = xs + g * geo.xstride;
+  int cslot = 0, ul = 0, tile = warp;
+  uint32_t phase = 0;
+  for (int q = 0; q < Q; q++) {
+    if (lane == 0) issue_next();
+    tc::mbar_wait(&bar[cslot], phase, err);
+    unit_tile<QT, 1>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
+                     QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
+    if (++cslot == R) {
+      cslot = 0;
+      phase ^= 1u;
+    }
+    if (++ul < nu) continue;
+    ul = 0;
+    const int r0 = tile * 16;
+    const int p0 = pr[2 * t], p1 = pr[2 * t + 1];
+    if (epi == EPI_SWIGLU) {
+      const int o = (r0 >> 1) + g;
+      if (p0 >= 0) y[(int64_t)p0 * ldy + o] = silu(acc[0][0]) * acc[0][2];
+      if (p1 >= 0) y[(int64_t)p1 * ldy + o] = silu(acc[0][1]) * acc[0][3];
+    } else {
+      if (p0 >= 0) {
+        y[(int64_t)p0 * ldy + r0 + g] = acc[0][0];
+        y[(int64_t)p0 * ldy + r0 + g + 8] = acc[0][2];
+      }
+      if (p1 >= 0) {
+        y[(int64_t)p1 * ldy + r0 + g] = acc[0][1];
+        y[(int64_t)p1 * ldy + r0 + g + 8] = acc[0][3];
+      }
+    }
+    acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
+    tile += W;
+  }
+  pdl_launch_dependents();
+}
+
 struct Plan {
   int W, R, NT;
   TGeo geo;
@@ -762,4 +893,57 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   else FAK_TG(QT_Q8_0)
 #undef FAK_TG
 #undef FAK_TG_NT
+}
+
+// Grouped expert GEMV over tile-packed experts (MoE decode).  w: tile-packed [E_local * rows_per_expert
+// rows, K]; pairs grouped by moe_group (chunk_expert [max_chunks], chunk_pairs [max_chunks, 8], n_chunks [1]).
+void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, torch::Tensor qx,
+               torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
+               torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err) {
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "moe_tgemv: w");
+  TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "moe_tgemv: qtype");
+  TORCH_CHECK(rows_per_expert % 16 == 0 && K % 256 == 0, "moe_tgemv: rows per expert % 16, K % 256");
+  TORCH_CHECK(qx.scalar_type() == torch::kInt8 && qx.is_contiguous() &&
+                  reinterpret_cast<uintptr_t>(qx.data_ptr()) % 16 == 0, "moe_tgemv: qx");
+  TORCH_CHECK(ds.scalar_type() == torch::kFloat32 && ds.is_contiguous() &&
+                  reinterpret_cast<uintptr_t>(ds.data_ptr()) % 16 == 0, "moe_tgemv: ds");
+  TORCH_CHECK(y.scalar_type() == torch::kFloat32 && y.stride(1) == 1, "moe_tgemv: y");
+  TORCH_CHECK(chunk_pairs.numel() >= max_chunks * 8 && chunk_expert.numel() >= max_chunks, "moe_tgemv: chunks");
+  static int max_smem = 0;
+  if (!max_smem)
+    FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, w.get_device()));
+  TGeo g = make_geo((int)qtype, (int)(rows_per_expert / 16), (int)(K / 256), 1, 1);
+  const int Te = (int)(rows_per_expert / 16);
+  int W = 16, R = 3;
+  if (tsmem((int)qtype, 16, 3, 1, g).total > max_smem) W = 8;
+  TORCH_CHECK(tsmem((int)qtype, W, R, 1, g).total <= max_smem, "moe_tgemv: K too large for shared memory");
+  const int smem = tsmem((int)qtype, W, R, 1, g).total;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(W * 32);
+  cfg.gridDim = dim3((unsigned)max_chunks);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto go = [&](auto kern) {
+    FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.data_ptr<uint8_t>(), Te, (int)K,
+                                      (const int8_t*)qx.data_ptr<int8_t>(),
+                                      reinterpret_cast<const float2*>(ds.data_ptr<float>()), (int)topk,
+                                      (int)act_by_token, (const int*)chunk_expert.data_ptr<int>(),
+                                      (const int*)chunk_pairs.data_ptr<int>(), (const int*)n_chunks.data_ptr<int>(),
+                                      y.data_ptr<float>(), (int64_t)y.stride(0), (int)epi, err.data_ptr<int>(), g));
+  };
+#define FAK_TGM(QTV)                                       \
+  {                                                        \
+    if (W == 16) go(k_tgemv_moe<QTV, 16, 3>);              \
+    else go(k_tgemv_moe<QTV, 8, 3>);                       \
+  }
+  if (qtype == QT_Q4_K) FAK_TGM(QT_Q4_K)
+  else if (qtype == QT_Q6_K) FAK_TGM(QT_Q6_K)
+  else FAK_TGM(QT_Q8_0)
+#undef FAK_TGM
 }

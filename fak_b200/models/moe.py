@@ -57,11 +57,19 @@ def _grouped_ffn(rn, L, st: MoEState, n_tok: int, act) -> None:
     P = n_tok * st.k
     C.moe_group(st.ids[:n_tok], P, st.e0, st.E_local, st.max_chunks, st.chunk_expert, st.chunk_pairs, st.n_chunks)
     gu, dn = L.experts_gate_up, L.experts_down
-    C.moe_qmmv(gu.buf, gu.qtype, gu.rows // st.E_local, gu.cols, gu.pitch, act.q, act.ds, st.k, True,
-               st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.h, 2, st.err)
-    K.quant_act(st.h[:P], st.act_h)
-    C.moe_qmmv(dn.buf, dn.qtype, dn.rows // st.E_local, dn.cols, dn.pitch, st.act_h.q, st.act_h.ds, st.k, False,
-               st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.out, 0, st.err)
+    if gu.tp is not None and dn.tp is not None:
+        # tile-packed experts: one CTA per chunk streams its expert's tiles through per-warp rings
+        C.moe_tgemv(gu.tp, gu.qtype, gu.rows // st.E_local, gu.cols, act.q, act.ds, st.k, True,
+                    st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.h, 2, st.err)
+        K.quant_act(st.h[:P], st.act_h)
+        C.moe_tgemv(dn.tp, dn.qtype, dn.rows // st.E_local, dn.cols, st.act_h.q, st.act_h.ds, st.k, False,
+                    st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.out, 0, st.err)
+    else:
+        C.moe_qmmv(gu.buf, gu.qtype, gu.rows // st.E_local, gu.cols, gu.pitch, act.q, act.ds, st.k, True,
+                   st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.h, 2, st.err)
+        K.quant_act(st.h[:P], st.act_h)
+        C.moe_qmmv(dn.buf, dn.qtype, dn.rows // st.E_local, dn.cols, dn.pitch, st.act_h.q, st.act_h.ds, st.k,
+                   False, st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.out, 0, st.err)
     K.count(3)
 
 

@@ -385,3 +385,6 @@ def _load_moe_layer(cfg, get, quant, p, L: LayerWeights, device, expert_filter) 
     L.experts_gate_up = QuantWeight.from_rows(gu, gt, d, device)
     L.experts_down = QuantWeight.from_rows(draw[e0:e1].reshape((e1 - e0) * d, -1).contiguous(), dt, f, device)
     L.expert_ids = list(range(e0, e1))
+    if f % 256 == 0 and d % 256 == 0:  # tile-packed copies for the grouped expert GEMV
+        L.experts_gate_up.pack()
+        L.experts_down.pack()

@@ -222,7 +222,8 @@ def test_argmax_first_index():
     assert out[1].item() == 7
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 256, 128), (200, 512, 576), (1280, 4608, 3584), (77, 240, 1536)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 256, 128), (200, 512, 576), (1280, 4608, 3584), (77, 240, 1536),
+                                   (1024, 16384, 256)])
 @pytest.mark.parametrize("epi", [0, 1, 2])
 def test_gemm_tcgen05(M, N, K, epi):
     from fak_b200.ops import kernels as Kn
@@ -359,3 +360,19 @@ def test_tgemv_fp32_input_fused_norm(qt, blk, norm, N):
         y1 = torch.zeros(1, N, device="cuda")
         K.gemv(w, K.FAct(x[b:b + 1], gamma, 1e-6), 1, y1)
         assert torch.equal(y1[0], y[b]), b
+
+
+def test_gemm_tcgen05_bf16_out_many_tiles_per_cta():
+    """Persistent GEMM: several output tiles per CTA (both TMEM accumulators reused), bf16 output."""
+    from fak_b200.ops import kernels as Kn
+    torch.manual_seed(5)
+    M, N, K = 1536, 12288, 512
+    a = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    ref = a.float() @ b.float().T
+    out = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    Kn.gemm(a, b, out, 0, None, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert torch.allclose(out.float(), ref, atol=2e-2 * math.sqrt(K) / 8 + 1e-2, rtol=2e-2), (out.float() - ref).abs().max()
