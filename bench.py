@@ -43,6 +43,10 @@ def parse():
     ap.add_argument("--user", type=int, default=256)
     ap.add_argument("--decode", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--arm", default="C", choices=["A", "B", "C"],
+                    help="C: shared radix prefix + batched decode (the product); B: per-agent warm KV "
+                         "(each agent's own prefix cache, agents one at a time); A: no cache (every turn "
+                         "re-prefills the whole history)")
     return ap.parse_args()
 
 
@@ -137,7 +141,8 @@ def main():
     max_ctx = (max_ctx + 15) // 16 * 16
     ecfg = EngineConfig(max_batch=max(8, args.agents), cuda_graph=True,
                         graph_batch_buckets=tuple(sorted({1, 2, 4, 8, args.agents})),
-                        max_prefill_tokens=max(args.prefix, args.agents * args.user), tp=world)
+                        max_prefill_tokens=max(args.prefix, args.agents * args.user), tp=world,
+                        radix_cache=args.arm != "A")
     t0 = time.perf_counter()
     eng = Engine.synthetic(cfg, args.mix, args.seed, ecfg, dev, max_context=max_ctx, tp_group=group)
     eng.warmup_graphs()
@@ -146,12 +151,15 @@ def main():
     rng = np.random.default_rng(args.seed)
     V = cfg.vocab_size
     prefix = rng.integers(0, V, args.prefix).tolist()
-    hist = [list(prefix) for _ in range(args.agents)]
+    if args.arm == "B":  # per-agent caches: no agent reuses another agent's pages
+        hist = [rng.integers(0, V, args.prefix).tolist() for _ in range(args.agents)]
+    else:
+        hist = [list(prefix) for _ in range(args.agents)]
 
     # the shared system+tools prefix is prefilled once (setup)
     torch.cuda.synchronize()
     ts = time.perf_counter()
-    eng.generate([prefix], max_new_tokens=1)
+    eng.generate([prefix] if args.arm != "B" else [list(h) for h in hist], max_new_tokens=1)
     torch.cuda.synchronize()
     t_prefix = time.perf_counter() - ts
 
@@ -160,6 +168,8 @@ def main():
         for a in range(args.agents):
             hist[a].extend(rng.integers(0, V, args.user).tolist())
             reqs.append(eng.add_request(hist[a], args.decode))
+            if args.arm == "B":  # one agent at a time
+                eng.run_until_done(reqs[-1:])
         eng.run_until_done(reqs)
         for a, r in enumerate(reqs):
             hist[a].extend(r.output)
@@ -221,6 +231,8 @@ def main():
             "parallelism": f"tp{world}",
             "workload": f"{args.agents} agents x turns: +{args.user} user tokens, {args.decode} greedy decode tokens, "
                         f"shared {args.prefix}-token prefix, 16-token pages, radix reuse",
+            "arm": {"C": "shared radix prefix + batched decode", "B": "per-agent warm KV, one agent at a time",
+                    "A": "no KV reuse: full re-prefill every turn"}[args.arm],
             "l2": "each decode step streams the 4.4 GB weight set (>> 126 MB L2); no explicit flush",
             "kv_dtype": "bf16", "weight_format": "GGUF Q4_K/Q6_K blocks (decode), bf16 copy (prefill GEMM)",
         },

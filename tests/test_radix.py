@@ -126,3 +126,14 @@ def test_native_radix_matches_python_on_agent_turns():
                 log.append((n, list(pages), pool.n_free()))
         sims.append((log, rc.stats(), rc.n_cached_pages))
     assert sims[0] == sims[1]
+
+
+def test_radixbench_workloads():
+    from fak_b200.benchmarks import radixbench as RB
+    import numpy as np
+    for name, fn in RB.WORKLOADS.items():
+        reqs = fn(np.random.default_rng(0))
+        py = RB.run(reqs, 16, native=False)
+        assert 0.5 < py["hit_rate"] < 1.0, (name, py)
+        if len(IMPLS) > 1:
+            assert RB.run(reqs, 16, native=True) == py
