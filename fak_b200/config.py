@@ -191,6 +191,8 @@ class EngineConfig:
     seed: int = 0
     spec_k: int = 0                     # draft tokens per verify step (0: no speculation)
     spec_draft_layers: int = 4          # self-speculation: the draft is the first N layers + LM head
+    fused_activations: bool = False     # decode GEMVs normalise+quantize fp32 inputs themselves
+    attention_merge: bool = False       # merge attention splits in the last split's CTA (no combine launch)
 
     ENV_KEYS = {
         "page_size": ("FAK_PAGED_KV_BLOCK_TOKENS", int),
@@ -208,6 +210,8 @@ class EngineConfig:
         "seed": ("FAK_SEED", int),
         "spec_k": ("FAK_SPEC_K", int),
         "spec_draft_layers": ("FAK_SPEC_DRAFT_LAYERS", int),
+        "fused_activations": ("FAK_FUSED_ACT", bool),
+        "attention_merge": ("FAK_ATTN_MERGE", bool),
     }
 
     @classmethod

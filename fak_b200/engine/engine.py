@@ -88,7 +88,8 @@ class Engine:
         self.tp_group = tp_group
         self.runner = ModelRunner(weights, self.kv, max_batch=self.ecfg.max_batch,
                                   max_prefill_tokens=self.ecfg.max_prefill_tokens, max_context=self.max_context,
-                                  collectives=collectives)
+                                  collectives=collectives, fused_activations=self.ecfg.fused_activations,
+                                  attention_merge=self.ecfg.attention_merge)
         self.bt_width = math.ceil(self.max_context / ps)
         self.waiting: list[Request] = []
         self.prefilling: list[Request] = []

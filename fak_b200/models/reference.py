@@ -101,12 +101,20 @@ class ReferenceModel:
         """Run T tokens at absolute positions start_pos.. ; ``kv`` (per layer [Tctx,Hkv,D]) is extended in place."""
         cfg = self.cfg
         ids = torch.as_tensor(ids, dtype=torch.long, device=self.device).reshape(-1)
-        T = ids.numel()
-        x = self.embed(ids)
+        x = self.forward_band(self.embed(ids), start_pos, 0, cfg.n_layers, kv)
+        x = rmsnorm(x, self.t["output_norm.weight"], cfg.rms_eps)
+        return x if hidden_only else self.lm_head(x)
+
+    def forward_band(self, x: torch.Tensor, start_pos: int, l0: int, l1: int,
+                     kv: list[tuple[torch.Tensor, torch.Tensor]] | None = None) -> torch.Tensor:
+        """Layers [l0, l1) on the residual stream x [T, d] (a pipeline stage's band).  ``kv`` holds
+        the band's layers, index i - l0."""
+        cfg = self.cfg
+        T = x.shape[0]
         pos = torch.arange(start_pos, start_pos + T, device=self.device)
         cos, sin = rope_cos_sin(pos, cfg.head_dim, cfg.rope_theta)
         H, Hk, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
-        for i in range(cfg.n_layers):
+        for i in range(l0, l1):
             p = f"blk.{i}."
             h = rmsnorm(x, self.w(p + "attn_norm.weight"), cfg.rms_eps)
             q = h @ self.w(p + "attn_q.weight").T
@@ -124,20 +132,20 @@ class ReferenceModel:
                 k = rmsnorm(k, self.w(p + "attn_k_norm.weight"), cfg.rms_eps)
             q = apply_rope(q, cos, sin)
             k = apply_rope(k, cos, sin)
+            j = i - l0
             if kv is not None:
-                if len(kv) <= i:
+                if len(kv) <= j:
                     kv.append((k, v))
                 else:
-                    kv[i] = (torch.cat([kv[i][0], k]), torch.cat([kv[i][1], v]))
-                K, V = kv[i]
+                    kv[j] = (torch.cat([kv[j][0], k]), torch.cat([kv[j][1], v]))
+                K, V = kv[j]
             else:
                 K, V = k, v
             a = attention(q, K, V, start_pos)
             x = x + a.reshape(T, H * D) @ self.w(p + "attn_output.weight").T
             h = rmsnorm(x, self.w(p + "ffn_norm.weight"), cfg.rms_eps)
             x = x + self._ffn(i, h)
-        x = rmsnorm(x, self.t["output_norm.weight"], cfg.rms_eps)
-        return x if hidden_only else self.lm_head(x)
+        return x
 
     @torch.no_grad()
     def generate_greedy(self, prompt: list[int], n_new: int) -> list[int]:

@@ -21,7 +21,6 @@ from __future__ import annotations
 
 import dataclasses
 import math
-import os
 
 import torch
 
@@ -84,7 +83,8 @@ class PrefillMeta:
 
 class ModelRunner:
     def __init__(self, weights: ModelWeights, kv: KVCache, max_batch: int = 64, max_prefill_tokens: int = 4096,
-                 max_context: int | None = None, collectives=None):
+                 max_context: int | None = None, collectives=None, fused_activations: bool = False,
+                 attention_merge: bool = False):
         self.w = weights
         self.cfg: ModelConfig = weights.cfg
         self.kv = kv
@@ -112,12 +112,12 @@ class ModelRunner:
         self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
         # decode GEMV inputs: activations quantized by a separate kernel (default), or fp32 sources
-        # the GEMV normalises and quantizes itself (FAK_FUSED_ACT=1: fewer launches, but every CTA
+        # the GEMV normalises and quantizes itself (fused_activations: fewer launches, but every CTA
         # repeats the row's quantization; measured 0.14 ms/step slower on Qwen2.5-7B B=5).
-        # FAK_ATTN_MERGE=1 merges the attention splits in the last split's CTA instead of a combine
-        # kernel (one CTA then reads all 32 partials of its heads: a long tail, 0.7 ms/step slower).
-        self.fused_act = os.environ.get("FAK_FUSED_ACT", "0") == "1"
-        self.attn_merge = os.environ.get("FAK_ATTN_MERGE", "0") == "1"
+        # attention_merge merges the attention splits in the last split's CTA instead of a combine
+        # kernel (one CTA then reads all the partials of its heads: a long tail, 0.7 ms/step slower).
+        self.fused_act = fused_activations
+        self.attn_merge = attention_merge
         self.ffn_in = K.FAct(self.h) if self.fused_act else self.act_ffn   # SwiGLU output -> down projection
         self.lm_in = K.FAct(self.x) if self.fused_act else self.act_d      # final norm -> LM head
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
