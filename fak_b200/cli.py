@@ -44,11 +44,17 @@ def build_model_backend(args):
     from .config import EngineConfig, preset
     from .gguf import open_gguf
     from .tokenizer import Tokenizer
+    hf = getattr(args, "hf", None)
     if args.cpu:
         from .models.reference import ReferenceModel
         from .serve import ReferenceBackend
+        if hf:
+            from .models.hf import load_reference_tensors_hf
+            cfg, tensors = load_reference_tensors_hf(hf)
+            return ReferenceBackend(ReferenceModel(cfg, tensors),
+                                    Tokenizer.from_tokenizer_json(os.path.join(hf, "tokenizer.json")))
         if not args.gguf:
-            raise SystemExit("--cpu needs --gguf")
+            raise SystemExit("--cpu needs --gguf or --hf")
         tok = Tokenizer.from_gguf_metadata(open_gguf(args.gguf).metadata)
         return ReferenceBackend(ReferenceModel.from_gguf(args.gguf), tok)
     import torch
@@ -57,7 +63,10 @@ def build_model_backend(args):
     ecfg = EngineConfig.from_env(max_batch=args.max_batch)
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
-    if args.gguf:
+    if hf:
+        eng = Engine.from_hf(hf, ecfg, dev, max_context=args.max_context)
+        tok = Tokenizer.from_tokenizer_json(os.path.join(hf, "tokenizer.json"))
+    elif args.gguf:
         eng = Engine.from_gguf(args.gguf, ecfg, dev, max_context=args.max_context)
         tok = Tokenizer.from_gguf_metadata(open_gguf(args.gguf).metadata)
     else:
@@ -78,6 +87,8 @@ def build_model_backend(args):
 
 def _add_model_args(ap):
     ap.add_argument("--gguf", help="GGUF checkpoint (Q4_K/Q6_K/Q8_0/f16/f32 blocks)")
+    ap.add_argument("--hf", help="Hugging Face checkpoint directory (config.json, *.safetensors, tokenizer.json); "
+                                 "float weights are quantized to Q8_0 on load")
     ap.add_argument("--synthetic", default="tiny-qwen2", help="random-init preset when no --gguf is given")
     ap.add_argument("--mix", default="q4_k_m")
     ap.add_argument("--cpu", action="store_true", help="fp32 reference forward on the CPU")

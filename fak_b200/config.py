@@ -193,6 +193,7 @@ class EngineConfig:
     spec_draft_layers: int = 4          # self-speculation: the draft is the first N layers + LM head
     fused_activations: bool = False     # decode GEMVs normalise+quantize fp32 inputs themselves
     attention_merge: bool = False       # merge attention splits in the last split's CTA (no combine launch)
+    l2_prefetch: bool = False           # decode kernels warm L2 with the next GEMV's weights (measured neutral)
 
     ENV_KEYS = {
         "page_size": ("FAK_PAGED_KV_BLOCK_TOKENS", int),
@@ -212,6 +213,7 @@ class EngineConfig:
         "spec_draft_layers": ("FAK_SPEC_DRAFT_LAYERS", int),
         "fused_activations": ("FAK_FUSED_ACT", bool),
         "attention_merge": ("FAK_ATTN_MERGE", bool),
+        "l2_prefetch": ("FAK_L2_PREFETCH", bool),
     }
 
     @classmethod

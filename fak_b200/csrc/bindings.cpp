@@ -11,7 +11,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
-                      c10::optional<torch::Tensor> tickets);
+                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch);
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
                        torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out);
@@ -28,7 +28,7 @@ void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out, c10::option
 void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, torch::Tensor qx, torch::Tensor ds,
           int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, int64_t flags);
 void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx,
-                    torch::Tensor ds);
+                    torch::Tensor ds, c10::optional<torch::Tensor> prefetch);
 void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
                         int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
                         torch::Tensor counters, torch::Tensor err, int64_t ctas, c10::optional<torch::Tensor> src2,
@@ -46,7 +46,8 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
-           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs);
+           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
+           c10::optional<torch::Tensor> prefetch);
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device);
 int64_t tgemv_unit_bytes(int64_t qtype);
 void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, torch::Tensor qx,
@@ -69,7 +70,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &decode_attention, pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"),
         pybind11::arg("block_table"), pybind11::arg("ctx_len"), pybind11::arg("n_split"),
         pybind11::arg("pages_per_split"), pybind11::arg("out"), pybind11::arg("qx"), pybind11::arg("ds"),
-        pybind11::arg("workspace"), pybind11::arg("ldo") = 0, pybind11::arg("tickets") = pybind11::none());
+        pybind11::arg("workspace"), pybind11::arg("ldo") = 0, pybind11::arg("tickets") = pybind11::none(),
+        pybind11::arg("prefetch") = pybind11::none());
   m.def("prefill_attention", &prefill_attention);
   m.def("embed", &embed);
   m.def("rope_kv", &rope_kv);
@@ -90,13 +92,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qmmv", &qmmv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
         pybind11::arg("pitch"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"),
         pybind11::arg("bias"), pybind11::arg("epi"), pybind11::arg("flags") = 0);
-  m.def("quant_act_wide", &quant_act_wide);
+  m.def("quant_act_wide", &quant_act_wide, pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
+        pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("prefetch") = pybind11::none());
   m.def("tgemv", &tgemv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
         pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
         pybind11::arg("B"), pybind11::arg("y"), pybind11::arg("bias"),
         pybind11::arg("epi"), pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
         pybind11::arg("flags") = 0, pybind11::arg("ar_peers") = pybind11::none(), pybind11::arg("ar_me") = 0,
-        pybind11::arg("ar_parts_off") = 0, pybind11::arg("ar_flags_off") = 0, pybind11::arg("ar_epochs") = pybind11::none());
+        pybind11::arg("ar_parts_off") = 0, pybind11::arg("ar_flags_off") = 0, pybind11::arg("ar_epochs") = pybind11::none(),
+        pybind11::arg("prefetch") = pybind11::none());
   m.def("tgemv_workspace", &tgemv_workspace);
   m.def("tgemv_unit_bytes", &tgemv_unit_bytes);
   m.def("moe_tgemv", &moe_tgemv);

@@ -67,7 +67,8 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
               const int* __restrict__ block_table, int bt_stride, const int* __restrict__ ctx_len, int H, int Hkv,
               int n_split, int pages_per_split, float scale_log2, float* __restrict__ part_o,
               float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
-              float2* __restrict__ ds, int ldo, int* __restrict__ tickets) {
+              float2* __restrict__ ds, int ldo, int* __restrict__ tickets, const uint8_t* __restrict__ pf,
+              int64_t pf_bytes) {
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -77,6 +78,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;
   const int G = H / Hkv;
+  l2_prefetch(pf, pf_bytes);
   pdl_wait();
   const int ctx = ctx_len[b];
   const int n_pages = (ctx + PAGE - 1) / PAGE;
@@ -496,7 +498,9 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
-                      c10::optional<torch::Tensor> tickets) {
+                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch) {
+  const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
+  const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
   TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
   TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(), "v_cache");
@@ -545,7 +549,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<128>, (const float*)q.data_ptr<float>(),
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk));
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
+                                      pfp, pfb));
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -553,7 +558,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<64>, (const float*)q.data_ptr<float>(),
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk));
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
+                                      pfp, pfb));
   }
   if (n_split > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
@@ -713,14 +719,14 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     e = cudaFuncSetAttribute(k_decode_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<128>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0);
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
     e = cudaFuncSetAttribute(k_decode_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<64>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0);
   }
   if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode attention launch: %s", cudaGetErrorString(e));
   if (n_split > 1) {

@@ -53,6 +53,21 @@ FAK_DEV uint2 ldg_stream8(const void* p) {
 FAK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 FAK_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// Warm L2 with [base, base + bytes) for a LATER kernel (e.g. the next GEMV's weights while this
+// kernel is latency-bound): CTA b issues the 64 KB pieces b, b + grid, ... from one thread; no
+// shared memory is written and nothing waits for completion.  Call before pdl_wait: the bytes must
+// not depend on the previous kernel.
+FAK_DEV void l2_prefetch(const uint8_t* base, int64_t bytes) {
+  if (base == nullptr || bytes <= 0 || threadIdx.x != 0) return;
+  const int64_t nb = (int64_t)gridDim.x * gridDim.y * gridDim.z;
+  const int64_t b = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y + (int64_t)gridDim.y * blockIdx.z);
+  constexpr int64_t CH = 65536;
+  for (int64_t off = b * CH; off < bytes; off += nb * CH) {
+    const uint32_t n = (uint32_t)(bytes - off < CH ? bytes - off : CH) & ~15u;
+    if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(n) : "memory");
+  }
+}
+
 FAK_DEV int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
 // Exact int -> float for |c| < 2^22 without the (low-throughput) conversion pipe: adding c to

@@ -349,7 +349,9 @@ k_qmmv(const uint8_t* __restrict__ W, int N, int K, int64_t pitch, const int8_t*
 // activation quantizer with enough CTAs to fill the GPU: grid (B, ceil(K / 256)); each CTA
 // quantizes 8 blocks of 32 and, for the fused RMSNorm, recomputes its row's sum of squares.
 __global__ void k_quant_act_wide(const float* __restrict__ x, int64_t ldx, const float* __restrict__ gamma, float eps,
-                                 int K, int8_t* __restrict__ qx, float2* __restrict__ ds) {
+                                 int K, int8_t* __restrict__ qx, float2* __restrict__ ds, const uint8_t* __restrict__ pf,
+                                 int64_t pf_bytes) {
+  l2_prefetch(pf, pf_bytes);
   pdl_wait();
   const int b = blockIdx.x;
   const float* xr = x + (int64_t)b * ldx;
@@ -475,7 +477,9 @@ void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, t
 }
 
 void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx,
-                    torch::Tensor ds) {
+                    torch::Tensor ds, c10::optional<torch::Tensor> prefetch) {
+  const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
+  const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.dim() == 2 && x.stride(1) == 1, "x: [B,K] f32");
   const int B = (int)x.size(0), K = (int)x.size(1);
   TORCH_CHECK(K % 32 == 0 && x.stride(0) % 4 == 0, "K multiple of 32, row stride multiple of 4");
@@ -498,5 +502,6 @@ void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_quant_act_wide, (const float*)x.data_ptr<float>(), (int64_t)x.stride(0), g,
-                                    (float)eps, K, qx.data_ptr<int8_t>(), reinterpret_cast<float2*>(ds.data_ptr<float>())));
+                                    (float)eps, K, qx.data_ptr<int8_t>(), reinterpret_cast<float2*>(ds.data_ptr<float>()),
+                                    pfp, pfb));
 }

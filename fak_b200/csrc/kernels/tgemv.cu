@@ -361,7 +361,8 @@ __global__ void __launch_bounds__(W * 32, 1)
 k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
         const float* __restrict__ xf, int64_t ldx, const float* __restrict__ gamma, float eps,
         int B, float* __restrict__ y, int64_t ldy, const float* __restrict__ bias, int epi,
-        float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo, ArPeers ar) {
+        float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo, ArPeers ar,
+        const uint8_t* __restrict__ pf, int64_t pf_bytes) {
   constexpr int UT = Tile<QT>::UT;
   constexpr int TABF = Tile<QT>::TABF;
   constexpr int MB = 8 * NT;  // token rows staged
@@ -412,6 +413,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   // weights do not depend on the previous kernel: their first copies go out before the wait
   if (lane == 0)
     for (int i = 0; i < R - 1; i++) issue_next();
+  l2_prefetch(pf, pf_bytes);
   pdl_wait();
   if (xf != nullptr) {
     // fp32 activations: optional RMSNorm (statistics over the whole row), then int8 per 32-block
@@ -780,8 +782,11 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
-           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs) {
+           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
+           c10::optional<torch::Tensor> prefetch) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "tgemv: w cuda uint8");
+  const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
+  const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   ArPeers ar{};
   if (ar_peers.has_value()) {  // fused all-reduce over the ranks' symmetric buffers, then residual add
     auto h = ar_peers->cpu();
@@ -872,7 +877,8 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
                                         xp ? xp + b0 * ldx : nullptr, ldx, gp, (float)eps, nb,
                                         y.data_ptr<float>() + b0 * y.stride(0), (int64_t)y.stride(0), bp, (int)epi,
                                         p.geo.S > 1 ? part.data_ptr<float>() : nullptr,
-                                        p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo, ar));
+                                        p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo, ar,
+                                        b0 == 0 ? pfp : nullptr, pfb));
     }
   };
 #define FAK_TG_NT(QTV, NTV)                                              \

@@ -89,7 +89,7 @@ class Engine:
         self.runner = ModelRunner(weights, self.kv, max_batch=self.ecfg.max_batch,
                                   max_prefill_tokens=self.ecfg.max_prefill_tokens, max_context=self.max_context,
                                   collectives=collectives, fused_activations=self.ecfg.fused_activations,
-                                  attention_merge=self.ecfg.attention_merge)
+                                  attention_merge=self.ecfg.attention_merge, l2_prefetch=self.ecfg.l2_prefetch)
         self.bt_width = math.ceil(self.max_context / ps)
         self.waiting: list[Request] = []
         self.prefilling: list[Request] = []
@@ -111,6 +111,16 @@ class Engine:
     def from_gguf(cls, path: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None, **kw) -> "Engine":
         r, n = cls._tp(tp_group)
         w = load_weights(gguf_source(path), device, tp_rank=r, tp_size=n,
+                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
+        return cls(w, ecfg, device, tp_group=tp_group, **kw)
+
+    @classmethod
+    def from_hf(cls, model_dir: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None,
+                **kw) -> "Engine":
+        """Hugging Face checkpoint directory (safetensors); float matrices are quantized to Q8_0."""
+        from ..models.hf import hf_source
+        r, n = cls._tp(tp_group)
+        w = load_weights(hf_source(model_dir), device, tp_rank=r, tp_size=n,
                          prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 

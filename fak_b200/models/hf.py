@@ -1,0 +1,204 @@
+"""Hugging Face checkpoints: safetensors shards + config.json as a weight source.
+
+``hf_source(dir)`` returns the same (config, getter, close) triple as the GGUF source, with tensors
+renamed to the GGUF names the loaders use and float matrices handed over unquantized, so
+``load_weights`` quantizes them to Q8_0 on load (the reference's quant-on-load path) and the fp32
+reference model reads them as they are.  HF stores q/k rows in rotate_half order already (no
+GGML "llama" permutation to undo).  Expert weights of Qwen3-MoE checkpoints (one tensor per
+expert) are stacked into the [E, rows, cols] tensors of the GGUF layout.
+
+The safetensors container is read directly (8-byte little-endian header length, JSON header of
+{name: {dtype, shape, data_offsets}}, raw little-endian data) through a memory map.
+
+Reference: safetensors loading and HF config parsing (internal/model/weights.go:333, Load;
+internal/model/config.go:374-605), quant-on-load (internal/ggufload/gguf_weightsource.go:35-60).
+"""
+from __future__ import annotations
+
+import glob
+import json
+import os
+import re
+import struct
+from typing import Callable
+
+import numpy as np
+import torch
+
+from ..config import ModelConfig
+from ..gguf import GGMLType
+
+_NP = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "I32": np.int32, "I64": np.int64, "U8": np.uint8}
+_GG = {"F32": GGMLType.F32, "F16": GGMLType.F16, "BF16": GGMLType.BF16}
+
+
+def read_safetensors(path: str) -> dict[str, tuple[str, tuple[int, ...], np.ndarray]]:
+    """name -> (dtype, shape, memory-mapped array of the raw elements)."""
+    with open(path, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        header = json.loads(f.read(n))
+    mm = np.memmap(path, dtype=np.uint8, mode="r")
+    base = 8 + n
+    out = {}
+    for name, info in header.items():
+        if name == "__metadata__":
+            continue
+        a, b = info["data_offsets"]
+        dt = info["dtype"]
+        if dt not in _NP:
+            raise ValueError(f"{path}: unsupported safetensors dtype {dt} for {name}")
+        arr = mm[base + a:base + b].view(_NP[dt]).reshape(info["shape"] or [1])
+        out[name] = (dt, tuple(info["shape"]), arr)
+    return out
+
+
+def write_safetensors(path: str, tensors: dict[str, torch.Tensor], metadata: dict | None = None) -> None:
+    """Write float32/float16/bfloat16 tensors in the safetensors layout."""
+    names = sorted(tensors)
+    header, blobs, off = {}, [], 0
+    for n in names:
+        t = tensors[n].detach().cpu().contiguous()
+        dt = {torch.float32: "F32", torch.float16: "F16", torch.bfloat16: "BF16"}[t.dtype]
+        raw = t.view(torch.uint16).numpy().tobytes() if t.dtype == torch.bfloat16 else t.numpy().tobytes()
+        header[n] = {"dtype": dt, "shape": list(t.shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    if metadata:
+        header["__metadata__"] = {k: str(v) for k, v in metadata.items()}
+    hb = json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hb)))
+        f.write(hb)
+        for b in blobs:
+            f.write(b)
+
+
+def config_from_hf(hf: dict) -> ModelConfig:
+    arch_name = (hf.get("architectures") or [hf.get("model_type", "")])[0].lower()
+    if "qwen3moe" in arch_name or hf.get("model_type") == "qwen3_moe":
+        arch = "qwen3moe"
+    elif "qwen3" in arch_name:
+        arch = "qwen3"
+    elif "qwen2" in arch_name:
+        arch = "qwen2"
+    elif "llama" in arch_name or "mistral" in arch_name:
+        arch = "llama"
+    else:
+        raise ValueError(f"unsupported HF architecture {arch_name!r}")
+    d, H = int(hf["hidden_size"]), int(hf["num_attention_heads"])
+    cfg = ModelConfig(
+        arch=arch, n_layers=int(hf["num_hidden_layers"]), d_model=d, n_heads=H,
+        n_kv_heads=int(hf.get("num_key_value_heads", H)), head_dim=int(hf.get("head_dim") or d // H),
+        ffn_dim=int(hf.get("intermediate_size", 0)), vocab_size=int(hf["vocab_size"]),
+        rms_eps=float(hf.get("rms_norm_eps", 1e-6)), rope_theta=float(hf.get("rope_theta", 10000.0)),
+        tie_embeddings=bool(hf.get("tie_word_embeddings", False)), qkv_bias=arch == "qwen2",
+        qk_norm=arch in ("qwen3", "qwen3moe"),
+        n_experts=int(hf.get("num_experts", 0)) if arch == "qwen3moe" else 0,
+        n_experts_used=int(hf.get("num_experts_per_tok", 0)) if arch == "qwen3moe" else 0,
+        expert_ffn_dim=int(hf.get("moe_intermediate_size", 0)) if arch == "qwen3moe" else 0,
+        norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
+        max_context=int(hf.get("max_position_embeddings", 32768)),
+        bos_token_id=int(hf.get("bos_token_id") or 1), eos_token_id=int(hf.get("eos_token_id") or 2),
+        name=str(hf.get("_name_or_path", arch_name)),
+    )
+    cfg.validate()
+    return cfg
+
+
+_LAYER = {
+    "self_attn.q_proj.weight": "attn_q.weight", "self_attn.k_proj.weight": "attn_k.weight",
+    "self_attn.v_proj.weight": "attn_v.weight", "self_attn.o_proj.weight": "attn_output.weight",
+    "self_attn.q_proj.bias": "attn_q.bias", "self_attn.k_proj.bias": "attn_k.bias",
+    "self_attn.v_proj.bias": "attn_v.bias", "self_attn.q_norm.weight": "attn_q_norm.weight",
+    "self_attn.k_norm.weight": "attn_k_norm.weight", "input_layernorm.weight": "attn_norm.weight",
+    "post_attention_layernorm.weight": "ffn_norm.weight", "mlp.gate_proj.weight": "ffn_gate.weight",
+    "mlp.up_proj.weight": "ffn_up.weight", "mlp.down_proj.weight": "ffn_down.weight",
+    "mlp.gate.weight": "ffn_gate_inp.weight",
+}
+_EXPERT = re.compile(r"model\.layers\.(\d+)\.mlp\.experts\.(\d+)\.(gate|up|down)_proj\.weight")
+_EXP_NAME = {"gate": "ffn_gate_exps.weight", "up": "ffn_up_exps.weight", "down": "ffn_down_exps.weight"}
+
+
+def gguf_name(hf_name: str) -> str | None:
+    if hf_name == "model.embed_tokens.weight":
+        return "token_embd.weight"
+    if hf_name == "model.norm.weight":
+        return "output_norm.weight"
+    if hf_name == "lm_head.weight":
+        return "output.weight"
+    m = re.fullmatch(r"model\.layers\.(\d+)\.(.+)", hf_name)
+    if m and m.group(2) in _LAYER:
+        return f"blk.{m.group(1)}.{_LAYER[m.group(2)]}"
+    return None
+
+
+def _to_f32(dt: str, a: np.ndarray) -> np.ndarray:
+    if dt == "BF16":
+        return (a.astype(np.uint32) << 16).view(np.float32)
+    return a.astype(np.float32)
+
+
+def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]]:
+    with open(os.path.join(model_dir, "config.json")) as f:
+        cfg = config_from_hf(json.load(f))
+    files = sorted(glob.glob(os.path.join(model_dir, "*.safetensors")))
+    if not files:
+        raise FileNotFoundError(f"no *.safetensors in {model_dir}")
+    table: dict[str, tuple[str, tuple[int, ...], np.ndarray]] = {}
+    experts: dict[str, dict[int, tuple[str, np.ndarray]]] = {}
+    for p in files:
+        for n, (dt, shape, arr) in read_safetensors(p).items():
+            m = _EXPERT.fullmatch(n)
+            if m:
+                key = f"blk.{m.group(1)}.{_EXP_NAME[m.group(3)]}"
+                experts.setdefault(key, {})[int(m.group(2))] = (dt, arr)
+                continue
+            g = gguf_name(n)
+            if g is not None:
+                table[g] = (dt, shape, arr)
+    for key, per in experts.items():
+        dts = {d for d, _ in per.values()}
+        stacked = np.stack([per[e][1] for e in range(len(per))])
+        table[key] = (dts.pop(), stacked.shape, stacked)
+    if cfg.tie_embeddings or "output.weight" not in table:
+        cfg = cfg.replace(tie_embeddings=True)
+
+    def get(name: str):
+        if name not in table:
+            raise KeyError(f"{model_dir}: no tensor for {name}")
+        dt, shape, arr = table[name]
+        if dt not in _GG:
+            raise ValueError(f"{name}: dtype {dt} is not a float type")
+        a = np.ascontiguousarray(arr)
+        rows = int(np.prod(shape[:-1])) if len(shape) > 1 else 1
+        return tuple(shape), int(_GG[dt]), torch.from_numpy(a.view(np.uint8).reshape(rows, -1).copy())
+
+    return cfg, get, lambda: None
+
+
+def load_reference_tensors_hf(model_dir: str) -> tuple[ModelConfig, dict[str, torch.Tensor]]:
+    """fp32 tensors under GGUF names for the reference model."""
+    cfg, get, _ = hf_source(model_dir)
+    from ..gguf.quants import dequantize
+    out = {}
+    names = ["token_embd.weight", "output_norm.weight"] + ([] if cfg.tie_embeddings else ["output.weight"])
+    for i in range(cfg.n_layers):
+        p = f"blk.{i}."
+        names += [p + n for n in ("attn_norm.weight", "ffn_norm.weight", "attn_q.weight", "attn_k.weight",
+                                  "attn_v.weight", "attn_output.weight")]
+        if cfg.qkv_bias:
+            names += [p + n for n in ("attn_q.bias", "attn_k.bias", "attn_v.bias")]
+        if cfg.qk_norm:
+            names += [p + "attn_q_norm.weight", p + "attn_k_norm.weight"]
+        if cfg.is_moe:
+            names += [p + n for n in ("ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                      "ffn_down_exps.weight")]
+        else:
+            names += [p + n for n in ("ffn_gate.weight", "ffn_up.weight", "ffn_down.weight")]
+    for n in names:
+        shape, t, raw = get(n)
+        out[n] = torch.from_numpy(dequantize(raw.numpy().reshape(-1), t, shape).astype(np.float32))
+    if cfg.tie_embeddings:
+        out["output.weight"] = out["token_embd.weight"]
+    return cfg, out

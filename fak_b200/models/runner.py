@@ -84,7 +84,7 @@ class PrefillMeta:
 class ModelRunner:
     def __init__(self, weights: ModelWeights, kv: KVCache, max_batch: int = 64, max_prefill_tokens: int = 4096,
                  max_context: int | None = None, collectives=None, fused_activations: bool = False,
-                 attention_merge: bool = False):
+                 attention_merge: bool = False, l2_prefetch: bool = False):
         self.w = weights
         self.cfg: ModelConfig = weights.cfg
         self.kv = kv
@@ -118,6 +118,7 @@ class ModelRunner:
         # kernel (one CTA then reads all the partials of its heads: a long tail, 0.7 ms/step slower).
         self.fused_act = fused_activations
         self.attn_merge = attention_merge
+        self.l2_prefetch = l2_prefetch
         self.ffn_in = K.FAct(self.h) if self.fused_act else self.act_ffn   # SwiGLU output -> down projection
         self.lm_in = K.FAct(self.x) if self.fused_act else self.act_d      # final norm -> LM head
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
@@ -143,23 +144,31 @@ class ModelRunner:
         at 2K-9K contexts on B200 (8 is faster at batch 5 but leaves batch 1 with 32 CTAs)."""
         return 16
 
+    def _pf(self, w):
+        """Tile-packed weights of ``w`` to warm L2 with during the current kernel (or None)."""
+        return w.tp if self.l2_prefetch and w is not None and w.tp is not None else None
+
     def _layer_decode(self, i: int, B: int, pos, slot, bt, ctx, n_split: int) -> None:
         cfg, L, kv = self.cfg, self.w.layers[i], self.kv
         x = self.x[:B]
+        nxt = self.w.layers[i + 1] if i + 1 < cfg.n_layers else None
+        segs = L.qkv
         if self.fused_act:
             xin = K.FAct(x, L.attn_norm, cfg.rms_eps)  # RMSNorm + quantization inside the GEMV
         else:
-            K.quant_act(x, self.act_d, L.attn_norm, cfg.rms_eps)
+            K.quant_act(x, self.act_d, L.attn_norm, cfg.rms_eps, prefetch=self._pf(segs[0][0]))
             xin = self.act_d
-        for seg, off in L.qkv:
+        for j, (seg, off) in enumerate(segs):
             bias = L.qkv_bias[off:off + seg.rows] if L.qkv_bias is not None else None
-            K.gemv(seg, xin, B, self.qkv[:B, off:off + seg.rows], bias, K.EPI_STORE)
+            pf = segs[j + 1][0] if j + 1 < len(segs) else None
+            K.gemv(seg, xin, B, self.qkv[:B, off:off + seg.rows], bias, K.EPI_STORE, prefetch=self._pf(pf))
         K.rope_kv(self.qkv[:B], pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
                   self.q[:B], None, kv.k[i], kv.v[i])
         if self.coll is None:
             K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_attn,
-                               workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None)
-            K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD)
+                               workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None,
+                               prefetch=self._pf(L.o))
+            K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD, prefetch=self._pf(L.gate_up))
         else:
             self.coll.decode_attn_o(self, i, B, bt, ctx, n_split)
         if cfg.is_moe:
@@ -171,10 +180,12 @@ class ModelRunner:
             K.gemv(L.gate_up, K.FAct(x, L.ffn_norm, cfg.rms_eps), B, self.h[:B], None, K.EPI_SWIGLU)
         else:
             K.quant_act(x, self.act_d, L.ffn_norm, cfg.rms_eps)
-            K.gemv(L.gate_up, self.act_d, B, self.h[:B], None, K.EPI_SWIGLU)
+            K.gemv(L.gate_up, self.act_d, B, self.h[:B], None, K.EPI_SWIGLU, prefetch=self._pf(L.down))
             K.quant_act(self.h[:B, :self.ffn_local], self.act_ffn)
         if self.coll is None:
-            K.gemv(L.down, self.ffn_in, B, x, None, K.EPI_ADD)
+            nxt_w = nxt.qkv[0][0] if nxt is not None else self.w.lm_head
+            K.gemv(L.down, self.ffn_in, B, x, None, K.EPI_ADD,
+                   prefetch=self._pf(nxt_w) if nxt is not None else None)
         else:
             self.coll.decode_down(self, i, B)
 

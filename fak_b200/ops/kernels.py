@@ -43,8 +43,10 @@ class FAct:
         self.x, self.gamma, self.eps = x, gamma, float(eps)
 
 
-def quant_act(x: torch.Tensor, act: ActQ, gamma: torch.Tensor | None = None, eps: float = 1e-6) -> None:
-    ext().quant_act_wide(x, gamma, eps, act.q, act.ds)
+def quant_act(x: torch.Tensor, act: ActQ, gamma: torch.Tensor | None = None, eps: float = 1e-6,
+              prefetch: torch.Tensor | None = None) -> None:
+    """prefetch: a tensor (e.g. the next GEMV's tile-packed weights) to warm L2 with meanwhile."""
+    ext().quant_act_wide(x, gamma, eps, act.q, act.ds, prefetch)
     count()
 
 
@@ -76,7 +78,7 @@ def tgemv_workspace(device, weights=()) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None, epi: int = EPI_STORE,
-         flags: int = 0, ar: tuple | None = None) -> None:
+         flags: int = 0, ar: tuple | None = None, prefetch: torch.Tensor | None = None) -> None:
     """y[:B] (op)= W . x for a decode batch (w: models.weights.QuantWeight); chunks of 8 tokens.
 
     Matrices with a tile-packed copy (``QuantWeight.pack``) run the tile-packed tensor-core GEMV;
@@ -99,6 +101,8 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
                 raise ValueError("the fused all-reduce GEMV takes at most 32 tokens")
             arkw = {} if ar is None else dict(ar_peers=ar[0], ar_me=ar[1], ar_parts_off=ar[2], ar_flags_off=ar[3],
                                               ar_epochs=ar[4])
+            if prefetch is not None and b0 == 0:
+                arkw["prefetch"] = prefetch
             if isinstance(act, FAct):
                 C.tgemv(w.tp, w.qtype, w.rows, w.cols, None, None, act.x[b0:b0 + nb], act.gamma, act.eps, nb,
                         y[b0:b0 + nb], bias, epi, part, cnt, None, flags, **arkw)
@@ -121,13 +125,13 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 
 
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
-                     workspace=None, ldo: int = 0, tickets=None) -> None:
+                     workspace=None, ldo: int = 0, tickets=None, prefetch: torch.Tensor | None = None) -> None:
     """ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
     [B * kv heads]; when given, the last split of each (sequence, KV group) merges the splits in the
     same kernel instead of a separate combine launch (the kernel leaves the tickets at zero)."""
     ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
                            act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo,
-                           tickets)
+                           tickets, prefetch)
     count(2 if n_split > 1 and tickets is None else 1)
 
 

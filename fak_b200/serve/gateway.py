@@ -59,6 +59,35 @@ class Metrics:
         self.prompt_tokens = Counter("fak_gateway_prompt_tokens_total", "prompt tokens", registry=self.registry)
         self.verdicts = Counter("fak_kernel_verdicts_total", "tool-call verdicts", ["kind", "reason"],
                                 registry=self.registry)
+        self.tpot = Histogram("fak_gateway_tpot_seconds", "time per output token after the first",
+                              registry=self.registry,
+                              buckets=(0.001, 0.0025, 0.005, 0.01, 0.025, 0.05, 0.1, 0.25))
+        from prometheus_client import Gauge
+        self.engine = Gauge("fak_engine_stat", "engine counters and gauges (scraped from the engine)", ["stat"],
+                            registry=self.registry)
+
+    def scrape_engine(self, backend) -> None:
+        """Copy the local engine's counters (prefill tokens avoided, radix hit rate, KV pages, spec
+        acceptance, queue depths) into gauges at scrape time."""
+        eng = getattr(backend, "engine", None)
+        if eng is None:
+            return
+        st = dict(getattr(eng, "stats", {}))
+        radix = getattr(eng, "radix", None)
+        if radix is not None:
+            for k, v in radix.stats().items():
+                st["radix_" + k] = v
+        pool = getattr(eng, "pool", None)
+        if pool is not None:
+            st["kv_pages_free"] = pool.n_free()
+        for name in ("waiting", "prefilling", "running"):
+            if hasattr(eng, name):
+                st["requests_" + name] = len(getattr(eng, name))
+        if st.get("spec_proposed"):
+            st["spec_acceptance"] = st.get("spec_accepted", 0) / st["spec_proposed"]
+        for k, v in st.items():
+            if isinstance(v, (int, float)):
+                self.engine.labels(k).set(float(v))
 
 
 class Gateway:
@@ -121,6 +150,8 @@ class Gateway:
             text += tail
             yield tail, {}
         self.metrics.tokens.inc(n)
+        if first is not None and n > 1:
+            self.metrics.tpot.observe((time.perf_counter() - t0 - first) / (n - 1))
         yield "", {"prompt_tokens": len(ids), "completion_tokens": n, "finish_reason": finish,
                    "ttft_s": first, "text": text}
 
@@ -331,6 +362,7 @@ def create_app(gw: Gateway) -> FastAPI:
     @app.get("/metrics")
     def metrics():
         from prometheus_client import generate_latest
+        gw.metrics.scrape_engine(gw.backend)
         return PlainTextResponse(generate_latest(gw.metrics.registry).decode(), media_type="text/plain")
 
     @app.post("/v1/chat/completions")

@@ -110,3 +110,35 @@ def test_reference_backend_end_to_end(tok):
     assert r["usage"]["completion_tokens"] >= 1
     r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4})
     assert r.status_code == 200 and r.json()["usage"]["prompt_tokens"] > 5
+
+
+def test_metrics_expose_tpot_and_engine_stats(tok):
+    _, t = tok
+
+    class FakeEngine:
+        stats = {"prefill_tokens_avoided": 4096, "decode_tokens": 7, "spec_proposed": 8, "spec_accepted": 6}
+        waiting, prefilling, running = [1], [], [1, 2]
+
+    b = ScriptedBackend(t, "hello there, general")
+    b.engine = FakeEngine()
+    gw = Gateway(b, Kernel())
+    c = TestClient(create_app(gw))
+    c.post("/v1/chat/completions", json={"model": "x", "messages": [{"role": "user", "content": "go"}]})
+    text = c.get("/metrics").text
+    assert "fak_gateway_tpot_seconds_count" in text
+    assert 'fak_engine_stat{stat="prefill_tokens_avoided"} 4096.0' in text
+    assert 'fak_engine_stat{stat="spec_acceptance"} 0.75' in text
+    assert 'fak_engine_stat{stat="requests_running"} 2.0' in text
+
+
+def test_response_format_json_mask_is_built_from_the_vocabulary(tok, monkeypatch):
+    _, t = tok
+    gw = Gateway(ScriptedBackend(t, '{"a": 1}'), Kernel())
+    from fak_b200.serve.gateway import _sampling
+    sp = _sampling({"response_format": {"type": "json_object"}}, gw._json_mask)
+    assert sp.mask is not None and sp.mask is gw._json_mask()  # built once
+    monkeypatch.setenv("FAK_NATIVE_GUIDED_DECODE", "1")
+    assert not sp.greedy
+    ok = sp.mask.allowed([], t.vocab_size)
+    brace = t.token_to_id.get("{")
+    assert brace is None or bool(ok[brace])

@@ -1,0 +1,68 @@
+"""Hugging Face checkpoints (safetensors + config.json): our fp32 reference model, loaded through
+the HF source, reproduces the transformers implementation's logits (CPU)."""
+import json
+
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from fak_b200.models.hf import config_from_hf, hf_source, load_reference_tensors_hf, read_safetensors, write_safetensors  # noqa: E402
+from fak_b200.models.reference import ReferenceModel  # noqa: E402
+
+
+def _save(model, tmp_path):
+    write_safetensors(str(tmp_path / "model.safetensors"), {k: v for k, v in model.state_dict().items()})
+    cfg = model.config.to_dict()
+    cfg["architectures"] = [type(model).__name__]
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    return str(tmp_path)
+
+
+@pytest.mark.parametrize("arch", ["qwen2", "llama", "qwen3"])
+def test_reference_matches_transformers(arch, tmp_path):
+    common = dict(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                  num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256, rms_norm_eps=1e-6,
+                  rope_theta=10000.0, tie_word_embeddings=False)
+    if arch == "qwen2":
+        m = transformers.Qwen2ForCausalLM(transformers.Qwen2Config(**common))
+    elif arch == "llama":
+        m = transformers.LlamaForCausalLM(transformers.LlamaConfig(**common, attention_bias=False, mlp_bias=False))
+    else:
+        m = transformers.Qwen3ForCausalLM(transformers.Qwen3Config(**common, head_dim=32))
+    torch.manual_seed(0)
+    for p in m.parameters():  # visible norms / biases
+        torch.nn.init.normal_(p, std=0.05 if p.dim() > 1 else 0.5)
+    m = m.eval().float()
+    d = _save(m, tmp_path)
+    cfg, tensors = load_reference_tensors_hf(d)
+    assert cfg.arch == arch and cfg.n_kv_heads == 2
+    ref = ReferenceModel(cfg, tensors)
+    ids = torch.tensor([3, 17, 200, 45, 9, 311, 7])
+    with torch.no_grad():
+        want = m(ids[None]).logits[0]
+    got = ref.forward(ids)
+    assert torch.allclose(got, want, atol=2e-4, rtol=1e-4), (got - want).abs().max()
+
+
+def test_safetensors_roundtrip_and_bf16(tmp_path):
+    t = {"a": torch.randn(3, 5), "b": torch.randn(4).bfloat16(), "c": torch.randn(2, 2).half()}
+    write_safetensors(str(tmp_path / "x.safetensors"), t, {"format": "pt"})
+    r = read_safetensors(str(tmp_path / "x.safetensors"))
+    assert r["a"][0] == "F32" and torch.equal(torch.from_numpy(r["a"][2].copy()), t["a"])
+    assert r["b"][0] == "BF16" and torch.equal(torch.from_numpy(r["b"][2].copy()).view(torch.bfloat16), t["b"])
+    assert r["c"][1] == (2, 2)
+
+
+def test_hf_source_feeds_the_device_loader_shapes(tmp_path):
+    m = transformers.Qwen2ForCausalLM(transformers.Qwen2Config(
+        vocab_size=256, hidden_size=64, intermediate_size=128, num_hidden_layers=1, num_attention_heads=2,
+        num_key_value_heads=1, tie_word_embeddings=True))
+    d = _save(m.eval(), tmp_path)
+    cfg, get, close = hf_source(d)
+    assert cfg.tie_embeddings and cfg.qkv_bias
+    shape, t, raw = get("blk.0.attn_q.weight")
+    assert shape == (64, 64) and raw.shape == (64, 64 * 4)
+    with pytest.raises(ValueError):
+        config_from_hf({"architectures": ["GPT2LMHeadModel"], "hidden_size": 8, "num_attention_heads": 2,
+                        "num_hidden_layers": 1, "vocab_size": 10})
