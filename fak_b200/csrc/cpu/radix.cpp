@@ -8,6 +8,7 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <memory>
@@ -180,6 +181,27 @@ class RadixCache {
     return freed;
   }
 
+  // (tokens, pages) of every root-to-leaf path, sorted (a session checkpoint saves these)
+  std::vector<std::pair<std::vector<int64_t>, std::vector<int>>> sequences() const {
+    std::vector<std::pair<std::vector<int64_t>, std::vector<int>>> out;
+    struct Item {
+      const Node* nd;
+      std::vector<int64_t> toks;
+      std::vector<int> pages;
+    };
+    std::vector<Item> stack{{root_.get(), {}, {}}};
+    while (!stack.empty()) {
+      Item it = std::move(stack.back());
+      stack.pop_back();
+      it.toks.insert(it.toks.end(), it.nd->key.begin(), it.nd->key.end());
+      it.pages.insert(it.pages.end(), it.nd->pages.begin(), it.nd->pages.end());
+      if (it.nd->children.empty() && it.nd != root_.get()) out.emplace_back(it.toks, it.pages);
+      for (auto& kv : it.nd->children) stack.push_back({kv.second.get(), it.toks, it.pages});
+    }
+    std::sort(out.begin(), out.end());
+    return out;
+  }
+
   py::dict stats() const {
     py::dict d;
     d["cached_pages"] = n_cached_pages_;
@@ -275,6 +297,7 @@ void register_radix(py::module& m) {
       .def("insert", &RadixCache::insert)
       .def("evict", &RadixCache::evict)
       .def("stats", &RadixCache::stats)
+      .def("sequences", &RadixCache::sequences)
       .def_property_readonly("n_cached_pages", &RadixCache::n_cached_pages)
       .def_property_readonly("pool", &RadixCache::pool)
       .def_property_readonly("ps", &RadixCache::page_size);

@@ -56,6 +56,7 @@ class Request:
     finished: bool = False
     finish_reason: str = ""
     on_token: Callable[[int], None] | None = None
+    output_before_preempt: list[int] = dataclasses.field(default_factory=list)  # tokens emitted before a requeue
 
     @property
     def ttft(self) -> float | None:

@@ -193,6 +193,19 @@ class RadixCache:
             freed += len(victim.pages)
         return freed
 
+    def sequences(self) -> list[tuple[list[int], list[int]]]:
+        """(tokens, pages) of every root-to-leaf path -- what a session checkpoint saves."""
+        out = []
+        stack = [(self.root, [], [])]
+        while stack:
+            nd, toks, pages = stack.pop()
+            toks, pages = toks + list(nd.key), pages + list(nd.pages)
+            if not nd.children and nd is not self.root:
+                out.append((toks, pages))
+            for ch in nd.children.values():
+                stack.append((ch, toks, pages))
+        return sorted(out)
+
     def stats(self) -> dict:
         return {"cached_pages": self.n_cached_pages, "hit_tokens": self.hits_tokens,
                 "lookup_tokens": self.lookup_tokens,

@@ -116,3 +116,35 @@ def test_self_speculative_decode_matches_greedy(model_file):
         got = eng.generate(prompts, max_new_tokens=16)
         assert got == want, (k, got, want)
         assert eng.stats["spec_proposed"] > 0
+
+
+@pytest.mark.parametrize("include_kv", [False, True])
+def test_session_checkpoint_restore(model_file, tmp_path, include_kv):
+    """Checkpoint mid-generation, restore into a fresh engine, finish: the cached prefixes come back
+    (K/V copied or recomputed) and the continued outputs follow the uninterrupted run."""
+    from fak_b200.engine.session import load_session, save_session
+    rng = np.random.default_rng(21)
+    shared = rng.integers(0, 500, 48).tolist()
+    prompts = [shared + rng.integers(0, 500, n).tolist() for n in (9, 14)]
+    base = _engine(model_file, graphs=False)
+    want = base.generate(prompts, max_new_tokens=10)
+    a = _engine(model_file, graphs=False)
+    a.generate([shared + [1, 2, 3]], max_new_tokens=2)   # puts the shared prefix in the radix cache
+    reqs = [a.add_request(p, 10) for p in prompts]
+    for _ in range(4):
+        a.step()
+    path = str(tmp_path / "s.faksession")
+    info = save_session(a, path, include_kv=include_kv)
+    assert info["requests"] == 2 and info["cached_sequences"] >= 1
+    b = _engine(model_file, graphs=False)
+    restored = load_session(b, path)
+    avoided0 = b.stats["prefill_tokens_avoided"]
+    b.run_until_done(restored)
+    assert b.stats["prefill_tokens_avoided"] > avoided0  # the restored cache serves the requests
+    for r, w in zip(restored, want):
+        got = r.output_before_preempt + r.output
+        assert len(got) == 10
+        k = 0
+        while k < 10 and got[k] == w[k]:
+            k += 1
+        assert k >= 4, (got, w)

@@ -137,3 +137,19 @@ def test_radixbench_workloads():
         assert 0.5 < py["hit_rate"] < 1.0, (name, py)
         if len(IMPLS) > 1:
             assert RB.run(reqs, 16, native=True) == py
+
+
+def test_sequences_lists_every_cached_path(impl):
+    PagePool, RadixCache = impl
+    pool = PagePool(64, reserve=1)
+    rc = RadixCache(pool, page_size=4)
+    pg = pool.alloc(3)
+    rc.insert(list(range(12)), pg)
+    pool.release(pg)
+    pg2 = pg[:2] + pool.alloc(1)
+    pool.retain(pg[:2])
+    rc.insert(list(range(8)) + [50, 51, 52, 53], pg2)
+    pool.release(pg2)
+    seqs = rc.sequences()
+    assert [t for t, _ in seqs] == [list(range(12)), list(range(8)) + [50, 51, 52, 53]]
+    assert [p for _, p in seqs] == [pg, pg2]
