@@ -38,6 +38,9 @@ class ModelConfig:
     expert_ffn_dim: int = 0
     norm_topk_prob: bool = True
     max_context: int = 32768
+    # context-extension RoPE scaling as sorted (key, value) pairs (hashable; a dict is accepted):
+    # type linear|yarn|llama3, factor, original_max_position_embeddings, beta_fast/slow, ...
+    rope_scaling: tuple | None = None
     bos_token_id: int = 1
     eos_token_id: int = 2
     name: str = ""
@@ -57,6 +60,11 @@ class ModelConfig:
     @property
     def is_moe(self) -> bool:
         return self.n_experts > 0
+
+    def __post_init__(self) -> None:
+        if isinstance(self.rope_scaling, dict):
+            items = ((k, tuple(v) if isinstance(v, list) else v) for k, v in self.rope_scaling.items())
+            object.__setattr__(self, "rope_scaling", tuple(sorted(items)) or None)
 
     def validate(self) -> None:
         if self.n_heads % self.n_kv_heads:
@@ -147,6 +155,7 @@ def config_from_gguf_metadata(meta: dict[str, Any], tensor_shapes: dict[str, tup
         vocab_size=int(vocab),
         rms_eps=float(f"{float(g('attention.layer_norm_rms_epsilon', 1e-5)):.6g}"),
         rope_theta=float(f"{float(g('rope.freq_base', 10000.0)):.7g}"),
+        rope_scaling=_gguf_rope_scaling(g),
         tie_embeddings=tied,
         qkv_bias=qkv_bias,
         qk_norm=qk_norm,
@@ -161,6 +170,23 @@ def config_from_gguf_metadata(meta: dict[str, Any], tensor_shapes: dict[str, tup
     )
     cfg.validate()
     return cfg
+
+
+def _gguf_rope_scaling(g) -> dict | None:
+    """``{arch}.rope.scaling.*`` keys (type, factor, original_context_length, yarn betas/log-mul)."""
+    kind = str(g("rope.scaling.type", "") or "").lower()
+    factor = float(g("rope.scaling.factor", 0.0) or 0.0)
+    if kind in ("", "none") or factor in (0.0, 1.0):
+        return None
+    out: dict[str, Any] = {"type": kind, "factor": factor}
+    orig = g("rope.scaling.original_context_length", None)
+    if orig:
+        out["original_max_position_embeddings"] = int(orig)
+    for src, dst in (("rope.scaling.yarn_beta_fast", "beta_fast"), ("rope.scaling.yarn_beta_slow", "beta_slow")):
+        v = g(src, None)
+        if v is not None:
+            out[dst] = float(v)
+    return out
 
 
 def _env(name: str, default: Any, typ: type) -> Any:

@@ -87,11 +87,13 @@ def config_from_hf(hf: dict) -> ModelConfig:
     else:
         raise ValueError(f"unsupported HF architecture {arch_name!r}")
     d, H = int(hf["hidden_size"]), int(hf["num_attention_heads"])
+    rp = hf.get("rope_parameters") or hf.get("rope_scaling") or {}   # v5 configs nest rope_theta here
+    theta = float(hf.get("rope_theta") or rp.get("rope_theta") or 10000.0)
     cfg = ModelConfig(
         arch=arch, n_layers=int(hf["num_hidden_layers"]), d_model=d, n_heads=H,
         n_kv_heads=int(hf.get("num_key_value_heads", H)), head_dim=int(hf.get("head_dim") or d // H),
         ffn_dim=int(hf.get("intermediate_size", 0)), vocab_size=int(hf["vocab_size"]),
-        rms_eps=float(hf.get("rms_norm_eps", 1e-6)), rope_theta=float(hf.get("rope_theta", 10000.0)),
+        rms_eps=float(hf.get("rms_norm_eps", 1e-6)), rope_theta=theta,
         tie_embeddings=bool(hf.get("tie_word_embeddings", False)), qkv_bias=arch == "qwen2",
         qk_norm=arch in ("qwen3", "qwen3moe"),
         n_experts=int(hf.get("num_experts", 0)) if arch == "qwen3moe" else 0,
@@ -99,11 +101,23 @@ def config_from_hf(hf: dict) -> ModelConfig:
         expert_ffn_dim=int(hf.get("moe_intermediate_size", 0)) if arch == "qwen3moe" else 0,
         norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
         max_context=int(hf.get("max_position_embeddings", 32768)),
+        rope_scaling=_hf_rope_scaling(rp),
         bos_token_id=int(hf.get("bos_token_id") or 1), eos_token_id=int(hf.get("eos_token_id") or 2),
         name=str(hf.get("_name_or_path", arch_name)),
     )
     cfg.validate()
     return cfg
+
+
+def _hf_rope_scaling(rs: dict | None) -> dict | None:
+    if not rs:
+        return None
+    kind = str(rs.get("rope_type") or rs.get("type") or "default").lower()
+    if kind == "default":
+        return None
+    out = {k: v for k, v in rs.items() if k not in ("rope_type", "type", "rope_theta") and v is not None}
+    out["type"] = kind
+    return out
 
 
 _LAYER = {

@@ -28,13 +28,12 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return xf * inv * w.float()
 
 
-def rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float) -> tuple[torch.Tensor, torch.Tensor]:
-    """cos/sin tables [T, head_dim/2] with angles evaluated in float64."""
-    half = head_dim // 2
-    j = torch.arange(half, dtype=torch.float64)
-    inv = 1.0 / torch.pow(torch.tensor(theta, dtype=torch.float64), 2.0 * j / head_dim)
-    ang = positions.to(torch.float64)[:, None].cpu() * inv[None, :]
-    return torch.cos(ang).float().to(positions.device), torch.sin(ang).float().to(positions.device)
+def rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float, scaling=None, max_context: int | None = None
+                 ) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin tables [T, head_dim/2] with angles evaluated in float64 (scaled RoPE variants included)."""
+    from .rope import cos_sin
+    c, s = cos_sin(positions, head_dim, theta, scaling, max_context)
+    return c.to(positions.device), s.to(positions.device)
 
 
 def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
@@ -112,7 +111,7 @@ class ReferenceModel:
         cfg = self.cfg
         T = x.shape[0]
         pos = torch.arange(start_pos, start_pos + T, device=self.device)
-        cos, sin = rope_cos_sin(pos, cfg.head_dim, cfg.rope_theta)
+        cos, sin = rope_cos_sin(pos, cfg.head_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_context)
         H, Hk, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         for i in range(l0, l1):
             p = f"blk.{i}."

@@ -29,12 +29,12 @@ from ..ops import kernels as K
 from .weights import ModelWeights
 
 
-def rope_tables(max_pos: int, head_dim: int, theta: float, device) -> tuple[torch.Tensor, torch.Tensor]:
-    half = head_dim // 2
-    j = torch.arange(half, dtype=torch.float64)
-    inv = 1.0 / torch.pow(torch.tensor(theta, dtype=torch.float64), 2.0 * j / head_dim)
-    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
-    return torch.cos(ang).float().to(device).contiguous(), torch.sin(ang).float().to(device).contiguous()
+def rope_tables(max_pos: int, head_dim: int, theta: float, device, scaling=None, trained_context: int | None = None
+                ) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [max_pos, head_dim/2] (fp32, float64 angles; scaled RoPE resolved for the trained context)."""
+    from .rope import cos_sin
+    c, s = cos_sin(torch.arange(max_pos), head_dim, theta, scaling, trained_context)
+    return c.to(device).contiguous(), s.to(device).contiguous()
 
 
 @dataclasses.dataclass
@@ -101,7 +101,8 @@ class ModelRunner:
         self.qkv_dim = (self.Hq + 2 * self.Hkv) * self.D
         f0, f1 = weights.ffn_slice
         self.ffn_local = (f1 - f0) if not cfg.is_moe else cfg.expert_ffn_dim
-        self.cos, self.sin = rope_tables(self.max_context, self.D, cfg.rope_theta, dev)
+        self.cos, self.sin = rope_tables(self.max_context, self.D, cfg.rope_theta, dev, cfg.rope_scaling,
+                                         cfg.max_context)
         B, d = max_batch, cfg.d_model
         # decode buffers (static: CUDA graphs capture their addresses)
         self.x = torch.zeros(B, d, dtype=torch.float32, device=dev)
