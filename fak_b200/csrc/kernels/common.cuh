@@ -11,7 +11,9 @@
 namespace fak {
 
 constexpr int QK_K = 256;
-enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q8_0 = 8, QT_Q4_K = 12, QT_Q6_K = 14, QT_BF16 = 30 };
+// QT_G4 is framework-internal: group-wise asymmetric 4-bit (AWQ / GPTQ) in 144-byte blocks of 256,
+// [s0 f32][m0 f32][s1 f32][m1 f32][codes in the Q4_K nibble order], w = s_g * q - m_g per 128-group.
+enum QType : int { QT_F32 = 0, QT_F16 = 1, QT_Q8_0 = 8, QT_Q4_K = 12, QT_Q6_K = 14, QT_BF16 = 30, QT_G4 = 64 };
 
 FAK_DEV float warp_sum(float v) {
 #pragma unroll

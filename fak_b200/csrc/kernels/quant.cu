@@ -125,6 +125,37 @@ __global__ void k_quantize_q6_k(const float* __restrict__ x, uint8_t* __restrict
   *reinterpret_cast<uint16_t*>(o + 208) = __half_as_ushort(d);  // 210*b + 208 is even
 }
 
+// G4: one thread per 256-weight block (two 128-groups); scale (max - min) / 15 with min <= 0 <= max,
+// zero point rint(-min / s), codes clamp(rint(x / s) + z, 0, 15) -- the numpy codec's arithmetic.
+__global__ void k_quantize_g4(const float* __restrict__ x, uint8_t* __restrict__ out, int64_t nblocks) {
+  int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (b >= nblocks) return;
+  const float* xb = x + b * QK_K;
+  uint8_t* ob = out + b * 144;
+  float hdr[4];
+  for (int g = 0; g < 2; g++) {
+    float lo = 0.f, hi = 0.f;
+    for (int i = 0; i < 128; i++) {
+      lo = fminf(lo, xb[128 * g + i]);
+      hi = fmaxf(hi, xb[128 * g + i]);
+    }
+    float s = (hi - lo) / 15.0f;
+    if (!(s > 0.f)) s = 1.0f;
+    const float z = fminf(fmaxf(rintf(-lo / s), 0.f), 15.f);
+    hdr[2 * g] = s;
+    hdr[2 * g + 1] = z * s;
+    for (int i = 0; i < 128; i += 64) {
+      for (int l = 0; l < 32; l++) {
+        const int e = 128 * g + i + l;
+        const int q0 = (int)fminf(fmaxf(rintf(xb[e] / s) + z, 0.f), 15.f);
+        const int q1 = (int)fminf(fmaxf(rintf(xb[e + 32] / s) + z, 0.f), 15.f);
+        ob[16 + (e / 64) * 32 + l] = (uint8_t)(q0 | (q1 << 4));
+      }
+    }
+  }
+  for (int k = 0; k < 4; k++) reinterpret_cast<float*>(ob)[k] = hdr[k];
+}
+
 // ------------------------------------------------------------------------------------------
 // dequantizers: rows of GGML blocks (row pitch in bytes may exceed the packed row) -> T
 // one thread per 32 output elements
@@ -167,6 +198,15 @@ __global__ void k_dequant(const uint8_t* __restrict__ w, int qtype, int64_t rows
     const uint8_t* q = blk + 16 + (j / 2) * 32;
     int shift = (j & 1) * 4;
     for (int l = 0; l < 32; l++) store_out(o + l, d1 * (float)((q[l] >> shift) & 15) - m1);
+  } else if (qtype == QT_G4) {
+    int64_t sb = c0 / QK_K;
+    int j = (int)((c0 % QK_K) / 32);  // sub-block 0..7; groups of 128 = sub-blocks 0-3 / 4-7
+    const uint8_t* blk = row + sb * 144;
+    const float sc = reinterpret_cast<const float*>(blk)[2 * (j >> 2)];
+    const float mn = reinterpret_cast<const float*>(blk)[2 * (j >> 2) + 1];
+    const uint8_t* q = blk + 16 + (j / 2) * 32;
+    int shift = (j & 1) * 4;
+    for (int l = 0; l < 32; l++) store_out(o + l, sc * (float)((q[l] >> shift) & 15) - mn);
   } else if (qtype == QT_Q6_K) {
     int64_t sb = c0 / QK_K;
     int e0 = (int)(c0 % QK_K);  // multiple of 32
@@ -243,8 +283,8 @@ torch::Tensor quantize_blocks(torch::Tensor x, int64_t qtype) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "x: contiguous cuda f32");
   int64_t n = x.numel();
   int64_t blk = qtype == QT_Q8_0 ? 32 : 256;
-  int64_t bytes = qtype == QT_Q8_0 ? 34 : (qtype == QT_Q4_K ? 144 : 210);
-  TORCH_CHECK(qtype == QT_Q8_0 || qtype == QT_Q4_K || qtype == QT_Q6_K, "unsupported qtype");
+  int64_t bytes = qtype == QT_Q8_0 ? 34 : ((qtype == QT_Q4_K || qtype == QT_G4) ? 144 : 210);
+  TORCH_CHECK(qtype == QT_Q8_0 || qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_G4, "unsupported qtype");
   TORCH_CHECK(n % blk == 0, "element count not a multiple of the block size");
   int64_t nb = n / blk;
   auto out = torch::empty({nb * bytes}, x.options().dtype(torch::kUInt8));
@@ -256,6 +296,8 @@ torch::Tensor quantize_blocks(torch::Tensor x, int64_t qtype) {
     k_quantize_q8_0<<<grid, threads, 0, stream>>>(x.data_ptr<float>(), out.data_ptr<uint8_t>(), nb);
   else if (qtype == QT_Q4_K)
     k_quantize_q4_k<<<grid, threads, 0, stream>>>(x.data_ptr<float>(), out.data_ptr<uint8_t>(), nb);
+  else if (qtype == QT_G4)
+    k_quantize_g4<<<grid, threads, 0, stream>>>(x.data_ptr<float>(), out.data_ptr<uint8_t>(), nb);
   else
     k_quantize_q6_k<<<grid, threads, 0, stream>>>(x.data_ptr<float>(), out.data_ptr<uint8_t>(), nb);
   FAK_CUDA_CHECK(cudaGetLastError());

@@ -94,6 +94,7 @@ struct TGeo {
   int P;        // CTAs per slice
   int xstride;  // shared bytes per token row of activation codes
   int dstride;  // float2 per token row of the staged (scale, sum) pairs
+  int grp;      // Q4_K-shaped tiles: 0 = K-quant header, 1 = G4 group header (AWQ / GPTQ)
 };
 
 // Shared-memory carve-up (byte offsets), identical on host and device.
@@ -124,12 +125,21 @@ __host__ __device__ inline TSmem tsmem(int qt, int W, int R, int NT, const TGeo&
 template <int QT, int NT>
 FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, const int8_t* __restrict__ xr,
                        int xstride, const float2* __restrict__ dsT, const int* __restrict__ czT, int lane,
-                       float (&acc)[NT][4]) {
+                       float (&acc)[NT][4], int grp = 0) {
   constexpr int MB = 8 * NT;
   const int g = lane >> 2, t = lane & 3;
   const int sA = 2 * g, sB = 2 * g + 1;
   if constexpr (QT == QT_Q4_K) {
-    {  // scale table: lane -> slot lane>>1, sub-blocks 4*(lane&1) .. +3
+    if (grp) {  // G4 header (s0, m0, s1, m1): lane -> slot lane>>1, 128-group lane&1 = sub-blocks 4*(lane&1) .. +3
+      const int s = lane >> 1, jh = lane & 1;
+      const float4 h = *reinterpret_cast<const float4*>(wt + 16 * s);
+      const float sc = jh ? h.z : h.x, mn = jh ? h.w : h.y;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int j = 4 * jh + i;
+        reinterpret_cast<float2*>(tab)[j * 16 + s] = make_float2(sc * ((j & 1) ? 0.0625f : 1.0f), mn);
+      }
+    } else {  // scale table: lane -> slot lane>>1, sub-blocks 4*(lane&1) .. +3
       const int s = lane >> 1, jh = lane & 1;
       const uint4 h = *reinterpret_cast<const uint4*>(wt + 16 * s);
       const float d = __half2float(__ushort_as_half((uint16_t)(h.x & 0xffff)));
@@ -517,7 +527,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
     if (lane == 0) issue_next();  // into the slot released at the end of the previous iteration
     tc::mbar_wait(&bar[cslot], phase, err);
     unit_tile<QT, NT>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
-                      QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
+                      QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc, geo.grp);
     if (++cslot == R) {
       cslot = 0;
       phase ^= 1u;
@@ -665,7 +675,7 @@ k_tgemv_moe(const uint8_t* __restrict__ Wt, int Te, int K, const int8_t* __restr
     if (lane == 0) issue_next();
     tc::mbar_wait(&bar[cslot], phase, err);
     unit_tile<QT, 1>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
-                     QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
+                     QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc, geo.grp);
     if (++cslot == R) {
       cslot = 0;
       phase ^= 1u;
@@ -721,6 +731,7 @@ TGeo make_geo(int qt, int T, int U, int S0, int n_sm) {
   // activation rows 32 mod 128 bytes apart (8-byte loads, Q4_K/Q8_0) or 16 mod 128 (4-byte, Q6_K)
   g.xstride = ((Us * 256 + 127) / 128) * 128 + (qt == QT_Q6_K ? 16 : 32);
   g.dstride = Us * 8;
+  g.grp = 0;
   return g;
 }
 
@@ -762,10 +773,14 @@ Plan make_plan(int qt, int64_t N, int64_t K, int NT, int n_sm, int max_smem, int
 
 }  // namespace
 
-int64_t tgemv_unit_bytes(int64_t qtype) { return tile_bytes((int)qtype); }
+// G4 (AWQ / GPTQ) tiles have the Q4_K shape: the Q4_K kernels run them with geo.grp = 1.
+static int64_t kernel_qt(int64_t qtype) { return qtype == QT_G4 ? QT_Q4_K : qtype; }
+
+int64_t tgemv_unit_bytes(int64_t qtype) { return tile_bytes((int)kernel_qt(qtype)); }
 
 // Scratch floats / counters the split-K reduction of this shape needs.
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device) {
+  qtype = kernel_qt(qtype);
   int n_sm = 0, max_smem = 0;
   FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, (int)device));
   FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, (int)device));
@@ -801,6 +816,8 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     ar.flags_off = ar_flags_off;
     ar.epochs = reinterpret_cast<uint32_t*>(ar_epochs->data_ptr<int>());
   }
+  const int grp = qtype == QT_G4;
+  qtype = kernel_qt(qtype);
   TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "tgemv: qtype");
   TORCH_CHECK(K % 64 == 0 && (qtype == QT_Q8_0 || K % 256 == 0), "tgemv: K must be a multiple of 256 (64 for Q8_0)");
   const int64_t T = (N + 15) / 16, U = (K + 255) / 256;
@@ -848,6 +865,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   }
   Plan p = make_plan((int)qtype, N, K, NT, n_sm, max_smem, (int)(flags & 31), (int)((flags >> 5) & 15),
                      (int)((flags >> 9) & 255));
+  p.geo.grp = grp;
   if (p.geo.S > 1) {
     TORCH_CHECK(part.scalar_type() == torch::kFloat32 && part.numel() >= (int64_t)p.geo.S * p.geo.T * 128 * p.NT,
                 "tgemv: split-K scratch too small");
@@ -907,6 +925,8 @@ void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t 
                torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
                torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "moe_tgemv: w");
+  const int grp = qtype == QT_G4;
+  qtype = kernel_qt(qtype);
   TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "moe_tgemv: qtype");
   TORCH_CHECK(rows_per_expert % 16 == 0 && K % 256 == 0, "moe_tgemv: rows per expert % 16, K % 256");
   TORCH_CHECK(qx.scalar_type() == torch::kInt8 && qx.is_contiguous() &&
@@ -919,6 +939,7 @@ void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t 
   if (!max_smem)
     FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, w.get_device()));
   TGeo g = make_geo((int)qtype, (int)(rows_per_expert / 16), (int)(K / 256), 1, 1);
+  g.grp = grp;
   const int Te = (int)(rows_per_expert / 16);
   int W = 16, R = 3;
   if (tsmem((int)qtype, 16, 3, 1, g).total > max_smem) W = 8;

@@ -54,6 +54,10 @@ class GGMLType(enum.IntEnum):
     I64 = 27
     F64 = 28
     BF16 = 30
+    # framework-internal (not a GGML type): group-wise asymmetric 4-bit, groups of 128 along the
+    # row -- the AWQ / GPTQ weight format.  Block of 256 weights, 144 bytes:
+    # [s0 f32][m0 f32][s1 f32][m1 f32][128 B of codes in the Q4_K nibble order], w = s_g * q - m_g
+    G4 = 64
 
 
 QK_K = 256
@@ -82,6 +86,7 @@ BLOCK_INFO: dict[GGMLType, tuple[int, int]] = {
     GGMLType.Q8_K: (QK_K, 292),
     GGMLType.IQ4_NL: (32, 18),
     GGMLType.IQ4_XS: (QK_K, 136),
+    GGMLType.G4: (QK_K, 144),
 }
 
 # llama.cpp "file_type" codes that appear in general.file_type

@@ -288,6 +288,61 @@ def f32_to_bf16(x: np.ndarray) -> np.ndarray:
     return rounded.astype(np.uint16)
 
 
+# ---- G4: group-wise asymmetric 4-bit (AWQ / GPTQ), groups of 128 --------------------------------
+# 144 B per 256 weights: (s0, m0, s1, m1) as f32 then 128 B of codes laid out like Q4_K's qs
+# (chunk c of 64 weights: byte b holds weight 64c+b in its low nibble and 64c+32+b in its high one).
+# w = s_g * q - m_g with m_g = s_g * z_g, i.e. (q - z_g) * s_g of the AWQ/GPTQ checkpoints.
+G4_GROUP = 128
+
+
+def _g4_nibbles(codes: np.ndarray) -> np.ndarray:
+    """codes [nb, 256] (0..15) -> [nb, 128] bytes in the Q4_K order."""
+    c = codes.reshape(-1, 4, 2, 32).astype(np.uint8)
+    return (c[:, :, 0, :] | (c[:, :, 1, :] << 4)).reshape(-1, 128)
+
+
+def _g4_codes(qs: np.ndarray) -> np.ndarray:
+    q = qs.reshape(-1, 4, 1, 32)
+    return np.concatenate([q & 15, q >> 4], axis=2).reshape(-1, 256)
+
+
+def g4_from_codes(codes: np.ndarray, scales: np.ndarray, zeros: np.ndarray, group: int) -> np.ndarray:
+    """Rows of G4 blocks from per-weight codes [out, in] (0..15), scales / zero points [out, in/group].
+
+    ``group`` must be a multiple of 128 (each 128-group of a block takes its group's pair)."""
+    out_, in_ = codes.shape
+    if group % G4_GROUP or in_ % QK_K:
+        raise ValueError(f"G4 needs groups of a multiple of {G4_GROUP} and rows of a multiple of {QK_K}")
+    rep = group // G4_GROUP
+    s = np.repeat(np.asarray(scales, _f32), rep, axis=1).reshape(-1, 2)         # [out*in/256, 2]
+    m = (np.repeat(np.asarray(zeros, _f32), rep, axis=1).reshape(-1, 2) * s).astype(_f32)
+    hdr = np.stack([s[:, 0], m[:, 0], s[:, 1], m[:, 1]], axis=1).astype(_f32).view(np.uint8)
+    qs = _g4_nibbles(np.asarray(codes).reshape(-1, QK_K))
+    return np.concatenate([hdr, qs], axis=1).reshape(out_, -1)
+
+
+def quantize_g4(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest asymmetric 4-bit per 128-group (scale (max - min) / 15, integer zero point)."""
+    g = np.ascontiguousarray(x, _f32).reshape(-1, G4_GROUP)
+    lo = np.minimum(g.min(axis=1), 0).astype(_f32)
+    hi = np.maximum(g.max(axis=1), 0).astype(_f32)
+    s = ((hi - lo) / _f32(15)).astype(_f32)
+    s = np.where(s > 0, s, _f32(1)).astype(_f32)
+    z = np.clip(np.rint(-lo / s), 0, 15).astype(_f32)
+    q = np.clip(np.rint(g / s[:, None]) + z[:, None], 0, 15).astype(np.uint8)
+    rows = g.shape[0] // 2
+    return g4_from_codes(q.reshape(rows, QK_K), s.reshape(rows, 2), z.reshape(rows, 2), G4_GROUP).reshape(-1)
+
+
+def dequantize_g4(raw: np.ndarray) -> np.ndarray:
+    b = _as_blocks(raw, 144)
+    hdr = np.ascontiguousarray(b[:, :16]).view(_f32)                               # [nb, 4]
+    q = _g4_codes(b[:, 16:]).astype(_f32).reshape(-1, 2, G4_GROUP)
+    s = hdr[:, [0, 2]][:, :, None]
+    m = hdr[:, [1, 3]][:, :, None]
+    return (s * q - m).astype(_f32).reshape(-1)
+
+
 _DEQUANT = {
     GGMLType.Q8_0: dequantize_q8_0,
     GGMLType.Q4_0: dequantize_q4_0,
@@ -298,16 +353,18 @@ _DEQUANT = {
     GGMLType.Q4_K: dequantize_q4_k,
     GGMLType.Q5_K: dequantize_q5_k,
     GGMLType.Q6_K: dequantize_q6_k,
+    GGMLType.G4: dequantize_g4,
 }
 
 _QUANT = {
     GGMLType.Q8_0: quantize_q8_0,
     GGMLType.Q4_K: quantize_q4_k,
     GGMLType.Q6_K: quantize_q6_k,
+    GGMLType.G4: quantize_g4,
 }
 
 SUPPORTED_DEQUANT = frozenset(_DEQUANT) | {GGMLType.F32, GGMLType.F16, GGMLType.BF16}
-DEVICE_RESIDENT_QUANTS = frozenset({GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K})
+DEVICE_RESIDENT_QUANTS = frozenset({GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.G4})
 
 
 def dequantize(raw: np.ndarray, ggml_type: int, shape: tuple[int, ...] | None = None) -> np.ndarray:

@@ -33,7 +33,7 @@ from .constants import (FILE_TYPE_ALL_F32, FILE_TYPE_MOSTLY_BF16, FILE_TYPE_MOST
 from .quants import quantize
 from .writer import GGUFWriter
 
-QUANT_MIXES = ("q8_0", "q4_k_m", "f32", "f16", "bf16")
+QUANT_MIXES = ("q8_0", "q4_k_m", "g4", "f32", "f16", "bf16")
 
 
 def use_more_bits(i: int, n: int) -> bool:
@@ -100,6 +100,10 @@ def choose_type(cfg: ModelConfig, name: str, shape: tuple[int, ...], role: str, 
         if role in ("attn_v", "ffn_down") and use_more_bits(_layer_of(name), cfg.n_layers):
             return GGMLType.Q6_K
         return GGMLType.Q4_K
+    if mix == "g4":  # AWQ / GPTQ-style checkpoints: int4 groups of 128 for the block matrices
+        if role in ("embed", "output") or row % QK_K:
+            return GGMLType.Q8_0 if row % 32 == 0 else GGMLType.F16
+        return GGMLType.G4
     raise ValueError(f"unknown quant mix {mix!r}; choose one of {QUANT_MIXES}")
 
 

@@ -28,7 +28,8 @@ import torch
 from ..config import ModelConfig
 from ..gguf import GGMLType
 
-_NP = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "I32": np.int32, "I64": np.int64, "U8": np.uint8}
+_NP = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "I32": np.int32, "I64": np.int64, "U8": np.uint8,
+       "I8": np.int8, "I16": np.int16}
 _GG = {"F32": GGMLType.F32, "F16": GGMLType.F16, "BF16": GGMLType.BF16}
 
 
@@ -53,12 +54,13 @@ def read_safetensors(path: str) -> dict[str, tuple[str, tuple[int, ...], np.ndar
 
 
 def write_safetensors(path: str, tensors: dict[str, torch.Tensor], metadata: dict | None = None) -> None:
-    """Write float32/float16/bfloat16 tensors in the safetensors layout."""
+    """Write float32/float16/bfloat16 (and int32/int64/uint8/int8) tensors in the safetensors layout."""
     names = sorted(tensors)
     header, blobs, off = {}, [], 0
     for n in names:
         t = tensors[n].detach().cpu().contiguous()
-        dt = {torch.float32: "F32", torch.float16: "F16", torch.bfloat16: "BF16"}[t.dtype]
+        dt = {torch.float32: "F32", torch.float16: "F16", torch.bfloat16: "BF16", torch.int32: "I32",
+              torch.int64: "I64", torch.uint8: "U8", torch.int8: "I8"}[t.dtype]
         raw = t.view(torch.uint16).numpy().tobytes() if t.dtype == torch.bfloat16 else t.numpy().tobytes()
         header[n] = {"dtype": dt, "shape": list(t.shape), "data_offsets": [off, off + len(raw)]}
         blobs.append(raw)
@@ -153,16 +155,62 @@ def _to_f32(dt: str, a: np.ndarray) -> np.ndarray:
     return a.astype(np.float32)
 
 
+_QPARTS = (".qweight", ".qzeros", ".scales", ".g_idx")
+
+
+def _quant_config(hf: dict) -> dict | None:
+    q = hf.get("quantization_config")
+    if not q:
+        return None
+    method = str(q.get("quant_method", "")).lower()
+    if method not in ("awq", "gptq"):
+        raise ValueError(f"unsupported quantization method {method!r} (AWQ and GPTQ are)")
+    return q
+
+
+def _decode_quantized(qc: dict, parts: dict[str, np.ndarray]) -> tuple[tuple[int, int], int, np.ndarray]:
+    """One qweight/qzeros/scales[/g_idx] triple -> ((out, in), ggml type, rows)."""
+    from . import quantized_ckpt as qk
+    bits, group = int(qc.get("bits", 4)), int(qc.get("group_size", 128))
+    if qc["quant_method"].lower() == "awq":
+        if bits != 4:
+            raise ValueError("AWQ checkpoints are 4-bit")
+        n_in = parts["qweight"].shape[0]
+        group = n_in if group <= 0 else group
+        codes, sc, z, _ = qk.unpack_awq(parts["qweight"], parts["qzeros"], _f32s(parts["scales"]), group)
+        gidx = np.arange(n_in) // group
+    else:
+        n_in = parts["qweight"].shape[0] * 32 // bits
+        group = n_in if group <= 0 else group
+        v1 = str(qc.get("checkpoint_format", "gptq")).lower() != "gptq_v2"
+        codes, sc, z, gidx = qk.unpack_gptq(parts["qweight"], parts["qzeros"], _f32s(parts["scales"]),
+                                           parts.get("g_idx"), bits, group, v1)
+    rows, t = qk.device_rows(codes, sc, z, gidx, group, bits)
+    return codes.shape, t, rows
+
+
+def _f32s(a: tuple[str, np.ndarray] | np.ndarray) -> np.ndarray:
+    dt, arr = a
+    return _to_f32(dt, np.asarray(arr))
+
+
 def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]]:
     with open(os.path.join(model_dir, "config.json")) as f:
-        cfg = config_from_hf(json.load(f))
+        hfcfg = json.load(f)
+    cfg = config_from_hf(hfcfg)
+    qc = _quant_config(hfcfg)
     files = sorted(glob.glob(os.path.join(model_dir, "*.safetensors")))
     if not files:
         raise FileNotFoundError(f"no *.safetensors in {model_dir}")
     table: dict[str, tuple[str, tuple[int, ...], np.ndarray]] = {}
     experts: dict[str, dict[int, tuple[str, np.ndarray]]] = {}
+    qparts: dict[str, dict[str, object]] = {}   # base name -> {qweight, qzeros, scales, g_idx}
     for p in files:
         for n, (dt, shape, arr) in read_safetensors(p).items():
+            if qc is not None and n.endswith(_QPARTS):
+                base, part = n.rsplit(".", 1)
+                qparts.setdefault(base, {})[part] = (dt, arr) if part == "scales" else np.asarray(arr)
+                continue
             m = _EXPERT.fullmatch(n)
             if m:
                 key = f"blk.{m.group(1)}.{_EXP_NAME[m.group(3)]}"
@@ -171,14 +219,39 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
             g = gguf_name(n)
             if g is not None:
                 table[g] = (dt, shape, arr)
+    # quantized layers: decoded on first use; experts (one triple per expert) stacked
+    qlayers: dict[str, list[dict]] = {}
+    for base, parts in qparts.items():
+        if "qweight" not in parts:
+            continue
+        m = _EXPERT.fullmatch(base + ".weight")
+        if m:
+            key = f"blk.{m.group(1)}.{_EXP_NAME[m.group(3)]}"
+            lst = qlayers.setdefault(key, [])
+            lst.extend([None] * (int(m.group(2)) + 1 - len(lst)))
+            lst[int(m.group(2))] = parts
+            continue
+        g = gguf_name(base + ".weight")
+        if g is not None:
+            qlayers[g] = [parts]
     for key, per in experts.items():
         dts = {d for d, _ in per.values()}
         stacked = np.stack([per[e][1] for e in range(len(per))])
         table[key] = (dts.pop(), stacked.shape, stacked)
-    if cfg.tie_embeddings or "output.weight" not in table:
+    if cfg.tie_embeddings or ("output.weight" not in table and "output.weight" not in qlayers):
         cfg = cfg.replace(tie_embeddings=True)
 
     def get(name: str):
+        if name in qlayers:
+            dec = [_decode_quantized(qc, parts) for parts in qlayers[name]]
+            types = {t for _, t, _ in dec}
+            if len(types) > 1:   # mixed layouts across experts: every one as float32
+                dec = [(sh, int(GGMLType.F32), np.ascontiguousarray(
+                    _dequant_rows(r, t, sh))) for sh, t, r in dec]
+            (o, i), t, _ = dec[0]
+            rows = np.concatenate([r for _, _, r in dec]) if len(dec) > 1 else dec[0][2]
+            shape = (len(dec), o, i) if len(dec) > 1 else (o, i)
+            return shape, int(dec[0][1]), torch.from_numpy(np.ascontiguousarray(rows).view(np.uint8))
         if name not in table:
             raise KeyError(f"{model_dir}: no tensor for {name}")
         dt, shape, arr = table[name]
@@ -189,6 +262,12 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
         return tuple(shape), int(_GG[dt]), torch.from_numpy(a.view(np.uint8).reshape(rows, -1).copy())
 
     return cfg, get, lambda: None
+
+
+def _dequant_rows(rows: np.ndarray, t: int, shape) -> np.ndarray:
+    from ..gguf.quants import dequantize
+    return dequantize(np.ascontiguousarray(rows).reshape(-1), t, shape).astype(np.float32).view(np.uint8).reshape(
+        shape[0], -1)
 
 
 def load_reference_tensors_hf(model_dir: str) -> tuple[ModelConfig, dict[str, torch.Tensor]]:

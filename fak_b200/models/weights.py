@@ -275,6 +275,10 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
         return shape, t2, rows2
 
     emb_shape, emb_t, emb_raw = get("token_embd.weight")
+    if emb_t == int(GGMLType.G4):   # the embedding gather reads K-quant / Q8_0 / float rows
+        emb_raw, emb_t = _as_device_quant(emb_shape, int(GGMLType.F32), torch.from_numpy(
+            np_dequantize(emb_raw.cpu().numpy().reshape(-1), emb_t).astype(np.float32)).view(torch.uint8), device)
+        emb_raw = emb_raw.cpu()
     if emb_t in (int(GGMLType.F32), int(GGMLType.F16), int(GGMLType.BF16)) or emb_t in dq.DEVICE_QTYPES:
         embed = QuantWeight.from_rows(emb_raw.view(torch.uint8).reshape(emb_shape[0], -1), emb_t, emb_shape[1], device)
     else:

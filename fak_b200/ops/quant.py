@@ -6,8 +6,8 @@ import torch
 from ..gguf.constants import BLOCK_INFO, GGMLType
 from ._ext import ext
 
-QT_F32, QT_F16, QT_Q8_0, QT_Q4_K, QT_Q6_K, QT_BF16 = 0, 1, 8, 12, 14, 30
-DEVICE_QTYPES = (QT_Q8_0, QT_Q4_K, QT_Q6_K)
+QT_F32, QT_F16, QT_Q8_0, QT_Q4_K, QT_Q6_K, QT_BF16, QT_G4 = 0, 1, 8, 12, 14, 30, 64
+DEVICE_QTYPES = (QT_Q8_0, QT_Q4_K, QT_Q6_K, QT_G4)
 
 
 def row_bytes(qtype: int, cols: int) -> int:
@@ -64,7 +64,7 @@ def synth_quantized(shape: tuple[int, ...], ggml_type: int, seed: int, std: floa
 # "unit tile" whose fields are split into planes.  Plane row ("slot") s holds tile row
 # (s >> 1) + 8 (s & 1) (except the Q6_K qh plane, kept in tile-row order); 16-byte chunks of the
 # quant planes are XOR-swizzled.  The block bytes are unchanged, only placed differently.
-TILE_UNIT_BYTES = {QT_Q4_K: 2304, QT_Q6_K: 3360, QT_Q8_0: 4352}
+TILE_UNIT_BYTES = {QT_Q4_K: 2304, QT_Q6_K: 3360, QT_Q8_0: 4352, QT_G4: 2304}
 SLOT_ROWS = [(s >> 1) + 8 * (s & 1) for s in range(16)]
 
 
@@ -92,11 +92,11 @@ def tile_pack(buf: torch.Tensor, qtype: int, rows: int, cols: int, pitch: int) -
         qs = _swizzle(x[..., 2:].reshape(T, U, 16, 16, 16), lambda s: s & 6).reshape(T, U, 4096)
         planes = [qs, d]
     else:
-        ub = 144 if qtype == QT_Q4_K else 210
+        ub = 144 if qtype in (QT_Q4_K, QT_G4) else 210
         full = torch.zeros(T * 16, U * ub, dtype=torch.uint8, device=buf.device)
         full[:rows] = m
         x = full.view(T, 16, U, ub).permute(0, 2, 1, 3)[:, :, SLOT_ROWS]  # [T,U,16,ub]
-        if qtype == QT_Q4_K:
+        if qtype in (QT_Q4_K, QT_G4):  # 16-byte header (K-quant scales, or G4's two (s, m) pairs)
             hdr = x[..., :16].reshape(T, U, 256)
             qs = _swizzle(x[..., 16:144].reshape(T, U, 16, 8, 16), lambda s: s & 6).reshape(T, U, 2048)
             planes = [hdr, qs]

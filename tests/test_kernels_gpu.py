@@ -12,6 +12,8 @@ from fak_b200.gguf.constants import GGMLType
 pytestmark = pytest.mark.gpu
 
 QTYPES = [(GGMLType.Q8_0, 32), (GGMLType.Q4_K, 256), (GGMLType.Q6_K, 256)]
+# G4 (AWQ / GPTQ group-int4) runs only tile-packed (tgemv) and through the dequantizer
+QTYPES_TILE = QTYPES + [(GGMLType.G4, 256)]
 
 
 def _ext():
@@ -26,7 +28,7 @@ def _swiglu_ref(y):
     return (torch.nn.functional.silu(blocks[:, :, 0]) * blocks[:, :, 1]).reshape(M, N // 2)
 
 
-@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("qt,blk", QTYPES_TILE)
 def test_quantize_matches_numpy_bitexact(qt, blk):
     rng = np.random.default_rng(1)
     x = (rng.standard_normal((64, 4 * 256)) * 0.02).astype(np.float32)
@@ -42,7 +44,7 @@ def test_quantize_matches_numpy_bitexact(qt, blk):
     assert match > 0.9, match
 
 
-@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("qt,blk", QTYPES_TILE)
 def test_dequantize_rows(qt, blk):
     from fak_b200.ops import quant as dq
     rng = np.random.default_rng(2)
@@ -260,7 +262,7 @@ def _tg_case(qt, N, Kd, B, seed=3):
     return w, Wd, x, act
 
 
-@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("qt,blk", QTYPES_TILE)
 @pytest.mark.parametrize("B", [1, 5, 8, 13, 32])
 @pytest.mark.parametrize("epi", [0, 1, 2])
 @pytest.mark.parametrize("N", [576, 16 * 2400])
@@ -287,7 +289,7 @@ def test_tgemv_tile_packed(qt, blk, B, epi, N):
     assert cos > tol_cos and err < tol_err, (cos, err)
 
 
-@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("qt,blk", QTYPES_TILE)
 def test_tgemv_batch_invariant_and_repeatable(qt, blk):
     """Each token's output is bit-identical whether it runs alone or in a batch of 8 or 32, and the
     split-K tickets are left at zero so a second launch gives the same bits."""
@@ -336,7 +338,7 @@ def test_decode_attention_fused_merge_bitexact(D, H, Hkv):
         assert torch.equal(o[0], outs[0][0]) and torch.equal(o[1], outs[0][1]) and torch.equal(o[2], outs[0][2])
 
 
-@pytest.mark.parametrize("qt,blk", QTYPES)
+@pytest.mark.parametrize("qt,blk", QTYPES_TILE)
 @pytest.mark.parametrize("norm", [False, True])
 @pytest.mark.parametrize("N", [576, 16 * 2400])
 def test_tgemv_fp32_input_fused_norm(qt, blk, norm, N):
