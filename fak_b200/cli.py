@@ -51,12 +51,20 @@ def build_model_backend(args):
         if hf:
             from .models.hf import load_reference_tensors_hf
             cfg, tensors = load_reference_tensors_hf(hf)
-            return ReferenceBackend(ReferenceModel(cfg, tensors),
-                                    Tokenizer.from_tokenizer_json(os.path.join(hf, "tokenizer.json")))
-        if not args.gguf:
+            ref = ReferenceModel(cfg, tensors)
+            tok = Tokenizer.from_tokenizer_json(os.path.join(hf, "tokenizer.json"))
+        elif args.gguf:
+            ref = ReferenceModel.from_gguf(args.gguf)
+            tok = Tokenizer.from_gguf_metadata(open_gguf(args.gguf).metadata)
+        else:
             raise SystemExit("--cpu needs --gguf or --hf")
-        tok = Tokenizer.from_gguf_metadata(open_gguf(args.gguf).metadata)
-        return ReferenceBackend(ReferenceModel.from_gguf(args.gguf), tok)
+        if args.lora:   # applied dynamically after each patched projection
+            from .models.lora import LoRASet, load_peft_adapter
+            ls = LoRASet()
+            for d in args.lora:
+                load_peft_adapter(d, ls)
+            ref.set_lora(ls)
+        return ReferenceBackend(ref, tok)
     import torch
     from .engine import Engine
     from .serve import EngineBackend
@@ -64,10 +72,10 @@ def build_model_backend(args):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     if hf:
-        eng = Engine.from_hf(hf, ecfg, dev, max_context=args.max_context)
+        eng = Engine.from_hf(hf, ecfg, dev, max_context=args.max_context, lora=args.lora)
         tok = Tokenizer.from_tokenizer_json(os.path.join(hf, "tokenizer.json"))
     elif args.gguf:
-        eng = Engine.from_gguf(args.gguf, ecfg, dev, max_context=args.max_context)
+        eng = Engine.from_gguf(args.gguf, ecfg, dev, max_context=args.max_context, lora=args.lora)
         tok = Tokenizer.from_gguf_metadata(open_gguf(args.gguf).metadata)
     else:
         import tempfile
@@ -89,6 +97,8 @@ def _add_model_args(ap):
     ap.add_argument("--gguf", help="GGUF checkpoint (Q4_K/Q6_K/Q8_0/f16/f32 blocks)")
     ap.add_argument("--hf", help="Hugging Face checkpoint directory (config.json, *.safetensors, tokenizer.json); "
                                  "float weights are quantized to Q8_0 on load")
+    ap.add_argument("--lora", action="append", default=[],
+                    help="PEFT LoRA adapter directory (repeatable; merged into the device weights at load)")
     ap.add_argument("--synthetic", default="tiny-qwen2", help="random-init preset when no --gguf is given")
     ap.add_argument("--mix", default="q4_k_m")
     ap.add_argument("--cpu", action="store_true", help="fp32 reference forward on the CPU")

@@ -108,20 +108,35 @@ class Engine:
         import torch.distributed as dist
         return dist.get_rank(tp_group), dist.get_world_size(tp_group)
 
+    @staticmethod
+    def _with_lora(source, lora):
+        """lora: adapter directories (merged into the weights at load) or a models.lora.LoRASet."""
+        if not lora:
+            return source
+        from ..models.lora import LoRASet, load_peft_adapter, merged_source
+        if not isinstance(lora, LoRASet):
+            s = LoRASet()
+            for d in ([lora] if isinstance(lora, str) else lora):
+                load_peft_adapter(d, s)
+            lora = s
+        return merged_source(source, lora)
+
     @classmethod
-    def from_gguf(cls, path: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None, **kw) -> "Engine":
+    def from_gguf(cls, path: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None, lora=None,
+                  **kw) -> "Engine":
         r, n = cls._tp(tp_group)
-        w = load_weights(gguf_source(path), device, tp_rank=r, tp_size=n,
+        w = load_weights(cls._with_lora(gguf_source(path), lora), device, tp_rank=r, tp_size=n,
                          prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 
     @classmethod
-    def from_hf(cls, model_dir: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None,
+    def from_hf(cls, model_dir: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None, lora=None,
                 **kw) -> "Engine":
-        """Hugging Face checkpoint directory (safetensors); float matrices are quantized to Q8_0."""
+        """Hugging Face checkpoint directory (safetensors); float matrices are quantized to Q8_0,
+        AWQ / GPTQ int4 layers run as G4 blocks."""
         from ..models.hf import hf_source
         r, n = cls._tp(tp_group)
-        w = load_weights(hf_source(model_dir), device, tp_rank=r, tp_size=n,
+        w = load_weights(cls._with_lora(hf_source(model_dir), lora), device, tp_rank=r, tp_size=n,
                          prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 

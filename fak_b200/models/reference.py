@@ -61,6 +61,19 @@ class ReferenceModel:
         self.cfg = cfg
         self.device = torch.device(device)
         self.t = {k: v.to(self.device, torch.float32) for k, v in tensors.items()}
+        self.lora = None   # models.lora.LoRASet applied dynamically after each patched projection
+
+    def set_lora(self, lora_set) -> None:
+        self.lora = lora_set
+
+    def mm(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        """x @ W^T (+ the active LoRA deltas of W)."""
+        y = x @ self.t[name].T
+        if self.lora is not None:
+            d = self.lora.delta(name, x)
+            if d is not None:
+                y = y + d
+        return y
 
     @classmethod
     def from_gguf(cls, path_or_file, device: str | torch.device = "cpu") -> "ReferenceModel":
@@ -81,9 +94,9 @@ class ReferenceModel:
     def _ffn(self, i: int, x: torch.Tensor) -> torch.Tensor:
         cfg, p = self.cfg, f"blk.{i}."
         if not cfg.is_moe:
-            g = x @ self.w(p + "ffn_gate.weight").T
-            u = x @ self.w(p + "ffn_up.weight").T
-            return (torch.nn.functional.silu(g) * u) @ self.w(p + "ffn_down.weight").T
+            g = self.mm(x, p + "ffn_gate.weight")
+            u = self.mm(x, p + "ffn_up.weight")
+            return self.mm(torch.nn.functional.silu(g) * u, p + "ffn_down.weight")
         wts, idx = moe_route(x @ self.w(p + "ffn_gate_inp.weight").T, cfg.n_experts_used, cfg.norm_topk_prob)
         G, U, D = self.w(p + "ffn_gate_exps.weight"), self.w(p + "ffn_up_exps.weight"), self.w(p + "ffn_down_exps.weight")
         out = torch.zeros_like(x)
@@ -116,9 +129,9 @@ class ReferenceModel:
         for i in range(l0, l1):
             p = f"blk.{i}."
             h = rmsnorm(x, self.w(p + "attn_norm.weight"), cfg.rms_eps)
-            q = h @ self.w(p + "attn_q.weight").T
-            k = h @ self.w(p + "attn_k.weight").T
-            v = h @ self.w(p + "attn_v.weight").T
+            q = self.mm(h, p + "attn_q.weight")
+            k = self.mm(h, p + "attn_k.weight")
+            v = self.mm(h, p + "attn_v.weight")
             if cfg.qkv_bias:
                 q = q + self.w(p + "attn_q.bias")
                 k = k + self.w(p + "attn_k.bias")
@@ -141,7 +154,7 @@ class ReferenceModel:
             else:
                 K, V = k, v
             a = attention(q, K, V, start_pos)
-            x = x + a.reshape(T, H * D) @ self.w(p + "attn_output.weight").T
+            x = x + self.mm(a.reshape(T, H * D), p + "attn_output.weight")
             h = rmsnorm(x, self.w(p + "ffn_norm.weight"), cfg.rms_eps)
             x = x + self._ffn(i, h)
         return x

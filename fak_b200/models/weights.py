@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import dataclasses
 import os
+import warnings
 from typing import Callable, Iterator
 
 import numpy as np
@@ -140,7 +141,9 @@ def gguf_source(path: str) -> tuple[ModelConfig, RawGetter, Callable[[], None]]:
         if cfg.arch == "llama" and (name.endswith("attn_q.weight") or name.endswith("attn_k.weight")):
             heads = cfg.n_heads if name.endswith("attn_q.weight") else cfg.n_kv_heads
             raw = llama_rope_unpermute_rows(raw, heads, cfg.head_dim)
-        return ti.shape, int(ti.ggml_type), torch.from_numpy(np.ascontiguousarray(raw))
+        with warnings.catch_warnings():   # read-only memory map: the rows are only read
+            warnings.simplefilter("ignore", UserWarning)
+            return ti.shape, int(ti.ggml_type), torch.from_numpy(np.ascontiguousarray(raw))
 
     return cfg, get, g.close
 

@@ -32,6 +32,47 @@ def test_prefill_logits_match_reference(model_file):
     eng = _engine(model_file, graphs=False)
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, eng.cfg.vocab_size, 77).tolist()
+    logits = _prefill_logits(eng, prompt)
+    want = ref.forward(torch.tensor(prompt))[-1]
+    cos = torch.nn.functional.cosine_similarity(logits[0], want, dim=0).item()
+    assert cos > 0.995, cos
+
+
+def test_lora_merged_engine_matches_dynamic_reference(tmp_path):
+    """A PEFT adapter merged into the device weights at load gives the logits of the fp32 reference
+    applying the same adapter dynamically."""
+    import json
+    from fak_b200.engine import Engine
+    from fak_b200.models.hf import write_safetensors
+    from fak_b200.models.lora import load_peft_adapter
+    from fak_b200.models.reference import ReferenceModel
+    cfg = preset("tiny-llama")
+    path = str(tmp_path / "m.gguf")
+    write_synthetic_gguf(path, cfg, "q8_0", seed=5, std=0.05)
+    g = torch.Generator().manual_seed(3)
+    t = {}
+    for mod, (i, o) in {"model.layers.0.self_attn.q_proj": (cfg.d_model, cfg.q_dim),
+                        "model.layers.1.mlp.up_proj": (cfg.d_model, cfg.ffn_dim)}.items():
+        t[f"base_model.model.{mod}.lora_A.weight"] = torch.randn(8, i, generator=g) * 0.2
+        t[f"base_model.model.{mod}.lora_B.weight"] = torch.randn(o, 8, generator=g) * 0.2
+    ad = tmp_path / "adapter"
+    ad.mkdir()
+    write_safetensors(str(ad / "adapter_model.safetensors"), t)
+    (ad / "adapter_config.json").write_text(json.dumps({"r": 8, "lora_alpha": 16, "peft_type": "LORA"}))
+    eng = Engine.from_gguf(path, EngineConfig(max_batch=8, kv_pages=512, cuda_graph=False), "cuda",
+                           max_context=1024, lora=[str(ad)])
+    ref = ReferenceModel.from_gguf(path, "cuda")
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, 40).tolist()
+    base = ref.forward(torch.tensor(prompt))[-1]
+    ref.set_lora(load_peft_adapter(str(ad)))
+    want = ref.forward(torch.tensor(prompt))[-1]
+    got = _prefill_logits(eng, prompt)[0]
+    cos = torch.nn.functional.cosine_similarity(got, want, dim=0).item()
+    cos_base = torch.nn.functional.cosine_similarity(got, base, dim=0).item()
+    assert cos > 0.995 and cos_base < cos, (cos, cos_base)
+
+
+def _prefill_logits(eng, prompt):
     r = eng.add_request(prompt, 1)
     eng._admit()
     # run the prefill by hand to capture logits
@@ -42,11 +83,8 @@ def test_prefill_logits_match_reference(model_file):
     slot = (pages[pos.cpu().long() // ps] * ps + pos.cpu().long() % ps).int().cuda()
     bt = torch.tensor([r.pages], dtype=torch.int32, device="cuda")
     meta = PrefillMeta.build([len(prompt)], [0], "cuda")
-    logits = eng.runner.prefill(torch.tensor(prompt, dtype=torch.int32, device="cuda"), pos, slot, bt, meta,
-                                torch.tensor([len(prompt) - 1], dtype=torch.int32, device="cuda"))
-    want = ref.forward(torch.tensor(prompt))[-1]
-    cos = torch.nn.functional.cosine_similarity(logits[0], want, dim=0).item()
-    assert cos > 0.995, cos
+    return eng.runner.prefill(torch.tensor(prompt, dtype=torch.int32, device="cuda"), pos, slot, bt, meta,
+                              torch.tensor([len(prompt) - 1], dtype=torch.int32, device="cuda"))
 
 
 @pytest.mark.parametrize("graphs", [False, True])
