@@ -41,6 +41,10 @@ class ModelConfig:
     # context-extension RoPE scaling as sorted (key, value) pairs (hashable; a dict is accepted):
     # type linear|yarn|llama3, factor, original_max_position_embeddings, beta_fast/slow, ...
     rope_scaling: tuple | None = None
+    # sliding-window attention: each query sees the last ``sliding_window`` keys (0 = full causal)
+    # on the layers in ``swa_layers`` (None = every layer)
+    sliding_window: int = 0
+    swa_layers: tuple | None = None
     bos_token_id: int = 1
     eos_token_id: int = 2
     name: str = ""
@@ -65,6 +69,17 @@ class ModelConfig:
         if isinstance(self.rope_scaling, dict):
             items = ((k, tuple(v) if isinstance(v, list) else v) for k, v in self.rope_scaling.items())
             object.__setattr__(self, "rope_scaling", tuple(sorted(items)) or None)
+
+    def layer_window(self, i: int) -> int:
+        if self.sliding_window <= 0:
+            return 0
+        return self.sliding_window if self.swa_layers is None or i in self.swa_layers else 0
+
+    def max_window(self) -> int:
+        """The widest window when EVERY layer is windowed (keys older than it are never read
+        again), else 0."""
+        ws = [self.layer_window(i) for i in range(self.n_layers)]
+        return max(ws) if ws and min(ws) > 0 else 0
 
     def validate(self) -> None:
         if self.n_heads % self.n_kv_heads:
@@ -156,6 +171,7 @@ def config_from_gguf_metadata(meta: dict[str, Any], tensor_shapes: dict[str, tup
         rms_eps=float(f"{float(g('attention.layer_norm_rms_epsilon', 1e-5)):.6g}"),
         rope_theta=float(f"{float(g('rope.freq_base', 10000.0)):.7g}"),
         rope_scaling=_gguf_rope_scaling(g),
+        sliding_window=int(g("attention.sliding_window", 0) or 0),
         tie_embeddings=tied,
         qkv_bias=qkv_bias,
         qk_norm=qk_norm,

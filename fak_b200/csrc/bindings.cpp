@@ -11,10 +11,10 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
-                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch);
+                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window);
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
-                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out);
+                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window);
 void embed(torch::Tensor table, int64_t qtype, int64_t pitch, int64_t V, int64_t d, torch::Tensor ids,
            c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> out_bf16,
            c10::optional<torch::Tensor> err);
@@ -71,8 +71,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("block_table"), pybind11::arg("ctx_len"), pybind11::arg("n_split"),
         pybind11::arg("pages_per_split"), pybind11::arg("out"), pybind11::arg("qx"), pybind11::arg("ds"),
         pybind11::arg("workspace"), pybind11::arg("ldo") = 0, pybind11::arg("tickets") = pybind11::none(),
-        pybind11::arg("prefetch") = pybind11::none());
-  m.def("prefill_attention", &prefill_attention);
+        pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("window") = 0);
+  m.def("prefill_attention", &prefill_attention, pybind11::arg("q"), pybind11::arg("k_cache"),
+        pybind11::arg("v_cache"), pybind11::arg("block_table"), pybind11::arg("tile_seq"), pybind11::arg("tile_q0"),
+        pybind11::arg("seq_qoff"), pybind11::arg("seq_qlen"), pybind11::arg("seq_pos0"), pybind11::arg("n_tiles"),
+        pybind11::arg("out"), pybind11::arg("window") = 0);
   m.def("embed", &embed);
   m.def("rope_kv", &rope_kv);
   m.def("rmsnorm_bf16", &rmsnorm_bf16);

@@ -68,7 +68,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
               int n_split, int pages_per_split, float scale_log2, float* __restrict__ part_o,
               float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
               float2* __restrict__ ds, int ldo, int* __restrict__ tickets, const uint8_t* __restrict__ pf,
-              int64_t pf_bytes) {
+              int64_t pf_bytes, int win) {
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -82,9 +82,13 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   pdl_wait();
   const int ctx = ctx_len[b];
   const int n_pages = (ctx + PAGE - 1) / PAGE;
+  // sliding window (win > 0): the query at ctx - 1 sees keys [ctx - win, ctx); pages before the
+  // window are never read
+  const int lo = win > 0 ? max(0, ctx - win) : 0;
+  const int pg0 = lo / PAGE;
   // pages per split follow the live context so every split gets an even share of the pages
-  const int pps = max(pages_per_split, (n_pages + n_split - 1) / n_split);
-  const int p_begin = split * pps;
+  const int pps = max(pages_per_split, (n_pages - pg0 + n_split - 1) / n_split);
+  const int p_begin = pg0 + split * pps;
   const int p_end = min(n_pages, p_begin + pps);
 
   // Q fragments (rows = query heads of this group, zero beyond G)
@@ -158,13 +162,13 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
         mma_bf16_16816(s[1], qa[ks], r2, r3);
       }
     }
-    const int valid = min(PAGE, ctx - p * PAGE);
+    const int valid = min(PAGE, ctx - p * PAGE), first = lo - p * PAGE;
 #pragma unroll
     for (int j = 0; j < 2; j++) {
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         int tok = 8 * j + 2 * tq + (e & 1);
-        s[j][e] = tok < valid ? s[j][e] * scale_log2 : NEG_INF;
+        s[j][e] = (tok < valid && tok >= first) ? s[j][e] * scale_log2 : NEG_INF;
       }
     }
     float mx0 = quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1])));
@@ -331,7 +335,7 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
                const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_table, int bt_stride,
                const int* __restrict__ tile_seq, const int* __restrict__ tile_q0, const int* __restrict__ seq_qoff,
                const int* __restrict__ seq_qlen, const int* __restrict__ seq_pos0, int H, int Hkv, float scale_log2,
-               __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+               __nv_bfloat16* __restrict__ out, int64_t out_stride, int win) {
   constexpr int KS = D / 16;
   constexpr int NT = D / 8;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -384,8 +388,11 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
     cp_async_commit();
   };
 
-  if (n_kv_tiles > 0) issue_tile(0, 0);
-  for (int kt = 0; kt < n_kv_tiles; kt++) {
+  // sliding window (win > 0): row qp sees keys (qp - win, qp]; key tiles below the first row's
+  // window are skipped
+  const int kt0 = win > 0 ? max(0, pos0 + q0 - win + 1) / PF_KV : 0;
+  if (kt0 < n_kv_tiles) issue_tile(kt0, kt0 & 1);
+  for (int kt = kt0; kt < n_kv_tiles; kt++) {
     const int buf = kt & 1;
     if (kt + 1 < n_kv_tiles) {
       issue_tile(kt + 1, buf ^ 1);
@@ -417,7 +424,7 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
       for (int e = 0; e < 4; e++) {
         int kp = kt * PF_KV + 8 * j + 2 * tq + (e & 1);
         int qp = (e < 2) ? qpos0 : qpos1;
-        s[j][e] = (kp <= qp && kp < kv_end) ? s[j][e] * scale_log2 : NEG_INF;
+        s[j][e] = (kp <= qp && kp < kv_end && (win <= 0 || kp > qp - win)) ? s[j][e] * scale_log2 : NEG_INF;
       }
     }
     float mx0 = NEG_INF, mx1 = NEG_INF;
@@ -494,11 +501,12 @@ void set_pdl(cudaLaunchConfig_t& cfg) {
 // q [B,H,D] f32; caches [P,Hkv,16,D] bf16; block_table [B, *] int32; ctx_len [B] int32.
 // Writes out [B,H*D] f32 (optional) and/or the int8 quantized output (qx [B,H*D], ds [B,H*D/32,2]).
 // workspace: f32 buffer of at least B*H*n_split*(D+2) floats when n_split > 1.
+// window > 0: sliding-window attention (the last ``window`` keys of each sequence).
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
-                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch) {
+                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window) {
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
   const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
@@ -550,7 +558,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
                                       H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb));
+                                      pfp, pfb, (int)window));
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -559,7 +567,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
                                       H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb));
+                                      pfp, pfb, (int)window));
   }
   if (n_split > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
@@ -580,7 +588,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
 // Per-tile metadata (int32, device): tile_seq, tile_q0; per-sequence: seq_qoff, seq_qlen, seq_pos0.
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
-                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out) {
+                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.stride(2) == 1, "q [T,H,D] bf16");
   TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
   int H = (int)q.size(1), D = (int)q.size(2), Hkv = (int)k_cache.size(1);
@@ -604,7 +612,7 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
         (const __nv_bfloat16*)v_cache.data_ptr(), (const int*)block_table.data_ptr<int>(), (int)block_table.stride(0),
         (const int*)tile_seq.data_ptr<int>(), (const int*)tile_q0.data_ptr<int>(), (const int*)seq_qoff.data_ptr<int>(),
         (const int*)seq_qlen.data_ptr<int>(), (const int*)seq_pos0.data_ptr<int>(), H, Hkv, scale_log2,
-        (__nv_bfloat16*)out.data_ptr(), (int64_t)out.stride(0)));
+        (__nv_bfloat16*)out.data_ptr(), (int64_t)out.stride(0), (int)window));
   };
   if (D == 128) args(k_prefill_attn<128>, sizeof(PrefillSmem<128>));
   else args(k_prefill_attn<64>, sizeof(PrefillSmem<64>));
@@ -719,14 +727,14 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     e = cudaFuncSetAttribute(k_decode_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<128>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0);
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
     e = cudaFuncSetAttribute(k_decode_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<64>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0);
   }
   if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode attention launch: %s", cudaGetErrorString(e));
   if (n_split > 1) {

@@ -9,6 +9,8 @@ llama.cpp's naming conventions:
 * ``q4_k_m`` -- Q4_K everywhere except ``output.weight`` (Q6_K) and the
   ``attn_v`` / ``ffn_down`` weights of layers picked by ``use_more_bits``
   (Q6_K), which is how llama.cpp's Q4_K_M recipe spends extra bits.
+* ``g4``     -- AWQ / GPTQ-style int4 (G4 blocks, groups of 128) for the layer matrices, Q8_0
+  embeddings and LM head.
 * ``f32`` / ``f16`` / ``bf16`` -- unquantized.
 
 Rows whose length is not a multiple of 256 cannot hold K-quant blocks and fall
@@ -191,7 +193,8 @@ def synthetic_vocab(cfg: ModelConfig) -> tuple[list[str], list[int], list[str]]:
 
 
 _FILE_TYPE = {"q8_0": FILE_TYPE_MOSTLY_Q8_0, "q4_k_m": FILE_TYPE_MOSTLY_Q4_K_M, "f32": FILE_TYPE_ALL_F32,
-              "f16": FILE_TYPE_MOSTLY_F16, "bf16": FILE_TYPE_MOSTLY_BF16}
+              "f16": FILE_TYPE_MOSTLY_F16, "bf16": FILE_TYPE_MOSTLY_BF16,
+              "g4": 1024}   # no llama.cpp file type holds G4 blocks: 1024 is llama.cpp's "guessed"
 
 
 def write_metadata(w: GGUFWriter, cfg: ModelConfig, mix: str, with_vocab: bool = True) -> None:
@@ -209,6 +212,15 @@ def write_metadata(w: GGUFWriter, cfg: ModelConfig, mix: str, with_vocab: bool =
     w.add(f"{a}.attention.value_length", cfg.head_dim, ValueType.UINT32)
     w.add(f"{a}.attention.layer_norm_rms_epsilon", float(cfg.rms_eps), ValueType.FLOAT32)
     w.add(f"{a}.rope.freq_base", float(cfg.rope_theta), ValueType.FLOAT32)
+    if cfg.sliding_window > 0 and cfg.swa_layers is None:   # every layer windowed
+        w.add(f"{a}.attention.sliding_window", int(cfg.sliding_window), ValueType.UINT32)
+    if cfg.rope_scaling:
+        rs = dict(cfg.rope_scaling)
+        w.add(f"{a}.rope.scaling.type", str(rs.get("type") or rs.get("rope_type")))
+        w.add(f"{a}.rope.scaling.factor", float(rs.get("factor", 1.0)), ValueType.FLOAT32)
+        if "original_max_position_embeddings" in rs:
+            w.add(f"{a}.rope.scaling.original_context_length", int(rs["original_max_position_embeddings"]),
+                  ValueType.UINT32)
     w.add(f"{a}.vocab_size", cfg.vocab_size, ValueType.UINT32)
     if cfg.is_moe:
         w.add(f"{a}.expert_count", cfg.n_experts, ValueType.UINT32)

@@ -104,11 +104,30 @@ def config_from_hf(hf: dict) -> ModelConfig:
         norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
         max_context=int(hf.get("max_position_embeddings", 32768)),
         rope_scaling=_hf_rope_scaling(rp),
+        **_hf_sliding_window(hf, int(hf["num_hidden_layers"])),
         bos_token_id=int(hf.get("bos_token_id") or 1), eos_token_id=int(hf.get("eos_token_id") or 2),
         name=str(hf.get("_name_or_path", arch_name)),
     )
     cfg.validate()
     return cfg
+
+
+def _hf_sliding_window(hf: dict, n_layers: int) -> dict:
+    """Mistral: ``sliding_window`` on every layer; Qwen2: ``use_sliding_window`` from layer
+    ``max_window_layers`` on; configs with ``layer_types``: the "sliding_attention" layers."""
+    w = int(hf.get("sliding_window") or 0)
+    if w <= 0:
+        return {}
+    types = hf.get("layer_types")
+    if types:
+        layers = tuple(i for i, t in enumerate(types) if t == "sliding_attention")
+        return {"sliding_window": w, "swa_layers": layers} if layers else {}
+    if "use_sliding_window" in hf:
+        if not hf["use_sliding_window"]:
+            return {}
+        first = int(hf.get("max_window_layers", 0) or 0)
+        return {"sliding_window": w, "swa_layers": tuple(range(first, n_layers))}
+    return {"sliding_window": w}
 
 
 def _hf_rope_scaling(rs: dict | None) -> dict | None:

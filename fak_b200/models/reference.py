@@ -153,7 +153,7 @@ class ReferenceModel:
                 K, V = kv[j]
             else:
                 K, V = k, v
-            a = attention(q, K, V, start_pos)
+            a = attention(q, K, V, start_pos, cfg.layer_window(i))
             x = x + self.mm(a.reshape(T, H * D), p + "attn_output.weight")
             h = rmsnorm(x, self.w(p + "ffn_norm.weight"), cfg.rms_eps)
             x = x + self._ffn(i, h)
@@ -174,8 +174,9 @@ class ReferenceModel:
         return out
 
 
-def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int) -> torch.Tensor:
-    """q [T,H,D] at positions start_pos..; K,V [Tctx,Hk,D] covering positions 0..Tctx-1 (causal)."""
+def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int, window: int = 0) -> torch.Tensor:
+    """q [T,H,D] at positions start_pos..; K,V [Tctx,Hk,D] covering positions 0..Tctx-1 (causal;
+    window > 0: each query sees keys (qpos - window, qpos])."""
     T, H, D = q.shape
     Tc, Hk, _ = K.shape
     g = H // Hk
@@ -184,7 +185,10 @@ def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int)
     s = torch.einsum("thd,chd->htc", q.float(), Kx.float()) / math.sqrt(D)
     qpos = torch.arange(start_pos, start_pos + T, device=q.device)[:, None]
     kpos = torch.arange(Tc, device=q.device)[None, :]
-    s = s.masked_fill((kpos > qpos)[None], float("-inf"))
+    masked = kpos > qpos
+    if window > 0:
+        masked = masked | (kpos <= qpos - window)
+    s = s.masked_fill(masked[None], float("-inf"))
     pr = torch.softmax(s, dim=-1)
     return torch.einsum("htc,chd->thd", pr, Vx.float())
 

@@ -168,7 +168,7 @@ class ModelRunner:
         if self.coll is None:
             K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_attn,
                                workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None,
-                               prefetch=self._pf(L.o))
+                               prefetch=self._pf(L.o), window=cfg.layer_window(i))
             K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD, prefetch=self._pf(L.gate_up))
         else:
             self.coll.decode_attn_o(self, i, B, bt, ctx, n_split)
@@ -296,7 +296,7 @@ class ModelRunner:
                 K.gemm(hb, seg, qkv[:, off:off + seg.rows], K.EPI_STORE, bias)
             K.rope_kv(qkv, pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
                       None, qb, self.kv.k[i], self.kv.v[i])
-            K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab)
+            K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab, cfg.layer_window(i))
             if self.coll is None:
                 K.gemm(ab, L.o, x, K.EPI_ADD)
             else:

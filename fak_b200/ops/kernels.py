@@ -125,19 +125,21 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 
 
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
-                     workspace=None, ldo: int = 0, tickets=None, prefetch: torch.Tensor | None = None) -> None:
+                     workspace=None, ldo: int = 0, tickets=None, prefetch: torch.Tensor | None = None,
+                     window: int = 0) -> None:
     """ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
     [B * kv heads]; when given, the last split of each (sequence, KV group) merges the splits in the
-    same kernel instead of a separate combine launch (the kernel leaves the tickets at zero)."""
+    same kernel instead of a separate combine launch (the kernel leaves the tickets at zero).
+    window > 0: sliding-window attention over the last ``window`` keys."""
     ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
                            act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo,
-                           tickets, prefetch)
+                           tickets, prefetch, window)
     count(2 if n_split > 1 and tickets is None else 1)
 
 
-def prefill_attention(q, k_cache, v_cache, block_table, meta, out) -> None:
+def prefill_attention(q, k_cache, v_cache, block_table, meta, out, window: int = 0) -> None:
     ext().prefill_attention(q, k_cache, v_cache, block_table, meta.tile_seq, meta.tile_q0, meta.seq_qoff,
-                            meta.seq_qlen, meta.seq_pos0, meta.n_tiles, out)
+                            meta.seq_qlen, meta.seq_pos0, meta.n_tiles, out, window)
     count()
 
 

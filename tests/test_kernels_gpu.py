@@ -130,7 +130,8 @@ def _gather(kc, bt_row, L):
 
 @pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3), (128, 8, 8)])
 @pytest.mark.parametrize("n_split", [1, 7])
-def test_decode_attention(D, H, Hkv, n_split):
+@pytest.mark.parametrize("window", [0, 40])
+def test_decode_attention(D, H, Hkv, n_split, window):
     from fak_b200.ops import kernels as K
     ctx = [1, 17, 100, 333, 1000]
     B = len(ctx)
@@ -140,11 +141,12 @@ def test_decode_attention(D, H, Hkv, n_split):
     act = K.ActQ(B, H * D, "cuda")
     ws = torch.zeros(B * H * n_split * (D + 2), device="cuda")
     K.decode_attention(q, kc, vc, bt, torch.tensor(ctx, dtype=torch.int32, device="cuda"), n_split, out=out, act=act,
-                       workspace=ws)
+                       workspace=ws, window=window)
     torch.cuda.synchronize()
     G = H // Hkv
     for b, L in enumerate(ctx):
-        Kb, Vb = _gather(kc, bt[b], L), _gather(vc, bt[b], L)
+        lo = max(0, L - window) if window else 0   # sliding window: the last `window` keys
+        Kb, Vb = _gather(kc, bt[b], L)[lo:], _gather(vc, bt[b], L)[lo:]
         qb = q[b].bfloat16().float()
         s = torch.einsum("hd,thd->ht", qb, Kb.repeat_interleave(G, 1)) / math.sqrt(D)
         ref = torch.einsum("ht,thd->hd", torch.softmax(s, -1), Vb.repeat_interleave(G, 1)).reshape(-1)
@@ -154,7 +156,8 @@ def test_decode_attention(D, H, Hkv, n_split):
 
 
 @pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3)])
-def test_prefill_attention(D, H, Hkv):
+@pytest.mark.parametrize("window", [0, 50])
+def test_prefill_attention(D, H, Hkv, window):
     from fak_b200.models.runner import PrefillMeta
     from fak_b200.ops import kernels as K
     qlens, pos0s = [70, 5, 130], [0, 40, 300]
@@ -164,7 +167,7 @@ def test_prefill_attention(D, H, Hkv):
     q = torch.randn(T, H, D, device="cuda").bfloat16()
     out = torch.zeros(T, H * D, device="cuda", dtype=torch.bfloat16)
     meta = PrefillMeta.build(qlens, pos0s, "cuda")
-    K.prefill_attention(q, kc, vc, bt, meta, out)
+    K.prefill_attention(q, kc, vc, bt, meta, out, window)
     torch.cuda.synchronize()
     G = H // Hkv
     off = 0
@@ -175,7 +178,8 @@ def test_prefill_attention(D, H, Hkv):
         sc = torch.einsum("qhd,thd->hqt", qs, Kb) / math.sqrt(D)
         qpos = torch.arange(p0, p0 + ql, device="cuda")[:, None]
         kpos = torch.arange(p0 + ql, device="cuda")[None, :]
-        sc = sc.masked_fill((kpos > qpos)[None], float("-inf"))
+        masked = (kpos > qpos) | ((kpos <= qpos - window) if window else torch.zeros_like(kpos > qpos))
+        sc = sc.masked_fill(masked[None], float("-inf"))
         ref = torch.einsum("hqt,thd->qhd", torch.softmax(sc, -1), Vb).reshape(ql, -1)
         got = out[off:off + ql].float()
         assert torch.allclose(got, ref, atol=3e-2, rtol=3e-2), (s, (got - ref).abs().max())

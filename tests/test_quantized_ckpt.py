@@ -136,3 +136,16 @@ def test_quantized_llama_logits_match_transformers(method, tmp_path):
         want = m(ids[None]).logits[0]
     got = ref.forward(ids)
     assert torch.allclose(got, want, atol=3e-4, rtol=1e-4), (got - want).abs().max()
+
+
+def test_g4_synthetic_gguf_loads_in_the_reference(tmp_path):
+    from fak_b200.config import preset
+    from fak_b200.gguf.synth import write_synthetic_gguf
+    from fak_b200.models.loader import load_reference_tensors
+    path = str(tmp_path / "g4.gguf")
+    write_synthetic_gguf(path, preset("tiny-qwen2"), "g4", seed=1, std=0.05)
+    from fak_b200.gguf import open_gguf
+    types = {int(t.ggml_type) for t in open_gguf(path).tensors.values()}
+    assert int(GGMLType.G4) in types and int(GGMLType.Q8_0) in types
+    cfg, tensors = load_reference_tensors(path)
+    assert tensors["blk.0.attn_q.weight"].shape == (cfg.q_dim, cfg.d_model)
