@@ -42,12 +42,14 @@ FAK_DEV float quad_sum(float v) {
   return v;
 }
 
-// quantize one 32-wide block held one value per lane; writes int8 codes and (scale, sum)
+// quantize one 32-wide block held one value per lane; writes int8 codes and (scale, sum of the
+// dequantized values d * sum(codes))
 FAK_DEV void warp_quant_store(float v, int8_t* qdst, float2* dsdst, int lane) {
   float amax = warp_max(fabsf(v));
-  float s = warp_sum(v);
   float d = amax / 127.f;
-  qdst[lane] = (int8_t)(d > 0.f ? rintf(v / d) : 0.f);
+  const float q = d > 0.f ? rintf(v / d) : 0.f;
+  const float s = warp_sum(q) * d;
+  qdst[lane] = (int8_t)q;
   if (lane == 0) *dsdst = make_float2(d, s);
 }
 

@@ -3,7 +3,7 @@
 // W keeps its GGML block layout (Q4_K 144 B / Q6_K 210 B / Q8_0 34 B per block) with rows at a
 // 16-byte-aligned pitch.  Activations arrive pre-quantized to int8 per 32-element block with a
 // float2 (scale, exact float sum) per block, so every inner product is an integer dp4a:
-//   Q4_K: sum (d*sc*q - dmin*m) * x  =  d*sc*dx * sum(q*qx)  -  dmin*m * sum(x)
+//   Q4_K: sum (d*sc*q - dmin*m) * x  ~  d*sc*dx * sum(q*qx)  -  dmin*m * dx * sum(qx)
 //   Q6_K: d*sc * dx * sum((q-32)*qx)         Q8_0: dw*dx * sum(qw*qx)
 // (the reference's Q8 CUDA lane quantizes activations the same per-block way,
 //  internal/compute/cuda_kernels.cu:374-427; its Q4_K lane keeps f32 activations, :478-526).

@@ -1,14 +1,14 @@
 // Quantized matrix x (few tokens) product on the integer tensor cores, for decode batches.
 //
 // y[b, n] = sum_k W[n, k] x[b, k], W in GGML Q4_K / Q6_K / Q8_0 blocks (16-byte row pitch),
-// x pre-quantized to int8 per 32-element block with (scale, exact sum) per block, B <= 8.
+// x pre-quantized to int8 per 32-element block with (scale, sum of the dequantized block), B <= 8.
 //
 // Each CTA owns one 16-row tile; its 8 warps split K.  Per quantization sub-block the weights
 // of the 16 rows form the A operand of an integer MMA (m16n8k32 for 32-element sub-blocks,
 // m16n8k16 for Q6_K's 16-element ones) and the 8 token columns the B operand, so one
 // instruction does 16 x 8 x 32 multiply-adds; the int32 fragment is then scaled by
 // (weight block scale x activation block scale) and accumulated in fp32:
-//   Q4_K:  d*sc * dx * sum(q*qx)  -  dmin*m * sum(x)       (q in 0..15)
+//   Q4_K:  d*sc * dx * sum(q*qx)  -  dmin*m * dx * sum(qx)  (q in 0..15)
 //   Q6_K:  d*sc * dx * sum((q-32)*qx)
 //   Q8_0:  dw * dx * sum(qw*qx)
 // The k order inside a sub-block is free (it is summed), so each thread loads 8 contiguous
@@ -379,9 +379,10 @@ __global__ void k_quant_act_wide(const float* __restrict__ x, int64_t ldx, const
   float v = xr[i] * inv;
   if (gamma) v *= gamma[i];
   float amax = warp_max(fabsf(v));
-  float s = warp_sum(v);
   float d = amax / 127.f;
-  qx[(int64_t)b * K + i] = (int8_t)(d > 0.f ? rintf(v / d) : 0.f);
+  const float q = d > 0.f ? rintf(v / d) : 0.f;
+  const float s = warp_sum(q) * d;  // sum of the dequantized values (exact integer sum x scale)
+  qx[(int64_t)b * K + i] = (int8_t)q;
   if (lane == 0) ds[(int64_t)b * (K / 32) + blk] = make_float2(d, s);
 }
 

@@ -235,7 +235,9 @@ __global__ void k_dequant(const uint8_t* __restrict__ w, int qtype, int64_t rows
 }
 
 // ------------------------------------------------------------------------------------------
-// activation quantizer: x [B,K] fp32 -> qx int8 [B,K], ds float2 [B,K/32] = (scale, sum(x))
+// activation quantizer: x [B,K] fp32 -> qx int8 [B,K], ds float2 [B,K/32] = (scale, scale * sum(qx)):
+// the offset term of K-quant / G4 weights then uses the same quantized values as the dot product
+// (an exact-sum offset with quantized products nearly doubles the rounding error of offset formats)
 // optional fused RMSNorm (gamma != nullptr).  One CTA per row, 256 threads.
 // ------------------------------------------------------------------------------------------
 __global__ void k_quant_act(const float* __restrict__ x, int64_t ldx, const float* __restrict__ gamma, float eps,
@@ -266,9 +268,9 @@ __global__ void k_quant_act(const float* __restrict__ x, int64_t ldx, const floa
     float v = xr[i] * inv;
     if (gamma) v *= gamma[i];
     float amax = warp_max(fabsf(v));
-    float s = warp_sum(v);
     float d = amax / 127.f;
     float q = d > 0.f ? rintf(v / d) : 0.f;
+    float s = warp_sum(q) * d;  // sum of the dequantized values (exact integer sum x scale)
     qx[(int64_t)b * K + i] = (int8_t)q;
     if (lane == 0) ds[(int64_t)b * (K / 32) + blk] = make_float2(d, s);
   }

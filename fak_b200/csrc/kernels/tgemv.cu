@@ -25,7 +25,7 @@
 // Per 32-element sub-block and thread (rows g, g+8; tokens 2t, 2t+1): one m16n8k32 integer MMA
 // whose accumulator starts at the float-conversion constant 0x4B400000, so the int32 result read
 // as a float is 12582912 + dot exactly (|dot| < 2^22), then
-//   Q4_K  acc += (d*sc) * dx * dot - (dmin*m) * sum(x)     (nibbles via u8 x s8; high nibbles
+//   Q4_K  acc += (d*sc) * dx * dot - (dmin*m) * sum(xq)    (nibbles via u8 x s8; high nibbles
 //                                                           in place, scale pre-divided by 16)
 //   Q6_K  acc += (d*sc) * dx * dot16                        (m16n8k16 per 16-element sub-block;
 //                                                           the -32 offset enters through the
@@ -427,7 +427,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   pdl_wait();
   if (xf != nullptr) {
     // fp32 activations: optional RMSNorm (statistics over the whole row), then int8 per 32-block
-    // with (scale, exact sum) -- the activation quantizer, done while the weight copies fly
+    // with (scale, sum of the dequantized block) -- the activation quantizer, done while the weight copies fly
     __shared__ float s_inv[8 * MAXNT];
     if (gamma != nullptr) {
       for (int b = warp; b < B; b += W) {
@@ -462,20 +462,19 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
           v[4 * j + 2] = f.z * inv * gm.z;
           v[4 * j + 3] = f.w * inv * gm.w;
         }
-        float amax = 0.f, sum = 0.f;
+        float amax = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          amax = fmaxf(amax, fabsf(v[j]));
-          sum += v[j];
-        }
+        for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(v[j]));
         const float d = amax / 127.f;
         const float id = d > 0.f ? 1.f / d : 0.f;
+        int isum = 0;
 #pragma unroll
         for (int j = 0; j < 32; j++) {
-          const uint32_t c = (uint32_t)(int)rintf(v[j] * id) & 0xffu;
-          w[j >> 2] |= c << (8 * (j & 3));
+          const int qc = (int)rintf(v[j] * id);
+          isum += qc;
+          w[j >> 2] |= ((uint32_t)qc & 0xffu) << (8 * (j & 3));
         }
-        dsv = make_float2(d, sum);
+        dsv = make_float2(d, (float)isum * d);  // sum of the dequantized values
       }
       uint4* dst = reinterpret_cast<uint4*>(xs + b * geo.xstride + kk);
       dst[0] = make_uint4(w[0], w[1], w[2], w[3]);

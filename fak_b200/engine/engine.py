@@ -57,6 +57,7 @@ class Request:
     finish_reason: str = ""
     on_token: Callable[[int], None] | None = None
     output_before_preempt: list[int] = dataclasses.field(default_factory=list)  # tokens emitted before a requeue
+    swap: tuple | None = None        # (K, V) of its pages in pinned host memory while swapped out
 
     @property
     def ttft(self) -> float | None:
@@ -93,11 +94,13 @@ class Engine:
                                   attention_merge=self.ecfg.attention_merge, l2_prefetch=self.ecfg.l2_prefetch)
         self.bt_width = math.ceil(self.max_context / ps)
         self.waiting: list[Request] = []
+        self.swapped: list[Request] = []   # preempted by swap: resumed (K/V copied back) before new work
+        self._swap_bytes = 0
         self.prefilling: list[Request] = []
         self.running: list[Request] = []
         self._rid = itertools.count()
         self.stats = {"prefill_tokens": 0, "prefill_tokens_avoided": 0, "decode_tokens": 0, "steps": 0,
-                      "preemptions": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+                      "preemptions": 0, "h2d_bytes": 0, "d2h_bytes": 0, "swap_out_pages": 0, "swap_in_pages": 0}
         self._graphs_ready = False
 
     # ------------------------------------------------------------------------------------
@@ -193,7 +196,7 @@ class Engine:
         return r
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.prefilling or self.running)
+        return bool(self.waiting or self.prefilling or self.running or self.swapped)
 
     def _alloc(self, n: int) -> list[int]:
         if n <= 0:
@@ -202,8 +205,31 @@ class Engine:
             self.radix.evict(n - self.pool.n_free())
         return self.pool.alloc(n)
 
+    def _resume_swapped(self) -> bool:
+        """Swap preempted requests back in (oldest first); False while one does not fit yet."""
+        while self.swapped and len(self.running) + len(self.prefilling) < self.ecfg.max_batch:
+            r = self.swapped[0]
+            k, v = r.swap
+            try:
+                pages = self._alloc(k.shape[1])
+            except OutOfPages:
+                return False
+            self.swapped.pop(0)
+            idx = torch.tensor(pages, dtype=torch.long).to(self.device, non_blocking=True)
+            self.kv.k.index_copy_(1, idx, k.to(self.device, non_blocking=True))
+            self.kv.v.index_copy_(1, idx, v.to(self.device, non_blocking=True))
+            self.stats["swap_in_pages"] += len(pages)
+            self.stats["h2d_bytes"] += 2 * k.numel() * k.element_size()
+            self._swap_bytes -= 2 * k.numel() * k.element_size()
+            r.swap = None
+            r.pages = pages
+            self.running.append(r)
+        return not self.swapped
+
     def _admit(self) -> None:
         ps = self.ecfg.page_size
+        if not self._resume_swapped():
+            return   # swapped requests go first: admitting new work would only evict them again
         while self.waiting and len(self.running) + len(self.prefilling) < self.ecfg.max_batch:
             r = self.waiting[0]
             hit, pages = 0, []
@@ -423,10 +449,30 @@ class Engine:
         self.running = [r for r in self.running if not r.finished]
 
     def _preempt(self, r: Request) -> None:
-        """Out of pages: give this request's pages back and recompute it later (recompute
-        preemption; its finished prefix goes to the radix cache so the recompute is cheap)."""
+        """Out of pages: give this request's pages back.  Swap mode copies their K/V to pinned host
+        memory and resumes the request later with the K/V copied back (no recompute); otherwise
+        (or when the swap space is full) the request is recomputed later, its finished prefix in
+        the radix cache so the recompute is cheap."""
         self.stats["preemptions"] += 1
         self.running.remove(r)
+        nbytes = 2 * len(r.pages) * self.kv.k[:, :1].numel() * self.kv.k.element_size()
+        if (self.ecfg.preempt_mode == "swap" and r.pages
+                and self._swap_bytes + nbytes <= self.ecfg.swap_space_gb * (1 << 30)):
+            idx = torch.tensor(r.pages, dtype=torch.long).to(self.device, non_blocking=True)
+            host = []
+            for t in (self.kv.k, self.kv.v):
+                g = t.index_select(1, idx)   # [L, n, Hkv, page, D] gathered on the device
+                h = torch.empty(g.shape, dtype=g.dtype, pin_memory=True)
+                h.copy_(g, non_blocking=True)   # stream-ordered before the pages are reused
+                host.append(h)
+            r.swap = (host[0], host[1])
+            self._swap_bytes += nbytes
+            self.stats["swap_out_pages"] += len(r.pages)
+            self.stats["d2h_bytes"] += nbytes
+            self.pool.release(r.pages)
+            r.pages = []
+            self.swapped.append(r)
+            return
         if self.radix is not None:
             self.radix.insert(r.tokens[:r.n_kv], r.pages)
         self.pool.release(r.pages)

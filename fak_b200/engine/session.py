@@ -34,7 +34,7 @@ def save_session(engine, path: str, include_kv: bool = False) -> dict:
             idx = torch.tensor(pages, dtype=torch.long, device=engine.kv.k.device)
             kv.append((engine.kv.k[:, idx].cpu(), engine.kv.v[:, idx].cpu()))
     reqs = []
-    for r in list(engine.running) + list(engine.prefilling) + list(engine.waiting):
+    for r in list(engine.running) + list(engine.prefilling) + list(engine.swapped) + list(engine.waiting):
         if r.finished:
             continue
         reqs.append({"tokens": list(r.tokens), "output": list(r.output),

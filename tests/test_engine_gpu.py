@@ -216,3 +216,27 @@ def test_sliding_window_engine_matches_reference(tmp_path):
     while k < len(out) and out[k] == want_ids[k]:
         k += 1
     assert k >= 8, (out, want_ids)
+
+
+@pytest.mark.parametrize("mode", ["swap", "recompute"])
+def test_preemption_under_kv_pressure(tmp_path, mode):
+    """Too few KV pages for the batch: requests are preempted and resumed.  Swap mode copies their
+    K/V to host memory and back, so the outputs are bit-identical to an unconstrained run."""
+    from fak_b200.engine import Engine
+    path = str(tmp_path / "m.gguf")
+    write_synthetic_gguf(path, preset("tiny-llama"), "q8_0", seed=5, std=0.05)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, 500, 40).tolist() for _ in range(4)]
+    big = Engine.from_gguf(path, EngineConfig(max_batch=8, kv_pages=256, cuda_graph=False), "cuda", max_context=512)
+    want = big.generate(prompts, max_new_tokens=60)
+    ecfg = EngineConfig(max_batch=8, kv_pages=20, cuda_graph=False, radix_cache=False, preempt_mode=mode)
+    eng = Engine.from_gguf(path, ecfg, "cuda", max_context=512)
+    reqs = [eng.add_request(p, 60) for p in prompts]
+    eng.run_until_done(reqs)
+    assert eng.stats["preemptions"] > 0
+    got = [r.output_before_preempt + r.output for r in reqs]
+    if mode == "swap":
+        assert eng.stats["swap_out_pages"] > 0 and eng.stats["swap_in_pages"] == eng.stats["swap_out_pages"]
+        assert got == want
+    else:
+        assert all(len(g) == 60 for g in got)
