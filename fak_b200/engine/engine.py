@@ -57,7 +57,9 @@ class Request:
     finish_reason: str = ""
     on_token: Callable[[int], None] | None = None
     output_before_preempt: list[int] = dataclasses.field(default_factory=list)  # tokens emitted before a requeue
-    swap: tuple | None = None        # (K, V) of its pages in pinned host memory while swapped out
+    swap: tuple | None = None        # (K, V, host bytes) of its pages while swapped out / handed over
+    hold_pages: bool = False         # keep the pages at finish (prefill side of a P/D handoff)
+    held_pages: list[int] = dataclasses.field(default_factory=list)
 
     @property
     def ttft(self) -> float | None:
@@ -209,7 +211,7 @@ class Engine:
         """Swap preempted requests back in (oldest first); False while one does not fit yet."""
         while self.swapped and len(self.running) + len(self.prefilling) < self.ecfg.max_batch:
             r = self.swapped[0]
-            k, v = r.swap
+            k, v, host_bytes = r.swap
             try:
                 pages = self._alloc(k.shape[1])
             except OutOfPages:
@@ -220,7 +222,7 @@ class Engine:
             self.kv.v.index_copy_(1, idx, v.to(self.device, non_blocking=True))
             self.stats["swap_in_pages"] += len(pages)
             self.stats["h2d_bytes"] += 2 * k.numel() * k.element_size()
-            self._swap_bytes -= 2 * k.numel() * k.element_size()
+            self._swap_bytes -= host_bytes
             r.swap = None
             r.pages = pages
             self.running.append(r)
@@ -320,7 +322,10 @@ class Engine:
         if self.radix is not None:
             # the K/V of tokens[:n_kv] is in the pages; the last sampled token was never fed
             self.radix.insert(r.tokens[:r.n_kv], r.pages)
-        self.pool.release(r.pages)
+        if r.hold_pages:
+            r.held_pages = r.pages   # the caller exports their K/V, then releases them
+        else:
+            self.pool.release(r.pages)
         r.pages = []
 
     def _ensure_pages(self, r: Request, last_pos: int) -> bool:
@@ -465,7 +470,7 @@ class Engine:
                 h = torch.empty(g.shape, dtype=g.dtype, pin_memory=True)
                 h.copy_(g, non_blocking=True)   # stream-ordered before the pages are reused
                 host.append(h)
-            r.swap = (host[0], host[1])
+            r.swap = (host[0], host[1], nbytes)
             self._swap_bytes += nbytes
             self.stats["swap_out_pages"] += len(r.pages)
             self.stats["d2h_bytes"] += nbytes

@@ -240,3 +240,16 @@ def test_preemption_under_kv_pressure(tmp_path, mode):
         assert got == want
     else:
         assert all(len(g) == 60 for g in got)
+
+
+def test_prefill_decode_disaggregation_matches_one_engine(model_file):
+    """Prefill on one engine, K/V handed over to two decode engines: the outputs are bit-identical to
+    one engine doing both (same kernels, K/V copied exactly)."""
+    from fak_b200.engine.disagg import PDCluster
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 500, n).tolist() for n in (33, 50, 17, 64)]
+    want = _engine(model_file, graphs=False).generate(prompts, max_new_tokens=20)
+    pd = PDCluster(_engine(model_file, graphs=False), [_engine(model_file, graphs=True), _engine(model_file, graphs=False)])
+    got = pd.generate(prompts, max_new_tokens=20)
+    assert got == want
+    assert pd.stats["handoffs"] == 4 and all(e.stats["swap_in_pages"] > 0 for e in pd.decoders)

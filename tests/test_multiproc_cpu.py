@@ -104,3 +104,36 @@ def test_dead_rank_is_detected_by_the_group_timeout():
             p.kill()
     assert msgs[1] == "left"
     assert msgs[0].startswith("error after"), msgs
+
+
+def _handoff_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from fak_b200.engine.disagg import KVHandoff, recv_handoff, send_handoff
+    from fak_b200.parallel import dist as pdist
+    pdist.init(world, rank, 0, timeout_s=60, backend="gloo")
+    try:
+        if rank == 0:
+            g = torch.Generator().manual_seed(7)
+            h = KVHandoff([5, 6, 7, 8], 42, torch.randn(3, 2, 2, 16, 8, generator=g).bfloat16(),
+                          torch.randn(3, 2, 2, 16, 8, generator=g).bfloat16(), 16)
+            send_handoff(h, 1)
+            q.put((0, h.prompt, h.first_token, h.k.float().sum().item(), h.v.float().sum().item()))
+        else:
+            h = recv_handoff(0, "cpu")
+            q.put((1, h.prompt, h.first_token, h.k.float().sum().item(), h.v.float().sum().item()))
+    finally:
+        pdist.shutdown()
+
+
+def test_kv_handoff_transport_between_processes():
+    """A prefill-side KV handoff crosses processes (gloo point-to-point) intact."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_handoff_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((m[0], m[1:]) for m in (q.get(timeout=120) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == res[1] and res[1][0] == [5, 6, 7, 8] and res[1][1] == 42
