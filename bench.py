@@ -172,7 +172,7 @@ def main():
                 eng.run_until_done(reqs[-1:])
         eng.run_until_done(reqs)
         for a, r in enumerate(reqs):
-            hist[a].extend(r.output)
+            hist[a].extend(r.full_output)
         return reqs
 
     for _ in range(args.warmup):
@@ -192,7 +192,7 @@ def main():
     for _ in range(args.steps):
         reqs = turn()
         ttfts.extend(r.ttft for r in reqs)
-        decoded += sum(len(r.output) for r in reqs)
+        decoded += sum(len(r.full_output) for r in reqs)
     ev1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0

@@ -12,6 +12,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
                       c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window);
+void kv_move(torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor src_slot, torch::Tensor dst_slot,
+             torch::Tensor rot, torch::Tensor cos_n, torch::Tensor sin_n);
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
                        torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window);
@@ -77,6 +79,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("seq_qoff"), pybind11::arg("seq_qlen"), pybind11::arg("seq_pos0"), pybind11::arg("n_tiles"),
         pybind11::arg("out"), pybind11::arg("window") = 0);
   m.def("embed", &embed);
+  m.def("kv_move", &kv_move, "move K/V rows between slots of all layers, re-rotating flagged keys back by n");
   m.def("rope_kv", &rope_kv);
   m.def("rmsnorm_bf16", &rmsnorm_bf16);
   m.def("argmax_rows", &argmax_rows, pybind11::arg("logits"), pybind11::arg("V"), pybind11::arg("out"),

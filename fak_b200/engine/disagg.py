@@ -151,4 +151,4 @@ class PDCluster:
                 if e.has_work():
                     e.step()
                     busy = True
-        return [r.output for _, r in reqs]
+        return [r.full_output for _, r in reqs]

@@ -59,11 +59,17 @@ class Request:
     output_before_preempt: list[int] = dataclasses.field(default_factory=list)  # tokens emitted before a requeue
     swap: tuple | None = None        # (K, V, host bytes) of its pages while swapped out / handed over
     hold_pages: bool = False         # keep the pages at finish (prefill side of a P/D handoff)
+    cache_limit: int | None = None   # tokens of this request the radix cache may take (span eviction)
     held_pages: list[int] = dataclasses.field(default_factory=list)
 
     @property
     def ttft(self) -> float | None:
         return None if self.first_token_time is None else self.first_token_time - self.arrival
+
+    @property
+    def full_output(self) -> list[int]:
+        """Every token generated so far (across recompute preemptions)."""
+        return self.output_before_preempt + self.output
 
 
 class Engine:
@@ -321,12 +327,56 @@ class Engine:
         r.finish_time = time.perf_counter()
         if self.radix is not None:
             # the K/V of tokens[:n_kv] is in the pages; the last sampled token was never fed
-            self.radix.insert(r.tokens[:r.n_kv], r.pages)
+            self.radix.insert(r.tokens[:self._cacheable(r)], r.pages)
         if r.hold_pages:
             r.held_pages = r.pages   # the caller exports their K/V, then releases them
         else:
             self.pool.release(r.pages)
         r.pages = []
+
+    @staticmethod
+    def _cacheable(r: Request) -> int:
+        return r.n_kv if r.cache_limit is None else min(r.n_kv, r.cache_limit)
+
+    def evict_span(self, r: Request, start: int, end: int) -> int:
+        """Remove token positions [start, end) from a request's K/V between steps: later positions
+        move down by end - start with their keys re-rotated to the new positions, so the model can no
+        longer attend to the span.  Pages from the span's first page on are rewritten into fresh
+        pages (shared prefix pages are never modified).  Returns the number of positions removed.
+
+        The K/V of tokens after the span were computed while the span was visible, so from then on
+        only the tokens before the span may enter the radix cache."""
+        from ..models.rope import inv_freq
+        if r.finished or r.swap is not None or r in self.waiting or r in self.prefilling:
+            raise ValueError("evict_span: the request must be decoding (between steps)")
+        if not 0 <= start < end <= r.n_kv:
+            raise ValueError(f"evict_span: span [{start}, {end}) outside the cached {r.n_kv} positions")
+        ps, n, N = self.ecfg.page_size, end - start, r.n_kv
+        first = start // ps
+        new_len = N - n
+        fresh = self._alloc(-(-new_len // ps) - first) if new_len > first * ps else []
+        q = np.arange(first * ps, new_len)
+        src = np.where(q < start, q, q + n)
+        old = np.asarray(r.pages, dtype=np.int64)
+        dst_pages = np.asarray(fresh, dtype=np.int64)
+        src_slot = old[src // ps] * ps + src % ps
+        dst_slot = dst_pages[q // ps - first] * ps + q % ps if len(q) else np.zeros(0, np.int64)
+        inv, _ = inv_freq(self.cfg.head_dim, self.cfg.rope_theta, self.cfg.rope_scaling, self.cfg.max_context)
+        ang = inv * float(n)
+        dev = self.device
+        K.kv_move(self.kv, torch.from_numpy(src_slot.astype(np.int32)).to(dev),
+                  torch.from_numpy(dst_slot.astype(np.int32)).to(dev),
+                  torch.from_numpy((q >= start).astype(np.uint8)).to(dev),
+                  torch.cos(ang).float().to(dev), torch.sin(ang).float().to(dev))
+        self.pool.release(r.pages[first:])
+        r.pages = r.pages[:first] + fresh
+        survivors_after = N - end
+        r.tokens = r.tokens[:start] + r.tokens[end:]
+        r.n_kv = new_len
+        limit = start if survivors_after > 0 else new_len
+        r.cache_limit = limit if r.cache_limit is None else min(r.cache_limit, limit)
+        self.stats["evicted_positions"] = self.stats.get("evicted_positions", 0) + n
+        return n
 
     def _ensure_pages(self, r: Request, last_pos: int) -> bool:
         need = last_pos // self.ecfg.page_size + 1 - len(r.pages)
@@ -479,12 +529,14 @@ class Engine:
             self.swapped.append(r)
             return
         if self.radix is not None:
-            self.radix.insert(r.tokens[:r.n_kv], r.pages)
+            self.radix.insert(r.tokens[:self._cacheable(r)], r.pages)
         self.pool.release(r.pages)
         r.pages = []
+        r.cache_limit = None   # recomputed from its tokens: its K/V will be plain again
         r.prompt = list(r.tokens)
         r.max_new_tokens -= len(r.output)
-        r.output_before_preempt = list(r.output)
+        r.output_before_preempt = r.output_before_preempt + r.output
+        r.output = []
         r.n_kv = 0
         self.waiting.insert(0, r)
 
@@ -504,4 +556,4 @@ class Engine:
                  stop_ids=()) -> list[list[int]]:
         reqs = [self.add_request(p, max_new_tokens, sampling, stop_ids) for p in prompts]
         self.run_until_done(reqs)
-        return [r.output for r in reqs]
+        return [r.full_output for r in reqs]

@@ -67,4 +67,4 @@ def sample_row(row: torch.Tensor, sp: SamplingParams, generated: list[int]) -> i
 def sample(logits: torch.Tensor, params: list[SamplingParams], reqs) -> list[int]:
     if all(p.greedy for p in params):
         return torch.argmax(logits, dim=-1).tolist()
-    return [sample_row(logits[i], params[i], list(reqs[i].output)) for i in range(len(params))]
+    return [sample_row(logits[i], params[i], list(reqs[i].full_output)) for i in range(len(params))]

@@ -37,7 +37,7 @@ def save_session(engine, path: str, include_kv: bool = False) -> dict:
     for r in list(engine.running) + list(engine.prefilling) + list(engine.swapped) + list(engine.waiting):
         if r.finished:
             continue
-        reqs.append({"tokens": list(r.tokens), "output": list(r.output),
+        reqs.append({"tokens": list(r.tokens), "output": list(r.full_output),
                      "remaining": r.max_new_tokens - len(r.output),
                      "sampling": dataclasses.asdict(dataclasses.replace(r.sampling, mask=None)),
                      "stop_ids": sorted(r.stop_ids)})

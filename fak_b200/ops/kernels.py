@@ -143,6 +143,14 @@ def prefill_attention(q, k_cache, v_cache, block_table, meta, out, window: int =
     count()
 
 
+def kv_move(kv, src_slot: torch.Tensor, dst_slot: torch.Tensor, rot: torch.Tensor, cos_n: torch.Tensor,
+            sin_n: torch.Tensor) -> None:
+    """Move K/V rows (all layers) from src to dst slots; keys of rows with rot=1 are re-rotated back
+    by the shift whose cos/sin per pair are cos_n / sin_n."""
+    ext().kv_move(kv.k, kv.v, src_slot, dst_slot, rot, cos_n, sin_n)
+    count()
+
+
 def embed(w, ids: torch.Tensor, out_f32=None, out_bf16=None, err=None) -> None:
     ext().embed(w.buf, w.qtype, w.pitch, w.rows, w.cols, ids, out_f32, out_bf16, err)
     count()
