@@ -347,6 +347,7 @@ class Engine:
         The K/V of tokens after the span were computed while the span was visible, so from then on
         only the tokens before the span may enter the radix cache."""
         from ..models.rope import inv_freq
+        from ..ops import kernels as K
         if r.finished or r.swap is not None or r in self.waiting or r in self.prefilling:
             raise ValueError("evict_span: the request must be decoding (between steps)")
         if not 0 <= start < end <= r.n_kv:

@@ -269,7 +269,8 @@ def test_evict_span_tail_equals_never_seen_and_middle_follows_reference(model_fi
     want = _engine(model_file, graphs=False).generate([base], max_new_tokens=12)[0]
     eng = _engine(model_file, graphs=False)
     r = eng.add_request(base + span, 12)
-    eng.step()                                   # prefill + first sampled token
+    eng._admit()
+    eng._run_prefill()                           # prefill + first sampled token (not yet fed)
     assert r.n_kv == len(base) + len(span) and len(r.output) == 1
     # drop the span and the token sampled after it, then feed the token the clean run sampled first
     eng.evict_span(r, len(base), r.n_kv)
@@ -281,7 +282,8 @@ def test_evict_span_tail_equals_never_seen_and_middle_follows_reference(model_fi
     # middle span: compare the compacted cache with the reference's K rows re-rotated
     eng2 = _engine(model_file, graphs=False)
     r2 = eng2.add_request(base + span, 30)
-    eng2.step()
+    eng2._admit()
+    eng2._run_prefill()
     a, b = 10, 25
     ps = eng2.ecfg.page_size
     before = [(eng2.kv.k[:, r2.pages[p // ps], :, p % ps].float().clone()) for p in range(r2.n_kv)]
