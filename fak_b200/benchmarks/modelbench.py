@@ -103,6 +103,7 @@ def main(argv=None):
         out.update({"prefill_seqs": S, "prefill_tokens": T, "prefill_ms": round(pms, 3), "prefill_tok_s": round(T * 1000 / pms, 1),
                     "prefill_linear_tflops": round(flops / pms / 1e9, 1)})
     print(json.dumps(out), flush=True)
+    return out
 
 
 if __name__ == "__main__":

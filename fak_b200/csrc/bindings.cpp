@@ -14,6 +14,10 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window);
 void kv_move(torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor src_slot, torch::Tensor dst_slot,
              torch::Tensor rot, torch::Tensor cos_n, torch::Tensor sin_n);
+torch::Tensor dsa_index_score(torch::Tensor iq, torch::Tensor ik, torch::Tensor w, int64_t qpos, double scale);
+std::vector<torch::Tensor> dsa_topk(torch::Tensor score, int64_t qpos, int64_t topk);
+torch::Tensor dsa_sparse_attend(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor sel,
+                                torch::Tensor count, double scale);
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
                        torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window);
@@ -79,6 +83,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("seq_qoff"), pybind11::arg("seq_qlen"), pybind11::arg("seq_pos0"), pybind11::arg("n_tiles"),
         pybind11::arg("out"), pybind11::arg("window") = 0);
   m.def("embed", &embed);
+  m.def("dsa_index_score", &dsa_index_score);
+  m.def("dsa_topk", &dsa_topk);
+  m.def("dsa_sparse_attend", &dsa_sparse_attend);
   m.def("kv_move", &kv_move, "move K/V rows between slots of all layers, re-rotating flagged keys back by n");
   m.def("rope_kv", &rope_kv);
   m.def("rmsnorm_bf16", &rmsnorm_bf16);

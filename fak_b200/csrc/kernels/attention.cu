@@ -332,7 +332,7 @@ struct PrefillSmem {
 };
 
 template <int D>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, D == 128 ? 3 : 0)   // D=128: keep 3 CTAs per SM (<= 168 registers)
 k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv_bfloat16* __restrict__ kc,
                const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_table, int bt_stride,
                const int* __restrict__ tile_seq, const int* __restrict__ tile_q0, const int* __restrict__ seq_qoff,
@@ -368,6 +368,8 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
     }
   }
   const int qpos0 = pos0 + r0, qpos1 = pos0 + r1;
+  // lowest visible key of each row minus one (sliding window), or below every position
+  const int lo0 = win > 0 ? qpos0 - win : -1, lo1 = win > 0 ? qpos1 - win : -1;
   const int kv_end = pos0 + min(q0 + PF_Q, qlen);  // exclusive bound on keys any row of this tile sees
   const int n_kv_tiles = (kv_end + PF_KV - 1) / PF_KV;
 
@@ -426,7 +428,8 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
       for (int e = 0; e < 4; e++) {
         int kp = kt * PF_KV + 8 * j + 2 * tq + (e & 1);
         int qp = (e < 2) ? qpos0 : qpos1;
-        s[j][e] = (kp <= qp && kp < kv_end && (win <= 0 || kp > qp - win)) ? s[j][e] * scale_log2 : NEG_INF;
+        int lo = (e < 2) ? lo0 : lo1;
+        s[j][e] = (kp <= qp && kp > lo && kp < kv_end) ? s[j][e] * scale_log2 : NEG_INF;
       }
     }
     float mx0 = NEG_INF, mx1 = NEG_INF;

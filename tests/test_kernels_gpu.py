@@ -383,3 +383,29 @@ def test_gemm_tcgen05_bf16_out_many_tiles_per_cta():
     torch.cuda.synchronize()
     assert err.item() == 0
     assert torch.allclose(out.float(), ref, atol=2e-2 * math.sqrt(K) / 8 + 1e-2, rtol=2e-2), (out.float() - ref).abs().max()
+
+
+@pytest.mark.parametrize("n_keys,qpos,topk", [(300, 299, 64), (5000, 4321, 2048), (40, 10, 64)])
+def test_dsa_index_topk_and_sparse_attention(n_keys, qpos, topk):
+    """GLM-DSA path: f64 indexer scores, top-k selection (ties to the lower position) and MLA sparse
+    attention (kd 192, vd 128) against the PyTorch definitions."""
+    from fak_b200.models.dsa import dsa_decode, index_scores_ref, sparse_attend_ref, topk_ref
+    from fak_b200.ops._ext import ext
+    g = torch.Generator(device="cuda").manual_seed(n_keys)
+    nh, dim, H, kd, vd = 32, 128, 16, 192, 128
+    iq = torch.randn(nh, dim, device="cuda", generator=g)
+    ik = torch.randn(n_keys, dim, device="cuda", generator=g)
+    ik[7] = ik[3]                                           # an exact tie: position 3 wins
+    w = torch.randn(nh, device="cuda", generator=g)
+    q = torch.randn(H, kd, device="cuda", generator=g)
+    kc = torch.randn(n_keys, H, kd, device="cuda", generator=g)
+    vc = torch.randn(n_keys, H, vd, device="cuda", generator=g)
+    score = ext().dsa_index_score(iq, ik, w, qpos, 0.1)
+    ref = index_scores_ref(iq, ik, w, qpos, 0.1)
+    assert torch.allclose(score[: qpos + 1], ref[: qpos + 1], rtol=1e-12, atol=1e-9)
+    assert torch.isinf(score[qpos + 1:]).all()
+    out, sel = dsa_decode(q, kc, vc, iq, ik, w, qpos, topk, 0.1, 1 / math.sqrt(kd))
+    want_sel = topk_ref(ref.cpu(), qpos, topk)
+    assert sel.tolist() == want_sel
+    want = sparse_attend_ref(q, kc, vc, want_sel, 1 / math.sqrt(kd))
+    assert torch.allclose(out, want, atol=1e-4, rtol=1e-4), (out - want).abs().max()

@@ -71,3 +71,23 @@ def test_param_counts():
     assert 7.0e9 < preset("qwen2.5-7b").param_count() < 7.8e9
     assert 1.2e8 < preset("smollm2-135m").param_count() < 1.5e8
     assert 2.9e10 < preset("qwen3-30b-a3b").param_count() < 3.2e10
+
+
+def test_dsa_reference_definitions():
+    """Sparse-attention definitions: top-k order (score, then position) and attention over the full
+    set equal to dense softmax attention."""
+    import math
+    from fak_b200.models.dsa import index_scores_ref, sparse_attend_ref, topk_ref
+    g = torch.Generator().manual_seed(0)
+    iq, ik, w = torch.randn(4, 8, generator=g), torch.randn(20, 8, generator=g), torch.rand(4, generator=g)
+    ik[5] = ik[2]
+    s = index_scores_ref(iq, ik, w, 15, 0.5)
+    assert torch.isinf(s[16:]).all()
+    sel = topk_ref(s, 15, 6)
+    assert len(sel) == 6 and sorted(s[sel].tolist(), reverse=True) == s[sel].tolist()
+    if 2 in sel or 5 in sel:
+        assert (2 in sel) and (sel.index(2) < sel.index(5) if 5 in sel else True)
+    q, kc, vc = torch.randn(3, 6, generator=g), torch.randn(20, 3, 6, generator=g), torch.randn(20, 3, 4, generator=g)
+    full = sparse_attend_ref(q, kc, vc, list(range(20)), 1 / math.sqrt(6))
+    dense = torch.softmax(torch.einsum("hd,nhd->hn", q, kc) / math.sqrt(6), -1)
+    assert torch.allclose(full, torch.einsum("hn,nhv->hv", dense, vc), atol=1e-6)
