@@ -18,13 +18,17 @@ from .adjudicator import Adjudicator
 from .ctxmmu import ContextMMU
 from .journal import Journal
 from .policy import Policy
+from .preflight import Preflight
+from .vdso import VDSO
 
 Handler = Callable[[dict], Any]
 
 
 class Kernel:
     def __init__(self, policy: Policy | None = None, journal_path: str | None = None, mmu: ContextMMU | None = None,
-                 workers: int = 4):
+                 workers: int = 4, preflight: Preflight | None = None, vdso: VDSO | None = None):
+        self.preflight = preflight or Preflight()
+        self.vdso = vdso or VDSO()
         self.adjudicator = Adjudicator(policy)
         self.journal = Journal(journal_path)
         self.mmu = mmu or ContextMMU()
@@ -43,7 +47,9 @@ class Kernel:
 
     def decide(self, call: ToolCall) -> Verdict:
         t0 = time.perf_counter_ns()
-        v = self.adjudicator.adjudicate(call)
+        v = self.preflight.check(call)          # malformed calls never reach the policy
+        if v.kind == VerdictKind.DEFER:
+            v = self.adjudicator.adjudicate(call)
         dt = time.perf_counter_ns() - t0
         with self._lock:
             self.stats["calls"] += 1
@@ -56,6 +62,10 @@ class Kernel:
 
     def _execute(self, call: ToolCall, verdict: Verdict) -> Result:
         args = verdict.new_args if verdict.kind == VerdictKind.TRANSFORM and verdict.new_args is not None else call.args
+        hit, out, tier = self.vdso.lookup(call.tool, args)
+        if hit:   # answered by the fast path: the same result a fresh call gives
+            self.journal.append("vdso_hit", tool=call.tool, seq=call.seq, tier=tier)
+            return Result(call, out, Status.OK, verdict)
         h = self.handlers.get(call.tool)
         if h is None:
             return Result(call, None, Status.ERROR, Verdict(VerdictKind.DENY, Reason.UNKNOWN_TOOL, by="kernel",
@@ -65,6 +75,8 @@ class Kernel:
         except Exception as e:  # a failing tool is a result, not a kernel crash
             return Result(call, f"{type(e).__name__}: {e}", Status.ERROR, verdict)
         adm = self.mmu.admit(call.tool, out if isinstance(out, str) else str(out))
+        # the cache holds what the model was shown (the admitted content), never a raw result
+        self.vdso.complete(call.tool, args, adm.content, cacheable=adm.verdict.kind != VerdictKind.DENY)
         self.journal.append("admission", tool=call.tool, seq=call.seq, verdict=adm.verdict.to_dict(),
                             findings=len(adm.findings))
         if adm.verdict.kind == VerdictKind.DENY:

@@ -37,7 +37,8 @@ def build_gateway(args):
         backend = UpstreamBackend(args.upstream, os.environ.get("FAK_UPSTREAM_API_KEY", ""))
     else:
         backend = build_model_backend(args)
-    return Gateway(backend, kernel, model_name=args.model_name)
+    return Gateway(backend, kernel, model_name=args.model_name,
+                   ctx_view_budget=getattr(args, "ctx_view_budget", 0))
 
 
 def build_model_backend(args):
@@ -106,6 +107,8 @@ def _add_model_args(ap):
     ap.add_argument("--policy", help="policy manifest (fak-policy/v1 JSON); default: built-in floor")
     ap.add_argument("--journal", help="append the hash-chained decision journal to this file")
     ap.add_argument("--model-name", default=None)
+    ap.add_argument("--ctx-view-budget", type=int, default=0,
+                    help="plan each chat prompt as a view of at most this many tokens (0: whole transcript)")
     ap.add_argument("--max-batch", type=int, default=32)
     ap.add_argument("--max-context", type=int, default=8192)
 

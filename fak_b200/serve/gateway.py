@@ -92,14 +92,23 @@ class Metrics:
 
 class Gateway:
     def __init__(self, backend, kernel: Kernel | None = None, model_name: str | None = None,
-                 default_max_tokens: int = 256):
+                 default_max_tokens: int = 256, ctx_view_budget: int = 0):
         self.backend = backend
+        self.planner = None   # planned context views under a token budget (0: whole transcript)
+        if ctx_view_budget > 0:
+            from .ctxplan import ContextPlanner
+            tok = getattr(backend, "tok", None)
+            count = (lambda s: len(tok.encode(s))) if tok is not None else None
+            self.planner = ContextPlanner(ctx_view_budget, count)
         self.kernel = kernel or Kernel()
         self.model_name = model_name or getattr(backend, "name", "fak-b200")
         self.default_max_tokens = default_max_tokens
         self.metrics = Metrics()
         self.tok = getattr(backend, "tok", None)
         self._json = None
+
+    def _view(self, messages: list[dict]) -> list[dict]:
+        return self.planner.plan(messages).messages if self.planner is not None and messages else messages
 
     # ------------------------------------------------------------------ generation core
     def _stop_ids(self) -> set[int]:
@@ -196,7 +205,8 @@ class Gateway:
                 if notes:
                     msg["content"] = ((msg.get("content") or "") + "\n" + "\n".join(notes)).strip()
             return resp
-        prompt = render_chatml(body.get("messages", []), body.get("tools"))
+        self.kernel.preflight.register_openai_tools(body.get("tools"))   # schemas for the pre-flight rungs
+        prompt = render_chatml(self._view(body.get("messages", [])), body.get("tools"))
         info = {}
         text = ""
         stop = body.get("stop")
@@ -230,7 +240,8 @@ class Gateway:
                                           "choices": [{"index": 0, "delta": delta, "finish_reason": finish}]}) + "\n\n"
 
         yield chunk({"role": "assistant"})
-        prompt = render_chatml(body.get("messages", []), body.get("tools"))
+        self.kernel.preflight.register_openai_tools(body.get("tools"))   # schemas for the pre-flight rungs
+        prompt = render_chatml(self._view(body.get("messages", [])), body.get("tools"))
         text, info, held = "", {}, ""
         for piece, inf in self.stream_text(prompt, int(body.get("max_tokens") or self.default_max_tokens),
                                            _sampling(body, self._json_mask), None):
