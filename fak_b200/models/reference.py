@@ -62,6 +62,8 @@ class ReferenceModel:
         self.device = torch.device(device)
         self.t = {k: v.to(self.device, torch.float32) for k, v in tensors.items()}
         self.lora = None   # models.lora.LoRASet applied dynamically after each patched projection
+        self.taps: dict[int, torch.Tensor] | None = None   # hidden tap: residual stream after layer i
+        self.attn_observer = None   # callable(layer, probs [H, Tq, Tctx]) for every attention
 
     def set_lora(self, lora_set) -> None:
         self.lora = lora_set
@@ -153,11 +155,30 @@ class ReferenceModel:
                 K, V = kv[j]
             else:
                 K, V = k, v
-            a = attention(q, K, V, start_pos, cfg.layer_window(i))
+            a = attention(q, K, V, start_pos, cfg.layer_window(i),
+                          None if self.attn_observer is None else (lambda pr, i=i: self.attn_observer(i, pr)))
             x = x + self.mm(a.reshape(T, H * D), p + "attn_output.weight")
             h = rmsnorm(x, self.w(p + "ffn_norm.weight"), cfg.rms_eps)
             x = x + self._ffn(i, h)
+            if self.taps is not None:
+                self.taps[i] = x.detach().clone()
         return x
+
+    @torch.no_grad()
+    def logit_lens(self, ids, layers: list[int] | None = None, top: int = 1) -> dict[int, torch.Tensor]:
+        """Top-``top`` token ids of the final norm + LM head applied to the residual stream after
+        each layer (the logit lens), for every position: {layer: [T, top]}."""
+        self.taps = {}
+        try:
+            self.forward(torch.as_tensor(ids), hidden_only=True)
+            taps = self.taps
+        finally:
+            self.taps = None
+        out = {}
+        for i in (layers if layers is not None else sorted(taps)):
+            h = rmsnorm(taps[i], self.t["output_norm.weight"], self.cfg.rms_eps)
+            out[i] = torch.topk(self.lm_head(h), top, dim=-1).indices
+        return out
 
     @torch.no_grad()
     def generate_greedy(self, prompt: list[int], n_new: int) -> list[int]:
@@ -174,7 +195,8 @@ class ReferenceModel:
         return out
 
 
-def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int, window: int = 0) -> torch.Tensor:
+def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int, window: int = 0,
+              observe=None) -> torch.Tensor:
     """q [T,H,D] at positions start_pos..; K,V [Tctx,Hk,D] covering positions 0..Tctx-1 (causal;
     window > 0: each query sees keys (qpos - window, qpos])."""
     T, H, D = q.shape
@@ -190,6 +212,8 @@ def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int,
         masked = masked | (kpos <= qpos - window)
     s = s.masked_fill(masked[None], float("-inf"))
     pr = torch.softmax(s, dim=-1)
+    if observe is not None:
+        observe(pr)
     return torch.einsum("htc,chd->thd", pr, Vx.float())
 
 

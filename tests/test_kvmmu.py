@@ -49,3 +49,45 @@ def test_verdicts_drive_eviction():
     assert m.apply(adm.verdict, "res") == 10 and e.calls == [(40, 50)]
     m.append("ok", 5)
     assert m.apply(Verdict(VerdictKind.ALLOW, Reason.NONE), "ok") == 0
+
+
+def test_evict_coldest_blocks():
+    import torch
+    e, r = _Eng(), _Req(200)
+    m = KVMMU(e, r)
+    m.record("pinned", 32, 48)
+    mass = torch.ones(200)
+    mass[16:32] = 0.1       # cold
+    mass[32:48] = 0.0       # colder, but a recorded segment: protected
+    mass[80:96] = 0.2       # cold
+    mass[190:200] = 0.0     # inside the recent window: protected
+    spans = m.evict_coldest(mass, 2, block=16, keep_sink=4, keep_recent=32)
+    assert spans == [(16, 32), (80, 96)] and e.calls == [(80, 96), (16, 32)] and r.n_kv == 168
+    pinned = m.segments[0]
+    assert (pinned.start, pinned.end) == (16, 32)
+
+
+def test_attention_mass_observer_on_the_reference():
+    import torch
+    from fak_b200.config import preset
+    from fak_b200.gguf.synth import write_synthetic_gguf
+    from fak_b200.kv.kvmmu import AttentionMass
+    from fak_b200.models.reference import ReferenceModel
+    import tempfile, os
+    d = tempfile.mkdtemp()
+    path = os.path.join(d, "m.gguf")
+    write_synthetic_gguf(path, preset("tiny-llama"), "f32", seed=1, std=0.05)
+    ref = ReferenceModel.from_gguf(path)
+    acc = AttentionMass()
+    ref.attn_observer = acc.observe
+    ref.forward(torch.arange(10))
+    # every query's probabilities sum to one: total mass = layers x heads x queries
+    assert acc.mass.numel() == 10
+    assert abs(float(acc.mass.sum()) - ref.cfg.n_layers * ref.cfg.n_heads * 10) < 1e-6
+    assert acc.mass[0] > acc.mass[9]   # causal: position 0 is seen by every query
+    lens = ref.logit_lens(torch.arange(10))
+    assert sorted(lens) == list(range(ref.cfg.n_layers)) and lens[0].shape == (10, 1)
+    final = torch.argmax(ref.forward(torch.arange(10)), -1)
+    assert torch.equal(lens[ref.cfg.n_layers - 1][:, 0], final)
+    acc.drop(2, 5)
+    assert acc.mass.numel() == 7
