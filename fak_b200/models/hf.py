@@ -175,6 +175,7 @@ def _to_f32(dt: str, a: np.ndarray) -> np.ndarray:
 
 
 _QPARTS = (".qweight", ".qzeros", ".scales", ".g_idx")
+_EXL2_PARTS = (".q_weight", ".q_groups", ".q_scale", ".q_scale_max", ".q_invperm")
 
 
 def _quant_config(hf: dict) -> dict | None:
@@ -182,8 +183,10 @@ def _quant_config(hf: dict) -> dict | None:
     if not q:
         return None
     method = str(q.get("quant_method", "")).lower()
+    if method == "exl2":
+        return None   # EXL2 layers are recognised by their tensors (q_groups, q_weight, ...)
     if method not in ("awq", "gptq"):
-        raise ValueError(f"unsupported quantization method {method!r} (AWQ and GPTQ are)")
+        raise ValueError(f"unsupported quantization method {method!r} (AWQ, GPTQ and EXL2 are)")
     return q
 
 
@@ -224,11 +227,16 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
     table: dict[str, tuple[str, tuple[int, ...], np.ndarray]] = {}
     experts: dict[str, dict[int, tuple[str, np.ndarray]]] = {}
     qparts: dict[str, dict[str, object]] = {}   # base name -> {qweight, qzeros, scales, g_idx}
+    exl2_parts: dict[str, dict[str, tuple]] = {}   # base name -> {q_weight, q_groups, q_scale, ...}
     for p in files:
         for n, (dt, shape, arr) in read_safetensors(p).items():
             if qc is not None and n.endswith(_QPARTS):
                 base, part = n.rsplit(".", 1)
                 qparts.setdefault(base, {})[part] = (dt, arr) if part == "scales" else np.asarray(arr)
+                continue
+            if n.endswith(_EXL2_PARTS):
+                base, part = n.rsplit(".", 1)
+                exl2_parts.setdefault(base, {})[part] = (dt, np.asarray(arr))
                 continue
             m = _EXPERT.fullmatch(n)
             if m:
@@ -253,6 +261,15 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
         g = gguf_name(base + ".weight")
         if g is not None:
             qlayers[g] = [parts]
+    for base, parts in exl2_parts.items():   # mixed-precision layers: float32 rows (quantized on load)
+        g = gguf_name(base + ".weight")
+        if g is None or "q_weight" not in parts:
+            continue
+        from . import exl2
+        f = lambda k: _to_f32(*parts[k]) if parts[k][0] in ("F16", "BF16", "F32") else parts[k][1]
+        w = exl2.dequantize(parts["q_weight"][1], parts["q_groups"][1], f("q_scale"), f("q_scale_max"),
+                            parts["q_invperm"][1] if "q_invperm" in parts else None)
+        table[g] = ("F32", tuple(w.shape), w)
     for key, per in experts.items():
         dts = {d for d, _ in per.values()}
         stacked = np.stack([per[e][1] for e in range(len(per))])

@@ -149,3 +149,66 @@ def test_g4_synthetic_gguf_loads_in_the_reference(tmp_path):
     assert int(GGMLType.G4) in types and int(GGMLType.Q8_0) in types
     cfg, tensors = load_reference_tensors(path)
     assert tensors["blk.0.attn_q.weight"].shape == (cfg.q_dim, cfg.d_model)
+
+
+def test_exl2_packing_roundtrip_and_error_bound():
+    from fak_b200.models import exl2
+    rng = np.random.default_rng(0)
+    groups = [(4, 32), (3, 64), (8, 32), (2, 96), (5, 32), (6, 32)]
+    in_ = sum(s for _, s in groups)
+    codes = np.concatenate([rng.integers(0, 1 << b, (7, s)) for b, s in groups], axis=1)
+    qw = exl2.pack(codes, groups)
+    assert qw.dtype == np.int32 and qw.shape == (7, -(-sum(b * s for b, s in groups) // 32))
+    assert (exl2.unpack(qw, groups) == codes).all()
+    w = (rng.standard_normal((7, in_)) * 0.1).astype(np.float32)
+    perm = rng.permutation(in_)
+    t = exl2.quantize(w, groups, perm)
+    d = exl2.dequantize(*t)
+    scale = (t[2].astype(np.float32) * t[3].astype(np.float32)[None, :])
+    bits, _, gidx, _ = exl2._bit_layout(groups)
+    bound = np.empty_like(w)
+    bound[:, perm] = scale[:, gidx] * 0.5 + 1e-6
+    assert (np.abs(d - w) <= bound * 1.01).all()
+
+
+def test_exl2_llama_logits_match_transformers(tmp_path):
+    transformers = pytest.importorskip("transformers")
+    from fak_b200.models import exl2
+    from fak_b200.models.hf import load_reference_tensors_hf, write_safetensors
+    from fak_b200.models.reference import ReferenceModel
+    cfg = transformers.LlamaConfig(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=256,
+                                   rms_norm_eps=1e-6, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    m = transformers.LlamaForCausalLM(cfg)
+    for p in m.parameters():
+        torch.nn.init.normal_(p, std=0.05 if p.dim() > 1 else 0.5)
+    m = m.eval().float()
+    sd = m.state_dict()
+    tensors = {}
+    rng = np.random.default_rng(1)
+    for name, w in sd.items():
+        if not (name.endswith("_proj.weight") and ".layers." in name):
+            tensors[name] = w
+            continue
+        in_ = w.shape[1]
+        groups = [(6, in_ // 4), (4, in_ // 2), (3, in_ // 4)]
+        qw, qg, qs, qm, qi = exl2.quantize(w.numpy(), groups, rng.permutation(in_))
+        sd[name].copy_(torch.from_numpy(exl2.dequantize(qw, qg, qs, qm, qi)))
+        base = name[: -len(".weight")]
+        tensors[base + ".q_weight"] = torch.from_numpy(qw)
+        tensors[base + ".q_groups"] = torch.from_numpy(qg.astype(np.int32)).to(torch.int32)
+        tensors[base + ".q_scale"] = torch.from_numpy(qs)
+        tensors[base + ".q_scale_max"] = torch.from_numpy(qm)
+        tensors[base + ".q_invperm"] = torch.from_numpy(qi)
+    write_safetensors(str(tmp_path / "model.safetensors"), tensors)
+    d = m.config.to_dict()
+    d["architectures"] = ["LlamaForCausalLM"]
+    d["quantization_config"] = {"quant_method": "exl2", "bits": 4.5}
+    (tmp_path / "config.json").write_text(json.dumps(d))
+    ours_cfg, ref_t = load_reference_tensors_hf(str(tmp_path))
+    ids = torch.tensor([3, 17, 200, 45, 9, 311, 7])
+    with torch.no_grad():
+        want = m(ids[None]).logits[0]
+    got = ReferenceModel(ours_cfg, ref_t).forward(ids)
+    assert torch.allclose(got, want, atol=3e-4, rtol=1e-4), (got - want).abs().max()
