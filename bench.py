@@ -139,7 +139,7 @@ def main():
     cfg = preset(args.model)
     max_ctx = args.prefix + (args.warmup + args.steps) * (args.user + args.decode) + 64
     max_ctx = (max_ctx + 15) // 16 * 16
-    ecfg = EngineConfig(max_batch=max(8, args.agents), cuda_graph=True,
+    ecfg = EngineConfig.from_env(max_batch=max(8, args.agents), cuda_graph=True,
                         graph_batch_buckets=tuple(sorted({1, 2, 4, 8, args.agents})),
                         max_prefill_tokens=max(args.prefix, args.agents * args.user), tp=world,
                         radix_cache=args.arm != "A")

@@ -41,7 +41,7 @@ def main(argv=None):
     B = args.batch
     # the RoPE tables and block tables cover both the decode contexts and the timed prefill
     max_ctx = (max(args.ctx + args.steps + args.warmup + 64, args.prefill) + 15) // 16 * 16
-    ecfg = EngineConfig(max_batch=max(B, 8), cuda_graph=not args.eager, graph_batch_buckets=(B,),
+    ecfg = EngineConfig.from_env(max_batch=max(B, 8), cuda_graph=not args.eager, graph_batch_buckets=(B,),
                         max_prefill_tokens=max(4096, args.prefill * args.prefill_seqs))
     eng = Engine.synthetic(cfg, args.mix, 0, ecfg, dev, max_context=max_ctx)
     if not args.eager:

@@ -236,6 +236,7 @@ class EngineConfig:
     fused_activations: bool = False     # decode GEMVs normalise+quantize fp32 inputs themselves
     attention_merge: bool = False       # merge attention splits in the last split's CTA (no combine launch)
     l2_prefetch: bool = False           # decode kernels warm L2 with the next GEMV's weights (measured neutral)
+    cascade_attention: bool = True      # decode: a batch's shared prefix pages are attended once for all lanes
     preempt_mode: str = "recompute"     # out of KV pages: "recompute" (radix-assisted) or "swap" to host memory
     swap_space_gb: float = 16.0         # pinned host memory for swapped-out KV pages
 
@@ -258,6 +259,7 @@ class EngineConfig:
         "fused_activations": ("FAK_FUSED_ACT", bool),
         "attention_merge": ("FAK_ATTN_MERGE", bool),
         "l2_prefetch": ("FAK_L2_PREFETCH", bool),
+        "cascade_attention": ("FAK_CASCADE_ATTN", bool),
         "preempt_mode": ("FAK_PREEMPT_MODE", str),
         "swap_space_gb": ("FAK_SWAP_SPACE_GB", float),
     }

@@ -11,7 +11,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
-                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window);
+                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window,
+                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits);
 void kv_move(torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor src_slot, torch::Tensor dst_slot,
              torch::Tensor rot, torch::Tensor cos_n, torch::Tensor sin_n);
 torch::Tensor dsa_index_score(torch::Tensor iq, torch::Tensor ik, torch::Tensor w, int64_t qpos, double scale);
@@ -77,7 +78,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("block_table"), pybind11::arg("ctx_len"), pybind11::arg("n_split"),
         pybind11::arg("pages_per_split"), pybind11::arg("out"), pybind11::arg("qx"), pybind11::arg("ds"),
         pybind11::arg("workspace"), pybind11::arg("ldo") = 0, pybind11::arg("tickets") = pybind11::none(),
-        pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("window") = 0);
+        pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("window") = 0,
+        pybind11::arg("shared_pages") = pybind11::none(), pybind11::arg("prefix_splits") = 0);
   m.def("prefill_attention", &prefill_attention, pybind11::arg("q"), pybind11::arg("k_cache"),
         pybind11::arg("v_cache"), pybind11::arg("block_table"), pybind11::arg("tile_seq"), pybind11::arg("tile_q0"),
         pybind11::arg("seq_qoff"), pybind11::arg("seq_qlen"), pybind11::arg("seq_pos0"), pybind11::arg("n_tiles"),

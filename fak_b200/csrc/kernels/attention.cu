@@ -70,7 +70,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
               int n_split, int pages_per_split, float scale_log2, float* __restrict__ part_o,
               float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
               float2* __restrict__ ds, int ldo, int* __restrict__ tickets, const uint8_t* __restrict__ pf,
-              int64_t pf_bytes, int win) {
+              int64_t pf_bytes, int win, const int* __restrict__ skip_pages, int slot0, int n_slots) {
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -86,7 +86,8 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   const int n_pages = (ctx + PAGE - 1) / PAGE;
   // sliding window (win > 0): the query at ctx - 1 sees keys [ctx - win, ctx); pages before the
   // window are never read
-  const int lo = win > 0 ? max(0, ctx - win) : 0;
+  int lo = win > 0 ? max(0, ctx - win) : 0;
+  if (skip_pages != nullptr) lo = max(lo, min(ctx, *skip_pages * PAGE));   // pages another kernel covers
   const int pg0 = lo / PAGE;
   // pages per split follow the live context so every split gets an even share of the pages
   const int pps = max(pages_per_split, (n_pages - pg0 + n_split - 1) / n_split);
@@ -249,19 +250,19 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
       float acc = 0.f;
 #pragma unroll
       for (int w = 0; w < 4; w++) acc += f[w] * so[(w * 16 + r) * D + dd];
-      if (n_split == 1) {
+      if (n_slots == 1) {
         float v = L > 0.f ? acc / L : 0.f;
         int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
         if (out) out[oi] = v;
         if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), lane);
       } else {
-        int64_t pi = (((int64_t)b * H + h) * n_split + split);
+        int64_t pi = (((int64_t)b * H + h) * n_slots + slot0 + split);
         part_o[pi * D + dd] = acc;
         if (dd == 0) part_ml[pi] = make_float2(mstar, L);
       }
     }
   }
-  if (n_split == 1 || tickets == nullptr) return;
+  if (n_slots == 1 || tickets == nullptr) return;   // (tickets are only passed with n_slots == n_split)
   // the last split CTA of this (sequence, KV group) merges all splits (same order and arithmetic
   // as k_decode_combine) and leaves its ticket at zero for the next launch
   __shared__ int s_ticket;
@@ -293,6 +294,166 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
     }
   }
   if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Shared-prefix ("cascade") decode attention: the first *shared_pages pages of every sequence's
+// block table are the same physical pages (a radix-shared prompt prefix), so one CTA per (KV head,
+// page range) streams each shared page into shared memory ONCE and attends it with the queries of
+// every sequence in the batch: row r of the B*G query rows (sequence r / G, head kvh*G + r % G)
+// belongs to warp r / 16.  Each warp writes its rows' unnormalised partials (o, max, sum) into
+// slot `split` of the split-KV scratch; the per-sequence kernel covers the pages after the shared
+// prefix in the remaining slots and k_decode_combine merges all of them.
+// B*G <= 64 (four 16-row tiles).  Pages in flight per CTA: DEC_STAGES.
+template <int D>
+struct PrefixSmem {
+  __nv_bfloat16 k[DEC_STAGES][PAGE][D + 8];
+  __nv_bfloat16 v[DEC_STAGES][PAGE][D + 8];
+};
+
+template <int D>
+__global__ void __launch_bounds__(128)
+k_decode_attn_prefix(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
+                     const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_table, int bt_stride,
+                     const int* __restrict__ shared_pages, int B, int H, int Hkv, int n_prefix_split,
+                     float scale_log2, float* __restrict__ part_o, float2* __restrict__ part_ml, int n_slots) {
+  constexpr int KS = D / 16;
+  constexpr int NT = D / 8;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  PrefixSmem<D>& sm = *reinterpret_cast<PrefixSmem<D>*>(smem_raw);
+  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int G = H / Hkv, R = B * G;
+  pdl_wait();
+  const int n_shared = *shared_pages;
+  const int pps = (n_shared + n_prefix_split - 1) / n_prefix_split;
+  const int p_begin = min(n_shared, split * pps), p_end = min(n_shared, p_begin + pps);
+
+  // this warp's 16 query rows
+  const int r0 = warp * 16 + gq, r1 = r0 + 8;
+  const bool v0 = r0 < R, v1 = r1 < R;
+  const int b0 = r0 / G, h0 = kvh * G + r0 % G, b1 = r1 / G, h1 = kvh * G + r1 % G;
+  uint32_t qa[KS][4];
+  {
+    const float* q0 = q + ((int64_t)b0 * H + h0) * D;
+    const float* q1 = q + ((int64_t)b1 * H + h1) * D;
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+      int c = ks * 16 + 2 * tq;
+      float2 a0 = v0 ? *reinterpret_cast<const float2*>(q0 + c) : make_float2(0.f, 0.f);
+      float2 a1 = v1 ? *reinterpret_cast<const float2*>(q1 + c) : make_float2(0.f, 0.f);
+      float2 a2 = v0 ? *reinterpret_cast<const float2*>(q0 + c + 8) : make_float2(0.f, 0.f);
+      float2 a3 = v1 ? *reinterpret_cast<const float2*>(q1 + c + 8) : make_float2(0.f, 0.f);
+      qa[ks][0] = pack_bf16(a0.x, a0.y);
+      qa[ks][1] = pack_bf16(a1.x, a1.y);
+      qa[ks][2] = pack_bf16(a2.x, a2.y);
+      qa[ks][3] = pack_bf16(a3.x, a3.y);
+    }
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
+  const bool active = warp * 16 < R;   // warps past the last row tile only help with the copies
+
+  // the shared pages are identical in every block table: read them through sequence 0's row
+  auto issue_page = [&](int p, int buf) {
+    const int pid = block_table[p];
+    const __nv_bfloat16* ks = kc + ((int64_t)pid * Hkv + kvh) * PAGE * D;
+    const __nv_bfloat16* vs = vc + ((int64_t)pid * Hkv + kvh) * PAGE * D;
+    constexpr int CHUNKS = PAGE * D / 8;
+    for (int c = threadIdx.x; c < CHUNKS; c += 128) {
+      int tok = c / (D / 8), part = c % (D / 8);
+      cp_async16(smem_u32(&sm.k[buf][tok][part * 8]), ks + tok * D + part * 8);
+      cp_async16(smem_u32(&sm.v[buf][tok][part * 8]), vs + tok * D + part * 8);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < DEC_STAGES - 1; i++) {
+    if (p_begin + i < p_end) issue_page(p_begin + i, i);
+    else cp_async_commit();
+  }
+  for (int p = p_begin, it = 0; p < p_end; p++, it++) {
+    const int pn = p + DEC_STAGES - 1;
+    // the slot refilled below was consumed in the previous iteration by every warp
+    __syncthreads();
+    if (pn < p_end) issue_page(pn, (it + DEC_STAGES - 1) % DEC_STAGES);
+    else cp_async_commit();
+    cp_async_wait<DEC_STAGES - 1>();
+    __syncthreads();
+    const int buf = it % DEC_STAGES;
+    if (!active) continue;
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int jj = mi >> 1, hh = mi & 1;
+#pragma unroll
+      for (int ks = 0; ks < KS; ks++) {
+        uint32_t x0, x1, x2, x3;
+        ldmatrix_x4(smem_u32(&sm.k[buf][8 * jj + ri][16 * ks + 8 * hh]), x0, x1, x2, x3);
+        mma_bf16_16816(s[0], qa[ks], x0, x1);
+        mma_bf16_16816(s[1], qa[ks], x2, x3);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) s[j][e] *= scale_log2;   // shared pages are full: no mask
+    float mx0 = quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1])));
+    float mx1 = quad_max(fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3])));
+    float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float pr[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      pr[j][0] = exp2f(s[j][0] - mn0);
+      pr[j][1] = exp2f(s[j][1] - mn0);
+      pr[j][2] = exp2f(s[j][2] - mn1);
+      pr[j][3] = exp2f(s[j][3] - mn1);
+    }
+    l0 = l0 * c0 + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
+    l1 = l1 * c1 + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
+#pragma unroll
+    for (int i = 0; i < NT; i++) {
+      o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1;
+    }
+    uint32_t pa[4] = {pack_bf16(pr[0][0], pr[0][1]), pack_bf16(pr[0][2], pr[0][3]), pack_bf16(pr[1][0], pr[1][1]),
+                      pack_bf16(pr[1][2], pr[1][3])};
+    {
+      const int mi = lane >> 3, ri = lane & 7;
+      const int tok = (mi & 1) * 8 + ri, dsel = (mi >> 1) * 8;
+#pragma unroll
+      for (int d = 0; d < NT; d += 2) {
+        uint32_t x0, x1, x2, x3;
+        ldmatrix_x4_trans(smem_u32(&sm.v[buf][tok][8 * d + dsel]), x0, x1, x2, x3);
+        mma_bf16_16816(o[d], pa, x0, x1);
+        mma_bf16_16816(o[d + 1], pa, x2, x3);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  pdl_launch_dependents();
+  if (!active) return;
+  l0 = quad_sum(l0);
+  l1 = quad_sum(l1);
+  // partials of this warp's rows (an empty range leaves max -inf, sum 0)
+  const int64_t pi0 = (((int64_t)b0 * H + h0) * n_slots + split), pi1 = (((int64_t)b1 * H + h1) * n_slots + split);
+#pragma unroll
+  for (int i = 0; i < NT; i++) {
+    const int c = 8 * i + 2 * tq;
+    if (v0) *reinterpret_cast<float2*>(part_o + pi0 * D + c) = make_float2(o[i][0], o[i][1]);
+    if (v1) *reinterpret_cast<float2*>(part_o + pi1 * D + c) = make_float2(o[i][2], o[i][3]);
+  }
+  if (tq == 0) {
+    if (v0) part_ml[pi0] = make_float2(m0, l0);
+    if (v1) part_ml[pi1] = make_float2(m1, l1);
+  }
 }
 
 template <int D>
@@ -511,7 +672,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       torch::Tensor ctx_len, int64_t n_split, int64_t pages_per_split,
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
-                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window) {
+                      c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window,
+                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits) {
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
   const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
@@ -533,16 +695,23 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   const int64_t need = (int64_t)(B - 1) * ldo + (int64_t)H * D;  // last element written + 1
   if (qp) TORCH_CHECK(dp && qx->numel() >= need && ds->numel() >= need / 16, "qx/ds size");
   if (op) TORCH_CHECK(out->numel() >= need && out->is_contiguous(), "out");
+  // cascade: the first *shared_pages pages (the same physical pages in every block table) are
+  // attended once for the whole batch by k_decode_attn_prefix in prefix_splits extra slots
+  const bool cascade = shared_pages.has_value() && prefix_splits > 0 && B * (H / Hkv) <= 64 && window <= 0;
+  const int64_t n_slots = n_split + (cascade ? prefix_splits : 0);
+  if (cascade)
+    TORCH_CHECK(shared_pages->is_cuda() && shared_pages->scalar_type() == torch::kInt32 && shared_pages->numel() >= 1,
+                "decode_attention: shared_pages int32 [1] on the device");
   float* pw = nullptr;
-  if (n_split > 1) {
+  if (n_slots > 1) {
     TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == torch::kFloat32 &&
-                    workspace->numel() >= (int64_t)B * H * n_split * (D + 2),
+                    workspace->numel() >= (int64_t)B * H * n_slots * (D + 2),
                 "decode_attention: workspace too small");
     pw = workspace->data_ptr<float>();
   }
-  float2* pml = pw ? reinterpret_cast<float2*>(pw + (int64_t)B * H * n_split * D) : nullptr;
+  float2* pml = pw ? reinterpret_cast<float2*>(pw + (int64_t)B * H * n_slots * D) : nullptr;
   int* tk = nullptr;  // given: the last split CTA merges (no combine launch)
-  if (n_split > 1 && tickets.has_value()) {
+  if (n_split > 1 && tickets.has_value() && !cascade) {
     TORCH_CHECK(tickets->scalar_type() == torch::kInt32 && tickets->numel() >= (int64_t)B * Hkv,
                 "decode_attention: tickets [B * Hkv] int32");
     tk = tickets->data_ptr<int>();
@@ -555,6 +724,26 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   cfg.stream = stream;
   set_pdl(cfg);
   int bts = (int)block_table.stride(0);
+  const int* skip = cascade ? shared_pages->data_ptr<int>() : nullptr;
+  const int slot0 = cascade ? (int)prefix_splits : 0;
+  if (cascade) {
+    cudaLaunchConfig_t cp = {};
+    cp.gridDim = dim3(Hkv, (unsigned)prefix_splits);
+    cp.blockDim = dim3(128);
+    cp.stream = stream;
+    set_pdl(cp);
+    auto go = [&](auto kern, size_t smem) {
+      cp.dynamicSmemBytes = smem;
+      FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      FAK_CUDA_CHECK(cudaLaunchKernelEx(&cp, kern, (const float*)q.data_ptr<float>(),
+                                        (const __nv_bfloat16*)k_cache.data_ptr(),
+                                        (const __nv_bfloat16*)v_cache.data_ptr(),
+                                        (const int*)block_table.data_ptr<int>(), bts, skip, B, H, Hkv,
+                                        (int)prefix_splits, scale_log2, pw, pml, (int)n_slots));
+    };
+    if (D == 128) go(k_decode_attn_prefix<128>, sizeof(PrefixSmem<128>));
+    else go(k_decode_attn_prefix<64>, sizeof(PrefixSmem<64>));
+  }
   if (D == 128) {
     size_t smem = std::max(sizeof(DecodeSmem<128>), (size_t)(4 * 16 * 128 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -563,7 +752,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
                                       H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb, (int)window));
+                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots));
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -572,9 +761,9 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
                                       H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb, (int)window));
+                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots));
   }
-  if (n_split > 1 && tk == nullptr) {
+  if (n_slots > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
     c2.gridDim = dim3(B, H);
     c2.blockDim = dim3(D);
@@ -582,10 +771,10 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     set_pdl(c2);
     if (D == 128)
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H,
-                                        (int)n_split, op, qp, dp, (int)ldo));
+                                        (int)n_slots, op, qp, dp, (int)ldo));
     else
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H,
-                                        (int)n_split, op, qp, dp, (int)ldo));
+                                        (int)n_slots, op, qp, dp, (int)ldo));
   }
 }
 
@@ -732,14 +921,16 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     e = cudaFuncSetAttribute(k_decode_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<128>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0,
+                             nullptr, 0, n_split);
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
     e = cudaFuncSetAttribute(k_decode_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<64>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
-                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0);
+                             pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0,
+                             nullptr, 0, n_split);
   }
   if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode attention launch: %s", cudaGetErrorString(e));
   if (n_split > 1) {

@@ -99,7 +99,8 @@ class Engine:
         self.runner = ModelRunner(weights, self.kv, max_batch=self.ecfg.max_batch,
                                   max_prefill_tokens=self.ecfg.max_prefill_tokens, max_context=self.max_context,
                                   collectives=collectives, fused_activations=self.ecfg.fused_activations,
-                                  attention_merge=self.ecfg.attention_merge, l2_prefetch=self.ecfg.l2_prefetch)
+                                  attention_merge=self.ecfg.attention_merge, l2_prefetch=self.ecfg.l2_prefetch,
+                                  cascade_attention=self.ecfg.cascade_attention)
         self.bt_width = math.ceil(self.max_context / ps)
         self.waiting: list[Request] = []
         self.swapped: list[Request] = []   # preempted by swap: resumed (K/V copied back) before new work
@@ -427,12 +428,13 @@ class Engine:
             ctx[k] = p + 1
             bt[k, :len(r.pages)] = r.pages
         dev = self.device
-        h = torch.from_numpy(np.concatenate([ids, pos, slot, ctx])).pin_memory()
+        shared = np.array([self._shared_pages(bt, ctx)], np.int32)
+        h = torch.from_numpy(np.concatenate([ids, pos, slot, ctx, shared])).pin_memory()
         d = h.to(dev, non_blocking=True)
         btd = torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True)
         greedy = all(r.sampling.greedy for r in lanes)
         out = self.runner.decode(d[0:B], d[B:2 * B], d[2 * B:3 * B], btd, d[3 * B:4 * B], B,
-                                 use_graph=self._graphs_ready)
+                                 use_graph=self._graphs_ready, shared=d[4 * B:4 * B + 1])
         self.stats["h2d_bytes"] += h.numel() * 4 + bt.size * 4
         if greedy:
             toks = out.cpu().tolist()
@@ -445,6 +447,19 @@ class Engine:
             r.n_kv += 1
             self._emit(r, tok)
         self.running = [r for r in self.running if not r.finished]
+
+    def _shared_pages(self, bt: np.ndarray, ctx: np.ndarray) -> int:
+        """Leading block-table pages that are the same physical page in every lane and lie before
+        every lane's current page (the radix-shared prefix of the batch): cascade attention reads
+        them once for all lanes."""
+        B = bt.shape[0]
+        if B < 2:
+            return 0
+        k = int((ctx.min() - 1) // self.ecfg.page_size)
+        if k <= 0:
+            return 0
+        same = (bt[:, :k] == bt[0:1, :k]).all(axis=0)
+        return int(k if same.all() else np.argmin(same))
 
     def _run_decode_spec(self, lanes: list[Request], k: int) -> None:
         """Greedy self-speculative decode (reference: spec.SpeculativeGreedy, internal/spec/spec.go:214-300).

@@ -84,7 +84,7 @@ class PrefillMeta:
 class ModelRunner:
     def __init__(self, weights: ModelWeights, kv: KVCache, max_batch: int = 64, max_prefill_tokens: int = 4096,
                  max_context: int | None = None, collectives=None, fused_activations: bool = False,
-                 attention_merge: bool = False, l2_prefetch: bool = False):
+                 attention_merge: bool = False, l2_prefetch: bool = False, cascade_attention: bool = True):
         self.w = weights
         self.cfg: ModelConfig = weights.cfg
         self.kv = kv
@@ -128,6 +128,12 @@ class ModelRunner:
         self.max_split = 64
         self.attn_ws = torch.zeros(B * self.Hq * self.max_split * (self.D + 2), dtype=torch.float32, device=dev)
         self.attn_tickets = torch.zeros(B * self.Hkv, dtype=torch.int32, device=dev)  # split-merge tickets
+        # cascade attention: pages shared by every lane of the step (a radix-shared prefix) are
+        # attended once for the whole batch; the count lives on the device so graphs stay valid
+        self.cascade = cascade_attention
+        self.shared_pages = torch.zeros(1, dtype=torch.int32, device=dev)
+        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
+        self.prefix_splits = min(self.max_split - 16, max(16, 2 * n_sm // max(1, self.Hkv)))
         # per-device kernel scratch, allocated here so no graph capture allocates it
         mats = [weights.lm_head] + [m for L in weights.layers
                                     for m in [s for s, _ in L.qkv] + [L.o, L.gate_up, L.down]]
@@ -144,6 +150,12 @@ class ModelRunner:
         splits, so short contexts just leave some splits empty.  16 measured best across batch 1-5
         at 2K-9K contexts on B200 (8 is faster at batch 5 but leaves batch 1 with 32 CTAs)."""
         return 16
+
+    def cascade_args(self, B: int, window: int = 0) -> dict:
+        """Arguments that turn on cascade attention for a B-lane step (none when it cannot apply)."""
+        if not self.cascade or B < 2 or window > 0 or B * (self.Hq // max(1, self.Hkv)) > 64:
+            return {}
+        return {"shared_pages": self.shared_pages, "prefix_splits": self.prefix_splits}
 
     def _pf(self, w):
         """Tile-packed weights of ``w`` to warm L2 with during the current kernel (or None)."""
@@ -168,7 +180,8 @@ class ModelRunner:
         if self.coll is None:
             K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_attn,
                                workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None,
-                               prefetch=self._pf(L.o), window=cfg.layer_window(i))
+                               prefetch=self._pf(L.o), window=cfg.layer_window(i),
+                               **self.cascade_args(B, cfg.layer_window(i)))
             K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD, prefetch=self._pf(L.gate_up))
         else:
             self.coll.decode_attn_o(self, i, B, bt, ctx, n_split)
@@ -253,9 +266,15 @@ class ModelRunner:
         cands = [b for b, nl in self._graphs if b >= B and nl == n_layers]
         return min(cands) if cands else None
 
-    def decode(self, ids, pos, slot, bt, ctx, B: int, use_graph: bool = True, n_layers: int | None = None
-               ) -> torch.Tensor:
-        """Decode one token for B lanes; returns next ids (device int32 [B])."""
+    def decode(self, ids, pos, slot, bt, ctx, B: int, use_graph: bool = True, n_layers: int | None = None,
+               shared: torch.Tensor | None = None) -> torch.Tensor:
+        """Decode one token for B lanes; returns next ids (device int32 [B]).  ``shared`` (int32 [1]
+        on the device): leading block-table pages that are the same physical pages in every lane
+        and lie before every lane's current page (cascade attention); None = 0."""
+        if shared is not None:
+            self.shared_pages.copy_(shared)
+        else:
+            self.shared_pages.zero_()
         bucket = self.graph_bucket(B, n_layers) if use_graph else None
         if bucket is None:
             self.decode_eager(ids, pos, slot, bt, ctx, B, n_layers=n_layers)

@@ -126,15 +126,21 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
                      workspace=None, ldo: int = 0, tickets=None, prefetch: torch.Tensor | None = None,
-                     window: int = 0) -> None:
+                     window: int = 0, shared_pages: torch.Tensor | None = None, prefix_splits: int = 0) -> None:
     """ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
     [B * kv heads]; when given, the last split of each (sequence, KV group) merges the splits in the
     same kernel instead of a separate combine launch (the kernel leaves the tickets at zero).
-    window > 0: sliding-window attention over the last ``window`` keys."""
+    window > 0: sliding-window attention over the last ``window`` keys.
+    shared_pages (int32 [1] on the device) with prefix_splits > 0: cascade attention -- the first
+    *shared_pages pages, identical in every block table, are attended once for the whole batch
+    (workspace sized for n_split + prefix_splits slots)."""
     ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
                            act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo,
-                           tickets, prefetch, window)
-    count(2 if n_split > 1 and tickets is None else 1)
+                           tickets, prefetch, window, shared_pages, prefix_splits)
+    cascade = shared_pages is not None and prefix_splits > 0 and window <= 0 and \
+        q.shape[0] * (q.shape[1] // k_cache.shape[1]) <= 64
+    n_slots = n_split + (prefix_splits if cascade else 0)
+    count((1 if cascade else 0) + (2 if n_slots > 1 and (tickets is None or cascade) else 1))
 
 
 def prefill_attention(q, k_cache, v_cache, block_table, meta, out, window: int = 0) -> None:

@@ -105,7 +105,8 @@ class P2PTP(NcclTP):
     def decode_attn_o(self, rn, i: int, B: int, bt, ctx, n_split: int) -> None:
         C, kv, D, H = ext(), rn.kv, self.D, self.cfg.n_heads
         K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_mine, workspace=rn.attn_ws,
-                           tickets=rn.attn_tickets, ldo=H * D, window=self.cfg.layer_window(i))
+                           tickets=rn.attn_tickets, ldo=H * D, window=self.cfg.layer_window(i),
+                           **rn.cascade_args(B, self.cfg.layer_window(i)))
         # codes and (scale, sum) pairs of this rank's heads, pushed to every rank in one launch
         C.p2p_allgather_cols(self.peers, self.buf[self.q_off:], H * D, self.q_off, H * D, self.h0 * D, self.nh * D,
                              B, self.flags_off, 3 * i, self.me, self.counters, self.err, AG_CTAS,

@@ -76,7 +76,8 @@ class NcclTP:
             self.act_local.q[:B].zero_()
             self.act_local.ds[:B].zero_()
         K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_local, workspace=rn.attn_ws,
-                           tickets=rn.attn_tickets, ldo=self.maxHq * self.D, window=rn.cfg.layer_window(i))
+                           tickets=rn.attn_tickets, ldo=self.maxHq * self.D, window=rn.cfg.layer_window(i),
+                           **rn.cascade_args(B, rn.cfg.layer_window(i)))
         self._gather_heads_q(B, rn.act_attn)
         K.gemv(rn.w.layers[i].o, rn.act_attn, B, rn.x[:B], None, K.EPI_ADD)
 

@@ -409,3 +409,38 @@ def test_dsa_index_topk_and_sparse_attention(n_keys, qpos, topk):
     assert sel.tolist() == want_sel
     want = sparse_attend_ref(q, kc, vc, want_sel, 1 / math.sqrt(kd))
     assert torch.allclose(out, want, atol=1e-4, rtol=1e-4), (out - want).abs().max()
+
+
+
+@pytest.mark.parametrize("D,H,Hkv,B", [(128, 28, 4, 5), (64, 9, 3, 2), (128, 8, 8, 8)])
+@pytest.mark.parametrize("shared", [0, 3, 40])
+def test_decode_attention_cascade(D, H, Hkv, B, shared):
+    """Cascade attention (the batch's shared prefix pages attended once for all lanes) gives the
+    per-sequence result: same pages, same softmax, merged with each lane's own suffix."""
+    from fak_b200.ops import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(shared + B)
+    n_pages = 512
+    kc = torch.randn(n_pages, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+    vc = torch.randn(n_pages, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+    ctx = [shared * 16 + 1 + 37 * i for i in range(B)]
+    W = max(math.ceil(c / 16) for c in ctx)
+    bt = torch.zeros(B, W, dtype=torch.int32)
+    nxt = 1 + shared
+    for i, c in enumerate(ctx):
+        bt[i, :shared] = torch.arange(1, 1 + shared)                 # the same physical prefix pages
+        own = math.ceil(c / 16) - shared
+        bt[i, shared:shared + own] = torch.arange(nxt, nxt + own)
+        nxt += own
+    bt = bt.cuda()
+    q = torch.randn(B, H, D, device="cuda", generator=g)
+    ctx_t = torch.tensor(ctx, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(B * H * 64 * (D + 2), device="cuda")
+    ref = torch.zeros(B, H * D, device="cuda")
+    K.decode_attention(q, kc, vc, bt, ctx_t, 16, out=ref, workspace=ws)
+    out = torch.zeros(B, H * D, device="cuda")
+    sp = torch.tensor([shared], dtype=torch.int32, device="cuda")
+    K.decode_attention(q, kc, vc, bt, ctx_t, 16, out=out, workspace=ws, shared_pages=sp, prefix_splits=32)
+    torch.cuda.synchronize()
+    assert torch.allclose(out, ref, atol=2e-3, rtol=2e-3), (out - ref).abs().max()
+    if shared == 0:
+        assert torch.equal(out, ref)   # nothing shared: bit-identical to the plain path
