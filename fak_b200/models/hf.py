@@ -84,8 +84,8 @@ def config_from_hf(hf: dict) -> ModelConfig:
         arch = "qwen3"
     elif "qwen2" in arch_name:
         arch = "qwen2"
-    elif "llama" in arch_name or "mistral" in arch_name:
-        arch = "llama"
+    elif "llama" in arch_name or "mistral" in arch_name or "phi3" in arch_name:
+        arch = "llama"   # Phi-3: fused qkv / gate_up projections are split on load
     else:
         raise ValueError(f"unsupported HF architecture {arch_name!r}")
     d, H = int(hf["hidden_size"]), int(hf["num_attention_heads"])
@@ -103,7 +103,7 @@ def config_from_hf(hf: dict) -> ModelConfig:
         expert_ffn_dim=int(hf.get("moe_intermediate_size", 0)) if arch == "qwen3moe" else 0,
         norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
         max_context=int(hf.get("max_position_embeddings", 32768)),
-        rope_scaling=_hf_rope_scaling(rp),
+        rope_scaling=_hf_rope_scaling(rp, hf),
         **_hf_sliding_window(hf, int(hf["num_hidden_layers"])),
         bos_token_id=int(hf.get("bos_token_id") or 1), eos_token_id=int(hf.get("eos_token_id") or 2),
         name=str(hf.get("_name_or_path", arch_name)),
@@ -130,7 +130,7 @@ def _hf_sliding_window(hf: dict, n_layers: int) -> dict:
     return {"sliding_window": w}
 
 
-def _hf_rope_scaling(rs: dict | None) -> dict | None:
+def _hf_rope_scaling(rs: dict | None, hf: dict | None = None) -> dict | None:
     if not rs:
         return None
     kind = str(rs.get("rope_type") or rs.get("type") or "default").lower()
@@ -138,6 +138,8 @@ def _hf_rope_scaling(rs: dict | None) -> dict | None:
         return None
     out = {k: v for k, v in rs.items() if k not in ("rope_type", "type", "rope_theta") and v is not None}
     out["type"] = kind
+    if hf and "original_max_position_embeddings" not in out and hf.get("original_max_position_embeddings"):
+        out["original_max_position_embeddings"] = int(hf["original_max_position_embeddings"])   # Phi-3
     return out
 
 
@@ -242,6 +244,19 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
             if m:
                 key = f"blk.{m.group(1)}.{_EXP_NAME[m.group(3)]}"
                 experts.setdefault(key, {})[int(m.group(2))] = (dt, arr)
+                continue
+            m2 = re.fullmatch(r"model\.layers\.(\d+)\.(self_attn\.qkv_proj|mlp\.gate_up_proj)\.weight", n)
+            if m2:   # fused projections: row ranges of one matrix
+                i = m2.group(1)
+                if m2.group(2) == "self_attn.qkv_proj":
+                    q, kv = cfg.q_dim, cfg.kv_dim
+                    parts = (("attn_q", 0, q), ("attn_k", q, q + kv), ("attn_v", q + kv, q + 2 * kv))
+                else:
+                    f = shape[0] // 2
+                    parts = (("ffn_gate", 0, f), ("ffn_up", f, 2 * f))
+                for nm, a, b in parts:
+                    sub = arr[a:b]
+                    table[f"blk.{i}.{nm}.weight"] = (dt, (b - a,) + tuple(shape[1:]), sub)
                 continue
             g = gguf_name(n)
             if g is not None:

@@ -66,3 +66,41 @@ def test_hf_source_feeds_the_device_loader_shapes(tmp_path):
     with pytest.raises(ValueError):
         config_from_hf({"architectures": ["GPT2LMHeadModel"], "hidden_size": 8, "num_attention_heads": 2,
                         "num_hidden_layers": 1, "vocab_size": 10})
+
+
+@pytest.mark.parametrize("longrope", [False, True])
+def test_phi3_fused_projections_and_longrope(longrope, tmp_path):
+    """Phi-3: fused qkv / gate_up projections split on load; longrope factors pinned to the
+    model's max-context regime."""
+    kw = dict(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2, num_attention_heads=4,
+              num_key_value_heads=2, max_position_embeddings=512, pad_token_id=0, bos_token_id=1, eos_token_id=2,
+              rms_norm_eps=1e-5, tie_word_embeddings=False)
+    if longrope:
+        kw["original_max_position_embeddings"] = 128
+        kw["rope_parameters"] = {"rope_type": "longrope", "rope_theta": 10000.0,
+                                 "short_factor": [1.0 + 0.02 * i for i in range(16)],
+                                 "long_factor": [1.0 + 0.3 * i for i in range(16)]}
+    m = transformers.Phi3ForCausalLM(transformers.Phi3Config(**kw))
+    torch.manual_seed(0)
+    for p in m.parameters():
+        torch.nn.init.normal_(p, std=0.05 if p.dim() > 1 else 0.5)
+    m = m.eval().float()
+    d = _save(m, tmp_path)
+    cfg, tensors = load_reference_tensors_hf(d)
+    assert cfg.arch == "llama" and tensors["blk.0.attn_k.weight"].shape == (64, 128)
+    if longrope:
+        assert dict(cfg.rope_scaling)["original_max_position_embeddings"] == 128
+    ref = ReferenceModel(cfg, tensors)
+    ids = torch.tensor([3, 17, 200, 45, 9, 311, 7, 99])
+    with torch.no_grad():
+        # transformers switches longrope factors by the live length; our tables pin the long factor
+        # (the model's max context exceeds the original), which transformers uses past 128 tokens
+        want = m(ids[None]).logits[0] if not longrope else None
+    got = ref.forward(ids)
+    if not longrope:
+        assert torch.allclose(got, want, atol=2e-4, rtol=1e-4), (got - want).abs().max()
+    else:
+        long_ids = torch.randint(0, 512, (140,), generator=torch.Generator().manual_seed(1))
+        with torch.no_grad():
+            want_long = m(long_ids[None]).logits[0]
+        assert torch.allclose(ref.forward(long_ids), want_long, atol=3e-4, rtol=1e-4)
