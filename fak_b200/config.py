@@ -20,7 +20,7 @@ from typing import Any
 
 @dataclasses.dataclass(frozen=True)
 class ModelConfig:
-    arch: str  # "llama" | "qwen2" | "qwen3" | "qwen3moe"
+    arch: str  # "llama" | "qwen2" | "qwen3" | "qwen3moe" | "gemma2"
     n_layers: int
     d_model: int
     n_heads: int
@@ -45,6 +45,15 @@ class ModelConfig:
     # on the layers in ``swa_layers`` (None = every layer)
     sliding_window: int = 0
     swa_layers: tuple | None = None
+    # Gemma-style blocks: gated activation ("silu" or "gelu_tanh"), score / logit soft-capping
+    # (cap * tanh(x / cap); 0 = none), sandwich norms (a norm after attention and after the FFN,
+    # before each residual add), embedding scale, attention scale (0 = 1/sqrt(head_dim))
+    act: str = "silu"
+    attn_softcap: float = 0.0
+    final_softcap: float = 0.0
+    sandwich_norms: bool = False
+    embed_scale: float = 1.0
+    attn_scale: float = 0.0
     bos_token_id: int = 1
     eos_token_id: int = 2
     name: str = ""
@@ -123,6 +132,11 @@ PRESETS: dict[str, ModelConfig] = {
                               max_context=1024, name="tiny-llama"),
     "tiny-qwen2": ModelConfig("qwen2", 2, 512, 8, 2, 64, 1024, 1024, 1e-6, 1e6, qkv_bias=True,
                               max_context=2048, name="tiny-qwen2"),
+    # Gemma-2 shaped test model: GELU-tanh FFN, sandwich norms, soft-capping, alternating windows
+    "tiny-gemma2": ModelConfig("gemma2", 2, 256, 4, 2, 64, 512, 512, 1e-6, 1e4, tie_embeddings=True,
+                               act="gelu_tanh", attn_softcap=50.0, final_softcap=30.0, sandwich_norms=True,
+                               embed_scale=16.0, sliding_window=32, swa_layers=(0,), max_context=1024,
+                               name="tiny-gemma2"),
     "tiny-qwen3moe": ModelConfig("qwen3moe", 2, 512, 8, 2, 64, 1024, 1024, 1e-6, 1e6, qk_norm=True,
                                  n_experts=8, n_experts_used=2, expert_ffn_dim=256, max_context=2048,
                                  name="tiny-qwen3moe"),
@@ -140,7 +154,7 @@ def config_from_gguf_metadata(meta: dict[str, Any], tensor_shapes: dict[str, tup
                               ) -> ModelConfig:
     """Derive a ModelConfig from GGUF metadata (keys ``{arch}.*`` as written by llama.cpp)."""
     arch = meta.get("general.architecture")
-    if arch not in ("llama", "qwen2", "qwen3", "qwen3moe", "mistral"):
+    if arch not in ("llama", "qwen2", "qwen3", "qwen3moe", "mistral", "gemma2"):
         raise ValueError(f"unsupported GGUF architecture {arch!r}")
 
     def g(key: str, default: Any = None) -> Any:
@@ -184,6 +198,12 @@ def config_from_gguf_metadata(meta: dict[str, Any], tensor_shapes: dict[str, tup
         eos_token_id=int(meta.get("tokenizer.ggml.eos_token_id", 2)),
         name=str(meta.get("general.name", "")),
     )
+    if arch == "gemma2":   # GELU-tanh FFN, sandwich norms, soft-capping, every other layer windowed
+        cfg = cfg.replace(act="gelu_tanh", sandwich_norms=True, embed_scale=float(d) ** 0.5,
+                          attn_softcap=float(g("attn_logit_softcapping", 50.0) or 0.0),
+                          final_softcap=float(g("final_logit_softcapping", 30.0) or 0.0),
+                          sliding_window=int(g("attention.sliding_window", 4096) or 0),
+                          swa_layers=tuple(range(0, cfg.n_layers, 2)))
     cfg.validate()
     return cfg
 

@@ -12,7 +12,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
                       c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window,
-                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits);
+                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits, double scale, double softcap);
 void kv_move(torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor src_slot, torch::Tensor dst_slot,
              torch::Tensor rot, torch::Tensor cos_n, torch::Tensor sin_n);
 torch::Tensor dsa_index_score(torch::Tensor iq, torch::Tensor ik, torch::Tensor w, int64_t qpos, double scale);
@@ -21,10 +21,12 @@ torch::Tensor dsa_sparse_attend(torch::Tensor q, torch::Tensor k_cache, torch::T
                                 torch::Tensor count, double scale);
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
-                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window);
+                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window, double scale,
+                       double softcap);
 void embed(torch::Tensor table, int64_t qtype, int64_t pitch, int64_t V, int64_t d, torch::Tensor ids,
            c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> out_bf16,
-           c10::optional<torch::Tensor> err);
+           c10::optional<torch::Tensor> err, double scale);
+void rmsnorm_add(torch::Tensor y, torch::Tensor w, double eps, torch::Tensor x);
 void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Tensor cos_t, torch::Tensor sin_t,
              int64_t H, int64_t Hkv, c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double eps,
              c10::optional<torch::Tensor> q_f32, c10::optional<torch::Tensor> q_bf16, torch::Tensor k_cache,
@@ -79,12 +81,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("pages_per_split"), pybind11::arg("out"), pybind11::arg("qx"), pybind11::arg("ds"),
         pybind11::arg("workspace"), pybind11::arg("ldo") = 0, pybind11::arg("tickets") = pybind11::none(),
         pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("window") = 0,
-        pybind11::arg("shared_pages") = pybind11::none(), pybind11::arg("prefix_splits") = 0);
+        pybind11::arg("shared_pages") = pybind11::none(), pybind11::arg("prefix_splits") = 0,
+        pybind11::arg("scale") = 0.0, pybind11::arg("softcap") = 0.0);
   m.def("prefill_attention", &prefill_attention, pybind11::arg("q"), pybind11::arg("k_cache"),
         pybind11::arg("v_cache"), pybind11::arg("block_table"), pybind11::arg("tile_seq"), pybind11::arg("tile_q0"),
         pybind11::arg("seq_qoff"), pybind11::arg("seq_qlen"), pybind11::arg("seq_pos0"), pybind11::arg("n_tiles"),
-        pybind11::arg("out"), pybind11::arg("window") = 0);
-  m.def("embed", &embed);
+        pybind11::arg("out"), pybind11::arg("window") = 0, pybind11::arg("scale") = 0.0,
+        pybind11::arg("softcap") = 0.0);
+  m.def("embed", &embed, pybind11::arg("table"), pybind11::arg("qtype"), pybind11::arg("pitch"), pybind11::arg("V"),
+        pybind11::arg("d"), pybind11::arg("ids"), pybind11::arg("out_f32"), pybind11::arg("out_bf16"),
+        pybind11::arg("err"), pybind11::arg("scale") = 1.0);
+  m.def("rmsnorm_add", &rmsnorm_add);
   m.def("dsa_index_score", &dsa_index_score);
   m.def("dsa_topk", &dsa_topk);
   m.def("dsa_sparse_attend", &dsa_sparse_attend);

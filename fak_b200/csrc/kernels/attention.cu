@@ -42,6 +42,12 @@ FAK_DEV float quad_sum(float v) {
   return v;
 }
 
+// attention logit in the log2 domain: raw * scale * log2(e), or with soft-capping (cap_out > 0)
+// cap * tanh(raw * scale / cap) * log2(e)  (cap_in = scale / cap, cap_out = cap * log2(e))
+FAK_DEV float attn_logit(float raw, float scale_log2, float cap_in, float cap_out) {
+  return cap_out > 0.f ? cap_out * tanhf(raw * cap_in) : raw * scale_log2;
+}
+
 // quantize one 32-wide block held one value per lane; writes int8 codes and (scale, sum of the
 // dequantized values d * sum(codes))
 FAK_DEV void warp_quant_store(float v, int8_t* qdst, float2* dsdst, int lane) {
@@ -70,7 +76,8 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
               int n_split, int pages_per_split, float scale_log2, float* __restrict__ part_o,
               float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
               float2* __restrict__ ds, int ldo, int* __restrict__ tickets, const uint8_t* __restrict__ pf,
-              int64_t pf_bytes, int win, const int* __restrict__ skip_pages, int slot0, int n_slots) {
+              int64_t pf_bytes, int win, const int* __restrict__ skip_pages, int slot0, int n_slots, float cap_in,
+              float cap_out) {
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -171,7 +178,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         int tok = 8 * j + 2 * tq + (e & 1);
-        s[j][e] = (tok < valid && tok >= first) ? s[j][e] * scale_log2 : NEG_INF;
+        s[j][e] = (tok < valid && tok >= first) ? attn_logit(s[j][e], scale_log2, cap_in, cap_out) : NEG_INF;
       }
     }
     float mx0 = quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1])));
@@ -316,7 +323,8 @@ __global__ void __launch_bounds__(128)
 k_decode_attn_prefix(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
                      const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_table, int bt_stride,
                      const int* __restrict__ shared_pages, int B, int H, int Hkv, int n_prefix_split,
-                     float scale_log2, float* __restrict__ part_o, float2* __restrict__ part_ml, int n_slots) {
+                     float scale_log2, float* __restrict__ part_o, float2* __restrict__ part_ml, int n_slots,
+                     float cap_in, float cap_out) {
   constexpr int KS = D / 16;
   constexpr int NT = D / 8;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -402,7 +410,7 @@ k_decode_attn_prefix(const float* __restrict__ q, const __nv_bfloat16* __restric
 #pragma unroll
     for (int j = 0; j < 2; j++)
 #pragma unroll
-      for (int e = 0; e < 4; e++) s[j][e] *= scale_log2;   // shared pages are full: no mask
+      for (int e = 0; e < 4; e++) s[j][e] = attn_logit(s[j][e], scale_log2, cap_in, cap_out);   // full pages: no mask
     float mx0 = quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1])));
     float mx1 = quad_max(fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3])));
     float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
@@ -492,13 +500,13 @@ struct PrefillSmem {
   __nv_bfloat16 v[2][PF_KV][D + 8];
 };
 
-template <int D>
+template <int D, bool CAP>   // CAP: soft-capped logits (a separate instantiation keeps the plain one lean)
 __global__ void __launch_bounds__(128, D == 128 ? 3 : 0)   // D=128: keep 3 CTAs per SM (<= 168 registers)
 k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv_bfloat16* __restrict__ kc,
                const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_table, int bt_stride,
                const int* __restrict__ tile_seq, const int* __restrict__ tile_q0, const int* __restrict__ seq_qoff,
                const int* __restrict__ seq_qlen, const int* __restrict__ seq_pos0, int H, int Hkv, float scale_log2,
-               __nv_bfloat16* __restrict__ out, int64_t out_stride, int win) {
+               __nv_bfloat16* __restrict__ out, int64_t out_stride, int win, float cap_in, float cap_out) {
   constexpr int KS = D / 16;
   constexpr int NT = D / 8;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -590,7 +598,8 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
         int kp = kt * PF_KV + 8 * j + 2 * tq + (e & 1);
         int qp = (e < 2) ? qpos0 : qpos1;
         int lo = (e < 2) ? lo0 : lo1;
-        s[j][e] = (kp <= qp && kp > lo && kp < kv_end) ? s[j][e] * scale_log2 : NEG_INF;
+        const float lg = CAP ? cap_out * tanhf(s[j][e] * cap_in) : s[j][e] * scale_log2;
+        s[j][e] = (kp <= qp && kp > lo && kp < kv_end) ? lg : NEG_INF;
       }
     }
     float mx0 = NEG_INF, mx1 = NEG_INF;
@@ -673,7 +682,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
                       c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window,
-                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits) {
+                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits, double scale, double softcap) {
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
   const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
@@ -716,7 +725,11 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                 "decode_attention: tickets [B * Hkv] int32");
     tk = tickets->data_ptr<int>();
   }
-  float scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
+  // logit scale (default 1/sqrt(D)) and optional soft-cap, in the log2 domain of the kernels
+  const float sc = scale > 0 ? (float)scale : 1.0f / sqrtf((float)D);
+  float scale_log2 = sc * 1.4426950408889634f;
+  const float cap_in = softcap > 0 ? sc / (float)softcap : 0.f;
+  const float cap_out = softcap > 0 ? (float)softcap * 1.4426950408889634f : 0.f;
   auto stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(Hkv, B, (unsigned)n_split);
@@ -739,7 +752,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                         (const __nv_bfloat16*)k_cache.data_ptr(),
                                         (const __nv_bfloat16*)v_cache.data_ptr(),
                                         (const int*)block_table.data_ptr<int>(), bts, skip, B, H, Hkv,
-                                        (int)prefix_splits, scale_log2, pw, pml, (int)n_slots));
+                                        (int)prefix_splits, scale_log2, pw, pml, (int)n_slots, cap_in, cap_out));
     };
     if (D == 128) go(k_decode_attn_prefix<128>, sizeof(PrefixSmem<128>));
     else go(k_decode_attn_prefix<64>, sizeof(PrefixSmem<64>));
@@ -752,7 +765,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
                                       H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots));
+                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots, cap_in, cap_out));
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -761,7 +774,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
                                       H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots));
+                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots, cap_in, cap_out));
   }
   if (n_slots > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
@@ -782,7 +795,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
 // Per-tile metadata (int32, device): tile_seq, tile_q0; per-sequence: seq_qoff, seq_qlen, seq_pos0.
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
-                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window) {
+                       torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window, double scale,
+                       double softcap) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.stride(2) == 1, "q [T,H,D] bf16");
   TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
   int H = (int)q.size(1), D = (int)q.size(2), Hkv = (int)k_cache.size(1);
@@ -791,7 +805,11 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
   TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "out [T,H*D] bf16");
   TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && block_table.stride(1) == 1, "block_table");
   if (n_tiles == 0) return;
-  float scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
+  // logit scale (default 1/sqrt(D)) and optional soft-cap, in the log2 domain of the kernels
+  const float sc = scale > 0 ? (float)scale : 1.0f / sqrtf((float)D);
+  float scale_log2 = sc * 1.4426950408889634f;
+  const float cap_in = softcap > 0 ? sc / (float)softcap : 0.f;
+  const float cap_out = softcap > 0 ? (float)softcap * 1.4426950408889634f : 0.f;
   auto stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)n_tiles, H);
@@ -806,10 +824,15 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
         (const __nv_bfloat16*)v_cache.data_ptr(), (const int*)block_table.data_ptr<int>(), (int)block_table.stride(0),
         (const int*)tile_seq.data_ptr<int>(), (const int*)tile_q0.data_ptr<int>(), (const int*)seq_qoff.data_ptr<int>(),
         (const int*)seq_qlen.data_ptr<int>(), (const int*)seq_pos0.data_ptr<int>(), H, Hkv, scale_log2,
-        (__nv_bfloat16*)out.data_ptr(), (int64_t)out.stride(0), (int)window));
+        (__nv_bfloat16*)out.data_ptr(), (int64_t)out.stride(0), (int)window, cap_in, cap_out));
   };
-  if (D == 128) args(k_prefill_attn<128>, sizeof(PrefillSmem<128>));
-  else args(k_prefill_attn<64>, sizeof(PrefillSmem<64>));
+  if (D == 128) {
+    if (cap_out > 0.f) args(k_prefill_attn<128, true>, sizeof(PrefillSmem<128>));
+    else args(k_prefill_attn<128, false>, sizeof(PrefillSmem<128>));
+  } else {
+    if (cap_out > 0.f) args(k_prefill_attn<64, true>, sizeof(PrefillSmem<64>));
+    else args(k_prefill_attn<64, false>, sizeof(PrefillSmem<64>));
+  }
 }
 
 // =============================================================================================
@@ -922,7 +945,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<128>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
                              pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0,
-                             nullptr, 0, n_split);
+                             nullptr, 0, n_split, 0.f, 0.f);
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -930,7 +953,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<64>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
                              pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0,
-                             nullptr, 0, n_split);
+                             nullptr, 0, n_split, 0.f, 0.f);
   }
   if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode attention launch: %s", cudaGetErrorString(e));
   if (n_split > 1) {

@@ -78,6 +78,10 @@ FAK_DEV int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 FAK_DEV float i2f_exact22(int c) { return __int_as_float(c + 0x4B400000) - 12582912.0f; }
 
 FAK_DEV float silu(float x) { return x / (1.0f + __expf(-x)); }
+// GELU, tanh approximation (Hendrycks & Gimpel): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+FAK_DEV float gelu_tanh(float x) { return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x))); }
+// gated-FFN activation of the fused gate/up epilogues: 2 = SiLU (SwiGLU), 3 = GELU-tanh (GEGLU)
+FAK_DEV float gated_act(int epi, float g) { return epi == 3 ? gelu_tanh(g) : silu(g); }
 
 FAK_DEV float bf16_bits_lo(uint32_t v) { return __uint_as_float(v << 16); }
 FAK_DEV float bf16_bits_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }

@@ -46,7 +46,7 @@ FAK_DEV float dequant_one(const uint8_t* row, int qtype, int c) {
 
 __global__ void k_embed(const uint8_t* __restrict__ table, int qtype, int64_t pitch, int V, int d,
                         const int* __restrict__ ids, float* __restrict__ out_f32, __nv_bfloat16* __restrict__ out_bf16,
-                        int* __restrict__ err) {
+                        int* __restrict__ err, float scale) {
   pdl_wait();
   int t = blockIdx.x;
   int id = ids[t];
@@ -56,7 +56,7 @@ __global__ void k_embed(const uint8_t* __restrict__ table, int qtype, int64_t pi
   }
   const uint8_t* row = table + (int64_t)id * pitch;
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float v = dequant_one(row, qtype, c);
+    float v = dequant_one(row, qtype, c) * scale;   // scale: embedding multiplier (Gemma: sqrt(d))
     if (out_f32) out_f32[(int64_t)t * d + c] = v;
     if (out_bf16) out_bf16[(int64_t)t * d + c] = __float2bfloat16_rn(v);
   }
@@ -253,7 +253,7 @@ cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem = 0) {
 
 void embed(torch::Tensor table, int64_t qtype, int64_t pitch, int64_t V, int64_t d, torch::Tensor ids,
            c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> out_bf16,
-           c10::optional<torch::Tensor> err) {
+           c10::optional<torch::Tensor> err, double scale) {
   TORCH_CHECK(table.is_cuda() && table.scalar_type() == torch::kUInt8, "table");
   TORCH_CHECK(ids.scalar_type() == torch::kInt32 && ids.is_contiguous(), "ids int32");
   int T = (int)ids.numel();
@@ -265,7 +265,42 @@ void embed(torch::Tensor table, int64_t qtype, int64_t pitch, int64_t V, int64_t
   int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
   auto cfg = make_cfg(dim3(T), dim3(256));
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_embed, (const uint8_t*)table.data_ptr<uint8_t>(), (int)qtype, pitch, (int)V,
-                                    (int)d, (const int*)ids.data_ptr<int>(), of, ob, ep));
+                                    (int)d, (const int*)ids.data_ptr<int>(), of, ob, ep, (float)scale));
+}
+
+// x[t] += rmsnorm(y[t]) * w  (Gemma's sandwich norms: the attention / FFN output is normalised
+// before the residual add).  One CTA of 256 threads per row; y and x rows of d floats.
+__global__ void k_rmsnorm_add(const float* __restrict__ y, int64_t ldy, const float* __restrict__ w, float eps,
+                              int d, float* __restrict__ x, int64_t ldx) {
+  __shared__ float red[8];
+  pdl_wait();
+  const int t = blockIdx.x;
+  const float* yr = y + (int64_t)t * ldy;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) ss += yr[c] * yr[c];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) tot += red[i];
+  const float inv = rsqrtf(tot / (float)d + eps);
+  pdl_launch_dependents();
+  float* xr = x + (int64_t)t * ldx;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) xr[c] += yr[c] * inv * w[c];
+}
+
+void rmsnorm_add(torch::Tensor y, torch::Tensor w, double eps, torch::Tensor x) {
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == torch::kFloat32 && y.dim() == 2 && y.stride(1) == 1, "y [T, d] f32");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.dim() == 2 && x.stride(1) == 1 && x.size(0) >= y.size(0) &&
+                  x.size(1) == y.size(1), "x [T, d] f32");
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.numel() == y.size(1), "w [d] f32");
+  const int T = (int)y.size(0);
+  if (T == 0) return;
+  auto cfg = make_cfg(dim3(T), dim3(256));
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_rmsnorm_add, (const float*)y.data_ptr<float>(), (int64_t)y.stride(0),
+                                    (const float*)w.data_ptr<float>(), (float)eps, (int)y.size(1), x.data_ptr<float>(),
+                                    (int64_t)x.stride(0)));
 }
 
 void rope_kv(torch::Tensor qkv, torch::Tensor pos, torch::Tensor slot, torch::Tensor cos_t, torch::Tensor sin_t,

@@ -27,7 +27,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int GEMM_THREADS = 192;
 
-enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2 };
+enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2, G_GEGLU = 3 };
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -123,7 +123,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       tc::tmem_ld_wait();
       if (row >= M) continue;
       const int col0 = n0 + c;
-      if (epi == G_SWIGLU) {
+      if (epi >= G_SWIGLU) {
         // columns [col0, col0+8) are gate rows of outputs col0/2 + j, [col0+8, col0+16) the up rows
 #pragma unroll
         for (int j = 0; j < 8; j++) {
@@ -131,7 +131,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           if (col + 8 < N) {
             float g = __uint_as_float(r[j]), u = __uint_as_float(r[j + 8]);
             if (bias) { g += bias[col]; u += bias[col + 8]; }
-            store_val(out + (int64_t)row * ldo + (col0 >> 1) + j, silu(g) * u);
+            store_val(out + (int64_t)row * ldo + (col0 >> 1) + j, gated_act(epi, g) * u);
           }
         }
       } else {
@@ -292,11 +292,11 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
         float v[16];
 #pragma unroll
         for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]) + ((bias && col0 + j < N) ? bias[col0 + j] : 0.f);
-        if (epi == G_SWIGLU) {
+        if (epi >= G_SWIGLU) {
           // columns [col0, col0+8) gate rows of outputs col0/2 + j, [col0+8, col0+16) the up rows
           float o[16];
 #pragma unroll
-          for (int j = 0; j < 8; j++) o[j] = silu(v[j]) * v[j + 8];
+          for (int j = 0; j < 8; j++) o[j] = gated_act(epi, v[j]) * v[j + 8];
           OutT* p = out + (int64_t)row * ldo + (col0 >> 1);
           if (col0 + 16 <= N && std::is_same<OutT, float>::value && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
             float* pf = reinterpret_cast<float*>(p);
@@ -390,8 +390,9 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
               "operands must be 16-byte aligned");
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out: [M, *] row-major");
   const int64_t M = a.size(0), N = b.size(0);
-  TORCH_CHECK(out.size(0) >= M && out.size(1) >= (epi == G_SWIGLU ? N / 2 : N), "out too small");
-  if (epi == G_SWIGLU) TORCH_CHECK(N % 16 == 0, "SwiGLU needs 8-column interleaved gate/up blocks");
+  TORCH_CHECK(epi >= 0 && epi <= 3, "gemm: epilogue");
+  TORCH_CHECK(out.size(0) >= M && out.size(1) >= (epi >= G_SWIGLU ? N / 2 : N), "out too small");
+  if (epi >= G_SWIGLU) TORCH_CHECK(N % 16 == 0, "gated epilogues need 8-column interleaved gate/up blocks");
   if (M == 0 || N == 0) return;
   const float* bp = nullptr;
   if (bias.has_value()) {

@@ -44,7 +44,7 @@ using namespace fak;
 
 namespace {
 
-enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_GEGLU = 3 };
 constexpr int MAXNT = 4;  // n8 token tiles per launch: up to 32 tokens
 constexpr int MAGIC_I = 0x4B400000;
 constexpr float MAGIC_F = 12582912.0f;
@@ -274,13 +274,13 @@ FAK_DEV void epilogue(int tile, const float (&v)[4], int tokb, int lane, int N, 
   const int g = lane >> 2, t = lane & 3;
   const int r0 = tile * 16, tok0 = tokb + 2 * t, tok1 = tokb + 2 * t + 1;
   const int rowa = r0 + g, rowb = r0 + g + 8;
-  if (epi == EPI_SWIGLU) {
+  if (epi >= EPI_SWIGLU) {
     // rows [r0, r0+8) are the gate rows of outputs [r0/2, r0/2+8), rows [r0+8, r0+16) the up rows
     if (rowb < N) {
       const int o = (r0 >> 1) + g;
       const float bg = bias ? bias[rowa] : 0.f, bu = bias ? bias[rowb] : 0.f;
-      if (tok0 < B) y[(int64_t)tok0 * ldy + o] = silu(v[0] + bg) * (v[2] + bu);
-      if (tok1 < B) y[(int64_t)tok1 * ldy + o] = silu(v[1] + bg) * (v[3] + bu);
+      if (tok0 < B) y[(int64_t)tok0 * ldy + o] = gated_act(epi, v[0] + bg) * (v[2] + bu);
+      if (tok1 < B) y[(int64_t)tok1 * ldy + o] = gated_act(epi, v[1] + bg) * (v[3] + bu);
     }
     return;
   }
@@ -683,10 +683,10 @@ k_tgemv_moe(const uint8_t* __restrict__ Wt, int Te, int K, const int8_t* __restr
     ul = 0;
     const int r0 = tile * 16;
     const int p0 = pr[2 * t], p1 = pr[2 * t + 1];
-    if (epi == EPI_SWIGLU) {
+    if (epi >= EPI_SWIGLU) {
       const int o = (r0 >> 1) + g;
-      if (p0 >= 0) y[(int64_t)p0 * ldy + o] = silu(acc[0][0]) * acc[0][2];
-      if (p1 >= 0) y[(int64_t)p1 * ldy + o] = silu(acc[0][1]) * acc[0][3];
+      if (p0 >= 0) y[(int64_t)p0 * ldy + o] = gated_act(epi, acc[0][0]) * acc[0][2];
+      if (p1 >= 0) y[(int64_t)p1 * ldy + o] = gated_act(epi, acc[0][1]) * acc[0][3];
     } else {
       if (p0 >= 0) {
         y[(int64_t)p0 * ldy + r0 + g] = acc[0][0];
@@ -850,8 +850,9 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   TORCH_CHECK(y.scalar_type() == torch::kFloat32 && y.dim() == 2 && y.stride(1) == 1, "tgemv: y [B, *] f32");
   TORCH_CHECK(B >= 1 && B <= 8 * MAXNT, "tgemv: 1 <= B <= 32");
   const int NT = (int)((B + 7) / 8) <= 1 ? 1 : ((B + 7) / 8 <= 2 ? 2 : 4);
-  if (epi == EPI_SWIGLU) TORCH_CHECK(N % 16 == 0, "tgemv: SwiGLU needs 8-row interleaved gate/up blocks");
-  TORCH_CHECK(y.size(0) >= B && y.size(1) >= (epi == EPI_SWIGLU ? N / 2 : N), "tgemv: y too small");
+  TORCH_CHECK(epi >= EPI_STORE && epi <= EPI_GEGLU, "tgemv: epilogue");
+  if (epi >= EPI_SWIGLU) TORCH_CHECK(N % 16 == 0, "tgemv: gated epilogues need 8-row interleaved gate/up blocks");
+  TORCH_CHECK(y.size(0) >= B && y.size(1) >= (epi >= EPI_SWIGLU ? N / 2 : N), "tgemv: y too small");
   const float* bp = nullptr;
   if (bias.has_value()) {
     TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "tgemv: bias");

@@ -302,7 +302,8 @@ class Engine:
                 done.append((k, r))
         if done:
             rows = torch.tensor([k for k, _ in done], device=dev)
-            toks = sample(logits.index_select(0, rows), [r.sampling for _, r in done], [r for _, r in done])
+            toks = sample(self._capped(logits.index_select(0, rows)), [r.sampling for _, r in done],
+                          [r for _, r in done])
             self.stats["d2h_bytes"] += 8 * len(done)
             now = time.perf_counter()
             for (k, r), tok in zip(done, toks):
@@ -334,6 +335,11 @@ class Engine:
         else:
             self.pool.release(r.pages)
         r.pages = []
+
+    def _capped(self, logits: torch.Tensor) -> torch.Tensor:
+        """Final-logit soft-capping (Gemma-2) before sampling; greedy argmax is unaffected by it."""
+        c = self.cfg.final_softcap
+        return c * torch.tanh(logits / c) if c > 0 else logits
 
     @staticmethod
     def _cacheable(r: Request) -> int:
@@ -440,7 +446,7 @@ class Engine:
             toks = out.cpu().tolist()
             self.stats["d2h_bytes"] += 4 * B
         else:
-            toks = sample(self.runner.logits[:B], [r.sampling for r in lanes], lanes)
+            toks = sample(self._capped(self.runner.logits[:B]), [r.sampling for r in lanes], lanes)
             self.stats["d2h_bytes"] += 8 * B
         self.stats["decode_tokens"] += B
         for r, tok in zip(lanes, toks):

@@ -62,6 +62,9 @@ def tensor_plan(cfg: ModelConfig) -> list[tuple[str, tuple[int, ...], str]]:
             out.append((p + "attn_k_norm.weight", (cfg.head_dim,), "norm"))
         out.append((p + "attn_output.weight", (d, cfg.q_dim), "attn_output"))
         out.append((p + "ffn_norm.weight", (d,), "norm"))
+        if cfg.sandwich_norms:
+            out.append((p + "post_attention_norm.weight", (d,), "norm"))
+            out.append((p + "post_ffw_norm.weight", (d,), "norm"))
         if cfg.is_moe:
             E, f = cfg.n_experts, cfg.expert_ffn_dim
             out.append((p + "ffn_gate_inp.weight", (E, d), "router"))
@@ -212,8 +215,11 @@ def write_metadata(w: GGUFWriter, cfg: ModelConfig, mix: str, with_vocab: bool =
     w.add(f"{a}.attention.value_length", cfg.head_dim, ValueType.UINT32)
     w.add(f"{a}.attention.layer_norm_rms_epsilon", float(cfg.rms_eps), ValueType.FLOAT32)
     w.add(f"{a}.rope.freq_base", float(cfg.rope_theta), ValueType.FLOAT32)
-    if cfg.sliding_window > 0 and cfg.swa_layers is None:   # every layer windowed
+    if cfg.sliding_window > 0 and (cfg.swa_layers is None or a == "gemma2"):   # every (gemma2: every other) layer
         w.add(f"{a}.attention.sliding_window", int(cfg.sliding_window), ValueType.UINT32)
+    if a == "gemma2":
+        w.add(f"{a}.attn_logit_softcapping", float(cfg.attn_softcap), ValueType.FLOAT32)
+        w.add(f"{a}.final_logit_softcapping", float(cfg.final_softcap), ValueType.FLOAT32)
     if cfg.rope_scaling:
         rs = dict(cfg.rope_scaling)
         w.add(f"{a}.rope.scaling.type", str(rs.get("type") or rs.get("rope_type")))

@@ -78,7 +78,9 @@ def write_safetensors(path: str, tensors: dict[str, torch.Tensor], metadata: dic
 
 def config_from_hf(hf: dict) -> ModelConfig:
     arch_name = (hf.get("architectures") or [hf.get("model_type", "")])[0].lower()
-    if "qwen3moe" in arch_name or hf.get("model_type") == "qwen3_moe":
+    if "gemma2" in arch_name or hf.get("model_type") == "gemma2":
+        arch = "gemma2"
+    elif "qwen3moe" in arch_name or hf.get("model_type") == "qwen3_moe":
         arch = "qwen3moe"
     elif "qwen3" in arch_name:
         arch = "qwen3"
@@ -104,12 +106,22 @@ def config_from_hf(hf: dict) -> ModelConfig:
         norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
         max_context=int(hf.get("max_position_embeddings", 32768)),
         rope_scaling=_hf_rope_scaling(rp, hf),
+        **(_gemma_fields(hf) if arch == "gemma2" else {}),
         **_hf_sliding_window(hf, int(hf["num_hidden_layers"])),
         bos_token_id=int(hf.get("bos_token_id") or 1), eos_token_id=int(hf.get("eos_token_id") or 2),
         name=str(hf.get("_name_or_path", arch_name)),
     )
     cfg.validate()
     return cfg
+
+
+def _gemma_fields(hf: dict) -> dict:
+    act = str(hf.get("hidden_activation") or hf.get("hidden_act") or "gelu_pytorch_tanh")
+    return {"act": "gelu_tanh" if "gelu" in act else "silu",
+            "attn_softcap": float(hf.get("attn_logit_softcapping") or 0.0),
+            "final_softcap": float(hf.get("final_logit_softcapping") or 0.0),
+            "sandwich_norms": True, "embed_scale": float(hf["hidden_size"]) ** 0.5,
+            "attn_scale": float(hf.get("query_pre_attn_scalar") or hf.get("head_dim") or 256) ** -0.5}
 
 
 def _hf_sliding_window(hf: dict, n_layers: int) -> dict:
@@ -157,7 +169,12 @@ _EXPERT = re.compile(r"model\.layers\.(\d+)\.mlp\.experts\.(\d+)\.(gate|up|down)
 _EXP_NAME = {"gate": "ffn_gate_exps.weight", "up": "ffn_up_exps.weight", "down": "ffn_down_exps.weight"}
 
 
-def gguf_name(hf_name: str) -> str | None:
+_GEMMA_LAYER = {"post_attention_layernorm.weight": "post_attention_norm.weight",
+                "pre_feedforward_layernorm.weight": "ffn_norm.weight",
+                "post_feedforward_layernorm.weight": "post_ffw_norm.weight"}
+
+
+def gguf_name(hf_name: str, arch: str = "") -> str | None:
     if hf_name == "model.embed_tokens.weight":
         return "token_embd.weight"
     if hf_name == "model.norm.weight":
@@ -165,6 +182,8 @@ def gguf_name(hf_name: str) -> str | None:
     if hf_name == "lm_head.weight":
         return "output.weight"
     m = re.fullmatch(r"model\.layers\.(\d+)\.(.+)", hf_name)
+    if m and arch == "gemma2" and m.group(2) in _GEMMA_LAYER:
+        return f"blk.{m.group(1)}.{_GEMMA_LAYER[m.group(2)]}"
     if m and m.group(2) in _LAYER:
         return f"blk.{m.group(1)}.{_LAYER[m.group(2)]}"
     return None
@@ -258,8 +277,11 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
                     sub = arr[a:b]
                     table[f"blk.{i}.{nm}.weight"] = (dt, (b - a,) + tuple(shape[1:]), sub)
                 continue
-            g = gguf_name(n)
+            g = gguf_name(n, cfg.arch)
             if g is not None:
+                if cfg.arch == "gemma2" and g.endswith("norm.weight"):   # Gemma scales by (1 + w)
+                    arr = _to_f32(dt, np.asarray(arr)) + np.float32(1.0)
+                    dt = "F32"
                 table[g] = (dt, shape, arr)
     # quantized layers: decoded on first use; experts (one triple per expert) stacked
     qlayers: dict[str, list[dict]] = {}
@@ -335,6 +357,8 @@ def load_reference_tensors_hf(model_dir: str) -> tuple[ModelConfig, dict[str, to
             names += [p + n for n in ("attn_q.bias", "attn_k.bias", "attn_v.bias")]
         if cfg.qk_norm:
             names += [p + "attn_q_norm.weight", p + "attn_k_norm.weight"]
+        if cfg.sandwich_norms:
+            names += [p + "post_attention_norm.weight", p + "post_ffw_norm.weight"]
         if cfg.is_moe:
             names += [p + n for n in ("ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
                                       "ffn_down_exps.weight")]

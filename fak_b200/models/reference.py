@@ -7,7 +7,8 @@ is tested against it.  Semantics kept identical to the reference:
 
 * RMSNorm ``x * rsqrt(mean(x^2) + eps) * w`` (cuda_kernels.cu:529-548).
 * HF rotate_half RoPE with the angle computed in float64 (cuda_kernels.cu:551-567).
-* SiLU-gated FFN; qkv bias (Qwen2); per-head q/k RMSNorm before RoPE (Qwen3).
+* SiLU-gated FFN; qkv bias (Qwen2); per-head q/k RMSNorm before RoPE (Qwen3); GELU-tanh gated FFN,
+  score and logit soft-capping, sandwich norms, embedding scale (Gemma-2).
 * MoE router: softmax over all experts, then top-k, renormalised when
   ``norm_topk_prob`` (internal/model/moe.go:279-311).
 * Causal attention with GQA head groups.
@@ -20,6 +21,18 @@ import numpy as np
 import torch
 
 from ..config import ModelConfig
+
+
+def softcap(x: torch.Tensor, cap: float) -> torch.Tensor:
+    return cap * torch.tanh(x / cap) if cap > 0 else x
+
+
+def act_fn(name: str, g: torch.Tensor) -> torch.Tensor:
+    if name == "silu":
+        return torch.nn.functional.silu(g)
+    if name == "gelu_tanh":
+        return torch.nn.functional.gelu(g, approximate="tanh")
+    raise ValueError(f"unknown activation {name!r}")
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -87,25 +100,26 @@ class ReferenceModel:
         return self.t[name]
 
     def embed(self, ids: torch.Tensor) -> torch.Tensor:
-        return self.t["token_embd.weight"][ids.to(self.device)]
+        e = self.t["token_embd.weight"][ids.to(self.device)]
+        return e * self.cfg.embed_scale if self.cfg.embed_scale != 1.0 else e
 
     def lm_head(self, h: torch.Tensor) -> torch.Tensor:
         W = self.t["token_embd.weight"] if self.cfg.tie_embeddings else self.t["output.weight"]
-        return h @ W.T
+        return softcap(h @ W.T, self.cfg.final_softcap)
 
     def _ffn(self, i: int, x: torch.Tensor) -> torch.Tensor:
         cfg, p = self.cfg, f"blk.{i}."
         if not cfg.is_moe:
             g = self.mm(x, p + "ffn_gate.weight")
             u = self.mm(x, p + "ffn_up.weight")
-            return self.mm(torch.nn.functional.silu(g) * u, p + "ffn_down.weight")
+            return self.mm(act_fn(cfg.act, g) * u, p + "ffn_down.weight")
         wts, idx = moe_route(x @ self.w(p + "ffn_gate_inp.weight").T, cfg.n_experts_used, cfg.norm_topk_prob)
         G, U, D = self.w(p + "ffn_gate_exps.weight"), self.w(p + "ffn_up_exps.weight"), self.w(p + "ffn_down_exps.weight")
         out = torch.zeros_like(x)
         for t in range(x.shape[0]):
             for j in range(cfg.n_experts_used):
                 e = int(idx[t, j])
-                h = torch.nn.functional.silu(G[e] @ x[t]) * (U[e] @ x[t])
+                h = act_fn(cfg.act, G[e] @ x[t]) * (U[e] @ x[t])
                 out[t] += wts[t, j] * (D[e] @ h)
         return out
 
@@ -156,10 +170,17 @@ class ReferenceModel:
             else:
                 K, V = k, v
             a = attention(q, K, V, start_pos, cfg.layer_window(i),
-                          None if self.attn_observer is None else (lambda pr, i=i: self.attn_observer(i, pr)))
-            x = x + self.mm(a.reshape(T, H * D), p + "attn_output.weight")
+                          None if self.attn_observer is None else (lambda pr, i=i: self.attn_observer(i, pr)),
+                          scale=cfg.attn_scale, softcap_=cfg.attn_softcap)
+            o = self.mm(a.reshape(T, H * D), p + "attn_output.weight")
+            if cfg.sandwich_norms:
+                o = rmsnorm(o, self.w(p + "post_attention_norm.weight"), cfg.rms_eps)
+            x = x + o
             h = rmsnorm(x, self.w(p + "ffn_norm.weight"), cfg.rms_eps)
-            x = x + self._ffn(i, h)
+            f = self._ffn(i, h)
+            if cfg.sandwich_norms:
+                f = rmsnorm(f, self.w(p + "post_ffw_norm.weight"), cfg.rms_eps)
+            x = x + f
             if self.taps is not None:
                 self.taps[i] = x.detach().clone()
         return x
@@ -196,7 +217,7 @@ class ReferenceModel:
 
 
 def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int, window: int = 0,
-              observe=None) -> torch.Tensor:
+              observe=None, scale: float = 0.0, softcap_: float = 0.0) -> torch.Tensor:
     """q [T,H,D] at positions start_pos..; K,V [Tctx,Hk,D] covering positions 0..Tctx-1 (causal;
     window > 0: each query sees keys (qpos - window, qpos])."""
     T, H, D = q.shape
@@ -204,7 +225,8 @@ def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int,
     g = H // Hk
     Kx = K.repeat_interleave(g, dim=1)
     Vx = V.repeat_interleave(g, dim=1)
-    s = torch.einsum("thd,chd->htc", q.float(), Kx.float()) / math.sqrt(D)
+    s = torch.einsum("thd,chd->htc", q.float(), Kx.float()) * (scale if scale > 0 else 1.0 / math.sqrt(D))
+    s = softcap(s, softcap_)
     qpos = torch.arange(start_pos, start_pos + T, device=q.device)[:, None]
     kpos = torch.arange(Tc, device=q.device)[None, :]
     masked = kpos > qpos

@@ -109,6 +109,11 @@ class ModelRunner:
         self.qkv = torch.zeros(B, self.qkv_dim, dtype=torch.float32, device=dev)
         self.q = torch.zeros(B, self.Hq, self.D, dtype=torch.float32, device=dev)
         self.h = torch.zeros(B, max(self.ffn_local, 32), dtype=torch.float32, device=dev)
+        self.tmp = torch.zeros(B, d, dtype=torch.float32, device=dev)   # sandwich norms: projection outputs
+        # gated FFN epilogue of the gate/up GEMV and GEMM: SwiGLU or GEGLU (GELU-tanh)
+        self.gated_epi = K.EPI_GEGLU if cfg.act == "gelu_tanh" else K.EPI_SWIGLU
+        if cfg.sandwich_norms and collectives is not None:
+            raise NotImplementedError("sandwich-norm models (Gemma-2) run on one GPU per replica")
         self.act_d = K.ActQ(B, d, dev)
         self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
@@ -181,8 +186,13 @@ class ModelRunner:
             K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_attn,
                                workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None,
                                prefetch=self._pf(L.o), window=cfg.layer_window(i),
+                               scale=cfg.attn_scale, softcap=cfg.attn_softcap,
                                **self.cascade_args(B, cfg.layer_window(i)))
-            K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD, prefetch=self._pf(L.gate_up))
+            if L.post_attn_norm is not None:   # sandwich norm: x += rmsnorm(o_proj(a))
+                K.gemv(L.o, self.act_attn, B, self.tmp[:B], None, K.EPI_STORE, prefetch=self._pf(L.gate_up))
+                K.rmsnorm_add(self.tmp[:B], L.post_attn_norm, cfg.rms_eps, x)
+            else:
+                K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD, prefetch=self._pf(L.gate_up))
         else:
             self.coll.decode_attn_o(self, i, B, bt, ctx, n_split)
         if cfg.is_moe:
@@ -191,15 +201,19 @@ class ModelRunner:
             moe_decode(self, i, B)
             return
         if self.fused_act:
-            K.gemv(L.gate_up, K.FAct(x, L.ffn_norm, cfg.rms_eps), B, self.h[:B], None, K.EPI_SWIGLU)
+            K.gemv(L.gate_up, K.FAct(x, L.ffn_norm, cfg.rms_eps), B, self.h[:B], None, self.gated_epi)
         else:
             K.quant_act(x, self.act_d, L.ffn_norm, cfg.rms_eps)
-            K.gemv(L.gate_up, self.act_d, B, self.h[:B], None, K.EPI_SWIGLU, prefetch=self._pf(L.down))
+            K.gemv(L.gate_up, self.act_d, B, self.h[:B], None, self.gated_epi, prefetch=self._pf(L.down))
             K.quant_act(self.h[:B, :self.ffn_local], self.act_ffn)
         if self.coll is None:
             nxt_w = nxt.qkv[0][0] if nxt is not None else self.w.lm_head
-            K.gemv(L.down, self.ffn_in, B, x, None, K.EPI_ADD,
-                   prefetch=self._pf(nxt_w) if nxt is not None else None)
+            pf = self._pf(nxt_w) if nxt is not None else None
+            if L.post_ffn_norm is not None:   # sandwich norm: x += rmsnorm(down(h))
+                K.gemv(L.down, self.ffn_in, B, self.tmp[:B], None, K.EPI_STORE, prefetch=pf)
+                K.rmsnorm_add(self.tmp[:B], L.post_ffn_norm, cfg.rms_eps, x)
+            else:
+                K.gemv(L.down, self.ffn_in, B, x, None, K.EPI_ADD, prefetch=pf)
         else:
             self.coll.decode_down(self, i, B)
 
@@ -210,7 +224,7 @@ class ModelRunner:
         the early-exit draft model of self-speculative decoding (its KV pages are the target's)."""
         cfg = self.cfg
         n_split = self.n_split_for(B)
-        K.embed(self.w.embed, ids, self.x[:B], None, self.err)
+        K.embed(self.w.embed, ids, self.x[:B], None, self.err, scale=cfg.embed_scale)
         for i in range(cfg.n_layers if n_layers is None else n_layers):
             self._layer_decode(i, B, pos, slot, bt, ctx, n_split)
         if self.fused_act:
@@ -306,7 +320,8 @@ class ModelRunner:
         qkv = torch.empty(T, self.qkv_dim, dtype=torch.float32, device=dev)
         qb = torch.empty(T, self.Hq, self.D, dtype=torch.bfloat16, device=dev)
         ab = torch.empty(T, self.Hq * self.D, dtype=torch.bfloat16, device=dev)
-        K.embed(self.w.embed, ids, x, None, self.err)
+        K.embed(self.w.embed, ids, x, None, self.err, scale=cfg.embed_scale)
+        tmp = torch.empty(T, d, dtype=torch.float32, device=dev) if cfg.sandwich_norms else None
         for i in range(cfg.n_layers):
             L = self.w.layers[i]
             K.rmsnorm_bf16(x, L.attn_norm, cfg.rms_eps, hb)
@@ -315,8 +330,12 @@ class ModelRunner:
                 K.gemm(hb, seg, qkv[:, off:off + seg.rows], K.EPI_STORE, bias)
             K.rope_kv(qkv, pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
                       None, qb, self.kv.k[i], self.kv.v[i])
-            K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab, cfg.layer_window(i))
-            if self.coll is None:
+            K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab, cfg.layer_window(i), cfg.attn_scale,
+                                cfg.attn_softcap)
+            if self.coll is None and L.post_attn_norm is not None:
+                K.gemm(ab, L.o, tmp, K.EPI_STORE)
+                K.rmsnorm_add(tmp, L.post_attn_norm, cfg.rms_eps, x)
+            elif self.coll is None:
                 K.gemm(ab, L.o, x, K.EPI_ADD)
             else:
                 self.coll.prefill_attn_o(self, i, ab, x)
@@ -326,9 +345,12 @@ class ModelRunner:
                 moe_prefill(self, i, hb, x)
                 continue
             hf = torch.empty(T, self.ffn_local, dtype=torch.float32, device=dev)
-            K.gemm(hb, L.gate_up, hf, K.EPI_SWIGLU)
+            K.gemm(hb, L.gate_up, hf, self.gated_epi)
             hb2 = hf.to(torch.bfloat16)
-            if self.coll is None:
+            if self.coll is None and L.post_ffn_norm is not None:
+                K.gemm(hb2, L.down, tmp, K.EPI_STORE)
+                K.rmsnorm_add(tmp, L.post_ffn_norm, cfg.rms_eps, x)
+            elif self.coll is None:
                 K.gemm(hb2, L.down, x, K.EPI_ADD)
             else:
                 self.coll.prefill_down(self, i, hb2, x)

@@ -91,6 +91,8 @@ class LayerWeights:
     experts_gate_up: QuantWeight | None = None  # local experts stacked, 8-row interleaved gate/up
     experts_down: QuantWeight | None = None
     expert_ids: list[int] | None = None  # global ids of the experts held here
+    post_attn_norm: torch.Tensor | None = None   # sandwich norms (Gemma-2): after o_proj / down
+    post_ffn_norm: torch.Tensor | None = None
 
 
 @dataclasses.dataclass
@@ -328,6 +330,9 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
             ffn_norm=_vec(get, p + "ffn_norm.weight", device),
             qkv=segs, qkv_bias=bias, q_norm=qn, k_norm=kn, o=o, gate_up=None, down=None,
         )
+        if cfg.sandwich_norms:
+            L.post_attn_norm = _vec(get, p + "post_attention_norm.weight", device)
+            L.post_ffn_norm = _vec(get, p + "post_ffw_norm.weight", device)
         if cfg.is_moe:
             # expert parallelism rides on the tensor-parallel group: rank r owns a band of experts
             band = expert_filter if expert_filter is not None else expert_slice(cfg.n_experts, tp_rank, tp_size)

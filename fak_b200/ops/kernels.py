@@ -5,7 +5,7 @@ import torch
 
 from ._ext import ext
 
-EPI_STORE, EPI_ADD, EPI_SWIGLU = 0, 1, 2
+EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_GEGLU = 0, 1, 2, 3
 GEMV_MAX_B = 8      # tokens per launch of the row-major kernels
 TGEMV_MAX_B = 32    # tokens per launch of the tile-packed GEMV (4 MMA column tiles)
 
@@ -126,7 +126,8 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
                      workspace=None, ldo: int = 0, tickets=None, prefetch: torch.Tensor | None = None,
-                     window: int = 0, shared_pages: torch.Tensor | None = None, prefix_splits: int = 0) -> None:
+                     window: int = 0, shared_pages: torch.Tensor | None = None, prefix_splits: int = 0,
+                     scale: float = 0.0, softcap: float = 0.0) -> None:
     """ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
     [B * kv heads]; when given, the last split of each (sequence, KV group) merges the splits in the
     same kernel instead of a separate combine launch (the kernel leaves the tickets at zero).
@@ -136,16 +137,18 @@ def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, ou
     (workspace sized for n_split + prefix_splits slots)."""
     ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
                            act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo,
-                           tickets, prefetch, window, shared_pages, prefix_splits)
+                           tickets, prefetch, window, shared_pages, prefix_splits, scale, softcap)
     cascade = shared_pages is not None and prefix_splits > 0 and window <= 0 and \
         q.shape[0] * (q.shape[1] // k_cache.shape[1]) <= 64
     n_slots = n_split + (prefix_splits if cascade else 0)
     count((1 if cascade else 0) + (2 if n_slots > 1 and (tickets is None or cascade) else 1))
 
 
-def prefill_attention(q, k_cache, v_cache, block_table, meta, out, window: int = 0) -> None:
+def prefill_attention(q, k_cache, v_cache, block_table, meta, out, window: int = 0, scale: float = 0.0,
+                      softcap: float = 0.0) -> None:
+    """scale: logit scale (0 = 1/sqrt(head_dim)); softcap > 0: logits cap * tanh(logit / cap)."""
     ext().prefill_attention(q, k_cache, v_cache, block_table, meta.tile_seq, meta.tile_q0, meta.seq_qoff,
-                            meta.seq_qlen, meta.seq_pos0, meta.n_tiles, out, window)
+                            meta.seq_qlen, meta.seq_pos0, meta.n_tiles, out, window, scale, softcap)
     count()
 
 
@@ -157,8 +160,14 @@ def kv_move(kv, src_slot: torch.Tensor, dst_slot: torch.Tensor, rot: torch.Tenso
     count()
 
 
-def embed(w, ids: torch.Tensor, out_f32=None, out_bf16=None, err=None) -> None:
-    ext().embed(w.buf, w.qtype, w.pitch, w.rows, w.cols, ids, out_f32, out_bf16, err)
+def embed(w, ids: torch.Tensor, out_f32=None, out_bf16=None, err=None, scale: float = 1.0) -> None:
+    ext().embed(w.buf, w.qtype, w.pitch, w.rows, w.cols, ids, out_f32, out_bf16, err, scale)
+    count()
+
+
+def rmsnorm_add(y: torch.Tensor, w: torch.Tensor, eps: float, x: torch.Tensor) -> None:
+    """x += rmsnorm(y) * w (row-wise; sandwich norms before the residual add)."""
+    ext().rmsnorm_add(y, w, eps, x)
     count()
 
 

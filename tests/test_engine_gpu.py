@@ -9,7 +9,8 @@ from fak_b200.gguf.synth import write_synthetic_gguf
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module", params=[("tiny-qwen2", "q4_k_m"), ("tiny-llama", "q8_0"), ("tiny-qwen2", "g4")])
+@pytest.fixture(scope="module", params=[("tiny-qwen2", "q4_k_m"), ("tiny-llama", "q8_0"), ("tiny-qwen2", "g4"),
+                                        ("tiny-gemma2", "q8_0")])
 def model_file(request, tmp_path_factory):
     name, mix = request.param
     path = str(tmp_path_factory.mktemp("m") / f"{name}.gguf")

@@ -104,3 +104,29 @@ def test_phi3_fused_projections_and_longrope(longrope, tmp_path):
         with torch.no_grad():
             want_long = m(long_ids[None]).logits[0]
         assert torch.allclose(ref.forward(long_ids), want_long, atol=3e-4, rtol=1e-4)
+
+
+def test_gemma2_matches_transformers(tmp_path):
+    """Gemma-2: GELU-tanh gated FFN, sandwich norms with (1 + w) scales, score and final-logit
+    soft-capping, query_pre_attn_scalar, embedding scale, alternating sliding windows."""
+    c = transformers.Gemma2Config(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                                  num_attention_heads=4, num_key_value_heads=2, head_dim=32,
+                                  max_position_embeddings=512, pad_token_id=0, bos_token_id=2, eos_token_id=1,
+                                  sliding_window=6, query_pre_attn_scalar=24, attn_logit_softcapping=5.0,
+                                  final_logit_softcapping=3.0)
+    m = transformers.Gemma2ForCausalLM(c)
+    m.config._attn_implementation = "eager"
+    torch.manual_seed(0)
+    for p in m.parameters():
+        torch.nn.init.normal_(p, std=0.08 if p.dim() > 1 else 0.3)
+    m = m.eval().float()
+    d = _save(m, tmp_path)
+    cfg, tensors = load_reference_tensors_hf(d)
+    assert cfg.arch == "gemma2" and cfg.sandwich_norms and cfg.act == "gelu_tanh"
+    assert [cfg.layer_window(i) for i in range(2)] == [6, 0]
+    ref = ReferenceModel(cfg, tensors)
+    ids = torch.tensor([3, 17, 200, 45, 9, 311, 7, 99, 12, 400, 5])
+    with torch.no_grad():
+        want = m(ids[None]).logits[0]
+    got = ref.forward(ids)
+    assert torch.allclose(got, want, atol=2e-4, rtol=1e-4), (got - want).abs().max()

@@ -21,11 +21,13 @@ def _ext():
     return ext()
 
 
-def _swiglu_ref(y):
-    """SwiGLU over 8-row interleaved (gate x8, up x8) blocks of the output dim."""
+def _swiglu_ref(y, gelu: bool = False):
+    """SwiGLU (or GEGLU with GELU-tanh) over 8-row interleaved (gate x8, up x8) blocks of the output dim."""
     M, N = y.shape
     blocks = y.view(M, N // 16, 2, 8)
-    return (torch.nn.functional.silu(blocks[:, :, 0]) * blocks[:, :, 1]).reshape(M, N // 2)
+    g = blocks[:, :, 0]
+    a = torch.nn.functional.gelu(g, approximate="tanh") if gelu else torch.nn.functional.silu(g)
+    return (a * blocks[:, :, 1]).reshape(M, N // 2)
 
 
 @pytest.mark.parametrize("qt,blk", QTYPES_TILE)
@@ -231,7 +233,7 @@ def test_argmax_first_index():
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 256, 128), (200, 512, 576), (1280, 4608, 3584), (77, 240, 1536),
                                    (1024, 16384, 256)])
-@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
 def test_gemm_tcgen05(M, N, K, epi):
     from fak_b200.ops import kernels as Kn
     torch.manual_seed(M + N + K)
@@ -240,8 +242,8 @@ def test_gemm_tcgen05(M, N, K, epi):
     bias = torch.randn(N, device="cuda") * 0.1
     ref = a.float() @ b.float().T + bias
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    if epi == 2:
-        ref = _swiglu_ref(ref)
+    if epi >= 2:
+        ref = _swiglu_ref(ref, gelu=epi == 3)
         out = torch.zeros(M, N // 2, device="cuda")
     else:
         out = torch.randn(M, N, device="cuda")
@@ -269,7 +271,7 @@ def _tg_case(qt, N, Kd, B, seed=3):
 
 @pytest.mark.parametrize("qt,blk", QTYPES_TILE)
 @pytest.mark.parametrize("B", [1, 5, 8, 13, 32])
-@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
 @pytest.mark.parametrize("N", [576, 16 * 2400])
 def test_tgemv_tile_packed(qt, blk, B, epi, N):
     """Tile-packed tensor-core GEMV vs an fp32 reference; N=576 runs split-K, the tall matrix one
@@ -279,8 +281,8 @@ def test_tgemv_tile_packed(qt, blk, B, epi, N):
     w, Wd, x, act = _tg_case(qt, N, Kd, B)
     bias = torch.randn(N, device="cuda") * 0.1
     ref = x @ Wd.T + bias
-    if epi == K.EPI_SWIGLU:
-        ref = _swiglu_ref(ref)
+    if epi >= K.EPI_SWIGLU:
+        ref = _swiglu_ref(ref, gelu=epi == K.EPI_GEGLU)
         y = torch.zeros(B, N // 2, device="cuda")
     else:
         y = torch.randn(B, N, device="cuda")
@@ -290,7 +292,7 @@ def test_tgemv_tile_packed(qt, blk, B, epi, N):
     torch.cuda.synchronize()
     err = (y - ref).abs().max().item() / ref.abs().max().item()
     cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
-    tol_cos, tol_err = (0.999, 0.06) if epi == K.EPI_SWIGLU else (0.9995, 0.03)
+    tol_cos, tol_err = (0.999, 0.06) if epi >= K.EPI_SWIGLU else (0.9995, 0.03)
     assert cos > tol_cos and err < tol_err, (cos, err)
 
 

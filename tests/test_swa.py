@@ -73,3 +73,20 @@ def test_gguf_roundtrip_of_window_and_rope_scaling(tmp_path):
     write_synthetic_gguf(path, cfg, "q8_0", seed=0)
     _, c2 = open_model(path)
     assert c2.max_window() == 32 and dict(c2.rope_scaling) == {"type": "linear", "factor": 2.0}
+
+
+def test_gemma2_gguf_roundtrip_and_reference_features(tmp_path):
+    import torch
+    from fak_b200.config import preset
+    from fak_b200.gguf.synth import write_synthetic_gguf
+    from fak_b200.models.reference import ReferenceModel
+    cfg = preset("tiny-gemma2")
+    path = str(tmp_path / "g.gguf")
+    write_synthetic_gguf(path, cfg, "q8_0", seed=1, std=0.05)
+    ref = ReferenceModel.from_gguf(path)
+    c = ref.cfg
+    assert (c.arch, c.act, c.sandwich_norms, c.attn_softcap, c.final_softcap) == ("gemma2", "gelu_tanh", True, 50.0, 30.0)
+    assert c.embed_scale == 16.0 and [c.layer_window(i) for i in range(2)] == [32, 0]
+    assert "blk.1.post_ffw_norm.weight" in ref.t
+    logits = ref.forward(torch.arange(40))
+    assert logits.abs().max() <= 30.0 + 1e-4          # final soft-cap
