@@ -26,7 +26,9 @@ def main(argv=None):
     ap.add_argument("--head-dim", type=int, default=128)
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--split", type=int, default=32)
+    ap.add_argument("--split", type=int, default=16)
+    ap.add_argument("--cascade", type=int, default=0,
+                    help="prefix splits of cascade attention over the shared pages (0: plain split-KV path)")
     args = ap.parse_args(argv)
     from fak_b200.ops import kernels as K
 
@@ -48,11 +50,13 @@ def main(argv=None):
     ctx_t = torch.full((B,), ctx, dtype=torch.int32, device=dev)
     q = torch.randn(B, H, D, device=dev)
     act = K.ActQ(B, H * D, dev)
-    ws = torch.zeros(B * H * args.split * (D + 2), device=dev)
+    ws = torch.zeros(B * H * (args.split + args.cascade) * (D + 2), device=dev)
+    shared = torch.tensor([n_sh], dtype=torch.int32, device=dev)
+    casc = {"shared_pages": shared, "prefix_splits": args.cascade} if args.cascade else {}
 
     def run(i):
         kc, vc = caches[i % args.layers]
-        K.decode_attention(q, kc, vc, bt, ctx_t, args.split, act=act, workspace=ws)
+        K.decode_attention(q, kc, vc, bt, ctx_t, args.split, act=act, workspace=ws, **casc)
 
     for i in range(3):
         run(i)
@@ -67,7 +71,8 @@ def main(argv=None):
     page_bytes = 2 * Hkv * 16 * D * 2
     unique = (n_sh + B * (per_seq - n_sh)) * page_bytes
     print(json.dumps({"kernel": "decode_attention+combine", "batch": B, "ctx": ctx, "shared": n_sh * 16,
-                      "heads": H, "kv_heads": Hkv, "head_dim": D, "splits": args.split, "us": round(us, 2),
+                      "heads": H, "kv_heads": Hkv, "head_dim": D, "splits": args.split, "cascade": args.cascade,
+                      "us": round(us, 2),
                       "unique_kv_bytes": unique, "tb_s_unique": round(unique / us / 1e6, 3),
                       "tb_s_streamed": round(B * per_seq * page_bytes / us / 1e6, 3)}))
 

@@ -256,7 +256,8 @@ class EngineConfig:
     fused_activations: bool = False     # decode GEMVs normalise+quantize fp32 inputs themselves
     attention_merge: bool = False       # merge attention splits in the last split's CTA (no combine launch)
     l2_prefetch: bool = False           # decode kernels warm L2 with the next GEMV's weights (measured neutral)
-    cascade_attention: bool = True      # decode: a batch's shared prefix pages are attended once for all lanes
+    cascade_attention: bool = False     # decode: a batch's shared prefix pages attended once for all lanes
+                                        # (measured: no faster than the split-KV path yet at 5 lanes x 9K)
     preempt_mode: str = "recompute"     # out of KV pages: "recompute" (radix-assisted) or "swap" to host memory
     swap_space_gb: float = 16.0         # pinned host memory for swapped-out KV pages
 

@@ -311,11 +311,12 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
 // belongs to warp r / 16.  Each warp writes its rows' unnormalised partials (o, max, sum) into
 // slot `split` of the split-KV scratch; the per-sequence kernel covers the pages after the shared
 // prefix in the remaining slots and k_decode_combine merges all of them.
-// B*G <= 64 (four 16-row tiles).  Pages in flight per CTA: DEC_STAGES.
+// B*G <= 64 (four 16-row tiles).  Pages in flight per CTA: PREFIX_STAGES - 1.
+constexpr int PREFIX_STAGES = 6;   // pages in flight per CTA: a CTA's whole page range is ~one round trip
 template <int D>
 struct PrefixSmem {
-  __nv_bfloat16 k[DEC_STAGES][PAGE][D + 8];
-  __nv_bfloat16 v[DEC_STAGES][PAGE][D + 8];
+  __nv_bfloat16 k[PREFIX_STAGES][PAGE][D + 8];
+  __nv_bfloat16 v[PREFIX_STAGES][PAGE][D + 8];
 };
 
 template <int D>
@@ -379,19 +380,19 @@ k_decode_attn_prefix(const float* __restrict__ q, const __nv_bfloat16* __restric
     cp_async_commit();
   };
 #pragma unroll
-  for (int i = 0; i < DEC_STAGES - 1; i++) {
+  for (int i = 0; i < PREFIX_STAGES - 1; i++) {
     if (p_begin + i < p_end) issue_page(p_begin + i, i);
     else cp_async_commit();
   }
   for (int p = p_begin, it = 0; p < p_end; p++, it++) {
-    const int pn = p + DEC_STAGES - 1;
+    const int pn = p + PREFIX_STAGES - 1;
     // the slot refilled below was consumed in the previous iteration by every warp
     __syncthreads();
-    if (pn < p_end) issue_page(pn, (it + DEC_STAGES - 1) % DEC_STAGES);
+    if (pn < p_end) issue_page(pn, (it + PREFIX_STAGES - 1) % PREFIX_STAGES);
     else cp_async_commit();
-    cp_async_wait<DEC_STAGES - 1>();
+    cp_async_wait<PREFIX_STAGES - 1>();
     __syncthreads();
-    const int buf = it % DEC_STAGES;
+    const int buf = it % PREFIX_STAGES;
     if (!active) continue;
     float s[2][4];
 #pragma unroll

@@ -28,7 +28,7 @@ constexpr int kAttnMaxV = 512;       // value width held in registers (16 per la
 
 __global__ void k_dsa_index_score(const float* __restrict__ iq, const float* __restrict__ ik,
                                   const float* __restrict__ w, double* __restrict__ score, int n_keys, int nh,
-                                  int dim, int qpos, float scale) {
+                                  int dim, int qpos, double scale) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= n_keys) return;
   const int k = warp;
@@ -39,7 +39,7 @@ __global__ void k_dsa_index_score(const float* __restrict__ iq, const float* __r
       const float* q = iq + (int64_t)h * dim;
       double d = 0.0;
       for (int i = 0; i < dim; i++) d += (double)q[i] * (double)key[i];
-      const double s = d * (double)scale;
+      const double s = d * scale;
       acc += (double)w[h] * (s > 0.0 ? s : 0.0);
     }
   }
@@ -147,7 +147,7 @@ torch::Tensor dsa_index_score(torch::Tensor iq, torch::Tensor ik, torch::Tensor 
   const int threads = 256;
   k_dsa_index_score<<<(n_keys * 32 + threads - 1) / threads, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       iq.data_ptr<float>(), ik.data_ptr<float>(), w.data_ptr<float>(), score.data_ptr<double>(), n_keys,
-      (int)iq.size(0), (int)iq.size(1), (int)qpos, (float)scale);
+      (int)iq.size(0), (int)iq.size(1), (int)qpos, scale);
   FAK_CUDA_CHECK(cudaGetLastError());
   return score;
 }

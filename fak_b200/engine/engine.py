@@ -440,7 +440,7 @@ class Engine:
         btd = torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True)
         greedy = all(r.sampling.greedy for r in lanes)
         out = self.runner.decode(d[0:B], d[B:2 * B], d[2 * B:3 * B], btd, d[3 * B:4 * B], B,
-                                 use_graph=self._graphs_ready, shared=d[4 * B:4 * B + 1])
+                                 use_graph=self._graphs_ready, shared=d[4 * B:4 * B + 1], n_shared=int(shared[0]))
         self.stats["h2d_bytes"] += h.numel() * 4 + bt.size * 4
         if greedy:
             toks = out.cpu().tolist()

@@ -131,14 +131,20 @@ class ModelRunner:
         self.next_ids = torch.zeros(B, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.max_split = 64
-        self.attn_ws = torch.zeros(B * self.Hq * self.max_split * (self.D + 2), dtype=torch.float32, device=dev)
+        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
+        # cascade attention: prefix splits of the shared pages (about 2.6 CTAs per SM at 4 KV heads)
+        self.prefix_splits = max(16, min(128, (5 * n_sm) // (2 * max(1, self.Hkv))))
+        b_casc = min(B, 64 // max(1, self.Hq // max(1, self.Hkv)))   # lanes a cascade step can hold
+        slots = max(B * self.max_split, b_casc * (16 + self.prefix_splits))
+        self.attn_ws = torch.zeros(slots * self.Hq * (self.D + 2), dtype=torch.float32, device=dev)
         self.attn_tickets = torch.zeros(B * self.Hkv, dtype=torch.int32, device=dev)  # split-merge tickets
         # cascade attention: pages shared by every lane of the step (a radix-shared prefix) are
         # attended once for the whole batch; the count lives on the device so graphs stay valid
         self.cascade = cascade_attention
+        self._casc_on = False          # the step being run / captured uses cascade attention
+        self.min_shared_pages = 32     # below this many shared pages the plain path is faster
         self.shared_pages = torch.zeros(1, dtype=torch.int32, device=dev)
-        n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
-        self.prefix_splits = min(self.max_split - 16, max(16, 2 * n_sm // max(1, self.Hkv)))
+
         # per-device kernel scratch, allocated here so no graph capture allocates it
         mats = [weights.lm_head] + [m for L in weights.layers
                                     for m in [s for s, _ in L.qkv] + [L.o, L.gate_up, L.down]]
@@ -156,9 +162,14 @@ class ModelRunner:
         at 2K-9K contexts on B200 (8 is faster at batch 5 but leaves batch 1 with 32 CTAs)."""
         return 16
 
+    def cascade_ok(self, B: int) -> bool:
+        """Cascade attention can run for a B-lane step (its prefix kernel holds <= 64 query rows)."""
+        return self.cascade and B >= 2 and B * (self.Hq // max(1, self.Hkv)) <= 64
+
     def cascade_args(self, B: int, window: int = 0) -> dict:
-        """Arguments that turn on cascade attention for a B-lane step (none when it cannot apply)."""
-        if not self.cascade or B < 2 or window > 0 or B * (self.Hq // max(1, self.Hkv)) > 64:
+        """Arguments that turn on cascade attention in the step being run or captured (none when
+        the step is a plain one or cascade cannot apply)."""
+        if not self._casc_on or window > 0 or not self.cascade_ok(B):
             return {}
         return {"shared_pages": self.shared_pages, "prefix_splits": self.prefix_splits}
 
@@ -217,7 +228,15 @@ class ModelRunner:
         else:
             self.coll.decode_down(self, i, B)
 
-    def decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True, n_layers: int | None = None) -> None:
+    def decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True, n_layers: int | None = None,
+                     cascade: bool = False) -> None:
+        self._casc_on = cascade
+        try:
+            self._decode_eager(ids, pos, slot, bt, ctx, B, greedy, n_layers)
+        finally:
+            self._casc_on = False
+
+    def _decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True, n_layers: int | None = None) -> None:
         """One decode step for B lanes; results in self.logits[:B] / self.next_ids[:B].
 
         ``n_layers`` < cfg.n_layers runs only the first layers before the final norm and LM head:
@@ -259,41 +278,51 @@ class ModelRunner:
         }
 
     def capture(self, B: int, bt_width: int, n_layers: int | None = None) -> None:
+        """Capture the B-lane step: the plain variant, and (target model, cascade possible) the
+        cascade variant replayed when the lanes share enough prefix pages."""
         st = self._static_inputs(B, bt_width)
-        # warm up (also triggers lazy cudaFuncSetAttribute) on a side stream, then capture
-        s = torch.cuda.Stream(device=self.device)
-        s.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(s):
-            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers)
-        torch.cuda.current_stream(self.device).wait_stream(s)
-        torch.cuda.synchronize(self.device)
-        g = torch.cuda.CUDAGraph()
-        before = K.launches()
-        with torch.cuda.graph(g):
-            self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers)
-        key = (B, n_layers)
-        self._graph_kernels[key] = K.launches() - before
-        K._launches[0] = before
-        self._graphs[key] = (g, st)
+        variants = [False] + ([True] if n_layers is None and self.cascade_ok(B) else [])
+        for casc in variants:
+            # warm up (also triggers lazy cudaFuncSetAttribute) on a side stream, then capture
+            s = torch.cuda.Stream(device=self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers,
+                                  cascade=casc)
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            before = K.launches()
+            with torch.cuda.graph(g):
+                self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers,
+                                  cascade=casc)
+            key = (B, n_layers, casc)
+            self._graph_kernels[key] = K.launches() - before
+            K._launches[0] = before
+            self._graphs[key] = (g, st)
 
-    def graph_bucket(self, B: int, n_layers: int | None = None) -> int | None:
-        cands = [b for b, nl in self._graphs if b >= B and nl == n_layers]
+    def graph_bucket(self, B: int, n_layers: int | None = None, cascade: bool = False) -> int | None:
+        cands = [b for b, nl, c in self._graphs if b >= B and nl == n_layers and c == cascade]
         return min(cands) if cands else None
 
     def decode(self, ids, pos, slot, bt, ctx, B: int, use_graph: bool = True, n_layers: int | None = None,
-               shared: torch.Tensor | None = None) -> torch.Tensor:
+               shared: torch.Tensor | None = None, n_shared: int = 0) -> torch.Tensor:
         """Decode one token for B lanes; returns next ids (device int32 [B]).  ``shared`` (int32 [1]
-        on the device): leading block-table pages that are the same physical pages in every lane
-        and lie before every lane's current page (cascade attention); None = 0."""
-        if shared is not None:
+        on the device) / ``n_shared`` (the same count on the host): leading block-table pages that are
+        the same physical pages in every lane and lie before every lane's current page; with at
+        least ``min_shared_pages`` of them the step runs cascade attention."""
+        casc = shared is not None and n_shared >= self.min_shared_pages and n_layers is None
+        if casc:
             self.shared_pages.copy_(shared)
-        else:
-            self.shared_pages.zero_()
-        bucket = self.graph_bucket(B, n_layers) if use_graph else None
+        bucket = None
+        if use_graph:
+            bucket = self.graph_bucket(B, n_layers, casc) if casc else None
+            if bucket is None:
+                casc, bucket = False, self.graph_bucket(B, n_layers, False)
         if bucket is None:
-            self.decode_eager(ids, pos, slot, bt, ctx, B, n_layers=n_layers)
+            self.decode_eager(ids, pos, slot, bt, ctx, B, n_layers=n_layers, cascade=casc and self.cascade_ok(B))
             return self.next_ids[:B]
-        g, st = self._graphs[(bucket, n_layers)]
+        g, st = self._graphs[(bucket, n_layers, casc)]
         st["ids"][:B].copy_(ids)
         st["pos"][:B].copy_(pos)
         st["slot"][:B].copy_(slot)
@@ -304,7 +333,7 @@ class ModelRunner:
             st["ctx"][B:].fill_(1)
             st["slot"][B:].fill_(-1)
         g.replay()
-        K.count(self._graph_kernels[(bucket, n_layers)])
+        K.count(self._graph_kernels[(bucket, n_layers, casc)])
         return self.next_ids[:B]
 
     # ------------------------------------------------------------------------------------

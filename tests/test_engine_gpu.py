@@ -115,6 +115,7 @@ def test_radix_reuse_and_batched_equals_serial(model_file, cascade):
     """Without cascade attention a sequence reduces in the same order in any batch (bit-identical);
     with it the batch's shared prefix is attended once for all lanes (same values up to rounding)."""
     eng = _engine(model_file, graphs=True, cascade_attention=cascade)
+    eng.runner.min_shared_pages = 1   # cascade on even for this short shared prefix
     rng = np.random.default_rng(2)
     prefix = rng.integers(0, eng.cfg.vocab_size, 64).tolist()
     a = prefix + rng.integers(0, eng.cfg.vocab_size, 10).tolist()
