@@ -258,6 +258,8 @@ class EngineConfig:
     l2_prefetch: bool = False           # decode kernels warm L2 with the next GEMV's weights (measured neutral)
     cascade_attention: bool = False     # decode: a batch's shared prefix pages attended once for all lanes
                                         # (measured: no faster than the split-KV path yet at 5 lanes x 9K)
+    debug_poison: bool = False          # fill scratch with NaN and the KV cache with a large sentinel at start
+                                        # (a kernel reading memory nobody wrote shows up in its outputs)
     preempt_mode: str = "recompute"     # out of KV pages: "recompute" (radix-assisted) or "swap" to host memory
     swap_space_gb: float = 16.0         # pinned host memory for swapped-out KV pages
 
@@ -281,6 +283,7 @@ class EngineConfig:
         "attention_merge": ("FAK_ATTN_MERGE", bool),
         "l2_prefetch": ("FAK_L2_PREFETCH", bool),
         "cascade_attention": ("FAK_CASCADE_ATTN", bool),
+        "debug_poison": ("FAK_DEBUG_POISON", bool),
         "preempt_mode": ("FAK_PREEMPT_MODE", str),
         "swap_space_gb": ("FAK_SWAP_SPACE_GB", float),
     }

@@ -32,6 +32,7 @@ import torch
 
 from ..config import EngineConfig, ModelConfig
 from ..kv import OutOfPages, PagePool, RadixCache
+from ..ops import kernels as K
 from ..models.runner import KVCache, ModelRunner, PrefillMeta
 from ..models.weights import ModelWeights, gguf_source, load_weights, synthetic_source
 from .sampling import SamplingParams, sample
@@ -102,6 +103,8 @@ class Engine:
                                   attention_merge=self.ecfg.attention_merge, l2_prefetch=self.ecfg.l2_prefetch,
                                   cascade_attention=self.ecfg.cascade_attention)
         self.bt_width = math.ceil(self.max_context / ps)
+        if self.ecfg.debug_poison:
+            self._poison()
         self.waiting: list[Request] = []
         self.swapped: list[Request] = []   # preempted by swap: resumed (K/V copied back) before new work
         self._swap_bytes = 0
@@ -110,6 +113,8 @@ class Engine:
         self._rid = itertools.count()
         self.stats = {"prefill_tokens": 0, "prefill_tokens_avoided": 0, "decode_tokens": 0, "steps": 0,
                       "preemptions": 0, "h2d_bytes": 0, "d2h_bytes": 0, "swap_out_pages": 0, "swap_in_pages": 0}
+        # weight-load phases (seconds): read, convert (quant-on-load), upload, pack (tile layout), dense
+        self.stats.update({"load_" + k + "_s": v for k, v in getattr(weights, "load_profile", {}).items()})
         self._graphs_ready = False
 
     # ------------------------------------------------------------------------------------
@@ -335,6 +340,19 @@ class Engine:
         else:
             self.pool.release(r.pages)
         r.pages = []
+
+    def _poison(self) -> None:
+        """Debug: NaN in every float scratch buffer and a large finite sentinel in the KV cache, so a
+        kernel that reads scratch it did not write, or K/V positions its mask should exclude, changes
+        the outputs (masked positions are multiplied by an exact zero, which a finite sentinel keeps)."""
+        nan = float("nan")
+        rn = self.runner
+        for t in (rn.attn_ws, rn.qkv, rn.q, rn.h, rn.tmp, rn.logits, rn.x):
+            t.fill_(nan)
+        part, _ = K.tgemv_workspace(self.device)
+        part.fill_(nan)
+        self.kv.k.fill_(3.0e4)
+        self.kv.v.fill_(3.0e4)
 
     def _capped(self, logits: torch.Tensor) -> torch.Tensor:
         """Final-logit soft-capping (Gemma-2) before sampling; greedy argmax is unaffected by it."""

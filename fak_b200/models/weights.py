@@ -107,6 +107,7 @@ class ModelWeights:
     ffn_slice: tuple[int, int]  # [start, end) of the FFN dim on this rank
     tp_rank: int = 0
     tp_size: int = 1
+    load_profile: dict = dataclasses.field(default_factory=dict)   # seconds per load phase
 
     @property
     def n_q_local(self) -> int:
@@ -264,8 +265,18 @@ def _col_block_slice(raw: torch.Tensor, t: int, cols: int, c0: int, c1: int) -> 
 def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], device: str | torch.device = "cuda",
                  tp_rank: int = 0, tp_size: int = 1, expert_filter: tuple[int, int] | None = None,
                  prefill_dense: bool = False) -> ModelWeights:
-    cfg, get, close = source
+    import time
+    cfg, get0, close = source
     device = torch.device(device)
+    prof = {"read": 0.0, "convert": 0.0, "pack": 0.0, "dense": 0.0}
+    t_start = time.perf_counter()
+
+    def get(name: str):   # tensor reads, timed for the load profile
+        t = time.perf_counter()
+        try:
+            return get0(name)
+        finally:
+            prof["read"] += time.perf_counter() - t
     D = cfg.head_dim
     q_heads, kv_heads = head_assignment(cfg, tp_rank, tp_size)
     granule = 256
@@ -276,7 +287,9 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
 
     def quant(name: str) -> tuple[tuple[int, ...], int, torch.Tensor]:
         shape, t, raw = get(name)
+        t0 = time.perf_counter()
         rows2, t2 = _as_device_quant(shape, t, raw, device)
+        prof["convert"] += time.perf_counter() - t0
         return shape, t2, rows2
 
     emb_shape, emb_t, emb_raw = get("token_embd.weight")
@@ -348,12 +361,14 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
             if tp_size > 1:
                 draw = _col_block_slice(draw, dt, ds_[1], f0, f1)
             L.down = QuantWeight.from_rows(draw, dt, f1 - f0, device)
+        t0 = time.perf_counter()
         for s, _ in L.qkv:
             s.pack()
         L.o.pack()
         if L.gate_up is not None:
             L.gate_up.pack()
             L.down.pack()
+        t1 = time.perf_counter()
         if prefill_dense:
             for s, _ in L.qkv:
                 s.dense()
@@ -361,6 +376,8 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
             if L.gate_up is not None:
                 L.gate_up.dense()
                 L.down.dense()
+        prof["pack"] += t1 - t0
+        prof["dense"] += time.perf_counter() - t1
         layers.append(L)
     final_norm = _vec(get, "output_norm.weight", device)
     # lm_head: split by vocab rows under TP (ceil(V/T) rows per rank, the last rank may hold fewer)
@@ -372,7 +389,12 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
         lm_head = QuantWeight.from_rows(raw[v0:v1].contiguous(), t, shape[1], device)
     lm_head.pack()
     close()
-    return ModelWeights(cfg, embed, layers, final_norm, lm_head, q_heads, kv_heads, (f0, f1), tp_rank, tp_size)
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
+    prof["total"] = time.perf_counter() - t_start
+    prof["upload"] = max(0.0, prof["total"] - prof["read"] - prof["convert"] - prof["pack"] - prof["dense"])
+    return ModelWeights(cfg, embed, layers, final_norm, lm_head, q_heads, kv_heads, (f0, f1), tp_rank, tp_size,
+                        load_profile={k: round(v, 4) for k, v in prof.items()})
 
 
 def expert_slice(E: int, rank: int, size: int) -> tuple[int, int]:

@@ -329,3 +329,15 @@ def test_kvmmu_quarantine_on_a_running_request(model_file):
     assert m.apply(verdict, "tool-result") == 34 and r.n_kv == n0 - 34
     eng.run_until_done([r])
     assert len(r.full_output) == 16 and eng.pool.n_free() > 0
+
+
+def test_poisoned_scratch_changes_nothing(model_file):
+    """Debug poison: NaN in every float scratch buffer and a large sentinel in the KV cache at start.
+    A kernel that read scratch it never wrote, or K/V its mask should exclude, would change the
+    outputs; they stay identical.  The weight-load phase profile is reported in the engine stats."""
+    rng = np.random.default_rng(31)
+    prompts = [rng.integers(0, 500, n).tolist() for n in (23, 40, 7)]
+    want = _engine(model_file, graphs=True).generate(prompts, max_new_tokens=10)
+    eng = _engine(model_file, graphs=True, debug_poison=True)
+    assert eng.generate(prompts, max_new_tokens=10) == want
+    assert eng.stats["load_total_s"] > 0 and "load_pack_s" in eng.stats
