@@ -59,67 +59,6 @@ FAK_DEV void warp_quant_store(float v, int8_t* qdst, float2* dsdst, int lane) {
   if (lane == 0) *dsdst = make_float2(d, s);
 }
 
-// Merge the n_slots split partials (unnormalised o, running max in the log2 domain, sum) of one
-// (sequence, head) with all 128 threads: warp w folds slots w, w + 4, ... into an online-softmax
-// state (each lane holds D/32 output dims, read as one vector), then the four warp states merge in
-// shared memory and thread t finalises dim t (quantized output per 32 dims = one warp).  `sm` holds
-// 4 * D + 8 floats.  Empty slots (max -inf) are skipped.  Used by the combine kernel and by the
-// last-split merge inside k_decode_attn, so both give the same bits.
-template <int D>
-FAK_DEV void merge_slots(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int64_t base,
-                         int n_slots, float* __restrict__ sm, float* __restrict__ out, int8_t* __restrict__ qx,
-                         float2* __restrict__ ds, int64_t oi0) {
-  constexpr int V = D / 32;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float m = NEG_INF, L = 0.f, acc[V];
-#pragma unroll
-  for (int i = 0; i < V; i++) acc[i] = 0.f;
-  for (int sl = warp; sl < n_slots; sl += 4) {
-    const float2 ml = __ldcg(&part_ml[base + sl]);
-    if (ml.x == NEG_INF) continue;
-    float o[V];
-    const float* src = part_o + (base + sl) * D + lane * V;
-    if constexpr (V == 4) {
-      const float4 t = __ldcg(reinterpret_cast<const float4*>(src));
-      o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
-    } else {
-      const float2 t = __ldcg(reinterpret_cast<const float2*>(src));
-      o[0] = t.x; o[1] = t.y;
-    }
-    const float mn = fmaxf(m, ml.x);
-    const float c = exp2f(m - mn), f = exp2f(ml.x - mn);
-    L = L * c + f * ml.y;
-#pragma unroll
-    for (int i = 0; i < V; i++) acc[i] = acc[i] * c + f * o[i];
-    m = mn;
-  }
-  float* sacc = sm;              // [4][D]
-  float* sml = sm + 4 * D;       // [4][2]
-#pragma unroll
-  for (int i = 0; i < V; i++) sacc[warp * D + lane * V + i] = acc[i];
-  if (lane == 0) {
-    sml[2 * warp] = m;
-    sml[2 * warp + 1] = L;
-  }
-  __syncthreads();
-  const float mstar = fmaxf(fmaxf(sml[0], sml[2]), fmaxf(sml[4], sml[6]));
-  float f[4], Lt = 0.f;
-#pragma unroll
-  for (int w = 0; w < 4; w++) {
-    f[w] = sml[2 * w] == NEG_INF ? 0.f : exp2f(sml[2 * w] - mstar);
-    Lt += f[w] * sml[2 * w + 1];
-  }
-  const int dd = threadIdx.x;
-  if (dd < D) {
-    const float a = f[0] * sacc[dd] + f[1] * sacc[D + dd] + f[2] * sacc[2 * D + dd] + f[3] * sacc[3 * D + dd];
-    const float v = Lt > 0.f ? a / Lt : 0.f;
-    const int64_t oi = oi0 + dd;
-    if (out) out[oi] = v;
-    if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), lane);
-  }
-  __syncthreads();   // sm is free again
-}
-
 // =============================================================================================
 // decode
 // =============================================================================================
@@ -331,8 +270,8 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
     }
   }
   if (n_slots == 1 || tickets == nullptr) return;   // (tickets are only passed with n_slots == n_split)
-  // the last split CTA of this (sequence, KV group) merges all splits (merge_slots: the same order
-  // and arithmetic as k_decode_combine) and leaves its ticket at zero for the next launch
+  // the last split CTA of this (sequence, KV group) merges all splits (same order and arithmetic
+  // as k_decode_combine) and leaves its ticket at zero for the next launch
   __shared__ int s_ticket;
   __threadfence();
   __syncthreads();
@@ -340,11 +279,26 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   __syncthreads();
   if (s_ticket != n_split - 1) return;
   __threadfence();
-  float* msm = reinterpret_cast<float*>(smem_raw);   // the staging area is free again
-  for (int r = 0; r < G; r++) {
+  for (int r = warp; r < G; r += 4) {
     const int h = kvh * G + r;
-    merge_slots<D>(part_o, part_ml, ((int64_t)b * H + h) * n_split, n_split, msm, out, qx, ds,
-                   (int64_t)b * ldo + (int64_t)h * D);
+    const int64_t base = ((int64_t)b * H + h) * n_split;
+    float mstar = NEG_INF;
+    for (int s = 0; s < n_split; s++) mstar = fmaxf(mstar, __ldcg(&part_ml[base + s].x));
+    const float mb = mstar == NEG_INF ? 0.f : mstar;
+    for (int d0 = 0; d0 < D; d0 += 32) {
+      const int dd = d0 + lane;
+      float L = 0.f, acc = 0.f;
+      for (int s = 0; s < n_split; s++) {
+        const float2 ml = __ldcg(&part_ml[base + s]);
+        const float f = exp2f(ml.x - mb);
+        L += f * ml.y;
+        acc += f * __ldcg(&part_o[(base + s) * D + dd]);
+      }
+      const float v = L > 0.f ? acc / L : 0.f;
+      const int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
+      if (out) out[oi] = v;
+      if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), lane);
+    }
   }
   if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
 }
@@ -512,15 +466,27 @@ k_decode_attn_prefix(const float* __restrict__ q, const __nv_bfloat16* __restric
 }
 
 template <int D>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(D)
 k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int H, int n_split,
                  float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds, int ldo) {
-  __shared__ __align__(16) float sm[4 * D + 8];
   pdl_wait();
-  const int b = blockIdx.x, h = blockIdx.y;
-  merge_slots<D>(part_o, part_ml, ((int64_t)b * H + h) * n_split, n_split, sm, out, qx, ds,
-                 (int64_t)b * ldo + (int64_t)h * D);
+  const int b = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
+  const int64_t base = ((int64_t)b * H + h) * n_split;
+  float mstar = NEG_INF;
+  for (int s = 0; s < n_split; s++) mstar = fmaxf(mstar, part_ml[base + s].x);
+  float mb = mstar == NEG_INF ? 0.f : mstar;
+  float L = 0.f, acc = 0.f;
+  for (int s = 0; s < n_split; s++) {
+    float2 ml = part_ml[base + s];
+    float f = exp2f(ml.x - mb);
+    L += f * ml.y;
+    acc += f * part_o[(base + s) * D + dd];
+  }
   pdl_launch_dependents();
+  float v = L > 0.f ? acc / L : 0.f;
+  int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
+  if (out) out[oi] = v;
+  if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), dd & 31);
 }
 
 // =============================================================================================
@@ -819,7 +785,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   if (n_slots > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
     c2.gridDim = dim3(B, H);
-    c2.blockDim = dim3(128);
+    c2.blockDim = dim3(D);
     c2.stream = stream;
     set_pdl(c2);
     if (D == 128)
@@ -1003,7 +969,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
   if (n_split > 1) {
     cudaLaunchConfig_t c2 = {};
     c2.gridDim = dim3(B, H);
-    c2.blockDim = dim3(128);
+    c2.blockDim = dim3(D);
     c2.stream = static_cast<cudaStream_t>(stream);
     if (D == 128)
       e = cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
