@@ -7,6 +7,7 @@
 //   Q4_K  2304 B: hdr [16][16] (d, dmin, 12 scale bytes) | qs [16][128]
 //   Q6_K  3360 B: ql [16][128] | qh [16][64] (tile-row order) | scales [16][16] | d [16][2]
 //   Q8_0  4352 B: qs [16][256] (8 blocks x 32) | d [16][8][2]
+//   G4    2304 B: as Q4_K, the header holding (s0, m0, s1, m1) f32 of the two 128-groups (AWQ / GPTQ)
 // Plane row ("slot") s holds tile row (s >> 1) + 8 (s & 1), so the two rows an MMA thread owns
 // (g and g + 8) are adjacent slots; the 16-byte chunks of the quant planes are XOR-swizzled by slot
 // (Q4_K/Q8_0 qs: chunk ^ (s & 6); Q6_K ql: chunk ^ ((s >> 1) & 7)).  The Q6_K qh plane keeps tile-row
@@ -51,6 +52,7 @@ constexpr float MAGIC_F = 12582912.0f;
 
 template <int QT> struct Tile;
 template <> struct Tile<QT_Q4_K> { static constexpr int UT = 2304; static constexpr int TABF = 16 * 8 * 2; };
+template <> struct Tile<QT_G4> { static constexpr int UT = 2304; static constexpr int TABF = 16 * 8 * 2; };   // Q4_K shape
 template <> struct Tile<QT_Q6_K> { static constexpr int UT = 3360; static constexpr int TABF = 16 * 16; };
 template <> struct Tile<QT_Q8_0> { static constexpr int UT = 4352; static constexpr int TABF = 16 * 8; };
 
@@ -94,7 +96,6 @@ struct TGeo {
   int P;        // CTAs per slice
   int xstride;  // shared bytes per token row of activation codes
   int dstride;  // float2 per token row of the staged (scale, sum) pairs
-  int grp;      // Q4_K-shaped tiles: 0 = K-quant header, 1 = G4 group header (AWQ / GPTQ)
 };
 
 // Shared-memory carve-up (byte offsets), identical on host and device.
@@ -102,8 +103,9 @@ struct TSmem {
   int ring, xs, dsr, dsT, czT, tab, bars, total;
 };
 __host__ __device__ inline TSmem tsmem(int qt, int W, int R, int NT, const TGeo& g) {
-  const int UT = qt == QT_Q4_K ? 2304 : (qt == QT_Q6_K ? 3360 : 4352);
-  const int TABF = qt == QT_Q4_K ? 256 : (qt == QT_Q6_K ? 256 : 128);
+  const bool q4 = qt == QT_Q4_K || qt == QT_G4;   // G4 (AWQ / GPTQ) tiles have the Q4_K shape
+  const int UT = q4 ? 2304 : (qt == QT_Q6_K ? 3360 : 4352);
+  const int TABF = q4 ? 256 : (qt == QT_Q6_K ? 256 : 128);
   const int MB = 8 * NT;  // token rows staged
   TSmem s;
   s.ring = 0;
@@ -125,12 +127,12 @@ __host__ __device__ inline TSmem tsmem(int qt, int W, int R, int NT, const TGeo&
 template <int QT, int NT>
 FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, const int8_t* __restrict__ xr,
                        int xstride, const float2* __restrict__ dsT, const int* __restrict__ czT, int lane,
-                       float (&acc)[NT][4], int grp = 0) {
+                       float (&acc)[NT][4]) {
   constexpr int MB = 8 * NT;
   const int g = lane >> 2, t = lane & 3;
   const int sA = 2 * g, sB = 2 * g + 1;
-  if constexpr (QT == QT_Q4_K) {
-    if (grp) {  // G4 header (s0, m0, s1, m1): lane -> slot lane>>1, 128-group lane&1 = sub-blocks 4*(lane&1) .. +3
+  if constexpr (QT == QT_Q4_K || QT == QT_G4) {
+    if constexpr (QT == QT_G4) {  // header (s0, m0, s1, m1): lane -> slot lane>>1, 128-group lane&1 = sub-blocks 4*(lane&1) .. +3
       const int s = lane >> 1, jh = lane & 1;
       const float4 h = *reinterpret_cast<const float4*>(wt + 16 * s);
       const float sc = jh ? h.z : h.x, mn = jh ? h.w : h.y;
@@ -526,7 +528,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
     if (lane == 0) issue_next();  // into the slot released at the end of the previous iteration
     tc::mbar_wait(&bar[cslot], phase, err);
     unit_tile<QT, NT>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
-                      QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc, geo.grp);
+                      QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
     if (++cslot == R) {
       cslot = 0;
       phase ^= 1u;
@@ -674,7 +676,7 @@ k_tgemv_moe(const uint8_t* __restrict__ Wt, int Te, int K, const int8_t* __restr
     if (lane == 0) issue_next();
     tc::mbar_wait(&bar[cslot], phase, err);
     unit_tile<QT, 1>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
-                     QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc, geo.grp);
+                     QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
     if (++cslot == R) {
       cslot = 0;
       phase ^= 1u;
@@ -709,7 +711,7 @@ struct Plan {
   int smem;
 };
 
-int tile_bytes(int qt) { return qt == QT_Q4_K ? 2304 : (qt == QT_Q6_K ? 3360 : 4352); }
+int tile_bytes(int qt) { return (qt == QT_Q4_K || qt == QT_G4) ? 2304 : (qt == QT_Q6_K ? 3360 : 4352); }
 
 // Choose the K split, then (warps per CTA, ring depth) and the token tile width.  The split
 // minimises the unit tiles on the busiest warp (rounds of tiles x units per slice, plus the split-K
@@ -730,7 +732,6 @@ TGeo make_geo(int qt, int T, int U, int S0, int n_sm) {
   // activation rows 32 mod 128 bytes apart (8-byte loads, Q4_K/Q8_0) or 16 mod 128 (4-byte, Q6_K)
   g.xstride = ((Us * 256 + 127) / 128) * 128 + (qt == QT_Q6_K ? 16 : 32);
   g.dstride = Us * 8;
-  g.grp = 0;
   return g;
 }
 
@@ -772,14 +773,10 @@ Plan make_plan(int qt, int64_t N, int64_t K, int NT, int n_sm, int max_smem, int
 
 }  // namespace
 
-// G4 (AWQ / GPTQ) tiles have the Q4_K shape: the Q4_K kernels run them with geo.grp = 1.
-static int64_t kernel_qt(int64_t qtype) { return qtype == QT_G4 ? QT_Q4_K : qtype; }
-
-int64_t tgemv_unit_bytes(int64_t qtype) { return tile_bytes((int)kernel_qt(qtype)); }
+int64_t tgemv_unit_bytes(int64_t qtype) { return tile_bytes((int)qtype); }
 
 // Scratch floats / counters the split-K reduction of this shape needs.
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device) {
-  qtype = kernel_qt(qtype);
   int n_sm = 0, max_smem = 0;
   FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, (int)device));
   FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, (int)device));
@@ -815,9 +812,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     ar.flags_off = ar_flags_off;
     ar.epochs = reinterpret_cast<uint32_t*>(ar_epochs->data_ptr<int>());
   }
-  const int grp = qtype == QT_G4;
-  qtype = kernel_qt(qtype);
-  TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "tgemv: qtype");
+  TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0 || qtype == QT_G4, "tgemv: qtype");
   TORCH_CHECK(K % 64 == 0 && (qtype == QT_Q8_0 || K % 256 == 0), "tgemv: K must be a multiple of 256 (64 for Q8_0)");
   const int64_t T = (N + 15) / 16, U = (K + 255) / 256;
   TORCH_CHECK(w.numel() >= T * U * tile_bytes((int)qtype), "tgemv: weight buffer smaller than the tile-packed size");
@@ -865,7 +860,6 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   }
   Plan p = make_plan((int)qtype, N, K, NT, n_sm, max_smem, (int)(flags & 31), (int)((flags >> 5) & 15),
                      (int)((flags >> 9) & 255));
-  p.geo.grp = grp;
   if (p.geo.S > 1) {
     TORCH_CHECK(part.scalar_type() == torch::kFloat32 && part.numel() >= (int64_t)p.geo.S * p.geo.T * 128 * p.NT,
                 "tgemv: split-K scratch too small");
@@ -913,6 +907,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     else FAK_TG_NT(QTV, 4)                \
   }
   if (qtype == QT_Q4_K) FAK_TG(QT_Q4_K)
+  else if (qtype == QT_G4) FAK_TG(QT_G4)
   else if (qtype == QT_Q6_K) FAK_TG(QT_Q6_K)
   else FAK_TG(QT_Q8_0)
 #undef FAK_TG
@@ -925,9 +920,7 @@ void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t 
                torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
                torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "moe_tgemv: w");
-  const int grp = qtype == QT_G4;
-  qtype = kernel_qt(qtype);
-  TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0, "moe_tgemv: qtype");
+  TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0 || qtype == QT_G4, "moe_tgemv: qtype");
   TORCH_CHECK(rows_per_expert % 16 == 0 && K % 256 == 0, "moe_tgemv: rows per expert % 16, K % 256");
   TORCH_CHECK(qx.scalar_type() == torch::kInt8 && qx.is_contiguous() &&
                   reinterpret_cast<uintptr_t>(qx.data_ptr()) % 16 == 0, "moe_tgemv: qx");
@@ -939,7 +932,6 @@ void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t 
   if (!max_smem)
     FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, w.get_device()));
   TGeo g = make_geo((int)qtype, (int)(rows_per_expert / 16), (int)(K / 256), 1, 1);
-  g.grp = grp;
   const int Te = (int)(rows_per_expert / 16);
   int W = 16, R = 3;
   if (tsmem((int)qtype, 16, 3, 1, g).total > max_smem) W = 8;
@@ -970,6 +962,7 @@ void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t 
     else go(k_tgemv_moe<QTV, 8, 3>);                       \
   }
   if (qtype == QT_Q4_K) FAK_TGM(QT_Q4_K)
+  else if (qtype == QT_G4) FAK_TGM(QT_G4)
   else if (qtype == QT_Q6_K) FAK_TGM(QT_Q6_K)
   else FAK_TGM(QT_Q8_0)
 #undef FAK_TGM
