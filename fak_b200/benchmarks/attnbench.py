@@ -27,6 +27,8 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--split", type=int, default=16)
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="time prefill attention instead: each sequence's last N tokens attend to the whole context")
     ap.add_argument("--cascade", type=int, default=0,
                     help="prefix splits of cascade attention over the shared pages (0: plain split-KV path)")
     args = ap.parse_args(argv)
@@ -58,6 +60,17 @@ def main(argv=None):
         kc, vc = caches[i % args.layers]
         K.decode_attention(q, kc, vc, bt, ctx_t, args.split, act=act, workspace=ws, **casc)
 
+    if args.prefill:   # B chunks of the last `prefill` tokens over the cached context
+        from fak_b200.models.runner import PrefillMeta
+        Q = args.prefill
+        meta = PrefillMeta.build([Q] * B, [ctx - Q] * B, dev)
+        qp = torch.randn(B * Q, H, D, device=dev, generator=g).bfloat16()
+        outp = torch.empty(B * Q, H * D, device=dev, dtype=torch.bfloat16)
+
+        def run(i):  # noqa: F811
+            kc, vc = caches[i % args.layers]
+            K.prefill_attention(qp, kc, vc, bt, meta, outp)
+
     for i in range(3):
         run(i)
     torch.cuda.synchronize()
@@ -70,7 +83,9 @@ def main(argv=None):
     us = e0.elapsed_time(e1) * 1000 / args.iters
     page_bytes = 2 * Hkv * 16 * D * 2
     unique = (n_sh + B * (per_seq - n_sh)) * page_bytes
-    print(json.dumps({"kernel": "decode_attention+combine", "batch": B, "ctx": ctx, "shared": n_sh * 16,
+    print(json.dumps({"kernel": "prefill_attention" if args.prefill else "decode_attention+combine",
+                      "prefill": args.prefill,
+                      "batch": B, "ctx": ctx, "shared": n_sh * 16,
                       "heads": H, "kv_heads": Hkv, "head_dim": D, "splits": args.split, "cascade": args.cascade,
                       "us": round(us, 2),
                       "unique_kv_bytes": unique, "tb_s_unique": round(unique / us / 1e6, 3),
