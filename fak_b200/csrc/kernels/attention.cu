@@ -20,6 +20,7 @@
 #include <c10/cuda/CUDAStream.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "mma.cuh"
@@ -62,14 +63,17 @@ FAK_DEV void warp_quant_store(float v, int8_t* qdst, float2* dsdst, int lane) {
 // =============================================================================================
 // decode
 // =============================================================================================
-constexpr int DEC_STAGES = 3;  // pages in flight per warp (ring depth)
-template <int D>
+// pages in flight per warp (ring depth).  Two pages (68 KB of shared memory at head dim 128) let
+// three CTAs share an SM; three pages (102 KB) only two.  At 5 sequences x 4 KV heads x 16 splits
+// (320 CTAs on 148 SMs) the deeper ring measured 28.0 us against 21.3 us for two.
+constexpr int DEC_STAGES = 2;
+template <int D, int ST = DEC_STAGES>
 struct DecodeSmem {
-  __nv_bfloat16 k[4][DEC_STAGES][PAGE][D + 8];
-  __nv_bfloat16 v[4][DEC_STAGES][PAGE][D + 8];
+  __nv_bfloat16 k[4][ST][PAGE][D + 8];
+  __nv_bfloat16 v[4][ST][PAGE][D + 8];
 };
 
-template <int D>
+template <int D, int ST = DEC_STAGES>   // ST: pages in flight per warp
 __global__ void __launch_bounds__(128)
 k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc,
               const int* __restrict__ block_table, int bt_stride, const int* __restrict__ ctx_len, int H, int Hkv,
@@ -81,7 +85,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  DecodeSmem<D>& sm = *reinterpret_cast<DecodeSmem<D>*>(smem_raw);
+  DecodeSmem<D, ST>& sm = *reinterpret_cast<DecodeSmem<D, ST>*>(smem_raw);
 
   const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -141,21 +145,21 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
     cp_async_commit();
   };
 
-  // warp w takes pages p_begin + w, + 4, ...; DEC_STAGES - 1 of them stay in flight while it
+  // warp w takes pages p_begin + w, + 4, ...; ST - 1 of them stay in flight while it
   // computes on one (an empty commit group keeps the group count uniform past the end)
   const int p0 = p_begin + warp;
 #pragma unroll
-  for (int i = 0; i < DEC_STAGES - 1; i++) {
+  for (int i = 0; i < ST - 1; i++) {
     if (p0 + 4 * i < p_end) issue_page(p0 + 4 * i, i);
     else cp_async_commit();
   }
   int buf = 0;
   for (int p = p0, it = 0; p < p_end; p += 4, it++) {
-    const int pn = p + 4 * (DEC_STAGES - 1);
-    if (pn < p_end) issue_page(pn, (it + DEC_STAGES - 1) % DEC_STAGES);
+    const int pn = p + 4 * (ST - 1);
+    if (pn < p_end) issue_page(pn, (it + ST - 1) % ST);
     else cp_async_commit();
-    cp_async_wait<DEC_STAGES - 1>();
-    buf = it % DEC_STAGES;
+    cp_async_wait<ST - 1>();
+    buf = it % ST;
     __syncwarp();
     // S = Q K^T for 16 tokens
     float s[2][4];
@@ -763,24 +767,27 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     if (D == 128) go(k_decode_attn_prefix<128>, sizeof(PrefixSmem<128>));
     else go(k_decode_attn_prefix<64>, sizeof(PrefixSmem<64>));
   }
+  // page-ring depth per warp: DEC_STAGES (2), or 3 with FAK_DEC_STAGES=3
+  static const int dec_st = [] {
+    const char* e = std::getenv("FAK_DEC_STAGES");
+    return (e && std::atoi(e) == 3) ? 3 : DEC_STAGES;
+  }();
+  auto go = [&](auto kern, size_t smem) {
+    cfg.dynamicSmemBytes = smem;
+    FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const float*)q.data_ptr<float>(),
+                                      (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
+                                      (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
+                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
+                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots, cap_in, cap_out));
+  };
+  const size_t merge128 = (size_t)(4 * 16 * 128 + 4 * 16 * 2) * 4, merge64 = (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4;
   if (D == 128) {
-    size_t smem = std::max(sizeof(DecodeSmem<128>), (size_t)(4 * 16 * 128 + 4 * 16 * 2) * 4);
-    cfg.dynamicSmemBytes = smem;
-    FAK_CUDA_CHECK(cudaFuncSetAttribute(k_decode_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<128>, (const float*)q.data_ptr<float>(),
-                                      (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
-                                      (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots, cap_in, cap_out));
+    if (dec_st == 2) go(k_decode_attn<128, 2>, std::max(sizeof(DecodeSmem<128, 2>), merge128));
+    else go(k_decode_attn<128, 3>, std::max(sizeof(DecodeSmem<128, 3>), merge128));
   } else {
-    size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
-    cfg.dynamicSmemBytes = smem;
-    FAK_CUDA_CHECK(cudaFuncSetAttribute(k_decode_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_attn<64>, (const float*)q.data_ptr<float>(),
-                                      (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
-                                      (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
-                                      H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots, cap_in, cap_out));
+    if (dec_st == 2) go(k_decode_attn<64, 2>, std::max(sizeof(DecodeSmem<64, 2>), merge64));
+    else go(k_decode_attn<64, 3>, std::max(sizeof(DecodeSmem<64, 3>), merge64));
   }
   if (n_slots > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
