@@ -54,6 +54,17 @@ class ModelConfig:
     sandwich_norms: bool = False
     embed_scale: float = 1.0
     attn_scale: float = 0.0
+    # gpt-oss blocks: a learned per-head sink logit in every attention softmax (``attn_sinks``),
+    # an output-projection bias, a biased router that keeps the top-k logits and then takes the
+    # softmax over those k (``router`` "topk_softmax"; default "softmax_topk" = softmax over all
+    # experts, then top-k), biased experts, and the clamped OAI gate
+    # (up + 1) * g * sigmoid(alpha * g) with g <= limit, |up| <= limit (``swiglu_alpha`` > 0)
+    attn_sinks: bool = False
+    attn_out_bias: bool = False
+    router: str = "softmax_topk"
+    moe_bias: bool = False
+    swiglu_alpha: float = 0.0
+    swiglu_limit: float = 0.0
     bos_token_id: int = 1
     eos_token_id: int = 2
     name: str = ""
@@ -97,6 +108,8 @@ class ModelConfig:
             raise ValueError("head_dim must be even for RoPE")
         if self.is_moe and not (0 < self.n_experts_used <= self.n_experts):
             raise ValueError("MoE config needs 0 < n_experts_used <= n_experts")
+        if self.router not in ("softmax_topk", "topk_softmax"):
+            raise ValueError(f"unknown router {self.router!r}")
 
     def param_count(self) -> int:
         d, L = self.d_model, self.n_layers
@@ -127,6 +140,16 @@ PRESETS: dict[str, ModelConfig] = {
                                  n_experts=128, n_experts_used=8, expert_ffn_dim=768, norm_topk_prob=True,
                                  max_context=32768, bos_token_id=151643, eos_token_id=151645,
                                  name="qwen3-30b-a3b"),
+    # gpt-oss-20b: 24 layers, 2880 wide, 64/8 heads of 64, 32 experts top-4 of width 2880 (MXFP4 in
+    # the checkpoint), attention sinks, biases everywhere, 128-token windows on the even layers,
+    # YaRN x32 over a 4096-token original context, theta 150000
+    "gpt-oss-20b": ModelConfig("gptoss", 24, 2880, 64, 8, 64, 2880, 201088, 1e-5, 150000.0, qkv_bias=True,
+                               n_experts=32, n_experts_used=4, expert_ffn_dim=2880, max_context=131072,
+                               rope_scaling={"type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                                             "original_max_position_embeddings": 4096, "truncate": False},
+                               sliding_window=128, swa_layers=tuple(range(0, 24, 2)), attn_sinks=True,
+                               attn_out_bias=True, router="topk_softmax", moe_bias=True, swiglu_alpha=1.702,
+                               swiglu_limit=7.0, bos_token_id=199998, eos_token_id=200002, name="gpt-oss-20b"),
     # small shapes for tests (same structure, few layers)
     "tiny-llama": ModelConfig("llama", 2, 256, 4, 2, 64, 512, 512, 1e-5, 10000.0, tie_embeddings=True,
                               max_context=1024, name="tiny-llama"),
@@ -137,6 +160,13 @@ PRESETS: dict[str, ModelConfig] = {
                                act="gelu_tanh", attn_softcap=50.0, final_softcap=30.0, sandwich_norms=True,
                                embed_scale=16.0, sliding_window=32, swa_layers=(0,), max_context=1024,
                                name="tiny-gemma2"),
+    "tiny-gptoss": ModelConfig("gptoss", 2, 256, 4, 2, 64, 256, 512, 1e-5, 150000.0, qkv_bias=True,
+                               n_experts=4, n_experts_used=2, expert_ffn_dim=128, max_context=2048,
+                               rope_scaling={"type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                                             "original_max_position_embeddings": 64, "truncate": False},
+                               sliding_window=16, swa_layers=(0,), attn_sinks=True, attn_out_bias=True,
+                               router="topk_softmax", moe_bias=True, swiglu_alpha=1.702, swiglu_limit=7.0,
+                               name="tiny-gptoss"),
     "tiny-qwen3moe": ModelConfig("qwen3moe", 2, 512, 8, 2, 64, 1024, 1024, 1e-6, 1e6, qk_norm=True,
                                  n_experts=8, n_experts_used=2, expert_ffn_dim=256, max_context=2048,
                                  name="tiny-qwen3moe"),

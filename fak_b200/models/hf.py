@@ -80,6 +80,8 @@ def config_from_hf(hf: dict) -> ModelConfig:
     arch_name = (hf.get("architectures") or [hf.get("model_type", "")])[0].lower()
     if "gemma2" in arch_name or hf.get("model_type") == "gemma2":
         arch = "gemma2"
+    elif "gptoss" in arch_name or hf.get("model_type") == "gpt_oss":
+        arch = "gptoss"
     elif "qwen3moe" in arch_name or hf.get("model_type") == "qwen3_moe":
         arch = "qwen3moe"
     elif "qwen3" in arch_name:
@@ -98,11 +100,13 @@ def config_from_hf(hf: dict) -> ModelConfig:
         n_kv_heads=int(hf.get("num_key_value_heads", H)), head_dim=int(hf.get("head_dim") or d // H),
         ffn_dim=int(hf.get("intermediate_size", 0)), vocab_size=int(hf["vocab_size"]),
         rms_eps=float(hf.get("rms_norm_eps", 1e-6)), rope_theta=theta,
-        tie_embeddings=bool(hf.get("tie_word_embeddings", False)), qkv_bias=arch == "qwen2",
+        tie_embeddings=bool(hf.get("tie_word_embeddings", False)),
+        qkv_bias=arch == "qwen2" or (arch == "gptoss" and bool(hf.get("attention_bias", True))),
         qk_norm=arch in ("qwen3", "qwen3moe"),
-        n_experts=int(hf.get("num_experts", 0)) if arch == "qwen3moe" else 0,
-        n_experts_used=int(hf.get("num_experts_per_tok", 0)) if arch == "qwen3moe" else 0,
-        expert_ffn_dim=int(hf.get("moe_intermediate_size", 0)) if arch == "qwen3moe" else 0,
+        **(_gptoss_fields(hf) if arch == "gptoss" else {
+            "n_experts": int(hf.get("num_experts", 0)) if arch == "qwen3moe" else 0,
+            "n_experts_used": int(hf.get("num_experts_per_tok", 0)) if arch == "qwen3moe" else 0,
+            "expert_ffn_dim": int(hf.get("moe_intermediate_size", 0)) if arch == "qwen3moe" else 0}),
         norm_topk_prob=bool(hf.get("norm_topk_prob", True)),
         max_context=int(hf.get("max_position_embeddings", 32768)),
         rope_scaling=_hf_rope_scaling(rp, hf),
@@ -122,6 +126,16 @@ def _gemma_fields(hf: dict) -> dict:
             "final_softcap": float(hf.get("final_logit_softcapping") or 0.0),
             "sandwich_norms": True, "embed_scale": float(hf["hidden_size"]) ** 0.5,
             "attn_scale": float(hf.get("query_pre_attn_scalar") or hf.get("head_dim") or 256) ** -0.5}
+
+
+def _gptoss_fields(hf: dict) -> dict:
+    """gpt-oss: every layer routed (num_local_experts, top num_experts_per_tok, width
+    intermediate_size), attention sinks, biased projections, router and experts, clamped OAI gate."""
+    bias = bool(hf.get("attention_bias", True))
+    return {"n_experts": int(hf["num_local_experts"]), "n_experts_used": int(hf["num_experts_per_tok"]),
+            "expert_ffn_dim": int(hf["intermediate_size"]), "attn_sinks": True, "attn_out_bias": bias,
+            "router": "topk_softmax", "moe_bias": True, "swiglu_alpha": 1.702,
+            "swiglu_limit": float(hf.get("swiglu_limit") or 7.0)}
 
 
 def _hf_sliding_window(hf: dict, n_layers: int) -> dict:
@@ -164,7 +178,12 @@ _LAYER = {
     "post_attention_layernorm.weight": "ffn_norm.weight", "mlp.gate_proj.weight": "ffn_gate.weight",
     "mlp.up_proj.weight": "ffn_up.weight", "mlp.down_proj.weight": "ffn_down.weight",
     "mlp.gate.weight": "ffn_gate_inp.weight",
+    # gpt-oss
+    "self_attn.sinks": "attn_sinks.weight", "self_attn.o_proj.bias": "attn_output.bias",
+    "mlp.router.weight": "ffn_gate_inp.weight", "mlp.router.bias": "ffn_gate_inp.bias",
 }
+# gpt-oss experts: all experts of a layer in one tensor; gate and up rows interleaved (gate even)
+_FUSED_EXPERTS = re.compile(r"model\.layers\.(\d+)\.mlp\.experts\.(gate_up_proj|down_proj)(_blocks|_scales|_bias)?")
 _EXPERT = re.compile(r"model\.layers\.(\d+)\.mlp\.experts\.(\d+)\.(gate|up|down)_proj\.weight")
 _EXP_NAME = {"gate": "ffn_gate_exps.weight", "up": "ffn_up_exps.weight", "down": "ffn_down_exps.weight"}
 
@@ -204,10 +223,10 @@ def _quant_config(hf: dict) -> dict | None:
     if not q:
         return None
     method = str(q.get("quant_method", "")).lower()
-    if method == "exl2":
-        return None   # EXL2 layers are recognised by their tensors (q_groups, q_weight, ...)
+    if method in ("exl2", "mxfp4"):
+        return None   # recognised by their tensors (q_groups, q_weight, ... / _blocks, _scales)
     if method not in ("awq", "gptq"):
-        raise ValueError(f"unsupported quantization method {method!r} (AWQ, GPTQ and EXL2 are)")
+        raise ValueError(f"unsupported quantization method {method!r} (AWQ, GPTQ, EXL2 and MXFP4 are)")
     return q
 
 
@@ -249,6 +268,7 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
     experts: dict[str, dict[int, tuple[str, np.ndarray]]] = {}
     qparts: dict[str, dict[str, object]] = {}   # base name -> {qweight, qzeros, scales, g_idx}
     exl2_parts: dict[str, dict[str, tuple]] = {}   # base name -> {q_weight, q_groups, q_scale, ...}
+    fused: dict[tuple[str, str], dict[str, tuple]] = {}   # (layer, gate_up_proj | down_proj) -> parts
     for p in files:
         for n, (dt, shape, arr) in read_safetensors(p).items():
             if qc is not None and n.endswith(_QPARTS):
@@ -263,6 +283,10 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
             if m:
                 key = f"blk.{m.group(1)}.{_EXP_NAME[m.group(3)]}"
                 experts.setdefault(key, {})[int(m.group(2))] = (dt, arr)
+                continue
+            m = _FUSED_EXPERTS.fullmatch(n)
+            if m:
+                fused.setdefault((m.group(1), m.group(2)), {})[m.group(3) or ""] = (dt, np.asarray(arr))
                 continue
             m2 = re.fullmatch(r"model\.layers\.(\d+)\.(self_attn\.qkv_proj|mlp\.gate_up_proj)\.weight", n)
             if m2:   # fused projections: row ranges of one matrix
@@ -307,6 +331,8 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
         w = exl2.dequantize(parts["q_weight"][1], parts["q_groups"][1], f("q_scale"), f("q_scale_max"),
                             parts["q_invperm"][1] if "q_invperm" in parts else None)
         table[g] = ("F32", tuple(w.shape), w)
+    for (i, kind), parts in fused.items():
+        table.update(_fused_experts(i, kind, parts))
     for key, per in experts.items():
         dts = {d for d, _ in per.values()}
         stacked = np.stack([per[e][1] for e in range(len(per))])
@@ -337,6 +363,37 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
     return cfg, get, lambda: None
 
 
+def _fused_experts(i: str, kind: str, parts: dict[str, tuple]) -> dict[str, tuple]:
+    """gpt-oss expert tensors of one layer as float32 [E, out, in] matrices and [E, out] biases
+    under GGUF names.  MXFP4 (``_blocks`` + ``_scales``) is stored out-major already; the float form
+    is [E, in, out] (multiplied from the right) and is transposed.  gate_up rows interleave the gate
+    (even) and the linear branch (odd)."""
+    out = {}
+    if "_blocks" in parts:
+        from . import mxfp4
+        w = mxfp4.dequantize(parts["_blocks"][1], parts["_scales"][1])
+    elif "" in parts:
+        w = np.ascontiguousarray(np.swapaxes(_to_f32(*parts[""]), 1, 2))
+    else:
+        w = None
+    b = _to_f32(*parts["_bias"]) if "_bias" in parts else None
+    p = f"blk.{i}."
+    if kind == "gate_up_proj":
+        for nm, sl in (("ffn_gate_exps", slice(0, None, 2)), ("ffn_up_exps", slice(1, None, 2))):
+            if w is not None:
+                m = np.ascontiguousarray(w[:, sl])
+                out[p + nm + ".weight"] = ("F32", m.shape, m)
+            if b is not None:
+                v = np.ascontiguousarray(b[:, sl])
+                out[p + nm + ".bias"] = ("F32", v.shape, v)
+    else:
+        if w is not None:
+            out[p + "ffn_down_exps.weight"] = ("F32", w.shape, np.ascontiguousarray(w))
+        if b is not None:
+            out[p + "ffn_down_exps.bias"] = ("F32", b.shape, np.ascontiguousarray(b))
+    return out
+
+
 def _dequant_rows(rows: np.ndarray, t: int, shape) -> np.ndarray:
     from ..gguf.quants import dequantize
     return dequantize(np.ascontiguousarray(rows).reshape(-1), t, shape).astype(np.float32).view(np.uint8).reshape(
@@ -355,6 +412,13 @@ def load_reference_tensors_hf(model_dir: str) -> tuple[ModelConfig, dict[str, to
                                   "attn_v.weight", "attn_output.weight")]
         if cfg.qkv_bias:
             names += [p + n for n in ("attn_q.bias", "attn_k.bias", "attn_v.bias")]
+        if cfg.attn_out_bias:
+            names.append(p + "attn_output.bias")
+        if cfg.attn_sinks:
+            names.append(p + "attn_sinks.weight")
+        if cfg.moe_bias:
+            names += [p + n for n in ("ffn_gate_inp.bias", "ffn_gate_exps.bias", "ffn_up_exps.bias",
+                                      "ffn_down_exps.bias")]
         if cfg.qk_norm:
             names += [p + "attn_q_norm.weight", p + "attn_k_norm.weight"]
         if cfg.sandwich_norms:

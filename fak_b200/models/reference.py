@@ -12,6 +12,9 @@ is tested against it.  Semantics kept identical to the reference:
 * MoE router: softmax over all experts, then top-k, renormalised when
   ``norm_topk_prob`` (internal/model/moe.go:279-311).
 * Causal attention with GQA head groups.
+* gpt-oss blocks: a per-head sink logit that joins every softmax and is then dropped
+  (internal/model/arch.go:304-333, softmaxDropSinkInPlace), output-projection bias, a biased
+  top-k-then-softmax router, biased experts and the clamped OAI gate (internal/model/config.go:205-214).
 """
 from __future__ import annotations
 
@@ -57,8 +60,23 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return torch.cat([x0 * c - x1 * s, x1 * c + x0 * s], dim=-1)
 
 
-def moe_route(logits: torch.Tensor, k: int, norm_topk: bool) -> tuple[torch.Tensor, torch.Tensor]:
-    """Softmax-then-top-k router. Returns (weights [T,k], expert ids [T,k])."""
+def oai_gate(g: torch.Tensor, u: torch.Tensor, alpha: float, limit: float) -> torch.Tensor:
+    """gpt-oss gated activation: (u + 1) * g * sigmoid(alpha * g), the gate clamped to <= limit and
+    the linear branch to [-limit, limit] (limit 0: no clamp)."""
+    if limit > 0:
+        g = g.clamp(max=limit)
+        u = u.clamp(-limit, limit)
+    return (u + 1.0) * g * torch.sigmoid(alpha * g)
+
+
+def moe_route(logits: torch.Tensor, k: int, norm_topk: bool, kind: str = "softmax_topk"
+              ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns (weights [T,k], expert ids [T,k]).  "softmax_topk": softmax over every expert, then
+    the top k (renormalised when ``norm_topk``); "topk_softmax": the top k logits, then a softmax
+    over those k."""
+    if kind == "topk_softmax":
+        v, idx = torch.topk(logits.float(), k, dim=-1)
+        return torch.softmax(v, dim=-1), idx
     p = torch.softmax(logits.float(), dim=-1)
     w, idx = torch.topk(p, k, dim=-1)
     if norm_topk:
@@ -113,14 +131,26 @@ class ReferenceModel:
             g = self.mm(x, p + "ffn_gate.weight")
             u = self.mm(x, p + "ffn_up.weight")
             return self.mm(act_fn(cfg.act, g) * u, p + "ffn_down.weight")
-        wts, idx = moe_route(x @ self.w(p + "ffn_gate_inp.weight").T, cfg.n_experts_used, cfg.norm_topk_prob)
+        logits = x @ self.w(p + "ffn_gate_inp.weight").T
+        if cfg.moe_bias:
+            logits = logits + self.w(p + "ffn_gate_inp.bias")
+        wts, idx = moe_route(logits, cfg.n_experts_used, cfg.norm_topk_prob, cfg.router)
         G, U, D = self.w(p + "ffn_gate_exps.weight"), self.w(p + "ffn_up_exps.weight"), self.w(p + "ffn_down_exps.weight")
+        if cfg.moe_bias:
+            bg, bu, bd = (self.w(p + n) for n in ("ffn_gate_exps.bias", "ffn_up_exps.bias", "ffn_down_exps.bias"))
         out = torch.zeros_like(x)
         for t in range(x.shape[0]):
             for j in range(cfg.n_experts_used):
                 e = int(idx[t, j])
-                h = act_fn(cfg.act, G[e] @ x[t]) * (U[e] @ x[t])
-                out[t] += wts[t, j] * (D[e] @ h)
+                g, u = G[e] @ x[t], U[e] @ x[t]
+                if cfg.moe_bias:
+                    g, u = g + bg[e], u + bu[e]
+                h = oai_gate(g, u, cfg.swiglu_alpha, cfg.swiglu_limit) if cfg.swiglu_alpha > 0 \
+                    else act_fn(cfg.act, g) * u
+                y = D[e] @ h
+                if cfg.moe_bias:
+                    y = y + bd[e]
+                out[t] += wts[t, j] * y
         return out
 
     def forward(self, ids: torch.Tensor, start_pos: int = 0,
@@ -171,8 +201,11 @@ class ReferenceModel:
                 K, V = k, v
             a = attention(q, K, V, start_pos, cfg.layer_window(i),
                           None if self.attn_observer is None else (lambda pr, i=i: self.attn_observer(i, pr)),
-                          scale=cfg.attn_scale, softcap_=cfg.attn_softcap)
+                          scale=cfg.attn_scale, softcap_=cfg.attn_softcap,
+                          sinks=self.w(p + "attn_sinks.weight") if cfg.attn_sinks else None)
             o = self.mm(a.reshape(T, H * D), p + "attn_output.weight")
+            if cfg.attn_out_bias:
+                o = o + self.w(p + "attn_output.bias")
             if cfg.sandwich_norms:
                 o = rmsnorm(o, self.w(p + "post_attention_norm.weight"), cfg.rms_eps)
             x = x + o
@@ -217,9 +250,11 @@ class ReferenceModel:
 
 
 def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int, window: int = 0,
-              observe=None, scale: float = 0.0, softcap_: float = 0.0) -> torch.Tensor:
+              observe=None, scale: float = 0.0, softcap_: float = 0.0,
+              sinks: torch.Tensor | None = None) -> torch.Tensor:
     """q [T,H,D] at positions start_pos..; K,V [Tctx,Hk,D] covering positions 0..Tctx-1 (causal;
-    window > 0: each query sees keys (qpos - window, qpos])."""
+    window > 0: each query sees keys (qpos - window, qpos]).  sinks [H]: one extra logit per head
+    that joins the softmax's normaliser and attends to nothing."""
     T, H, D = q.shape
     Tc, Hk, _ = K.shape
     g = H // Hk
@@ -233,7 +268,11 @@ def attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, start_pos: int,
     if window > 0:
         masked = masked | (kpos <= qpos - window)
     s = s.masked_fill(masked[None], float("-inf"))
-    pr = torch.softmax(s, dim=-1)
+    if sinks is not None:
+        sk = sinks.float().to(s.device)[:, None, None].expand(H, T, 1)
+        pr = torch.softmax(torch.cat([s, sk], dim=-1), dim=-1)[..., :-1]
+    else:
+        pr = torch.softmax(s, dim=-1)
     if observe is not None:
         observe(pr)
     return torch.einsum("htc,chd->thd", pr, Vx.float())

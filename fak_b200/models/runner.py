@@ -114,6 +114,10 @@ class ModelRunner:
         self.gated_epi = K.EPI_GEGLU if cfg.act == "gelu_tanh" else K.EPI_SWIGLU
         if cfg.sandwich_norms and collectives is not None:
             raise NotImplementedError("sandwich-norm models (Gemma-2) run on one GPU per replica")
+        if cfg.attn_sinks or cfg.attn_out_bias or cfg.moe_bias or cfg.router != "softmax_topk" or cfg.swiglu_alpha:
+            raise NotImplementedError("gpt-oss blocks (attention sinks, biased top-k-then-softmax router and "
+                                      "experts, clamped OAI gate) run on the fp32 reference model "
+                                      "(models.reference.ReferenceModel); the device kernels do not have them")
         self.act_d = K.ActQ(B, d, dev)
         self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
