@@ -65,6 +65,20 @@ class ModelConfig:
     moe_bias: bool = False
     swiglu_alpha: float = 0.0
     swiglu_limit: float = 0.0
+    # Qwen3.5 hybrid blocks: the layers in ``linear_layers`` mix tokens with a gated delta rule
+    # (Gated DeltaNet: causal depthwise conv of width ``gdn_conv``, ``gdn_k_heads`` key heads of
+    # ``gdn_k_dim``, ``gdn_v_heads`` value heads of ``gdn_v_dim``, a decayed key-value state per
+    # head) instead of softmax attention; full-attention layers gate their output per channel with
+    # sigmoid(gate) from a doubled q projection (``attn_out_gate``) and rotate only the first
+    # ``rotary_dim`` dims of each head (0 = all)
+    linear_layers: tuple | None = None
+    gdn_conv: int = 4
+    gdn_k_heads: int = 0
+    gdn_v_heads: int = 0
+    gdn_k_dim: int = 0
+    gdn_v_dim: int = 0
+    attn_out_gate: bool = False
+    rotary_dim: int = 0
     bos_token_id: int = 1
     eos_token_id: int = 2
     name: str = ""
@@ -89,6 +103,13 @@ class ModelConfig:
         if isinstance(self.rope_scaling, dict):
             items = ((k, tuple(v) if isinstance(v, list) else v) for k, v in self.rope_scaling.items())
             object.__setattr__(self, "rope_scaling", tuple(sorted(items)) or None)
+
+    def is_linear(self, i: int) -> bool:
+        return self.linear_layers is not None and i in self.linear_layers
+
+    @property
+    def rope_dim(self) -> int:
+        return self.rotary_dim or self.head_dim
 
     def layer_window(self, i: int) -> int:
         if self.sliding_window <= 0:

@@ -78,7 +78,14 @@ def write_safetensors(path: str, tensors: dict[str, torch.Tensor], metadata: dic
 
 def config_from_hf(hf: dict) -> ModelConfig:
     arch_name = (hf.get("architectures") or [hf.get("model_type", "")])[0].lower()
-    if "gemma2" in arch_name or hf.get("model_type") == "gemma2":
+    if isinstance(hf.get("text_config"), dict):   # multimodal wrapper: the text decoder's config
+        hf = {**hf["text_config"], "architectures": hf.get("architectures")}
+    mt = str(hf.get("model_type") or "")
+    if "qwen3_5" in arch_name or mt.startswith("qwen3_5"):
+        if "moe" in arch_name or "moe" in mt:
+            raise ValueError("Qwen3.5-MoE is not supported (the dense Qwen3.5 hybrid is)")
+        arch = "qwen35"
+    elif "gemma2" in arch_name or hf.get("model_type") == "gemma2":
         arch = "gemma2"
     elif "gptoss" in arch_name or hf.get("model_type") == "gpt_oss":
         arch = "gptoss"
@@ -102,7 +109,7 @@ def config_from_hf(hf: dict) -> ModelConfig:
         rms_eps=float(hf.get("rms_norm_eps", 1e-6)), rope_theta=theta,
         tie_embeddings=bool(hf.get("tie_word_embeddings", False)),
         qkv_bias=arch == "qwen2" or (arch == "gptoss" and bool(hf.get("attention_bias", True))),
-        qk_norm=arch in ("qwen3", "qwen3moe"),
+        qk_norm=arch in ("qwen3", "qwen3moe", "qwen35"),
         **(_gptoss_fields(hf) if arch == "gptoss" else {
             "n_experts": int(hf.get("num_experts", 0)) if arch == "qwen3moe" else 0,
             "n_experts_used": int(hf.get("num_experts_per_tok", 0)) if arch == "qwen3moe" else 0,
@@ -111,6 +118,7 @@ def config_from_hf(hf: dict) -> ModelConfig:
         max_context=int(hf.get("max_position_embeddings", 32768)),
         rope_scaling=_hf_rope_scaling(rp, hf),
         **(_gemma_fields(hf) if arch == "gemma2" else {}),
+        **(_qwen35_fields(hf, rp) if arch == "qwen35" else {}),
         **_hf_sliding_window(hf, int(hf["num_hidden_layers"])),
         bos_token_id=int(hf.get("bos_token_id") or 1), eos_token_id=int(hf.get("eos_token_id") or 2),
         name=str(hf.get("_name_or_path", arch_name)),
@@ -126,6 +134,19 @@ def _gemma_fields(hf: dict) -> dict:
             "final_softcap": float(hf.get("final_logit_softcapping") or 0.0),
             "sandwich_norms": True, "embed_scale": float(hf["hidden_size"]) ** 0.5,
             "attn_scale": float(hf.get("query_pre_attn_scalar") or hf.get("head_dim") or 256) ** -0.5}
+
+
+def _qwen35_fields(hf: dict, rp: dict) -> dict:
+    """Qwen3.5 hybrid: "linear_attention" layers run Gated DeltaNet; full-attention layers have a
+    sigmoid output gate and rotate partial_rotary_factor of each head."""
+    types = hf.get("layer_types") or []
+    hd = int(hf.get("head_dim") or hf["hidden_size"] // hf["num_attention_heads"])
+    prf = float(rp.get("partial_rotary_factor") or hf.get("partial_rotary_factor") or 1.0)
+    return {"linear_layers": tuple(i for i, t in enumerate(types) if t == "linear_attention"),
+            "gdn_conv": int(hf.get("linear_conv_kernel_dim", 4)),
+            "gdn_k_heads": int(hf["linear_num_key_heads"]), "gdn_v_heads": int(hf["linear_num_value_heads"]),
+            "gdn_k_dim": int(hf["linear_key_head_dim"]), "gdn_v_dim": int(hf["linear_value_head_dim"]),
+            "attn_out_gate": True, "rotary_dim": int(hd * prf)}
 
 
 def _gptoss_fields(hf: dict) -> dict:
@@ -181,6 +202,12 @@ _LAYER = {
     # gpt-oss
     "self_attn.sinks": "attn_sinks.weight", "self_attn.o_proj.bias": "attn_output.bias",
     "mlp.router.weight": "ffn_gate_inp.weight", "mlp.router.bias": "ffn_gate_inp.bias",
+    # Qwen3.5 Gated DeltaNet layers
+    "linear_attn.in_proj_qkv.weight": "ssm_in_qkv.weight", "linear_attn.in_proj_z.weight": "ssm_in_z.weight",
+    "linear_attn.in_proj_b.weight": "ssm_in_b.weight", "linear_attn.in_proj_a.weight": "ssm_in_a.weight",
+    "linear_attn.conv1d.weight": "ssm_conv1d.weight", "linear_attn.dt_bias": "ssm_dt.bias",
+    "linear_attn.A_log": "ssm_a", "linear_attn.norm.weight": "ssm_norm.weight",
+    "linear_attn.out_proj.weight": "ssm_out.weight",
 }
 # gpt-oss experts: all experts of a layer in one tensor; gate and up rows interleaved (gate even)
 _FUSED_EXPERTS = re.compile(r"model\.layers\.(\d+)\.mlp\.experts\.(gate_up_proj|down_proj)(_blocks|_scales|_bias)?")
@@ -303,9 +330,13 @@ def hf_source(model_dir: str) -> tuple[ModelConfig, Callable, Callable[[], None]
                 continue
             g = gguf_name(n, cfg.arch)
             if g is not None:
-                if cfg.arch == "gemma2" and g.endswith("norm.weight"):   # Gemma scales by (1 + w)
+                if g.endswith("norm.weight") and (cfg.arch == "gemma2" or (
+                        cfg.arch == "qwen35" and not g.endswith("ssm_norm.weight"))):   # scaled by (1 + w)
                     arr = _to_f32(dt, np.asarray(arr)) + np.float32(1.0)
                     dt = "F32"
+                if g.endswith("ssm_conv1d.weight"):   # [C, 1, K] -> [C, K]
+                    shape = (shape[0], shape[-1])
+                    arr = np.asarray(arr).reshape(shape)
                 table[g] = (dt, shape, arr)
     # quantized layers: decoded on first use; experts (one triple per expert) stacked
     qlayers: dict[str, list[dict]] = {}
@@ -408,6 +439,12 @@ def load_reference_tensors_hf(model_dir: str) -> tuple[ModelConfig, dict[str, to
     names = ["token_embd.weight", "output_norm.weight"] + ([] if cfg.tie_embeddings else ["output.weight"])
     for i in range(cfg.n_layers):
         p = f"blk.{i}."
+        if cfg.is_linear(i):
+            names += [p + n for n in ("attn_norm.weight", "ffn_norm.weight", "ssm_in_qkv.weight", "ssm_in_z.weight",
+                                      "ssm_in_b.weight", "ssm_in_a.weight", "ssm_conv1d.weight", "ssm_dt.bias",
+                                      "ssm_a", "ssm_norm.weight", "ssm_out.weight", "ffn_gate.weight",
+                                      "ffn_up.weight", "ffn_down.weight")]
+            continue
         names += [p + n for n in ("attn_norm.weight", "ffn_norm.weight", "attn_q.weight", "attn_k.weight",
                                   "attn_v.weight", "attn_output.weight")]
         if cfg.qkv_bias:

@@ -12,6 +12,10 @@ is tested against it.  Semantics kept identical to the reference:
 * MoE router: softmax over all experts, then top-k, renormalised when
   ``norm_topk_prob`` (internal/model/moe.go:279-311).
 * Causal attention with GQA head groups.
+* Qwen3.5 hybrid blocks: Gated DeltaNet token mixing on the linear layers (causal depthwise conv
+  + SiLU, L2-normalised q/k, per-head decay exp(g) and write strength beta, the delta-rule state
+  update S <- exp(g) S + k (beta (v - S^T k))^T, gated RMSNorm of the read-out), sigmoid output
+  gate and partial rotary on the full-attention layers (internal/model/qwen35.go:32-561).
 * gpt-oss blocks: a per-head sink logit that joins every softmax and is then dropped
   (internal/model/arch.go:304-333, softmaxDropSinkInPlace), output-projection bias, a biased
   top-k-then-softmax router, biased experts and the clamped OAI gate (internal/model/config.go:205-214).
@@ -58,6 +62,24 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     x0, x1 = x[..., :half], x[..., half:]
     c, s = cos[:, None, :], sin[:, None, :]
     return torch.cat([x0 * c - x1 * s, x1 * c + x0 * s], dim=-1)
+
+
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
+
+
+def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                     S: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Token-serial gated delta rule.  q, k [T, H, dk] (q already scaled), v [T, H, dv], g, beta
+    [T, H], S [H, dk, dv] the state before the first token.  Returns (out [T, H, dv], final S)."""
+    out = torch.empty(q.shape[0], q.shape[1], v.shape[-1], dtype=torch.float32, device=q.device)
+    for t in range(q.shape[0]):
+        S = S * torch.exp(g[t])[:, None, None]
+        mem = torch.einsum("hkv,hk->hv", S, k[t])
+        delta = (v[t] - mem) * beta[t][:, None]
+        S = S + k[t][:, :, None] * delta[:, None, :]
+        out[t] = torch.einsum("hkv,hk->hv", S, q[t])
+    return out, S
 
 
 def oai_gate(g: torch.Tensor, u: torch.Tensor, alpha: float, limit: float) -> torch.Tensor:
@@ -153,6 +175,33 @@ class ReferenceModel:
                 out[t] += wts[t, j] * y
         return out
 
+    def _gdn(self, i: int, h: torch.Tensor, state) -> tuple[torch.Tensor, tuple]:
+        """Gated DeltaNet token mixing of layer i over h [T, d].  ``state`` = (the last gdn_conv - 1
+        conv inputs [gdn_conv - 1, C], the delta-rule state [v heads, dk, dv]) or None at position 0."""
+        cfg, p = self.cfg, f"blk.{i}."
+        T = h.shape[0]
+        Hk, Hv, dk, dv, Kc = cfg.gdn_k_heads, cfg.gdn_v_heads, cfg.gdn_k_dim, cfg.gdn_v_dim, cfg.gdn_conv
+        mixed = self.mm(h, p + "ssm_in_qkv.weight")                    # [T, C]
+        C = mixed.shape[1]
+        if state is None:
+            state = (torch.zeros(Kc - 1, C, device=h.device), torch.zeros(Hv, dk, dv, device=h.device))
+        xin = torch.cat([state[0], mixed])                               # [Kc - 1 + T, C]
+        w = self.w(p + "ssm_conv1d.weight")                              # [C, Kc]
+        conv = sum(xin[k:k + T] * w[:, k] for k in range(Kc))
+        mixed = torch.nn.functional.silu(conv)
+        q, k, v = torch.split(mixed, [Hk * dk, Hk * dk, Hv * dv], dim=-1)
+        q, k, v = q.reshape(T, Hk, dk), k.reshape(T, Hk, dk), v.reshape(T, Hv, dv)
+        if Hv > Hk:
+            q, k = q.repeat_interleave(Hv // Hk, dim=1), k.repeat_interleave(Hv // Hk, dim=1)
+        q, k = l2norm(q) * dk ** -0.5, l2norm(k)
+        beta = torch.sigmoid(self.mm(h, p + "ssm_in_b.weight"))
+        g = -torch.exp(self.w(p + "ssm_a")) * torch.nn.functional.softplus(
+            self.mm(h, p + "ssm_in_a.weight") + self.w(p + "ssm_dt.bias"))
+        o, S = gated_delta_rule(q, k, v, g, beta, state[1])
+        z = self.mm(h, p + "ssm_in_z.weight").view(T, Hv, dv)
+        o = rmsnorm(o, self.w(p + "ssm_norm.weight"), cfg.rms_eps) * torch.nn.functional.silu(z)
+        return self.mm(o.reshape(T, Hv * dv), p + "ssm_out.weight"), (xin[-(Kc - 1):], S)
+
     def forward(self, ids: torch.Tensor, start_pos: int = 0,
                 kv: list[tuple[torch.Tensor, torch.Tensor]] | None = None,
                 hidden_only: bool = False) -> torch.Tensor:
@@ -170,12 +219,34 @@ class ReferenceModel:
         cfg = self.cfg
         T = x.shape[0]
         pos = torch.arange(start_pos, start_pos + T, device=self.device)
-        cos, sin = rope_cos_sin(pos, cfg.head_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_context)
-        H, Hk, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        cos, sin = rope_cos_sin(pos, cfg.rope_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_context)
+        H, Hk, D, rd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.rope_dim
+
+        def rope(t):
+            return apply_rope(t, cos, sin) if rd == D else torch.cat([apply_rope(t[..., :rd], cos, sin), t[..., rd:]], -1)
+
         for i in range(l0, l1):
             p = f"blk.{i}."
             h = rmsnorm(x, self.w(p + "attn_norm.weight"), cfg.rms_eps)
+            if cfg.is_linear(i):
+                j = i - l0
+                state = kv[j] if kv is not None and len(kv) > j else None
+                o, state = self._gdn(i, h, state)
+                if kv is not None:
+                    if len(kv) <= j:
+                        kv.append(state)
+                    else:
+                        kv[j] = state
+                x = x + o
+                x = x + self._ffn(i, rmsnorm(x, self.w(p + "ffn_norm.weight"), cfg.rms_eps))
+                if self.taps is not None:
+                    self.taps[i] = x.detach().clone()
+                continue
             q = self.mm(h, p + "attn_q.weight")
+            gate = None
+            if cfg.attn_out_gate:   # per head: D query dims, then D gate dims
+                qg = q.view(T, H, 2 * D)
+                q, gate = qg[..., :D].reshape(T, H * D), qg[..., D:].reshape(T, H * D)
             k = self.mm(h, p + "attn_k.weight")
             v = self.mm(h, p + "attn_v.weight")
             if cfg.qkv_bias:
@@ -188,8 +259,8 @@ class ReferenceModel:
             if cfg.qk_norm:
                 q = rmsnorm(q, self.w(p + "attn_q_norm.weight"), cfg.rms_eps)
                 k = rmsnorm(k, self.w(p + "attn_k_norm.weight"), cfg.rms_eps)
-            q = apply_rope(q, cos, sin)
-            k = apply_rope(k, cos, sin)
+            q = rope(q)
+            k = rope(k)
             j = i - l0
             if kv is not None:
                 if len(kv) <= j:
@@ -203,7 +274,10 @@ class ReferenceModel:
                           None if self.attn_observer is None else (lambda pr, i=i: self.attn_observer(i, pr)),
                           scale=cfg.attn_scale, softcap_=cfg.attn_softcap,
                           sinks=self.w(p + "attn_sinks.weight") if cfg.attn_sinks else None)
-            o = self.mm(a.reshape(T, H * D), p + "attn_output.weight")
+            a = a.reshape(T, H * D)
+            if gate is not None:
+                a = a * torch.sigmoid(gate)
+            o = self.mm(a, p + "attn_output.weight")
             if cfg.attn_out_bias:
                 o = o + self.w(p + "attn_output.bias")
             if cfg.sandwich_norms:

@@ -118,6 +118,10 @@ class ModelRunner:
             raise NotImplementedError("gpt-oss blocks (attention sinks, biased top-k-then-softmax router and "
                                       "experts, clamped OAI gate) run on the fp32 reference model "
                                       "(models.reference.ReferenceModel); the device kernels do not have them")
+        if cfg.linear_layers or cfg.attn_out_gate or (cfg.rotary_dim and cfg.rotary_dim != cfg.head_dim):
+            raise NotImplementedError("Qwen3.5 hybrid blocks (Gated DeltaNet layers, gated partial-rotary "
+                                      "attention) run on the fp32 reference model "
+                                      "(models.reference.ReferenceModel); the device kernels do not have them")
         self.act_d = K.ActQ(B, d, dev)
         self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
