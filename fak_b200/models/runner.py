@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import dataclasses
 import math
+import os
 
 import torch
 
@@ -140,10 +141,13 @@ class ModelRunner:
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.max_split = 64
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
+        self.n_split = int(os.environ.get("FAK_DEC_SPLITS", "0")) or 16
+        if not 1 <= self.n_split <= self.max_split:
+            raise ValueError(f"decode attention splits must be in [1, {self.max_split}]")
         # cascade attention: prefix splits of the shared pages (about 2.6 CTAs per SM at 4 KV heads)
         self.prefix_splits = max(16, min(128, (5 * n_sm) // (2 * max(1, self.Hkv))))
         b_casc = min(B, 64 // max(1, self.Hq // max(1, self.Hkv)))   # lanes a cascade step can hold
-        slots = max(B * self.max_split, b_casc * (16 + self.prefix_splits))
+        slots = max(B * self.max_split, b_casc * (self.n_split + self.prefix_splits))
         self.attn_ws = torch.zeros(slots * self.Hq * (self.D + 2), dtype=torch.float32, device=dev)
         self.attn_tickets = torch.zeros(B * self.Hkv, dtype=torch.int32, device=dev)  # split-merge tickets
         # cascade attention: pages shared by every lane of the step (a radix-shared prefix) are
@@ -166,9 +170,12 @@ class ModelRunner:
         """Context splits of the decode attention.  Independent of B on purpose: a sequence's
         attention then reduces in the same order whatever batch it runs in, so batched decode
         is bit-identical to serial decode.  The kernel spreads the live pages evenly over the
-        splits, so short contexts just leave some splits empty.  16 measured best across batch 1-5
-        at 2K-9K contexts on B200 (8 is faster at batch 5 but leaves batch 1 with 32 CTAs)."""
-        return 16
+        splits, so short contexts just leave some splits empty.  16 (``FAK_DEC_SPLITS`` overrides):
+        with 3 resident CTAs per SM, 22 splits fill one wave at 5 lanes x 4 KV heads and measured
+        faster on the attention alone (20.1 against 21.4 us at 5 x 9K tokens with an 8K shared
+        prefix), but the whole decode step at 5 x 9K unshared tokens ran 2% slower with 22 on the
+        same box (3.17 against 3.11 ms), so 16 stays."""
+        return self.n_split
 
     def cascade_ok(self, B: int) -> bool:
         """Cascade attention can run for a B-lane step (its prefix kernel holds <= 64 query rows)."""
