@@ -50,15 +50,28 @@ def build_model_backend(args):
         from .models.reference import ReferenceModel
         from .serve import ReferenceBackend
         if hf:
-            from .models.hf import load_reference_tensors_hf
-            cfg, tensors = load_reference_tensors_hf(hf)
-            ref = ReferenceModel(cfg, tensors)
+            import json
+            with open(os.path.join(hf, "config.json")) as f:
+                mt = str(json.load(f).get("model_type", ""))
+            if mt == "glm_moe_dsa" or mt.startswith("gemma4"):   # whole-sequence models
+                from .serve.backend import CachelessModel
+                if mt == "glm_moe_dsa":
+                    from .models.glm_dsa import GlmDsaReference as whole
+                else:
+                    from .models.gemma4 import Gemma4Reference as whole
+                ref = CachelessModel(whole.from_hf(hf))
+            else:
+                from .models.hf import load_reference_tensors_hf
+                cfg, tensors = load_reference_tensors_hf(hf)
+                ref = ReferenceModel(cfg, tensors)
             tok = Tokenizer.from_tokenizer_json(os.path.join(hf, "tokenizer.json"))
         elif args.gguf:
             ref = ReferenceModel.from_gguf(args.gguf)
             tok = Tokenizer.from_gguf_metadata(open_gguf(args.gguf).metadata)
         else:
             raise SystemExit("--cpu needs --gguf or --hf")
+        if args.lora and not isinstance(ref, ReferenceModel):
+            raise SystemExit("--lora needs a model that runs on the incremental reference forward")
         if args.lora:   # applied dynamically after each patched projection
             from .models.lora import LoRASet, load_peft_adapter
             ls = LoRASet()

@@ -71,6 +71,25 @@ class EngineBackend:
         self._thread.join(timeout=5)
 
 
+class CachelessModel:
+    """Adapts a whole-sequence model (``forward(ids) -> logits``, e.g. GlmDsaReference or
+    Gemma4Reference) to the incremental ``forward(ids, start_pos, kv)`` the reference backend
+    calls: ``kv`` keeps the token history and every call re-runs the full sequence, returning the
+    logits of the new tokens (quadratic in length; a correctness path, not a fast one)."""
+
+    def __init__(self, model):
+        self.model = model
+
+    def forward(self, ids, start_pos: int = 0, kv: list | None = None):
+        import torch
+        ids = torch.as_tensor(ids, dtype=torch.long).reshape(-1)
+        hist = kv if kv is not None else []
+        if len(hist) != start_pos:
+            raise ValueError(f"history holds {len(hist)} tokens, call starts at {start_pos}")
+        hist.extend(int(t) for t in ids)
+        return self.model.forward(torch.tensor(hist))[-ids.numel():]
+
+
 class ReferenceBackend:
     def __init__(self, model, tokenizer, name: str = "fak-b200-reference"):
         import torch  # noqa: F401

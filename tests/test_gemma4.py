@@ -46,3 +46,30 @@ def test_gemma4_matches_transformers(tmp_path, k_eq_v, softcap):
         want = m(ids[None]).logits[0]
     got = ref.forward(ids)
     assert torch.allclose(got, want, atol=3e-4, rtol=1e-4), (got - want).abs().max()
+
+
+def test_cacheless_adapter_serves_a_whole_sequence_model():
+    """The reference backend drives whole-sequence models through CachelessModel: greedy tokens
+    equal the argmax chain of full forwards over the growing sequence."""
+    from fak_b200.engine.sampling import SamplingParams
+    from fak_b200.serve.backend import CachelessModel, ReferenceBackend
+
+    class Whole:
+        V = 37
+
+        def forward(self, ids):
+            ids = torch.as_tensor(ids)
+            cs = torch.cumsum(ids * torch.arange(1, ids.numel() + 1), 0)
+            return torch.nn.functional.one_hot((cs * 7 + 3) % self.V, self.V).float()
+
+    m = Whole()
+    be = ReferenceBackend(CachelessModel(m), tokenizer=None)
+    got = list(be.generate([5, 11, 2], 6, SamplingParams()))
+    seq, want = [5, 11, 2], []
+    for _ in range(6):
+        t = int(m.forward(seq)[-1].argmax())
+        want.append(t)
+        seq.append(t)
+    assert got == want
+    with pytest.raises(ValueError):
+        CachelessModel(m).forward(torch.tensor([1]), 3, [])
