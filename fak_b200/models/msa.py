@@ -16,8 +16,13 @@ Everything here is batched over queries as dense masks (``[Tq, n_blocks]``, ``[T
 as a handful of tensor ops on either device.  Like the reference, this covers the selection and the
 sparse attention; the learned indexer projections of a real checkpoint are not wired into a model.
 
+Two selection rules exist: ``select_blocks`` is the union above; ``select_blocks_fixed`` is the
+fixed-count rule of the MiniMax-M3 forward (local blocks forced in, displacing the lowest-scored
+ones), with the block scores max-pooled over the indexer's heads (``pooled_over_heads``).
+
 Reference: internal/model/msa_index.go (msaBlockScores :37-68, msaSelectBlocks :70-118,
-msaSelectedKeyPositions :120-160, msaAttention :162-192).
+msaSelectedKeyPositions :120-160, msaAttention :162-192); internal/model/minimax_m3.go
+(minimaxIndexerSelectBlocks :223-263, minimaxSelectBlocks :265-298).
 """
 from __future__ import annotations
 
@@ -63,6 +68,35 @@ def select_blocks(pooled: torch.Tensor, topk: int, local: int) -> torch.Tensor:
         top.scatter_(1, order, True)
         sel |= top & cand
     return sel
+
+
+def select_blocks_fixed(pooled: torch.Tensor, q_pos: torch.Tensor, block: int, topk: int, local: int
+                        ) -> torch.Tensor:
+    """The fixed-count selection of the MiniMax-M3 forward: the ``local`` blocks ending at the
+    query's own block are forced to +inf, then exactly min(topk, candidates) blocks are kept by
+    score (ties: lower id), so a forced local block displaces the lowest-scored one instead of
+    adding to the set.  pooled [Tq, nb] -> bool [Tq, nb]."""
+    if topk < 0 or local < 0:
+        raise ValueError("topk and local must be non-negative")
+    cand = pooled > -math.inf
+    nb = pooled.shape[1]
+    ids = torch.arange(nb, device=pooled.device)[None, :]
+    qb = (q_pos // block)[:, None]
+    forced = cand & (ids <= qb) & (ids > qb - local)
+    key = torch.where(forced, torch.full_like(pooled, -math.inf), -pooled)
+    key = torch.where(cand, key, torch.full_like(pooled, math.inf))
+    order = torch.sort(key, dim=1, stable=True).indices
+    n = cand.sum(1).clamp(max=topk)
+    rank = torch.empty_like(order)
+    rank.scatter_(1, order, torch.arange(nb, device=pooled.device).expand_as(order))
+    return cand & (rank < n[:, None])
+
+
+def pooled_over_heads(scores: torch.Tensor, key_pos: torch.Tensor, q_pos: torch.Tensor, block: int) -> torch.Tensor:
+    """Block scores of a multi-head indexer: per-head scores [Tq, heads, Tk] max-pooled over each
+    block and then over the heads -> [Tq, nb] (one selection shared by every attention head)."""
+    per = [block_scores(scores[:, h], key_pos, q_pos, block) for h in range(scores.shape[1])]
+    return torch.stack(per, 0).amax(0)
 
 
 def key_mask(sel: torch.Tensor, key_pos: torch.Tensor, q_pos: torch.Tensor, block: int) -> torch.Tensor:

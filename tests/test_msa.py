@@ -76,3 +76,31 @@ def test_msa_attention_matches_the_per_query_rules(block, topk, local):
     if local:
         own = (key_pos // block) == (q_pos[:, None] // block)
         assert bool((mask | ~(own & (key_pos[None, :] <= q_pos[:, None]))).all())
+
+
+def _fixed_loop(pooled, q_pos, block, topk, local):
+    out = []
+    for t in range(pooled.shape[0]):
+        qb = int(q_pos[t]) // block
+        cands = [(b, float(pooled[t, b])) for b in range(pooled.shape[1]) if pooled[t, b] > -math.inf]
+        cands = [(b, math.inf if local and qb - local < b <= qb else s) for b, s in cands]
+        cands.sort(key=lambda c: (-c[1], c[0]))
+        out.append(sorted(b for b, _ in cands[:topk]))
+    return out
+
+
+@pytest.mark.parametrize("topk,local", [(2, 1), (3, 2), (1, 3), (5, 0)])
+def test_fixed_count_selection_displaces_instead_of_adding(topk, local):
+    from fak_b200.models.msa import pooled_over_heads, select_blocks_fixed
+    torch.manual_seed(topk * 10 + local)
+    Tk, block = 40, 4
+    key_pos = torch.arange(Tk)
+    q_pos = torch.tensor([3, 9, 18, 27, 39])
+    scores = torch.randn(5, 3, Tk)                       # 3 index heads
+    pooled = pooled_over_heads(scores, key_pos, q_pos, block)
+    want = torch.stack([block_scores(scores[:, h], key_pos, q_pos, block) for h in range(3)]).amax(0)
+    assert torch.equal(pooled, want)
+    sel = select_blocks_fixed(pooled, q_pos, block, topk, local)
+    assert [torch.nonzero(r).flatten().tolist() for r in sel] == _fixed_loop(pooled, q_pos, block, topk, local)
+    # the count is fixed: min(topk, causal blocks) whatever the local window
+    assert sel.sum(1).tolist() == [min(topk, int(q) // block + 1) for q in q_pos]
