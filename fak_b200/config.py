@@ -111,6 +111,16 @@ class ModelConfig:
     def rope_dim(self) -> int:
         return self.rotary_dim or self.head_dim
 
+    def device_gap(self) -> str | None:
+        """Why the device engine cannot run this config (None when it can).  Such models run on the
+        fp32 reference model (``models.reference.ReferenceModel``)."""
+        if self.attn_sinks or self.attn_out_bias or self.moe_bias or self.router != "softmax_topk" or self.swiglu_alpha:
+            return ("gpt-oss blocks (attention sinks, biased top-k-then-softmax router and experts, clamped OAI "
+                    "gate) have no device kernels")
+        if self.linear_layers or self.attn_out_gate or (self.rotary_dim and self.rotary_dim != self.head_dim):
+            return "Qwen3.5 hybrid blocks (Gated DeltaNet layers, gated partial-rotary attention) have no device kernels"
+        return None
+
     def layer_window(self, i: int) -> int:
         if self.sliding_window <= 0:
             return 0

@@ -138,6 +138,13 @@ class Engine:
             lora = s
         return merged_source(source, lora)
 
+    @staticmethod
+    def _check_device(cfg: ModelConfig) -> None:
+        """Refuse, before any weight is loaded, a model the device kernels cannot run."""
+        gap = cfg.device_gap()
+        if gap:
+            raise NotImplementedError(f"{gap}; run it on the fp32 reference model (serve --cpu)")
+
     @classmethod
     def from_gguf(cls, path: str, ecfg: EngineConfig | None = None, device="cuda", tp_group=None, lora=None,
                   **kw) -> "Engine":
@@ -153,13 +160,16 @@ class Engine:
         AWQ / GPTQ int4 layers run as G4 blocks."""
         from ..models.hf import hf_source
         r, n = cls._tp(tp_group)
-        w = load_weights(cls._with_lora(hf_source(model_dir), lora), device, tp_rank=r, tp_size=n,
+        src = hf_source(model_dir)
+        cls._check_device(src[0])
+        w = load_weights(cls._with_lora(src, lora), device, tp_rank=r, tp_size=n,
                          prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 
     @classmethod
     def synthetic(cls, cfg: ModelConfig, mix: str = "q4_k_m", seed: int = 0, ecfg: EngineConfig | None = None,
                   device="cuda", tp_group=None, std: float = 0.02, **kw) -> "Engine":
+        cls._check_device(cfg)
         r, n = cls._tp(tp_group)
         w = load_weights(synthetic_source(cfg, mix, seed, std=std, device=str(device)), device, tp_rank=r, tp_size=n,
                          prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)

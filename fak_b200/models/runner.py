@@ -115,14 +115,9 @@ class ModelRunner:
         self.gated_epi = K.EPI_GEGLU if cfg.act == "gelu_tanh" else K.EPI_SWIGLU
         if cfg.sandwich_norms and collectives is not None:
             raise NotImplementedError("sandwich-norm models (Gemma-2) run on one GPU per replica")
-        if cfg.attn_sinks or cfg.attn_out_bias or cfg.moe_bias or cfg.router != "softmax_topk" or cfg.swiglu_alpha:
-            raise NotImplementedError("gpt-oss blocks (attention sinks, biased top-k-then-softmax router and "
-                                      "experts, clamped OAI gate) run on the fp32 reference model "
-                                      "(models.reference.ReferenceModel); the device kernels do not have them")
-        if cfg.linear_layers or cfg.attn_out_gate or (cfg.rotary_dim and cfg.rotary_dim != cfg.head_dim):
-            raise NotImplementedError("Qwen3.5 hybrid blocks (Gated DeltaNet layers, gated partial-rotary "
-                                      "attention) run on the fp32 reference model "
-                                      "(models.reference.ReferenceModel); the device kernels do not have them")
+        gap = cfg.device_gap()
+        if gap:
+            raise NotImplementedError(f"{gap}; run it on the fp32 reference model (models.reference.ReferenceModel)")
         self.act_d = K.ActQ(B, d, dev)
         self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)

@@ -110,3 +110,14 @@ def test_sink_softmax_matches_the_explicit_form():
             e = torch.exp(s - s.max())
             den = e.sum() + torch.exp(sinks[h] - s.max())
             assert torch.allclose(got[t, h], (e[:, None] * Vx[: 5 + t, h]).sum(0) / den, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["tiny-gptoss", "gpt-oss-20b"])
+def test_device_engine_refuses_gptoss_before_loading(name):
+    from fak_b200.config import preset
+    from fak_b200.engine import Engine
+    cfg = preset(name)
+    assert "gpt-oss" in cfg.device_gap()
+    with pytest.raises(NotImplementedError, match="reference model"):
+        Engine.synthetic(cfg, device="cpu")
+    assert preset("qwen2.5-7b").device_gap() is None
