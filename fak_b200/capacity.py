@@ -119,3 +119,42 @@ def max_context(cfg: ModelConfig, budget_bytes: int, mix: str = "q4_k_m", batch:
     per_token = kv_bytes_per_token(cfg, tp) * batch
     ctx = (free // per_token) // PAGE_TOKENS * PAGE_TOKENS
     return int(min(ctx, cfg.max_context))
+
+
+@dataclasses.dataclass(frozen=True)
+class KVResidencySplit:
+    """Placement of a KV cache over the device (hot: the span decode reads every step) and host
+    memory (cold: the least recently attended span, spilled instead of evicted)."""
+    hot_tokens: int
+    cold_tokens: int
+    bytes_per_token: int
+
+    @property
+    def tokens(self) -> int:
+        return self.hot_tokens + self.cold_tokens
+
+    @property
+    def hot_bytes(self) -> int:
+        return self.hot_tokens * self.bytes_per_token
+
+    @property
+    def cold_bytes(self) -> int:
+        return self.cold_tokens * self.bytes_per_token
+
+
+def kv_residency_split(want_tokens: int, bytes_per_token: int, device_free: int, host_free: int,
+                       page_tokens: int = PAGE_TOKENS) -> KVResidencySplit:
+    """How many of ``want_tokens`` stay on the device and how many spill to the host, given the
+    free bytes of each pool.  Hot tokens fill whole pages of the device first; the rest spill to
+    the host up to its room.  Fail-open: a non-positive want or per-token cost gives an empty
+    split, and no host room gives the device-only sizing, so the effective context is never below
+    device-only sizing.
+
+    Reference: internal/compute/kvresidency.go (KVResidencySplit, the hot / cold policy)."""
+    if want_tokens <= 0 or bytes_per_token <= 0:
+        return KVResidencySplit(0, 0, max(0, bytes_per_token))
+    page = page_tokens * bytes_per_token
+    hot = min(want_tokens, max(0, device_free) // page * page_tokens)
+    rest = want_tokens - hot
+    cold = min(rest, max(0, host_free) // bytes_per_token) if rest > 0 else 0
+    return KVResidencySplit(hot, cold, bytes_per_token)

@@ -59,3 +59,19 @@ def test_measured_peaks_file_is_read(tmp_path):
     pk = R.load_peaks(str(f))
     assert pk.hbm_gbs == 6000 and pk.source == "measured"
     assert R.load_peaks(str(tmp_path / "missing.json")).source == "nominal B200"
+
+
+def test_kv_residency_split_spills_cold_tokens_to_the_host():
+    from fak_b200.capacity import PAGE_TOKENS, kv_residency_split
+    bpt = 1000
+    s = kv_residency_split(10_000, bpt, device_free=50 * PAGE_TOKENS * bpt + 999, host_free=10 ** 9)
+    assert s.hot_tokens == 50 * PAGE_TOKENS and s.tokens == 10_000 and s.cold_bytes == s.cold_tokens * bpt
+    # everything fits on the device: nothing spills
+    assert kv_residency_split(100, bpt, 10 ** 9, 10 ** 9).cold_tokens == 0
+    # no host room: device-only sizing, never smaller
+    only = kv_residency_split(10_000, bpt, 20 * PAGE_TOKENS * bpt, 0)
+    assert only.hot_tokens == 20 * PAGE_TOKENS and only.cold_tokens == 0
+    # host room caps the spill
+    assert kv_residency_split(10_000, bpt, 0, 1234 * bpt).cold_tokens == 1234
+    # fail-open on missing geometry
+    assert kv_residency_split(0, bpt, 1, 1).tokens == 0 and kv_residency_split(10, 0, 1, 1).tokens == 0
