@@ -323,6 +323,8 @@ class EngineConfig:
                                         # (a kernel reading memory nobody wrote shows up in its outputs)
     preempt_mode: str = "recompute"     # out of KV pages: "recompute" (radix-assisted) or "swap" to host memory
     swap_space_gb: float = 16.0         # pinned host memory for swapped-out KV pages
+    async_decode: bool = True           # device-resident lane state; tokens read back one step behind
+    p2p_spin_limit: int = 0             # polls before a cross-rank wait gives up (0: kernel default, ~1 s)
 
     ENV_KEYS = {
         "page_size": ("FAK_PAGED_KV_BLOCK_TOKENS", int),
@@ -347,6 +349,8 @@ class EngineConfig:
         "debug_poison": ("FAK_DEBUG_POISON", bool),
         "preempt_mode": ("FAK_PREEMPT_MODE", str),
         "swap_space_gb": ("FAK_SWAP_SPACE_GB", float),
+        "async_decode": ("FAK_ASYNC_DECODE", bool),
+        "p2p_spin_limit": ("FAK_P2P_SPIN_LIMIT", int),
     }
 
     @classmethod

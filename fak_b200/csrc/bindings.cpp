@@ -41,12 +41,14 @@ void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double 
 void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
                         int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
                         torch::Tensor counters, torch::Tensor err, int64_t ctas, c10::optional<torch::Tensor> src2,
-                        int64_t src2_ld, int64_t dst2_off, int64_t dst2_ld, int64_t col2, int64_t ncols2);
+                        int64_t src2_ld, int64_t dst2_off, int64_t dst2_ld, int64_t col2, int64_t ncols2,
+                        int64_t spin_limit);
 void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, int64_t n, int64_t flags_off,
-                       int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas);
+                       int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas,
+                       int64_t spin_limit);
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
                 torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
-                torch::Tensor err);
+                torch::Tensor err, int64_t spin_limit);
 void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor wr, int64_t k, bool norm_topk,
                torch::Tensor ids, torch::Tensor wts);
 void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_t max_chunks, torch::Tensor chunk_expert,
@@ -56,7 +58,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
            int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
-           c10::optional<torch::Tensor> prefetch);
+           c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit);
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device);
 int64_t tgemv_unit_bytes(int64_t qtype);
 void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, torch::Tensor qx,
@@ -69,6 +71,14 @@ void moe_combine(torch::Tensor out, torch::Tensor ids, torch::Tensor wts, int64_
                  torch::Tensor x);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias, int64_t epi,
                c10::optional<torch::Tensor> err);
+void decode_advance(torch::Tensor next, torch::Tensor ids, torch::Tensor pos, torch::Tensor slot, torch::Tensor ctx,
+                    torch::Tensor bt, int64_t B);
+void scatter_i32(torch::Tensor dst, torch::Tensor idx_val, int64_t n);
+std::tuple<int64_t, torch::Tensor> ipc_alloc(int64_t nbytes, int64_t device);
+int64_t ipc_open(torch::Tensor handle, int64_t device);
+void ipc_close(int64_t ptr);
+void ipc_free(int64_t ptr);
+torch::Tensor ipc_view(int64_t ptr, int64_t nbytes, int64_t device);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fak_b200 sm_100a kernels";
@@ -104,9 +114,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("dst_off"), pybind11::arg("dst_ld"), pybind11::arg("col0"), pybind11::arg("ncols"), pybind11::arg("B"),
         pybind11::arg("flags_off"), pybind11::arg("site"), pybind11::arg("me"), pybind11::arg("counters"),
         pybind11::arg("err"), pybind11::arg("ctas"), pybind11::arg("src2") = pybind11::none(), pybind11::arg("src2_ld") = 0,
-        pybind11::arg("dst2_off") = 0, pybind11::arg("dst2_ld") = 0, pybind11::arg("col2") = 0, pybind11::arg("ncols2") = 0);
-  m.def("p2p_allreduce_add", &p2p_allreduce_add);
-  m.def("p2p_argmax", &p2p_argmax);
+        pybind11::arg("dst2_off") = 0, pybind11::arg("dst2_ld") = 0, pybind11::arg("col2") = 0, pybind11::arg("ncols2") = 0,
+        pybind11::arg("spin_limit") = 0);
+  m.def("p2p_allreduce_add", &p2p_allreduce_add, pybind11::arg("peers"), pybind11::arg("part_off"), pybind11::arg("x"),
+        pybind11::arg("n"), pybind11::arg("flags_off"), pybind11::arg("site"), pybind11::arg("me"),
+        pybind11::arg("counters"), pybind11::arg("err"), pybind11::arg("ctas"), pybind11::arg("spin_limit") = 0);
+  m.def("p2p_argmax", &p2p_argmax, pybind11::arg("peers"), pybind11::arg("logits"), pybind11::arg("Vl"),
+        pybind11::arg("v_off"), pybind11::arg("cand_off"), pybind11::arg("out"), pybind11::arg("B"),
+        pybind11::arg("flags_off"), pybind11::arg("site"), pybind11::arg("me"), pybind11::arg("counters"),
+        pybind11::arg("err"), pybind11::arg("spin_limit") = 0);
   m.def("moe_route", &moe_route);
   m.def("moe_group", &moe_group);
   m.def("moe_qmmv", &moe_qmmv);
@@ -122,10 +138,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("epi"), pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
         pybind11::arg("flags") = 0, pybind11::arg("ar_peers") = pybind11::none(), pybind11::arg("ar_me") = 0,
         pybind11::arg("ar_parts_off") = 0, pybind11::arg("ar_flags_off") = 0, pybind11::arg("ar_epochs") = pybind11::none(),
-        pybind11::arg("prefetch") = pybind11::none());
+        pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("ar_spin_limit") = 0);
   m.def("tgemv_workspace", &tgemv_workspace);
   m.def("tgemv_unit_bytes", &tgemv_unit_bytes);
   m.def("moe_tgemv", &moe_tgemv);
+  m.def("decode_advance", &decode_advance, "next step's lane inputs from this step's tokens (device-resident state)");
+  m.def("scatter_i32", &scatter_i32, "dst.flatten()[idx] = val for (idx, val) pairs on the device");
+  m.def("ipc_alloc", &ipc_alloc, "zeroed device buffer + its CUDA IPC handle");
+  m.def("ipc_open", &ipc_open, "map a peer's IPC handle (lazy peer access)");
+  m.def("ipc_close", &ipc_close);
+  m.def("ipc_free", &ipc_free);
+  m.def("ipc_view", &ipc_view, "non-owning uint8 tensor over a device buffer");
   m.def("gemm_bf16", &gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"),
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("epi") = 0, pybind11::arg("err") = pybind11::none());
 }

@@ -87,7 +87,8 @@ FAK_DEV float bf16_bits_lo(uint32_t v) { return __uint_as_float(v << 16); }
 FAK_DEV float bf16_bits_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
 // Device-side error word: kernels never trap; they record a code and return.
-// Codes: 1 = bounded wait expired, 2 = index out of range, 3 = bad argument.
+// Codes: 1 = bounded wait expired, 2 = index out of range, 3 = bad argument, 4 = a peer rank never
+// arrived at a fused all-reduce tile (tgemv epilogue).
 FAK_DEV void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

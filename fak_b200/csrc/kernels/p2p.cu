@@ -11,8 +11,9 @@
 //   flags[s][c][r] >= e for every r.  Epochs come from a per-(site, cta) counter in local
 //   memory, incremented by the kernel itself, so the kernels replay correctly inside CUDA graphs.
 //
-// Every wait is bounded: after kSpinLimit polls the kernel records error code 1 in `err` and
-// continues, so a missing peer produces an error status on the host instead of a hung GPU.
+// Every wait is bounded: after a spin limit (a launch argument, default kSpinLimit polls) the kernel
+// records error code 1 in `err` and continues, so a missing peer produces an error status on the
+// host instead of a hung GPU; a short limit lets a test make the wait run out on purpose.
 // No TMA or multicast loads are used here; peer memory is only touched by ordinary ld/st.
 //
 // Reference counterpart: the NCCL AllReduce/AllGather of internal/compute/cuda_nccl.cu:72-134 and
@@ -41,6 +42,7 @@ FAK_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
 
 struct Peers {
   uint8_t* base[MAX_W];  // symmetric buffer base of every rank
+  uint32_t spin;         // polls of a flag before a wait gives up
 };
 
 // Cross-rank barrier for CTA `cta` at `site`: all threads of the CTA call it; prior writes of the
@@ -64,7 +66,7 @@ FAK_DEV void rank_barrier(const Peers& P, int64_t flags_off, int site, int cta, 
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(P.base[me] + flags_off) + slot + threadIdx.x;
     uint32_t i = 0;
     while (ld_acquire_sys(mine) < epoch) {
-      if (++i > kSpinLimit) {
+      if (++i > P.spin) {
         report_error(err, 1);
         break;
       }
@@ -172,10 +174,12 @@ __global__ void k_p2p_argmax(Peers P, const float* __restrict__ logits, int64_t 
   pdl_launch_dependents();
 }
 
-Peers make_peers(torch::Tensor ptrs) {
+Peers make_peers(torch::Tensor ptrs, int64_t spin_limit) {
   TORCH_CHECK(ptrs.scalar_type() == torch::kInt64 && ptrs.numel() <= MAX_W, "peer pointer table");
+  TORCH_CHECK(spin_limit >= 0 && spin_limit <= 0xffffffffll, "spin limit");
   auto h = ptrs.cpu();
   Peers P{};
+  P.spin = spin_limit > 0 ? (uint32_t)spin_limit : kSpinLimit;
   for (int i = 0; i < ptrs.numel(); i++) P.base[i] = reinterpret_cast<uint8_t*>(h.data_ptr<int64_t>()[i]);
   return P;
 }
@@ -200,7 +204,8 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaLaunchAttribute* attr) {
 void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
                         int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
                         torch::Tensor counters, torch::Tensor err, int64_t ctas, c10::optional<torch::Tensor> src2,
-                        int64_t src2_ld, int64_t dst2_off, int64_t dst2_ld, int64_t col2, int64_t ncols2) {
+                        int64_t src2_ld, int64_t dst2_off, int64_t dst2_ld, int64_t col2, int64_t ncols2,
+                        int64_t spin_limit) {
   const int W = (int)peers.numel();
   auto check = [](int64_t n, int64_t c, int64_t sl, int64_t dl, int64_t off) {
     TORCH_CHECK(n % 16 == 0 && c % 16 == 0 && sl % 16 == 0 && dl % 16 == 0 && off % 16 == 0,
@@ -216,7 +221,7 @@ void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, 
     s1 = AgSeg{(const uint8_t*)src2->data_ptr(), src2_ld, dst2_off, dst2_ld, col2, ncols2};
     nseg = 2;
   }
-  Peers P = make_peers(peers);
+  Peers P = make_peers(peers, spin_limit);
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_allgather_cols, P, s0, s1, nseg, (int)B, flags_off, (int)site,
@@ -224,12 +229,13 @@ void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, 
 }
 
 void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, int64_t n, int64_t flags_off,
-                       int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas) {
+                       int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas,
+                       int64_t spin_limit) {
   const int W = (int)peers.numel();
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.numel() >= n && n % 4 == 0, "x");
   TORCH_CHECK(part_off % 16 == 0, "partials must be 16-byte aligned");
   TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allreduce: 1..64 CTAs");
-  Peers P = make_peers(peers);
+  Peers P = make_peers(peers, spin_limit);
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_allreduce_add, P, part_off, x.data_ptr<float>(), n, flags_off,
@@ -238,11 +244,11 @@ void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, i
 
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
                 torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
-                torch::Tensor err) {
+                torch::Tensor err, int64_t spin_limit) {
   const int W = (int)peers.numel();
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.stride(1) == 1, "logits");
   TORCH_CHECK(B >= 1 && B <= MAX_CTAS, "argmax: batch 1..64");
-  Peers P = make_peers(peers);
+  Peers P = make_peers(peers, spin_limit);
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_cfg(dim3((unsigned)B), dim3(1024), attr);
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_argmax, P, (const float*)logits.data_ptr<float>(),

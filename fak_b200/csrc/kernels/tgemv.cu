@@ -303,13 +303,18 @@ FAK_DEV void epilogue(int tile, const float (&v)[4], int tokb, int lane, int N, 
   }
 }
 
-// Tensor-parallel all-reduce fused into the epilogue (K-split row-parallel layers such as the
-// down projection): the warp that finishes a tile pushes its partial into slot [me][tile] of every
-// rank's symmetric buffer with plain stores, publishes a per-tile epoch flag on every rank (release,
-// system scope), waits (acquire, bounded) for all ranks' flags of that tile, and sums the W slots of
-// its own buffer in rank order -- every rank computes bit-identical values -- before the residual
-// add.  Epochs count launches per tile in local memory, so the kernel replays inside CUDA graphs.
-// No multicast, no TMA from peer memory: peer memory is touched by ordinary stores only.
+// Tensor-parallel all-reduce fused into the epilogue (K-split row-parallel layers: the attention
+// output projection and the down projection): the warp that finishes a tile pushes its partial into
+// slot [parity][me][tile] of every rank's symmetric buffer with plain stores, publishes a per-tile
+// epoch flag on every rank (release, system scope), waits (acquire, bounded) for all ranks' flags of
+// that tile, and sums the W slots of its own buffer in rank order -- every rank computes
+// bit-identical values -- before the residual add.  Epochs count launches per tile in local memory,
+// so the kernel replays inside CUDA graphs; the slots alternate between two halves by epoch parity,
+// so a fast rank's next launch (the next projection sharing the slots) cannot overwrite a partial a
+// slow rank has not summed yet: to reach epoch e + 2 it must pass epoch e + 1, which every rank
+// publishes only after its launch of epoch e finished.  The wait gives up after ``spin`` polls
+// (a launch argument) and records error code 4.  No multicast, no TMA from peer memory: peer memory
+// is touched by ordinary stores only.
 constexpr int AR_MAX_W = 8;
 constexpr uint32_t kArSpinLimit = 1u << 24;
 struct ArPeers {
@@ -317,6 +322,7 @@ struct ArPeers {
   int W, me;
   int64_t parts_off, flags_off;
   uint32_t* epochs;         // local [T]
+  uint32_t spin;            // polls of a flag before the wait gives up
 };
 
 FAK_DEV void ar_st_release(uint32_t* p, uint32_t v) {
@@ -330,17 +336,19 @@ FAK_DEV uint32_t ar_ld_acquire(const uint32_t* p) {
 
 template <int NT>
 FAK_DEV void ar_tile(const ArPeers& ar, int T, int tile, int lane, float (&v)[NT][4], int* err) {
+  uint32_t ep = 0;
+  if (lane == 0) ep = ar.epochs[tile] + 1;
+  ep = __shfl_sync(0xffffffffu, ep, 0);
+  // the half of the slots this epoch uses: [AR_MAX_W][T][<= 4 n8 tiles][32 lanes] float4 each
+  const int64_t half = (int64_t)(ep & 1u) * AR_MAX_W * T * 4 * 32;
   // push this rank's partial of the tile to every rank
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
     const float4 val = make_float4(v[nt][0], v[nt][1], v[nt][2], v[nt][3]);
-    const int64_t slot = (((int64_t)ar.me * T + tile) * NT + nt) * 32 + lane;
+    const int64_t slot = half + (((int64_t)ar.me * T + tile) * NT + nt) * 32 + lane;
     for (int r = 0; r < ar.W; r++) reinterpret_cast<float4*>(ar.base[r] + ar.parts_off)[slot] = val;
   }
   __syncwarp();
-  uint32_t ep = 0;
-  if (lane == 0) ep = ar.epochs[tile] + 1;
-  ep = __shfl_sync(0xffffffffu, ep, 0);
   if (lane < ar.W) {
     __threadfence_system();
     ar_st_release(reinterpret_cast<uint32_t*>(ar.base[lane] + ar.flags_off) + (int64_t)tile * AR_MAX_W + ar.me, ep);
@@ -348,8 +356,8 @@ FAK_DEV void ar_tile(const ArPeers& ar, int T, int tile, int lane, float (&v)[NT
                            (int64_t)tile * AR_MAX_W + lane;
     uint32_t i = 0;
     while (ar_ld_acquire(mine) < ep) {
-      if (++i > kArSpinLimit) {
-        report_error(err, 2);
+      if (++i > ar.spin) {
+        report_error(err, 4);
         break;
       }
     }
@@ -359,7 +367,7 @@ FAK_DEV void ar_tile(const ArPeers& ar, int T, int tile, int lane, float (&v)[NT
   for (int nt = 0; nt < NT; nt++) {
     float s[4] = {0.f, 0.f, 0.f, 0.f};
     for (int r = 0; r < ar.W; r++) {
-      const int64_t slot = (((int64_t)r * T + tile) * NT + nt) * 32 + lane;
+      const int64_t slot = half + (((int64_t)r * T + tile) * NT + nt) * 32 + lane;
       const float4 p = __ldcg(reinterpret_cast<const float4*>(ar.base[ar.me] + ar.parts_off) + slot);
       s[0] += p.x; s[1] += p.y; s[2] += p.z; s[3] += p.w;
     }
@@ -794,7 +802,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
            int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
-           c10::optional<torch::Tensor> prefetch) {
+           c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "tgemv: w cuda uint8");
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
   const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
@@ -811,6 +819,8 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     ar.parts_off = ar_parts_off;
     ar.flags_off = ar_flags_off;
     ar.epochs = reinterpret_cast<uint32_t*>(ar_epochs->data_ptr<int>());
+    TORCH_CHECK(ar_spin_limit >= 0 && ar_spin_limit <= 0xffffffffll, "tgemv: spin limit");
+    ar.spin = ar_spin_limit > 0 ? (uint32_t)ar_spin_limit : kArSpinLimit;
   }
   TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0 || qtype == QT_G4, "tgemv: qtype");
   TORCH_CHECK(K % 64 == 0 && (qtype == QT_Q8_0 || K % 256 == 0), "tgemv: K must be a multiple of 256 (64 for Q8_0)");

@@ -62,6 +62,7 @@ class Request:
     hold_pages: bool = False         # keep the pages at finish (prefill side of a P/D handoff)
     cache_limit: int | None = None   # tokens of this request the radix cache may take (span eviction)
     held_pages: list[int] = dataclasses.field(default_factory=list)
+    inflight: int = 0                # decode steps launched for it whose token is not read back yet
 
     @property
     def ttft(self) -> float | None:
@@ -92,7 +93,8 @@ class Engine:
         if collectives is None and tp_group is not None and weights.tp_size > 1:
             if self.ecfg.fused_collectives:
                 from ..parallel.p2p import P2PTP
-                collectives = P2PTP(tp_group, weights, self.ecfg.max_batch, self.device)
+                collectives = P2PTP(tp_group, weights, self.ecfg.max_batch, self.device,
+                                    spin_limit=self.ecfg.p2p_spin_limit)
             else:
                 from ..parallel.tp import NcclTP
                 collectives = NcclTP(tp_group, weights, self.ecfg.max_batch, self.device)
@@ -116,6 +118,14 @@ class Engine:
         # weight-load phases (seconds): read, convert (quant-on-load), upload, pack (tile layout), dense
         self.stats.update({"load_" + k + "_s": v for k, v in getattr(weights, "load_profile", {}).items()})
         self._graphs_ready = False
+        # device-resident decode loop (_run_decode_async): lanes whose state lives in the runner's
+        # static buffers, in row order; the launched step whose tokens are not read back yet
+        self._lanes: list[Request] = []
+        self._lanes_valid = False
+        self._pending: tuple | None = None
+        self._rb = [torch.zeros(self.ecfg.max_batch + 2, dtype=torch.int32).pin_memory()
+                    for _ in range(2)] if self.device.type == "cuda" else []
+        self._rb_i = 0
 
     # ------------------------------------------------------------------------------------
     @staticmethod
@@ -168,18 +178,23 @@ class Engine:
 
     @classmethod
     def synthetic(cls, cfg: ModelConfig, mix: str = "q4_k_m", seed: int = 0, ecfg: EngineConfig | None = None,
-                  device="cuda", tp_group=None, std: float = 0.02, **kw) -> "Engine":
+                  device="cuda", tp_group=None, std: float = 0.02, repeat_layers: bool = False, **kw) -> "Engine":
+        """Random-init N(0, std) weights of ``cfg`` quantized on the device (``repeat_layers``: every
+        layer shares block 0's weights -- for smoke tests of large architectures)."""
         cls._check_device(cfg)
         r, n = cls._tp(tp_group)
         w = load_weights(synthetic_source(cfg, mix, seed, std=std, device=str(device)), device, tp_rank=r, tp_size=n,
-                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
+                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights, repeat_layers=repeat_layers)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 
     def shutdown(self) -> None:
         """Release CUDA graphs (they may hold collectives) before the process group goes away."""
+        self._drain()
         self.runner._graphs.clear()
         self._graphs_ready = False
         torch.cuda.synchronize(self.device)
+        if self.runner.coll is not None and hasattr(self.runner.coll, "close"):
+            self.runner.coll.close()
 
     def _pages_from_memory(self) -> int:
         """KV pages from the free device memory after the weights; fails closed (FitError) when not
@@ -220,7 +235,7 @@ class Engine:
         return r
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.prefilling or self.running or self.swapped)
+        return bool(self.waiting or self.prefilling or self.running or self.swapped or self._pending)
 
     def _alloc(self, n: int) -> list[int]:
         if n <= 0:
@@ -383,6 +398,8 @@ class Engine:
         only the tokens before the span may enter the radix cache."""
         from ..models.rope import inv_freq
         from ..ops import kernels as K
+        self._drain()
+        self._lanes_valid = False   # pages and positions change under the resident lanes
         if r.finished or r.swap is not None or r in self.waiting or r in self.prefilling:
             raise ValueError("evict_span: the request must be decoding (between steps)")
         if not 0 <= start < end <= r.n_kv:
@@ -424,7 +441,145 @@ class Engine:
                 return False
         return True
 
+    def _async_ok(self) -> bool:
+        return (self.ecfg.async_decode and self._graphs_ready and self.ecfg.spec_k == 0
+                and all(r.sampling.greedy for r in self.running))
+
     def _run_decode(self) -> None:
+        if self.running and self._async_ok():
+            if self._run_decode_async():
+                return
+        self._drain()
+        self._lanes_valid = False    # the synchronous step rewrites the static inputs
+        self._run_decode_sync()
+
+    # ---- device-resident decode loop -------------------------------------------------------
+    def _need(self, r: Request) -> int:
+        """Decode steps still to launch for r (its remaining tokens minus those in flight)."""
+        return 0 if r.finished else r.max_new_tokens - len(r.output) - r.inflight
+
+    def _run_decode_async(self) -> bool:
+        """One decode step of the device-resident loop; False when it cannot run (out of pages).
+
+        The lanes' inputs stay on the device between steps (the graph's last kernel advances them);
+        this launches step t, then reads back step t - 1's tokens, so the host's bookkeeping overlaps
+        the GPU's work.  The lane set is re-uploaded only when it changes (a request joined or
+        finished), after the in-flight step was read back.  A lane that stops on a stop token runs
+        one extra step whose token is dropped; stops by length are known ahead and cost nothing."""
+        ps, W = self.ecfg.page_size, self.bt_width
+        lanes = [r for r in self.running if self._need(r) > 0]
+        if [id(r) for r in lanes] != [id(r) for r in self._lanes] or not self._lanes_valid:
+            self._drain()
+            lanes = [r for r in self.running if self._need(r) > 0]
+            if not lanes:
+                return True
+            if not self._map_pages(lanes, None):
+                return False
+            self._upload_lanes(lanes)
+        else:
+            patches: list[int] = []
+            if not self._map_pages(lanes, patches):
+                return False
+            if patches:
+                _, bt = self.runner.lane_state(W)
+                iv = torch.tensor(patches, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
+                K.scatter_i32(bt, iv, len(patches) // 2)
+                self.stats["h2d_bytes"] += 4 * len(patches)
+        B = len(lanes)
+        self.runner.replay_resident(B)
+        buf = self._rb[self._rb_i]
+        self._rb_i ^= 1
+        rn = self.runner
+        buf[:B].copy_(rn.status[:B], non_blocking=True)
+        buf[-2:].copy_(rn.status[rn.max_batch:rn.max_batch + 2], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        for r in lanes:
+            r.n_kv += 1
+            r.inflight += 1
+        prev, self._pending = self._pending, (ev, buf, list(lanes))
+        self.stats["decode_tokens"] += B
+        self.stats["d2h_bytes"] += 4 * (B + 2)
+        if prev is not None:
+            self._collect(prev)
+        return True
+
+    def _map_pages(self, lanes: list[Request], patches: list[int] | None) -> bool:
+        """Pages for the position each lane feeds now and, when it runs again, the next one (the
+        graph computes that slot on the device).  ``patches`` collects (flat index, page) pairs of
+        new block-table entries of resident lanes.  False (nothing changed for the lane that failed)
+        when the pool runs dry: the caller falls back to the synchronous step, which preempts."""
+        ps, W = self.ecfg.page_size, self.bt_width
+        for b, r in enumerate(lanes):
+            last = r.n_kv + (1 if self._need(r) > 1 else 0)
+            need = min(last, self.max_context - 1) // ps + 1 - len(r.pages)
+            if need > 0:
+                try:
+                    new = self._alloc(need)
+                except OutOfPages:
+                    return False
+                if patches is not None:
+                    for j, pg in enumerate(new):
+                        patches += [b * W + len(r.pages) + j, pg]
+                r.pages.extend(new)
+        return True
+
+    def _upload_lanes(self, lanes: list[Request]) -> None:
+        """Write every lane's state (and idle rows after them) into the runner's static inputs."""
+        ps, W, mb = self.ecfg.page_size, self.bt_width, self.ecfg.max_batch
+        vec = np.zeros((4, mb), np.int32)
+        vec[2, :] = -1
+        vec[3, :] = 1
+        bt = np.zeros((mb, W), np.int32)
+        for b, r in enumerate(lanes):
+            p = r.n_kv
+            vec[0, b] = r.tokens[-1]
+            vec[1, b] = p
+            vec[2, b] = r.pages[p // ps] * ps + p % ps
+            vec[3, b] = p + 1
+            bt[b, :len(r.pages)] = r.pages
+        dv, dbt = self.runner.lane_state(W)
+        dv.copy_(torch.from_numpy(vec).pin_memory(), non_blocking=True)
+        dbt.copy_(torch.from_numpy(bt).pin_memory(), non_blocking=True)
+        self.stats["h2d_bytes"] += vec.nbytes + bt.nbytes
+        self._lanes = list(lanes)
+        self._lanes_valid = True
+
+    def _collect(self, pending) -> None:
+        """Read back one launched step: emit each lane's token (dropped for a lane that stopped
+        meanwhile), fail loudly on a device error word."""
+        ev, buf, lanes = pending
+        ev.synchronize()
+        vals = buf.tolist()
+        kerr, cerr = vals[-2], vals[-1]
+        for r in lanes:
+            r.inflight -= 1
+        if kerr or cerr:
+            self._device_error(kerr, cerr)
+        for b, r in enumerate(lanes):
+            if not r.finished:
+                self._emit(r, int(vals[b]))
+        self.running = [r for r in self.running if not r.finished]
+
+    def _drain(self) -> None:
+        if self._pending is not None:
+            p, self._pending = self._pending, None
+            self._collect(p)
+
+    def _device_error(self, kerr: int, cerr: int) -> None:
+        """A kernel's bounded wait expired (or it saw an out-of-range id): the step's outputs are not
+        trustworthy.  Every running request fails and the engine refuses further steps."""
+        from ..parallel.errors import DeviceStepError
+        msg = (f"decode step failed on the device: kernel error word {kerr}, collective error word {cerr} "
+               "(kernel: 1 = a bounded wait expired, 2 = an index out of range, 4 = a peer rank never arrived at a "
+               "fused all-reduce; collective: 1 = a peer rank never arrived at a barrier)")
+        for r in list(self.running):
+            r.finished = True
+            r.finish_reason = "error"
+        self.running = []
+        raise DeviceStepError(msg, kerr, cerr)
+
+    def _run_decode_sync(self) -> None:
         if not self.running:
             return
         ps = self.ecfg.page_size
@@ -470,9 +625,13 @@ class Engine:
         out = self.runner.decode(d[0:B], d[B:2 * B], d[2 * B:3 * B], btd, d[3 * B:4 * B], B,
                                  use_graph=self._graphs_ready, shared=d[4 * B:4 * B + 1], n_shared=int(shared[0]))
         self.stats["h2d_bytes"] += h.numel() * 4 + bt.size * 4
+        mb = self.runner.max_batch
+        kerr, cerr = self.runner.status[mb:mb + 2].tolist()
+        if kerr or cerr:
+            self._device_error(kerr, cerr)
         if greedy:
             toks = out.cpu().tolist()
-            self.stats["d2h_bytes"] += 4 * B
+            self.stats["d2h_bytes"] += 4 * B + 8
         else:
             toks = sample(self._capped(self.runner.logits[:B]), [r.sampling for r in lanes], lanes)
             self.stats["d2h_bytes"] += 8 * B

@@ -10,7 +10,7 @@ The quantizers are this framework's own: a min/max scale search per
 sub-block (no iterative refinement).  They produce valid blocks of each
 format from float weights, which is what the random-init test and benchmark
 checkpoints need.  Every float step is written so that the CUDA quantizer
-(csrc/kernels/quantize.cu) performs the same IEEE float32 operations in the
+(csrc/kernels/quant.cu) performs the same IEEE float32 operations in the
 same order and therefore produces identical bytes.
 """
 from __future__ import annotations

@@ -119,7 +119,10 @@ class ModelRunner:
         if gap:
             raise NotImplementedError(f"{gap}; run it on the fp32 reference model (models.reference.ReferenceModel)")
         self.act_d = K.ActQ(B, d, dev)
-        self.act_attn = K.ActQ(B, cfg.n_heads * self.D, dev)
+        # o_proj input: this rank's slice [a0, a1) of the attention output columns (all of them on one
+        # GPU); under TP the columns of other ranks' heads inside the slice stay zero
+        a0, a1, _, _ = weights.o_cols if weights.o_cols[1] else (0, cfg.n_heads * self.D, 0, 0)
+        self.act_attn = K.ActQ(B, a1 - a0, dev)
         self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
         # decode GEMV inputs: activations quantized by a separate kernel (default), or fp32 sources
         # the GEMV normalises and quantizes itself (fused_activations: fewer launches, but every CTA
@@ -132,8 +135,14 @@ class ModelRunner:
         self.ffn_in = K.FAct(self.h) if self.fused_act else self.act_ffn   # SwiGLU output -> down projection
         self.lm_in = K.FAct(self.x) if self.fused_act else self.act_d      # final norm -> LM head
         self.logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
-        self.next_ids = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # step status, read back by the host in one copy: the sampled ids of every lane, the kernels'
+        # error word (bounded waits that expired, out-of-range ids) and the collectives' error word
+        self.status = torch.zeros(B + 2, dtype=torch.int32, device=dev)
+        self.next_ids = self.status[:B]
+        self.err = self.status[B:B + 1]
+        if collectives is not None and hasattr(collectives, "err"):
+            collectives.err = self.status[B + 1:B + 2]
+        K.register_error_word(dev, self.err)
         self.max_split = 64
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
         self.n_split = int(os.environ.get("FAK_DEC_SPLITS", "0")) or 16
@@ -159,6 +168,11 @@ class ModelRunner:
         K.argmax_workspace(dev, B)
         self._graphs: dict[int, tuple[torch.cuda.CUDAGraph, dict]] = {}
         self._graph_kernels: dict[int, int] = {}
+        # static decode inputs shared by every graph bucket (graphs capture their addresses): rows
+        # ids / pos / slot / ctx of ``vec`` and the block table, one row per lane.  Between steps of
+        # the device-resident decode loop they hold the lanes' state (Engine._run_decode_async)
+        self._vec: torch.Tensor | None = None
+        self._bt: torch.Tensor | None = None
 
     # ------------------------------------------------------------------------------------
     def n_split_for(self, B: int) -> int:
@@ -277,15 +291,22 @@ class ModelRunner:
     # ------------------------------------------------------------------------------------
     # CUDA graph per batch bucket
     # ------------------------------------------------------------------------------------
+    def lane_state(self, bt_width: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """The shared static decode inputs: ``vec`` int32 [4, max_batch] (rows ids, pos, slot, ctx)
+        and the block table int32 [max_batch, bt_width].  Idle lanes have slot -1 and ctx 1."""
+        if self._vec is None:
+            dev = self.device
+            self._vec = torch.zeros(4, self.max_batch, dtype=torch.int32, device=dev)
+            self._vec[2].fill_(-1)
+            self._vec[3].fill_(1)
+            self._bt = torch.zeros(self.max_batch, bt_width, dtype=torch.int32, device=dev)
+        if self._bt.shape[1] != bt_width:
+            raise ValueError(f"block-table width {bt_width} differs from the captured {self._bt.shape[1]}")
+        return self._vec, self._bt
+
     def _static_inputs(self, B: int, bt_width: int) -> dict:
-        dev = self.device
-        return {
-            "ids": torch.zeros(B, dtype=torch.int32, device=dev),
-            "pos": torch.zeros(B, dtype=torch.int32, device=dev),
-            "slot": torch.zeros(B, dtype=torch.int32, device=dev),
-            "bt": torch.zeros(B, bt_width, dtype=torch.int32, device=dev),
-            "ctx": torch.ones(B, dtype=torch.int32, device=dev),
-        }
+        vec, bt = self.lane_state(bt_width)
+        return {"ids": vec[0, :B], "pos": vec[1, :B], "slot": vec[2, :B], "ctx": vec[3, :B], "bt": bt[:B]}
 
     def capture(self, B: int, bt_width: int, n_layers: int | None = None) -> None:
         """Capture the B-lane step: the plain variant, and (target model, cascade possible) the
@@ -306,10 +327,23 @@ class ModelRunner:
             with torch.cuda.graph(g):
                 self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers,
                                   cascade=casc)
+                if n_layers is None:
+                    # the step's tokens become the next step's inputs on the device (idle lanes stay idle)
+                    K.decode_advance(self.next_ids, st["ids"], st["pos"], st["slot"], st["ctx"], st["bt"], B)
             key = (B, n_layers, casc)
             self._graph_kernels[key] = K.launches() - before
             K._launches[0] = before
             self._graphs[key] = (g, st)
+
+    def replay_resident(self, B: int) -> None:
+        """One decode step of the device-resident lanes [0, B) (their inputs already in the shared
+        static buffers, lanes [B, bucket) idle); the graph ends by advancing the lanes' inputs."""
+        bucket = self.graph_bucket(B, None, False)
+        if bucket is None:
+            raise RuntimeError(f"no captured decode graph holds {B} lanes")
+        g, _ = self._graphs[(bucket, None, False)]
+        g.replay()
+        K.count(self._graph_kernels[(bucket, None, False)])
 
     def graph_bucket(self, B: int, n_layers: int | None = None, cascade: bool = False) -> int | None:
         cands = [b for b, nl, c in self._graphs if b >= B and nl == n_layers and c == cascade]

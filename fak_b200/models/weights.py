@@ -108,6 +108,9 @@ class ModelWeights:
     tp_rank: int = 0
     tp_size: int = 1
     load_profile: dict = dataclasses.field(default_factory=dict)   # seconds per load phase
+    # o_proj input columns: this rank holds columns [a0, a1) of the attention output projection; its
+    # own heads' outputs fill [c0, c1) and the rest of [a0, a1) stays zero (a1 - a0 == the matrix's K)
+    o_cols: tuple[int, int, int, int] = (0, 0, 0, 0)
 
     @property
     def n_q_local(self) -> int:
@@ -221,6 +224,30 @@ def head_assignment(cfg: ModelConfig, tp_rank: int, tp_size: int) -> tuple[list[
     return [k * G + start + i for i in range(n)], [k]
 
 
+def o_proj_columns(cfg: ModelConfig, q_heads: list[int], tp_size: int) -> tuple[int, int, int, int]:
+    """(a0, a1, c0, c1): the row-parallel slice of the attention output projection a rank holds.
+
+    The rank's heads produce input columns [c0, c1) = [first head * D, (last head + 1) * D).  Quantized
+    rows can only be cut on block boundaries (256 weights for K-quant super-blocks and the int4 group
+    format; 64 suffices for Q8_0 in the tile-packed GEMV and is used when the width is not a multiple
+    of 256, which K-quant rows never are), so the rank keeps the aligned range [a0, a1) around
+    its heads and feeds zero activations (zero codes and zero block scales) to the columns of other
+    ranks' heads inside it: those weights then contribute exactly zero, and the rank-order sum of the
+    partial outputs over ranks is the full projection.  Qwen2.5-7B at TP=8 (3 or 4 heads of 128 per
+    rank) keeps 512 or 768 of the 3584 columns instead of the whole matrix."""
+    K = cfg.n_heads * cfg.head_dim
+    if tp_size == 1:
+        return 0, K, 0, K
+    D = cfg.head_dim
+    c0, c1 = q_heads[0] * D, (q_heads[-1] + 1) * D
+    if q_heads != list(range(q_heads[0], q_heads[-1] + 1)):
+        raise ValueError("row-parallel o_proj expects each rank's query heads to be contiguous")
+    g = 256 if K % 256 == 0 else 64   # one slice for every layer, whatever its block type
+    a0 = c0 // g * g
+    a1 = min(K, -(-c1 // g) * g)
+    return a0, a1, c0, c1
+
+
 def vocab_slice(V: int, tp_rank: int, tp_size: int) -> tuple[int, int]:
     per = -(-V // tp_size)
     return min(V, tp_rank * per), min(V, (tp_rank + 1) * per)
@@ -264,7 +291,9 @@ def _col_block_slice(raw: torch.Tensor, t: int, cols: int, c0: int, c1: int) -> 
 
 def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], device: str | torch.device = "cuda",
                  tp_rank: int = 0, tp_size: int = 1, expert_filter: tuple[int, int] | None = None,
-                 prefill_dense: bool = False) -> ModelWeights:
+                 prefill_dense: bool = False, repeat_layers: bool = False) -> ModelWeights:
+    """repeat_layers: load only block 0 and let every layer share it (smoke tests of a large
+    architecture: the same shapes and kernels, one layer's worth of weight synthesis and memory)."""
     import time
     cfg, get0, close = source
     device = torch.device(device)
@@ -306,7 +335,7 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
         return torch.cat([torch.arange(h * D, (h + 1) * D) for h in heads]) if heads else torch.zeros(0, dtype=torch.long)
 
     layers = []
-    for i in range(cfg.n_layers):
+    for i in range(1 if repeat_layers else cfg.n_layers):
         p = f"blk.{i}."
         segs: list[tuple[QuantWeight, int]] = []
         parts = []
@@ -332,12 +361,14 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
             bias = torch.cat([qb, kb, vb]).contiguous()
         qn = _vec(get, p + "attn_q_norm.weight", device) if cfg.qk_norm else None
         kn = _vec(get, p + "attn_k_norm.weight", device) if cfg.qk_norm else None
-        # o_proj stays whole on every rank: the attention outputs of all heads are gathered and
-        # each rank applies the full projection, so the residual stream stays replicated without a
-        # second collective.  (A K-split at head boundaries is impossible for Q4_K rows when a rank
-        # owns an odd number of 128-wide heads: super-blocks are 256 wide.)
+        # o_proj is row-parallel (split along its input): each rank multiplies its own heads'
+        # outputs into a partial of the full output row, and the partials are summed across ranks
+        # (in the GEMV epilogue on the fused path); see o_proj_columns for the block-aligned slice.
         shape, t, raw = quant(p + "attn_output.weight")
-        o = QuantWeight.from_rows(raw, t, shape[1], device)
+        o_cols = o_proj_columns(cfg, q_heads, tp_size)
+        if (o_cols[0], o_cols[1]) != (0, shape[1]):
+            raw = _col_block_slice(raw, t, shape[1], o_cols[0], o_cols[1])
+        o = QuantWeight.from_rows(raw, t, o_cols[1] - o_cols[0], device)
         L = LayerWeights(
             attn_norm=_vec(get, p + "attn_norm.weight", device),
             ffn_norm=_vec(get, p + "ffn_norm.weight", device),
@@ -379,6 +410,8 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
         prof["pack"] += t1 - t0
         prof["dense"] += time.perf_counter() - t1
         layers.append(L)
+    if repeat_layers:
+        layers = layers * cfg.n_layers
     final_norm = _vec(get, "output_norm.weight", device)
     # lm_head: split by vocab rows under TP (ceil(V/T) rows per rank, the last rank may hold fewer)
     v0, v1 = vocab_slice(cfg.vocab_size, tp_rank, tp_size)
@@ -394,7 +427,7 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
     prof["total"] = time.perf_counter() - t_start
     prof["upload"] = max(0.0, prof["total"] - prof["read"] - prof["convert"] - prof["pack"] - prof["dense"])
     return ModelWeights(cfg, embed, layers, final_norm, lm_head, q_heads, kv_heads, (f0, f1), tp_rank, tp_size,
-                        load_profile={k: round(v, 4) for k, v in prof.items()})
+                        load_profile={k: round(v, 4) for k, v in prof.items()}, o_cols=o_cols)
 
 
 def expert_slice(E: int, rank: int, size: int) -> tuple[int, int]:

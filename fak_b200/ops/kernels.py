@@ -25,6 +25,36 @@ def reset_launches() -> None:
     _launches[0] = 0
 
 
+# per-device error word the kernels report bounded-wait expiries into (ModelRunner registers its
+# status word here, so the host reads it back with the step's tokens)
+_err_word: dict = {}
+
+
+def register_error_word(device, word: torch.Tensor | None) -> None:
+    key = torch.device(device)
+    if word is None:
+        _err_word.pop(key, None)
+    else:
+        _err_word[key] = word
+
+
+def error_word(device) -> torch.Tensor | None:
+    return _err_word.get(torch.device(device))
+
+
+def decode_advance(next_ids, ids, pos, slot, ctx, bt, B: int) -> None:
+    """Next decode step's lane inputs from this step's tokens, on the device: ids <- next_ids,
+    pos += 1, ctx = pos + 1, slot from the block table (lanes with slot < 0 stay idle)."""
+    ext().decode_advance(next_ids, ids, pos, slot, ctx, bt, B)
+    count()
+
+
+def scatter_i32(dst: torch.Tensor, idx_val: torch.Tensor, n: int) -> None:
+    """dst.flatten()[idx_val[i, 0]] = idx_val[i, 1] for i < n (device tensors)."""
+    ext().scatter_i32(dst, idx_val, n)
+    count()
+
+
 class ActQ:
     """int8-quantized activations: codes [B, K] and per-32 (scale, sum) [B, K/32, 2]."""
 
@@ -82,8 +112,10 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
     """y[:B] (op)= W . x for a decode batch (w: models.weights.QuantWeight); chunks of 8 tokens.
 
     Matrices with a tile-packed copy (``QuantWeight.pack``) run the tile-packed tensor-core GEMV;
-    others the row-major kernels.  ``ar`` = (peer bases, rank, parts offset, flags offset, epochs)
-    fuses a tensor-parallel all-reduce of the result into the GEMV (EPI_ADD, one launch, B <= 32)."""
+    others the row-major kernels.  ``ar`` = (peer bases, rank, parts offset, flags offset, epochs
+    [, spin limit]) fuses a tensor-parallel all-reduce of the result into the GEMV (EPI_ADD, one
+    launch, B <= 32); a peer that never arrives makes the wait give up after the spin limit (0: the
+    kernel default) and report error 4 in the registered error word."""
     C = ext()
     if w.tp is not None:
         part, cnt = tgemv_workspace(w.tp.device)
@@ -100,15 +132,16 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
             if ar is not None and B > TGEMV_MAX_B:
                 raise ValueError("the fused all-reduce GEMV takes at most 32 tokens")
             arkw = {} if ar is None else dict(ar_peers=ar[0], ar_me=ar[1], ar_parts_off=ar[2], ar_flags_off=ar[3],
-                                              ar_epochs=ar[4])
+                                              ar_epochs=ar[4], ar_spin_limit=ar[5] if len(ar) > 5 else 0)
             if prefetch is not None and b0 == 0:
                 arkw["prefetch"] = prefetch
+            ew = _err_word.get(w.tp.device)
             if isinstance(act, FAct):
                 C.tgemv(w.tp, w.qtype, w.rows, w.cols, None, None, act.x[b0:b0 + nb], act.gamma, act.eps, nb,
-                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags, **arkw)
+                        y[b0:b0 + nb], bias, epi, part, cnt, ew, flags, **arkw)
             else:
                 C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q[b0:b0 + nb], act.ds[b0:b0 + nb], None, None, 0.0, nb,
-                        y[b0:b0 + nb], bias, epi, part, cnt, None, flags, **arkw)
+                        y[b0:b0 + nb], bias, epi, part, cnt, ew, flags, **arkw)
             count()
         return
     if isinstance(act, FAct):

@@ -1,22 +1,22 @@
-"""Tensor parallelism over NCCL: the collectives between the per-rank GEMVs/GEMMs.
+"""Tensor parallelism over NCCL: the collectives between the per-rank GEMVs/GEMMs (the baseline).
 
 Sharding (models/weights.py):
 * q/k/v: by heads.  With fewer KV heads than ranks a KV head is replicated and its query
   group split (Qwen2.5-7B at TP=8: 4 + 3 query heads per rank);
 * attention: local heads only;
-* o_proj: whole on every rank.  The attention outputs of all heads are all-gathered (int8
-  codes + per-32 scales for decode, bf16 for prefill) and every rank applies the full
-  projection, so the residual stream stays replicated with a single collective;
+* o_proj: row-parallel (split along its input).  A rank holds the block-aligned column range around
+  its heads (``weights.o_proj_columns``), multiplies its heads' outputs into a partial of the whole
+  output row, and the partials are all-reduced into the replicated residual stream;
 * gate/up: split by FFN rows in whole 256-wide super-blocks; down: split the same way along
   its input (K) dim -> partial sums -> all-reduce;
-* lm_head: split by vocab rows -> all-gather of logits.
+* lm_head: split by vocab rows -> all-gather of logits (or a distributed argmax, fused path).
 
-The reference's TP (internal/model/tensor_parallel_forward.go:456-527) is the Megatron
-column/row scheme on host f32 buffers with an AllReduceSum after o_proj and down
-(:246, :371), cacheless prefill only; this one runs decode and prefill on the GPU.
+Megatron's column/row scheme, the reference's TP (internal/model/tensor_parallel_forward.go:456-527)
+on host f32 buffers with an AllReduceSum after o_proj and after down (:246, :371), cacheless prefill
+only; this one runs decode and prefill on the GPU.
 
-This class is the NCCL baseline.  The fused path (parallel/fused.py) replaces the
-collectives with in-kernel peer-memory transfers.
+This class is the NCCL baseline: the product path (``parallel/p2p.py``, ``P2PTP``) moves both
+all-reduces into the GEMV epilogue over peer memory.
 """
 from __future__ import annotations
 
@@ -26,6 +26,13 @@ import torch.distributed as dist
 from ..ops import kernels as K
 
 
+class _ActView:
+    """ActQ-compatible view (codes ``q`` [B, K] int8, ``ds`` [B, K/32, 2] f32) over raw storage."""
+
+    def __init__(self, q: torch.Tensor, ds: torch.Tensor, K: int):
+        self.q, self.ds, self.K = q, ds, K
+
+
 class NcclTP:
     def __init__(self, group, weights, max_batch: int, device):
         self.group = group
@@ -33,53 +40,42 @@ class NcclTP:
         self.rank = dist.get_rank(group)
         cfg = weights.cfg
         self.cfg = cfg
-        D = cfg.head_dim
-        self.D = D
-        # head ownership of every rank (deterministic: recomputed, not communicated)
-        from ..models.weights import head_assignment
-        owners = [head_assignment(cfg, r, self.world)[0] for r in range(self.world)]
-        self.maxHq = max(len(o) for o in owners)
-        slot = [0] * cfg.n_heads
-        for r, heads in enumerate(owners):
-            for j, h in enumerate(heads):
-                slot[h] = r * self.maxHq + j
-        self.head_slot = torch.tensor(slot, dtype=torch.long, device=device)
-        self.Hq_local = len(owners[self.rank])
+        self.D = cfg.head_dim
+        self.o_cols = weights.o_cols
+        self.Hq_local = len(weights.q_heads)
         B = max_batch
-        self.act_local = K.ActQ(B, self.maxHq * D, device)
-        # gather targets are flat: [world, b, ...] views of their first world*b rows stay contiguous
-        self.recv_q = torch.zeros(self.world * B * self.maxHq * D, dtype=torch.int8, device=device)
-        self.recv_ds = torch.zeros(self.world * B * self.maxHq * D // 16, dtype=torch.float32, device=device)
         self.tmp = torch.zeros(B, cfg.d_model, dtype=torch.float32, device=device)
         # every rank gathers ceil(V/T) logits (ranks with fewer real rows pad with -inf)
         self.Vl = -(-cfg.vocab_size // self.world)
         self.Vl_real = weights.lm_head.rows
         self.logits_local = torch.full((B, self.Vl), float("-inf"), dtype=torch.float32, device=device)
         self.logits_all = torch.zeros(self.world * B * self.Vl, dtype=torch.float32, device=device)
+        self._act_view = None
+        self._o_dense: dict[int, torch.Tensor] = {}
 
     # ---------------------------------------------------------------------------------
-    def _gather_heads_q(self, B: int, act_dst) -> None:
-        D, H, Wd = self.D, self.cfg.n_heads, self.world
-        rq = self.recv_q[:Wd * B * self.maxHq * D]
-        rd = self.recv_ds[:Wd * B * self.maxHq * D // 16]
-        dist.all_gather_into_tensor(rq, self.act_local.q[:B].reshape(-1), group=self.group)
-        dist.all_gather_into_tensor(rd, self.act_local.ds[:B].reshape(-1), group=self.group)
-        q = rq.view(Wd, B, self.maxHq, D).permute(1, 0, 2, 3).reshape(B, -1, D)
-        ds = rd.view(Wd, B, self.maxHq, D // 32, 2).permute(1, 0, 2, 3, 4)
-        ds = ds.reshape(B, -1, D // 32, 2)
-        act_dst.q[:B].view(B, H, D).copy_(q.index_select(1, self.head_slot))
-        act_dst.ds[:B].view(B, H, D // 32, 2).copy_(ds.index_select(1, self.head_slot))
+    def attn_out(self, rn) -> _ActView:
+        """This rank's heads' columns inside the o_proj input slice (rows of a1 - a0 elements)."""
+        if self._act_view is None:
+            a0, a1, c0, _ = self.o_cols
+            off = c0 - a0
+            act = rn.act_attn
+            self._act_view = _ActView(act.q.view(-1)[off:], act.ds.view(-1)[off // 16:], a1 - a0)
+        return self._act_view
+
+    def attention(self, rn, i: int, B: int, bt, ctx, n_split: int) -> None:
+        """Decode attention of the local heads, written int8-quantized into the o_proj input slice."""
+        kv = rn.kv
+        K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.attn_out(rn), workspace=rn.attn_ws,
+                           tickets=rn.attn_tickets, ldo=self.o_cols[1] - self.o_cols[0],
+                           window=rn.cfg.layer_window(i), **rn.cascade_args(B, rn.cfg.layer_window(i)))
 
     def decode_attn_o(self, rn, i: int, B: int, bt, ctx, n_split: int) -> None:
-        kv = rn.kv
-        if self.Hq_local < self.maxHq:  # pad slots of ranks with fewer heads stay zero
-            self.act_local.q[:B].zero_()
-            self.act_local.ds[:B].zero_()
-        K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_local, workspace=rn.attn_ws,
-                           tickets=rn.attn_tickets, ldo=self.maxHq * self.D, window=rn.cfg.layer_window(i),
-                           **rn.cascade_args(B, rn.cfg.layer_window(i)))
-        self._gather_heads_q(B, rn.act_attn)
-        K.gemv(rn.w.layers[i].o, rn.act_attn, B, rn.x[:B], None, K.EPI_ADD)
+        self.attention(rn, i, B, bt, ctx, n_split)
+        t = self.tmp[:B]
+        K.gemv(rn.w.layers[i].o, rn.act_attn, B, t, None, K.EPI_STORE)
+        dist.all_reduce(t, group=self.group)
+        rn.x[:B].add_(t)
 
     def decode_down(self, rn, i: int, B: int) -> None:
         t = self.tmp[:B]
@@ -103,16 +99,20 @@ class NcclTP:
         self._gather_logits(n, out)
 
     # ---------------------------------------------------------------------------------
+    def o_dense_local(self, rn, i: int) -> torch.Tensor:
+        """bf16 [d, n_local_heads * D]: the columns of o_proj that this rank's heads feed (prefill)."""
+        w = self._o_dense.get(i)
+        if w is None:
+            a0, _, c0, c1 = self.o_cols
+            w = rn.w.layers[i].o.dense()[:, c0 - a0:c1 - a0].contiguous()
+            self._o_dense[i] = w
+        return w
+
     def prefill_attn_o(self, rn, i: int, ab: torch.Tensor, x: torch.Tensor) -> None:
-        T = ab.shape[0]
-        D = self.D
-        send = torch.zeros(T, self.maxHq * D, dtype=torch.bfloat16, device=ab.device)
-        send[:, :ab.shape[1]].copy_(ab)
-        recv = torch.empty(self.world, T, self.maxHq * D, dtype=torch.bfloat16, device=ab.device)
-        dist.all_gather_into_tensor(recv.view(-1), send.view(-1), group=self.group)
-        full = recv.view(self.world, T, self.maxHq, D).permute(1, 0, 2, 3).reshape(T, -1, D)
-        full = full.index_select(1, self.head_slot).reshape(T, -1).contiguous()
-        K.gemm(full, rn.w.layers[i].o, x, K.EPI_ADD)
+        part = torch.empty_like(x)
+        K.gemm(ab, self.o_dense_local(rn, i), part, K.EPI_STORE)
+        dist.all_reduce(part, group=self.group)
+        x.add_(part)
 
     def prefill_down(self, rn, i: int, hb2: torch.Tensor, x: torch.Tensor) -> None:
         t = torch.empty_like(x)

@@ -341,3 +341,50 @@ def test_poisoned_scratch_changes_nothing(model_file):
     eng = _engine(model_file, graphs=True, debug_poison=True)
     assert eng.generate(prompts, max_new_tokens=10) == want
     assert eng.stats["load_total_s"] > 0 and "load_pack_s" in eng.stats
+
+
+def _staggered_run(eng, prompts, stops, lengths):
+    """Requests arriving over several steps, some stopping on a token, different lengths."""
+    reqs = []
+    for i, (p, mx) in enumerate(zip(prompts, lengths)):
+        reqs.append(eng.add_request(p, mx, stop_ids=stops))
+        for _ in range(i % 3):
+            if eng.has_work():
+                eng.step()
+    eng.run_until_done(reqs)
+    return [r.full_output for r in reqs], [r.finish_reason for r in reqs]
+
+
+def test_async_decode_matches_sync_loop(model_file):
+    """The device-resident loop (lane inputs advanced on the device, tokens read one step behind)
+    emits exactly the tokens of the synchronous loop: arrivals mid-decode, stop tokens (one wasted
+    step each, its token dropped) and different lengths included."""
+    rng = np.random.default_rng(7)
+    eng = _engine(model_file, graphs=True, async_decode=False)
+    V = eng.cfg.vocab_size
+    prompts = [rng.integers(0, V, int(n)).tolist() for n in rng.integers(5, 90, 7)]
+    lengths = [int(n) for n in rng.integers(3, 30, 7)]
+    # a stop set that the greedy outputs hit: the first tokens of two sync runs
+    probe, _ = _staggered_run(eng, prompts[:2], frozenset(), [8, 8])
+    stops = frozenset({probe[0][5], probe[1][3]})
+    want, why_want = _staggered_run(eng, prompts, stops, lengths)
+    eng2 = _engine(model_file, graphs=True, async_decode=True)
+    got, why_got = _staggered_run(eng2, prompts, stops, lengths)
+    assert got == want and why_got == why_want, (got, want, why_got, why_want)
+    assert "stop" in why_want
+    assert eng2._pending is None and not eng2.running
+
+
+def test_device_error_word_fails_the_step(model_file):
+    """A non-zero device error word in the step's readback raises DeviceStepError and fails the
+    running requests (no tokens computed from missing data are emitted)."""
+    from fak_b200.parallel.errors import DeviceStepError
+    eng = _engine(model_file, graphs=True, async_decode=True)
+    r = eng.add_request(list(range(3, 30)), 20)
+    eng.step()
+    eng.step()
+    eng.runner.err.fill_(1)        # as a kernel whose bounded wait expired would
+    with pytest.raises(DeviceStepError) as ei:
+        for _ in range(4):
+            eng.step()
+    assert ei.value.kernel_code == 1 and r.finished and r.finish_reason == "error"

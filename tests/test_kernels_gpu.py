@@ -1,6 +1,5 @@
 """Numerics of the sm_100a kernels against plain fp32 PyTorch references (GPU only)."""
 import math
-import os
 
 import numpy as np
 import pytest
@@ -38,7 +37,6 @@ def test_quantize_matches_numpy_bitexact(qt, blk):
     got = _ext().quantize_blocks(torch.from_numpy(x).cuda().reshape(-1), int(qt)).cpu().numpy()
     assert got.shape == ref.shape
     match = (got == ref).mean()
-    np.save(f"gpurun_out/quant_{int(qt)}_got.npy", got) if os.path.isdir("gpurun_out") else None
     # same format, same decoded values up to one quantization step
     dg, dr = Q.dequantize(got, qt), Q.dequantize(ref, qt)
     step = np.abs(x).max() / (127 if qt == GGMLType.Q8_0 else 15)

@@ -37,3 +37,19 @@ def test_ep2_moe_matches_ep1():
     assert p.returncode == 0, p.stderr[-3000:]
     res = json.loads([l for l in p.stdout.splitlines() if l.startswith("{")][-1])
     assert res["ok"], res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_that_never_arrives_fails_the_step():
+    """Rank 1 stops launching between steps; rank 0's fused all-reduce wait runs out under a short
+    spin limit, returns with error 4 in the step's kernel word, and the engine raises DeviceStepError
+    (no GPU is faulted or hung: the waits are bounded; NVLS off, peer buffers through CUDA IPC)."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT, FAK_P2P_MEM="ipc")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29535", "-m",
+           "fak_b200.benchmarks.faultcheck"]
+    p = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-3000:]
+    res = json.loads([l for l in p.stdout.splitlines() if l.startswith("{")][-1])
+    assert res["ok"], res
+    assert res["ranks"][0]["seconds_to_error"] < 60, res
