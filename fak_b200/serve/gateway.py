@@ -10,6 +10,12 @@ Routes (reference surface: internal/gateway/http.go:54-131):
   GET  /v1/fak/journal        tail of the hash-chained decision journal (+ chain check)
   POST /v1/fak/policy         hot-reload a validated policy manifest
   GET  /v1/fak/stats          kernel + engine counters (radix reuse, TTFT, verdicts)
+  + the Responses / count_tokens / moderations / Gemini / syscall / admit / MCP / A2A surfaces and
+    the admission and autoscaler views of ``serve/surfaces.py``
+
+With an ``AdmissionController`` every generating request holds an admission lease (priority from the
+``X-Fak-Priority`` header or the body's ``priority``; a full waiting queue answers 429, a denied
+tenant 403).  Completed requests feed the autoscaler's signal window (TTFT, TPOT, goodput).
 
 Every tool call the model proposes is adjudicated before it is returned to the client: allowed
 calls pass (with redacted arguments under TRANSFORM), refused calls are removed from the
@@ -25,9 +31,13 @@ from typing import Any, Iterator
 from fastapi import FastAPI, HTTPException, Request
 from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
+import contextlib
+
 from ..agentkernel import Kernel, ToolCall, VerdictKind, policy_from_dict
 from ..engine.sampling import SamplingParams
 from ..tokenizer import IncrementalDecoder
+from .admission import AdmissionController, AdmissionError, SeqRequest
+from .autoscale import PoolObjective, ServingAutoscaler, SignalWindow
 from .backend import UpstreamBackend
 from .chat import extract_tool_calls, render_chatml
 
@@ -92,8 +102,13 @@ class Metrics:
 
 class Gateway:
     def __init__(self, backend, kernel: Kernel | None = None, model_name: str | None = None,
-                 default_max_tokens: int = 256, ctx_view_budget: int = 0):
+                 default_max_tokens: int = 256, ctx_view_budget: int = 0,
+                 admission: AdmissionController | None = None, objective: PoolObjective | None = None):
         self.backend = backend
+        self.admission = admission
+        self.objective = objective or PoolObjective()
+        self.signals = SignalWindow(self.objective)
+        self.autoscaler = ServingAutoscaler({"decode": self.objective})
         self.planner = None   # planned context views under a token budget (0: whole transcript)
         if ctx_view_budget > 0:
             from .ctxplan import ContextPlanner
@@ -106,6 +121,39 @@ class Gateway:
         self.metrics = Metrics()
         self.tok = getattr(backend, "tok", None)
         self._json = None
+
+    # ------------------------------------------------------------------ admission / autoscale
+    def count_prompt_tokens(self, text: str) -> int:
+        return len(self.tok.encode(text)) if self.tok is not None else max(1, len(text) // 4)
+
+    @contextlib.contextmanager
+    def lease(self, body: dict, route: str, priority: int | None = None):
+        """Hold an admission lease around one generating request (no-op without a controller)."""
+        if self.admission is None:
+            yield None
+            return
+        msgs = body.get("messages") or []
+        est = sum(len(json.dumps(m)) for m in msgs) // 4 + len(str(body.get("prompt", ""))) // 4
+        toks = est + int(body.get("max_tokens") or body.get("max_completion_tokens") or self.default_max_tokens)
+        pr = int(body.get("priority", 0) if priority is None else priority)
+        r = SeqRequest(trace_id=f"{route}-{uuid.uuid4().hex[:16]}", priority=pr, tokens=toks)
+        try:
+            with self.admission.lease(r) as held:
+                yield held
+        except AdmissionError as e:
+            raise HTTPException(e.status, str(e))
+
+    def autoscale_decision(self, replicas: int = 1) -> dict:
+        eng = getattr(self.backend, "engine", None)
+        depth = len(getattr(eng, "waiting", [])) if eng is not None else 0
+        if self.admission is not None:
+            depth += self.admission.snapshot()["waiting"]
+        kv = 0.0
+        pool = getattr(eng, "pool", None)
+        if pool is not None and getattr(pool, "n_pages", 0):
+            kv = 1.0 - pool.n_free() / pool.n_pages
+        sig = self.signals.signals(depth, kv)
+        return self.autoscaler.plan("decode", int(replicas), sig).to_dict()
 
     def _view(self, messages: list[dict]) -> list[dict]:
         return self.planner.plan(messages).messages if self.planner is not None and messages else messages
@@ -159,8 +207,11 @@ class Gateway:
             text += tail
             yield tail, {}
         self.metrics.tokens.inc(n)
+        tpot = None
         if first is not None and n > 1:
-            self.metrics.tpot.observe((time.perf_counter() - t0 - first) / (n - 1))
+            tpot = (time.perf_counter() - t0 - first) / (n - 1)
+            self.metrics.tpot.observe(tpot)
+        self.signals.observe(first, tpot)
         yield "", {"prompt_tokens": len(ids), "completion_tokens": n, "finish_reason": finish,
                    "ttft_s": first, "text": text}
 
@@ -376,18 +427,31 @@ def create_app(gw: Gateway) -> FastAPI:
         gw.metrics.scrape_engine(gw.backend)
         return PlainTextResponse(generate_latest(gw.metrics.registry).decode(), media_type="text/plain")
 
+    def leased_stream(gen, body, route, priority):
+        with gw.lease(body, route, priority):
+            yield from gen
+
+    def prio(req: Request) -> int | None:
+        h = req.headers.get("x-fak-priority")
+        return int(h) if h is not None and h.strip().lstrip("-").isdigit() else None
+
     @app.post("/v1/chat/completions")
     async def chat(req: Request):
         body = await req.json()
         with timed("chat"):
             if body.get("stream"):
-                return StreamingResponse(gw.chat_completion_stream(body), media_type="text/event-stream")
-            return JSONResponse(gw.chat_completion(body))
+                if gw.admission is not None and gw.admission.policy.max_waiting > 0 and \
+                        gw.admission.snapshot()["waiting"] >= gw.admission.policy.max_waiting:
+                    raise HTTPException(429, "server overloaded: waiting queue full")
+                return StreamingResponse(leased_stream(gw.chat_completion_stream(body), body, "chat", prio(req)),
+                                         media_type="text/event-stream")
+            with gw.lease(body, "chat", prio(req)):
+                return JSONResponse(gw.chat_completion(body))
 
     @app.post("/v1/completions")
     async def completions(req: Request):
         body = await req.json()
-        with timed("completions"):
+        with timed("completions"), gw.lease(body, "completions", prio(req)):
             return JSONResponse(gw.completion(body))
 
     @app.post("/v1/messages")
@@ -395,8 +459,10 @@ def create_app(gw: Gateway) -> FastAPI:
         body = await req.json()
         with timed("messages"):
             if body.get("stream"):
-                return StreamingResponse(gw.messages_stream(body), media_type="text/event-stream")
-            return JSONResponse(gw.messages(body))
+                return StreamingResponse(leased_stream(gw.messages_stream(body), body, "messages", prio(req)),
+                                         media_type="text/event-stream")
+            with gw.lease(body, "messages", prio(req)):
+                return JSONResponse(gw.messages(body))
 
     @app.post("/v1/embeddings")
     async def embeddings(req: Request):
@@ -426,6 +492,9 @@ def create_app(gw: Gateway) -> FastAPI:
             raise HTTPException(400, str(e))
         gw.kernel.set_policy(p)
         return {"ok": True}
+
+    from .surfaces import add_routes
+    add_routes(app, gw)
 
     @app.get("/v1/fak/stats")
     def stats():
