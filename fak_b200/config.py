@@ -314,6 +314,8 @@ class EngineConfig:
     seed: int = 0
     spec_k: int = 0                     # draft tokens per verify step (0: no speculation)
     spec_draft_layers: int = 4          # self-speculation: the draft is the first N layers + LM head
+    spec_drafter: str = "self"          # self | lookup | multi (self vs lookup by acceptance) | tree (lookup tree)
+    spec_tree_width: int = 3            # tree speculation: continuations (branches) per round
     fused_activations: bool = False     # decode GEMVs normalise+quantize fp32 inputs themselves
     attention_merge: bool = False       # merge attention splits in the last split's CTA (no combine launch)
     l2_prefetch: bool = False           # decode kernels warm L2 with the next GEMV's weights (measured neutral)
@@ -342,6 +344,8 @@ class EngineConfig:
         "seed": ("FAK_SEED", int),
         "spec_k": ("FAK_SPEC_K", int),
         "spec_draft_layers": ("FAK_SPEC_DRAFT_LAYERS", int),
+        "spec_drafter": ("FAK_SPEC_DRAFTER", str),
+        "spec_tree_width": ("FAK_SPEC_TREE_WIDTH", int),
         "fused_activations": ("FAK_FUSED_ACT", bool),
         "attention_merge": ("FAK_ATTN_MERGE", bool),
         "l2_prefetch": ("FAK_L2_PREFETCH", bool),

@@ -79,6 +79,9 @@ int64_t ipc_open(torch::Tensor handle, int64_t device);
 void ipc_close(int64_t ptr);
 void ipc_free(int64_t ptr);
 torch::Tensor ipc_view(int64_t ptr, int64_t nbytes, int64_t device);
+void sample_rows(torch::Tensor logits, int64_t V, torch::Tensor params, torch::Tensor bias_tok, torch::Tensor bias_val,
+                 c10::optional<torch::Tensor> counts, torch::Tensor out, int64_t B, double softcap);
+torch::Tensor philox4x32_10_host(std::vector<int64_t> ctr, std::vector<int64_t> key);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fak_b200 sm_100a kernels";
@@ -149,6 +152,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_view", &ipc_view, "non-owning uint8 tensor over a device buffer");
+  m.def("sample_rows", &sample_rows, "bias / penalties / temperature / top-k / top-p draw per row (Philox RNG)",
+        pybind11::arg("logits"), pybind11::arg("V"), pybind11::arg("params"), pybind11::arg("bias_tok"),
+        pybind11::arg("bias_val"), pybind11::arg("counts"), pybind11::arg("out"), pybind11::arg("B"),
+        pybind11::arg("softcap") = 0.0);
+  m.def("philox4x32_10_host", &philox4x32_10_host);
   m.def("gemm_bf16", &gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"),
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("epi") = 0, pybind11::arg("err") = pybind11::none());
 }

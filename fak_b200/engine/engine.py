@@ -35,7 +35,8 @@ from ..kv import OutOfPages, PagePool, RadixCache
 from ..ops import kernels as K
 from ..models.runner import KVCache, ModelRunner, PrefillMeta
 from ..models.weights import ModelWeights, gguf_source, load_weights, synthetic_source
-from .sampling import SamplingParams, sample
+from .constraints import guided_decode_enabled
+from .sampling import SamplingParams, device_sample, needs_counts, pack_params, request_seed, sample
 
 
 @dataclasses.dataclass
@@ -63,6 +64,7 @@ class Request:
     cache_limit: int | None = None   # tokens of this request the radix cache may take (span eviction)
     held_pages: list[int] = dataclasses.field(default_factory=list)
     inflight: int = 0                # decode steps launched for it whose token is not read back yet
+    seed: int = 0                    # 64-bit key of its random draws (SamplingParams.seed or derived)
 
     @property
     def ttft(self) -> float | None:
@@ -123,6 +125,8 @@ class Engine:
         self._lanes: list[Request] = []
         self._lanes_valid = False
         self._pending: tuple | None = None
+        self._n_shared = 0
+        self._sampled = False
         self._rb = [torch.zeros(self.ecfg.max_batch + 2, dtype=torch.int32).pin_memory()
                     for _ in range(2)] if self.device.type == "cuda" else []
         self._rb_i = 0
@@ -230,6 +234,8 @@ class Engine:
             raise ValueError(f"prompt {len(prompt)} + {max_new_tokens} new tokens exceeds context {self.max_context}")
         r = Request(next(self._rid), list(prompt), max_new_tokens, sampling or SamplingParams(),
                     frozenset(stop_ids), on_token=on_token)
+        r.seed = (int(r.sampling.seed) & 0xFFFFFFFFFFFFFFFF if r.sampling.seed is not None
+                  else request_seed(self.ecfg.seed, r.rid))
         r.tokens = list(prompt)
         self.waiting.append(r)
         return r
@@ -332,8 +338,7 @@ class Engine:
                 done.append((k, r))
         if done:
             rows = torch.tensor([k for k, _ in done], device=dev)
-            toks = sample(self._capped(logits.index_select(0, rows)), [r.sampling for _, r in done],
-                          [r for _, r in done])
+            toks = self._sample_rows(logits.index_select(0, rows), [r for _, r in done])
             self.stats["d2h_bytes"] += 8 * len(done)
             now = time.perf_counter()
             for (k, r), tok in zip(done, toks):
@@ -378,6 +383,22 @@ class Engine:
         part.fill_(nan)
         self.kv.k.fill_(3.0e4)
         self.kv.v.fill_(3.0e4)
+
+    @staticmethod
+    def _masked(r: Request) -> bool:
+        """Guided decoding: its token mask is computed on the host, so it samples on the host."""
+        return r.sampling.mask is not None and guided_decode_enabled()
+
+    def _sample_rows(self, logits: torch.Tensor, reqs: list[Request]) -> list[int]:
+        """One token per logit row (modified in place): the device sampler, or the host path when a
+        request's guided-decoding mask is active."""
+        if any(self._masked(r) for r in reqs):
+            return sample(self._capped(logits), [r.sampling for r in reqs], reqs)
+        if all(r.sampling.greedy for r in reqs):
+            return torch.argmax(logits, dim=-1).tolist()
+        return device_sample(logits, self.cfg.vocab_size, [r.sampling for r in reqs],
+                             [len(r.full_output) for r in reqs], [r.seed for r in reqs],
+                             [r.full_output for r in reqs], self.cfg.final_softcap)
 
     def _capped(self, logits: torch.Tensor) -> torch.Tensor:
         """Final-logit soft-capping (Gemma-2) before sampling; greedy argmax is unaffected by it."""
@@ -443,7 +464,7 @@ class Engine:
 
     def _async_ok(self) -> bool:
         return (self.ecfg.async_decode and self._graphs_ready and self.ecfg.spec_k == 0
-                and all(r.sampling.greedy for r in self.running))
+                and not any(self._masked(r) for r in self.running))
 
     def _run_decode(self) -> None:
         if self.running and self._async_ok():
@@ -486,7 +507,7 @@ class Engine:
                 K.scatter_i32(bt, iv, len(patches) // 2)
                 self.stats["h2d_bytes"] += 4 * len(patches)
         B = len(lanes)
-        self.runner.replay_resident(B)
+        self.runner.replay_resident(B, self._n_shared, self._sampled)
         buf = self._rb[self._rb_i]
         self._rb_i ^= 1
         rn = self.runner
@@ -542,6 +563,27 @@ class Engine:
         dv.copy_(torch.from_numpy(vec).pin_memory(), non_blocking=True)
         dbt.copy_(torch.from_numpy(bt).pin_memory(), non_blocking=True)
         self.stats["h2d_bytes"] += vec.nbytes + bt.nbytes
+        # sampled lanes: the device sampler's rows (parameters, bias lists, generated-token counts)
+        B = len(lanes)
+        rn = self.runner
+        self._sampled = any(not r.sampling.greedy for r in lanes)
+        if self._sampled:
+            P, tok, val = pack_params([r.sampling for r in lanes], [len(r.full_output) for r in lanes],
+                                      [r.seed for r in lanes])
+            rn.samp_params[:B].copy_(torch.from_numpy(P).pin_memory(), non_blocking=True)
+            if len(tok):
+                rn.bias_tok[:len(tok)].copy_(torch.from_numpy(tok).pin_memory(), non_blocking=True)
+                rn.bias_val[:len(val)].copy_(torch.from_numpy(val).pin_memory(), non_blocking=True)
+            if needs_counts([r.sampling for r in lanes]):
+                from .sampling import count_rows
+                rn.counts[:B].copy_(count_rows([r.full_output for r in lanes], self.cfg.vocab_size, self.device))
+            self.stats["h2d_bytes"] += P.nbytes + tok.nbytes + val.nbytes
+        # the lanes' common leading pages (a radix-shared prefix) cannot change while the lane set is
+        # fixed: new pages are private to their lane, and every lane's context only grows
+        self._n_shared = self._shared_pages(bt[:B], vec[3, :B]) if self.runner.cascade_ok(B) else 0
+        if self._n_shared >= self.runner.min_shared_pages:
+            self.runner.shared_pages.copy_(torch.tensor([self._n_shared], dtype=torch.int32).pin_memory(),
+                                           non_blocking=True)
         self._lanes = list(lanes)
         self._lanes_valid = True
 
@@ -622,8 +664,14 @@ class Engine:
         d = h.to(dev, non_blocking=True)
         btd = torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True)
         greedy = all(r.sampling.greedy for r in lanes)
-        out = self.runner.decode(d[0:B], d[B:2 * B], d[2 * B:3 * B], btd, d[3 * B:4 * B], B,
-                                 use_graph=self._graphs_ready, shared=d[4 * B:4 * B + 1], n_shared=int(shared[0]))
+        if not greedy and self.runner.coll is not None:
+            # the tensor-parallel greedy graph never gathers the full logits: run the step eagerly
+            self.runner.decode_eager(d[0:B], d[B:2 * B], d[2 * B:3 * B], btd, d[3 * B:4 * B], B, greedy=False)
+            out = self.runner.next_ids[:B]
+        else:
+            out = self.runner.decode(d[0:B], d[B:2 * B], d[2 * B:3 * B], btd, d[3 * B:4 * B], B,
+                                     use_graph=self._graphs_ready, shared=d[4 * B:4 * B + 1],
+                                     n_shared=int(shared[0]))
         self.stats["h2d_bytes"] += h.numel() * 4 + bt.size * 4
         mb = self.runner.max_batch
         kerr, cerr = self.runner.status[mb:mb + 2].tolist()
@@ -633,7 +681,7 @@ class Engine:
             toks = out.cpu().tolist()
             self.stats["d2h_bytes"] += 4 * B + 8
         else:
-            toks = sample(self._capped(self.runner.logits[:B]), [r.sampling for r in lanes], lanes)
+            toks = self._sample_rows(self.runner.logits[:B], lanes)
             self.stats["d2h_bytes"] += 8 * B
         self.stats["decode_tokens"] += B
         for r, tok in zip(lanes, toks):
@@ -655,13 +703,20 @@ class Engine:
         return int(k if same.all() else np.argmin(same))
 
     def _run_decode_spec(self, lanes: list[Request], k: int) -> None:
-        """Greedy self-speculative decode (reference: spec.SpeculativeGreedy, internal/spec/spec.go:214-300).
+        """Greedy speculative decode (reference: spec.SpeculativeGreedy, internal/spec/spec.go:214-300).
 
-        The draft (first layers + LM head, sharing the target's KV pages) proposes k tokens per
-        lane; the target verifies all k+1 positions in one forward, each position running as its
-        own attention lane with a causal context length; the longest agreeing prefix plus the
-        target's next token are kept, and the KV of rejected positions is dropped by truncating
-        the lane's KV length (its pages are simply overwritten later)."""
+        Drafts come from ``spec_drafter``: "self" (the target's first layers + LM head, sharing its KV
+        pages), "lookup" (n-gram prompt lookup over the request's own context, no model), "multi"
+        (per request, whichever of the two has been accepted more) or "tree" (several lookup
+        continuations verified as a tree, ``_run_decode_tree``).  The target verifies all k+1
+        positions of a chain in one forward, each position running as its own attention lane with a
+        causal context length; the longest agreeing prefix plus the target's next token are kept,
+        and the KV of rejected positions is dropped by truncating the lane's KV length (its pages are
+        simply overwritten later).  The output is identical to plain greedy decoding."""
+        mode = self.ecfg.spec_drafter
+        if mode == "tree":
+            self._run_decode_tree(lanes, k)
+            return
         ps, dev, B, W = self.ecfg.page_size, self.device, len(lanes), self.bt_width
         bt = np.zeros((B, W), np.int32)
         p0 = np.array([r.n_kv for r in lanes], np.int64)
@@ -673,17 +728,31 @@ class Engine:
             return np.array([pages[b][pos[b] // ps] * ps + pos[b] % ps for b in range(B)], np.int32)
 
         btd = torch.from_numpy(bt).pin_memory().to(dev, non_blocking=True)
-        cur = torch.tensor([r.tokens[-1] for r in lanes], dtype=torch.int32).to(dev)
-        feed = [cur]
-        Ld = self._draft_layers()
-        for j in range(k):
-            pos = np.minimum(p0 + j, self.max_context - 1)
-            h = torch.from_numpy(np.concatenate([pos.astype(np.int32), slots(pos), (pos + 1).astype(np.int32)]))
-            d = h.pin_memory().to(dev, non_blocking=True)
-            out = self.runner.decode(feed[-1], d[0:B], d[B:2 * B], btd, d[2 * B:3 * B], B,
-                                     use_graph=self._graphs_ready, n_layers=Ld)
-            feed.append(out.clone())
-        toks = torch.stack(feed, 1).reshape(-1)                # lane (b, j): token fed at p0 + j
+        cur = [r.tokens[-1] for r in lanes]
+        self_drafts = None
+        if mode in ("self", "multi"):
+            feed = [torch.tensor(cur, dtype=torch.int32).to(dev)]
+            Ld = self._draft_layers()
+            for j in range(k):
+                pos = np.minimum(p0 + j, self.max_context - 1)
+                h = torch.from_numpy(np.concatenate([pos.astype(np.int32), slots(pos), (pos + 1).astype(np.int32)]))
+                d = h.pin_memory().to(dev, non_blocking=True)
+                out = self.runner.decode(feed[-1], d[0:B], d[B:2 * B], btd, d[2 * B:3 * B], B,
+                                         use_graph=self._graphs_ready, n_layers=Ld)
+                feed.append(out.clone())
+            self_drafts = torch.stack(feed[1:], 1).cpu().numpy()
+        drafts = np.zeros((B, k), np.int64)
+        for b, r in enumerate(lanes):
+            if mode == "self":
+                drafts[b] = self_drafts[b]
+                continue
+            dr = self._drafter(r)
+            if mode == "multi":
+                dr.members[1][1].pending = list(self_drafts[b])
+            prop = list(dr.draft(k))[:k]
+            drafts[b] = prop + [cur[b]] * (k - len(prop))    # pad: a rejected filler, never a loss
+        toks_h = np.concatenate([np.asarray(cur, np.int64)[:, None], drafts], 1).astype(np.int32)
+        toks = torch.from_numpy(toks_h.reshape(-1)).pin_memory().to(dev, non_blocking=True)
         V = B * (k + 1)
         vpos = (p0[:, None] + np.arange(k + 1)[None, :]).reshape(-1)
         vpos = np.minimum(vpos, self.max_context - 1)
@@ -694,23 +763,153 @@ class Engine:
         tgt = self.runner.decode(toks, d[0:V], d[V:2 * V], vbt, d[2 * V:3 * V], V, use_graph=self._graphs_ready)
         t_host = tgt.view(B, k + 1).cpu().numpy()
         self.stats["spec_steps"] = self.stats.get("spec_steps", 0) + 1
-        d_host = toks.view(B, k + 1).cpu().numpy()[:, 1:]
         self.stats["h2d_bytes"] += bt.size * 4 + (k + 1) * 12 * B + 12 * V
         self.stats["d2h_bytes"] += 8 * V
         for b, r in enumerate(lanes):
             acc = 0
-            while acc < k and d_host[b, acc] == t_host[b, acc]:
+            while acc < k and drafts[b, acc] == t_host[b, acc]:
                 acc += 1
             self.stats["spec_proposed"] = self.stats.get("spec_proposed", 0) + k
             self.stats["spec_accepted"] = self.stats.get("spec_accepted", 0) + acc
-            emitted = list(d_host[b, :acc]) + [t_host[b, acc]]
+            emitted = [int(x) for x in drafts[b, :acc]] + [int(t_host[b, acc])]
+            if mode != "self":
+                self._drafter(r).commit(emitted)
             for t in emitted:
                 if r.finished:
                     break
                 r.n_kv += 1
-                self._emit(r, int(t))
+                self._emit(r, t)
         self.stats["decode_tokens"] += B
         self.running = [r for r in self.running if not r.finished]
+
+    def _drafter(self, r: Request):
+        """The request's drafter, created on first use over its tokens so far (kept in step with
+        the committed tokens by the spec paths)."""
+        from .drafters import LookupDrafter, MultiDrafter, TreeLookupDrafter
+        dr = getattr(r, "drafter", None)
+        if dr is None:
+            mode = self.ecfg.spec_drafter
+            if mode == "tree":
+                dr = TreeLookupDrafter(r.tokens, width=self.ecfg.spec_tree_width)
+            elif mode == "multi":
+                dr = MultiDrafter([("lookup", LookupDrafter(r.tokens)), ("self", _Pending())])
+            else:
+                dr = LookupDrafter(r.tokens)
+            r.drafter = dr
+        return dr
+
+    def _run_decode_tree(self, lanes: list[Request], depth: int) -> None:
+        """Greedy tree speculation (reference: spec.VerifyTree, internal/spec/verify.go:54-122).
+
+        Each lane's drafter proposes a token tree; every root-to-leaf path becomes a chain of
+        decode lanes (its positions base .. base + d, each lane attending causally along its own
+        path).  A chain gets private copies of the request's partial tail page, so sibling
+        branches writing the same positions never collide.  The accepted path is the longest one
+        whose tokens equal the target's greedy tokens; the pages of a chain holding it replace
+        the request's tail pages (no copy of the accepted K/V), the rest are released."""
+        from ..ops import kernels as K
+        from .drafters import accept_tree
+        ps, dev, W = self.ecfg.page_size, self.device, self.bt_width
+        lane_tok, lane_pos, lane_slot, lane_bt = [], [], [], []
+        plans = []
+        budget = self.ecfg.max_batch
+        src_slots, dst_slots = [], []
+        for r in lanes:
+            dr = self._drafter(r)
+            tree = dr.propose(depth)
+            base = r.n_kv
+            pg0 = base // ps
+            leaves = tree.leaves() if tree.tokens else []
+            chains = [tree.path(l) for l in leaves] or [[]]
+            chains = [c[:max(0, min(len(c), self.max_context - 1 - base))] for c in chains]
+            # at most the lanes that still fit this step (a chain of d nodes takes d + 1 lanes)
+            keep = []
+            for c in chains:
+                if budget - (len(c) + 1) < 0:
+                    break
+                keep.append(c)
+                budget -= len(c) + 1
+            if not keep:
+                keep = [[]]
+            priv = []
+            for c in keep:
+                n_tail = (base + len(c)) // ps - pg0 + 1
+                try:
+                    pages = self._alloc(n_tail)
+                except OutOfPages:
+                    for p_ in priv:
+                        self.pool.release(p_)
+                    self._release_plans(plans)
+                    self._run_decode_sync_plain(lanes)
+                    return
+                priv.append(pages)
+                for q in range(pg0 * ps, base):          # the committed rows of the partial tail page
+                    src_slots.append(r.pages[q // ps] * ps + q % ps)
+                    dst_slots.append(pages[0] * ps + q % ps)
+            plans.append((r, tree, base, pg0, keep, priv, len(lane_tok)))
+            for c, pages in zip(keep, priv):
+                row = np.zeros(W, np.int32)
+                row[:pg0] = r.pages[:pg0]
+                row[pg0:pg0 + len(pages)] = pages
+                feed = [r.tokens[-1]] + [tree.tokens[i] for i in c]
+                for j, t in enumerate(feed):
+                    p = base + j
+                    lane_tok.append(t)
+                    lane_pos.append(p)
+                    lane_slot.append(pages[p // ps - pg0] * ps + p % ps)
+                    lane_bt.append(row)
+        if src_slots:
+            z = torch.zeros(len(src_slots), dtype=torch.uint8, device=dev)
+            one = torch.ones(self.cfg.head_dim // 2, dtype=torch.float32, device=dev)
+            K.kv_move(self.kv, torch.tensor(src_slots, dtype=torch.int32, device=dev),
+                      torch.tensor(dst_slots, dtype=torch.int32, device=dev), z, one, one * 0)
+        V = len(lane_tok)
+        to = lambda a: torch.from_numpy(np.asarray(a, np.int32)).pin_memory().to(dev, non_blocking=True)
+        tgt = self.runner.decode(to(lane_tok), to(lane_pos), to(lane_slot), to(np.stack(lane_bt)),
+                                 to(np.asarray(lane_pos) + 1), V, use_graph=self._graphs_ready)
+        t_host = tgt.cpu().numpy()
+        self.stats["spec_steps"] = self.stats.get("spec_steps", 0) + 1
+        self.stats["h2d_bytes"] += 16 * V + V * W * 4
+        self.stats["d2h_bytes"] += 4 * V
+        for r, tree, base, pg0, keep, priv, off in plans:
+            node_tgt = [0] * len(tree.tokens)
+            root_tgt = int(t_host[off])
+            o = off
+            for c in keep:
+                for j, i in enumerate(c):
+                    node_tgt[i] = int(t_host[o + 1 + j])
+                o += len(c) + 1
+            path, committed = accept_tree(tree, root_tgt, node_tgt)
+            win = next(ci for ci, c in enumerate(keep) if c[:len(path)] == path)
+            self.stats["spec_proposed"] = self.stats.get("spec_proposed", 0) + len(tree.tokens)
+            self.stats["spec_accepted"] = self.stats.get("spec_accepted", 0) + len(path)
+            # the winning chain's pages hold the committed rows and the accepted path's K/V
+            self.pool.release(r.pages[pg0:])
+            r.pages = r.pages[:pg0] + priv[win]
+            for ci, pages in enumerate(priv):
+                if ci != win:
+                    self.pool.release(pages)
+            r.drafter.commit(committed)
+            for t in committed:
+                if r.finished:
+                    break
+                r.n_kv += 1
+                self._emit(r, int(t))
+        self.stats["decode_tokens"] += len(lanes)
+        self.running = [r for r in self.running if not r.finished]
+
+    def _release_plans(self, plans) -> None:
+        for _, _, _, _, _, priv, _ in plans:
+            for pages in priv:
+                self.pool.release(pages)
+
+    def _run_decode_sync_plain(self, lanes: list[Request]) -> None:
+        """Fallback of the tree path when private pages run out: one plain decode step."""
+        k, self.ecfg.spec_k = self.ecfg.spec_k, 0
+        try:
+            self._run_decode_sync()
+        finally:
+            self.ecfg.spec_k = k
 
     def _preempt(self, r: Request) -> None:
         """Out of pages: give this request's pages back.  Swap mode copies their K/V to pinned host
@@ -766,3 +965,17 @@ class Engine:
         reqs = [self.add_request(p, max_new_tokens, sampling, stop_ids) for p in prompts]
         self.run_until_done(reqs)
         return [r.full_output for r in reqs]
+
+
+class _Pending:
+    """A multi-drafter member whose proposal for the round (the batch's self-draft) is set before
+    the round's draft call."""
+
+    def __init__(self):
+        self.pending: list[int] = []
+
+    def draft(self, k: int) -> list[int]:
+        return [int(t) for t in self.pending[:k]]
+
+    def commit(self, tokens: list[int]) -> None:
+        pass

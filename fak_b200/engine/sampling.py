@@ -3,11 +3,19 @@
 Semantics follow the reference's in-kernel sampler (internal/agent/inkernel_sampling.go:21-185):
 penalties are applied to raw logits from the tokens generated so far, then temperature,
 then top-k and top-p truncation; temperature 0 is greedy (first index of the max).
+
+The serving path samples on the device (``csrc/kernels/sampler.cu``, one CTA per row inside the
+decode graph): ``pack_params`` lays out each row's parameters and ``device_sample`` runs the kernel
+on a block of logit rows (prefill's first tokens, the synchronous loop).  The draw of a request is
+keyed by its seed and the number of tokens it has generated (Philox), so it does not depend on the
+batch it runs in.  ``sample`` / ``sample_row`` are the host path kept for guided decoding (token
+masks computed on the host).
 """
 from __future__ import annotations
 
 import dataclasses
 
+import numpy as np
 import torch
 
 from .constraints import LogitMask, apply_constraint, guided_decode_enabled
@@ -68,3 +76,73 @@ def sample(logits: torch.Tensor, params: list[SamplingParams], reqs) -> list[int
     if all(p.greedy for p in params):
         return torch.argmax(logits, dim=-1).tolist()
     return [sample_row(logits[i], params[i], list(reqs[i].full_output)) for i in range(len(params))]
+
+
+# ------------------------------------------------------------------------------ device sampler
+MAX_BIAS = 4096      # logit-bias entries of one decode batch (all lanes together)
+
+
+def request_seed(engine_seed: int, rid: int) -> int:
+    """A 64-bit seed for a request without one (splitmix64 of the engine seed and the request id)."""
+    z = (int(engine_seed) * 0x9E3779B97F4A7C15 + int(rid) + 0x632BE59BD9B4E019) & 0xFFFFFFFFFFFFFFFF
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & 0xFFFFFFFFFFFFFFFF
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & 0xFFFFFFFFFFFFFFFF
+    return z ^ (z >> 31)
+
+
+def pack_params(sps: list[SamplingParams], steps: list[int], seeds: list[int]
+                ) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Rows of the device sampler's 10-word parameter block (temperature, top_k, top_p, frequency and
+    presence penalty, bias offset / count, seed lo / hi, step) and the flat logit-bias lists."""
+    n = len(sps)
+    f = np.zeros((n, 10), np.float32)
+    w = f.view(np.int32)
+    tok: list[int] = []
+    val: list[float] = []
+    for b, (sp, st, sd) in enumerate(zip(sps, steps, seeds)):
+        f[b, 0] = sp.temperature
+        w[b, 1] = int(sp.top_k)
+        f[b, 2] = sp.top_p
+        f[b, 3] = sp.frequency_penalty
+        f[b, 4] = sp.presence_penalty
+        bias = sorted((sp.logit_bias or {}).items())
+        w[b, 5] = len(tok)
+        w[b, 6] = len(bias)
+        tok += [int(t) for t, _ in bias]
+        val += [float(v) for _, v in bias]
+        w[b, 7] = np.uint32(sd & 0xFFFFFFFF).view(np.int32)
+        w[b, 8] = np.uint32((sd >> 32) & 0xFFFFFFFF).view(np.int32)
+        w[b, 9] = int(st)
+    if len(tok) > MAX_BIAS:
+        raise ValueError(f"logit_bias entries of one batch exceed {MAX_BIAS}")
+    return w.copy(), np.asarray(tok, np.int32), np.asarray(val, np.float32)
+
+
+def count_rows(generated: list[list[int]], V: int, device) -> torch.Tensor:
+    """int32 [B, V]: how often each token appears in each row's generated tokens."""
+    c = torch.zeros(len(generated), V, dtype=torch.int32, device=device)
+    rows = [b for b, g in enumerate(generated) for _ in g]
+    cols = [t for g in generated for t in g]
+    if rows:
+        c.index_put_((torch.tensor(rows, device=device), torch.tensor(cols, device=device)),
+                     torch.ones(len(rows), dtype=torch.int32, device=device), accumulate=True)
+    return c
+
+
+def needs_counts(sps: list[SamplingParams]) -> bool:
+    return any(sp.frequency_penalty != 0.0 or sp.presence_penalty != 0.0 for sp in sps)
+
+
+def device_sample(logits: torch.Tensor, V: int, sps: list[SamplingParams], steps: list[int], seeds: list[int],
+                  generated: list[list[int]], softcap: float = 0.0) -> list[int]:
+    """Draw one token per row of ``logits`` [n, >=V] f32 on the device (the rows are modified)."""
+    from ..ops import kernels as K
+    dev = logits.device
+    P, tok, val = pack_params(sps, steps, seeds)
+    p = torch.from_numpy(P).to(dev)
+    bt = torch.from_numpy(tok if len(tok) else np.full(1, -1, np.int32)).to(dev)
+    bv = torch.from_numpy(val if len(val) else np.zeros(1, np.float32)).to(dev)
+    counts = count_rows(generated, V, dev) if needs_counts(sps) else None
+    out = torch.empty(len(sps), dtype=torch.int32, device=dev)
+    K.sample_rows(logits, V, p, bt, bv, counts, out, len(sps), softcap)
+    return out.tolist()

@@ -143,6 +143,13 @@ class ModelRunner:
         if collectives is not None and hasattr(collectives, "err"):
             collectives.err = self.status[B + 1:B + 2]
         K.register_error_word(dev, self.err)
+        # device sampler (sampled decode steps): per-lane parameter rows, the batch's logit-bias lists
+        # and each lane's generated-token counts (frequency / presence penalties)
+        from ..engine.sampling import MAX_BIAS
+        self.samp_params = torch.zeros(B, 10, dtype=torch.int32, device=dev)
+        self.bias_tok = torch.full((MAX_BIAS,), -1, dtype=torch.int32, device=dev)
+        self.bias_val = torch.zeros(MAX_BIAS, dtype=torch.float32, device=dev)
+        self.counts = torch.zeros(B, cfg.vocab_size, dtype=torch.int32, device=dev)
         self.max_split = 64
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
         self.n_split = int(os.environ.get("FAK_DEC_SPLITS", "0")) or 16
@@ -253,18 +260,21 @@ class ModelRunner:
             self.coll.decode_down(self, i, B)
 
     def decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True, n_layers: int | None = None,
-                     cascade: bool = False) -> None:
+                     cascade: bool = False, sampled: bool = False) -> None:
         self._casc_on = cascade
         try:
-            self._decode_eager(ids, pos, slot, bt, ctx, B, greedy, n_layers)
+            self._decode_eager(ids, pos, slot, bt, ctx, B, greedy, n_layers, sampled)
         finally:
             self._casc_on = False
 
-    def _decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True, n_layers: int | None = None) -> None:
+    def _decode_eager(self, ids, pos, slot, bt, ctx, B: int, greedy: bool = True, n_layers: int | None = None,
+                      sampled: bool = False) -> None:
         """One decode step for B lanes; results in self.logits[:B] / self.next_ids[:B].
 
         ``n_layers`` < cfg.n_layers runs only the first layers before the final norm and LM head:
-        the early-exit draft model of self-speculative decoding (its KV pages are the target's)."""
+        the early-exit draft model of self-speculative decoding (its KV pages are the target's).
+        ``sampled``: every lane draws its token with the device sampler (``samp_params`` rows, greedy
+        rows included), from the full logits (gathered across tensor-parallel ranks)."""
         cfg = self.cfg
         n_split = self.n_split_for(B)
         K.embed(self.w.embed, ids, self.x[:B], None, self.err, scale=cfg.embed_scale)
@@ -275,12 +285,24 @@ class ModelRunner:
         else:
             K.quant_act(self.x[:B], self.act_d, self.w.final_norm, cfg.rms_eps)
             self.lm_in = self.act_d
+        if sampled:
+            rows, V = self._lm_head_full(B)
+            K.sample_rows(rows, V, self.samp_params[:B], self.bias_tok, self.bias_val, self.counts[:B],
+                          self.next_ids[:B], B, cfg.final_softcap)
+            return
         if greedy and self.coll is not None and hasattr(self.coll, "lm_head_greedy"):
             self.coll.lm_head_greedy(self, B)  # sharded logits -> distributed argmax, no logits gather
             return
         self._lm_head(B)
         if greedy:
             K.argmax(self.logits[:B], self.logits.shape[1], self.next_ids[:B])
+
+    def _lm_head_full(self, B: int) -> tuple[torch.Tensor, int]:
+        """Full-vocabulary logit rows [B, >=V] of the step and the column count to sample over."""
+        if self.coll is not None and hasattr(self.coll, "lm_head_rows"):
+            return self.coll.lm_head_rows(self, B)
+        self._lm_head(B)
+        return self.logits[:B], self.cfg.vocab_size
 
     def _lm_head(self, B: int) -> None:
         if self.coll is None:
@@ -312,41 +334,52 @@ class ModelRunner:
         """Capture the B-lane step: the plain variant, and (target model, cascade possible) the
         cascade variant replayed when the lanes share enough prefix pages."""
         st = self._static_inputs(B, bt_width)
-        variants = [False] + ([True] if n_layers is None and self.cascade_ok(B) else [])
-        for casc in variants:
+        variants = [(False, False)]
+        if n_layers is None:
+            variants += [(True, False)] if self.cascade_ok(B) else []
+            variants += [(False, True)]     # sampled lanes: the device sampler instead of the argmax
+        for casc, samp in variants:
             # warm up (also triggers lazy cudaFuncSetAttribute) on a side stream, then capture
             s = torch.cuda.Stream(device=self.device)
             s.wait_stream(torch.cuda.current_stream(self.device))
+            saved = self.samp_params[:B].clone()
             with torch.cuda.stream(s):
                 self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers,
-                                  cascade=casc)
+                                  cascade=casc, sampled=samp)
             torch.cuda.current_stream(self.device).wait_stream(s)
             torch.cuda.synchronize(self.device)
+            self.samp_params[:B].copy_(saved)      # the warm-up advanced the lanes' draw counters
             g = torch.cuda.CUDAGraph()
             before = K.launches()
             with torch.cuda.graph(g):
                 self.decode_eager(st["ids"], st["pos"], st["slot"], st["bt"], st["ctx"], B, n_layers=n_layers,
-                                  cascade=casc)
+                                  cascade=casc, sampled=samp)
                 if n_layers is None:
                     # the step's tokens become the next step's inputs on the device (idle lanes stay idle)
                     K.decode_advance(self.next_ids, st["ids"], st["pos"], st["slot"], st["ctx"], st["bt"], B)
-            key = (B, n_layers, casc)
+            key = (B, n_layers, casc, samp)
             self._graph_kernels[key] = K.launches() - before
             K._launches[0] = before
             self._graphs[key] = (g, st)
 
-    def replay_resident(self, B: int) -> None:
+    def replay_resident(self, B: int, n_shared: int = 0, sampled: bool = False) -> None:
         """One decode step of the device-resident lanes [0, B) (their inputs already in the shared
-        static buffers, lanes [B, bucket) idle); the graph ends by advancing the lanes' inputs."""
-        bucket = self.graph_bucket(B, None, False)
+        static buffers, lanes [B, bucket) idle); the graph ends by advancing the lanes' inputs.
+        ``n_shared``: the lanes' common leading pages (``shared_pages`` already holds the count on
+        the device); with at least ``min_shared_pages`` the cascade variant runs.  ``sampled``: the
+        variant that draws every lane's token with the device sampler (``samp_params`` filled)."""
+        casc = (not sampled and n_shared >= self.min_shared_pages
+                and self.graph_bucket(B, None, True) is not None)
+        bucket = self.graph_bucket(B, None, casc, sampled)
         if bucket is None:
             raise RuntimeError(f"no captured decode graph holds {B} lanes")
-        g, _ = self._graphs[(bucket, None, False)]
+        g, _ = self._graphs[(bucket, None, casc, sampled)]
         g.replay()
-        K.count(self._graph_kernels[(bucket, None, False)])
+        K.count(self._graph_kernels[(bucket, None, casc, sampled)])
 
-    def graph_bucket(self, B: int, n_layers: int | None = None, cascade: bool = False) -> int | None:
-        cands = [b for b, nl, c in self._graphs if b >= B and nl == n_layers and c == cascade]
+    def graph_bucket(self, B: int, n_layers: int | None = None, cascade: bool = False,
+                     sampled: bool = False) -> int | None:
+        cands = [b for b, nl, c, sm in self._graphs if b >= B and nl == n_layers and c == cascade and sm == sampled]
         return min(cands) if cands else None
 
     def decode(self, ids, pos, slot, bt, ctx, B: int, use_graph: bool = True, n_layers: int | None = None,
@@ -366,7 +399,7 @@ class ModelRunner:
         if bucket is None:
             self.decode_eager(ids, pos, slot, bt, ctx, B, n_layers=n_layers, cascade=casc and self.cascade_ok(B))
             return self.next_ids[:B]
-        g, st = self._graphs[(bucket, n_layers, casc)]
+        g, st = self._graphs[(bucket, n_layers, casc, False)]
         st["ids"][:B].copy_(ids)
         st["pos"][:B].copy_(pos)
         st["slot"][:B].copy_(slot)
@@ -377,7 +410,7 @@ class ModelRunner:
             st["ctx"][B:].fill_(1)
             st["slot"][B:].fill_(-1)
         g.replay()
-        K.count(self._graph_kernels[(bucket, n_layers, casc)])
+        K.count(self._graph_kernels[(bucket, n_layers, casc, False)])
         return self.next_ids[:B]
 
     # ------------------------------------------------------------------------------------

@@ -49,6 +49,15 @@ def decode_advance(next_ids, ids, pos, slot, ctx, bt, B: int) -> None:
     count()
 
 
+def sample_rows(logits: torch.Tensor, V: int, params: torch.Tensor, bias_tok: torch.Tensor, bias_val: torch.Tensor,
+                counts: torch.Tensor | None, out: torch.Tensor, B: int, softcap: float = 0.0) -> None:
+    """One token per row of logits [B, >=V] (modified in place): soft-cap, penalties from ``counts``,
+    clamped logit bias, temperature / top-k / top-p and a Philox draw keyed by each row's (seed, step);
+    params int32 [B, 10] (engine.sampling.pack_params; the step word is advanced)."""
+    ext().sample_rows(logits, V, params, bias_tok, bias_val, counts, out, B, softcap)
+    count()
+
+
 def scatter_i32(dst: torch.Tensor, idx_val: torch.Tensor, n: int) -> None:
     """dst.flatten()[idx_val[i, 0]] = idx_val[i, 1] for i < n (device tensors)."""
     ext().scatter_i32(dst, idx_val, n)

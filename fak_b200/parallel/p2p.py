@@ -37,6 +37,7 @@ from .tp import NcclTP
 MAX_CTAS = 64
 MAX_W = 8
 AR_CTAS = 16
+AG_CTAS = 16
 
 
 def _align(n: int, a: int = 256) -> int:
@@ -89,7 +90,7 @@ class P2PTP(NcclTP):
         B, d, L = max_batch, cfg.d_model, cfg.n_layers
         self.B = B
         self.spin_limit = int(spin_limit)
-        self.n_sites = 3 * L + 1
+        self.n_sites = 3 * L + 2
         off = 0
         self.flags_off = off
         off = _align(off + self.n_sites * MAX_CTAS * MAX_W * 4)
@@ -103,6 +104,10 @@ class P2PTP(NcclTP):
         off = _align(off + 2 * MAX_W * self.ar_tiles * 4 * 128 * 4)
         self.arflags_off = off
         off = _align(off + self.ar_tiles * MAX_W * 4)
+        # sampled steps: full-vocabulary logit rows [B, W * Vl], rank r's shard at columns [r Vl, (r+1) Vl)
+        self.lg_ok = self.Vl % 4 == 0
+        self.lg_off = off
+        off = _align(off + (B * self.world * self.Vl * 4 if self.lg_ok else 0))
         self.nbytes = off
         self.mem = None
         if os.environ.get("FAK_P2P_MEM", "ipc") == "symm":
@@ -120,6 +125,8 @@ class P2PTP(NcclTP):
         self.counters = torch.zeros(self.n_sites * MAX_CTAS, dtype=torch.int32, device=device)
         self.ar_epochs = torch.zeros(self.ar_tiles, dtype=torch.int32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)   # replaced by the runner's status word
+        if self.lg_ok:
+            self._rows().fill_(float("-inf"))     # shard tails past the real vocabulary stay -inf
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
         self.v_off = self.rank * self.Vl
@@ -160,6 +167,27 @@ class P2PTP(NcclTP):
 
     def decode_down(self, rn, i: int, B: int) -> None:
         self._row_parallel(rn, rn.w.layers[i].down, rn.ffn_in, B, i, 1)
+
+    def _rows(self) -> torch.Tensor:
+        n = self.B * self.world * self.Vl
+        return self.buf[self.lg_off:self.lg_off + 4 * n].view(torch.float32).view(self.B, self.world * self.Vl)
+
+    def lm_head_rows(self, rn, B: int) -> tuple[torch.Tensor, int]:
+        """Full logit rows for the device sampler: this rank's vocab shard written into its columns of
+        the gathered rows, then pushed to every rank by the in-kernel all-gather (no NCCL); every rank
+        then samples the same rows and draws the same tokens."""
+        if not self.lg_ok:
+            self.lm_head(rn, B)
+            return rn.logits[:B], self.cfg.vocab_size
+        rows = self._rows()
+        c0 = self.rank * self.Vl
+        K.gemv(rn.w.lm_head, rn.lm_in, B, rows[:B, c0:c0 + self.Vl_real], None, K.EPI_STORE)
+        ld = self.world * self.Vl * 4
+        ext().p2p_allgather_cols(self.peers, self.buf[self.lg_off:], ld, self.lg_off, ld, c0 * 4, self.Vl * 4, B,
+                                 self.flags_off, 3 * self.cfg.n_layers + 1, self.me, self.counters, self.err, AG_CTAS,
+                                 spin_limit=self.spin_limit)
+        K.count()
+        return rows[:B], self.world * self.Vl
 
     def lm_head_greedy(self, rn, B: int) -> None:
         """Local vocab-shard logits, then the distributed first-index argmax into rn.next_ids."""

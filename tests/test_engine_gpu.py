@@ -166,6 +166,28 @@ def test_self_speculative_decode_matches_greedy(model_file):
         assert eng.stats["spec_proposed"] > 0
 
 
+@pytest.mark.parametrize("drafter", ["lookup", "multi", "tree"])
+def test_drafted_speculation_matches_greedy(model_file, drafter):
+    """Lookup, multi (self vs lookup) and tree speculation emit exactly the greedy tokens; prompts
+    repeat a pattern so the lookup drafters find continuations to propose."""
+    from fak_b200.engine import Engine
+    base = _engine(model_file, graphs=True)
+    rng = np.random.default_rng(12)
+    pat = rng.integers(0, base.cfg.vocab_size, 9).tolist()
+    prompts = [pat * 5 + rng.integers(0, base.cfg.vocab_size, 3).tolist(), pat[:4] * 6,
+               rng.integers(0, base.cfg.vocab_size, 31).tolist()]
+    want = base.generate(prompts, max_new_tokens=24)
+    ecfg = EngineConfig(max_batch=32, kv_pages=1024, cuda_graph=True, graph_batch_buckets=(1, 2, 4, 8, 16, 32),
+                        spec_k=4, spec_draft_layers=1, spec_drafter=drafter, spec_tree_width=3)
+    eng = Engine.from_gguf(model_file, ecfg, "cuda", max_context=1024)
+    eng.warmup_graphs()
+    got = eng.generate(prompts, max_new_tokens=24)
+    assert got == want, (drafter, got, want)
+    assert eng.stats["spec_proposed"] > 0
+    # no page leaks: every page not free is held by the radix cache
+    assert eng.pool.n_free() + eng.radix.stats()["cached_pages"] == eng.pool.n_pages - 1
+
+
 @pytest.mark.parametrize("include_kv", [False, True])
 def test_session_checkpoint_restore(model_file, tmp_path, include_kv):
     """Checkpoint mid-generation, restore into a fresh engine, finish: the cached prefixes come back
