@@ -24,6 +24,7 @@
 #include <mutex>
 
 #include "mma.cuh"
+#include "fak_noalloc.h"
 
 using namespace fak;
 
@@ -854,41 +855,19 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
 
 // =============================================================================================
 // fak_decode_attention_noalloc: the split-KV decode attention above, as one C entry point that
-// allocates nothing.  This entry point has no counterpart in the reference.
-//
-// Who needs it: a caller that links this library through its C ABI without PyTorch (a C/C++
-// host runtime, or Python through ctypes) has no caching allocator that can hand it a split-KV
-// workspace, and a cudaMalloc/cudaFree pair per call would both cost more than the kernel and,
-// through cudaFree, wait for the whole device.  A server that sizes its memory once at start-up
-// (the KV page pool takes nearly all of HBM) also wants no allocation inside its decode loop,
-// where an out-of-memory error could only surface long after admission.  So the partial results
-// of the split-KV pass live in one statically sized device array of this file, and the call
-// touches no allocator: no cudaMalloc, no cudaFree, no torch tensor.
-//
-// Limit: B * H * n_split <= kNoAllocSlots (4096) (sequence, head, split) slots with head_dim <= 128,
-// i.e. 4096 * 130 floats = 2,129,920 bytes of scratch.  Larger calls are rejected with an error
-// message and launch nothing.  n_split == 1 uses no scratch and has no size limit.
-//
-// Set-up: the first call on a device (that device current) looks the scratch array up with
-// cudaGetSymbolAddress and caches the pointer for that device; make that first call before any
-// stream capture begins.  Nothing in the scratch must start at zero -- the attention kernel writes
-// every (sequence, head, split) slot, an empty split included, before the merge kernel reads it --
-// so nothing is cleared.
-//
-// Concurrency: there is one scratch array per device, so two calls in flight on the same device at
-// the same time (different streams, or different host threads without ordering) race on it and
-// corrupt each other's results.  Issue them on one stream or order them yourself.
-//
-// Returns 0 on success; 1 for an invalid argument, 2 for a call beyond the scratch limit, 3 for a
-// CUDA error.  On failure a message is written to err (err_len bytes, may be null).
+// allocates nothing.  This entry point has no counterpart in the reference.  Its declaration, the
+// callers it serves (runtimes that cannot allocate device memory while they run), its limits, the
+// set-up rule and the concurrency rule are in fak_noalloc.h beside this file; the definition
+// below must keep that signature (the header is included above, so the compiler checks it).
 // =============================================================================================
 namespace {
-constexpr int64_t kNoAllocSlots = 4096;
+constexpr int64_t kNoAllocSlots = FAK_NOALLOC_MAX_SLOTS;
 constexpr int kNoAllocMaxD = 128;
 constexpr int kNoAllocMaxDevices = 64;
 __device__ __align__(256) float g_noalloc_scratch[kNoAllocSlots * (kNoAllocMaxD + 2)];
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+static_assert(sizeof(g_noalloc_scratch) == 2129920, "the scratch size stated in fak_noalloc.h");
 
 template <typename... A>
 int noalloc_fail(char* err, size_t err_len, int code, const char* fmt, A... a) {
@@ -906,40 +885,40 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     float* ds, int ldo, void* stream, char* err, size_t err_len) {
   if (err && err_len) err[0] = 0;
   if (!q || !k_cache || !v_cache || !block_table || !ctx_len)
-    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: null input pointer");
-  if (!out && !qx) return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: no output (out or qx)");
-  if (qx && !ds) return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: qx given without ds");
+    return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: null input pointer");
+  if (!out && !qx) return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: no output (out or qx)");
+  if (qx && !ds) return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: qx given without ds");
   if (D != 64 && D != 128)
-    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: head dim %d (must be 64 or 128)", D);
+    return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: head dim %d (must be 64 or 128)", D);
   if (B < 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0 || H / Hkv > 16)
-    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: heads %d / kv heads %d (GQA group <= 16)", H,
+    return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: heads %d / kv heads %d (GQA group <= 16)", H,
                         Hkv);
   if (n_split < 1 || pages_per_split < 1 || bt_stride < 1)
-    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: n_split, pages_per_split, bt_stride >= 1");
+    return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: n_split, pages_per_split, bt_stride >= 1");
   if (ldo <= 0) ldo = H * D;
   if (ldo < H * D || ldo % 32 != 0)
-    return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: output row stride %d", ldo);
+    return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: output row stride %d", ldo);
   const int64_t slots = (int64_t)B * H * n_split;
   if (n_split > 1 && slots > kNoAllocSlots)
-    return noalloc_fail(err, err_len, 2,
+    return noalloc_fail(err, err_len, FAK_NOALLOC_ETOOBIG,
                         "fak_decode_attention_noalloc: B*H*n_split = %lld exceeds the static scratch limit of %lld "
                         "slots (%lld bytes); use fewer splits or the allocating entry point",
                         (long long)slots, (long long)kNoAllocSlots,
                         (long long)(kNoAllocSlots * (kNoAllocMaxD + 2) * sizeof(float)));
-  if (B == 0) return 0;
+  if (B == 0) return FAK_NOALLOC_OK;
 
   float* pw = nullptr;
   if (n_split > 1) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, FAK_NOALLOC_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= kNoAllocMaxDevices)
-      return noalloc_fail(err, err_len, 1, "fak_decode_attention_noalloc: device %d out of range", dev);
+      return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: device %d out of range", dev);
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (!g_noalloc_ptr[dev]) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-      if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      if (e != cudaSuccess) return noalloc_fail(err, err_len, FAK_NOALLOC_ECUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
       g_noalloc_ptr[dev] = static_cast<float*>(p);
     }
     pw = g_noalloc_ptr[dev];
@@ -972,7 +951,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
                              pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0,
                              nullptr, 0, n_split, 0.f, 0.f);
   }
-  if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode attention launch: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) return noalloc_fail(err, err_len, FAK_NOALLOC_ECUDA, "decode attention launch: %s", cudaGetErrorString(e));
   if (n_split > 1) {
     cudaLaunchConfig_t c2 = {};
     c2.gridDim = dim3(B, H);
@@ -984,7 +963,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     else
       e = cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
                              dp, ldo);
-    if (e != cudaSuccess) return noalloc_fail(err, err_len, 3, "decode combine launch: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return noalloc_fail(err, err_len, FAK_NOALLOC_ECUDA, "decode combine launch: %s", cudaGetErrorString(e));
   }
-  return 0;
+  return FAK_NOALLOC_OK;
 }
