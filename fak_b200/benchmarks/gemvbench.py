@@ -19,6 +19,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--kernel", default="tgemv", choices=["tgemv", "qmmv", "qgemv"])
     ap.add_argument("--flags", type=int, default=0)
+    ap.add_argument("--unit", type=int, default=0, help="1: activations with one scale per 256 columns")
     args = ap.parse_args(argv)
     from fak_b200.models.weights import QuantWeight
     from fak_b200.ops import kernels as K
@@ -35,7 +36,7 @@ def main(argv=None):
             w.pack()
             w.buf = None  # only the tile-packed copy is streamed
         ws.append(w)
-    act = K.ActQ(max(8, args.batch), args.cols, dev)
+    act = K.ActQ(max(8, args.batch), args.cols, dev, unit=bool(args.unit))
     K.quant_act(torch.randn(args.batch, args.cols, device=dev), act)
     y = torch.zeros(max(8, args.batch), args.rows, device=dev)
     C = ext()
@@ -45,7 +46,7 @@ def main(argv=None):
     def run(w):
         if args.kernel == "tgemv":
             C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q, act.ds, None, None, 0.0, args.batch, y, None, 0, part, cnt,
-                    None, args.flags)
+                    None, args.flags, unit=act.unit)
         elif args.kernel == "qmmv":
             C.qmmv(w.buf, w.qtype, w.rows, w.cols, w.pitch, act.q, act.ds, args.batch, y, None, 0, args.flags)
         else:
@@ -66,7 +67,7 @@ def main(argv=None):
         S, ticket, slices, W, R, smem = C.tgemv_workspace(args.qtype, args.rows, args.cols, 0)
         info = {"slices": slices, "warps": W, "depth": R, "smem": smem}
     print(json.dumps({"kernel": args.kernel, **info, "rows": args.rows, "cols": args.cols, "qtype": args.qtype,
-                      "batch": args.batch, "flags": args.flags, "us": round(us, 2),
+                      "batch": args.batch, "flags": args.flags, "unit": act.unit, "us": round(us, 2),
                       "tb_s": round(nbytes / us / 1e6, 3)}))
 
 

@@ -33,6 +33,9 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--turns", type=int, default=2, help="measured turns per loop mode")
     ap.add_argument("--modes", default="sync,async")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="N > 0: also attribute N async decode steps to kernels (CUPTI activity through "
+                         "torch.profiler; attribution only, the timings above are CUDA events)")
     args = ap.parse_args(argv)
 
     import torch.distributed as dist
@@ -110,6 +113,8 @@ def main(argv=None):
         results[mode] = {"device_ms_per_step_median": round(float(r[0]), 4), "gap_ms_per_step_median": round(float(r[1]), 4),
                          "device_ms_per_step_mean": round(float(r[2]), 4), "gap_ms_per_step_mean": round(float(r[3]), 4),
                          "turn_wall_ms_median": round(float(r[4]), 2)}
+    if args.profile > 0:
+        results["kernels_us_per_step"] = _kernel_profile(eng, turn, args, group, world)
     if rank == 0:
         print(json.dumps({"bench": "stepprof", "model": f"{cfg.name}-arch {args.mix}", "n_gpus": world,
                           "agents": args.agents, "prefix": args.prefix, "decode_steps_per_turn": args.decode - 1,
@@ -117,6 +122,43 @@ def main(argv=None):
     eng.shutdown()
     if group is not None:
         pdist.shutdown()
+
+
+def _kernel_profile(eng, turn, args, group, world) -> dict:
+    """Per-kernel device time of decode steps (us per step, max over ranks), from a profiled turn."""
+    import torch.distributed as dist
+    from torch.profiler import ProfilerActivity, profile
+    eng.ecfg.async_decode = True
+    rn = eng.runner
+    n_steps = [0]
+    real = rn.replay_resident
+
+    def counted(*a, **k):
+        n_steps[0] += 1
+        return real(*a, **k)
+    rn.replay_resident = counted
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        turn()
+        torch.cuda.synchronize()
+    rn.replay_resident = real
+    agg: dict[str, float] = {}
+    for ev in prof.events():
+        if ev.device_type.name != "CUDA":
+            continue
+        name = ev.name.split("(")[0].replace("void ", "").replace("(anonymous namespace)::", "")
+        name = name.replace("<unnamed>::", "")[:48]
+        agg[name] = agg.get(name, 0.0) + ev.device_time
+    # decode steps only: subtract nothing, report per decode step of the profiled turn
+    steps = max(1, n_steps[0])
+    per = {k: v / steps for k, v in agg.items()}
+    if group is not None:
+        allp = [None] * world
+        dist.all_gather_object(allp, per, group=group)
+        keys = set().union(*[set(p) for p in allp])
+        per = {k: max(p.get(k, 0.0) for p in allp) for k in keys}
+    top = sorted(per.items(), key=lambda kv: -kv[1])[:16]
+    return {k: round(v, 2) for k, v in top}
 
 
 if __name__ == "__main__":

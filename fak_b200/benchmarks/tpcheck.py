@@ -108,7 +108,9 @@ def main(argv=None):
             am_ok = [bool(a == b or m < args.tie) for a, b, m in
                      zip(got.argmax(1).tolist(), exp.argmax(1).tolist(), margin)]
             per_prompt.append({"min_cos": round(float(cos.min()), 6), "argmax_agree": all(am_ok),
-                               "min_margin": round(min(margin), 5), "steps": len(margin), "margins": margin})
+                               "min_margin": round(min(margin), 5), "steps": len(margin), "margins": margin,
+                               "cos": [round(float(c), 5) for c in cos.tolist()],
+                               "argmax_ok": am_ok})
     # 2. free-running greedy through the engine (device-resident loop, fused collectives)
     outs = eng.generate(prompts, args.new)
     mb = eng.runner.max_batch

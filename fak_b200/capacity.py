@@ -58,10 +58,39 @@ class MemoryPlan:
         return sum(self.items().values())
 
 
-def kv_bytes_per_token(cfg: ModelConfig, tp: int = 1) -> int:
-    """bf16 K and V of one token over all layers, for the KV heads one rank holds."""
+# KV precision tiers: bytes per stored K or V element (the scale of a block folded in)
+KV_PRECISION_BYTES = {
+    "bf16": 2.0,          # the engine's resident layout
+    "fp8": 1.0 + 4 / 128,  # e4m3 codes + one f32 scale per (token, KV head) of 128 elements
+    "q8": 34 / 32,         # q8_0 blocks: int8 codes + one f16 scale per 32 elements
+}
+
+
+def parse_kv_precision(s: str | None) -> str:
+    """'' / None -> bf16; 'q8_0' is accepted for q8; anything else is refused (no silent default)."""
+    t = (s or "bf16").lower()
+    t = "q8" if t == "q8_0" else t
+    if t not in KV_PRECISION_BYTES:
+        raise ValueError(f"unknown KV precision {s!r} (want one of {sorted(KV_PRECISION_BYTES)})")
+    return t
+
+
+def kv_bytes_per_token(cfg: ModelConfig, tp: int = 1, precision: str = "bf16") -> int:
+    """K and V of one token over all layers, for the KV heads one rank holds, at a KV precision tier.
+    Span eviction re-rotates stored keys, so the lossy tiers (fp8, q8) cost accuracy at an eviction
+    as well as at attention (the bf16 tier rounds once more per re-rotation)."""
     kv_heads = max(1, math.ceil(cfg.n_kv_heads / tp)) if cfg.n_kv_heads >= tp else 1
-    return cfg.n_layers * 2 * kv_heads * cfg.head_dim * 2
+    elems = cfg.n_layers * 2 * kv_heads * cfg.head_dim
+    return int(math.ceil(elems * KV_PRECISION_BYTES[parse_kv_precision(precision)]))
+
+
+def select_kv_precision(cfg: ModelConfig, want_tokens: int, kv_budget_bytes: int, tp: int = 1) -> str:
+    """The densest-needed tier: bf16 when ``want_tokens`` fit the KV budget in bf16, else the least
+    lossy tier that fits (fp8, then q8 -- the same density order); raises when none fits."""
+    for t in ("bf16", "fp8", "q8"):
+        if want_tokens * kv_bytes_per_token(cfg, tp, t) <= kv_budget_bytes:
+            return t
+    raise ValueError(f"{want_tokens} tokens of KV do not fit {kv_budget_bytes / 2**30:.2f} GiB at any precision tier")
 
 
 def weight_counts(cfg: ModelConfig, tp: int = 1, ep: int = 1) -> dict[str, int]:
@@ -70,7 +99,8 @@ def weight_counts(cfg: ModelConfig, tp: int = 1, ep: int = 1) -> dict[str, int]:
     q = cfg.n_heads * cfg.head_dim
     kv = cfg.n_kv_heads * cfg.head_dim
     attn_in = L * d * (q + 2 * kv) // tp
-    attn_out = L * q * d  # o_proj is kept whole on every rank (head-gathered input)
+    # o_proj is row-parallel: a rank holds the 256-aligned column range around its heads
+    attn_out = L * d * min(q, -(-(q // tp) // 256) * 256 + (256 if tp > 1 else 0))
     if cfg.is_moe:
         experts = L * -(-cfg.n_experts // max(ep, tp)) * 3 * d * cfg.expert_ffn_dim
         ffn = experts
@@ -82,7 +112,8 @@ def weight_counts(cfg: ModelConfig, tp: int = 1, ep: int = 1) -> dict[str, int]:
 
 
 def plan(cfg: ModelConfig, mix: str = "q4_k_m", max_context: int = 8192, batch: int = 8, tp: int = 1, ep: int = 1,
-         prefill_bf16: bool = True, max_prefill_tokens: int = 4096, kv_pages: int | None = None) -> MemoryPlan:
+         prefill_bf16: bool = True, max_prefill_tokens: int = 4096, kv_pages: int | None = None,
+         kv_precision: str = "bf16") -> MemoryPlan:
     """Device bytes per rank of serving ``cfg`` with ``batch`` sequences of ``max_context`` tokens."""
     bpw = MIX_WEIGHT_BYTES.get(mix, BYTES_PER_WEIGHT.get(mix, 2.0))
     wc = weight_counts(cfg, tp, ep)
@@ -94,7 +125,7 @@ def plan(cfg: ModelConfig, mix: str = "q4_k_m", max_context: int = 8192, batch: 
     p.prefill_bf16 = int(dense_linear * 2) if prefill_bf16 else 0
     pages = kv_pages if kv_pages is not None else batch * -(-max_context // PAGE_TOKENS) + 1
     p.kv_pages = pages
-    p.kv = pages * PAGE_TOKENS * kv_bytes_per_token(cfg, tp)
+    p.kv = pages * PAGE_TOKENS * kv_bytes_per_token(cfg, tp, kv_precision)
     d, f = cfg.d_model, (cfg.expert_ffn_dim * cfg.n_experts_used if cfg.is_moe else cfg.ffn_dim // tp)
     decode_act = batch * (4 * (d + 2 * f + cfg.vocab_size) + 2 * (d + f))
     prefill_act = max_prefill_tokens * (4 * 2 * d + 2 * (3 * d + 2 * f) + 4 * f)

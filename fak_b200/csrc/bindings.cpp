@@ -37,7 +37,7 @@ void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out, c10::option
 void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, torch::Tensor qx, torch::Tensor ds,
           int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, int64_t flags);
 void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx,
-                    torch::Tensor ds, c10::optional<torch::Tensor> prefetch);
+                    torch::Tensor ds, c10::optional<torch::Tensor> prefetch, bool unit);
 void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, int64_t dst_off, int64_t dst_ld,
                         int64_t col0, int64_t ncols, int64_t B, int64_t flags_off, int64_t site, int64_t me,
                         torch::Tensor counters, torch::Tensor err, int64_t ctas, c10::optional<torch::Tensor> src2,
@@ -49,6 +49,10 @@ void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, i
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
                 torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
                 torch::Tensor err, int64_t spin_limit);
+void p2p_moe_combine_ar(torch::Tensor peers, torch::Tensor out, torch::Tensor ids, torch::Tensor wts, int64_t k,
+                        int64_t e0, int64_t E_local, torch::Tensor x, int64_t B, int64_t parts_off, int64_t parity,
+                        int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err,
+                        int64_t ctas, int64_t spin_limit);
 void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor wr, int64_t k, bool norm_topk,
                torch::Tensor ids, torch::Tensor wts);
 void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_t max_chunks, torch::Tensor chunk_expert,
@@ -58,7 +62,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
            int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
-           c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit);
+           c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit, bool unit);
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device);
 int64_t tgemv_unit_bytes(int64_t qtype);
 void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, torch::Tensor qx,
@@ -126,6 +130,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("v_off"), pybind11::arg("cand_off"), pybind11::arg("out"), pybind11::arg("B"),
         pybind11::arg("flags_off"), pybind11::arg("site"), pybind11::arg("me"), pybind11::arg("counters"),
         pybind11::arg("err"), pybind11::arg("spin_limit") = 0);
+  m.def("p2p_moe_combine_ar", &p2p_moe_combine_ar, "MoE combine fused with the expert-parallel all-reduce");
   m.def("moe_route", &moe_route);
   m.def("moe_group", &moe_group);
   m.def("moe_qmmv", &moe_qmmv);
@@ -134,14 +139,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("pitch"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"), pybind11::arg("y"),
         pybind11::arg("bias"), pybind11::arg("epi"), pybind11::arg("flags") = 0);
   m.def("quant_act_wide", &quant_act_wide, pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
-        pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("prefetch") = pybind11::none());
+        pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("prefetch") = pybind11::none(),
+        pybind11::arg("unit") = false);
   m.def("tgemv", &tgemv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("N"), pybind11::arg("K"),
         pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
         pybind11::arg("B"), pybind11::arg("y"), pybind11::arg("bias"),
         pybind11::arg("epi"), pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
         pybind11::arg("flags") = 0, pybind11::arg("ar_peers") = pybind11::none(), pybind11::arg("ar_me") = 0,
         pybind11::arg("ar_parts_off") = 0, pybind11::arg("ar_flags_off") = 0, pybind11::arg("ar_epochs") = pybind11::none(),
-        pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("ar_spin_limit") = 0);
+        pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("ar_spin_limit") = 0,
+        pybind11::arg("unit") = false);
   m.def("tgemv_workspace", &tgemv_workspace);
   m.def("tgemv_unit_bytes", &tgemv_unit_bytes);
   m.def("moe_tgemv", &moe_tgemv);

@@ -174,6 +174,44 @@ __global__ void k_p2p_argmax(Peers P, const float* __restrict__ logits, int64_t 
   pdl_launch_dependents();
 }
 
+// ---- MoE combine fused with the expert-parallel all-reduce -----------------------------------
+// Expert parallelism with the residual stream replicated on every rank (attention is head-parallel),
+// so a token's activation is already on every rank and the grouped expert GEMV gathers the rows it
+// needs locally: the only cross-rank step is the combine.  CTA c owns elements [c * chunk, ...) of
+// the flattened [B, d] output: it sums, for each element, the router-weighted outputs of the experts
+// in this rank's band (the token's k slots in order), pushes those partials into slot [me] of every
+// rank's buffer (half `parity` of [2][W][B*d]), crosses the per-(site, CTA) barrier, and adds the
+// rank-order sum of the W slots to the residual -- bit-identical on every rank.  Consecutive MoE
+// layers alternate halves, so a fast rank's next layer cannot overwrite partials a slow rank has
+// not summed: reaching the next use of a half requires passing the layer in between.
+__global__ void k_moe_combine_ar(Peers P, const float* __restrict__ out, const int* __restrict__ ids,
+                                 const float* __restrict__ wts, int k, int e0, int E_local, float* __restrict__ x,
+                                 int B, int d, int64_t parts_off, int parity, int64_t flags_off, int site, int me, int W,
+                                 uint32_t* counters, int* err) {
+  pdl_wait();
+  const int64_t n = (int64_t)B * d;
+  const int64_t chunk = (n + gridDim.x - 1) / gridDim.x;
+  const int64_t i0 = blockIdx.x * chunk, i1 = min(n, i0 + chunk);
+  const int64_t half = (int64_t)parity * W * n;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int b = (int)(i / d), c = (int)(i - (int64_t)b * d);
+    float s = 0.f;
+    for (int j = 0; j < k; j++) {
+      const int e = ids[b * k + j] - e0;
+      if (e >= 0 && e < E_local) s += wts[b * k + j] * out[((int64_t)b * k + j) * d + c];
+    }
+    for (int r = 0; r < W; r++) reinterpret_cast<float*>(P.base[r] + parts_off)[half + (int64_t)me * n + i] = s;
+  }
+  rank_barrier(P, flags_off, site, blockIdx.x, me, W, counters, err);
+  const float* mine = reinterpret_cast<const float*>(P.base[me] + parts_off) + half;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < W; r++) s += __ldcg(mine + (int64_t)r * n + i);
+    x[i] += s;
+  }
+  pdl_launch_dependents();
+}
+
 Peers make_peers(torch::Tensor ptrs, int64_t spin_limit) {
   TORCH_CHECK(ptrs.scalar_type() == torch::kInt64 && ptrs.numel() <= MAX_W, "peer pointer table");
   TORCH_CHECK(spin_limit >= 0 && spin_limit <= 0xffffffffll, "spin limit");
@@ -254,5 +292,28 @@ void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_argmax, P, (const float*)logits.data_ptr<float>(),
                                     (int64_t)logits.stride(0), (int)Vl, v_off, cand_off, out.data_ptr<int>(),
                                     flags_off, (int)site, (int)me, W, (uint32_t*)counters.data_ptr<int>(),
+                                    err.data_ptr<int>()));
+}
+
+// out [B*k, d] f32 (expert outputs per (token, slot)); ids / wts [B, k]; x [B, d] f32 (residual, updated);
+// parts_off: [2][W][B*d] f32 region of the peer buffers; site: this layer's barrier site.
+void p2p_moe_combine_ar(torch::Tensor peers, torch::Tensor out, torch::Tensor ids, torch::Tensor wts, int64_t k,
+                        int64_t e0, int64_t E_local, torch::Tensor x, int64_t B, int64_t parts_off, int64_t parity,
+                        int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err,
+                        int64_t ctas, int64_t spin_limit) {
+  const int W = (int)peers.numel();
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.size(0) >= B * k, "moe_combine_ar: out");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.size(0) >= B, "moe_combine_ar: x");
+  TORCH_CHECK(ids.scalar_type() == torch::kInt32 && wts.scalar_type() == torch::kFloat32, "moe_combine_ar: ids / wts");
+  TORCH_CHECK(parts_off % 16 == 0 && (parity == 0 || parity == 1), "moe_combine_ar: parts layout");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "moe_combine_ar: 1..64 CTAs");
+  if (B <= 0) return;
+  Peers P = make_peers(peers, spin_limit);
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_moe_combine_ar, P, (const float*)out.data_ptr<float>(),
+                                    (const int*)ids.data_ptr<int>(), (const float*)wts.data_ptr<float>(), (int)k,
+                                    (int)e0, (int)E_local, x.data_ptr<float>(), (int)B, (int)x.size(1), parts_off,
+                                    (int)parity, flags_off, (int)site, (int)me, W, (uint32_t*)counters.data_ptr<int>(),
                                     err.data_ptr<int>()));
 }

@@ -348,9 +348,12 @@ k_qmmv(const uint8_t* __restrict__ W, int N, int K, int64_t pitch, const int8_t*
 
 // activation quantizer with enough CTAs to fill the GPU: grid (B, ceil(K / 256)); each CTA
 // quantizes 8 blocks of 32 and, for the fused RMSNorm, recomputes its row's sum of squares.
+// unit != 0: one scale for the CTA's whole 256-column unit (max |v| over the unit / 127), stored in
+// each of its eight (scale, sum) entries -- the same format, with the scale uniform over a unit,
+// which lets the tile-packed GEMV apply it once per unit instead of once per 32 columns.
 __global__ void k_quant_act_wide(const float* __restrict__ x, int64_t ldx, const float* __restrict__ gamma, float eps,
                                  int K, int8_t* __restrict__ qx, float2* __restrict__ ds, const uint8_t* __restrict__ pf,
-                                 int64_t pf_bytes) {
+                                 int64_t pf_bytes, int unit) {
   l2_prefetch(pf, pf_bytes);
   pdl_wait();
   const int b = blockIdx.x;
@@ -374,11 +377,19 @@ __global__ void k_quant_act_wide(const float* __restrict__ x, int64_t ldx, const
   }
   pdl_launch_dependents();
   const int blk = blockIdx.y * 8 + warp;
-  if (blk * 32 >= K) return;
+  const bool live = blk * 32 < K;
   const int i = blk * 32 + lane;
-  float v = xr[i] * inv;
-  if (gamma) v *= gamma[i];
+  float v = live ? xr[i] * inv : 0.f;
+  if (gamma && live) v *= gamma[i];
   float amax = warp_max(fabsf(v));
+  if (unit) {
+    __shared__ float umax[8];
+    if (lane == 0) umax[warp] = amax;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < 8; w++) amax = fmaxf(amax, umax[w]);
+  }
+  if (!live) return;
   float d = amax / 127.f;
   const float q = d > 0.f ? rintf(v / d) : 0.f;
   const float s = warp_sum(q) * d;  // sum of the dequantized values (exact integer sum x scale)
@@ -478,7 +489,7 @@ void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, t
 }
 
 void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, torch::Tensor qx,
-                    torch::Tensor ds, c10::optional<torch::Tensor> prefetch) {
+                    torch::Tensor ds, c10::optional<torch::Tensor> prefetch, bool unit) {
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
   const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.dim() == 2 && x.stride(1) == 1, "x: [B,K] f32");
@@ -504,5 +515,5 @@ void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double 
   cfg.numAttrs = 1;
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_quant_act_wide, (const float*)x.data_ptr<float>(), (int64_t)x.stride(0), g,
                                     (float)eps, K, qx.data_ptr<int8_t>(), reinterpret_cast<float2*>(ds.data_ptr<float>()),
-                                    pfp, pfb));
+                                    pfp, pfb, unit ? 1 : 0));
 }

@@ -271,6 +271,158 @@ FAK_DEV void unit_tile(const uint8_t* __restrict__ wt, float* __restrict__ tab, 
   __syncwarp();  // table and slot reads done before the next unit overwrites them
 }
 
+// ---- one Q4_K unit tile, activations with one scale per 256-column unit ("unit scale") ---------
+// The per-sub-block scales are integers (6 bits), so with a single activation scale dx per unit the
+// dot product of a row with a token is
+//   dx * ( d * sum_j sc_j * dot_j  -  dmin * sum_j m_j * s_j )
+// where dot_j = sum of code products of sub-block j (one m16n8k32 integer MMA) and s_j = sum of the
+// token's codes in sub-block j.  The first sum runs in int32 registers (one IMAD per MMA value; high
+// nibbles stay in place, so their products carry a factor 16 that one exact shift removes), the
+// second is four dp2a per (row, token) over 16-bit packed s_j -- one float conversion and three
+// float operations per value per unit, instead of four float operations per value per sub-block.
+// dxu: this unit's scale per staged token; s16: this unit's packed sums, [token][4] x (s_2i | s_2i+1 << 16).
+template <int NT>
+FAK_DEV void unit_tile_q4k_us(const uint8_t* __restrict__ wt, const int8_t* __restrict__ xr, int xstride,
+                              const float* __restrict__ dxu, const int* __restrict__ s16, int lane,
+                              float (&acc)[NT][4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const int sA = 2 * g, sB = 2 * g + 1;
+  const uint4 hA = *reinterpret_cast<const uint4*>(wt + 16 * sA);
+  const uint4 hB = *reinterpret_cast<const uint4*>(wt + 16 * sB);
+  // 6-bit (scale, min) bytes of sub-blocks 0-3 (low 6 bits of header bytes 0-3 / 4-7) and 4-7
+  // (nibbles of bytes 8-11 with the top 2 bits of bytes 0-7)
+  const uint32_t scA0 = hA.y & 0x3F3F3F3Fu, mA0 = hA.z & 0x3F3F3F3Fu;
+  const uint32_t scA1 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+  const uint32_t mA1 = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
+  const uint32_t scB0 = hB.y & 0x3F3F3F3Fu, mB0 = hB.z & 0x3F3F3F3Fu;
+  const uint32_t scB1 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+  const uint32_t mB1 = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
+  int ilo[NT][4], ihi[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int v = 0; v < 4; v++) ilo[nt][v] = ihi[nt][v] = 0;
+  const uint8_t* qs = wt + 256;
+  const uint8_t* rA = qs + 128 * sA + 8 * (t & 1);
+  const uint8_t* rB = qs + 128 * sB + 8 * (t & 1);
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const int q = 2 * c + (t >> 1);
+    const uint2 qa = *reinterpret_cast<const uint2*>(rA + 16 * (q ^ (sA & 6)));
+    const uint2 qb = *reinterpret_cast<const uint2*>(rB + 16 * (q ^ (sB & 6)));
+#pragma unroll
+    for (int hi = 0; hi < 2; hi++) {
+      const int j = 2 * c + hi;
+      const uint32_t m = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+      const uint32_t a[4] = {qa.x & m, qb.x & m, qa.y & m, qb.y & m};
+      const int sa = (int)(((j < 4 ? scA0 : scA1) >> (8 * (j & 3))) & 0xffu);
+      const int sb = (int)(((j < 4 ? scB0 : scB1) >> (8 * (j & 3))) & 0xffu);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        const uint2 xb = *reinterpret_cast<const uint2*>(xr + nt * 8 * xstride + 32 * j + 8 * t);
+        int cc[4];
+        mma_u8s8_k32(cc, a, xb.x, xb.y, 0, 0);
+        int(&I)[4] = hi ? ihi[nt] : ilo[nt];
+        I[0] += sa * cc[0];
+        I[1] += sa * cc[1];
+        I[2] += sb * cc[2];
+        I[3] += sb * cc[3];
+      }
+    }
+  }
+  const float dA = __half2float(__ushort_as_half((uint16_t)(hA.x & 0xffff)));
+  const float dmA = __half2float(__ushort_as_half((uint16_t)(hA.x >> 16)));
+  const float dB = __half2float(__ushort_as_half((uint16_t)(hB.x & 0xffff)));
+  const float dmB = __half2float(__ushort_as_half((uint16_t)(hB.x >> 16)));
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    const int k0 = nt * 8 + 2 * t;
+    const int4 p0 = *reinterpret_cast<const int4*>(s16 + 4 * k0);
+    const int4 p1 = *reinterpret_cast<const int4*>(s16 + 4 * (k0 + 1));
+    const float2 dx = *reinterpret_cast<const float2*>(dxu + k0);
+    const int mA_0 = __dp2a_hi(p0.w, (int)mA1, __dp2a_lo(p0.z, (int)mA1, __dp2a_hi(p0.y, (int)mA0, __dp2a_lo(p0.x, (int)mA0, 0))));
+    const int mA_1 = __dp2a_hi(p1.w, (int)mA1, __dp2a_lo(p1.z, (int)mA1, __dp2a_hi(p1.y, (int)mA0, __dp2a_lo(p1.x, (int)mA0, 0))));
+    const int mB_0 = __dp2a_hi(p0.w, (int)mB1, __dp2a_lo(p0.z, (int)mB1, __dp2a_hi(p0.y, (int)mB0, __dp2a_lo(p0.x, (int)mB0, 0))));
+    const int mB_1 = __dp2a_hi(p1.w, (int)mB1, __dp2a_lo(p1.z, (int)mB1, __dp2a_hi(p1.y, (int)mB0, __dp2a_lo(p1.x, (int)mB0, 0))));
+    const float v0 = (float)(ilo[nt][0] + (ihi[nt][0] >> 4)), v1 = (float)(ilo[nt][1] + (ihi[nt][1] >> 4));
+    const float v2 = (float)(ilo[nt][2] + (ihi[nt][2] >> 4)), v3 = (float)(ilo[nt][3] + (ihi[nt][3] >> 4));
+    acc[nt][0] = fmaf(dx.x, fmaf(dA, v0, -dmA * (float)mA_0), acc[nt][0]);
+    acc[nt][1] = fmaf(dx.y, fmaf(dA, v1, -dmA * (float)mA_1), acc[nt][1]);
+    acc[nt][2] = fmaf(dx.x, fmaf(dB, v2, -dmB * (float)mB_0), acc[nt][2]);
+    acc[nt][3] = fmaf(dx.y, fmaf(dB, v3, -dmB * (float)mB_1), acc[nt][3]);
+  }
+}
+
+// ---- one Q6_K unit tile with unit-scale activations ------------------------------------------
+// w = d * sc_j * (q - 32) with signed 8-bit sc_j per 16-element sub-block, so a row's dot product with
+// a token is dx * d * sum_j sc_j * dot'_j, where dot'_j = sum (q - 32) x over sub-block j comes out of
+// one m16n8k16 integer MMA whose accumulator starts at -32 * (sum of the token's 16 codes): one IMAD
+// per MMA value, one conversion and two float operations per value per unit.
+// cz: this unit's accumulator starts, [16 sub-blocks][staged tokens].
+template <int NT>
+FAK_DEV void unit_tile_q6k_us(const uint8_t* __restrict__ wt, const int8_t* __restrict__ xr, int xstride,
+                              const float* __restrict__ dxu, const int* __restrict__ cz, int lane,
+                              float (&acc)[NT][4]) {
+  constexpr int MB = 8 * NT;
+  const int g = lane >> 2, t = lane & 3;
+  const int sA = 2 * g, sB = 2 * g + 1;
+  const uint4 scA = *reinterpret_cast<const uint4*>(wt + 3072 + 16 * sA);
+  const uint4 scB = *reinterpret_cast<const uint4*>(wt + 3072 + 16 * sB);
+  const uint32_t scAw[4] = {scA.x, scA.y, scA.z, scA.w}, scBw[4] = {scB.x, scB.y, scB.z, scB.w};
+  int I[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) I[nt][0] = I[nt][1] = I[nt][2] = I[nt][3] = 0;
+  const uint8_t* ql = wt;
+  const uint8_t* qh = wt + 2048;
+  const int f8 = g, f4 = (g >> 1) & 3;
+#pragma unroll
+  for (int n = 0; n < 2; n++) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int c1 = 4 * n + h, c2 = 4 * n + 2 + h, ch = 2 * n + h;
+      const uint32_t la0 = *reinterpret_cast<const uint32_t*>(ql + 128 * sA + 16 * (c1 ^ f8) + 4 * t);
+      const uint32_t la1 = *reinterpret_cast<const uint32_t*>(ql + 128 * sA + 16 * (c2 ^ f8) + 4 * t);
+      const uint32_t lb0 = *reinterpret_cast<const uint32_t*>(ql + 128 * sB + 16 * (c1 ^ f8) + 4 * t);
+      const uint32_t lb1 = *reinterpret_cast<const uint32_t*>(ql + 128 * sB + 16 * (c2 ^ f8) + 4 * t);
+      const uint32_t ha = *reinterpret_cast<const uint32_t*>(qh + 64 * g + 16 * (ch ^ f4) + 4 * t);
+      const uint32_t hb = *reinterpret_cast<const uint32_t*>(qh + 64 * (g + 8) + 16 * (ch ^ f4) + 4 * t);
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const uint32_t la = (kk & 1) ? la1 : la0, lb = (kk & 1) ? lb1 : lb0;
+        const int ls = (kk >> 1) * 4, hs = 2 * kk;
+        const uint32_t a0 = ((la >> ls) & 0x0F0F0F0Fu) | (((ha >> hs) & 0x03030303u) << 4);
+        const uint32_t a1 = ((lb >> ls) & 0x0F0F0F0Fu) | (((hb >> hs) & 0x03030303u) << 4);
+        const int e0 = 128 * n + 32 * kk + 16 * h;   // first weight of this 16-block
+        const int j = e0 >> 4;                         // sub-block 0..15
+        // signed scale bytes (sign-replicating byte permute)
+        const int sa = (int)__byte_perm(scAw[j >> 2], 0u, 0x8880u | ((j & 3) * 0x1111u));
+        const int sb = (int)__byte_perm(scBw[j >> 2], 0u, 0x8880u | ((j & 3) * 0x1111u));
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+          const uint32_t xv = *reinterpret_cast<const uint32_t*>(xr + nt * 8 * xstride + e0 + 4 * t);
+          const int2 c0 = *reinterpret_cast<const int2*>(cz + j * MB + nt * 8 + 2 * t);
+          int cc[4];
+          mma_u8s8_k16(cc, a0, a1, xv, c0.x, c0.y);
+          I[nt][0] += sa * cc[0];
+          I[nt][1] += sa * cc[1];
+          I[nt][2] += sb * cc[2];
+          I[nt][3] += sb * cc[3];
+        }
+      }
+    }
+  }
+  const float dA = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(wt + 3328 + 2 * sA)));
+  const float dB = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(wt + 3328 + 2 * sB)));
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    const float2 dx = *reinterpret_cast<const float2*>(dxu + nt * 8 + 2 * t);
+    acc[nt][0] = fmaf(dx.x * dA, (float)I[nt][0], acc[nt][0]);
+    acc[nt][1] = fmaf(dx.y * dA, (float)I[nt][1], acc[nt][1]);
+    acc[nt][2] = fmaf(dx.x * dB, (float)I[nt][2], acc[nt][2]);
+    acc[nt][3] = fmaf(dx.y * dB, (float)I[nt][3], acc[nt][3]);
+  }
+}
+
 FAK_DEV void epilogue(int tile, const float (&v)[4], int tokb, int lane, int N, int B, float* __restrict__ y,
                       int64_t ldy, const float* __restrict__ bias, int epi) {
   const int g = lane >> 2, t = lane & 3;
@@ -376,7 +528,7 @@ FAK_DEV void ar_tile(const ArPeers& ar, int T, int tile, int lane, float (&v)[NT
   if (lane == 0) ar.epochs[tile] = ep;
 }
 
-template <int QT, int W, int R, int NT>
+template <int QT, int W, int R, int NT, bool US = false>
 __global__ void __launch_bounds__(W * 32, 1)
 k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
         const float* __restrict__ xf, int64_t ldx, const float* __restrict__ gamma, float eps,
@@ -506,9 +658,38 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       if (b >= B || c >= kb) *reinterpret_cast<uint4*>(xs + b * geo.xstride + c) = make_uint4(0, 0, 0, 0);
     }
     tc::mbar_wait(act_bar, 0, err);
-    for (int i = threadIdx.x; i < nu * 8 * MB; i += W * 32) {
-      const int blk = i / MB, b = i % MB;
-      dsT[i] = (b < B && blk * 32 < kb) ? dsr[b * geo.dstride + blk] : make_float2(0.f, 0.f);
+    if constexpr (US) {
+      // unit scale: the unit's scale per token, and the token's code sums per 32-block packed in
+      // 16-bit pairs ([unit][token][4]) -- both read by unit_tile_q4k_us
+      float* dxu = reinterpret_cast<float*>(dsT);
+      int* s16 = reinterpret_cast<int*>(dsT) + nu * MB;
+      for (int i = threadIdx.x; i < nu * MB; i += W * 32) {
+        const int u = i / MB, b = i % MB;
+        dxu[i] = (b < B && u * 256 < kb) ? dsr[b * geo.dstride + u * 8].x : 0.f;
+        if constexpr (QT != QT_Q4_K) continue;   // Q6_K: the sub-block sums go into czT below
+        const int4* src = reinterpret_cast<const int4*>(xs + b * geo.xstride + u * 256);
+        int sum[8];
+#pragma unroll
+        for (int jb = 0; jb < 8; jb++) {
+          const int4 v0 = src[2 * jb], v1 = src[2 * jb + 1];
+          int a = __dp4a(v0.x, 0x01010101, 0);
+          a = __dp4a(v0.y, 0x01010101, a);
+          a = __dp4a(v0.z, 0x01010101, a);
+          a = __dp4a(v0.w, 0x01010101, a);
+          a = __dp4a(v1.x, 0x01010101, a);
+          a = __dp4a(v1.y, 0x01010101, a);
+          a = __dp4a(v1.z, 0x01010101, a);
+          sum[jb] = __dp4a(v1.w, 0x01010101, a);
+        }
+        *reinterpret_cast<int4*>(s16 + 4 * i) =
+            make_int4((sum[0] & 0xffff) | (sum[1] << 16), (sum[2] & 0xffff) | (sum[3] << 16),
+                      (sum[4] & 0xffff) | (sum[5] << 16), (sum[6] & 0xffff) | (sum[7] << 16));
+      }
+    } else {
+      for (int i = threadIdx.x; i < nu * 8 * MB; i += W * 32) {
+        const int blk = i / MB, b = i % MB;
+        dsT[i] = (b < B && blk * 32 < kb) ? dsr[b * geo.dstride + blk] : make_float2(0.f, 0.f);
+      }
     }
   }
   if constexpr (QT == QT_Q6_K) {
@@ -520,7 +701,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       sm4 = __dp4a(v.y, 0x01010101, sm4);
       sm4 = __dp4a(v.z, 0x01010101, sm4);
       sm4 = __dp4a(v.w, 0x01010101, sm4);
-      czT[i] = MAGIC_I - 32 * sm4;
+      czT[i] = (US ? 0 : MAGIC_I) - 32 * sm4;   // unit scale: plain int32 accumulation
     }
   }
   __syncthreads();
@@ -535,8 +716,16 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   for (int q = 0; q < Q; q++) {
     if (lane == 0) issue_next();  // into the slot released at the end of the previous iteration
     tc::mbar_wait(&bar[cslot], phase, err);
-    unit_tile<QT, NT>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
-                      QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
+    if constexpr (US && QT == QT_Q4_K)
+      unit_tile_q4k_us<NT>(ring + cslot * UT, xg + ul * 256, geo.xstride,
+                           reinterpret_cast<const float*>(dsT) + ul * MB,
+                           reinterpret_cast<const int*>(dsT) + nu * MB + 4 * ul * MB, lane, acc);
+    else if constexpr (US && QT == QT_Q6_K)
+      unit_tile_q6k_us<NT>(ring + cslot * UT, xg + ul * 256, geo.xstride,
+                           reinterpret_cast<const float*>(dsT) + ul * MB, czT + ul * 16 * MB, lane, acc);
+    else
+      unit_tile<QT, NT>(ring + cslot * UT, tab, xg + ul * 256, geo.xstride, dsT + ul * 8 * MB,
+                        QT == QT_Q6_K ? czT + ul * 16 * MB : nullptr, lane, acc);
     if (++cslot == R) {
       cslot = 0;
       phase ^= 1u;
@@ -802,7 +991,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
            int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
-           c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit) {
+           c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit, bool unit) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "tgemv: w cuda uint8");
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
   const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
@@ -903,12 +1092,21 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
                                         b0 == 0 ? pfp : nullptr, pfb));
     }
   };
-#define FAK_TG_NT(QTV, NTV)                                              \
-  {                                                                      \
-    if (p.W == 16 && p.R == 3) go(k_tgemv<QTV, 16, 3, NTV>);             \
-    else if (p.W == 16 && p.R == 2) go(k_tgemv<QTV, 16, 2, NTV>);        \
-    else if (p.W == 8 && p.R == 3) go(k_tgemv<QTV, 8, 3, NTV>);          \
+  // unit-scale activations (one scale per 256 columns, ActQ.unit) on Q4_K / Q6_K weights: integer
+  // accumulation of the sub-block scales (unit_tile_q4k_us / unit_tile_q6k_us)
+  const bool us = unit && (qtype == QT_Q4_K || qtype == QT_Q6_K) && xp == nullptr;
+#define FAK_TG_W(QTV, NTV, USV)                                                   \
+  {                                                                               \
+    if (p.W == 16 && p.R == 3) go(k_tgemv<QTV, 16, 3, NTV, USV>);                 \
+    else if (p.W == 16 && p.R == 2) go(k_tgemv<QTV, 16, 2, NTV, USV>);            \
+    else if (p.W == 8 && p.R == 3) go(k_tgemv<QTV, 8, 3, NTV, USV>);              \
     else TORCH_CHECK(false, "tgemv: unsupported (warps, depth) ", p.W, ",", p.R); \
+  }
+#define FAK_TG_NT(QTV, NTV)                                          \
+  {                                                                  \
+    if constexpr (QTV == QT_Q4_K || QTV == QT_Q6_K) {                \
+      if (us) FAK_TG_W(QTV, NTV, true) else FAK_TG_W(QTV, NTV, false) \
+    } else FAK_TG_W(QTV, NTV, false)                                 \
   }
 #define FAK_TG(QTV)                     \
   {                                     \
@@ -922,6 +1120,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   else FAK_TG(QT_Q8_0)
 #undef FAK_TG
 #undef FAK_TG_NT
+#undef FAK_TG_W
 }
 
 // Grouped expert GEMV over tile-packed experts (MoE decode).  w: tile-packed [E_local * rows_per_expert

@@ -90,10 +90,11 @@ def request_seed(engine_seed: int, rid: int) -> int:
     return z ^ (z >> 31)
 
 
-def pack_params(sps: list[SamplingParams], steps: list[int], seeds: list[int]
+def pack_params(sps: list[SamplingParams], steps: list[int], seeds: list[int], max_bias: int | None = MAX_BIAS
                 ) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     """Rows of the device sampler's 10-word parameter block (temperature, top_k, top_p, frequency and
-    presence penalty, bias offset / count, seed lo / hi, step) and the flat logit-bias lists."""
+    presence penalty, bias offset / count, seed lo / hi, step) and the flat logit-bias lists
+    (at most ``max_bias`` entries: the decode graph's static bias buffer; None = unbounded)."""
     n = len(sps)
     f = np.zeros((n, 10), np.float32)
     w = f.view(np.int32)
@@ -113,8 +114,8 @@ def pack_params(sps: list[SamplingParams], steps: list[int], seeds: list[int]
         w[b, 7] = np.uint32(sd & 0xFFFFFFFF).view(np.int32)
         w[b, 8] = np.uint32((sd >> 32) & 0xFFFFFFFF).view(np.int32)
         w[b, 9] = int(st)
-    if len(tok) > MAX_BIAS:
-        raise ValueError(f"logit_bias entries of one batch exceed {MAX_BIAS}")
+    if max_bias is not None and len(tok) > max_bias:
+        raise ValueError(f"logit_bias entries of one batch exceed {max_bias}")
     return w.copy(), np.asarray(tok, np.int32), np.asarray(val, np.float32)
 
 
@@ -138,7 +139,7 @@ def device_sample(logits: torch.Tensor, V: int, sps: list[SamplingParams], steps
     """Draw one token per row of ``logits`` [n, >=V] f32 on the device (the rows are modified)."""
     from ..ops import kernels as K
     dev = logits.device
-    P, tok, val = pack_params(sps, steps, seeds)
+    P, tok, val = pack_params(sps, steps, seeds, max_bias=None)   # own buffers: any size
     p = torch.from_numpy(P).to(dev)
     bt = torch.from_numpy(tok if len(tok) else np.full(1, -1, np.int32)).to(dev)
     bv = torch.from_numpy(val if len(val) else np.zeros(1, np.float32)).to(dev)

@@ -10,7 +10,9 @@ Expert parallelism: rank r of the tensor-parallel group holds a contiguous band 
 (models.weights.expert_slice), computes the contributions of the pairs routed to its band and
 the partial sums are all-reduced into the residual -- the reference's EP decode scheme
 (replicated router, rank-local experts, dense partial all-reduce: internal/model/moe.go:523-553,
-internal/model/expert_parallel.go:85-200) with the reduction done by the in-kernel P2P all-reduce.
+internal/model/expert_parallel.go:85-200).  Attention is head-parallel, so every rank holds every
+token's activation and the "dispatch" is the local row gather in the grouped GEMV's staging; the
+combine and the cross-rank reduction are one kernel on the fused path (``P2PTP.moe_combine``).
 """
 from __future__ import annotations
 
@@ -83,6 +85,8 @@ def moe_decode(rn, i: int, B: int) -> None:
     if rn.coll is None:
         C.moe_combine(st.out, st.ids[:B], st.wts[:B], st.k, st.e0, st.E_local, x)
         K.count()
+    elif hasattr(rn.coll, "moe_combine"):
+        rn.coll.moe_combine(rn, i, B, st)      # combine fused with the all-reduce (one kernel)
     else:
         rn.coll.reduce_partial(rn, i, B, lambda part: (part.zero_(), C.moe_combine(
             st.out, st.ids[:B], st.wts[:B], st.k, st.e0, st.E_local, part)))
@@ -104,18 +108,25 @@ def moe_prefill(rn, i: int, hb: torch.Tensor, x: torch.Tensor) -> None:
     out = torch.zeros(T * k, d, dtype=torch.float32, device=x.device)
     flat = ids.view(-1).long()
     host_ids = flat.cpu()
+    # bf16 copies of the local experts, made at the first prefill and kept (like the dense layers'
+    # prefill copies): later prefills run the GEMMs without dequantizing
+    dense = getattr(L, "_dense_experts", None)
+    if dense is None:
+        dense = L._dense_experts = [None] * E_local
     for el in range(E_local):
         pairs = (host_ids == e0 + el).nonzero().view(-1)
         if pairs.numel() == 0:
             continue
         pairs_d = pairs.to(x.device)
         a = hb.index_select(0, pairs_d // k).contiguous()
-        wg = dq.dequantize_rows(gu.buf[el * rows_gu * gu.pitch:], gu.qtype, rows_gu, gu.cols, gu.pitch,
-                                torch.bfloat16)
+        if dense[el] is None:
+            dense[el] = (dq.dequantize_rows(gu.buf[el * rows_gu * gu.pitch:], gu.qtype, rows_gu, gu.cols, gu.pitch,
+                                            torch.bfloat16),
+                         dq.dequantize_rows(dn.buf[el * rows_dn * dn.pitch:], dn.qtype, rows_dn, dn.cols, dn.pitch,
+                                            torch.bfloat16))
+        wg, wd = dense[el]
         h = torch.empty(a.shape[0], f, dtype=torch.float32, device=x.device)
         K.gemm(a, wg, h, K.EPI_SWIGLU)
-        wd = dq.dequantize_rows(dn.buf[el * rows_dn * dn.pitch:], dn.qtype, rows_dn, dn.cols, dn.pitch,
-                                torch.bfloat16)
         o = torch.empty(a.shape[0], d, dtype=torch.float32, device=x.device)
         K.gemm(h.to(torch.bfloat16), wd, o, K.EPI_STORE)
         out.index_copy_(0, pairs_d, o)

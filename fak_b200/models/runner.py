@@ -118,12 +118,15 @@ class ModelRunner:
         gap = cfg.device_gap()
         if gap:
             raise NotImplementedError(f"{gap}; run it on the fp32 reference model (models.reference.ReferenceModel)")
-        self.act_d = K.ActQ(B, d, dev)
+        # activations quantized by quant_act feed the GEMVs with one scale per 256 columns
+        # (FAK_UNIT_SCALE=0 restores one scale per 32)
+        unit = os.environ.get("FAK_UNIT_SCALE", "1") != "0"
+        self.act_d = K.ActQ(B, d, dev, unit=unit)
         # o_proj input: this rank's slice [a0, a1) of the attention output columns (all of them on one
         # GPU); under TP the columns of other ranks' heads inside the slice stay zero
         a0, a1, _, _ = weights.o_cols if weights.o_cols[1] else (0, cfg.n_heads * self.D, 0, 0)
         self.act_attn = K.ActQ(B, a1 - a0, dev)
-        self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev)
+        self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev, unit=unit)
         # decode GEMV inputs: activations quantized by a separate kernel (default), or fp32 sources
         # the GEMV normalises and quantizes itself (fused_activations: fewer launches, but every CTA
         # repeats the row's quantization; measured 0.14 ms/step slower on Qwen2.5-7B B=5).

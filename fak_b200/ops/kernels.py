@@ -65,10 +65,15 @@ def scatter_i32(dst: torch.Tensor, idx_val: torch.Tensor, n: int) -> None:
 
 
 class ActQ:
-    """int8-quantized activations: codes [B, K] and per-32 (scale, sum) [B, K/32, 2]."""
+    """int8-quantized activations: codes [B, K] and per-32 (scale, sum) [B, K/32, 2].
 
-    def __init__(self, B: int, K: int, device):
+    ``unit``: the quantizer chooses one scale per 256 columns (stored in each of the unit's eight
+    entries, the format unchanged), so Q4_K GEMVs take their integer-accumulating path; producers
+    that fill the buffer some other way (the attention merge) leave it False."""
+
+    def __init__(self, B: int, K: int, device, unit: bool = False):
         self.K = K
+        self.unit = unit and K % 256 == 0
         self.q = torch.zeros(B, K, dtype=torch.int8, device=device)
         self.ds = torch.zeros(B, K // 32, 2, dtype=torch.float32, device=device)
 
@@ -85,7 +90,7 @@ class FAct:
 def quant_act(x: torch.Tensor, act: ActQ, gamma: torch.Tensor | None = None, eps: float = 1e-6,
               prefetch: torch.Tensor | None = None) -> None:
     """prefetch: a tensor (e.g. the next GEMV's tile-packed weights) to warm L2 with meanwhile."""
-    ext().quant_act_wide(x, gamma, eps, act.q, act.ds, prefetch)
+    ext().quant_act_wide(x, gamma, eps, act.q, act.ds, prefetch, getattr(act, "unit", False))
     count()
 
 
@@ -150,7 +155,7 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
                         y[b0:b0 + nb], bias, epi, part, cnt, ew, flags, **arkw)
             else:
                 C.tgemv(w.tp, w.qtype, w.rows, w.cols, act.q[b0:b0 + nb], act.ds[b0:b0 + nb], None, None, 0.0, nb,
-                        y[b0:b0 + nb], bias, epi, part, cnt, ew, flags, **arkw)
+                        y[b0:b0 + nb], bias, epi, part, cnt, ew, flags, unit=getattr(act, "unit", False), **arkw)
             count()
         return
     if isinstance(act, FAct):

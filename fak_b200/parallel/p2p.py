@@ -108,6 +108,9 @@ class P2PTP(NcclTP):
         self.lg_ok = self.Vl % 4 == 0
         self.lg_off = off
         off = _align(off + (B * self.world * self.Vl * 4 if self.lg_ok else 0))
+        # MoE combine fused with the expert-parallel all-reduce: [2 layer parities][W][B * d] partials
+        self.moe_off = off
+        off = _align(off + (2 * self.world * B * d * 4 if cfg.is_moe else 0))
         self.nbytes = off
         self.mem = None
         if os.environ.get("FAK_P2P_MEM", "ipc") == "symm":
@@ -195,6 +198,14 @@ class P2PTP(NcclTP):
         ext().p2p_argmax(self.peers, self.logits_local[:B], self.Vl_real, self.v_off, self.cand_off,
                          rn.next_ids[:B], B, self.flags_off, 3 * self.cfg.n_layers, self.me, self.counters, self.err,
                          self.spin_limit)
+        K.count()
+
+    def moe_combine(self, rn, i: int, B: int, st) -> None:
+        """x += sum over ranks of this rank's router-weighted expert outputs: one kernel (combine,
+        push to every rank, bounded barrier, rank-order sum)."""
+        ext().p2p_moe_combine_ar(self.peers, st.out, st.ids[:B], st.wts[:B], st.k, st.e0, st.E_local, rn.x[:B], B,
+                                 self.moe_off, i & 1, self.flags_off, 3 * i + 2, self.me, self.counters, self.err,
+                                 AR_CTAS * 2, self.spin_limit)
         K.count()
 
     def reduce_partial(self, rn, i: int, B: int, fill) -> None:

@@ -1,4 +1,6 @@
 """Capacity planner and roofline model (CPU)."""
+import math
+
 import pytest
 
 from fak_b200 import capacity as C
@@ -75,3 +77,23 @@ def test_kv_residency_split_spills_cold_tokens_to_the_host():
     assert kv_residency_split(10_000, bpt, 0, 1234 * bpt).cold_tokens == 1234
     # fail-open on missing geometry
     assert kv_residency_split(0, bpt, 1, 1).tokens == 0 and kv_residency_split(10, 0, 1, 1).tokens == 0
+
+
+def test_kv_precision_tiers():
+    from fak_b200.capacity import kv_bytes_per_token, parse_kv_precision, select_kv_precision
+    cfg = preset("qwen2.5-7b")
+    bf16 = kv_bytes_per_token(cfg, 1, "bf16")
+    assert bf16 == 28 * 2 * 4 * 128 * 2
+    assert kv_bytes_per_token(cfg, 1, "q8") == int(math.ceil(bf16 / 2 * 34 / 32))
+    assert bf16 / 2 < kv_bytes_per_token(cfg, 1, "fp8") < kv_bytes_per_token(cfg, 1, "q8")
+    assert parse_kv_precision("") == "bf16" and parse_kv_precision("Q8_0") == "q8"
+    with pytest.raises(ValueError):
+        parse_kv_precision("int4")
+    budget = 1000 * bf16
+    assert select_kv_precision(cfg, 1000, budget) == "bf16"
+    assert select_kv_precision(cfg, 1900, budget) == "fp8"
+    with pytest.raises(ValueError):
+        select_kv_precision(cfg, 2100, budget)
+    # the plan's KV line follows the tier
+    from fak_b200.capacity import plan
+    assert plan(cfg, kv_precision="fp8").kv < plan(cfg).kv

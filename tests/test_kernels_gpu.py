@@ -318,6 +318,49 @@ def test_tgemv_batch_invariant_and_repeatable(qt, blk):
     assert not K.tgemv_workspace("cuda")[1].any()
 
 
+@pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.Q6_K])
+@pytest.mark.parametrize("B", [1, 5, 13, 32])
+@pytest.mark.parametrize("N,Kd", [(576, 4096), (16 * 2400, 1024)])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_tgemv_unit_scale(qt, B, N, Kd, epi):
+    """Activations with one scale per 256 columns take the integer-accumulating Q4_K / Q6_K path: it
+    must compute exactly what the per-32 float path computes from the same quantized activations (the
+    sub-block scales are integers, so only float rounding differs), and stay close to fp32."""
+    from fak_b200.ops import kernels as K
+    w, Wd, x, _ = _tg_case(qt, N, Kd, B, seed=11)
+    act_u = K.ActQ(max(8, B), Kd, "cuda", unit=True)
+    K.quant_act(x, act_u)
+    ds = act_u.ds[:B].view(B, Kd // 256, 8, 2)
+    assert torch.equal(ds[..., 0], ds[..., :1, 0].expand_as(ds[..., 0])), "one scale per unit"
+    act_p = K.ActQ(max(8, B), Kd, "cuda")           # the same bytes through the per-32 path
+    act_p.q.copy_(act_u.q)
+    act_p.ds.copy_(act_u.ds)
+    bias = torch.randn(N, device="cuda") * 0.1
+    outs = []
+    for act in (act_u, act_p):
+        y = torch.zeros(B, N // 2, device="cuda") if epi == K.EPI_SWIGLU else torch.ones(B, N, device="cuda")
+        K.gemv(w, act, B, y, bias, epi)
+        outs.append(y)
+    torch.cuda.synchronize()
+    yu, yp = outs
+    scale = yp.abs().max().item()
+    assert (yu - yp).abs().max().item() <= 1e-4 * scale + 1e-6, (yu - yp).abs().max().item()
+    deq = (act_u.q[:B].float().view(B, -1, 32) * act_u.ds[:B, :, :1]).view(B, Kd)
+    ref = deq @ Wd.T + bias
+    if epi == K.EPI_SWIGLU:
+        ref = _swiglu_ref(ref)
+    elif epi == K.EPI_ADD:
+        ref = ref + 1.0
+    assert (yu - ref).abs().max().item() <= 1e-4 * ref.abs().max().item() + 1e-6
+    xr = x @ Wd.T + bias
+    if epi == K.EPI_SWIGLU:
+        xr = _swiglu_ref(xr)
+    elif epi == K.EPI_ADD:
+        xr = xr + 1.0
+    cos = torch.nn.functional.cosine_similarity(yu.flatten(), xr.flatten(), dim=0).item()
+    assert cos > (0.998 if epi == K.EPI_SWIGLU else 0.999), cos
+
+
 @pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3)])
 def test_decode_attention_fused_merge_bitexact(D, H, Hkv):
     """The in-kernel split merge (tickets) gives the same bits as the separate combine kernel and

@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 def _run(logits, sps, steps, seeds, generated=None, softcap=0.0):
     from fak_b200.ops import kernels as K
     n, V = logits.shape
-    P, tok, val = pack_params(sps, steps, seeds)
+    P, tok, val = pack_params(sps, steps, seeds, max_bias=None)
     p = torch.from_numpy(P).cuda()
     bt = torch.from_numpy(tok if len(tok) else np.full(1, -1, np.int32)).cuda()
     bv = torch.from_numpy(val if len(val) else np.zeros(1, np.float32)).cuda()

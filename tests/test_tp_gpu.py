@@ -24,7 +24,8 @@ def test_tp2_matches_tp1(model, fused):
     assert p.returncode == 0, p.stderr[-3000:]
     line = [l for l in p.stdout.splitlines() if l.startswith("{")][-1]
     res = json.loads(line)
-    assert res["ok"], res
+    assert res["ok"], json.dumps({k: res.get(k) for k in ("teacher_forced", "greedy", "kernel_error",
+                                                         "collective_error")})
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -36,7 +37,8 @@ def test_ep2_moe_matches_ep1():
     p = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
     assert p.returncode == 0, p.stderr[-3000:]
     res = json.loads([l for l in p.stdout.splitlines() if l.startswith("{")][-1])
-    assert res["ok"], res
+    assert res["ok"], json.dumps({k: res.get(k) for k in ("teacher_forced", "greedy", "kernel_error",
+                                                         "collective_error")})
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
