@@ -6,6 +6,7 @@ cache does, and times split-KV decode attention plus its combine.  Reports the K
 must read (shared pages counted once) and the effective bandwidth.
 
     python -m fak_b200.benchmarks.attnbench --batch 5 --ctx 9000 --shared 8192
+    python -m fak_b200.benchmarks.attnbench --batch 8 --ctx 4096 --shared 0 --prefill 4096 --impl tc
 """
 from __future__ import annotations
 
@@ -29,6 +30,8 @@ def main(argv=None):
     ap.add_argument("--split", type=int, default=16)
     ap.add_argument("--prefill", type=int, default=0,
                     help="time prefill attention instead: each sequence's last N tokens attend to the whole context")
+    ap.add_argument("--impl", default="tc", choices=("tc", "fa2"),
+                    help="prefill kernel: tcgen05 / TMEM (head dim 128) or the mma.sync one")
     ap.add_argument("--cascade", type=int, default=0,
                     help="prefix splits of cascade attention over the shared pages (0: plain split-KV path)")
     args = ap.parse_args(argv)
@@ -40,8 +43,9 @@ def main(argv=None):
     per_seq = math.ceil(ctx / 16)
     n_pages = n_sh + B * (per_seq - n_sh) + 1
     g = torch.Generator(device=dev).manual_seed(0)
-    caches = [(torch.randn(n_pages, Hkv, 16, D, device=dev, generator=g).bfloat16(),
-               torch.randn(n_pages, Hkv, 16, D, device=dev, generator=g).bfloat16()) for _ in range(args.layers)]
+    k_all = torch.randn(args.layers, n_pages, Hkv, 16, D, device=dev, generator=g).bfloat16()
+    v_all = torch.randn(args.layers, n_pages, Hkv, 16, D, device=dev, generator=g).bfloat16()
+    caches = [(k_all[i], v_all[i]) for i in range(args.layers)]
     bt = torch.zeros(B, per_seq, dtype=torch.int32)
     nxt = 1 + n_sh
     for b in range(B):
@@ -68,8 +72,11 @@ def main(argv=None):
         outp = torch.empty(B * Q, H * D, device=dev, dtype=torch.bfloat16)
 
         def run(i):  # noqa: F811
-            kc, vc = caches[i % args.layers]
-            K.prefill_attention(qp, kc, vc, bt, meta, outp)
+            if args.impl == "tc":
+                K.prefill_attention_tc(qp, k_all, v_all, i % args.layers, bt, meta, outp)
+            else:
+                kc, vc = caches[i % args.layers]
+                K.prefill_attention(qp, kc, vc, bt, meta, outp)
 
     for i in range(3):
         run(i)
@@ -83,8 +90,14 @@ def main(argv=None):
     us = e0.elapsed_time(e1) * 1000 / args.iters
     page_bytes = 2 * Hkv * 16 * D * 2
     unique = (n_sh + B * (per_seq - n_sh)) * page_bytes
+    extra = {}
+    if args.prefill:   # causal QK^T and PV FLOPs: query j of a chunk sees ctx - Q + j + 1 keys
+        Q = args.prefill
+        keys = B * (Q * (ctx - Q) + Q * (Q + 1) // 2)
+        flops = 4 * D * H * keys
+        extra = {"impl": args.impl, "tflops": round(flops / us / 1e6, 1)}
     print(json.dumps({"kernel": "prefill_attention" if args.prefill else "decode_attention+combine",
-                      "prefill": args.prefill,
+                      "prefill": args.prefill, **extra,
                       "batch": B, "ctx": ctx, "shared": n_sh * 16,
                       "heads": H, "kv_heads": Hkv, "head_dim": D, "splits": args.split, "cascade": args.cascade,
                       "us": round(us, 2),

@@ -146,8 +146,8 @@ def _kernel_profile(eng, turn, args, group, world) -> dict:
     for ev in prof.events():
         if ev.device_type.name != "CUDA":
             continue
-        name = ev.name.split("(")[0].replace("void ", "").replace("(anonymous namespace)::", "")
-        name = name.replace("<unnamed>::", "")[:48]
+        name = ev.name.replace("void ", "").replace("(anonymous namespace)::", "").replace("<unnamed>::", "")
+        name = name.split("(")[0][:48] or ev.name[:48]
         agg[name] = agg.get(name, 0.0) + ev.device_time
     # decode steps only: subtract nothing, report per decode step of the profiled turn
     steps = max(1, n_steps[0])

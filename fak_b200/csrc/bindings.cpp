@@ -86,6 +86,10 @@ torch::Tensor ipc_view(int64_t ptr, int64_t nbytes, int64_t device);
 void sample_rows(torch::Tensor logits, int64_t V, torch::Tensor params, torch::Tensor bias_tok, torch::Tensor bias_val,
                  c10::optional<torch::Tensor> counts, torch::Tensor out, int64_t B, double softcap);
 torch::Tensor philox4x32_10_host(std::vector<int64_t> ctr, std::vector<int64_t> key);
+void prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, int64_t layer,
+                          torch::Tensor block_table, torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff,
+                          torch::Tensor seq_qlen, torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out,
+                          c10::optional<torch::Tensor> err);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "fak_b200 sm_100a kernels";
@@ -164,6 +168,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("bias_val"), pybind11::arg("counts"), pybind11::arg("out"), pybind11::arg("B"),
         pybind11::arg("softcap") = 0.0);
   m.def("philox4x32_10_host", &philox4x32_10_host);
+  m.def("prefill_attention_tc", &prefill_attention_tc, "paged causal prefill attention on tcgen05 / TMEM (head dim 128)",
+        pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"), pybind11::arg("layer"),
+        pybind11::arg("block_table"), pybind11::arg("tile_seq"), pybind11::arg("tile_q0"), pybind11::arg("seq_qoff"),
+        pybind11::arg("seq_qlen"), pybind11::arg("seq_pos0"), pybind11::arg("n_tiles"), pybind11::arg("out"),
+        pybind11::arg("err") = pybind11::none());
   m.def("gemm_bf16", &gemm_bf16, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("out"),
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("epi") = 0, pybind11::arg("err") = pybind11::none());
 }

@@ -677,7 +677,7 @@ cudaLaunchAttribute g_pdl_attr[1];
 
 void set_pdl(cudaLaunchConfig_t& cfg) {
   g_pdl_attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  g_pdl_attr[0].val.programmaticStreamSerializationAllowed = 1;
+  g_pdl_attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = g_pdl_attr;
   cfg.numAttrs = 1;
 }

@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #define FAK_DEV __device__ __forceinline__
 
@@ -89,6 +90,17 @@ FAK_DEV float bf16_bits_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u)
 // Device-side error word: kernels never trap; they record a code and return.
 // Codes: 1 = bounded wait expired, 2 = index out of range, 3 = bad argument, 4 = a peer rank never
 // arrived at a fused all-reduce tile (tgemv epilogue).
+// Programmatic dependent launch is requested on every launch of this library unless FAK_PDL=0.
+// With it on, a profiler's span of a kernel includes its wait for the kernel before it, so a
+// per-kernel attribution is taken with it off.
+inline int pdl_allowed() {
+  static const int on = [] {
+    const char* e = getenv("FAK_PDL");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on;
+}
+
 FAK_DEV void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

@@ -243,7 +243,7 @@ cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem = 0) {
   cfg.dynamicSmemBytes = smem;
   cfg.stream = at::cuda::getCurrentCUDAStream();
   g_attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  g_attr[0].val.programmaticStreamSerializationAllowed = 1;
+  g_attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = g_attr;
   cfg.numAttrs = 1;
   return cfg;

@@ -1,0 +1,379 @@
+// Prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), over the paged KV cache.
+//
+// One CTA per (128-query tile of one sequence, query head).  The chunk's queries attend causally to
+// the sequence's cached prefix and to themselves (their K/V are already in the pages).  Warp roles:
+//   warp 0      TMA producer: the Q tile once (two 64-column halves, 128-byte swizzle), then per KV
+//               tile of 128 keys the 8 pages of K and of V (16 x 64 boxes of a 3-D map over the cache,
+//               [layer * pages * kv heads, 16 tokens, head dim]) into a 2-stage ring;
+//   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M = N = 128, K = head dim) into one of
+//               two TMEM S buffers, and O_j = P_j V_j (V as an MN-major operand: keys x head dim as it
+//               sits in the pages) into one of two TMEM O buffers; tcgen05.commit releases each stage;
+//   warps 2-5   softmax, one thread per query row (TMEM lane = row): pass 1 reads S and takes the
+//               masked row max, pass 2 reads it again and writes P = exp2(S - max) as bf16 into shared
+//               memory in the 128-byte-swizzled K-major layout the P.V MMA reads; the row's running
+//               output stays in registers, O_{j-1} is folded in with the online-softmax correction.
+// S of tile j + 1 is computed while tile j's softmax runs.  Every wait is bounded (tc::mbar_wait);
+// no load uses multicast.  Head dim 128, no window / soft-cap (those shapes use k_prefill_attn).
+// Reference: k_flash_attention, internal/compute/cuda_kernels.cu:701-759 (one block per head, SIMT).
+#include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cudaTypedefs.h>
+
+#include "mma.cuh"
+#include "tc.cuh"
+
+using namespace fak;
+
+namespace {
+
+constexpr int FA_QT = 128;     // queries per tile
+constexpr int FA_KT = 128;     // keys per KV tile (8 pages)
+constexpr int FA_D = 128;      // head dim
+constexpr int FA_PG = 16;      // tokens per page
+constexpr int FA_STAGES = 2;
+constexpr int FA_THREADS = 192;
+
+struct FaSmem {
+  alignas(1024) __nv_bfloat16 q[2][FA_QT * 64];               // [D half][128 rows x 64]
+  alignas(1024) __nv_bfloat16 k[FA_STAGES][2][FA_KT * 64];    // [stage][D half][128 keys x 64]
+  alignas(1024) __nv_bfloat16 v[FA_STAGES][2][FA_KT * 64];
+  alignas(1024) __nv_bfloat16 p[2][FA_QT * 64];               // [key half][128 rows x 64 keys]
+  uint64_t q_full;
+  uint64_t kv_full[FA_STAGES], kv_empty[FA_STAGES];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full, p_free;
+  uint64_t o_full[2], o_free[2];
+  uint32_t tmem_base;
+};
+
+FAK_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          tc::smem_addr(dst)),
+      "l"(map), "r"(tc::smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Shared-memory descriptor of an MN-major operand in the 128-byte swizzle (rows of 128 bytes along
+// MN = 64 bf16, atoms of 8 such rows along K): SBO = byte step between 8-row groups along K, LBO =
+// byte step between 64-element groups along MN.
+FAK_DEV uint64_t smem_desc_sw128_mn(const void* p, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t addr = tc::smem_addr(p);
+  uint64_t d = 0;
+  d |= (addr & 0x3FFFFull) >> 4;
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;   // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;   // 128-byte swizzle
+  return d;
+}
+
+__global__ void __launch_bounds__(FA_THREADS, 1)
+k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                  const __grid_constant__ CUtensorMap tmap_v, int layer, int n_pages, int Hkv, int Hq,
+                  const int* __restrict__ block_table, int bt_stride, const int* __restrict__ tile_seq,
+                  const int* __restrict__ tile_q0, const int* __restrict__ seq_qoff, const int* __restrict__ seq_qlen,
+                  const int* __restrict__ seq_pos0, __nv_bfloat16* __restrict__ out, int64_t ldo, float scale_log2,
+                  int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  FaSmem& sm = *reinterpret_cast<FaSmem*>(base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int g = h / (Hq / Hkv);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < FA_STAGES; s++) {
+      tc::mbar_init(&sm.kv_full[s], 1);
+      tc::mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      tc::mbar_init(&sm.s_full[i], 1);
+      tc::mbar_init(&sm.s_free[i], 4);   // one arrival per softmax warp
+      tc::mbar_init(&sm.o_full[i], 1);
+      tc::mbar_init(&sm.o_free[i], 4);
+    }
+    tc::mbar_init(&sm.p_full, 4);
+    tc::mbar_init(&sm.p_free, 1);
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmap_q);
+    tc::prefetch_tmap(&tmap_k);
+    tc::prefetch_tmap(&tmap_v);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sm.tmem_base, 512);   // S0 S1 O0 O1, 128 columns each
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  pdl_wait();   // Q and the chunk's K / V come from the previous kernel
+
+  const int s = tile_seq[tile], q0 = tile_q0[tile];
+  const int qlen = seq_qlen[s], qoff = seq_qoff[s], pos0 = seq_pos0[s];
+  const int q_end = min(qlen, q0 + FA_QT);
+  const int kmax = pos0 + q_end;                    // keys visible to the tile's last query
+  const int NJ = (kmax + FA_KT - 1) / FA_KT;
+  const int n_valid_pages = (kmax + FA_PG - 1) / FA_PG;
+  const int* bt = block_table + (int64_t)s * bt_stride;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tc::mbar_arrive_expect_tx(&sm.q_full, FA_QT * FA_D * 2);
+      tc::tma_load_2d(sm.q[0], &tmap_q, &sm.q_full, h * FA_D, qoff + q0);
+      tc::tma_load_2d(sm.q[1], &tmap_q, &sm.q_full, h * FA_D + 64, qoff + q0);
+      for (int j = 0; j < NJ; j++) {
+        const int st = j % FA_STAGES;
+        const uint32_t ph = (uint32_t)((j / FA_STAGES) & 1);
+        tc::mbar_wait(&sm.kv_empty[st], ph ^ 1, err);
+        tc::mbar_arrive_expect_tx(&sm.kv_full[st], 2 * FA_KT * FA_D * 2);
+#pragma unroll 1
+        for (int pi = 0; pi < FA_KT / FA_PG; pi++) {
+          // pages past the visible keys repeat the last one (their keys are masked; the data stays finite)
+          const int pidx = min(j * (FA_KT / FA_PG) + pi, n_valid_pages - 1);
+          const int z = (layer * n_pages + bt[pidx]) * Hkv + g;
+          for (int hd = 0; hd < 2; hd++) {
+            tma_load_3d(sm.k[st][hd] + pi * FA_PG * 64, &tmap_k, &sm.kv_full[st], hd * 64, 0, z);
+            tma_load_3d(sm.v[st][hd] + pi * FA_PG * 64, &tmap_v, &sm.kv_full[st], hd * 64, 0, z);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = tc::idesc_bf16_f32(FA_QT, FA_KT);
+      constexpr uint32_t idesc_pv = tc::idesc_bf16_f32(FA_QT, FA_D) | (1u << 16);   // B (V) MN-major
+      tc::mbar_wait(&sm.q_full, 0, err);
+      for (int j = 0; j <= NJ; j++) {
+        if (j < NJ) {
+          const int st = j % FA_STAGES, b = j & 1;
+          tc::mbar_wait(&sm.kv_full[st], (uint32_t)((j / FA_STAGES) & 1), err);
+          tc::mbar_wait(&sm.s_free[b], (uint32_t)(((j >> 1) & 1) ^ 1), err);
+          tc::tc_fence_after();
+          const uint32_t ts = tmem + (uint32_t)(b * 128);
+#pragma unroll
+          for (int hd = 0; hd < 2; hd++) {
+            const uint64_t ad = tc::smem_desc_sw128(sm.q[hd]);
+            const uint64_t bd = tc::smem_desc_sw128(sm.k[st][hd]);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) tc::mma_bf16(ts, ad + 2 * kk, bd + 2 * kk, idesc_s, (hd | kk) != 0);
+          }
+          tc::mma_commit(&sm.s_full[b]);
+        }
+        if (j > 0) {
+          const int jj = j - 1, st = jj % FA_STAGES, bo = jj & 1;
+          tc::mbar_wait(&sm.p_full, (uint32_t)(jj & 1), err);
+          tc::mbar_wait(&sm.o_free[bo], (uint32_t)(((jj >> 1) & 1) ^ 1), err);
+          tc::tc_fence_after();
+          const uint32_t to = tmem + 256u + (uint32_t)(bo * 128);
+#pragma unroll
+          for (int ks = 0; ks < FA_KT / 16; ks++) {
+            const uint64_t ad = tc::smem_desc_sw128(sm.p[ks >> 2]) + 2 * (ks & 3);
+            // 16 keys per step = 2 swizzle atoms of V; the two 64-column halves of the head dim are
+            // 16 KB apart (LBO), 8-key groups 1 KB apart (SBO)
+            const uint64_t bd = smem_desc_sw128_mn(sm.v[st][0] + ks * 16 * 64, FA_KT * 128, 1024);
+            tc::mma_bf16(to, ad, bd, idesc_pv, ks != 0);
+          }
+          tc::mma_commit(&sm.o_full[bo]);
+          tc::mma_commit(&sm.p_free);
+          tc::mma_commit(&sm.kv_empty[st]);
+        }
+      }
+    }
+  } else {
+    // softmax warps 2..5: TMEM lane quarter = warp % 4, one query row per thread
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qi = q0 + r;
+    const int pos = pos0 + qi;            // keys [0, pos] are visible
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float o[FA_D];
+#pragma unroll
+    for (int d = 0; d < FA_D; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, corr_prev = 1.f;
+    uint8_t* prow = reinterpret_cast<uint8_t*>(sm.p[0]) + r * 128;
+    for (int j = 0; j < NJ; j++) {
+      const int b = j & 1;
+      tc::mbar_wait(&sm.s_full[b], (uint32_t)((j >> 1) & 1), err);
+      tc::tc_fence_after();
+      const uint32_t ts = tmem + lane_off + (uint32_t)(b * 128);
+      const int k0 = j * FA_KT;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 8; c++) {
+        uint32_t v16[16];
+        tc::tmem_ld16(ts + c * 16, v16);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+          const float sv = k0 + c * 16 + e <= pos ? __uint_as_float(v16[e]) * scale_log2 : -INFINITY;
+          mx = fmaxf(mx, sv);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float bse = m_new == -INFINITY ? 0.f : m_new;
+      const float corr = exp2f(m - bse);
+      // P's buffer is free once the previous tile's P.V has completed
+      tc::mbar_wait(&sm.p_free, (uint32_t)((j & 1) ^ 1), err);
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 8; c++) {
+        uint32_t v16[16];
+        tc::tmem_ld16(ts + c * 16, v16);
+        tc::tmem_ld_wait();
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const int kk = k0 + c * 16 + e;
+          const float p0 = kk <= pos ? exp2f(__uint_as_float(v16[e]) * scale_log2 - bse) : 0.f;
+          const float p1 = kk + 1 <= pos ? exp2f(__uint_as_float(v16[e + 1]) * scale_log2 - bse) : 0.f;
+          sum += p0 + p1;
+          pk[e >> 1] = pack_bf16(p0, p1);
+        }
+        // keys c*16 .. c*16+15: half c/4 of P, 16-byte chunks 2(c%4) and 2(c%4)+1 of the row, swizzled
+        uint8_t* ph = prow + (c >> 2) * (FA_QT * 128);
+        const int ch0 = 2 * (c & 3), ch1 = ch0 + 1;
+        *reinterpret_cast<uint4*>(ph + 16 * (ch0 ^ (r & 7))) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(ph + 16 * (ch1 ^ (r & 7))) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      tc::tc_fence_before();
+      tc::fence_proxy_async();   // generic-proxy stores of P -> visible to the tensor cores
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(&sm.s_free[b]);
+        tc::mbar_arrive(&sm.p_full);
+      }
+      l = l * corr + sum;
+      m = m_new;
+      if (j > 0) {   // fold in O_{j-1} (relative to the max before this tile)
+        const int bo = (j - 1) & 1;
+        tc::mbar_wait(&sm.o_full[bo], (uint32_t)(((j - 1) >> 1) & 1), err);
+        tc::tc_fence_after();
+        const uint32_t to = tmem + lane_off + 256u + (uint32_t)(bo * 128);
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          uint32_t v16[16];
+          tc::tmem_ld16(to + c * 16, v16);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; e++) o[c * 16 + e] = fmaf(o[c * 16 + e], corr_prev, __uint_as_float(v16[e]));
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&sm.o_free[bo]);
+      }
+      corr_prev = corr;
+    }
+    {   // the last tile's P.V
+      const int bo = (NJ - 1) & 1;
+      tc::mbar_wait(&sm.o_full[bo], (uint32_t)(((NJ - 1) >> 1) & 1), err);
+      tc::tc_fence_after();
+      const uint32_t to = tmem + lane_off + 256u + (uint32_t)(bo * 128);
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        uint32_t v16[16];
+        tc::tmem_ld16(to + c * 16, v16);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; e++) o[c * 16 + e] = fmaf(o[c * 16 + e], corr_prev, __uint_as_float(v16[e]));
+      }
+    }
+    if (qi < q_end) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = out + (int64_t)(qoff + qi) * ldo + (int64_t)h * FA_D;
+#pragma unroll
+      for (int d = 0; d < FA_D; d += 8) {
+        uint4 w = make_uint4(pack_bf16(o[d] * inv, o[d + 1] * inv), pack_bf16(o[d + 2] * inv, o[d + 3] * inv),
+                             pack_bf16(o[d + 4] * inv, o[d + 5] * inv), pack_bf16(o[d + 6] * inv, o[d + 7] * inv));
+        *reinterpret_cast<uint4*>(dst + d) = w;
+      }
+    }
+  }
+  pdl_launch_dependents();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 fa_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    FAK_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// q [T, Hq, D] bf16 (after RoPE); k_cache / v_cache: the whole cache [L, P, Hkv, 16, D] bf16; layer;
+// block_table [S, W] int32; 128-query tiles (tile_seq, tile_q0, n_tiles) over the chunk's sequences
+// (seq_qoff / seq_qlen / seq_pos0); out [T, Hq * D] bf16 (row stride ldo).
+void prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, int64_t layer,
+                          torch::Tensor block_table, torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff,
+                          torch::Tensor seq_qlen, torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out,
+                          c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.is_contiguous() &&
+                  q.size(2) == FA_D, "prefill_attention_tc: q [T, Hq, 128] bf16");
+  TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 5 && k_cache.is_contiguous() &&
+                  k_cache.size(3) == FA_PG && k_cache.size(4) == FA_D && v_cache.sizes() == k_cache.sizes() &&
+                  v_cache.is_contiguous(), "prefill_attention_tc: caches [L, P, Hkv, 16, 128] bf16");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.stride(1) == 1 && out.stride(0) % 8 == 0,
+              "prefill_attention_tc: out [T, >=Hq*128] bf16");
+  const int T = (int)q.size(0), Hq = (int)q.size(1);
+  const int L = (int)k_cache.size(0), P = (int)k_cache.size(1), Hkv = (int)k_cache.size(2);
+  TORCH_CHECK(Hq % Hkv == 0 && layer >= 0 && layer < L, "prefill_attention_tc: heads / layer");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && block_table.stride(1) == 1, "prefill_attention_tc: bt");
+  if (n_tiles <= 0 || T == 0) return;
+  CUtensorMap mq, mk, mv;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)Hq * FA_D, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)Hq * FA_D * 2};
+    cuuint32_t box[2] = {64, FA_QT};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult rr = fa_encode()(&mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q.data_ptr(), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(rr == CUDA_SUCCESS, "prefill_attention_tc: Q tensor map (", (int)rr, ")");
+  }
+  auto cache_map = [&](CUtensorMap& m, const torch::Tensor& t) {
+    cuuint64_t dims[3] = {(cuuint64_t)FA_D, (cuuint64_t)FA_PG, (cuuint64_t)L * P * Hkv};
+    cuuint64_t strides[2] = {(cuuint64_t)FA_D * 2, (cuuint64_t)FA_PG * FA_D * 2};
+    cuuint32_t box[3] = {64, FA_PG, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult rr = fa_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(rr == CUDA_SUCCESS, "prefill_attention_tc: KV tensor map (", (int)rr, ")");
+  };
+  cache_map(mk, k_cache);
+  cache_map(mv, v_cache);
+  const size_t smem = sizeof(FaSmem) + 1024;
+  FAK_CUDA_CHECK(cudaFuncSetAttribute(k_prefill_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)n_tiles, (unsigned)Hq);
+  cfg.blockDim = dim3(FA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const float scale_log2 = (1.0f / sqrtf((float)FA_D)) * 1.4426950408889634f;
+  int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_prefill_attn_tc, mq, mk, mv, (int)layer, P, Hkv, Hq,
+                                    (const int*)block_table.data_ptr<int>(), (int)block_table.stride(0),
+                                    (const int*)tile_seq.data_ptr<int>(), (const int*)tile_q0.data_ptr<int>(),
+                                    (const int*)seq_qoff.data_ptr<int>(), (const int*)seq_qlen.data_ptr<int>(),
+                                    (const int*)seq_pos0.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
+                                    (int64_t)out.stride(0), scale_log2, ep));
+}

@@ -369,7 +369,7 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& 
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, reinterpret_cast<OutT*>(out.data_ptr()),

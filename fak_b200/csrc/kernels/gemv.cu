@@ -356,7 +356,7 @@ void qgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, 
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const uint8_t* W = w.data_ptr<uint8_t>();

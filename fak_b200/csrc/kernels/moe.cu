@@ -279,7 +279,7 @@ cudaLaunchConfig_t cfg_pdl(dim3 g, dim3 b, size_t smem, cudaLaunchAttribute* att
   cfg.dynamicSmemBytes = smem;
   cfg.stream = at::cuda::getCurrentCUDAStream();
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cfg;

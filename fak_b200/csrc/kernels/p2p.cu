@@ -228,7 +228,7 @@ cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaLaunchAttribute* attr) {
   cfg.blockDim = block;
   cfg.stream = at::cuda::getCurrentCUDAStream();
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cfg;

@@ -422,7 +422,7 @@ void qmmv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, int64_t pitch, t
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int ub = qtype == QT_Q4_K ? 144 : (qtype == QT_Q6_K ? 210 : 8 * 34);
@@ -510,7 +510,7 @@ void quant_act_wide(torch::Tensor x, c10::optional<torch::Tensor> gamma, double 
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_quant_act_wide, (const float*)x.data_ptr<float>(), (int64_t)x.stride(0), g,

@@ -348,7 +348,7 @@ void quant_act(torch::Tensor x, c10::optional<torch::Tensor> gamma, double eps, 
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_quant_act, (const float*)x.data_ptr<float>(), (int64_t)x.stride(0), g,

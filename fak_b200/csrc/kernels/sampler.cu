@@ -330,7 +330,7 @@ void sample_rows(torch::Tensor logits, int64_t V, torch::Tensor params, torch::T
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_sample_rows, logits.data_ptr<float>(), (int64_t)logits.stride(0), (int)V,

@@ -62,7 +62,7 @@ void decode_advance(torch::Tensor next, torch::Tensor ids, torch::Tensor pos, to
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_decode_advance, (const int*)next.data_ptr<int>(), ids.data_ptr<int>(),

@@ -39,9 +39,12 @@ FAK_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: returns false (and records code 1 in *err) if the phase never completed.
+// Once any wait of the launch has given up (the error word is set), later waits give up after at
+// most 1024 polls instead of their full budget, so a failed launch drains in bounded time.
 FAK_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   for (uint32_t i = 0; i < kWaitLimit; i++) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && err && *reinterpret_cast<volatile int*>(err) != 0) return false;
   }
   report_error(err, 1);
   return false;

@@ -394,9 +394,9 @@ FAK_DEV void unit_tile_q6k_us(const uint8_t* __restrict__ wt, const int8_t* __re
         const uint32_t a1 = ((lb >> ls) & 0x0F0F0F0Fu) | (((hb >> hs) & 0x03030303u) << 4);
         const int e0 = 128 * n + 32 * kk + 16 * h;   // first weight of this 16-block
         const int j = e0 >> 4;                         // sub-block 0..15
-        // signed scale bytes (sign-replicating byte permute)
-        const int sa = (int)__byte_perm(scAw[j >> 2], 0u, 0x8880u | ((j & 3) * 0x1111u));
-        const int sb = (int)__byte_perm(scBw[j >> 2], 0u, 0x8880u | ((j & 3) * 0x1111u));
+        // signed scale bytes: byte j & 3 moved to the top, then an arithmetic shift sign-extends it
+        const int sa = (int)(scAw[j >> 2] << (24 - 8 * (j & 3))) >> 24;
+        const int sb = (int)(scBw[j >> 2] << (24 - 8 * (j & 3))) >> 24;
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
           const uint32_t xv = *reinterpret_cast<const uint32_t*>(xr + nt * 8 * xstride + e0 + 4 * t);
@@ -1071,7 +1071,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
@@ -1153,7 +1153,7 @@ void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t 
   cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   auto go = [&](auto kern) {

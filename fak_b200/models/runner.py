@@ -61,25 +61,34 @@ class KVCache:
 
 @dataclasses.dataclass
 class PrefillMeta:
-    """Packed ragged chunk description (all int32 device tensors)."""
+    """Packed ragged chunk description (all int32 device tensors): 64-query tiles for the mma.sync
+    kernel and 128-query tiles (``tile128_*``) for the tcgen05 kernel."""
     tile_seq: torch.Tensor
     tile_q0: torch.Tensor
     seq_qoff: torch.Tensor
     seq_qlen: torch.Tensor
     seq_pos0: torch.Tensor
     n_tiles: int
+    tile128_seq: torch.Tensor | None = None
+    tile128_q0: torch.Tensor | None = None
+    n_tiles128: int = 0
 
     @classmethod
     def build(cls, qlens: list[int], pos0s: list[int], device) -> "PrefillMeta":
         tile_seq, tile_q0, off, offs = [], [], 0, []
+        t128_seq, t128_q0 = [], []
         for s, ql in enumerate(qlens):
             offs.append(off)
             for q0 in range(0, ql, 64):
                 tile_seq.append(s)
                 tile_q0.append(q0)
+            for q0 in range(0, ql, 128):
+                t128_seq.append(s)
+                t128_q0.append(q0)
             off += ql
         mk = lambda a: torch.tensor(a, dtype=torch.int32).to(device, non_blocking=True)
-        return cls(mk(tile_seq), mk(tile_q0), mk(offs), mk(qlens), mk(pos0s), len(tile_seq))
+        return cls(mk(tile_seq), mk(tile_q0), mk(offs), mk(qlens), mk(pos0s), len(tile_seq),
+                   mk(t128_seq), mk(t128_q0), len(t128_seq))
 
 
 class ModelRunner:
@@ -153,6 +162,10 @@ class ModelRunner:
         self.bias_tok = torch.full((MAX_BIAS,), -1, dtype=torch.int32, device=dev)
         self.bias_val = torch.zeros(MAX_BIAS, dtype=torch.float32, device=dev)
         self.counts = torch.zeros(B, cfg.vocab_size, dtype=torch.int32, device=dev)
+        # prefill attention on tcgen05 / TMEM (head dim 128, default scale, no soft-cap; windowed
+        # layers and other shapes use the mma.sync kernel); FAK_PREFILL_ATTN=fa2 forces the latter
+        self.tc_prefill_attn = (self.D == 128 and cfg.attn_scale == 0 and cfg.attn_softcap == 0
+                                and os.environ.get("FAK_PREFILL_ATTN", "tc") != "fa2")
         self.max_split = 64
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
         self.n_split = int(os.environ.get("FAK_DEC_SPLITS", "0")) or 16
@@ -439,8 +452,11 @@ class ModelRunner:
                 K.gemm(hb, seg, qkv[:, off:off + seg.rows], K.EPI_STORE, bias)
             K.rope_kv(qkv, pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
                       None, qb, self.kv.k[i], self.kv.v[i])
-            K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab, cfg.layer_window(i), cfg.attn_scale,
-                                cfg.attn_softcap)
+            if self.tc_prefill_attn and cfg.layer_window(i) <= 0:
+                K.prefill_attention_tc(qb, self.kv.k, self.kv.v, i, bt, meta, ab, self.err)
+            else:
+                K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab, cfg.layer_window(i),
+                                    cfg.attn_scale, cfg.attn_softcap)
             if self.coll is None and L.post_attn_norm is not None:
                 K.gemm(ab, L.o, tmp, K.EPI_STORE)
                 K.rmsnorm_add(tmp, L.post_attn_norm, cfg.rms_eps, x)

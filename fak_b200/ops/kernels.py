@@ -199,6 +199,14 @@ def prefill_attention(q, k_cache, v_cache, block_table, meta, out, window: int =
     count()
 
 
+def prefill_attention_tc(q, k_cache_all, v_cache_all, layer: int, block_table, meta, out, err=None) -> None:
+    """Causal paged prefill attention on tcgen05 / TMEM: q [T, H, 128] bf16, the whole caches
+    [L, P, Hkv, 16, 128] and the layer index (one TMA map covers every layer), out [T, H*128] bf16."""
+    ext().prefill_attention_tc(q, k_cache_all, v_cache_all, layer, block_table, meta.tile128_seq, meta.tile128_q0,
+                               meta.seq_qoff, meta.seq_qlen, meta.seq_pos0, meta.n_tiles128, out, err)
+    count()
+
+
 def kv_move(kv, src_slot: torch.Tensor, dst_slot: torch.Tensor, rot: torch.Tensor, cos_n: torch.Tensor,
             sin_n: torch.Tensor) -> None:
     """Move K/V rows (all layers) from src to dst slots; keys of rows with rot=1 are re-rotated back

@@ -187,6 +187,52 @@ def test_prefill_attention(D, H, Hkv, window):
         off += ql
 
 
+@pytest.mark.parametrize("H,Hkv", [(28, 4), (8, 8)])
+@pytest.mark.parametrize("qlens,pos0s", [([256, 256, 5], [8192, 300, 40]), ([130, 1, 383], [0, 17, 1000])])
+def test_prefill_attention_tcgen05(H, Hkv, qlens, pos0s):
+    """The tcgen05 / TMEM prefill attention against an fp32 reference (ragged chunk, cached prefixes,
+    partial 128-query tiles, keys not a multiple of the 128-key tile), over a multi-layer cache."""
+    from fak_b200.models.runner import PrefillMeta
+    from fak_b200.ops import kernels as K
+    D, L, layer = 128, 3, 1
+    ctx = [p + q for p, q in zip(pos0s, qlens)]
+    n_pages = sum(math.ceil(c / 16) for c in ctx) + 8
+    g = torch.Generator(device="cuda").manual_seed(7)
+    kc = torch.randn(L, n_pages, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+    vc = torch.randn(L, n_pages, Hkv, 16, D, device="cuda", generator=g).bfloat16()
+    perm = torch.randperm(n_pages - 1, generator=torch.Generator().manual_seed(3)) + 1
+    W = max(math.ceil(c / 16) for c in ctx)
+    bt = torch.zeros(len(ctx), W, dtype=torch.int32)
+    used = 0
+    for i, c in enumerate(ctx):
+        n = math.ceil(c / 16)
+        bt[i, :n] = perm[used:used + n]
+        used += n
+    bt = bt.cuda()
+    T = sum(qlens)
+    q = (torch.randn(T, H, D, device="cuda", generator=g) * 1.5).bfloat16()
+    out = torch.zeros(T, H * D, device="cuda", dtype=torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    meta = PrefillMeta.build(qlens, pos0s, "cuda")
+    K.prefill_attention_tc(q, kc, vc, layer, bt, meta, out, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    G = H // Hkv
+    off = 0
+    for s, (ql, p0) in enumerate(zip(qlens, pos0s)):
+        Kb = _gather(kc[layer], bt[s], p0 + ql).repeat_interleave(G, 1)
+        Vb = _gather(vc[layer], bt[s], p0 + ql).repeat_interleave(G, 1)
+        qs = q[off:off + ql].float()
+        sc = torch.einsum("qhd,thd->hqt", qs, Kb) / math.sqrt(D)
+        qpos = torch.arange(p0, p0 + ql, device="cuda")[:, None]
+        kpos = torch.arange(p0 + ql, device="cuda")[None, :]
+        sc = sc.masked_fill((kpos > qpos)[None], float("-inf"))
+        ref = torch.einsum("hqt,thd->qhd", torch.softmax(sc, -1), Vb).reshape(ql, -1)
+        got = out[off:off + ql].float()
+        assert torch.allclose(got, ref, atol=3e-2, rtol=3e-2), (s, (got - ref).abs().max())
+        off += ql
+
+
 @pytest.mark.parametrize("D,qk_norm", [(128, False), (64, True)])
 def test_rope_kv(D, qk_norm):
     from fak_b200.models.reference import apply_rope, rmsnorm, rope_cos_sin
