@@ -28,6 +28,8 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--split", type=int, default=16)
+    ap.add_argument("--pps", type=int, default=1, help="pages per split (a lower bound; with --split large enough "
+                    "for the context, each split holds exactly this many pages)")
     ap.add_argument("--prefill", type=int, default=0,
                     help="time prefill attention instead: each sequence's last N tokens attend to the whole context")
     ap.add_argument("--impl", default="tc", choices=("tc", "fa2"),
@@ -62,7 +64,7 @@ def main(argv=None):
 
     def run(i):
         kc, vc = caches[i % args.layers]
-        K.decode_attention(q, kc, vc, bt, ctx_t, args.split, act=act, workspace=ws, **casc)
+        K.decode_attention(q, kc, vc, bt, ctx_t, args.split, act=act, workspace=ws, pages_per_split=args.pps, **casc)
 
     if args.prefill:   # B chunks of the last `prefill` tokens over the cached context
         from fak_b200.models.runner import PrefillMeta
@@ -99,7 +101,8 @@ def main(argv=None):
     print(json.dumps({"kernel": "prefill_attention" if args.prefill else "decode_attention+combine",
                       "prefill": args.prefill, **extra,
                       "batch": B, "ctx": ctx, "shared": n_sh * 16,
-                      "heads": H, "kv_heads": Hkv, "head_dim": D, "splits": args.split, "cascade": args.cascade,
+                      "heads": H, "kv_heads": Hkv, "head_dim": D, "splits": args.split, "pps": args.pps,
+                      "cascade": args.cascade,
                       "us": round(us, 2),
                       "unique_kv_bytes": unique, "tb_s_unique": round(unique / us / 1e6, 3),
                       "tb_s_streamed": round(B * per_seq * page_bytes / us / 1e6, 3)}))

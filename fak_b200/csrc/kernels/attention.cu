@@ -105,6 +105,9 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   const int pps = max(pages_per_split, (n_pages - pg0 + n_split - 1) / n_split);
   const int p_begin = pg0 + split * pps;
   const int p_end = min(n_pages, p_begin + pps);
+  // a split past the live pages writes nothing: the combine reads only the live splits
+  // (dec_live_splits); the in-kernel merge (tickets) needs every split's ticket, so it keeps them
+  if (p_begin >= p_end && n_slots > 1 && tickets == nullptr) return;
 
   // Q fragments (rows = query heads of this group, zero beyond G)
   uint32_t qa[KS][4];
@@ -470,18 +473,35 @@ k_decode_attn_prefix(const float* __restrict__ q, const __nv_bfloat16* __restric
   }
 }
 
+// Suffix splits of k_decode_attn that hold pages for a sequence of ctx tokens: the same page range
+// arithmetic as the kernel (window start, pages another kernel covers, pages per split).
+FAK_DEV int dec_live_splits(int ctx, int win, const int* skip_pages, int n_split, int pages_per_split) {
+  const int n_pages = (ctx + PAGE - 1) / PAGE;
+  int lo = win > 0 ? max(0, ctx - win) : 0;
+  if (skip_pages != nullptr) lo = max(lo, min(ctx, *skip_pages * PAGE));
+  const int live = n_pages - lo / PAGE;
+  if (live <= 0) return 0;
+  const int pps = max(pages_per_split, (live + n_split - 1) / n_split);
+  return min(n_split, (live + pps - 1) / pps);
+}
+
+// Merges slots [0, slot0) (cascade prefix splits, all written) and the live suffix splits
+// [slot0, slot0 + live) of each (sequence, head); splits past a sequence's pages wrote nothing.
 template <int D>
 __global__ void __launch_bounds__(D)
-k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int H, int n_split,
-                 float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds, int ldo) {
+k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int H, int n_slots,
+                 float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds, int ldo,
+                 const int* __restrict__ ctx_len, int win, const int* __restrict__ skip_pages, int slot0, int n_split,
+                 int pages_per_split) {
   pdl_wait();
   const int b = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
-  const int64_t base = ((int64_t)b * H + h) * n_split;
+  const int64_t base = ((int64_t)b * H + h) * n_slots;
+  const int n_used = slot0 + dec_live_splits(ctx_len[b], win, skip_pages, n_split, pages_per_split);
   float mstar = NEG_INF;
-  for (int s = 0; s < n_split; s++) mstar = fmaxf(mstar, part_ml[base + s].x);
+  for (int s = 0; s < n_used; s++) mstar = fmaxf(mstar, part_ml[base + s].x);
   float mb = mstar == NEG_INF ? 0.f : mstar;
   float L = 0.f, acc = 0.f;
-  for (int s = 0; s < n_split; s++) {
+  for (int s = 0; s < n_used; s++) {
     float2 ml = part_ml[base + s];
     float f = exp2f(ml.x - mb);
     L += f * ml.y;
@@ -796,12 +816,15 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     c2.blockDim = dim3(D);
     c2.stream = stream;
     set_pdl(c2);
+    const int* cl = (const int*)ctx_len.data_ptr<int>();
     if (D == 128)
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H,
-                                        (int)n_slots, op, qp, dp, (int)ldo));
+                                        (int)n_slots, op, qp, dp, (int)ldo, cl, (int)window, skip, slot0, (int)n_split,
+                                        (int)pages_per_split));
     else
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H,
-                                        (int)n_slots, op, qp, dp, (int)ldo));
+                                        (int)n_slots, op, qp, dp, (int)ldo, cl, (int)window, skip, slot0, (int)n_split,
+                                        (int)pages_per_split));
   }
 }
 
@@ -959,10 +982,10 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     c2.stream = static_cast<cudaStream_t>(stream);
     if (D == 128)
       e = cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
-                             dp, ldo);
+                             dp, ldo, ctx_len, 0, (const int*)nullptr, 0, n_split, pages_per_split);
     else
       e = cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
-                             dp, ldo);
+                             dp, ldo, ctx_len, 0, (const int*)nullptr, 0, n_split, pages_per_split);
     if (e != cudaSuccess) return noalloc_fail(err, err_len, FAK_NOALLOC_ECUDA, "decode combine launch: %s", cudaGetErrorString(e));
   }
   return FAK_NOALLOC_OK;

@@ -127,15 +127,23 @@ class ModelRunner:
         gap = cfg.device_gap()
         if gap:
             raise NotImplementedError(f"{gap}; run it on the fp32 reference model (models.reference.ReferenceModel)")
-        # activations quantized by quant_act feed the GEMVs with one scale per 256 columns
-        # (FAK_UNIT_SCALE=0 restores one scale per 32)
-        unit = os.environ.get("FAK_UNIT_SCALE", "1") != "0"
-        self.act_d = K.ActQ(B, d, dev, unit=unit)
+        # activations quantized by quant_act feed the GEMVs with one scale per 256 columns when every
+        # matrix that reads them is Q4_K / Q6_K (their integer-accumulating path); other formats gain
+        # nothing from the coarser scale and keep one per 32 (so does FAK_UNIT_SCALE=0)
+        unit_ok = os.environ.get("FAK_UNIT_SCALE", "1") != "0"
+
+        def unit_for(mats) -> bool:
+            return unit_ok and all(m is not None and m.qtype in (12, 14) for m in mats)   # Q4_K, Q6_K
+        dense_layers = [L for L in weights.layers if getattr(L, "gate_up", None) is not None]
+        unit_d = unit_for([sg for L in weights.layers for sg, _ in L.qkv] + [L.gate_up for L in dense_layers]) \
+            and not cfg.is_moe
+        unit_f = unit_for([L.down for L in dense_layers]) and bool(dense_layers)
+        self.act_d = K.ActQ(B, d, dev, unit=unit_d)
         # o_proj input: this rank's slice [a0, a1) of the attention output columns (all of them on one
         # GPU); under TP the columns of other ranks' heads inside the slice stay zero
         a0, a1, _, _ = weights.o_cols if weights.o_cols[1] else (0, cfg.n_heads * self.D, 0, 0)
         self.act_attn = K.ActQ(B, a1 - a0, dev)
-        self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev, unit=unit)
+        self.act_ffn = K.ActQ(B, max(self.ffn_local, 32), dev, unit=unit_f)
         # decode GEMV inputs: activations quantized by a separate kernel (default), or fp32 sources
         # the GEMV normalises and quantizes itself (fused_activations: fewer launches, but every CTA
         # repeats the row's quantization; measured 0.14 ms/step slower on Qwen2.5-7B B=5).
@@ -166,11 +174,17 @@ class ModelRunner:
         # layers and other shapes use the mma.sync kernel); FAK_PREFILL_ATTN=fa2 forces the latter
         self.tc_prefill_attn = (self.D == 128 and cfg.attn_scale == 0 and cfg.attn_softcap == 0
                                 and os.environ.get("FAK_PREFILL_ATTN", "tc") != "fa2")
-        self.max_split = 64
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
-        self.n_split = int(os.environ.get("FAK_DEC_SPLITS", "0")) or 16
-        if not 1 <= self.n_split <= self.max_split:
-            raise ValueError(f"decode attention splits must be in [1, {self.max_split}]")
+        # decode attention: with dec_pps > 0 a split holds dec_pps pages (more for contexts past
+        # dec_pps x 256 pages) and the grid has a split for every dec_pps pages of the longest
+        # context; splits past a sequence's pages exit at once.  0: 16 splits spread over the pages.
+        self.dec_pps = int(os.environ.get("FAK_DEC_PPS", "0"))
+        max_pages = -(-self.max_context // 16)
+        auto = min(256, -(-max_pages // self.dec_pps)) if self.dec_pps > 0 else 16
+        self.n_split = int(os.environ.get("FAK_DEC_SPLITS", "0")) or auto
+        self.max_split = max(64, self.n_split)
+        if not 1 <= self.n_split <= 256:
+            raise ValueError("decode attention splits must be in [1, 256]")
         # cascade attention: prefix splits of the shared pages (about 2.6 CTAs per SM at 4 KV heads)
         self.prefix_splits = max(16, min(128, (5 * n_sm) // (2 * max(1, self.Hkv))))
         b_casc = min(B, 64 // max(1, self.Hq // max(1, self.Hkv)))   # lanes a cascade step can hold
@@ -241,7 +255,8 @@ class ModelRunner:
         K.rope_kv(self.qkv[:B], pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
                   self.q[:B], None, kv.k[i], kv.v[i])
         if self.coll is None:
-            K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.act_attn,
+            K.decode_attention(self.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, pages_per_split=max(1, self.dec_pps),
+                               act=self.act_attn,
                                workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None,
                                prefetch=self._pf(L.o), window=cfg.layer_window(i),
                                scale=cfg.attn_scale, softcap=cfg.attn_softcap,

@@ -174,15 +174,17 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
                      workspace=None, ldo: int = 0, tickets=None, prefetch: torch.Tensor | None = None,
                      window: int = 0, shared_pages: torch.Tensor | None = None, prefix_splits: int = 0,
-                     scale: float = 0.0, softcap: float = 0.0) -> None:
-    """ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
+                     scale: float = 0.0, softcap: float = 0.0, pages_per_split: int = 1) -> None:
+    """n_split splits of at least pages_per_split pages each (a sequence's live pages spread evenly
+    over the splits when there are more; splits past its pages are skipped).
+    ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
     [B * kv heads]; when given, the last split of each (sequence, KV group) merges the splits in the
     same kernel instead of a separate combine launch (the kernel leaves the tickets at zero).
     window > 0: sliding-window attention over the last ``window`` keys.
     shared_pages (int32 [1] on the device) with prefix_splits > 0: cascade attention -- the first
     *shared_pages pages, identical in every block table, are attended once for the whole batch
     (workspace sized for n_split + prefix_splits slots)."""
-    ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, 1, out,
+    ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, pages_per_split, out,
                            act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo,
                            tickets, prefetch, window, shared_pages, prefix_splits, scale, softcap)
     cascade = shared_pages is not None and prefix_splits > 0 and window <= 0 and \

@@ -68,7 +68,8 @@ class NcclTP:
         kv = rn.kv
         # the split merge runs as its own kernel unless attention_merge is on, as on one GPU (merging in
         # the last split's CTA serialises a long tail: 0.7 ms/step slower on Qwen2.5-7B at batch 5)
-        K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, act=self.attn_out(rn), workspace=rn.attn_ws,
+        K.decode_attention(rn.q[:B], kv.k[i], kv.v[i], bt, ctx, n_split, pages_per_split=max(1, rn.dec_pps),
+                           act=self.attn_out(rn), workspace=rn.attn_ws,
                            tickets=rn.attn_tickets if rn.attn_merge else None, ldo=self.o_cols[1] - self.o_cols[0],
                            window=rn.cfg.layer_window(i), **rn.cascade_args(B, rn.cfg.layer_window(i)))
 

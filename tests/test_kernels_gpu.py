@@ -130,9 +130,11 @@ def _gather(kc, bt_row, L):
 
 
 @pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3), (128, 8, 8)])
-@pytest.mark.parametrize("n_split", [1, 7])
+@pytest.mark.parametrize("n_split,pps", [(1, 1), (7, 1), (64, 2), (200, 8)])
 @pytest.mark.parametrize("window", [0, 40])
-def test_decode_attention(D, H, Hkv, n_split, window):
+def test_decode_attention(D, H, Hkv, n_split, pps, window):
+    """Split-KV decode attention against fp32; (200, 8): fixed 8-page splits, most of the grid past
+    every sequence's pages (those splits write nothing and the combine skips them)."""
     from fak_b200.ops import kernels as K
     ctx = [1, 17, 100, 333, 1000]
     B = len(ctx)
@@ -140,9 +142,9 @@ def test_decode_attention(D, H, Hkv, n_split, window):
     q = torch.randn(B, H, D, device="cuda")
     out = torch.zeros(B, H * D, device="cuda")
     act = K.ActQ(B, H * D, "cuda")
-    ws = torch.zeros(B * H * n_split * (D + 2), device="cuda")
+    ws = torch.full((B * H * n_split * (D + 2),), float("nan"), device="cuda")   # unread slots stay NaN
     K.decode_attention(q, kc, vc, bt, torch.tensor(ctx, dtype=torch.int32, device="cuda"), n_split, out=out, act=act,
-                       workspace=ws, window=window)
+                       workspace=ws, window=window, pages_per_split=pps)
     torch.cuda.synchronize()
     G = H // Hkv
     for b, L in enumerate(ctx):
