@@ -6,12 +6,14 @@
 //               tile of 128 keys the 8 pages of K and of V (16 x 64 boxes of a 3-D map over the cache,
 //               [layer * pages * kv heads, 16 tokens, head dim]) into a 2-stage ring;
 //   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M = N = 128, K = head dim) into one of
-//               two TMEM S buffers, and O_j = P_j V_j (V as an MN-major operand: keys x head dim as it
-//               sits in the pages) into one of two TMEM O buffers; tcgen05.commit releases each stage;
-//   warps 2-5   softmax, one thread per query row (TMEM lane = row): pass 1 reads S and takes the
-//               masked row max, pass 2 reads it again and writes P = exp2(S - max) as bf16 into shared
-//               memory in the 128-byte-swizzled K-major layout the P.V MMA reads; the row's running
-//               output stays in registers, O_{j-1} is folded in with the online-softmax correction.
+//               two TMEM S buffers, and O += P_j V_j (V as an MN-major operand: keys x head dim as it
+//               sits in the pages) into one TMEM O buffer that lives for the whole CTA;
+//   warps 2-5   softmax, one thread per query row (TMEM lane = row): each reads its row of S once
+//               into registers and frees the S buffer, takes the masked row max, and writes
+//               P = 2^(S - m) as bf16 into shared memory in the 128-byte-swizzled K-major layout the
+//               P.V MMA reads.  The exponent base m is the running row max, moved only when it grew
+//               by more than 2^8 (then the warp rescales its rows of O in TMEM, once the previous
+//               P.V has completed), so P <= 256 and most tiles touch O not at all.
 // S of tile j + 1 is computed while tile j's softmax runs.  Every wait is bounded (tc::mbar_wait);
 // no load uses multicast.  Head dim 128, no window / soft-cap (those shapes use k_prefill_attn).
 // Reference: k_flash_attention, internal/compute/cuda_kernels.cu:701-759 (one block per head, SIMT).
@@ -32,6 +34,7 @@ constexpr int FA_D = 128;      // head dim
 constexpr int FA_PG = 16;      // tokens per page
 constexpr int FA_STAGES = 2;
 constexpr int FA_THREADS = 192;
+constexpr float FA_HEADROOM = 8.f;   // log2 growth of a row max tolerated before O is rescaled
 
 struct FaSmem {
   alignas(1024) __nv_bfloat16 q[2][FA_QT * 64];               // [D half][128 rows x 64]
@@ -42,7 +45,6 @@ struct FaSmem {
   uint64_t kv_full[FA_STAGES], kv_empty[FA_STAGES];
   uint64_t s_full[2], s_free[2];
   uint64_t p_full, p_free;
-  uint64_t o_full[2], o_free[2];
   uint32_t tmem_base;
 };
 
@@ -52,6 +54,13 @@ FAK_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x
           tc::smem_addr(dst)),
       "l"(map), "r"(tc::smem_addr(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+
+// the hardware base-2 exponential (flushes denormal results to zero; 2^-inf = 0)
+FAK_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Shared-memory descriptor of an MN-major operand in the 128-byte swizzle (rows of 128 bytes along
@@ -91,8 +100,6 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     for (int i = 0; i < 2; i++) {
       tc::mbar_init(&sm.s_full[i], 1);
       tc::mbar_init(&sm.s_free[i], 4);   // one arrival per softmax warp
-      tc::mbar_init(&sm.o_full[i], 1);
-      tc::mbar_init(&sm.o_free[i], 4);
     }
     tc::mbar_init(&sm.p_full, 4);
     tc::mbar_init(&sm.p_free, 1);
@@ -102,7 +109,7 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     tc::prefetch_tmap(&tmap_v);
   }
   if (warp == 1) {
-    tc::tmem_alloc(&sm.tmem_base, 512);   // S0 S1 O0 O1, 128 columns each
+    tc::tmem_alloc(&sm.tmem_base, 512);   // S0 [0,128) S1 [128,256) O [256,384)
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -145,6 +152,7 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     if (lane == 0) {
       constexpr uint32_t idesc_s = tc::idesc_bf16_f32(FA_QT, FA_KT);
       constexpr uint32_t idesc_pv = tc::idesc_bf16_f32(FA_QT, FA_D) | (1u << 16);   // B (V) MN-major
+      const uint32_t to = tmem + 256u;
       tc::mbar_wait(&sm.q_full, 0, err);
       for (int j = 0; j <= NJ; j++) {
         if (j < NJ) {
@@ -163,21 +171,18 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
           tc::mma_commit(&sm.s_full[b]);
         }
         if (j > 0) {
-          const int jj = j - 1, st = jj % FA_STAGES, bo = jj & 1;
+          const int jj = j - 1, st = jj % FA_STAGES;
           tc::mbar_wait(&sm.p_full, (uint32_t)(jj & 1), err);
-          tc::mbar_wait(&sm.o_free[bo], (uint32_t)(((jj >> 1) & 1) ^ 1), err);
           tc::tc_fence_after();
-          const uint32_t to = tmem + 256u + (uint32_t)(bo * 128);
 #pragma unroll
           for (int ks = 0; ks < FA_KT / 16; ks++) {
             const uint64_t ad = tc::smem_desc_sw128(sm.p[ks >> 2]) + 2 * (ks & 3);
             // 16 keys per step = 2 swizzle atoms of V; the two 64-column halves of the head dim are
             // 16 KB apart (LBO), 8-key groups 1 KB apart (SBO)
             const uint64_t bd = smem_desc_sw128_mn(sm.v[st][0] + ks * 16 * 64, FA_KT * 128, 1024);
-            tc::mma_bf16(to, ad, bd, idesc_pv, ks != 0);
+            tc::mma_bf16(to, ad, bd, idesc_pv, (jj > 0 || ks != 0) ? 1u : 0u);
           }
-          tc::mma_commit(&sm.o_full[bo]);
-          tc::mma_commit(&sm.p_free);
+          tc::mma_commit(&sm.p_free);        // P.V_jj done: O current, P's buffer free
           tc::mma_commit(&sm.kv_empty[st]);
         }
       }
@@ -187,48 +192,72 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int qi = q0 + r;
-    const int pos = pos0 + qi;            // keys [0, pos] are visible
+    const int pos = pos0 + qi;                       // keys [0, pos] are visible
+    const int warp_pos = pos0 + q0 + quarter * 32;   // the smallest position among this warp's rows
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    float o[FA_D];
-#pragma unroll
-    for (int d = 0; d < FA_D; d++) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f, corr_prev = 1.f;
+    const uint32_t tO = tmem + lane_off + 256u;
+    float m = -INFINITY, l = 0.f;                    // exponent base (log2 units) and row sum against it
     uint8_t* prow = reinterpret_cast<uint8_t*>(sm.p[0]) + r * 128;
     for (int j = 0; j < NJ; j++) {
       const int b = j & 1;
       tc::mbar_wait(&sm.s_full[b], (uint32_t)((j >> 1) & 1), err);
       tc::tc_fence_after();
       const uint32_t ts = tmem + lane_off + (uint32_t)(b * 128);
+      uint32_t sv[8][16];
+#pragma unroll
+      for (int c = 0; c < 8; c++) tc::tmem_ld16(ts + c * 16, sv[c]);
+      tc::tmem_ld_wait();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&sm.s_free[b]);   // S is in registers: the buffer can take S_{j+2}
       const int k0 = j * FA_KT;
       float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 8; c++) {
-        uint32_t v16[16];
-        tc::tmem_ld16(ts + c * 16, v16);
-        tc::tmem_ld_wait();
+      if (k0 + FA_KT - 1 > warp_pos) {   // a diagonal tile for this warp: mask keys past each row's position
 #pragma unroll
-        for (int e = 0; e < 16; e++) {
-          const float sv = k0 + c * 16 + e <= pos ? __uint_as_float(v16[e]) * scale_log2 : -INFINITY;
-          mx = fmaxf(mx, sv);
-        }
+        for (int c = 0; c < 8; c++)
+#pragma unroll
+          for (int e = 0; e < 16; e++) {
+            const float x = k0 + c * 16 + e <= pos ? __uint_as_float(sv[c][e]) : -INFINITY;
+            sv[c][e] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+#pragma unroll
+          for (int e = 0; e < 16; e++) mx = fmaxf(mx, __uint_as_float(sv[c][e]));
       }
-      const float m_new = fmaxf(m, mx);
-      const float bse = m_new == -INFINITY ? 0.f : m_new;
-      const float corr = exp2f(m - bse);
-      // P's buffer is free once the previous tile's P.V has completed
+      const float m_new = fmaxf(m, mx * scale_log2);
+      // move the base (and rescale O and l) only when some row of the warp outgrew the headroom
+      const bool move = __any_sync(0xffffffffu, m_new > m + FA_HEADROOM);
+      // P's buffer and O are free once the previous tile's P.V has completed
       tc::mbar_wait(&sm.p_free, (uint32_t)((j & 1) ^ 1), err);
-      float sum = 0.f;
+      if (move) {
+        const float f = ex2(m - m_new);   // 0 on the first tile
+        if (j > 0) {
+          tc::tc_fence_after();
 #pragma unroll 1
+          for (int c = 0; c < 8; c++) {
+            uint32_t ov[16];
+            tc::tmem_ld16(tO + c * 16, ov);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * f);
+            tc::tmem_st16(tO + c * 16, ov);
+          }
+          tc::tmem_st_wait();
+        }
+        l *= f;
+        m = m_new;
+      }
+      float sum = 0.f;
+#pragma unroll
       for (int c = 0; c < 8; c++) {
-        uint32_t v16[16];
-        tc::tmem_ld16(ts + c * 16, v16);
-        tc::tmem_ld_wait();
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
-          const int kk = k0 + c * 16 + e;
-          const float p0 = kk <= pos ? exp2f(__uint_as_float(v16[e]) * scale_log2 - bse) : 0.f;
-          const float p1 = kk + 1 <= pos ? exp2f(__uint_as_float(v16[e + 1]) * scale_log2 - bse) : 0.f;
+          const float p0 = ex2(fmaf(__uint_as_float(sv[c][e]), scale_log2, -m));
+          const float p1 = ex2(fmaf(__uint_as_float(sv[c][e + 1]), scale_log2, -m));
           sum += p0 + p1;
           pk[e >> 1] = pack_bf16(p0, p1);
         }
@@ -238,56 +267,30 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         *reinterpret_cast<uint4*>(ph + 16 * (ch0 ^ (r & 7))) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *reinterpret_cast<uint4*>(ph + 16 * (ch1 ^ (r & 7))) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
+      l += sum;
       tc::tc_fence_before();
       tc::fence_proxy_async();   // generic-proxy stores of P -> visible to the tensor cores
       __syncwarp();
-      if (lane == 0) {
-        tc::mbar_arrive(&sm.s_free[b]);
-        tc::mbar_arrive(&sm.p_full);
-      }
-      l = l * corr + sum;
-      m = m_new;
-      if (j > 0) {   // fold in O_{j-1} (relative to the max before this tile)
-        const int bo = (j - 1) & 1;
-        tc::mbar_wait(&sm.o_full[bo], (uint32_t)(((j - 1) >> 1) & 1), err);
-        tc::tc_fence_after();
-        const uint32_t to = tmem + lane_off + 256u + (uint32_t)(bo * 128);
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          uint32_t v16[16];
-          tc::tmem_ld16(to + c * 16, v16);
-          tc::tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 16; e++) o[c * 16 + e] = fmaf(o[c * 16 + e], corr_prev, __uint_as_float(v16[e]));
-        }
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&sm.o_free[bo]);
-      }
-      corr_prev = corr;
+      if (lane == 0) tc::mbar_arrive(&sm.p_full);
     }
-    {   // the last tile's P.V
-      const int bo = (NJ - 1) & 1;
-      tc::mbar_wait(&sm.o_full[bo], (uint32_t)(((NJ - 1) >> 1) & 1), err);
-      tc::tc_fence_after();
-      const uint32_t to = tmem + lane_off + 256u + (uint32_t)(bo * 128);
+    // the last P.V
+    tc::mbar_wait(&sm.p_free, (uint32_t)((NJ - 1) & 1), err);
+    tc::tc_fence_after();
+    // every lane takes part in the warp-collective TMEM loads; rows past the chunk store nothing
+    const bool store = qi < q_end;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    __nv_bfloat16* dst = out + (int64_t)(qoff + (store ? qi : 0)) * ldo + (int64_t)h * FA_D;
+#pragma unroll 1
+    for (int c = 0; c < 8; c++) {
+      uint32_t ov[16];
+      tc::tmem_ld16(tO + c * 16, ov);
+      tc::tmem_ld_wait();
+      uint32_t w[8];
 #pragma unroll
-      for (int c = 0; c < 8; c++) {
-        uint32_t v16[16];
-        tc::tmem_ld16(to + c * 16, v16);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 16; e++) o[c * 16 + e] = fmaf(o[c * 16 + e], corr_prev, __uint_as_float(v16[e]));
-      }
-    }
-    if (qi < q_end) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = out + (int64_t)(qoff + qi) * ldo + (int64_t)h * FA_D;
-#pragma unroll
-      for (int d = 0; d < FA_D; d += 8) {
-        uint4 w = make_uint4(pack_bf16(o[d] * inv, o[d + 1] * inv), pack_bf16(o[d + 2] * inv, o[d + 3] * inv),
-                             pack_bf16(o[d + 4] * inv, o[d + 5] * inv), pack_bf16(o[d + 6] * inv, o[d + 7] * inv));
-        *reinterpret_cast<uint4*>(dst + d) = w;
+      for (int e = 0; e < 8; e++) w[e] = pack_bf16(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv);
+      if (store) {
+        *reinterpret_cast<uint4*>(dst + c * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(dst + c * 16 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
       }
     }
   }

@@ -10,6 +10,13 @@
 //              32*(w%4)..+31 = tile rows), fused bias / residual add / SwiGLU, global store.
 // No TMA multicast is used, so the kernel is safe on multi-GPU runs.  The persistent variant
 // (default) keeps two TMEM accumulators so each CTA's epilogue overlaps its next tile's MMAs.
+//
+// G_RS (persistent variant, tensor-parallel prefill): the reduce-scatter half of an all-reduce in
+// the epilogue.  Output m-block mb belongs to rank mb % W; each fp32 tile is stored straight into
+// the owner's peer buffer (slot [this rank][owner-local row][column]) and, once all 128 rows of the
+// tile are written and fenced system-wide, a tile flag on the owner is released with the call's
+// epoch.  The owner's k_p2p_rs_reduce then sums the W partials into the residual and broadcasts
+// it, so the partials cross NVLink tile by tile while later tiles are still being computed.
 #include <torch/extension.h>
 #include <c10/cuda/CUDAStream.h>
 #include <cudaTypedefs.h>
@@ -17,6 +24,7 @@
 #include <cstdlib>
 #include <type_traits>
 
+#include "mma.cuh"
 #include "tc.cuh"
 
 using namespace fak;
@@ -27,7 +35,20 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int GEMM_THREADS = 192;
 
-enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2, G_GEGLU = 3 };
+enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2, G_GEGLU = 3, G_RS = 4 };
+
+constexpr int RS_MAX_W = 8;
+struct RsPeers {
+  uint8_t* base[RS_MAX_W];   // every rank's peer buffer
+  int64_t parts_off;         // partial slots [W][MR][N] fp32
+  int64_t flags_off;         // tile flags [m-block][n-block][RS_MAX_W] uint32
+  int W, me, MR;             // ranks, this rank, owner-local rows per source slot
+  uint32_t epoch;            // this call's flag value
+};
+
+FAK_DEV void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -49,7 +70,8 @@ FAK_DEV void store_val<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2
 template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M, int N,
-            int K, OutT* __restrict__ out, int64_t ldo, const float* __restrict__ bias, int epi, int* __restrict__ err) {
+            int K, OutT* __restrict__ out, int64_t ldo, const float* __restrict__ bias, int epi, int* __restrict__ err,
+            RsPeers rs) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   GemmSmem<BN, STAGES>& sm = *reinterpret_cast<GemmSmem<BN, STAGES>*>(base);
@@ -202,7 +224,7 @@ template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                        int M, int N, int K, OutT* __restrict__ out, int64_t ldo, const float* __restrict__ bias,
-                       int epi, int* __restrict__ err) {
+                       int epi, int* __restrict__ err, RsPeers rs) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   GemmSmemP<BN, STAGES>& sm = *reinterpret_cast<GemmSmemP<BN, STAGES>*>(base);
@@ -302,10 +324,20 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
             float* pf = reinterpret_cast<float*>(p);
             reinterpret_cast<float4*>(pf)[0] = make_float4(o[0], o[1], o[2], o[3]);
             reinterpret_cast<float4*>(pf)[1] = make_float4(o[4], o[5], o[6], o[7]);
+          } else if (col0 + 16 <= N && std::is_same<OutT, __nv_bfloat16>::value &&
+                     ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+            *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]),
+                                                      pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
           } else {
             for (int j = 0; j < 8; j++)
               if (col0 + j + 8 < N) store_val(p + j, o[j]);
           }
+        } else if (epi == G_RS) {
+          const int mb = m0 / BM;
+          const int lr = (mb / rs.W) * BM + quarter * 32 + lane;   // row inside the owner's slot
+          float* dst = reinterpret_cast<float*>(rs.base[mb % rs.W] + rs.parts_off) +
+                       ((int64_t)rs.me * rs.MR + lr) * N + col0;
+          store16<float>(dst, v, false, min(16, N - col0));
         } else {
           store16<OutT>(out + (int64_t)row * ldo + col0, v, epi == G_ADD, min(16, N - col0));
         }
@@ -313,6 +345,17 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.acc_empty[buf]);
+      if (epi == G_RS) {
+        // every row of the tile is in the owner's memory before its flag is released
+        __threadfence_system();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const int mb = m0 / BM, nb = n0 / BN, n_n = (N + BN - 1) / BN;
+          uint32_t* f = reinterpret_cast<uint32_t*>(rs.base[mb % rs.W] + rs.flags_off) +
+                        ((int64_t)mb * n_n + nb) * RS_MAX_W + rs.me;
+          st_release_sys_u32(f, rs.epoch);
+        }
+      }
     }
   }
   pdl_launch_dependents();
@@ -351,8 +394,8 @@ CUtensorMap make_map_bf16_kmajor(const void* ptr, int64_t rows, int64_t cols, in
 }
 
 template <int BN, int STAGES, typename OutT>
-void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* bias, int epi,
-                 int* err, bool persistent) {
+void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, OutT* out, int64_t ldo, const float* bias, int epi,
+                 int* err, bool persistent, const RsPeers& rs) {
   const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
   CUtensorMap ma = make_map_bf16_kmajor(a.data_ptr(), M, K, a.stride(0), BM);
   CUtensorMap mb = make_map_bf16_kmajor(b.data_ptr(), N, K, b.stride(0), BN);
@@ -372,8 +415,7 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& 
   attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, reinterpret_cast<OutT*>(out.data_ptr()),
-                                    (int64_t)out.stride(0), bias, epi, err));
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, out, ldo, bias, epi, err, rs));
 }
 
 }  // namespace
@@ -405,10 +447,44 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
     const char* e = std::getenv("FAK_GEMM_PERSISTENT");
     return !(e && e[0] == '0');
   }();
+  const RsPeers rs = {};
   if (out.scalar_type() == torch::kFloat32)
-    launch_gemm<256, 4, float>(a, b, out, bp, (int)epi, ep, persistent);
+    launch_gemm<256, 4, float>(a, b, out.data_ptr<float>(), out.stride(0), bp, (int)epi, ep, persistent, rs);
   else if (out.scalar_type() == torch::kBFloat16)
-    launch_gemm<256, 4, __nv_bfloat16>(a, b, out, bp, (int)epi, ep, persistent);
+    launch_gemm<256, 4, __nv_bfloat16>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
+                                        out.stride(0), bp, (int)epi, ep, persistent, rs);
   else
     TORCH_CHECK(false, "out must be float32 or bfloat16");
+}
+
+// Tensor-parallel prefill: C = A . B^T with the reduce-scatter half of the all-reduce in the
+// epilogue (G_RS above).  peers: int64 [W] base addresses of every rank's peer buffer; the owner
+// rank of m-block mb is mb % W and holds MR rows per source slot (MR >= ceil(m-blocks / W) * 128).
+// N must be a multiple of 4.  k_p2p_rs_reduce (p2p.cu) completes the all-reduce.
+void gemm_bf16_rs(torch::Tensor a, torch::Tensor b, torch::Tensor peers, int64_t me, int64_t parts_off,
+                  int64_t flags_off, int64_t MR, int64_t epoch, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == torch::kBFloat16 && a.dim() == 2 && a.stride(1) == 1, "a: [M,K] bf16");
+  TORCH_CHECK(b.scalar_type() == torch::kBFloat16 && b.dim() == 2 && b.stride(1) == 1, "b: [N,K] bf16");
+  TORCH_CHECK(a.size(1) == b.size(1), "K mismatch");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "row strides must be multiples of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0,
+              "operands must be 16-byte aligned");
+  TORCH_CHECK(peers.device().is_cpu() && peers.scalar_type() == torch::kInt64, "peers: int64 CPU tensor");
+  const int W = (int)peers.numel();
+  TORCH_CHECK(W >= 1 && W <= RS_MAX_W && me >= 0 && me < W, "gemm_bf16_rs: ranks");
+  const int64_t M = a.size(0), N = b.size(0);
+  TORCH_CHECK(N % 4 == 0 && parts_off % 16 == 0 && flags_off % 4 == 0, "gemm_bf16_rs: N % 4, offsets");
+  const int64_t n_m = (M + BM - 1) / BM;
+  TORCH_CHECK(MR >= (n_m + W - 1) / W * BM, "gemm_bf16_rs: MR too small for ", M, " rows over ", W, " ranks");
+  if (M == 0 || N == 0) return;
+  RsPeers rs = {};
+  for (int r = 0; r < W; r++) rs.base[r] = reinterpret_cast<uint8_t*>(peers.data_ptr<int64_t>()[r]);
+  rs.parts_off = parts_off;
+  rs.flags_off = flags_off;
+  rs.W = W;
+  rs.me = (int)me;
+  rs.MR = (int)MR;
+  rs.epoch = (uint32_t)epoch;
+  int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
+  launch_gemm<256, 4, float>(a, b, nullptr, 0, nullptr, G_RS, ep, true, rs);
 }

@@ -124,6 +124,84 @@ __global__ void k_p2p_allreduce_add(Peers P, int64_t part_off, float* __restrict
   pdl_launch_dependents();
 }
 
+// ---- prefill all-reduce: reduce + broadcast of owned tiles ----------------------------------
+// The [M, N] fp32 output is cut into 128-row m-blocks and 256-column n-blocks; rank mb % W owns
+// m-block mb.  Every rank has stored its partial of each tile into the owner's slot
+// parts[src][owner-local row][N] and released the tile flag flags[mb][nb][src] with this call's
+// epoch (the G_RS epilogue of gemm_tc.cu, or k_p2p_rs_push below).  For each owned tile, in the
+// order the tiles are produced, a CTA waits (bounded) for the W flags, adds the partials in rank
+// order to the residual x (a [M, N] fp32 array in every rank's peer buffer at x_off) and stores the
+// sum into x on every rank; a cross-rank barrier per CTA then orders all broadcasts before the
+// kernel ends, so every rank's x holds the full reduced rows.
+constexpr int RS_BM = 128, RS_BN = 256;
+
+FAK_DEV bool wait_flag_ge(const uint32_t* f, uint32_t v, uint32_t spin, int* err) {
+  uint32_t i = 0;
+  while (ld_acquire_sys(f) < v) {
+    if (++i > spin) {
+      report_error(err, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+__global__ void k_p2p_rs_reduce(Peers P, int64_t parts_off, int64_t flags_off, int64_t x_off, int M, int N, int MR,
+                                int me, int W, uint32_t epoch, int64_t bar_off, int site, uint32_t* counters,
+                                int* err) {
+  pdl_wait();
+  const int n_m = (M + RS_BM - 1) / RS_BM, n_n = (N + RS_BN - 1) / RS_BN;
+  const int own = me < n_m ? (n_m - 1 - me) / W + 1 : 0;   // owned m-blocks me, me + W, ...
+  const uint8_t* mine = P.base[me];
+  const float* parts = reinterpret_cast<const float*>(mine + parts_off);
+  const float* xl = reinterpret_cast<const float*>(mine + x_off);
+  for (int it = blockIdx.x; it < own * n_n; it += gridDim.x) {
+    const int k = it % own, nb = it / own, mb = me + k * W;
+    if (threadIdx.x < W)
+      wait_flag_ge(reinterpret_cast<const uint32_t*>(mine + flags_off) + ((int64_t)mb * n_n + nb) * MAX_W + threadIdx.x,
+                   epoch, P.spin, err);
+    __syncthreads();
+    const int rows = min(RS_BM, M - mb * RS_BM), cols4 = min(RS_BN, N - nb * RS_BN) >> 2;
+    for (int e = threadIdx.x; e < rows * cols4; e += blockDim.x) {
+      const int rr = e / cols4, c = nb * RS_BN + 4 * (e - rr * cols4);
+      const int64_t xi = (int64_t)(mb * RS_BM + rr) * N + c;
+      float4 acc = *reinterpret_cast<const float4*>(xl + xi);
+      for (int r = 0; r < W; r++) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(parts + ((int64_t)r * MR + k * RS_BM + rr) * N + c));
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      for (int r = 0; r < W; r++) *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.base[r] + x_off) + xi) = acc;
+    }
+    __syncthreads();
+  }
+  rank_barrier(P, bar_off, site, blockIdx.x, me, W, counters, err);
+  pdl_launch_dependents();
+}
+
+// The reduce-scatter half for a partial that is not produced by a GEMM epilogue: part [M, N] fp32
+// (local) is copied tile by tile into the owners' slots, each tile's flag released after its rows.
+__global__ void k_p2p_rs_push(Peers P, const float* __restrict__ part, int M, int N, int MR, int64_t parts_off,
+                              int64_t flags_off, int me, int W, uint32_t epoch) {
+  pdl_wait();
+  const int n_m = (M + RS_BM - 1) / RS_BM, n_n = (N + RS_BN - 1) / RS_BN;
+  for (int t = blockIdx.x; t < n_m * n_n; t += gridDim.x) {
+    const int mb = t % n_m, nb = t / n_m, owner = mb % W;
+    float* dst = reinterpret_cast<float*>(P.base[owner] + parts_off);
+    const int rows = min(RS_BM, M - mb * RS_BM), cols4 = min(RS_BN, N - nb * RS_BN) >> 2;
+    for (int e = threadIdx.x; e < rows * cols4; e += blockDim.x) {
+      const int rr = e / cols4, c = nb * RS_BN + 4 * (e - rr * cols4);
+      const float4 v = *reinterpret_cast<const float4*>(part + (int64_t)(mb * RS_BM + rr) * N + c);
+      *reinterpret_cast<float4*>(dst + ((int64_t)me * MR + (mb / W) * RS_BM + rr) * N + c) = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0)
+      st_release_sys(reinterpret_cast<uint32_t*>(P.base[owner] + flags_off) + ((int64_t)mb * n_n + nb) * MAX_W + me,
+                     epoch);
+  }
+  pdl_launch_dependents();
+}
+
 // ---- greedy sampling over vocab-sharded logits ---------------------------------------------
 // CTA b: first-index argmax of row b of the local logits slice, published as (value, global id)
 // to every rank; after the barrier every rank reduces the W candidates in rank order.
@@ -278,6 +356,40 @@ void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, i
   auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_allreduce_add, P, part_off, x.data_ptr<float>(), n, flags_off,
                                     (int)site, (int)me, W, (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>()));
+}
+
+// Completes the prefill all-reduce started by gemm_bf16_rs / p2p_rs_push: x (at x_off in every
+// rank's peer buffer, [M, N] fp32) += sum over ranks of the partials; site: barrier site for the end.
+void p2p_rs_reduce(torch::Tensor peers, int64_t parts_off, int64_t flags_off, int64_t x_off, int64_t M, int64_t N,
+                   int64_t MR, int64_t me, int64_t epoch, int64_t bar_off, int64_t site, torch::Tensor counters,
+                   torch::Tensor err, int64_t ctas, int64_t spin_limit) {
+  const int W = (int)peers.numel();
+  TORCH_CHECK(N % 4 == 0 && parts_off % 16 == 0 && x_off % 16 == 0 && flags_off % 4 == 0, "rs_reduce: alignment");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "rs_reduce: 1..64 CTAs");
+  TORCH_CHECK(MR >= ((M + RS_BM - 1) / RS_BM + W - 1) / W * RS_BM, "rs_reduce: MR");
+  if (M == 0) return;
+  Peers P = make_peers(peers, spin_limit);
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_rs_reduce, P, parts_off, flags_off, x_off, (int)M, (int)N, (int)MR,
+                                    (int)me, W, (uint32_t)epoch, bar_off, (int)site,
+                                    (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>()));
+}
+
+void p2p_rs_push(torch::Tensor peers, torch::Tensor part, int64_t MR, int64_t parts_off, int64_t flags_off, int64_t me,
+                 int64_t epoch) {
+  const int W = (int)peers.numel();
+  TORCH_CHECK(part.is_cuda() && part.scalar_type() == torch::kFloat32 && part.dim() == 2 && part.is_contiguous() &&
+                  part.size(1) % 4 == 0, "rs_push: part [M, N] f32 contiguous, N % 4 == 0");
+  const int M = (int)part.size(0), N = (int)part.size(1);
+  TORCH_CHECK(MR >= ((M + RS_BM - 1) / RS_BM + W - 1) / W * RS_BM && parts_off % 16 == 0, "rs_push: MR / offset");
+  if (M == 0) return;
+  Peers P = make_peers(peers, 0);
+  const int tiles = ((M + RS_BM - 1) / RS_BM) * ((N + RS_BN - 1) / RS_BN);
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_cfg(dim3((unsigned)std::min(tiles, 148)), dim3(256), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_rs_push, P, (const float*)part.data_ptr<float>(), M, N, (int)MR,
+                                    parts_off, flags_off, (int)me, W, (uint32_t)epoch));
 }
 
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,

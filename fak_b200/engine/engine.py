@@ -96,7 +96,8 @@ class Engine:
             if self.ecfg.fused_collectives:
                 from ..parallel.p2p import P2PTP
                 collectives = P2PTP(tp_group, weights, self.ecfg.max_batch, self.device,
-                                    spin_limit=self.ecfg.p2p_spin_limit)
+                                    spin_limit=self.ecfg.p2p_spin_limit,
+                                    max_prefill_tokens=self.ecfg.max_prefill_tokens)
             else:
                 from ..parallel.tp import NcclTP
                 collectives = NcclTP(tp_group, weights, self.ecfg.max_batch, self.device)

@@ -452,7 +452,11 @@ class ModelRunner:
         cfg, dev = self.cfg, self.device
         T = ids.numel()
         d = cfg.d_model
-        x = torch.empty(T, d, dtype=torch.float32, device=dev)
+        # under fused tensor parallelism the residual lives in the peer buffer (the prefill all-reduce
+        # stores reduced rows into every rank's copy)
+        x = self.coll.prefill_x(T) if self.coll is not None and hasattr(self.coll, "prefill_x") else None
+        if x is None:
+            x = torch.empty(T, d, dtype=torch.float32, device=dev)
         hb = torch.empty(T, d, dtype=torch.bfloat16, device=dev)
         qkv = torch.empty(T, self.qkv_dim, dtype=torch.float32, device=dev)
         qb = torch.empty(T, self.Hq, self.D, dtype=torch.bfloat16, device=dev)
@@ -484,9 +488,8 @@ class ModelRunner:
                 from .moe import moe_prefill
                 moe_prefill(self, i, hb, x)
                 continue
-            hf = torch.empty(T, self.ffn_local, dtype=torch.float32, device=dev)
-            K.gemm(hb, L.gate_up, hf, self.gated_epi)
-            hb2 = hf.to(torch.bfloat16)
+            hb2 = torch.empty(T, self.ffn_local, dtype=torch.bfloat16, device=dev)   # the gated product, bf16
+            K.gemm(hb, L.gate_up, hb2, self.gated_epi)
             if self.coll is None and L.post_ffn_norm is not None:
                 K.gemm(hb2, L.down, tmp, K.EPI_STORE)
                 K.rmsnorm_add(tmp, L.post_ffn_norm, cfg.rms_eps, x)

@@ -17,8 +17,14 @@ tile and adds their rank-order sum to the replicated residual.  One kernel per p
 transfer of each tile overlapping the GEMV of the others, no separate collective launch and no
 all-gather of the attention output (each rank streams only its slice of o_proj).  Batches above 32
 tokens fall back to the GEMV + one-shot all-reduce kernel pair.  Greedy decoding ends with a
-distributed argmax instead of gathering 152k logits.  Prefill keeps the NCCL collectives of
-``NcclTP`` (large messages, bandwidth-bound).
+distributed argmax instead of gathering 152k logits.
+
+Prefill all-reduces both row-parallel projections (and the MoE expert sum) without NCCL: the
+tcgen05 GEMM's epilogue stores each 128 x 256 fp32 output tile into the owner rank's slot (owner =
+m-block mod W, the reduce-scatter half; ``gemm_tc.cu`` ``G_RS``) and releases a tile flag, and the
+owner's ``k_p2p_rs_reduce`` adds the W partials to the residual and stores the rows into every
+rank's residual (the all-gather half), which for that reason lives in the peer buffer
+(``prefill_x``) -- the partials cross NVLink tile by tile while the GEMM computes later tiles.
 
 Every wait is bounded (``spin_limit`` polls; 0 = the kernels' default of about a second) and writes
 an error word the engine reads back with each step's tokens (``engine.Engine._collect``).
@@ -38,6 +44,7 @@ MAX_CTAS = 64
 MAX_W = 8
 AR_CTAS = 16
 AG_CTAS = 16
+RS_CTAS = 64
 
 
 def _align(n: int, a: int = 256) -> int:
@@ -82,7 +89,7 @@ class PeerBuffer:
 
 
 class P2PTP(NcclTP):
-    def __init__(self, group, weights, max_batch: int, device, spin_limit: int = 0):
+    def __init__(self, group, weights, max_batch: int, device, spin_limit: int = 0, max_prefill_tokens: int = 0):
         super().__init__(group, weights, max_batch, device)
         cfg = self.cfg
         if self.world > MAX_W:
@@ -90,7 +97,7 @@ class P2PTP(NcclTP):
         B, d, L = max_batch, cfg.d_model, cfg.n_layers
         self.B = B
         self.spin_limit = int(spin_limit)
-        self.n_sites = 3 * L + 2
+        self.n_sites = 3 * L + 3   # per layer 3, the two LM-head sites, the prefill all-reduce's end barrier
         off = 0
         self.flags_off = off
         off = _align(off + self.n_sites * MAX_CTAS * MAX_W * 4)
@@ -111,6 +118,20 @@ class P2PTP(NcclTP):
         # MoE combine fused with the expert-parallel all-reduce: [2 layer parities][W][B * d] partials
         self.moe_off = off
         off = _align(off + (2 * self.world * B * d * 4 if cfg.is_moe else 0))
+        # prefill all-reduce: the residual [T, d], partial slots [W][MR][d] (MR rows of owned
+        # 128-row m-blocks per source rank) and tile flags [m-block][256-column block][MAX_W]
+        Tp = max(0, int(max_prefill_tokens))
+        self.pf_fused = Tp > 0 and d % 4 == 0 and os.environ.get("FAK_PREFILL_P2P", "1") != "0"
+        Tp = Tp if self.pf_fused else 0
+        n_m, n_n = -(-Tp // 128), -(-d // 256)
+        self.pf_T, self.pf_MR = Tp, -(-n_m // self.world) * 128
+        self.pf_x_off = off
+        off = _align(off + Tp * d * 4)
+        self.pf_parts_off = off
+        off = _align(off + (self.world * self.pf_MR * d * 4 if Tp else 0))
+        self.pf_flags_off = off
+        off = _align(off + n_m * n_n * MAX_W * 4)
+        self.pf_epoch = 0
         self.nbytes = off
         self.mem = None
         if os.environ.get("FAK_P2P_MEM", "ipc") == "symm":
@@ -207,6 +228,56 @@ class P2PTP(NcclTP):
                                  self.moe_off, i & 1, self.flags_off, 3 * i + 2, self.me, self.counters, self.err,
                                  AR_CTAS * 2, self.spin_limit)
         K.count()
+
+    # ---- prefill ----------------------------------------------------------------------
+    def prefill_x(self, T: int) -> torch.Tensor | None:
+        """The prefill residual [T, d] fp32 inside this rank's peer buffer (the fused all-reduce
+        stores reduced rows into every rank's copy), or None when the fused prefill path is off."""
+        if not self.pf_fused or T > self.pf_T:
+            return None
+        d = self.cfg.d_model
+        return self.buf[self.pf_x_off:self.pf_x_off + T * d * 4].view(torch.float32).view(T, d)
+
+    def _pf_ok(self, x: torch.Tensor) -> bool:
+        return (self.pf_fused and x.shape[0] <= self.pf_T and
+                x.data_ptr() == self.buf.data_ptr() + self.pf_x_off and x.is_contiguous())
+
+    def _pf_reduce(self, T: int) -> None:
+        ext().p2p_rs_reduce(self.peers, self.pf_parts_off, self.pf_flags_off, self.pf_x_off, T, self.cfg.d_model,
+                            self.pf_MR, self.me, self.pf_epoch, self.flags_off, self.n_sites - 1, self.counters,
+                            self.err, RS_CTAS, self.spin_limit)
+
+    def _pf_gemm_ar(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor) -> None:
+        """x += all-reduce(a . w^T): the GEMM pushes its tiles to their owners, the owners reduce
+        and broadcast."""
+        if a.shape[0] != x.shape[0] or w.shape[0] != self.cfg.d_model:
+            raise ValueError("prefill all-reduce: the slots hold [tokens, d_model] partials")
+        self.pf_epoch += 1
+        ext().gemm_bf16_rs(a, w, self.peers, self.me, self.pf_parts_off, self.pf_flags_off, self.pf_MR,
+                           self.pf_epoch, self.err)
+        self._pf_reduce(x.shape[0])
+        K.count(2)
+
+    def prefill_attn_o(self, rn, i: int, ab: torch.Tensor, x: torch.Tensor) -> None:
+        if not self._pf_ok(x):
+            return super().prefill_attn_o(rn, i, ab, x)
+        self._pf_gemm_ar(ab, self.o_dense_local(rn, i), x)
+
+    def prefill_down(self, rn, i: int, hb2: torch.Tensor, x: torch.Tensor) -> None:
+        if not self._pf_ok(x):
+            return super().prefill_down(rn, i, hb2, x)
+        self._pf_gemm_ar(hb2, rn.w.layers[i].down.dense(), x)
+
+    def prefill_reduce(self, part: torch.Tensor, x: torch.Tensor) -> None:
+        if not self._pf_ok(x):
+            return super().prefill_reduce(part, x)
+        if part.shape != x.shape:
+            raise ValueError("prefill all-reduce: partial and residual shapes differ")
+        self.pf_epoch += 1
+        ext().p2p_rs_push(self.peers, part.contiguous(), self.pf_MR, self.pf_parts_off, self.pf_flags_off, self.me,
+                          self.pf_epoch)
+        self._pf_reduce(x.shape[0])
+        K.count(2)
 
     def reduce_partial(self, rn, i: int, B: int, fill) -> None:
         """x += sum over ranks of the partial fill() writes (MoE expert bands), via the P2P all-reduce."""

@@ -460,6 +460,21 @@ def test_tgemv_fp32_input_fused_norm(qt, blk, norm, N):
         assert torch.equal(y1[0], y[b]), b
 
 
+@pytest.mark.parametrize("M,N,K", [(1280, 37888, 512), (77, 240, 1536)])
+def test_gemm_tcgen05_gated_bf16_out(M, N, K):
+    """The gated (SwiGLU) epilogue writing bf16 directly gives the bf16 rounding of the fp32 result."""
+    from fak_b200.ops import kernels as Kn
+    torch.manual_seed(N)
+    a = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    f32 = torch.zeros(M, N // 2, device="cuda")
+    b16 = torch.zeros(M, N // 2, device="cuda", dtype=torch.bfloat16)
+    Kn.gemm(a, b, f32, 2)
+    Kn.gemm(a, b, b16, 2)
+    torch.cuda.synchronize()
+    assert torch.equal(b16, f32.bfloat16())
+
+
 def test_gemm_tcgen05_bf16_out_many_tiles_per_cta():
     """Persistent GEMM: several output tiles per CTA (both TMEM accumulators reused), bf16 output."""
     from fak_b200.ops import kernels as Kn
