@@ -15,6 +15,7 @@ the same session, split across more GPUs).
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -188,11 +189,13 @@ def main():
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     w0 = time.perf_counter()
-    ttfts, decoded = [], 0
+    ttfts, decoded, first_turn = [], 0, None
     for _ in range(args.steps):
         reqs = turn()
         ttfts.extend(r.ttft for r in reqs)
         decoded += sum(len(r.full_output) for r in reqs)
+        if first_turn is None:
+            first_turn = [list(r.full_output) for r in reqs]
     ev1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
@@ -244,6 +247,9 @@ def main():
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
         "clocks": clocks,
+        # the first timed turn's greedy tokens (every agent, in order): equal across N when the
+        # tensor-parallel runs decode the same continuations
+        "first_turn_digest": hashlib.sha256(json.dumps(first_turn).encode()).hexdigest()[:16],
     }
     if rank == 0:
         print(json.dumps(out), flush=True)

@@ -143,12 +143,21 @@ def _kernel_profile(eng, turn, args, group, world) -> dict:
         torch.cuda.synchronize()
     rn.replay_resident = real
     agg: dict[str, float] = {}
+    seq: list[tuple[float, str, float]] = []
     for ev in prof.events():
         if ev.device_type.name != "CUDA":
             continue
         name = ev.name.replace("void ", "").replace("(anonymous namespace)::", "").replace("<unnamed>::", "")
         name = name.split("(")[0][:48] or ev.name[:48]
         agg[name] = agg.get(name, 0.0) + ev.device_time
+        seq.append((ev.time_range.start, name, ev.device_time))
+    # one decode step in launch order (a step starts with the embedding gather): the third one
+    seq.sort()
+    starts = [i for i, (_, n, _) in enumerate(seq) if n.startswith("k_embed")]
+    step_trace = []
+    if len(starts) >= 4:
+        a, b = starts[2], starts[3]
+        step_trace = [(n, round(t, 2)) for _, n, t in seq[a:b]]
     # decode steps only: subtract nothing, report per decode step of the profiled turn
     steps = max(1, n_steps[0])
     per = {k: v / steps for k, v in agg.items()}
@@ -158,7 +167,12 @@ def _kernel_profile(eng, turn, args, group, world) -> dict:
         keys = set().union(*[set(p) for p in allp])
         per = {k: max(p.get(k, 0.0) for p in allp) for k in keys}
     top = sorted(per.items(), key=lambda kv: -kv[1])[:16]
-    return {k: round(v, 2) for k, v in top}
+    out = {k: round(v, 2) for k, v in top}
+    if step_trace:   # this rank's (rank 0's) kernels of one step: the first layer, and the step's tail
+        out["_step_trace_first_layer_and_tail"] = step_trace[:16] + [("...", 0.0)] + step_trace[-8:]
+        out["_step_kernels"] = len(step_trace)
+        out["_step_us_sum"] = round(sum(t for _, t in step_trace), 1)
+    return out
 
 
 if __name__ == "__main__":
