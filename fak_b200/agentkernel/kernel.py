@@ -16,6 +16,7 @@ from typing import Any, Callable
 from .abi import Reason, Result, Status, ToolCall, Verdict, VerdictKind
 from .adjudicator import Adjudicator
 from .ctxmmu import ContextMMU
+from .grammar import GrammarRung
 from .journal import Journal
 from .policy import Policy
 from .preflight import Preflight
@@ -26,7 +27,9 @@ Handler = Callable[[dict], Any]
 
 class Kernel:
     def __init__(self, policy: Policy | None = None, journal_path: str | None = None, mmu: ContextMMU | None = None,
-                 workers: int = 4, preflight: Preflight | None = None, vdso: VDSO | None = None):
+                 workers: int = 4, preflight: Preflight | None = None, vdso: VDSO | None = None,
+                 grammar: GrammarRung | None = None):
+        self.grammar = grammar or GrammarRung()
         self.preflight = preflight or Preflight()
         self.vdso = vdso or VDSO()
         self.adjudicator = Adjudicator(policy)
@@ -47,9 +50,20 @@ class Kernel:
 
     def decide(self, call: ToolCall) -> Verdict:
         t0 = time.perf_counter_ns()
-        v = self.preflight.check(call)          # malformed calls never reach the policy
-        if v.kind == VerdictKind.DEFER:
-            v = self.adjudicator.adjudicate(call)
+        # the grammar rung first (cheapest): a mis-shaped call is repaired in place or refused
+        g = self.grammar.check(call)
+        if g.kind == VerdictKind.DENY:
+            v = g
+        else:
+            checked = call
+            if g.kind == VerdictKind.TRANSFORM:   # the repaired call goes through every later rung
+                checked = ToolCall(call.tool, g.new_args, call.op, call.engine, call.seq, call.trace_id, call.meta)
+            v = self.preflight.check(checked)       # malformed calls never reach the policy
+            if v.kind == VerdictKind.DEFER:
+                v = self.adjudicator.adjudicate(checked)
+            if g.kind == VerdictKind.TRANSFORM and v.kind == VerdictKind.ALLOW:
+                v = Verdict(VerdictKind.TRANSFORM, Reason.MISROUTE, by=f"grammar+{v.by}", claim=v.claim,
+                            new_args=g.new_args, meta={**g.meta, **v.meta})
         dt = time.perf_counter_ns() - t0
         with self._lock:
             self.stats["calls"] += 1

@@ -257,6 +257,7 @@ class Gateway:
                     msg["content"] = ((msg.get("content") or "") + "\n" + "\n".join(notes)).strip()
             return resp
         self.kernel.preflight.register_openai_tools(body.get("tools"))   # schemas for the pre-flight rungs
+        self.kernel.grammar.register_openai_tools(body.get("tools"))     # and the tools' argument grammars
         prompt = render_chatml(self._view(body.get("messages", [])), body.get("tools"))
         info = {}
         text = ""
@@ -292,6 +293,7 @@ class Gateway:
 
         yield chunk({"role": "assistant"})
         self.kernel.preflight.register_openai_tools(body.get("tools"))   # schemas for the pre-flight rungs
+        self.kernel.grammar.register_openai_tools(body.get("tools"))     # and the tools' argument grammars
         prompt = render_chatml(self._view(body.get("messages", [])), body.get("tools"))
         text, info, held = "", {}, ""
         for piece, inf in self.stream_text(prompt, int(body.get("max_tokens") or self.default_max_tokens),
