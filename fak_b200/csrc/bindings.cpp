@@ -79,7 +79,12 @@ void gemm_bf16_rs(torch::Tensor a, torch::Tensor b, torch::Tensor peers, int64_t
                   int64_t flags_off, int64_t MR, int64_t epoch, c10::optional<torch::Tensor> err);
 void p2p_rs_reduce(torch::Tensor peers, int64_t parts_off, int64_t flags_off, int64_t x_off, int64_t M, int64_t N,
                    int64_t MR, int64_t me, int64_t epoch, int64_t bar_off, int64_t site, torch::Tensor counters,
-                   torch::Tensor err, int64_t ctas, int64_t spin_limit);
+                   torch::Tensor err, int64_t ctas, int64_t spin_limit, c10::optional<torch::Tensor> x_local);
+void sp_rmsnorm_shard(torch::Tensor peers, torch::Tensor x_local, torch::Tensor gamma, double eps, int64_t valid,
+                      int64_t shard_off, int64_t flags_off, int64_t me, int64_t epoch);
+void gemm_bf16_ag(int64_t M, torch::Tensor b, torch::Tensor out, torch::Tensor peers, int64_t me, int64_t shard_off,
+                  int64_t MR, int64_t flags_off, int64_t epoch, int64_t spin, c10::optional<torch::Tensor> bias,
+                  int64_t epi, c10::optional<torch::Tensor> err);
 void p2p_rs_push(torch::Tensor peers, torch::Tensor part, int64_t MR, int64_t parts_off, int64_t flags_off, int64_t me,
                  int64_t epoch);
 void decode_advance(torch::Tensor next, torch::Tensor ids, torch::Tensor pos, torch::Tensor slot, torch::Tensor ctx,
@@ -188,7 +193,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_rs_reduce", &p2p_rs_reduce, pybind11::arg("peers"), pybind11::arg("parts_off"),
         pybind11::arg("flags_off"), pybind11::arg("x_off"), pybind11::arg("M"), pybind11::arg("N"), pybind11::arg("MR"),
         pybind11::arg("me"), pybind11::arg("epoch"), pybind11::arg("bar_off"), pybind11::arg("site"),
-        pybind11::arg("counters"), pybind11::arg("err"), pybind11::arg("ctas"), pybind11::arg("spin_limit") = 0);
+        pybind11::arg("counters"), pybind11::arg("err"), pybind11::arg("ctas"), pybind11::arg("spin_limit") = 0,
+        pybind11::arg("x_local") = pybind11::none());
+  m.def("sp_rmsnorm_shard", &sp_rmsnorm_shard, pybind11::arg("peers"), pybind11::arg("x_local"),
+        pybind11::arg("gamma"), pybind11::arg("eps"), pybind11::arg("valid"), pybind11::arg("shard_off"),
+        pybind11::arg("flags_off"), pybind11::arg("me"), pybind11::arg("epoch"));
+  m.def("gemm_bf16_ag", &gemm_bf16_ag, pybind11::arg("M"), pybind11::arg("b"), pybind11::arg("out"),
+        pybind11::arg("peers"), pybind11::arg("me"), pybind11::arg("shard_off"), pybind11::arg("MR"),
+        pybind11::arg("flags_off"), pybind11::arg("epoch"), pybind11::arg("spin") = 0,
+        pybind11::arg("bias") = pybind11::none(), pybind11::arg("epi") = 0, pybind11::arg("err") = pybind11::none());
   m.def("p2p_rs_push", &p2p_rs_push, pybind11::arg("peers"), pybind11::arg("part"), pybind11::arg("MR"),
         pybind11::arg("parts_off"), pybind11::arg("flags_off"), pybind11::arg("me"), pybind11::arg("epoch"));
 }

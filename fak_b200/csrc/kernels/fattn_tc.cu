@@ -8,12 +8,15 @@
 //   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M = N = 128, K = head dim) into one of
 //               two TMEM S buffers, and O += P_j V_j (V as an MN-major operand: keys x head dim as it
 //               sits in the pages) into one TMEM O buffer that lives for the whole CTA;
-//   warps 2-5   softmax, one thread per query row (TMEM lane = row): each reads its row of S once
-//               into registers and frees the S buffer, takes the masked row max, and writes
-//               P = 2^(S - m) as bf16 into shared memory in the 128-byte-swizzled K-major layout the
-//               P.V MMA reads.  The exponent base m is the running row max, moved only when it grew
-//               by more than 2^8 (then the warp rescales its rows of O in TMEM, once the previous
-//               P.V has completed), so P <= 256 and most tiles touch O not at all.
+//   warps 2-9   softmax, two threads per query row (TMEM lane = row; warps w and w + 4 cover the
+//               same lane quarter): warps 2-5 take keys 0-63 of each tile, warps 6-9 keys 64-127.
+//               Each reads its half row of S once into registers (the S buffer is then free), the
+//               two halves exchange their row max through shared memory (a named barrier per lane
+//               quarter), and each writes its half of P = 2^(S - m) as bf16 into shared memory in
+//               the 128-byte-swizzled K-major layout the P.V MMA reads.  The exponent base m is the
+//               running row max, moved only when it grew by more than 2^8 (then each half rescales
+//               its 64 columns of the rows' O in TMEM, once the previous P.V has completed), so
+//               P <= 256 and most tiles touch O not at all; the halves' row sums add at the end.
 // S of tile j + 1 is computed while tile j's softmax runs.  Every wait is bounded (tc::mbar_wait);
 // no load uses multicast.  Head dim 128, no window / soft-cap (those shapes use k_prefill_attn).
 // Reference: k_flash_attention, internal/compute/cuda_kernels.cu:701-759 (one block per head, SIMT).
@@ -33,7 +36,7 @@ constexpr int FA_KT = 128;     // keys per KV tile (8 pages)
 constexpr int FA_D = 128;      // head dim
 constexpr int FA_PG = 16;      // tokens per page
 constexpr int FA_STAGES = 2;
-constexpr int FA_THREADS = 192;
+constexpr int FA_THREADS = 320;   // producer, MMA issuer, 8 softmax warps
 constexpr float FA_HEADROOM = 8.f;   // log2 growth of a row max tolerated before O is rescaled
 
 struct FaSmem {
@@ -45,6 +48,8 @@ struct FaSmem {
   uint64_t kv_full[FA_STAGES], kv_empty[FA_STAGES];
   uint64_t s_full[2], s_free[2];
   uint64_t p_full, p_free;
+  float red[2][2][FA_QT];   // row max of each key half, by tile parity
+  float lsum[2][FA_QT];     // row sums of each key half (end of the CTA)
   uint32_t tmem_base;
 };
 
@@ -99,9 +104,9 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     }
     for (int i = 0; i < 2; i++) {
       tc::mbar_init(&sm.s_full[i], 1);
-      tc::mbar_init(&sm.s_free[i], 4);   // one arrival per softmax warp
+      tc::mbar_init(&sm.s_free[i], 8);   // one arrival per softmax warp
     }
-    tc::mbar_init(&sm.p_full, 4);
+    tc::mbar_init(&sm.p_full, 8);
     tc::mbar_init(&sm.p_free, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmap_q);
@@ -188,33 +193,33 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
       }
     }
   } else {
-    // softmax warps 2..5: TMEM lane quarter = warp % 4, one query row per thread
-    const int quarter = warp & 3;
+    // softmax warps 2..9: TMEM lane quarter = warp % 4, key half kh = (warp - 2) / 4
+    const int quarter = warp & 3, kh = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const int qi = q0 + r;
     const int pos = pos0 + qi;                       // keys [0, pos] are visible
     const int warp_pos = pos0 + q0 + quarter * 32;   // the smallest position among this warp's rows
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tO = tmem + lane_off + 256u;
-    float m = -INFINITY, l = 0.f;                    // exponent base (log2 units) and row sum against it
-    uint8_t* prow = reinterpret_cast<uint8_t*>(sm.p[0]) + r * 128;
+    const uint32_t tO = tmem + lane_off + 256u + (uint32_t)(kh * 64);   // this half's 64 columns of O
+    float m = -INFINITY, l = 0.f;                    // exponent base (log2 units) and half-row sum against it
+    uint8_t* prow = reinterpret_cast<uint8_t*>(sm.p[kh]) + r * 128;
     for (int j = 0; j < NJ; j++) {
       const int b = j & 1;
       tc::mbar_wait(&sm.s_full[b], (uint32_t)((j >> 1) & 1), err);
       tc::tc_fence_after();
-      const uint32_t ts = tmem + lane_off + (uint32_t)(b * 128);
-      uint32_t sv[8][16];
+      const uint32_t ts = tmem + lane_off + (uint32_t)(b * 128 + kh * 64);
+      uint32_t sv[4][16];
 #pragma unroll
-      for (int c = 0; c < 8; c++) tc::tmem_ld16(ts + c * 16, sv[c]);
+      for (int c = 0; c < 4; c++) tc::tmem_ld16(ts + c * 16, sv[c]);
       tc::tmem_ld_wait();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.s_free[b]);   // S is in registers: the buffer can take S_{j+2}
-      const int k0 = j * FA_KT;
+      const int k0 = j * FA_KT + kh * 64;
       float mx = -INFINITY;
-      if (k0 + FA_KT - 1 > warp_pos) {   // a diagonal tile for this warp: mask keys past each row's position
+      if (k0 + 63 > warp_pos) {   // a diagonal tile for this warp: mask keys past each row's position
 #pragma unroll
-        for (int c = 0; c < 8; c++)
+        for (int c = 0; c < 4; c++)
 #pragma unroll
           for (int e = 0; e < 16; e++) {
             const float x = k0 + c * 16 + e <= pos ? __uint_as_float(sv[c][e]) : -INFINITY;
@@ -223,12 +228,18 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
           }
       } else {
 #pragma unroll
-        for (int c = 0; c < 8; c++)
+        for (int c = 0; c < 4; c++)
 #pragma unroll
           for (int e = 0; e < 16; e++) mx = fmaxf(mx, __uint_as_float(sv[c][e]));
       }
+      // the other half's max of the same row (slots alternate by tile parity: a slot is rewritten
+      // two tiles later, after a barrier the partner passes only once it has read it)
+      sm.red[b][kh][r] = mx;
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+      mx = fmaxf(mx, sm.red[b][kh ^ 1][r]);
       const float m_new = fmaxf(m, mx * scale_log2);
-      // move the base (and rescale O and l) only when some row of the warp outgrew the headroom
+      // move the base (and rescale O and l) only when some row of the warp outgrew the headroom;
+      // the partner warp holds the same rows and values, so it takes the same decision
       const bool move = __any_sync(0xffffffffu, m_new > m + FA_HEADROOM);
       // P's buffer and O are free once the previous tile's P.V has completed
       tc::mbar_wait(&sm.p_free, (uint32_t)((j & 1) ^ 1), err);
@@ -237,7 +248,7 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         if (j > 0) {
           tc::tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 8; c++) {
+          for (int c = 0; c < 4; c++) {
             uint32_t ov[16];
             tc::tmem_ld16(tO + c * 16, ov);
             tc::tmem_ld_wait();
@@ -252,7 +263,7 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
       }
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 8; c++) {
+      for (int c = 0; c < 4; c++) {
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
@@ -261,11 +272,10 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
           sum += p0 + p1;
           pk[e >> 1] = pack_bf16(p0, p1);
         }
-        // keys c*16 .. c*16+15: half c/4 of P, 16-byte chunks 2(c%4) and 2(c%4)+1 of the row, swizzled
-        uint8_t* ph = prow + (c >> 2) * (FA_QT * 128);
-        const int ch0 = 2 * (c & 3), ch1 = ch0 + 1;
-        *reinterpret_cast<uint4*>(ph + 16 * (ch0 ^ (r & 7))) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(ph + 16 * (ch1 ^ (r & 7))) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        // keys kh*64 + c*16 .. +15: 16-byte chunks 2c and 2c+1 of the row in half kh, swizzled
+        const int ch0 = 2 * c, ch1 = ch0 + 1;
+        *reinterpret_cast<uint4*>(prow + 16 * (ch0 ^ (r & 7))) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(prow + 16 * (ch1 ^ (r & 7))) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
       l += sum;
       tc::tc_fence_before();
@@ -273,15 +283,18 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.p_full);
     }
-    // the last P.V
+    // the last P.V, then the row sum of both halves
     tc::mbar_wait(&sm.p_free, (uint32_t)((NJ - 1) & 1), err);
     tc::tc_fence_after();
+    sm.lsum[kh][r] = l;
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+    l += sm.lsum[kh ^ 1][r];
     // every lane takes part in the warp-collective TMEM loads; rows past the chunk store nothing
     const bool store = qi < q_end;
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    __nv_bfloat16* dst = out + (int64_t)(qoff + (store ? qi : 0)) * ldo + (int64_t)h * FA_D;
+    __nv_bfloat16* dst = out + (int64_t)(qoff + (store ? qi : 0)) * ldo + (int64_t)h * FA_D + kh * 64;
 #pragma unroll 1
-    for (int c = 0; c < 8; c++) {
+    for (int c = 0; c < 4; c++) {
       uint32_t ov[16];
       tc::tmem_ld16(tO + c * 16, ov);
       tc::tmem_ld_wait();

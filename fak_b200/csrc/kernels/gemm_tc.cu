@@ -49,6 +49,24 @@ struct RsPeers {
 FAK_DEV void st_release_sys_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+FAK_DEV uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Sequence-parallel prefill: the A operand gathered from its owners (the all-gather fused into the
+// GEMM's loads).  m-block mb of A lives in rank mb % W's shard at owner-local row (mb / W) * 128;
+// map[r] is a TMA map over rank r's shard ([MR, K] bf16 in its peer buffer; plain tiled loads of
+// peer memory, no multicast).  Before a tile's first load the producer waits (bounded) until the
+// owner has released flags[mb] >= epoch in THIS rank's memory (owners push the flag to every rank).
+struct alignas(64) AgMaps {
+  CUtensorMap map[RS_MAX_W];
+  const uint32_t* flags;   // local flags [m-block]
+  uint32_t epoch;
+  uint32_t spin;
+  int W;
+};
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -71,7 +89,7 @@ template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M, int N,
             int K, OutT* __restrict__ out, int64_t ldo, const float* __restrict__ bias, int epi, int* __restrict__ err,
-            RsPeers rs) {
+            RsPeers rs, const __grid_constant__ AgMaps ag) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   GemmSmem<BN, STAGES>& sm = *reinterpret_cast<GemmSmem<BN, STAGES>*>(base);
@@ -224,7 +242,7 @@ template <int BN, int STAGES, typename OutT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                        int M, int N, int K, OutT* __restrict__ out, int64_t ldo, const float* __restrict__ bias,
-                       int epi, int* __restrict__ err, RsPeers rs) {
+                       int epi, int* __restrict__ err, RsPeers rs, const __grid_constant__ AgMaps ag) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   GemmSmemP<BN, STAGES>& sm = *reinterpret_cast<GemmSmemP<BN, STAGES>*>(base);
@@ -259,14 +277,29 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
   if (warp == 0) {
     if (lane == 0) {
       int g = 0;  // k-blocks issued across tiles
+      for (int r = 0; r < ag.W; r++) tc::prefetch_tmap(&ag.map[r]);
       for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
         const int m0 = (t % n_m) * BM, n0 = (t / n_m) * BN;
+        const CUtensorMap* amap = &tmap_a;
+        int ay = m0;
+        if (ag.W > 0) {   // gathered A: the owner's shard, once its rows are released
+          const int mb = m0 / BM;
+          amap = &ag.map[mb % ag.W];
+          ay = (mb / ag.W) * BM;
+          uint32_t it = 0;
+          while (ld_acquire_sys_u32(ag.flags + mb) < ag.epoch) {
+            if (++it > ag.spin) {
+              report_error(err, 1);
+              break;
+            }
+          }
+        }
         for (int kb = 0; kb < nkb; kb++, g++) {
           const int s = g % STAGES;
           const uint32_t ph = (g / STAGES) & 1;
           tc::mbar_wait(&sm.empty[s], ph ^ 1, err);
           tc::mbar_arrive_expect_tx(&sm.full[s], (BM + BN) * BK * 2);
-          tc::tma_load_2d(sm.a[s], &tmap_a, &sm.full[s], kb * BK, m0);
+          tc::tma_load_2d(sm.a[s], amap, &sm.full[s], kb * BK, ay);
           tc::tma_load_2d(sm.b[s], &tmap_b, &sm.full[s], kb * BK, n0);
         }
       }
@@ -395,7 +428,7 @@ CUtensorMap make_map_bf16_kmajor(const void* ptr, int64_t rows, int64_t cols, in
 
 template <int BN, int STAGES, typename OutT>
 void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, OutT* out, int64_t ldo, const float* bias, int epi,
-                 int* err, bool persistent, const RsPeers& rs) {
+                 int* err, bool persistent, const RsPeers& rs, const AgMaps& ag) {
   const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
   CUtensorMap ma = make_map_bf16_kmajor(a.data_ptr(), M, K, a.stride(0), BM);
   CUtensorMap mb = make_map_bf16_kmajor(b.data_ptr(), N, K, b.stride(0), BN);
@@ -415,7 +448,7 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, OutT* out, int6
   attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, out, ldo, bias, epi, err, rs));
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, M, N, K, out, ldo, bias, epi, err, rs, ag));
 }
 
 }  // namespace
@@ -448,11 +481,12 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
     return !(e && e[0] == '0');
   }();
   const RsPeers rs = {};
+  static const AgMaps no_ag = {};
   if (out.scalar_type() == torch::kFloat32)
-    launch_gemm<256, 4, float>(a, b, out.data_ptr<float>(), out.stride(0), bp, (int)epi, ep, persistent, rs);
+    launch_gemm<256, 4, float>(a, b, out.data_ptr<float>(), out.stride(0), bp, (int)epi, ep, persistent, rs, no_ag);
   else if (out.scalar_type() == torch::kBFloat16)
     launch_gemm<256, 4, __nv_bfloat16>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
-                                        out.stride(0), bp, (int)epi, ep, persistent, rs);
+                                        out.stride(0), bp, (int)epi, ep, persistent, rs, no_ag);
   else
     TORCH_CHECK(false, "out must be float32 or bfloat16");
 }
@@ -486,5 +520,52 @@ void gemm_bf16_rs(torch::Tensor a, torch::Tensor b, torch::Tensor peers, int64_t
   rs.MR = (int)MR;
   rs.epoch = (uint32_t)epoch;
   int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
-  launch_gemm<256, 4, float>(a, b, nullptr, 0, nullptr, G_RS, ep, true, rs);
+  static const AgMaps no_ag = {};
+  launch_gemm<256, 4, float>(a, b, nullptr, 0, nullptr, G_RS, ep, true, rs, no_ag);
+}
+
+// Sequence-parallel prefill GEMM: out (op)= A . B^T with A's m-blocks gathered from their owners'
+// normalised shards (see AgMaps).  peers: int64 [W] peer-buffer bases; shard_off: the [MR, K] bf16
+// shard in every buffer; flags_off: this rank's release flags [m-blocks]; M: rows of A and out.
+// With rs_parts_off >= 0 the epilogue is the reduce-scatter of G_RS instead (out unused).
+void gemm_bf16_ag(int64_t M, torch::Tensor b, torch::Tensor out, torch::Tensor peers, int64_t me, int64_t shard_off,
+                  int64_t MR, int64_t flags_off, int64_t epoch, int64_t spin, c10::optional<torch::Tensor> bias,
+                  int64_t epi, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(b.scalar_type() == torch::kBFloat16 && b.dim() == 2 && b.stride(1) == 1 && b.stride(0) % 8 == 0,
+              "b: [N,K] bf16");
+  TORCH_CHECK(peers.device().is_cpu() && peers.scalar_type() == torch::kInt64, "peers: int64 CPU tensor");
+  const int W = (int)peers.numel();
+  TORCH_CHECK(W >= 1 && W <= RS_MAX_W && me >= 0 && me < W, "gemm_bf16_ag: ranks");
+  const int64_t N = b.size(0), K = b.size(1);
+  TORCH_CHECK(K % 8 == 0 && shard_off % 16 == 0 && flags_off % 4 == 0, "gemm_bf16_ag: K % 8, offsets");
+  TORCH_CHECK(MR >= ((M + BM - 1) / BM + W - 1) / W * BM, "gemm_bf16_ag: MR too small");
+  TORCH_CHECK(epi >= 0 && epi <= 3 && out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= M &&
+                  out.size(1) >= (epi >= G_SWIGLU ? N / 2 : N), "gemm_bf16_ag: out");
+  if (M == 0 || N == 0) return;
+  const float* bp = nullptr;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "bias");
+    bp = bias->data_ptr<float>();
+  }
+  AgMaps ag = {};
+  const int64_t* pp = peers.data_ptr<int64_t>();
+  for (int r = 0; r < W; r++)
+    ag.map[r] = make_map_bf16_kmajor(reinterpret_cast<const uint8_t*>(pp[r]) + shard_off, MR, K, K, BM);
+  ag.flags = reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(pp[me]) + flags_off);
+  ag.epoch = (uint32_t)epoch;
+  ag.spin = spin > 0 ? (uint32_t)spin : (1u << 26);
+  ag.W = W;
+  // launch_gemm takes M from a's rows and encodes a map of it for the plain path; in this mode that
+  // map is never read (every A load goes through ag.map), so a view of this rank's shard stands in
+  auto a_view = torch::from_blob(reinterpret_cast<uint8_t*>(pp[me]) + shard_off, {M, K},
+                                 torch::TensorOptions().dtype(torch::kBFloat16).device(out.device()));
+  const RsPeers rs = {};
+  int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
+  if (out.scalar_type() == torch::kFloat32)
+    launch_gemm<256, 4, float>(a_view, b, out.data_ptr<float>(), out.stride(0), bp, (int)epi, ep, true, rs, ag);
+  else if (out.scalar_type() == torch::kBFloat16)
+    launch_gemm<256, 4, __nv_bfloat16>(a_view, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
+                                        out.stride(0), bp, (int)epi, ep, true, rs, ag);
+  else
+    TORCH_CHECK(false, "out must be float32 or bfloat16");
 }

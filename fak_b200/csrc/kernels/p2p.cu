@@ -146,9 +146,11 @@ FAK_DEV bool wait_flag_ge(const uint32_t* f, uint32_t v, uint32_t spin, int* err
   return true;
 }
 
+// x_local != nullptr (sequence parallel): the residual is this rank's owned rows only, compacted
+// ([MR, N], owner-local row index), updated in place with no broadcast and no closing barrier.
 __global__ void k_p2p_rs_reduce(Peers P, int64_t parts_off, int64_t flags_off, int64_t x_off, int M, int N, int MR,
                                 int me, int W, uint32_t epoch, int64_t bar_off, int site, uint32_t* counters,
-                                int* err) {
+                                int* err, float* __restrict__ x_local) {
   pdl_wait();
   const int n_m = (M + RS_BM - 1) / RS_BM, n_n = (N + RS_BN - 1) / RS_BN;
   const int own = me < n_m ? (n_m - 1 - me) / W + 1 : 0;   // owned m-blocks me, me + W, ...
@@ -164,17 +166,60 @@ __global__ void k_p2p_rs_reduce(Peers P, int64_t parts_off, int64_t flags_off, i
     const int rows = min(RS_BM, M - mb * RS_BM), cols4 = min(RS_BN, N - nb * RS_BN) >> 2;
     for (int e = threadIdx.x; e < rows * cols4; e += blockDim.x) {
       const int rr = e / cols4, c = nb * RS_BN + 4 * (e - rr * cols4);
-      const int64_t xi = (int64_t)(mb * RS_BM + rr) * N + c;
-      float4 acc = *reinterpret_cast<const float4*>(xl + xi);
+      const int64_t xi = x_local ? (int64_t)(k * RS_BM + rr) * N + c : (int64_t)(mb * RS_BM + rr) * N + c;
+      float4 acc = *reinterpret_cast<const float4*>((x_local ? x_local : xl) + xi);
       for (int r = 0; r < W; r++) {
         const float4 v = __ldcg(reinterpret_cast<const float4*>(parts + ((int64_t)r * MR + k * RS_BM + rr) * N + c));
         acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
       }
-      for (int r = 0; r < W; r++) *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.base[r] + x_off) + xi) = acc;
+      if (x_local)
+        *reinterpret_cast<float4*>(x_local + xi) = acc;
+      else
+        for (int r = 0; r < W; r++) *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.base[r] + x_off) + xi) = acc;
     }
     __syncthreads();
   }
-  rank_barrier(P, bar_off, site, blockIdx.x, me, W, counters, err);
+  if (!x_local) rank_barrier(P, bar_off, site, blockIdx.x, me, W, counters, err);
+  pdl_launch_dependents();
+}
+
+// Sequence-parallel prefill: RMSNorm of this rank's owned rows (x_local [MR, N] compacted, `valid`
+// of them real) into the bf16 shard of its peer buffer (shard_off, [MR, N]); once a 128-row block is
+// written and fenced, its release flag (flags[m-block] = epoch) is stored into EVERY rank's buffer,
+// so the next GEMM's producers (gemm_bf16_ag) wait on local memory.  One CTA per owned block, a
+// warp per row.
+__global__ void k_sp_rmsnorm_shard(Peers P, const float* __restrict__ x_local, const float* __restrict__ gamma,
+                                   float eps, int N, int valid, int64_t shard_off, int64_t flags_off, int me, int W,
+                                   uint32_t epoch) {
+  pdl_wait();
+  const int k = blockIdx.x, mb = me + k * W;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __nv_bfloat16* shard = reinterpret_cast<__nv_bfloat16*>(P.base[me] + shard_off);
+  for (int rr = warp; rr < RS_BM; rr += nw) {
+    const int lr = k * RS_BM + rr;
+    if (lr >= valid) break;
+    const float* xr = x_local + (int64_t)lr * N;
+    float ss = 0.f;
+    for (int c = lane * 4; c < N; c += 128) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + c);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / (float)N + eps);
+    for (int c = lane * 4; c < N; c += 128) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + c);
+      const float4 gm = *reinterpret_cast<const float4*>(gamma + c);
+      __nv_bfloat162 a = __floats2bfloat162_rn(v.x * inv * gm.x, v.y * inv * gm.y);
+      __nv_bfloat162 b = __floats2bfloat162_rn(v.z * inv * gm.z, v.w * inv * gm.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&a);
+      pk.y = *reinterpret_cast<uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(shard + (int64_t)lr * N + c) = pk;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < W) st_release_sys(reinterpret_cast<uint32_t*>(P.base[threadIdx.x] + flags_off) + mb, epoch);
   pdl_launch_dependents();
 }
 
@@ -362,7 +407,7 @@ void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, i
 // rank's peer buffer, [M, N] fp32) += sum over ranks of the partials; site: barrier site for the end.
 void p2p_rs_reduce(torch::Tensor peers, int64_t parts_off, int64_t flags_off, int64_t x_off, int64_t M, int64_t N,
                    int64_t MR, int64_t me, int64_t epoch, int64_t bar_off, int64_t site, torch::Tensor counters,
-                   torch::Tensor err, int64_t ctas, int64_t spin_limit) {
+                   torch::Tensor err, int64_t ctas, int64_t spin_limit, c10::optional<torch::Tensor> x_local) {
   const int W = (int)peers.numel();
   TORCH_CHECK(N % 4 == 0 && parts_off % 16 == 0 && x_off % 16 == 0 && flags_off % 4 == 0, "rs_reduce: alignment");
   TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "rs_reduce: 1..64 CTAs");
@@ -371,9 +416,32 @@ void p2p_rs_reduce(torch::Tensor peers, int64_t parts_off, int64_t flags_off, in
   Peers P = make_peers(peers, spin_limit);
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
+  float* xl = nullptr;
+  if (x_local.has_value()) {
+    TORCH_CHECK(x_local->is_cuda() && x_local->scalar_type() == torch::kFloat32 && x_local->is_contiguous() &&
+                    x_local->numel() >= MR * N, "rs_reduce: x_local [MR, N] f32");
+    xl = x_local->data_ptr<float>();
+  }
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_rs_reduce, P, parts_off, flags_off, x_off, (int)M, (int)N, (int)MR,
                                     (int)me, W, (uint32_t)epoch, bar_off, (int)site,
-                                    (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>()));
+                                    (uint32_t*)counters.data_ptr<int>(), err.data_ptr<int>(), xl));
+}
+
+void sp_rmsnorm_shard(torch::Tensor peers, torch::Tensor x_local, torch::Tensor gamma, double eps, int64_t valid,
+                      int64_t shard_off, int64_t flags_off, int64_t me, int64_t epoch) {
+  const int W = (int)peers.numel();
+  TORCH_CHECK(x_local.is_cuda() && x_local.scalar_type() == torch::kFloat32 && x_local.dim() == 2 &&
+                  x_local.is_contiguous() && x_local.size(1) % 128 == 0, "sp_rmsnorm: x_local [MR, N] f32, N % 128");
+  TORCH_CHECK(gamma.scalar_type() == torch::kFloat32 && gamma.numel() >= x_local.size(1), "sp_rmsnorm: gamma");
+  TORCH_CHECK(shard_off % 16 == 0 && valid <= x_local.size(0), "sp_rmsnorm: shard / rows");
+  const int blocks = (int)((valid + RS_BM - 1) / RS_BM);
+  if (blocks == 0) return;
+  Peers P = make_peers(peers, 0);
+  cudaLaunchAttribute attr[1];
+  auto cfg = pdl_cfg(dim3((unsigned)blocks), dim3(512), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_sp_rmsnorm_shard, P, (const float*)x_local.data_ptr<float>(),
+                                    (const float*)gamma.data_ptr<float>(), (float)eps, (int)x_local.size(1),
+                                    (int)valid, shard_off, flags_off, (int)me, W, (uint32_t)epoch));
 }
 
 void p2p_rs_push(torch::Tensor peers, torch::Tensor part, int64_t MR, int64_t parts_off, int64_t flags_off, int64_t me,

@@ -452,6 +452,8 @@ class ModelRunner:
         cfg, dev = self.cfg, self.device
         T = ids.numel()
         d = cfg.d_model
+        if self.coll is not None and getattr(self.coll, "sp_ok", lambda *_: False)(T):
+            return self._prefill_sp(ids, pos, slot, bt, meta, last_idx)
         # under fused tensor parallelism the residual lives in the peer buffer (the prefill all-reduce
         # stores reduced rows into every rank's copy)
         x = self.coll.prefill_x(T) if self.coll is not None and hasattr(self.coll, "prefill_x") else None
@@ -497,8 +499,12 @@ class ModelRunner:
                 K.gemm(hb2, L.down, x, K.EPI_ADD)
             else:
                 self.coll.prefill_down(self, i, hb2, x)
-        S = last_idx.numel()
-        xl = x.index_select(0, last_idx.long())
+        return self._prefill_logits(x.index_select(0, last_idx.long()))
+
+    def _prefill_logits(self, xl: torch.Tensor) -> torch.Tensor:
+        """LM-head logits [S, V] of the chunk's last rows xl [S, d] (final norm inside the GEMV)."""
+        cfg, dev = self.cfg, self.device
+        S = xl.shape[0]
         logits = torch.empty(S, cfg.vocab_size, dtype=torch.float32, device=dev)
         for s0 in range(0, S, self.max_batch):
             s1 = min(S, s0 + self.max_batch)
@@ -509,3 +515,36 @@ class ModelRunner:
             else:
                 self.coll.lm_head_to(self, n, logits[s0:s1])
         return logits
+
+    def _prefill_sp(self, ids, pos, slot, bt, meta: PrefillMeta, last_idx: torch.Tensor) -> torch.Tensor:
+        """Sequence-parallel prefill under fused tensor parallelism (Megatron-SP).  The residual stays
+        sharded by 128-row blocks (rank r owns blocks r, r + W, ...): each rank embeds and normalises
+        only its rows, the column-parallel GEMMs (qkv, gate/up) gather their input blocks from the
+        owners inside the GEMM, and the row-parallel ones (o_proj, down) reduce-scatter their output
+        tiles to the owners, which add them to their rows -- no full-residual all-gather at all."""
+        cfg, dev, coll = self.cfg, self.device, self.coll
+        T = ids.numel()
+        x, own_rows, valid = coll.sp_begin(T)
+        K.embed(self.w.embed, ids.index_select(0, own_rows.clamp(min=0)), x, None, self.err, scale=cfg.embed_scale)
+        qkv = torch.empty(T, self.qkv_dim, dtype=torch.float32, device=dev)
+        qb = torch.empty(T, self.Hq, self.D, dtype=torch.bfloat16, device=dev)
+        ab = torch.empty(T, self.Hq * self.D, dtype=torch.bfloat16, device=dev)
+        for i in range(cfg.n_layers):
+            L = self.w.layers[i]
+            coll.sp_norm(x, L.attn_norm, cfg.rms_eps, valid)
+            for seg, off in L.qkv:
+                bias = L.qkv_bias[off:off + seg.rows] if L.qkv_bias is not None else None
+                coll.sp_gemm(T, seg.dense(), qkv[:, off:off + seg.rows], K.EPI_STORE, bias)
+            K.rope_kv(qkv, pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
+                      None, qb, self.kv.k[i], self.kv.v[i])
+            if self.tc_prefill_attn and cfg.layer_window(i) <= 0:
+                K.prefill_attention_tc(qb, self.kv.k, self.kv.v, i, bt, meta, ab, self.err)
+            else:
+                K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab, cfg.layer_window(i),
+                                    cfg.attn_scale, cfg.attn_softcap)
+            coll.sp_rs(ab, coll.o_dense_local(self, i), x)
+            coll.sp_norm(x, L.ffn_norm, cfg.rms_eps, valid)
+            hb2 = torch.empty(T, self.ffn_local, dtype=torch.bfloat16, device=dev)
+            coll.sp_gemm(T, L.gate_up.dense(), hb2, self.gated_epi, None)
+            coll.sp_rs(hb2, L.down.dense(), x)
+        return self._prefill_logits(coll.sp_rows(x, own_rows, last_idx))

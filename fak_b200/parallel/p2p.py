@@ -132,6 +132,16 @@ class P2PTP(NcclTP):
         self.pf_flags_off = off
         off = _align(off + n_m * n_n * MAX_W * 4)
         self.pf_epoch = 0
+        # sequence-parallel prefill: this rank's normalised rows [MR, d] bf16 (read by every rank's
+        # column-parallel GEMM) and the per-m-block release flags the owners push to every rank
+        self.sp = self.pf_fused and not cfg.is_moe and cfg.d_model % 128 == 0 and \
+            os.environ.get("FAK_PREFILL_SP", "0") == "1"
+        self.sp_shard_off = off
+        off = _align(off + (self.pf_MR * d * 2 if self.sp else 0))
+        self.sp_flags_off = off
+        off = _align(off + (n_m * 4 if self.sp else 0))
+        self.sp_epoch = 0
+        self._sp_x = None
         self.nbytes = off
         self.mem = None
         if os.environ.get("FAK_P2P_MEM", "ipc") == "symm":
@@ -278,6 +288,70 @@ class P2PTP(NcclTP):
                           self.pf_epoch)
         self._pf_reduce(x.shape[0])
         K.count(2)
+
+    # ---- sequence-parallel prefill ----------------------------------------------------
+    def sp_ok(self, T: int) -> bool:
+        return self.sp and 0 < T <= self.pf_T
+
+    def sp_begin(self, T: int) -> tuple[torch.Tensor, torch.Tensor, int]:
+        """(the owned-rows residual [MR, d] fp32, the global row of each of its rows (-1: padding),
+        how many of its rows are real).  Rank me owns 128-row blocks me, me + W, ..."""
+        d, W, MR = self.cfg.d_model, self.world, self.pf_MR
+        if self._sp_x is None:
+            self._sp_x = torch.zeros(MR, d, dtype=torch.float32, device=self.buf.device)
+        n_m = -(-T // 128)
+        rows = torch.full((MR,), -1, dtype=torch.int64)
+        valid = 0
+        for k, mb in enumerate(range(self.me, n_m, W)):
+            n = min(128, T - mb * 128)
+            rows[k * 128:k * 128 + n] = torch.arange(mb * 128, mb * 128 + n)
+            valid = k * 128 + n
+        return self._sp_x, rows.to(self.buf.device, non_blocking=True), valid
+
+    def sp_norm(self, x: torch.Tensor, gamma: torch.Tensor, eps: float, valid: int) -> None:
+        """RMSNorm of the owned rows into this rank's bf16 shard; each block's flag goes to every rank."""
+        self.sp_epoch += 1
+        ext().sp_rmsnorm_shard(self.peers, x, gamma, eps, valid, self.sp_shard_off, self.sp_flags_off, self.me,
+                               self.sp_epoch)
+        K.count()
+
+    def sp_gemm(self, T: int, w: torch.Tensor, out: torch.Tensor, epi: int, bias) -> None:
+        """out (op)= gathered-normalised-rows . w^T: each m-block of A read from its owner's shard."""
+        ext().gemm_bf16_ag(T, w, out, self.peers, self.me, self.sp_shard_off, self.pf_MR, self.sp_flags_off,
+                           self.sp_epoch, self.spin_limit, bias, epi, self.err)
+        K.count()
+
+    def sp_rs(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor) -> None:
+        """Owned rows += their slice of sum over ranks of a . w^T (reduce-scatter in the GEMM epilogue,
+        the owner's sum into its compacted rows, no broadcast)."""
+        if w.shape[0] != self.cfg.d_model:
+            raise ValueError("sequence-parallel reduce: the slots hold [tokens, d_model] partials")
+        T = a.shape[0]
+        self.pf_epoch += 1
+        ext().gemm_bf16_rs(a, w, self.peers, self.me, self.pf_parts_off, self.pf_flags_off, self.pf_MR,
+                           self.pf_epoch, self.err)
+        ext().p2p_rs_reduce(self.peers, self.pf_parts_off, self.pf_flags_off, self.pf_x_off, T, self.cfg.d_model,
+                            self.pf_MR, self.me, self.pf_epoch, self.flags_off, self.n_sites - 1, self.counters,
+                            self.err, RS_CTAS, self.spin_limit, x)
+        K.count(2)
+
+    def sp_rows(self, x: torch.Tensor, own_rows: torch.Tensor, last_idx: torch.Tensor) -> torch.Tensor:
+        """[S, d]: the residual rows last_idx (global rows) gathered from their owners, through the
+        in-kernel all-reduce (each rank contributes the rows it owns, zeros elsewhere)."""
+        S, d = last_idx.numel(), self.cfg.d_model
+        if S > self.B:
+            raise ValueError(f"sequence-parallel prefill: {S} sequences in a chunk (at most {self.B})")
+        loc = torch.full((self.pf_T + 128,), -1, dtype=torch.int64, device=x.device)
+        real = own_rows >= 0
+        loc[own_rows[real]] = torch.nonzero(real).flatten()
+        li = loc[last_idx.long()]
+        off, part = self._part(0, 0, S)
+        part.copy_(torch.where((li >= 0)[:, None], x[li.clamp(min=0)], torch.zeros((), device=x.device)))
+        out = torch.zeros(S, d, dtype=torch.float32, device=x.device)
+        ext().p2p_allreduce_add(self.peers, off, out, S * d, self.flags_off, self.n_sites - 1, self.me, self.counters,
+                                self.err, AR_CTAS, self.spin_limit)
+        K.count(4)
+        return out
 
     def reduce_partial(self, rn, i: int, B: int, fill) -> None:
         """x += sum over ranks of the partial fill() writes (MoE expert bands), via the P2P all-reduce."""
