@@ -3,8 +3,9 @@
 // One CTA per (128-query tile of one sequence, query head).  The chunk's queries attend causally to
 // the sequence's cached prefix and to themselves (their K/V are already in the pages).  Warp roles:
 //   warp 0      TMA producer: the Q tile once (two 64-column halves, 128-byte swizzle), then per KV
-//               tile of 128 keys the 8 pages of K and of V (16 x 64 boxes of a 3-D map over the cache,
-//               [layer * pages * kv heads, 16 tokens, head dim]) into a 2-stage ring;
+//               tile of 128 keys the 8 pages of K (one stage, refilled as soon as S of the previous
+//               tile is done) and of V (two stages) as 16 x 64 boxes of a 3-D map over the cache,
+//               [layer * pages * kv heads, 16 tokens, head dim];
 //   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M = N = 128, K = head dim) into one of
 //               two TMEM S buffers, and O += P_j V_j (V as an MN-major operand: keys x head dim as it
 //               sits in the pages) into one TMEM O buffer that lives for the whole CTA;
@@ -17,7 +18,8 @@
 //               running row max, moved only when it grew by more than 2^8 (then each half rescales
 //               its 64 columns of the rows' O in TMEM, once the previous P.V has completed), so
 //               P <= 256 and most tiles touch O not at all; the halves' row sums add at the end.
-// S of tile j + 1 is computed while tile j's softmax runs.  Every wait is bounded (tc::mbar_wait);
+// P has two buffers, so the softmax of tile j + 1 does not wait for P.V_j (only an O rescale does),
+// and S of tile j + 1 is computed while tile j's softmax runs.  Every wait is bounded (tc::mbar_wait);
 // no load uses multicast.  Head dim 128, no window / soft-cap (those shapes use k_prefill_attn).
 // Reference: k_flash_attention, internal/compute/cuda_kernels.cu:701-759 (one block per head, SIMT).
 #include <torch/extension.h>
@@ -41,13 +43,14 @@ constexpr float FA_HEADROOM = 8.f;   // log2 growth of a row max tolerated befor
 
 struct FaSmem {
   alignas(1024) __nv_bfloat16 q[2][FA_QT * 64];               // [D half][128 rows x 64]
-  alignas(1024) __nv_bfloat16 k[FA_STAGES][2][FA_KT * 64];    // [stage][D half][128 keys x 64]
-  alignas(1024) __nv_bfloat16 v[FA_STAGES][2][FA_KT * 64];
-  alignas(1024) __nv_bfloat16 p[2][FA_QT * 64];               // [key half][128 rows x 64 keys]
+  alignas(1024) __nv_bfloat16 k[2][FA_KT * 64];               // one stage: [D half][128 keys x 64]
+  alignas(1024) __nv_bfloat16 v[FA_STAGES][2][FA_KT * 64];    // [stage][D half][128 keys x 64]
+  alignas(1024) __nv_bfloat16 p[2][2][FA_QT * 64];            // [buffer][key half][128 rows x 64 keys]
   uint64_t q_full;
-  uint64_t kv_full[FA_STAGES], kv_empty[FA_STAGES];
+  uint64_t k_full, k_empty;
+  uint64_t v_full[FA_STAGES], v_empty[FA_STAGES];
   uint64_t s_full[2], s_free[2];
-  uint64_t p_full, p_free;
+  uint64_t p_full[2], p_free[2];   // per P buffer: written by the softmax / read by its P.V (done)
   float red[2][2][FA_QT];   // row max of each key half, by tile parity
   float lsum[2][FA_QT];     // row sums of each key half (end of the CTA)
   uint32_t tmem_base;
@@ -98,16 +101,18 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
 
   if (threadIdx.x == 0) {
     tc::mbar_init(&sm.q_full, 1);
+    tc::mbar_init(&sm.k_full, 1);
+    tc::mbar_init(&sm.k_empty, 1);
     for (int s = 0; s < FA_STAGES; s++) {
-      tc::mbar_init(&sm.kv_full[s], 1);
-      tc::mbar_init(&sm.kv_empty[s], 1);
+      tc::mbar_init(&sm.v_full[s], 1);
+      tc::mbar_init(&sm.v_empty[s], 1);
     }
     for (int i = 0; i < 2; i++) {
       tc::mbar_init(&sm.s_full[i], 1);
       tc::mbar_init(&sm.s_free[i], 8);   // one arrival per softmax warp
+      tc::mbar_init(&sm.p_full[i], 8);
+      tc::mbar_init(&sm.p_free[i], 1);
     }
-    tc::mbar_init(&sm.p_full, 8);
-    tc::mbar_init(&sm.p_free, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmap_q);
     tc::prefetch_tmap(&tmap_k);
@@ -137,19 +142,25 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
       tc::tma_load_2d(sm.q[0], &tmap_q, &sm.q_full, h * FA_D, qoff + q0);
       tc::tma_load_2d(sm.q[1], &tmap_q, &sm.q_full, h * FA_D + 64, qoff + q0);
       for (int j = 0; j < NJ; j++) {
-        const int st = j % FA_STAGES;
-        const uint32_t ph = (uint32_t)((j / FA_STAGES) & 1);
-        tc::mbar_wait(&sm.kv_empty[st], ph ^ 1, err);
-        tc::mbar_arrive_expect_tx(&sm.kv_full[st], 2 * FA_KT * FA_D * 2);
+        // K of tile j: its single stage is free once S_{j-1} has been computed
+        tc::mbar_wait(&sm.k_empty, (uint32_t)((j & 1) ^ 1), err);
+        tc::mbar_arrive_expect_tx(&sm.k_full, FA_KT * FA_D * 2);
 #pragma unroll 1
         for (int pi = 0; pi < FA_KT / FA_PG; pi++) {
           // pages past the visible keys repeat the last one (their keys are masked; the data stays finite)
           const int pidx = min(j * (FA_KT / FA_PG) + pi, n_valid_pages - 1);
           const int z = (layer * n_pages + bt[pidx]) * Hkv + g;
-          for (int hd = 0; hd < 2; hd++) {
-            tma_load_3d(sm.k[st][hd] + pi * FA_PG * 64, &tmap_k, &sm.kv_full[st], hd * 64, 0, z);
-            tma_load_3d(sm.v[st][hd] + pi * FA_PG * 64, &tmap_v, &sm.kv_full[st], hd * 64, 0, z);
-          }
+          for (int hd = 0; hd < 2; hd++) tma_load_3d(sm.k[hd] + pi * FA_PG * 64, &tmap_k, &sm.k_full, hd * 64, 0, z);
+        }
+        // V of tile j: stage j % 2, free once P.V_{j-2} has completed
+        const int st = j % FA_STAGES;
+        tc::mbar_wait(&sm.v_empty[st], (uint32_t)(((j / FA_STAGES) & 1) ^ 1), err);
+        tc::mbar_arrive_expect_tx(&sm.v_full[st], FA_KT * FA_D * 2);
+#pragma unroll 1
+        for (int pi = 0; pi < FA_KT / FA_PG; pi++) {
+          const int pidx = min(j * (FA_KT / FA_PG) + pi, n_valid_pages - 1);
+          const int z = (layer * n_pages + bt[pidx]) * Hkv + g;
+          for (int hd = 0; hd < 2; hd++) tma_load_3d(sm.v[st][hd] + pi * FA_PG * 64, &tmap_v, &sm.v_full[st], hd * 64, 0, z);
         }
       }
     }
@@ -161,34 +172,36 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
       tc::mbar_wait(&sm.q_full, 0, err);
       for (int j = 0; j <= NJ; j++) {
         if (j < NJ) {
-          const int st = j % FA_STAGES, b = j & 1;
-          tc::mbar_wait(&sm.kv_full[st], (uint32_t)((j / FA_STAGES) & 1), err);
+          const int b = j & 1;
+          tc::mbar_wait(&sm.k_full, (uint32_t)(j & 1), err);
           tc::mbar_wait(&sm.s_free[b], (uint32_t)(((j >> 1) & 1) ^ 1), err);
           tc::tc_fence_after();
           const uint32_t ts = tmem + (uint32_t)(b * 128);
 #pragma unroll
           for (int hd = 0; hd < 2; hd++) {
             const uint64_t ad = tc::smem_desc_sw128(sm.q[hd]);
-            const uint64_t bd = tc::smem_desc_sw128(sm.k[st][hd]);
+            const uint64_t bd = tc::smem_desc_sw128(sm.k[hd]);
 #pragma unroll
             for (int kk = 0; kk < 4; kk++) tc::mma_bf16(ts, ad + 2 * kk, bd + 2 * kk, idesc_s, (hd | kk) != 0);
           }
           tc::mma_commit(&sm.s_full[b]);
+          tc::mma_commit(&sm.k_empty);       // S_j done: K's stage takes tile j + 1
         }
         if (j > 0) {
-          const int jj = j - 1, st = jj % FA_STAGES;
-          tc::mbar_wait(&sm.p_full, (uint32_t)(jj & 1), err);
+          const int jj = j - 1, st = jj % FA_STAGES, pb = jj & 1;
+          tc::mbar_wait(&sm.p_full[pb], (uint32_t)((jj >> 1) & 1), err);
+          tc::mbar_wait(&sm.v_full[st], (uint32_t)((jj / FA_STAGES) & 1), err);
           tc::tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < FA_KT / 16; ks++) {
-            const uint64_t ad = tc::smem_desc_sw128(sm.p[ks >> 2]) + 2 * (ks & 3);
+            const uint64_t ad = tc::smem_desc_sw128(sm.p[pb][ks >> 2]) + 2 * (ks & 3);
             // 16 keys per step = 2 swizzle atoms of V; the two 64-column halves of the head dim are
             // 16 KB apart (LBO), 8-key groups 1 KB apart (SBO)
             const uint64_t bd = smem_desc_sw128_mn(sm.v[st][0] + ks * 16 * 64, FA_KT * 128, 1024);
             tc::mma_bf16(to, ad, bd, idesc_pv, (jj > 0 || ks != 0) ? 1u : 0u);
           }
-          tc::mma_commit(&sm.p_free);        // P.V_jj done: O current, P's buffer free
-          tc::mma_commit(&sm.kv_empty[st]);
+          tc::mma_commit(&sm.p_free[pb]);    // P.V_jj done: O holds tiles <= jj, P buffer pb free
+          tc::mma_commit(&sm.v_empty[st]);
         }
       }
     }
@@ -202,9 +215,9 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tO = tmem + lane_off + 256u + (uint32_t)(kh * 64);   // this half's 64 columns of O
     float m = -INFINITY, l = 0.f;                    // exponent base (log2 units) and half-row sum against it
-    uint8_t* prow = reinterpret_cast<uint8_t*>(sm.p[kh]) + r * 128;
     for (int j = 0; j < NJ; j++) {
       const int b = j & 1;
+      uint8_t* prow = reinterpret_cast<uint8_t*>(sm.p[b][kh]) + r * 128;
       tc::mbar_wait(&sm.s_full[b], (uint32_t)((j >> 1) & 1), err);
       tc::tc_fence_after();
       const uint32_t ts = tmem + lane_off + (uint32_t)(b * 128 + kh * 64);
@@ -216,22 +229,25 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.s_free[b]);   // S is in registers: the buffer can take S_{j+2}
       const int k0 = j * FA_KT + kh * 64;
-      float mx = -INFINITY;
-      if (k0 + 63 > warp_pos) {   // a diagonal tile for this warp: mask keys past each row's position
+      // row max over four independent accumulators (a short dependency chain)
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      const bool diag = k0 + 63 > warp_pos;   // warp-uniform
+      if (diag) {   // a diagonal tile for this warp: mask keys past each row's position
 #pragma unroll
         for (int c = 0; c < 4; c++)
 #pragma unroll
           for (int e = 0; e < 16; e++) {
             const float x = k0 + c * 16 + e <= pos ? __uint_as_float(sv[c][e]) : -INFINITY;
             sv[c][e] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
+            m4[e & 3] = fmaxf(m4[e & 3], x);
           }
       } else {
 #pragma unroll
         for (int c = 0; c < 4; c++)
 #pragma unroll
-          for (int e = 0; e < 16; e++) mx = fmaxf(mx, __uint_as_float(sv[c][e]));
+          for (int e = 0; e < 16; e++) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[c][e]));
       }
+      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       // the other half's max of the same row (slots alternate by tile parity: a slot is rewritten
       // two tiles later, after a barrier the partner passes only once it has read it)
       sm.red[b][kh][r] = mx;
@@ -241,11 +257,11 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
       // move the base (and rescale O and l) only when some row of the warp outgrew the headroom;
       // the partner warp holds the same rows and values, so it takes the same decision
       const bool move = __any_sync(0xffffffffu, m_new > m + FA_HEADROOM);
-      // P's buffer and O are free once the previous tile's P.V has completed
-      tc::mbar_wait(&sm.p_free, (uint32_t)((j & 1) ^ 1), err);
       if (move) {
         const float f = ex2(m - m_new);   // 0 on the first tile
         if (j > 0) {
+          // O must hold every earlier tile before it is rescaled: wait for P.V_{j-1}
+          tc::mbar_wait(&sm.p_free[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), err);
           tc::tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 4; c++) {
@@ -261,7 +277,9 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         l *= f;
         m = m_new;
       }
-      float sum = 0.f;
+      // this tile's P buffer is free once P.V_{j-2} has completed
+      tc::mbar_wait(&sm.p_free[b], (uint32_t)(((j >> 1) & 1) ^ 1), err);
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};   // row sum, four independent accumulators
 #pragma unroll
       for (int c = 0; c < 4; c++) {
         uint32_t pk[8];
@@ -269,7 +287,7 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         for (int e = 0; e < 16; e += 2) {
           const float p0 = ex2(fmaf(__uint_as_float(sv[c][e]), scale_log2, -m));
           const float p1 = ex2(fmaf(__uint_as_float(sv[c][e + 1]), scale_log2, -m));
-          sum += p0 + p1;
+          s4[(e >> 1) & 3] += p0 + p1;
           pk[e >> 1] = pack_bf16(p0, p1);
         }
         // keys kh*64 + c*16 .. +15: 16-byte chunks 2c and 2c+1 of the row in half kh, swizzled
@@ -277,14 +295,14 @@ k_prefill_attn_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         *reinterpret_cast<uint4*>(prow + 16 * (ch0 ^ (r & 7))) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         *reinterpret_cast<uint4*>(prow + 16 * (ch1 ^ (r & 7))) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
-      l += sum;
+      l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
       tc::tc_fence_before();
       tc::fence_proxy_async();   // generic-proxy stores of P -> visible to the tensor cores
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&sm.p_full);
+      if (lane == 0) tc::mbar_arrive(&sm.p_full[b]);
     }
     // the last P.V, then the row sum of both halves
-    tc::mbar_wait(&sm.p_free, (uint32_t)((NJ - 1) & 1), err);
+    tc::mbar_wait(&sm.p_free[(NJ - 1) & 1], (uint32_t)(((NJ - 1) >> 1) & 1), err);
     tc::tc_fence_after();
     sm.lsum[kh][r] = l;
     asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
