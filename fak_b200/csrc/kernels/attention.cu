@@ -64,6 +64,106 @@ FAK_DEV void warp_quant_store(float v, int8_t* qdst, float2* dsdst, int lane) {
 // =============================================================================================
 // decode
 // =============================================================================================
+// Suffix splits of k_decode_attn that hold pages for a sequence of ctx tokens: the same page range
+// arithmetic as the kernel (window start, pages another kernel covers, pages per split).
+FAK_DEV int dec_live_splits(int ctx, int win, const int* skip_pages, int n_split, int pages_per_split) {
+  const int n_pages = (ctx + PAGE - 1) / PAGE;
+  int lo = win > 0 ? max(0, ctx - win) : 0;
+  if (skip_pages != nullptr) lo = max(lo, min(ctx, *skip_pages * PAGE));
+  const int live = n_pages - lo / PAGE;
+  if (live <= 0) return 0;
+  const int pps = max(pages_per_split, (live + n_split - 1) / n_split);
+  return min(n_split, (live + pps - 1) / pps);
+}
+
+constexpr int kCombineMaxSlots = 384;   // 256 suffix splits + 128 cascade prefix splits
+
+// Merge of one (sequence, head)'s split partials (o_s unnormalised, (m_s, l_s) in log2 units) by a
+// 128-thread CTA: block max of the m_s, weights f_s = 2^(m_s - max) and L = sum f_s l_s, then each
+// warp accumulates the splits s = warp (mod 4) with D/32 dims per lane and the four warps' sums
+// are added in warp order.  Used by k_decode_combine and by the in-kernel merge (tickets), which
+// therefore give the same bits.  Output: fp32 out and/or int8 codes with (scale, sum) per 32.
+// smem: sf [kCombineMaxSlots], red [4 * D], s_red [8] floats.
+template <int D>
+FAK_DEV void combine_head(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int64_t base,
+                          int n_used, float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds,
+                          int64_t oi0, float* sf, float* red, float* s_red) {
+  constexpr int VEC = D / 32;   // dims per lane
+  constexpr int GL = 32 / VEC;  // lanes per 32-element quantization block
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float mloc = NEG_INF;
+  for (int s = tid; s < n_used; s += 128) mloc = fmaxf(mloc, __ldcg(&part_ml[base + s].x));
+  mloc = warp_max(mloc);
+  if (lane == 0) s_red[warp] = mloc;
+  __syncthreads();
+  const float mstar = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+  const float mb = mstar == NEG_INF ? 0.f : mstar;
+  float lloc = 0.f;
+  for (int s = tid; s < n_used; s += 128) {
+    const float2 ml = __ldcg(&part_ml[base + s]);
+    const float f = exp2f(ml.x - mb);
+    sf[s] = f;
+    lloc += f * ml.y;
+  }
+  lloc = warp_sum(lloc);
+  if (lane == 0) s_red[4 + warp] = lloc;
+  __syncthreads();
+  const float L = (s_red[4] + s_red[5]) + (s_red[6] + s_red[7]);
+  float acc[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; e++) acc[e] = 0.f;
+  for (int s = warp; s < n_used; s += 4) {
+    const float f = sf[s];
+    const float* po = part_o + (base + s) * D + VEC * lane;
+    if constexpr (VEC == 4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(po));
+      acc[0] += f * v.x; acc[1] += f * v.y; acc[2] += f * v.z; acc[3] += f * v.w;
+    } else {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(po));
+      acc[0] += f * v.x; acc[1] += f * v.y;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < VEC; e++) red[(warp * 32 + lane) * VEC + e] = acc[e];
+  __syncthreads();
+  if (warp == 0) {
+    float v[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; e++) {
+      const float t = ((red[lane * VEC + e] + red[(32 + lane) * VEC + e]) + red[(64 + lane) * VEC + e]) +
+                      red[(96 + lane) * VEC + e];
+      v[e] = L > 0.f ? t / L : 0.f;
+    }
+    const int64_t oi = oi0 + VEC * lane;
+    if (out) {
+      if constexpr (VEC == 4) *reinterpret_cast<float4*>(out + oi) = make_float4(v[0], v[1], v[2], v[3]);
+      else *reinterpret_cast<float2*>(out + oi) = make_float2(v[0], v[1]);
+    }
+    if (qx) {   // int8 per 32 elements with (scale, sum of the dequantized block), as warp_quant_store
+      float amax = 0.f;
+#pragma unroll
+      for (int e = 0; e < VEC; e++) amax = fmaxf(amax, fabsf(v[e]));
+#pragma unroll
+      for (int o = GL / 2; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float d = amax / 127.f;
+      float qs = 0.f;
+      uint32_t packed = 0;
+#pragma unroll
+      for (int e = 0; e < VEC; e++) {
+        const float q = d > 0.f ? rintf(v[e] / d) : 0.f;
+        qs += q;
+        packed |= ((uint32_t)(int)q & 0xffu) << (8 * e);
+      }
+#pragma unroll
+      for (int o = GL / 2; o; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+      if constexpr (VEC == 4) *reinterpret_cast<uint32_t*>(qx + oi) = packed;
+      else *reinterpret_cast<uint16_t*>(qx + oi) = (uint16_t)packed;
+      if ((lane & (GL - 1)) == 0) ds[oi >> 5] = make_float2(d, qs * d);
+    }
+  }
+  __syncthreads();   // sf / red / s_red are reused by the next head
+}
+
 // pages in flight per warp (ring depth).  Two pages (68 KB of shared memory at head dim 128) let
 // three CTAs share an SM; three pages (102 KB) only two.  At 5 sequences x 4 KV heads x 16 splits
 // (320 CTAs on 148 SMs) the deeper ring measured 28.0 us against 21.3 us for two.
@@ -287,25 +387,16 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   __syncthreads();
   if (s_ticket != n_split - 1) return;
   __threadfence();
-  for (int r = warp; r < G; r += 4) {
-    const int h = kvh * G + r;
-    const int64_t base = ((int64_t)b * H + h) * n_split;
-    float mstar = NEG_INF;
-    for (int s = 0; s < n_split; s++) mstar = fmaxf(mstar, __ldcg(&part_ml[base + s].x));
-    const float mb = mstar == NEG_INF ? 0.f : mstar;
-    for (int d0 = 0; d0 < D; d0 += 32) {
-      const int dd = d0 + lane;
-      float L = 0.f, acc = 0.f;
-      for (int s = 0; s < n_split; s++) {
-        const float2 ml = __ldcg(&part_ml[base + s]);
-        const float f = exp2f(ml.x - mb);
-        L += f * ml.y;
-        acc += f * __ldcg(&part_o[(base + s) * D + dd]);
-      }
-      const float v = L > 0.f ? acc / L : 0.f;
-      const int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
-      if (out) out[oi] = v;
-      if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), lane);
+  {
+    // the page ring is drained: its shared memory holds the merge scratch
+    float* sf = reinterpret_cast<float*>(smem_raw);
+    float* red = sf + kCombineMaxSlots;
+    float* s_red = red + 4 * D;
+    const int n_used = dec_live_splits(ctx, win, skip_pages, n_split, pages_per_split);
+    for (int r = 0; r < G; r++) {
+      const int h = kvh * G + r;
+      combine_head<D>(part_o, part_ml, ((int64_t)b * H + h) * n_split, n_used, out, qx, ds,
+                      (int64_t)b * ldo + (int64_t)h * D, sf, red, s_red);
     }
   }
   if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
@@ -473,45 +564,23 @@ k_decode_attn_prefix(const float* __restrict__ q, const __nv_bfloat16* __restric
   }
 }
 
-// Suffix splits of k_decode_attn that hold pages for a sequence of ctx tokens: the same page range
-// arithmetic as the kernel (window start, pages another kernel covers, pages per split).
-FAK_DEV int dec_live_splits(int ctx, int win, const int* skip_pages, int n_split, int pages_per_split) {
-  const int n_pages = (ctx + PAGE - 1) / PAGE;
-  int lo = win > 0 ? max(0, ctx - win) : 0;
-  if (skip_pages != nullptr) lo = max(lo, min(ctx, *skip_pages * PAGE));
-  const int live = n_pages - lo / PAGE;
-  if (live <= 0) return 0;
-  const int pps = max(pages_per_split, (live + n_split - 1) / n_split);
-  return min(n_split, (live + pps - 1) / pps);
-}
-
 // Merges slots [0, slot0) (cascade prefix splits, all written) and the live suffix splits
 // [slot0, slot0 + live) of each (sequence, head); splits past a sequence's pages wrote nothing.
 template <int D>
-__global__ void __launch_bounds__(D)
+__global__ void __launch_bounds__(128)
 k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int H, int n_slots,
                  float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds, int ldo,
                  const int* __restrict__ ctx_len, int win, const int* __restrict__ skip_pages, int slot0, int n_split,
                  int pages_per_split) {
+  __shared__ float sf[kCombineMaxSlots];
+  __shared__ float red[4 * D];
+  __shared__ float s_red[8];
   pdl_wait();
-  const int b = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
+  const int b = blockIdx.x, h = blockIdx.y;
   const int64_t base = ((int64_t)b * H + h) * n_slots;
   const int n_used = slot0 + dec_live_splits(ctx_len[b], win, skip_pages, n_split, pages_per_split);
-  float mstar = NEG_INF;
-  for (int s = 0; s < n_used; s++) mstar = fmaxf(mstar, part_ml[base + s].x);
-  float mb = mstar == NEG_INF ? 0.f : mstar;
-  float L = 0.f, acc = 0.f;
-  for (int s = 0; s < n_used; s++) {
-    float2 ml = part_ml[base + s];
-    float f = exp2f(ml.x - mb);
-    L += f * ml.y;
-    acc += f * part_o[(base + s) * D + dd];
-  }
+  combine_head<D>(part_o, part_ml, base, n_used, out, qx, ds, (int64_t)b * ldo + (int64_t)h * D, sf, red, s_red);
   pdl_launch_dependents();
-  float v = L > 0.f ? acc / L : 0.f;
-  int64_t oi = (int64_t)b * ldo + (int64_t)h * D + dd;
-  if (out) out[oi] = v;
-  if (qx) warp_quant_store(v, qx + (oi & ~int64_t(31)), ds + (oi >> 5), dd & 31);
 }
 
 // =============================================================================================
@@ -739,6 +808,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   // attended once for the whole batch by k_decode_attn_prefix in prefix_splits extra slots
   const bool cascade = shared_pages.has_value() && prefix_splits > 0 && B * (H / Hkv) <= 64 && window <= 0;
   const int64_t n_slots = n_split + (cascade ? prefix_splits : 0);
+  TORCH_CHECK(n_slots <= kCombineMaxSlots, "decode_attention: at most ", kCombineMaxSlots, " split slots");
   if (cascade)
     TORCH_CHECK(shared_pages->is_cuda() && shared_pages->scalar_type() == torch::kInt32 && shared_pages->numel() >= 1,
                 "decode_attention: shared_pages int32 [1] on the device");
@@ -813,7 +883,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   if (n_slots > 1 && tk == nullptr) {
     cudaLaunchConfig_t c2 = {};
     c2.gridDim = dim3(B, H);
-    c2.blockDim = dim3(D);
+    c2.blockDim = dim3(128);
     c2.stream = stream;
     set_pdl(c2);
     const int* cl = (const int*)ctx_len.data_ptr<int>();
@@ -922,6 +992,9 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
   if (ldo < H * D || ldo % 32 != 0)
     return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: output row stride %d", ldo);
   const int64_t slots = (int64_t)B * H * n_split;
+  if (n_split > kCombineMaxSlots)
+    return noalloc_fail(err, err_len, FAK_NOALLOC_EINVAL, "fak_decode_attention_noalloc: n_split %d above %d", n_split,
+                        kCombineMaxSlots);
   if (n_split > 1 && slots > kNoAllocSlots)
     return noalloc_fail(err, err_len, FAK_NOALLOC_ETOOBIG,
                         "fak_decode_attention_noalloc: B*H*n_split = %lld exceeds the static scratch limit of %lld "
@@ -978,7 +1051,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
   if (n_split > 1) {
     cudaLaunchConfig_t c2 = {};
     c2.gridDim = dim3(B, H);
-    c2.blockDim = dim3(D);
+    c2.blockDim = dim3(128);
     c2.stream = static_cast<cudaStream_t>(stream);
     if (D == 128)
       e = cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,

@@ -36,6 +36,8 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int GEMM_THREADS = 192;
 
 enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2, G_GEGLU = 3, G_RS = 4 };
+// the gated epilogues (8-column interleaved gate / up blocks); G_RS is not one of them
+__host__ __device__ constexpr bool gated(int epi) { return epi == G_SWIGLU || epi == G_GEGLU; }
 
 constexpr int RS_MAX_W = 8;
 struct RsPeers {
@@ -163,7 +165,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       tc::tmem_ld_wait();
       if (row >= M) continue;
       const int col0 = n0 + c;
-      if (epi >= G_SWIGLU) {
+      if (gated(epi)) {
         // columns [col0, col0+8) are gate rows of outputs col0/2 + j, [col0+8, col0+16) the up rows
 #pragma unroll
         for (int j = 0; j < 8; j++) {
@@ -347,7 +349,7 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
         float v[16];
 #pragma unroll
         for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]) + ((bias && col0 + j < N) ? bias[col0 + j] : 0.f);
-        if (epi >= G_SWIGLU) {
+        if (gated(epi)) {
           // columns [col0, col0+8) gate rows of outputs col0/2 + j, [col0+8, col0+16) the up rows
           float o[16];
 #pragma unroll
@@ -466,8 +468,8 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out: [M, *] row-major");
   const int64_t M = a.size(0), N = b.size(0);
   TORCH_CHECK(epi >= 0 && epi <= 3, "gemm: epilogue");
-  TORCH_CHECK(out.size(0) >= M && out.size(1) >= (epi >= G_SWIGLU ? N / 2 : N), "out too small");
-  if (epi >= G_SWIGLU) TORCH_CHECK(N % 16 == 0, "gated epilogues need 8-column interleaved gate/up blocks");
+  TORCH_CHECK(out.size(0) >= M && out.size(1) >= (gated(epi) ? N / 2 : N), "out too small");
+  if (gated(epi)) TORCH_CHECK(N % 16 == 0, "gated epilogues need 8-column interleaved gate/up blocks");
   if (M == 0 || N == 0) return;
   const float* bp = nullptr;
   if (bias.has_value()) {
@@ -540,7 +542,7 @@ void gemm_bf16_ag(int64_t M, torch::Tensor b, torch::Tensor out, torch::Tensor p
   TORCH_CHECK(K % 8 == 0 && shard_off % 16 == 0 && flags_off % 4 == 0, "gemm_bf16_ag: K % 8, offsets");
   TORCH_CHECK(MR >= ((M + BM - 1) / BM + W - 1) / W * BM, "gemm_bf16_ag: MR too small");
   TORCH_CHECK(epi >= 0 && epi <= 3 && out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= M &&
-                  out.size(1) >= (epi >= G_SWIGLU ? N / 2 : N), "gemm_bf16_ag: out");
+                  out.size(1) >= (gated(epi) ? N / 2 : N), "gemm_bf16_ag: out");
   if (M == 0 || N == 0) return;
   const float* bp = nullptr;
   if (bias.has_value()) {

@@ -749,9 +749,21 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
           float v[4] = {0.f, 0.f, 0.f, 0.f};
-          for (int s = 0; s < geo.S; s++) {
-            const float4 p =
-                __ldcg(reinterpret_cast<const float4*>(part + ((size_t)s * geo.T + tile) * 128 * NT) + 32 * nt + lane);
+          const float4* src = reinterpret_cast<const float4*>(part + (size_t)tile * 128 * NT) + 32 * nt + lane;
+          const size_t sstride = (size_t)geo.T * 128 * NT / 4;   // float4s between slices
+          int s = 0;
+          // eight slices' partials in flight at once (one L2 round trip per eight), added in order
+          for (; s + 8 <= geo.S; s += 8) {
+            float4 p[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) p[u] = __ldcg(src + (size_t)(s + u) * sstride);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+              v[0] += p[u].x; v[1] += p[u].y; v[2] += p[u].z; v[3] += p[u].w;
+            }
+          }
+          for (; s < geo.S; s++) {
+            const float4 p = __ldcg(src + (size_t)s * sstride);
             v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
           }
           acc[nt][0] = v[0]; acc[nt][1] = v[1]; acc[nt][2] = v[2]; acc[nt][3] = v[3];
