@@ -114,9 +114,10 @@ class ModelConfig:
     def device_gap(self) -> str | None:
         """Why the device engine cannot run this config (None when it can).  Such models run on the
         fp32 reference model (``models.reference.ReferenceModel``)."""
-        if self.attn_sinks or self.attn_out_bias or self.moe_bias or self.router != "softmax_topk" or self.swiglu_alpha:
-            return ("gpt-oss blocks (attention sinks, biased top-k-then-softmax router and experts, clamped OAI "
-                    "gate) have no device kernels")
+        if self.swiglu_alpha and (abs(self.swiglu_alpha - 1.702) > 1e-6 or abs(self.swiglu_limit - 7.0) > 1e-6):
+            return "the device's clamped gate is gpt-oss's (alpha 1.702, limit 7)"
+        if (self.attn_sinks or self.moe_bias or self.swiglu_alpha) and self.head_dim not in (64, 128):
+            return "gpt-oss blocks on the device need head dim 64 or 128"
         if self.linear_layers or self.attn_out_gate or (self.rotary_dim and self.rotary_dim != self.head_dim):
             return "Qwen3.5 hybrid blocks (Gated DeltaNet layers, gated partial-rotary attention) have no device kernels"
         return None

@@ -12,7 +12,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
                       c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window,
-                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits, double scale, double softcap);
+                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits, double scale, double softcap,
+                      c10::optional<torch::Tensor> sinks);
 void kv_move(torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor src_slot, torch::Tensor dst_slot,
              torch::Tensor rot, torch::Tensor cos_n, torch::Tensor sin_n);
 torch::Tensor dsa_index_score(torch::Tensor iq, torch::Tensor ik, torch::Tensor w, int64_t qpos, double scale);
@@ -22,7 +23,8 @@ torch::Tensor dsa_sparse_attend(torch::Tensor q, torch::Tensor k_cache, torch::T
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
                        torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window, double scale,
-                       double softcap);
+                       double softcap,
+                       c10::optional<torch::Tensor> sinks);
 void embed(torch::Tensor table, int64_t qtype, int64_t pitch, int64_t V, int64_t d, torch::Tensor ids,
            c10::optional<torch::Tensor> out_f32, c10::optional<torch::Tensor> out_bf16,
            c10::optional<torch::Tensor> err, double scale);
@@ -54,7 +56,8 @@ void p2p_moe_combine_ar(torch::Tensor peers, torch::Tensor out, torch::Tensor id
                         int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err,
                         int64_t ctas, int64_t spin_limit);
 void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor wr, int64_t k, bool norm_topk,
-               torch::Tensor ids, torch::Tensor wts);
+               torch::Tensor ids, torch::Tensor wts,
+               c10::optional<torch::Tensor> rbias, int64_t kind);
 void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_t max_chunks, torch::Tensor chunk_expert,
                torch::Tensor chunk_pairs, torch::Tensor n_chunks);
 void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<torch::Tensor> qx,
@@ -67,7 +70,8 @@ std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_
 int64_t tgemv_unit_bytes(int64_t qtype);
 void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, torch::Tensor qx,
                torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
-               torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err);
+               torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err,
+               c10::optional<torch::Tensor> bias);
 void moe_qmmv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, int64_t pitch, torch::Tensor qx,
               torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
               torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err);
@@ -115,12 +119,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("workspace"), pybind11::arg("ldo") = 0, pybind11::arg("tickets") = pybind11::none(),
         pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("window") = 0,
         pybind11::arg("shared_pages") = pybind11::none(), pybind11::arg("prefix_splits") = 0,
-        pybind11::arg("scale") = 0.0, pybind11::arg("softcap") = 0.0);
+        pybind11::arg("scale") = 0.0, pybind11::arg("softcap") = 0.0, pybind11::arg("sinks") = pybind11::none());
   m.def("prefill_attention", &prefill_attention, pybind11::arg("q"), pybind11::arg("k_cache"),
         pybind11::arg("v_cache"), pybind11::arg("block_table"), pybind11::arg("tile_seq"), pybind11::arg("tile_q0"),
         pybind11::arg("seq_qoff"), pybind11::arg("seq_qlen"), pybind11::arg("seq_pos0"), pybind11::arg("n_tiles"),
         pybind11::arg("out"), pybind11::arg("window") = 0, pybind11::arg("scale") = 0.0,
-        pybind11::arg("softcap") = 0.0);
+        pybind11::arg("softcap") = 0.0, pybind11::arg("sinks") = pybind11::none());
   m.def("embed", &embed, pybind11::arg("table"), pybind11::arg("qtype"), pybind11::arg("pitch"), pybind11::arg("V"),
         pybind11::arg("d"), pybind11::arg("ids"), pybind11::arg("out_f32"), pybind11::arg("out_bf16"),
         pybind11::arg("err"), pybind11::arg("scale") = 1.0);
@@ -147,7 +151,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("flags_off"), pybind11::arg("site"), pybind11::arg("me"), pybind11::arg("counters"),
         pybind11::arg("err"), pybind11::arg("spin_limit") = 0);
   m.def("p2p_moe_combine_ar", &p2p_moe_combine_ar, "MoE combine fused with the expert-parallel all-reduce");
-  m.def("moe_route", &moe_route);
+  m.def("moe_route", &moe_route, pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
+        pybind11::arg("wr"), pybind11::arg("k"), pybind11::arg("norm_topk"), pybind11::arg("ids"),
+        pybind11::arg("wts"), pybind11::arg("rbias") = pybind11::none(), pybind11::arg("kind") = 0);
   m.def("moe_group", &moe_group);
   m.def("moe_qmmv", &moe_qmmv);
   m.def("moe_combine", &moe_combine);
@@ -167,7 +173,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("unit") = false);
   m.def("tgemv_workspace", &tgemv_workspace);
   m.def("tgemv_unit_bytes", &tgemv_unit_bytes);
-  m.def("moe_tgemv", &moe_tgemv);
+  m.def("moe_tgemv", &moe_tgemv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("rows_per_expert"),
+        pybind11::arg("K"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("topk"),
+        pybind11::arg("act_by_token"), pybind11::arg("chunk_expert"), pybind11::arg("chunk_pairs"),
+        pybind11::arg("n_chunks"), pybind11::arg("max_chunks"), pybind11::arg("y"), pybind11::arg("epi"),
+        pybind11::arg("err"), pybind11::arg("bias") = pybind11::none());
   m.def("decode_advance", &decode_advance, "next step's lane inputs from this step's tokens (device-resident state)");
   m.def("scatter_i32", &scatter_i32, "dst.flatten()[idx] = val for (idx, val) pairs on the device");
   m.def("ipc_alloc", &ipc_alloc, "zeroed device buffer + its CUDA IPC handle");

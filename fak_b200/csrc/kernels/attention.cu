@@ -83,11 +83,12 @@ constexpr int kCombineMaxSlots = 384;   // 256 suffix splits + 128 cascade prefi
 // warp accumulates the splits s = warp (mod 4) with D/32 dims per lane and the four warps' sums
 // are added in warp order.  Used by k_decode_combine and by the in-kernel merge (tickets), which
 // therefore give the same bits.  Output: fp32 out and/or int8 codes with (scale, sum) per 32.
+// sink2: the head's attention-sink logit in log2 units (-inf: none).
 // smem: sf [kCombineMaxSlots], red [4 * D], s_red [8] floats.
 template <int D>
 FAK_DEV void combine_head(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int64_t base,
                           int n_used, float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds,
-                          int64_t oi0, float* sf, float* red, float* s_red) {
+                          int64_t oi0, float* sf, float* red, float* s_red, float sink2) {
   constexpr int VEC = D / 32;   // dims per lane
   constexpr int GL = 32 / VEC;  // lanes per 32-element quantization block
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -96,7 +97,8 @@ FAK_DEV void combine_head(const float* __restrict__ part_o, const float2* __rest
   mloc = warp_max(mloc);
   if (lane == 0) s_red[warp] = mloc;
   __syncthreads();
-  const float mstar = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+  // an attention sink (sink2 > -inf, log2 units) is one more logit of the softmax with no value
+  const float mstar = fmaxf(fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3])), sink2);
   const float mb = mstar == NEG_INF ? 0.f : mstar;
   float lloc = 0.f;
   for (int s = tid; s < n_used; s += 128) {
@@ -108,7 +110,7 @@ FAK_DEV void combine_head(const float* __restrict__ part_o, const float2* __rest
   lloc = warp_sum(lloc);
   if (lane == 0) s_red[4 + warp] = lloc;
   __syncthreads();
-  const float L = (s_red[4] + s_red[5]) + (s_red[6] + s_red[7]);
+  const float L = (s_red[4] + s_red[5]) + (s_red[6] + s_red[7]) + (sink2 > NEG_INF ? exp2f(sink2 - mb) : 0.f);
   float acc[VEC];
 #pragma unroll
   for (int e = 0; e < VEC; e++) acc[e] = 0.f;
@@ -182,7 +184,7 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
               float2* __restrict__ part_ml, float* __restrict__ out, int8_t* __restrict__ qx,
               float2* __restrict__ ds, int ldo, int* __restrict__ tickets, const uint8_t* __restrict__ pf,
               int64_t pf_bytes, int win, const int* __restrict__ skip_pages, int slot0, int n_slots, float cap_in,
-              float cap_out) {
+              float cap_out, const float* __restrict__ sinks) {
   constexpr int KS = D / 16;   // k-steps over the head dim
   constexpr int NT = D / 8;    // n-tiles over the head dim for P.V
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -350,17 +352,20 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   pdl_launch_dependents();
   // each warp finalizes dims [32*warp, 32*warp+32) (D=128) or warps 0-1 (D=64) for every head
   for (int r = 0; r < G; r++) {
+    const int h = kvh * G + r;
+    // the attention sink joins the final softmax only (split partials leave it to the combine)
+    const float sk = (n_slots == 1 && sinks != nullptr) ? sinks[h] * 1.4426950408889634f : NEG_INF;
     float mstar = NEG_INF;
 #pragma unroll
     for (int w = 0; w < 4; w++) mstar = fmaxf(mstar, sml[(w * 16 + r) * 2]);
-    float base = mstar == NEG_INF ? 0.f : mstar;
-    float L = 0.f, f[4];
+    const float mtot = fmaxf(mstar, sk);
+    float base = mtot == NEG_INF ? 0.f : mtot;
+    float L = sk > NEG_INF ? exp2f(sk - base) : 0.f, f[4];
 #pragma unroll
     for (int w = 0; w < 4; w++) {
       f[w] = exp2f(sml[(w * 16 + r) * 2] - base);
       L += f[w] * sml[(w * 16 + r) * 2 + 1];
     }
-    const int h = kvh * G + r;
     for (int dd = threadIdx.x; dd < D; dd += 128) {
       float acc = 0.f;
 #pragma unroll
@@ -396,7 +401,8 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
     for (int r = 0; r < G; r++) {
       const int h = kvh * G + r;
       combine_head<D>(part_o, part_ml, ((int64_t)b * H + h) * n_split, n_used, out, qx, ds,
-                      (int64_t)b * ldo + (int64_t)h * D, sf, red, s_red);
+                      (int64_t)b * ldo + (int64_t)h * D, sf, red, s_red,
+                      sinks != nullptr ? sinks[h] * 1.4426950408889634f : NEG_INF);
     }
   }
   if (threadIdx.x == 0) tickets[b * Hkv + kvh] = 0;
@@ -571,7 +577,7 @@ __global__ void __launch_bounds__(128)
 k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml, int H, int n_slots,
                  float* __restrict__ out, int8_t* __restrict__ qx, float2* __restrict__ ds, int ldo,
                  const int* __restrict__ ctx_len, int win, const int* __restrict__ skip_pages, int slot0, int n_split,
-                 int pages_per_split) {
+                 int pages_per_split, const float* __restrict__ sinks) {
   __shared__ float sf[kCombineMaxSlots];
   __shared__ float red[4 * D];
   __shared__ float s_red[8];
@@ -579,7 +585,8 @@ k_decode_combine(const float* __restrict__ part_o, const float2* __restrict__ pa
   const int b = blockIdx.x, h = blockIdx.y;
   const int64_t base = ((int64_t)b * H + h) * n_slots;
   const int n_used = slot0 + dec_live_splits(ctx_len[b], win, skip_pages, n_split, pages_per_split);
-  combine_head<D>(part_o, part_ml, base, n_used, out, qx, ds, (int64_t)b * ldo + (int64_t)h * D, sf, red, s_red);
+  combine_head<D>(part_o, part_ml, base, n_used, out, qx, ds, (int64_t)b * ldo + (int64_t)h * D, sf, red, s_red,
+                  sinks != nullptr ? sinks[h] * 1.4426950408889634f : NEG_INF);
   pdl_launch_dependents();
 }
 
@@ -606,7 +613,8 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
                const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_table, int bt_stride,
                const int* __restrict__ tile_seq, const int* __restrict__ tile_q0, const int* __restrict__ seq_qoff,
                const int* __restrict__ seq_qlen, const int* __restrict__ seq_pos0, int H, int Hkv, float scale_log2,
-               __nv_bfloat16* __restrict__ out, int64_t out_stride, int win, float cap_in, float cap_out) {
+               __nv_bfloat16* __restrict__ out, int64_t out_stride, int win, float cap_in, float cap_out,
+               const float* __restrict__ sinks) {
   constexpr int KS = D / 16;
   constexpr int NT = D / 8;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -751,6 +759,11 @@ k_prefill_attn(const __nv_bfloat16* __restrict__ q, int64_t q_stride, const __nv
   pdl_launch_dependents();
   l0 = quad_sum(l0);
   l1 = quad_sum(l1);
+  if (sinks != nullptr) {   // the head's sink logit joins each row's softmax denominator
+    const float sk = sinks[h] * 1.4426950408889634f;
+    l0 += exp2f(sk - m0);
+    l1 += exp2f(sk - m1);
+  }
   float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
   __nv_bfloat16* op0 = out + (int64_t)(qoff + r0) * out_stride + (int64_t)h * D;
   __nv_bfloat16* op1 = out + (int64_t)(qoff + r1) * out_stride + (int64_t)h * D;
@@ -782,7 +795,14 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> qx,
                       c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> workspace, int64_t ldo,
                       c10::optional<torch::Tensor> tickets, c10::optional<torch::Tensor> prefetch, int64_t window,
-                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits, double scale, double softcap) {
+                      c10::optional<torch::Tensor> shared_pages, int64_t prefix_splits, double scale, double softcap,
+                      c10::optional<torch::Tensor> sinks) {
+  const float* skp = nullptr;   // attention sinks [H] f32 (natural-log logits), optional
+  if (sinks.has_value()) {
+    TORCH_CHECK(sinks->is_cuda() && sinks->scalar_type() == torch::kFloat32 && sinks->numel() >= q.size(1),
+                "decode_attention: sinks [H] f32");
+    skp = sinks->data_ptr<float>();
+  }
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
   const int64_t pfb = prefetch.has_value() ? prefetch->numel() * prefetch->element_size() : 0;
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kFloat32 && q.dim() == 3 && q.is_contiguous(), "q [B,H,D] f32");
@@ -870,7 +890,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
                                       (const __nv_bfloat16*)k_cache.data_ptr(), (const __nv_bfloat16*)v_cache.data_ptr(),
                                       (const int*)block_table.data_ptr<int>(), bts, (const int*)ctx_len.data_ptr<int>(),
                                       H, Hkv, (int)n_split, (int)pages_per_split, scale_log2, pw, pml, op, qp, dp, (int)ldo, tk,
-                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots, cap_in, cap_out));
+                                      pfp, pfb, (int)window, skip, slot0, (int)n_slots, cap_in, cap_out, skp));
   };
   const size_t merge128 = (size_t)(4 * 16 * 128 + 4 * 16 * 2) * 4, merge64 = (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4;
   if (D == 128) {
@@ -890,11 +910,11 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
     if (D == 128)
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H,
                                         (int)n_slots, op, qp, dp, (int)ldo, cl, (int)window, skip, slot0, (int)n_split,
-                                        (int)pages_per_split));
+                                        (int)pages_per_split, skp));
     else
       FAK_CUDA_CHECK(cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H,
                                         (int)n_slots, op, qp, dp, (int)ldo, cl, (int)window, skip, slot0, (int)n_split,
-                                        (int)pages_per_split));
+                                        (int)pages_per_split, skp));
   }
 }
 
@@ -903,8 +923,14 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
 void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                        torch::Tensor tile_seq, torch::Tensor tile_q0, torch::Tensor seq_qoff, torch::Tensor seq_qlen,
                        torch::Tensor seq_pos0, int64_t n_tiles, torch::Tensor out, int64_t window, double scale,
-                       double softcap) {
+                       double softcap, c10::optional<torch::Tensor> sinks) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.stride(2) == 1, "q [T,H,D] bf16");
+  const float* skp = nullptr;   // attention sinks [H] f32 (natural-log logits), optional
+  if (sinks.has_value()) {
+    TORCH_CHECK(sinks->is_cuda() && sinks->scalar_type() == torch::kFloat32 && sinks->numel() >= q.size(1),
+                "prefill_attention: sinks [H] f32");
+    skp = sinks->data_ptr<float>();
+  }
   TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 && k_cache.dim() == 4 && k_cache.is_contiguous(), "k_cache");
   int H = (int)q.size(1), D = (int)q.size(2), Hkv = (int)k_cache.size(1);
   TORCH_CHECK(q.stride(1) == D, "q heads must be contiguous");
@@ -931,7 +957,7 @@ void prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
         (const __nv_bfloat16*)v_cache.data_ptr(), (const int*)block_table.data_ptr<int>(), (int)block_table.stride(0),
         (const int*)tile_seq.data_ptr<int>(), (const int*)tile_q0.data_ptr<int>(), (const int*)seq_qoff.data_ptr<int>(),
         (const int*)seq_qlen.data_ptr<int>(), (const int*)seq_pos0.data_ptr<int>(), H, Hkv, scale_log2,
-        (__nv_bfloat16*)out.data_ptr(), (int64_t)out.stride(0), (int)window, cap_in, cap_out));
+        (__nv_bfloat16*)out.data_ptr(), (int64_t)out.stride(0), (int)window, cap_in, cap_out, skp));
   };
   const bool cap = cap_out > 0.f, wn = window > 0;
 #define FAK_PF(DV)                                                                              \
@@ -1037,7 +1063,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<128>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
                              pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0,
-                             nullptr, 0, n_split, 0.f, 0.f);
+                             nullptr, 0, n_split, 0.f, 0.f, (const float*)nullptr);
   } else {
     size_t smem = std::max(sizeof(DecodeSmem<64>), (size_t)(4 * 16 * 64 + 4 * 16 * 2) * 4);
     cfg.dynamicSmemBytes = smem;
@@ -1045,7 +1071,7 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     if (e == cudaSuccess)
       e = cudaLaunchKernelEx(&cfg, k_decode_attn<64>, q, kc, vc, block_table, bt_stride, ctx_len, H, Hkv, n_split,
                              pages_per_split, scale_log2, pw, pml, out, qx, dp, ldo, nullptr, nullptr, 0, 0,
-                             nullptr, 0, n_split, 0.f, 0.f);
+                             nullptr, 0, n_split, 0.f, 0.f, (const float*)nullptr);
   }
   if (e != cudaSuccess) return noalloc_fail(err, err_len, FAK_NOALLOC_ECUDA, "decode attention launch: %s", cudaGetErrorString(e));
   if (n_split > 1) {
@@ -1055,10 +1081,12 @@ extern "C" __attribute__((visibility("default"))) int fak_decode_attention_noall
     c2.stream = static_cast<cudaStream_t>(stream);
     if (D == 128)
       e = cudaLaunchKernelEx(&c2, k_decode_combine<128>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
-                             dp, ldo, ctx_len, 0, (const int*)nullptr, 0, n_split, pages_per_split);
+                             dp, ldo, ctx_len, 0, (const int*)nullptr, 0, n_split, pages_per_split,
+                             (const float*)nullptr);
     else
       e = cudaLaunchKernelEx(&c2, k_decode_combine<64>, (const float*)pw, (const float2*)pml, H, n_split, out, qx,
-                             dp, ldo, ctx_len, 0, (const int*)nullptr, 0, n_split, pages_per_split);
+                             dp, ldo, ctx_len, 0, (const int*)nullptr, 0, n_split, pages_per_split,
+                             (const float*)nullptr);
     if (e != cudaSuccess) return noalloc_fail(err, err_len, FAK_NOALLOC_ECUDA, "decode combine launch: %s", cudaGetErrorString(e));
   }
   return FAK_NOALLOC_OK;

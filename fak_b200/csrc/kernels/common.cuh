@@ -84,6 +84,18 @@ FAK_DEV float gelu_tanh(float x) { return 0.5f * x * (1.0f + tanhf(0.79788456080
 // gated-FFN activation of the fused gate/up epilogues: 2 = SiLU (SwiGLU), 3 = GELU-tanh (GEGLU)
 FAK_DEV float gated_act(int epi, float g) { return epi == 3 ? gelu_tanh(g) : silu(g); }
 
+// Gated FFN output from a gate value g and an up value u.  epi: 2 SwiGLU, 3 GeGLU (GELU-tanh),
+// 4 the gpt-oss clamped gate: (clamp(u, -7, 7) + 1) * g' * sigmoid(1.702 g') with g' = min(g, 7)
+// (alpha 1.702 and limit 7 are the family's fixed constants; the loader refuses other values).
+FAK_DEV float gated_out(int epi, float g, float u) {
+  if (epi == 4) {
+    g = fminf(g, 7.f);
+    u = fminf(fmaxf(u, -7.f), 7.f);
+    return (u + 1.f) * g / (1.f + expf(-1.702f * g));
+  }
+  return gated_act(epi, g) * u;
+}
+
 FAK_DEV float bf16_bits_lo(uint32_t v) { return __uint_as_float(v << 16); }
 FAK_DEV float bf16_bits_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 

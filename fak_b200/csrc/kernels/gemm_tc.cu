@@ -35,9 +35,11 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int GEMM_THREADS = 192;
 
-enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2, G_GEGLU = 3, G_RS = 4 };
+enum GemmEpi : int { G_STORE = 0, G_ADD = 1, G_SWIGLU = 2, G_GEGLU = 3, G_RS = 4, G_OAI = 5 };
 // the gated epilogues (8-column interleaved gate / up blocks); G_RS is not one of them
-__host__ __device__ constexpr bool gated(int epi) { return epi == G_SWIGLU || epi == G_GEGLU; }
+__host__ __device__ constexpr bool gated(int epi) { return epi == G_SWIGLU || epi == G_GEGLU || epi == G_OAI; }
+// gated_out's code for a gated GEMM epilogue (the gpt-oss gate is 4 there)
+__device__ __forceinline__ int gate_code(int epi) { return epi == G_OAI ? 4 : epi; }
 
 constexpr int RS_MAX_W = 8;
 struct RsPeers {
@@ -173,7 +175,7 @@ k_gemm_bf16(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           if (col + 8 < N) {
             float g = __uint_as_float(r[j]), u = __uint_as_float(r[j + 8]);
             if (bias) { g += bias[col]; u += bias[col + 8]; }
-            store_val(out + (int64_t)row * ldo + (col0 >> 1) + j, gated_act(epi, g) * u);
+            store_val(out + (int64_t)row * ldo + (col0 >> 1) + j, gated_out(gate_code(epi), g, u));
           }
         }
       } else {
@@ -353,7 +355,7 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
           // columns [col0, col0+8) gate rows of outputs col0/2 + j, [col0+8, col0+16) the up rows
           float o[16];
 #pragma unroll
-          for (int j = 0; j < 8; j++) o[j] = gated_act(epi, v[j]) * v[j + 8];
+          for (int j = 0; j < 8; j++) o[j] = gated_out(gate_code(epi), v[j], v[j + 8]);
           OutT* p = out + (int64_t)row * ldo + (col0 >> 1);
           if (col0 + 16 <= N && std::is_same<OutT, float>::value && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
             float* pf = reinterpret_cast<float*>(p);
@@ -467,7 +469,9 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
               "operands must be 16-byte aligned");
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out: [M, *] row-major");
   const int64_t M = a.size(0), N = b.size(0);
-  TORCH_CHECK(epi >= 0 && epi <= 3, "gemm: epilogue");
+  // epilogue codes as the GEMVs use them (4: the gpt-oss clamped gate, G_OAI here)
+  TORCH_CHECK(epi >= 0 && epi <= 4, "gemm: epilogue");
+  if (epi == 4) epi = G_OAI;
   TORCH_CHECK(out.size(0) >= M && out.size(1) >= (gated(epi) ? N / 2 : N), "out too small");
   if (gated(epi)) TORCH_CHECK(N % 16 == 0, "gated epilogues need 8-column interleaved gate/up blocks");
   if (M == 0 || N == 0) return;
@@ -541,7 +545,8 @@ void gemm_bf16_ag(int64_t M, torch::Tensor b, torch::Tensor out, torch::Tensor p
   const int64_t N = b.size(0), K = b.size(1);
   TORCH_CHECK(K % 8 == 0 && shard_off % 16 == 0 && flags_off % 4 == 0, "gemm_bf16_ag: K % 8, offsets");
   TORCH_CHECK(MR >= ((M + BM - 1) / BM + W - 1) / W * BM, "gemm_bf16_ag: MR too small");
-  TORCH_CHECK(epi >= 0 && epi <= 3 && out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= M &&
+  if (epi == 4) epi = G_OAI;
+  TORCH_CHECK((epi >= 0 && epi <= 3 || epi == G_OAI) && out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= M &&
                   out.size(1) >= (gated(epi) ? N / 2 : N), "gemm_bf16_ag: out");
   if (M == 0 || N == 0) return;
   const float* bp = nullptr;

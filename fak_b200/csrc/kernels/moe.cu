@@ -28,9 +28,11 @@ constexpr int CH = 8;      // pairs per chunk (MMA N)
 // routing: one CTA per token.  x fp32 residual row -> RMSNorm(gamma) -> logits = W_r x (fp32) ->
 // softmax -> top-k -> renorm.  Writes ids [T, k] and weights [T, k].
 // ---------------------------------------------------------------------------------------------
+// kind 0: softmax over every expert, then the top k (renormalised with norm_topk); kind 1 (gpt-oss):
+// the top k logits, then a softmax over those k.  rbias (optional) is added to the logits first.
 __global__ void k_moe_route(const float* __restrict__ x, int64_t ldx, const float* __restrict__ gamma, float eps,
                             const float* __restrict__ wr, int E, int d, int k, int norm_topk, int* __restrict__ ids,
-                            float* __restrict__ wts) {
+                            float* __restrict__ wts, const float* __restrict__ rbias, int kind) {
   pdl_wait();
   extern __shared__ float rsm[];  // [d] normalized x | [E] logits
   float* xs = rsm;
@@ -58,10 +60,30 @@ __global__ void k_moe_route(const float* __restrict__ x, int64_t ldx, const floa
     float acc = 0.f;
     for (int i = lane; i < d; i += 32) acc += w[i] * xs[i];
     acc = warp_sum(acc);
-    if (lane == 0) lg[e] = acc;
+    if (lane == 0) lg[e] = acc + (rbias ? rbias[e] : 0.f);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && kind == 1) {
+    float sel_v[MAX_K];
+    int sel_i[MAX_K];
+    for (int j = 0; j < k; j++) {  // top-k logits in descending order, first index wins ties
+      int bi = -1;
+      float bv = -INFINITY;
+      for (int e = 0; e < E; e++) {
+        if (bi < 0 || lg[e] > bv) { bv = lg[e]; bi = e; }
+      }
+      sel_i[j] = bi;
+      sel_v[j] = bv;
+      lg[bi] = -INFINITY;   // chosen: never picked again
+    }
+    float s = 0.f;
+    for (int j = 0; j < k; j++) s += __expf(sel_v[j] - sel_v[0]);
+    for (int j = 0; j < k; j++) {
+      ids[(int64_t)t * k + j] = sel_i[j];
+      wts[(int64_t)t * k + j] = __expf(sel_v[j] - sel_v[0]) / s;
+    }
+  }
+  if (threadIdx.x == 0 && kind == 0) {
     float mx = -INFINITY;
     for (int e = 0; e < E; e++) mx = fmaxf(mx, lg[e]);
     float s = 0.f;
@@ -288,7 +310,13 @@ cudaLaunchConfig_t cfg_pdl(dim3 g, dim3 b, size_t smem, cudaLaunchAttribute* att
 }  // namespace
 
 void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor wr, int64_t k, bool norm_topk,
-               torch::Tensor ids, torch::Tensor wts) {
+               torch::Tensor ids, torch::Tensor wts, c10::optional<torch::Tensor> rbias, int64_t kind) {
+  TORCH_CHECK(kind == 0 || kind == 1, "route: kind 0 (softmax, top-k) or 1 (top-k, softmax)");
+  const float* rb = nullptr;
+  if (rbias.has_value()) {
+    TORCH_CHECK(rbias->scalar_type() == torch::kFloat32 && rbias->numel() >= wr.size(0), "route: bias [E] f32");
+    rb = rbias->data_ptr<float>();
+  }
   const int T = (int)x.size(0), d = (int)x.size(1), E = (int)wr.size(0);
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.stride(1) == 1 && wr.size(1) == d && wr.is_contiguous(), "route");
   TORCH_CHECK(k >= 1 && k <= MAX_K && k <= E, "top-k");
@@ -299,7 +327,8 @@ void moe_route(torch::Tensor x, torch::Tensor gamma, double eps, torch::Tensor w
   FAK_CUDA_CHECK(cudaFuncSetAttribute(k_moe_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_moe_route, (const float*)x.data_ptr<float>(), (int64_t)x.stride(0),
                                     (const float*)gamma.data_ptr<float>(), (float)eps, (const float*)wr.data_ptr<float>(),
-                                    E, d, (int)k, (int)norm_topk, ids.data_ptr<int>(), wts.data_ptr<float>()));
+                                    E, d, (int)k, (int)norm_topk, ids.data_ptr<int>(), wts.data_ptr<float>(), rb,
+                                    (int)kind));
 }
 
 void moe_group(torch::Tensor ids, int64_t P, int64_t e0, int64_t E_local, int64_t max_chunks, torch::Tensor chunk_expert,

@@ -164,18 +164,39 @@ __global__ void k_p2p_rs_reduce(Peers P, int64_t parts_off, int64_t flags_off, i
                    epoch, P.spin, err);
     __syncthreads();
     const int rows = min(RS_BM, M - mb * RS_BM), cols4 = min(RS_BN, N - nb * RS_BN) >> 2;
-    for (int e = threadIdx.x; e < rows * cols4; e += blockDim.x) {
-      const int rr = e / cols4, c = nb * RS_BN + 4 * (e - rr * cols4);
-      const int64_t xi = x_local ? (int64_t)(k * RS_BM + rr) * N + c : (int64_t)(mb * RS_BM + rr) * N + c;
-      float4 acc = *reinterpret_cast<const float4*>((x_local ? x_local : xl) + xi);
-      for (int r = 0; r < W; r++) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(parts + ((int64_t)r * MR + k * RS_BM + rr) * N + c));
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    const int n4 = rows * cols4;
+    // four float4 per thread in flight: the residual and every rank's partial of each are loaded
+    // before any is added (same addition order per element)
+    for (int e0 = threadIdx.x; e0 < n4; e0 += 4 * blockDim.x) {
+      float4 acc[4];
+      int64_t xi[4], pi[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int e = min(e0 + u * (int)blockDim.x, n4 - 1);   // tail lanes repeat the last element
+        const int rr = e / cols4, c = nb * RS_BN + 4 * (e - rr * cols4);
+        xi[u] = x_local ? (int64_t)(k * RS_BM + rr) * N + c : (int64_t)(mb * RS_BM + rr) * N + c;
+        pi[u] = (int64_t)(k * RS_BM + rr) * N + c;
+        acc[u] = *reinterpret_cast<const float4*>((x_local ? x_local : xl) + xi[u]);
       }
-      if (x_local)
-        *reinterpret_cast<float4*>(x_local + xi) = acc;
-      else
-        for (int r = 0; r < W; r++) *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.base[r] + x_off) + xi) = acc;
+      for (int r = 0; r < W; r++) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          v[u] = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)r * MR * N + pi[u]));
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        if (e0 + u * (int)blockDim.x >= n4) break;
+        if (x_local)
+          *reinterpret_cast<float4*>(x_local + xi[u]) = acc[u];
+        else
+          for (int r = 0; r < W; r++)
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(P.base[r] + x_off) + xi[u]) = acc[u];
+      }
     }
     __syncthreads();
   }
@@ -415,7 +436,7 @@ void p2p_rs_reduce(torch::Tensor peers, int64_t parts_off, int64_t flags_off, in
   if (M == 0) return;
   Peers P = make_peers(peers, spin_limit);
   cudaLaunchAttribute attr[1];
-  auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
+  auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(1024), attr);
   float* xl = nullptr;
   if (x_local.has_value()) {
     TORCH_CHECK(x_local->is_cuda() && x_local->scalar_type() == torch::kFloat32 && x_local->is_contiguous() &&

@@ -45,7 +45,7 @@ using namespace fak;
 
 namespace {
 
-enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_GEGLU = 3 };
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_GEGLU = 3, EPI_OAI = 4 };
 constexpr int MAXNT = 4;  // n8 token tiles per launch: up to 32 tokens
 constexpr int MAGIC_I = 0x4B400000;
 constexpr float MAGIC_F = 12582912.0f;
@@ -433,8 +433,8 @@ FAK_DEV void epilogue(int tile, const float (&v)[4], int tokb, int lane, int N, 
     if (rowb < N) {
       const int o = (r0 >> 1) + g;
       const float bg = bias ? bias[rowa] : 0.f, bu = bias ? bias[rowb] : 0.f;
-      if (tok0 < B) y[(int64_t)tok0 * ldy + o] = gated_act(epi, v[0] + bg) * (v[2] + bu);
-      if (tok1 < B) y[(int64_t)tok1 * ldy + o] = gated_act(epi, v[1] + bg) * (v[3] + bu);
+      if (tok0 < B) y[(int64_t)tok0 * ldy + o] = gated_out(epi, v[0] + bg, v[2] + bu);
+      if (tok1 < B) y[(int64_t)tok1 * ldy + o] = gated_out(epi, v[1] + bg, v[3] + bu);
     }
     return;
   }
@@ -486,46 +486,71 @@ FAK_DEV uint32_t ar_ld_acquire(const uint32_t* p) {
   return v;
 }
 
+// A warp's pushes are not fenced one tile at a time: it pushes the final partial of every tile it
+// completes (ar_push, plain stores into slot [parity][me][tile] of every rank), and after its last
+// tile (or after AR_PEND tiles) ar_finish issues ONE system-scope fence, releases the flags of all
+// those tiles on every rank, and only then waits for the other ranks' flags tile by tile, so the
+// NVLink round trips of a warp's tiles overlap instead of adding up.
+constexpr int AR_PEND = 8;
+
 template <int NT>
-FAK_DEV void ar_tile(const ArPeers& ar, int T, int tile, int lane, float (&v)[NT][4], int* err) {
+FAK_DEV uint32_t ar_push(const ArPeers& ar, int T, int tile, int lane, const float (&v)[NT][4]) {
   uint32_t ep = 0;
   if (lane == 0) ep = ar.epochs[tile] + 1;
   ep = __shfl_sync(0xffffffffu, ep, 0);
   // the half of the slots this epoch uses: [AR_MAX_W][T][<= 4 n8 tiles][32 lanes] float4 each
   const int64_t half = (int64_t)(ep & 1u) * AR_MAX_W * T * 4 * 32;
-  // push this rank's partial of the tile to every rank
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
     const float4 val = make_float4(v[nt][0], v[nt][1], v[nt][2], v[nt][3]);
     const int64_t slot = half + (((int64_t)ar.me * T + tile) * NT + nt) * 32 + lane;
     for (int r = 0; r < ar.W; r++) reinterpret_cast<float4*>(ar.base[r] + ar.parts_off)[slot] = val;
   }
+  return ep;
+}
+
+template <int NT>
+FAK_DEV void ar_finish(const ArPeers& ar, int T, const int (&pend)[AR_PEND], const uint32_t (&peps)[AR_PEND], int np,
+                       int lane, int N, int B, float* __restrict__ y, int64_t ldy, const float* __restrict__ bias,
+                       int epi, int* err) {
   __syncwarp();
   if (lane < ar.W) {
-    __threadfence_system();
-    ar_st_release(reinterpret_cast<uint32_t*>(ar.base[lane] + ar.flags_off) + (int64_t)tile * AR_MAX_W + ar.me, ep);
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(ar.base[ar.me] + ar.flags_off) +
-                           (int64_t)tile * AR_MAX_W + lane;
-    uint32_t i = 0;
-    while (ar_ld_acquire(mine) < ep) {
-      if (++i > ar.spin) {
-        report_error(err, 4);
-        break;
+    __threadfence_system();   // every lane's pushes (ordered by the warp barrier) before the flags
+    uint32_t* flags = reinterpret_cast<uint32_t*>(ar.base[lane] + ar.flags_off);
+#pragma unroll
+    for (int i = 0; i < AR_PEND; i++)
+      if (i < np) ar_st_release(flags + (int64_t)pend[i] * AR_MAX_W + ar.me, peps[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < AR_PEND; i++) {
+    if (i >= np) break;
+    const int tile = pend[i];
+    const uint32_t ep = peps[i];
+    if (lane < ar.W) {
+      const uint32_t* mine = reinterpret_cast<const uint32_t*>(ar.base[ar.me] + ar.flags_off) +
+                             (int64_t)tile * AR_MAX_W + lane;
+      uint32_t it = 0;
+      while (ar_ld_acquire(mine) < ep) {
+        if (++it > ar.spin) {
+          report_error(err, 4);
+          break;
+        }
       }
     }
-  }
-  __syncwarp();
+    __syncwarp();
+    const int64_t half = (int64_t)(ep & 1u) * AR_MAX_W * T * 4 * 32;
 #pragma unroll
-  for (int nt = 0; nt < NT; nt++) {
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < ar.W; r++) {
-      const int64_t slot = half + (((int64_t)r * T + tile) * NT + nt) * 32 + lane;
-      const float4 p = __ldcg(reinterpret_cast<const float4*>(ar.base[ar.me] + ar.parts_off) + slot);
-      s[0] += p.x; s[1] += p.y; s[2] += p.z; s[3] += p.w;
+    for (int nt = 0; nt < NT; nt++) {
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < ar.W; r++) {
+        const int64_t slot = half + (((int64_t)r * T + tile) * NT + nt) * 32 + lane;
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(ar.base[ar.me] + ar.parts_off) + slot);
+        v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
+      }
+      epilogue(tile, v, 8 * nt, lane, N, B, y, ldy, bias, epi);
     }
-    v[nt][0] = s[0]; v[nt][1] = s[1]; v[nt][2] = s[2]; v[nt][3] = s[3];
+    if (lane == 0) ar.epochs[tile] = ep;
   }
-  if (lane == 0) ar.epochs[tile] = ep;
 }
 
 template <int QT, int W, int R, int NT, bool US = false>
@@ -713,6 +738,8 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   const int8_t* xg = xs + g * geo.xstride;
   int cslot = 0, ul = 0, tile = wg;
   uint32_t phase = 0;
+  int pend[AR_PEND], npend = 0;   // fused all-reduce: tiles pushed, not yet summed
+  uint32_t peps[AR_PEND];
   for (int q = 0; q < Q; q++) {
     if (lane == 0) issue_next();  // into the slot released at the end of the previous iteration
     tc::mbar_wait(&bar[cslot], phase, err);
@@ -772,14 +799,25 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       }
     }
     if (have) {
-      if (ar.W > 0) ar_tile<NT>(ar, geo.T, tile, lane, acc, err);
+      if (ar.W > 0) {   // fused all-reduce: push now, fence / wait / sum / store in batches
+        const uint32_t ep = ar_push<NT>(ar, geo.T, tile, lane, acc);
 #pragma unroll
-      for (int nt = 0; nt < NT; nt++) epilogue(tile, acc[nt], 8 * nt, lane, N, B, y, ldy, bias, epi);
+        for (int i = 0; i < AR_PEND; i++)
+          if (i == npend) { pend[i] = tile; peps[i] = ep; }
+        if (++npend == AR_PEND) {
+          ar_finish<NT>(ar, geo.T, pend, peps, npend, lane, N, B, y, ldy, bias, epi, err);
+          npend = 0;
+        }
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) epilogue(tile, acc[nt], 8 * nt, lane, N, B, y, ldy, bias, epi);
+      }
     }
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     tile += wstride;
   }
+  if (npend > 0) ar_finish<NT>(ar, geo.T, pend, peps, npend, lane, N, B, y, ldy, bias, epi, err);
   pdl_launch_dependents();
 }
 
@@ -794,7 +832,7 @@ __global__ void __launch_bounds__(W * 32, 1)
 k_tgemv_moe(const uint8_t* __restrict__ Wt, int Te, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
             int topk, int act_by_token, const int* __restrict__ chunk_expert, const int* __restrict__ chunk_pairs,
             const int* __restrict__ n_chunks, float* __restrict__ y, int64_t ldy, int epi, int* __restrict__ err,
-            TGeo geo) {
+            TGeo geo, const float* __restrict__ bias) {
   constexpr int UT = Tile<QT>::UT;
   constexpr int TABF = Tile<QT>::TABF;
   constexpr int MB = 8;
@@ -894,18 +932,21 @@ k_tgemv_moe(const uint8_t* __restrict__ Wt, int Te, int K, const int8_t* __restr
     ul = 0;
     const int r0 = tile * 16;
     const int p0 = pr[2 * t], p1 = pr[2 * t + 1];
+    // per-expert bias (rows of this expert, in the same interleaved order as its weight rows)
+    const float* eb = bias ? bias + (int64_t)e * Te * 16 : nullptr;
+    const float ba = eb ? eb[r0 + g] : 0.f, bb = eb ? eb[r0 + g + 8] : 0.f;
     if (epi >= EPI_SWIGLU) {
       const int o = (r0 >> 1) + g;
-      if (p0 >= 0) y[(int64_t)p0 * ldy + o] = gated_act(epi, acc[0][0]) * acc[0][2];
-      if (p1 >= 0) y[(int64_t)p1 * ldy + o] = gated_act(epi, acc[0][1]) * acc[0][3];
+      if (p0 >= 0) y[(int64_t)p0 * ldy + o] = gated_out(epi, acc[0][0] + ba, acc[0][2] + bb);
+      if (p1 >= 0) y[(int64_t)p1 * ldy + o] = gated_out(epi, acc[0][1] + ba, acc[0][3] + bb);
     } else {
       if (p0 >= 0) {
-        y[(int64_t)p0 * ldy + r0 + g] = acc[0][0];
-        y[(int64_t)p0 * ldy + r0 + g + 8] = acc[0][2];
+        y[(int64_t)p0 * ldy + r0 + g] = acc[0][0] + ba;
+        y[(int64_t)p0 * ldy + r0 + g + 8] = acc[0][2] + bb;
       }
       if (p1 >= 0) {
-        y[(int64_t)p1 * ldy + r0 + g] = acc[0][1];
-        y[(int64_t)p1 * ldy + r0 + g + 8] = acc[0][3];
+        y[(int64_t)p1 * ldy + r0 + g] = acc[0][1] + ba;
+        y[(int64_t)p1 * ldy + r0 + g + 8] = acc[0][3] + bb;
       }
     }
     acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
@@ -1139,7 +1180,17 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
 // rows, K]; pairs grouped by moe_group (chunk_expert [max_chunks], chunk_pairs [max_chunks, 8], n_chunks [1]).
 void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, torch::Tensor qx,
                torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
-               torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err) {
+               torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err,
+               c10::optional<torch::Tensor> bias) {
+  const float* bp = nullptr;
+  if (bias.has_value()) {
+    // the packed experts hold (bytes / bytes per expert) experts; the bias has rows_per_expert per expert
+    const int64_t per_expert = (int64_t)tile_bytes((int)qtype) * (K / 256) * (rows_per_expert / 16);
+    const int64_t n_exp = per_expert > 0 ? w.numel() / per_expert : 0;
+    TORCH_CHECK(bias->is_cuda() && bias->scalar_type() == torch::kFloat32 && bias->is_contiguous() &&
+                    bias->numel() >= n_exp * rows_per_expert, "moe_tgemv: bias [experts x rows per expert] f32");
+    bp = bias->data_ptr<float>();
+  }
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "moe_tgemv: w");
   TORCH_CHECK(qtype == QT_Q4_K || qtype == QT_Q6_K || qtype == QT_Q8_0 || qtype == QT_G4, "moe_tgemv: qtype");
   TORCH_CHECK(rows_per_expert % 16 == 0 && K % 256 == 0, "moe_tgemv: rows per expert % 16, K % 256");
@@ -1175,7 +1226,7 @@ void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t 
                                       reinterpret_cast<const float2*>(ds.data_ptr<float>()), (int)topk,
                                       (int)act_by_token, (const int*)chunk_expert.data_ptr<int>(),
                                       (const int*)chunk_pairs.data_ptr<int>(), (const int*)n_chunks.data_ptr<int>(),
-                                      y.data_ptr<float>(), (int64_t)y.stride(0), (int)epi, err.data_ptr<int>(), g));
+                                      y.data_ptr<float>(), (int64_t)y.stride(0), (int)epi, err.data_ptr<int>(), g, bp));
   };
 #define FAK_TGM(QTV)                                       \
   {                                                        \

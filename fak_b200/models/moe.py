@@ -54,6 +54,17 @@ def _state(rn) -> MoEState:
     return st
 
 
+def _gate_epi(cfg) -> int:
+    """The gated epilogue of the experts: gpt-oss's clamped gate, else SwiGLU."""
+    return K.EPI_OAI if cfg.swiglu_alpha else K.EPI_SWIGLU
+
+
+def _route(rn, L, x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor) -> None:
+    cfg = rn.cfg
+    ext().moe_route(x, L.ffn_norm, cfg.rms_eps, L.router, cfg.n_experts_used, cfg.norm_topk_prob, ids, wts,
+                    L.router_bias, 1 if cfg.router == "topk_softmax" else 0)
+
+
 def _grouped_ffn(rn, L, st: MoEState, n_tok: int, act) -> None:
     C = ext()
     P = n_tok * st.k
@@ -62,11 +73,15 @@ def _grouped_ffn(rn, L, st: MoEState, n_tok: int, act) -> None:
     if gu.tp is not None and dn.tp is not None:
         # tile-packed experts: one CTA per chunk streams its expert's tiles through per-warp rings
         C.moe_tgemv(gu.tp, gu.qtype, gu.rows // st.E_local, gu.cols, act.q, act.ds, st.k, True,
-                    st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.h, 2, st.err)
+                    st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.h, _gate_epi(rn.cfg), st.err,
+                    L.experts_gate_up_bias)
         K.quant_act(st.h[:P], st.act_h)
         C.moe_tgemv(dn.tp, dn.qtype, dn.rows // st.E_local, dn.cols, st.act_h.q, st.act_h.ds, st.k, False,
-                    st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.out, 0, st.err)
+                    st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.out, 0, st.err,
+                    L.experts_down_bias)
     else:
+        if L.experts_gate_up_bias is not None or rn.cfg.swiglu_alpha:
+            raise NotImplementedError("biased / clamped-gate experts need tile-packed weights (widths % 256)")
         C.moe_qmmv(gu.buf, gu.qtype, gu.rows // st.E_local, gu.cols, gu.pitch, act.q, act.ds, st.k, True,
                    st.chunk_expert, st.chunk_pairs, st.n_chunks, st.max_chunks, st.h, 2, st.err)
         K.quant_act(st.h[:P], st.act_h)
@@ -79,7 +94,7 @@ def moe_decode(rn, i: int, B: int) -> None:
     cfg, L, st = rn.cfg, rn.w.layers[i], _state(rn)
     C = ext()
     x = rn.x[:B]
-    C.moe_route(x, L.ffn_norm, cfg.rms_eps, L.router, st.k, cfg.norm_topk_prob, st.ids[:B], st.wts[:B])
+    _route(rn, L, x, st.ids[:B], st.wts[:B])
     K.count()
     _grouped_ffn(rn, L, st, B, rn.act_d)
     if rn.coll is None:
@@ -100,7 +115,7 @@ def moe_prefill(rn, i: int, hb: torch.Tensor, x: torch.Tensor) -> None:
     k = cfg.n_experts_used
     ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
     wts = torch.empty(T, k, dtype=torch.float32, device=x.device)
-    C.moe_route(x, L.ffn_norm, cfg.rms_eps, L.router, k, cfg.norm_topk_prob, ids, wts)
+    _route(rn, L, x, ids, wts)
     e0, E_local = L.expert_ids[0], len(L.expert_ids)
     gu, dn = L.experts_gate_up, L.experts_down
     rows_gu, rows_dn = gu.rows // E_local, dn.rows // E_local
@@ -125,10 +140,12 @@ def moe_prefill(rn, i: int, hb: torch.Tensor, x: torch.Tensor) -> None:
                          dq.dequantize_rows(dn.buf[el * rows_dn * dn.pitch:], dn.qtype, rows_dn, dn.cols, dn.pitch,
                                             torch.bfloat16))
         wg, wd = dense[el]
-        h = torch.empty(a.shape[0], f, dtype=torch.float32, device=x.device)
-        K.gemm(a, wg, h, K.EPI_SWIGLU)
+        bgu = L.experts_gate_up_bias[el * rows_gu:(el + 1) * rows_gu] if L.experts_gate_up_bias is not None else None
+        bdn = L.experts_down_bias[el * d:(el + 1) * d] if L.experts_down_bias is not None else None
+        h = torch.empty(a.shape[0], f, dtype=torch.bfloat16, device=x.device)   # the gated product, bf16
+        K.gemm(a, wg, h, _gate_epi(cfg), bgu)
         o = torch.empty(a.shape[0], d, dtype=torch.float32, device=x.device)
-        K.gemm(h.to(torch.bfloat16), wd, o, K.EPI_STORE)
+        K.gemm(h, wd, o, K.EPI_STORE, bdn)
         out.index_copy_(0, pairs_d, o)
     if rn.coll is None:
         C.moe_combine(out, ids, wts, k, e0, E_local, x)

@@ -172,8 +172,10 @@ class ModelRunner:
         self.counts = torch.zeros(B, cfg.vocab_size, dtype=torch.int32, device=dev)
         # prefill attention on tcgen05 / TMEM (head dim 128, default scale, no soft-cap; windowed
         # layers and other shapes use the mma.sync kernel); FAK_PREFILL_ATTN=fa2 forces the latter
-        self.tc_prefill_attn = (self.D == 128 and cfg.attn_scale == 0 and cfg.attn_softcap == 0
+        self.tc_prefill_attn = (self.D == 128 and cfg.attn_scale == 0 and cfg.attn_softcap == 0 and not cfg.attn_sinks
                                 and os.environ.get("FAK_PREFILL_ATTN", "tc") != "fa2")
+        if collectives is not None and (cfg.attn_out_bias or cfg.moe_bias):
+            raise NotImplementedError("gpt-oss blocks run on one GPU per replica on the device path")
         n_sm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
         # decode attention: with dec_pps > 0 a split holds dec_pps pages (more for contexts past
         # dec_pps x 256 pages) and the grid has a split for every dec_pps pages of the longest
@@ -259,13 +261,13 @@ class ModelRunner:
                                act=self.act_attn,
                                workspace=self.attn_ws, tickets=self.attn_tickets if self.attn_merge else None,
                                prefetch=self._pf(L.o), window=cfg.layer_window(i),
-                               scale=cfg.attn_scale, softcap=cfg.attn_softcap,
+                               scale=cfg.attn_scale, softcap=cfg.attn_softcap, sinks=L.attn_sinks,
                                **self.cascade_args(B, cfg.layer_window(i)))
             if L.post_attn_norm is not None:   # sandwich norm: x += rmsnorm(o_proj(a))
-                K.gemv(L.o, self.act_attn, B, self.tmp[:B], None, K.EPI_STORE, prefetch=self._pf(L.gate_up))
+                K.gemv(L.o, self.act_attn, B, self.tmp[:B], L.o_bias, K.EPI_STORE, prefetch=self._pf(L.gate_up))
                 K.rmsnorm_add(self.tmp[:B], L.post_attn_norm, cfg.rms_eps, x)
             else:
-                K.gemv(L.o, self.act_attn, B, x, None, K.EPI_ADD, prefetch=self._pf(L.gate_up))
+                K.gemv(L.o, self.act_attn, B, x, L.o_bias, K.EPI_ADD, prefetch=self._pf(L.gate_up))
         else:
             self.coll.decode_attn_o(self, i, B, bt, ctx, n_split)
         if cfg.is_moe:
@@ -477,12 +479,12 @@ class ModelRunner:
                 K.prefill_attention_tc(qb, self.kv.k, self.kv.v, i, bt, meta, ab, self.err)
             else:
                 K.prefill_attention(qb, self.kv.k[i], self.kv.v[i], bt, meta, ab, cfg.layer_window(i),
-                                    cfg.attn_scale, cfg.attn_softcap)
+                                    cfg.attn_scale, cfg.attn_softcap, L.attn_sinks)
             if self.coll is None and L.post_attn_norm is not None:
-                K.gemm(ab, L.o, tmp, K.EPI_STORE)
+                K.gemm(ab, L.o, tmp, K.EPI_STORE, L.o_bias)
                 K.rmsnorm_add(tmp, L.post_attn_norm, cfg.rms_eps, x)
             elif self.coll is None:
-                K.gemm(ab, L.o, x, K.EPI_ADD)
+                K.gemm(ab, L.o, x, K.EPI_ADD, L.o_bias)
             else:
                 self.coll.prefill_attn_o(self, i, ab, x)
             K.rmsnorm_bf16(x, L.ffn_norm, cfg.rms_eps, hb)

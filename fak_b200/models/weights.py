@@ -93,6 +93,13 @@ class LayerWeights:
     expert_ids: list[int] | None = None  # global ids of the experts held here
     post_attn_norm: torch.Tensor | None = None   # sandwich norms (Gemma-2): after o_proj / down
     post_ffn_norm: torch.Tensor | None = None
+    # gpt-oss: attention sinks of this rank's heads [Hq_local], the o_proj bias [d], the router bias
+    # [E], and per-expert biases of the local experts (gate/up rows interleaved as the weights)
+    attn_sinks: torch.Tensor | None = None
+    o_bias: torch.Tensor | None = None
+    router_bias: torch.Tensor | None = None
+    experts_gate_up_bias: torch.Tensor | None = None
+    experts_down_bias: torch.Tensor | None = None
 
 
 @dataclasses.dataclass
@@ -377,6 +384,10 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
         if cfg.sandwich_norms:
             L.post_attn_norm = _vec(get, p + "post_attention_norm.weight", device)
             L.post_ffn_norm = _vec(get, p + "post_ffw_norm.weight", device)
+        if cfg.attn_sinks:
+            L.attn_sinks = _vec(get, p + "attn_sinks.weight", device)[torch.tensor(q_heads, device=device)].contiguous()
+        if cfg.attn_out_bias:
+            L.o_bias = _vec(get, p + "attn_output.bias", device)
         if cfg.is_moe:
             # expert parallelism rides on the tensor-parallel group: rank r owns a band of experts
             band = expert_filter if expert_filter is not None else expert_slice(cfg.n_experts, tp_rank, tp_size)
@@ -452,6 +463,13 @@ def _load_moe_layer(cfg, get, quant, p, L: LayerWeights, device, expert_filter) 
     L.experts_gate_up = QuantWeight.from_rows(gu, gt, d, device)
     L.experts_down = QuantWeight.from_rows(draw[e0:e1].reshape((e1 - e0) * d, -1).contiguous(), dt, f, device)
     L.expert_ids = list(range(e0, e1))
+    if cfg.moe_bias:   # gpt-oss: router and expert biases
+        L.router_bias = _vec(get, p + "ffn_gate_inp.bias", device)
+        bg = _vec(get, p + "ffn_gate_exps.bias", device).view(E, f)
+        bu = _vec(get, p + "ffn_up_exps.bias", device).view(E, f)
+        L.experts_gate_up_bias = torch.cat([interleave_gate_up(bg[e][:, None], bu[e][:, None]).view(-1)
+                                            for e in range(e0, e1)]).contiguous()
+        L.experts_down_bias = _vec(get, p + "ffn_down_exps.bias", device).view(E, d)[e0:e1].reshape(-1).contiguous()
     if f % 256 == 0 and d % 256 == 0:  # tile-packed copies for the grouped expert GEMV
         L.experts_gate_up.pack()
         L.experts_down.pack()

@@ -6,6 +6,7 @@ import torch
 from ._ext import ext
 
 EPI_STORE, EPI_ADD, EPI_SWIGLU, EPI_GEGLU = 0, 1, 2, 3
+EPI_OAI = 4   # the gpt-oss clamped gate: (clamp(u, -7, 7) + 1) * min(g, 7) * sigmoid(1.702 min(g, 7))
 GEMV_MAX_B = 8      # tokens per launch of the row-major kernels
 TGEMV_MAX_B = 32    # tokens per launch of the tile-packed GEMV (4 MMA column tiles)
 
@@ -174,7 +175,8 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,
                      workspace=None, ldo: int = 0, tickets=None, prefetch: torch.Tensor | None = None,
                      window: int = 0, shared_pages: torch.Tensor | None = None, prefix_splits: int = 0,
-                     scale: float = 0.0, softcap: float = 0.0, pages_per_split: int = 1) -> None:
+                     scale: float = 0.0, softcap: float = 0.0, pages_per_split: int = 1,
+                     sinks: torch.Tensor | None = None) -> None:
     """n_split splits of at least pages_per_split pages each (a sequence's live pages spread evenly
     over the splits when there are more; splits past its pages are skipped).
     ldo: elements per token row of the output (default: heads x head_dim).  tickets: zeroed int32
@@ -186,7 +188,7 @@ def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, ou
     (workspace sized for n_split + prefix_splits slots)."""
     ext().decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split, pages_per_split, out,
                            act.q if act is not None else None, act.ds if act is not None else None, workspace, ldo,
-                           tickets, prefetch, window, shared_pages, prefix_splits, scale, softcap)
+                           tickets, prefetch, window, shared_pages, prefix_splits, scale, softcap, sinks)
     cascade = shared_pages is not None and prefix_splits > 0 and window <= 0 and \
         q.shape[0] * (q.shape[1] // k_cache.shape[1]) <= 64
     n_slots = n_split + (prefix_splits if cascade else 0)
@@ -194,10 +196,11 @@ def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, ou
 
 
 def prefill_attention(q, k_cache, v_cache, block_table, meta, out, window: int = 0, scale: float = 0.0,
-                      softcap: float = 0.0) -> None:
-    """scale: logit scale (0 = 1/sqrt(head_dim)); softcap > 0: logits cap * tanh(logit / cap)."""
+                      softcap: float = 0.0, sinks: torch.Tensor | None = None) -> None:
+    """scale: logit scale (0 = 1/sqrt(head_dim)); softcap > 0: logits cap * tanh(logit / cap);
+    sinks [H] f32: one extra softmax logit per head that attends to nothing (gpt-oss)."""
     ext().prefill_attention(q, k_cache, v_cache, block_table, meta.tile_seq, meta.tile_q0, meta.seq_qoff,
-                            meta.seq_qlen, meta.seq_pos0, meta.n_tiles, out, window, scale, softcap)
+                            meta.seq_qlen, meta.seq_pos0, meta.n_tiles, out, window, scale, softcap, sinks)
     count()
 
 

@@ -158,6 +158,67 @@ def test_decode_attention(D, H, Hkv, n_split, pps, window):
     assert torch.allclose(deq.view(B, -1), out, atol=out.abs().max().item() / 127 + 1e-5)
 
 
+@pytest.mark.parametrize("n_split,cascade", [(1, 0), (7, 0), (16, 32)])
+def test_decode_attention_sinks(n_split, cascade):
+    """Attention sinks (gpt-oss): one extra logit per head in the softmax denominator, through the
+    single-split path, the split combine and the cascade prefix slots."""
+    from fak_b200.ops import kernels as K
+    D, H, Hkv = 64, 8, 2
+    shared = 64 if cascade else 0
+    ctx = [shared + 17, shared + 100, shared + 333]
+    B = len(ctx)
+    kc, vc, bt = _paged_cache(ctx, Hkv, D, seed=4)
+    if cascade:   # the first shared/16 pages identical in every block table
+        bt[:, :shared // 16] = bt[0, :shared // 16]
+    q = torch.randn(B, H, D, device="cuda")
+    sinks = torch.randn(H, device="cuda") * 2
+    out = torch.zeros(B, H * D, device="cuda")
+    ws = torch.zeros(B * H * (n_split + cascade) * (D + 2), device="cuda")
+    extra = {"shared_pages": torch.tensor([shared // 16], dtype=torch.int32, device="cuda"),
+             "prefix_splits": cascade} if cascade else {}
+    K.decode_attention(q, kc, vc, bt, torch.tensor(ctx, dtype=torch.int32, device="cuda"), n_split, out=out,
+                       workspace=ws, sinks=sinks, **extra)
+    torch.cuda.synchronize()
+    G = H // Hkv
+    for b, L in enumerate(ctx):
+        Kb, Vb = _gather(kc, bt[b], L), _gather(vc, bt[b], L)
+        s = torch.einsum("hd,thd->ht", q[b].bfloat16().float(), Kb.repeat_interleave(G, 1)) / math.sqrt(D)
+        pr = torch.softmax(torch.cat([s, sinks[:, None]], 1), 1)[:, :-1]
+        ref = torch.einsum("ht,thd->hd", pr, Vb.repeat_interleave(G, 1)).reshape(-1)
+        assert torch.allclose(out[b], ref, atol=2e-2, rtol=2e-2), (b, (out[b] - ref).abs().max())
+
+
+def test_prefill_attention_sinks():
+    from fak_b200.models.runner import PrefillMeta
+    from fak_b200.ops import kernels as K
+    D, H, Hkv = 64, 8, 2
+    qlens, pos0s = [70, 5, 130], [0, 40, 300]
+    ctx = [p + q for p, q in zip(pos0s, qlens)]
+    kc, vc, bt = _paged_cache(ctx, Hkv, D, seed=6)
+    T = sum(qlens)
+    q = torch.randn(T, H, D, device="cuda").bfloat16()
+    sinks = torch.randn(H, device="cuda") * 2
+    out = torch.zeros(T, H * D, device="cuda", dtype=torch.bfloat16)
+    meta = PrefillMeta.build(qlens, pos0s, "cuda")
+    K.prefill_attention(q, kc, vc, bt, meta, out, 0, sinks=sinks)
+    torch.cuda.synchronize()
+    G = H // Hkv
+    off = 0
+    for s_, (ql, p0) in enumerate(zip(qlens, pos0s)):
+        Kb = _gather(kc, bt[s_], p0 + ql).repeat_interleave(G, 1)
+        Vb = _gather(vc, bt[s_], p0 + ql).repeat_interleave(G, 1)
+        sc = torch.einsum("qhd,thd->hqt", q[off:off + ql].float(), Kb) / math.sqrt(D)
+        qpos = torch.arange(p0, p0 + ql, device="cuda")[:, None]
+        kpos = torch.arange(p0 + ql, device="cuda")[None, :]
+        sc = sc.masked_fill((kpos > qpos)[None], float("-inf"))
+        sk = sinks[:, None, None].expand(H, ql, 1)
+        pr = torch.softmax(torch.cat([sc, sk], -1), -1)[..., :-1]
+        ref = torch.einsum("hqt,thd->qhd", pr, Vb).reshape(ql, -1)
+        got = out[off:off + ql].float()
+        assert torch.allclose(got, ref, atol=3e-2, rtol=3e-2), (s_, (got - ref).abs().max())
+        off += ql
+
+
 @pytest.mark.parametrize("D,H,Hkv", [(128, 28, 4), (64, 9, 3)])
 @pytest.mark.parametrize("window", [0, 50])
 def test_prefill_attention(D, H, Hkv, window):
