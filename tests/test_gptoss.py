@@ -113,11 +113,15 @@ def test_sink_softmax_matches_the_explicit_form():
 
 
 @pytest.mark.parametrize("name", ["tiny-gptoss", "gpt-oss-20b"])
-def test_device_engine_refuses_gptoss_before_loading(name):
+def test_device_engine_takes_gptoss_and_refuses_other_gate_constants(name):
+    """The device kernels carry gpt-oss's gate constants (alpha 1.702, limit 7): the family runs on
+    the device engine, a model with other constants is refused before any weight is loaded."""
     from fak_b200.config import preset
     from fak_b200.engine import Engine
     cfg = preset(name)
-    assert "gpt-oss" in cfg.device_gap()
+    assert cfg.device_gap() is None
+    odd = cfg.replace(swiglu_alpha=1.5)
+    assert "1.702" in odd.device_gap()
     with pytest.raises(NotImplementedError, match="reference model"):
-        Engine.synthetic(cfg, device="cpu")
+        Engine.synthetic(odd, device="cpu")
     assert preset("qwen2.5-7b").device_gap() is None
