@@ -490,8 +490,10 @@ FAK_DEV uint32_t ar_ld_acquire(const uint32_t* p) {
 // completes (ar_push, plain stores into slot [parity][me][tile] of every rank), and after its last
 // tile (or after AR_PEND tiles) ar_finish issues ONE system-scope fence, releases the flags of all
 // those tiles on every rank, and only then waits for the other ranks' flags tile by tile, so the
-// NVLink round trips of a warp's tiles overlap instead of adding up.
-constexpr int AR_PEND = 8;
+// NVLink round trips of a warp's tiles overlap instead of adding up.  Two pending tiles: a warp
+// rarely finalises more (there are more warps than output tiles), and a longer list costs the
+// non-all-reduce launches registers they need.
+constexpr int AR_PEND = 2;
 
 template <int NT>
 FAK_DEV uint32_t ar_push(const ArPeers& ar, int T, int tile, int lane, const float (&v)[NT][4]) {

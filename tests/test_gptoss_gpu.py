@@ -49,11 +49,22 @@ def test_gptoss_engine_matches_reference(tmp_path):
     got_logits = forced_logits(eng, prompt, want_ids[:-1])
     with torch.no_grad():
         ref_logits = ref.forward(torch.tensor(prompt + want_ids[:-1]))[len(prompt) - 1:].float().cpu()
+    V = cfg.vocab_size
+    got_logits, ref_logits = got_logits[:, :V], ref_logits[:, :V]
     cos = torch.nn.functional.cosine_similarity(got_logits, ref_logits, dim=1)
     assert float(cos.min()) > 0.99, cos
+    agree = (got_logits.argmax(1) == ref_logits.argmax(1)).float().mean().item()
+    assert agree >= 0.75, agree
     out = eng.generate([prompt], max_new_tokens=12)[0]
+    eng.shutdown()
     k = 0
     while k < len(out) and out[k] == want_ids[k]:
         k += 1
-    assert k >= 4, (out, want_ids)
-    eng.shutdown()
+    if k < len(out):
+        # up to the first difference both runs saw the same tokens, so row k of the teacher-forced
+        # logits is the engine's own step k: the difference must be a near-tie of the fp32 model
+        # (its gap between the two tokens within twice the measured logit error on them)
+        a, b = want_ids[k], out[k]
+        gap = float(ref_logits[k, a] - ref_logits[k, b])
+        err = float((got_logits[k, a] - ref_logits[k, a]).abs() + (got_logits[k, b] - ref_logits[k, b]).abs())
+        assert gap <= max(0.05, 2.0 * err), (k, gap, err, out, want_ids)
