@@ -51,11 +51,13 @@ __global__ void k_embed(const uint8_t* __restrict__ table, int qtype, int64_t pi
   int t = blockIdx.x;
   int id = ids[t];
   if (id < 0 || id >= V) {
-    if (threadIdx.x == 0) report_error(err, 2);
+    if (threadIdx.x == 0 && blockIdx.y == 0) report_error(err, 2);
     id = 0;
   }
   const uint8_t* row = table + (int64_t)id * pitch;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+  // grid.y spreads a row over CTAs: one element per thread, so every element's block reads of a
+  // row are in flight at once (decode gathers only a few rows)
+  for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < d; c += blockDim.x * gridDim.y) {
     float v = dequant_one(row, qtype, c) * scale;   // scale: embedding multiplier (Gemma: sqrt(d))
     if (out_f32) out_f32[(int64_t)t * d + c] = v;
     if (out_bf16) out_bf16[(int64_t)t * d + c] = __float2bfloat16_rn(v);
@@ -263,7 +265,7 @@ void embed(torch::Tensor table, int64_t qtype, int64_t pitch, int64_t V, int64_t
   if (of) TORCH_CHECK(out_f32->is_contiguous() && out_f32->numel() >= (int64_t)T * d, "out_f32");
   if (ob) TORCH_CHECK(out_bf16->is_contiguous() && out_bf16->numel() >= (int64_t)T * d, "out_bf16");
   int* ep = err.has_value() ? err->data_ptr<int>() : nullptr;
-  auto cfg = make_cfg(dim3(T), dim3(256));
+  auto cfg = make_cfg(dim3(T, (unsigned)((d + 255) / 256)), dim3(256));
   FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_embed, (const uint8_t*)table.data_ptr<uint8_t>(), (int)qtype, pitch, (int)V,
                                     (int)d, (const int*)ids.data_ptr<int>(), of, ob, ep, (float)scale));
 }

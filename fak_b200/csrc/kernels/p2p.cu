@@ -148,7 +148,7 @@ FAK_DEV bool wait_flag_ge(const uint32_t* f, uint32_t v, uint32_t spin, int* err
 
 // x_local != nullptr (sequence parallel): the residual is this rank's owned rows only, compacted
 // ([MR, N], owner-local row index), updated in place with no broadcast and no closing barrier.
-__global__ void k_p2p_rs_reduce(Peers P, int64_t parts_off, int64_t flags_off, int64_t x_off, int M, int N, int MR,
+__global__ void __launch_bounds__(1024) k_p2p_rs_reduce(Peers P, int64_t parts_off, int64_t flags_off, int64_t x_off, int M, int N, int MR,
                                 int me, int W, uint32_t epoch, int64_t bar_off, int site, uint32_t* counters,
                                 int* err, float* __restrict__ x_local) {
   pdl_wait();

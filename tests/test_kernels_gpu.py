@@ -158,6 +158,29 @@ def test_decode_attention(D, H, Hkv, n_split, pps, window):
     assert torch.allclose(deq.view(B, -1), out, atol=out.abs().max().item() / 127 + 1e-5)
 
 
+@pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.Q8_0])
+def test_embed_rows(qt):
+    """The embedding gather (rows spread over several CTAs) returns the dequantized table rows, and
+    an id out of range reads row 0 and sets error code 2."""
+    from fak_b200.models.weights import QuantWeight
+    from fak_b200.ops import kernels as K
+    rng = np.random.default_rng(2)
+    V, d = 300, 3584
+    Wf = (rng.standard_normal((V, d)) * 0.05).astype(np.float32)
+    raw = Q.quantize(Wf, qt).reshape(V, -1)
+    w = QuantWeight.from_rows(torch.from_numpy(raw), int(qt), d, torch.device("cuda"))
+    Wd = torch.from_numpy(Q.dequantize(raw.reshape(-1), qt).reshape(V, d)).cuda()
+    ids = torch.tensor([5, 299, 0, 123, 77], dtype=torch.int32, device="cuda")
+    out = torch.zeros(5, d, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K.embed(w, ids, out, None, err, scale=2.0)
+    torch.cuda.synchronize()
+    assert torch.allclose(out, 2.0 * Wd[ids.long()], atol=1e-5) and int(err.item()) == 0
+    K.embed(w, torch.tensor([V + 3], dtype=torch.int32, device="cuda"), out, None, err)
+    torch.cuda.synchronize()
+    assert torch.allclose(out[0], Wd[0], atol=1e-5) and int(err.item()) == 2
+
+
 @pytest.mark.parametrize("n_split,cascade", [(1, 0), (7, 0), (16, 32)])
 def test_decode_attention_sinks(n_split, cascade):
     """Attention sinks (gpt-oss): one extra logit per head in the softmax denominator, through the
