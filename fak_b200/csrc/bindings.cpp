@@ -49,8 +49,8 @@ void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, i
                        int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err, int64_t ctas,
                        int64_t spin_limit);
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
-                torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
-                torch::Tensor err, int64_t spin_limit);
+                torch::Tensor out, int64_t B, torch::Tensor keys, torch::Tensor tickets, torch::Tensor epochs,
+                int64_t me, torch::Tensor err, int64_t spin_limit);
 void p2p_moe_combine_ar(torch::Tensor peers, torch::Tensor out, torch::Tensor ids, torch::Tensor wts, int64_t k,
                         int64_t e0, int64_t E_local, torch::Tensor x, int64_t B, int64_t parts_off, int64_t parity,
                         int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters, torch::Tensor err,
@@ -64,10 +64,16 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
-           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
+           int64_t ar_me, int64_t ar_parts_off, c10::optional<torch::Tensor> ar_epochs,
            c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit, bool unit);
 std::vector<int64_t> tgemv_workspace(int64_t qtype, int64_t N, int64_t K, int64_t device);
 int64_t tgemv_unit_bytes(int64_t qtype);
+std::vector<int64_t> tgemv_pair_plan(int64_t qa, int64_t Na, int64_t qb, int64_t Nb, int64_t K, int64_t B,
+                                     int64_t device);
+void tgemv_pair(torch::Tensor wa, int64_t qa, int64_t Na, torch::Tensor ya, c10::optional<torch::Tensor> bias_a,
+                torch::Tensor wb, int64_t qb, int64_t Nb, torch::Tensor yb, c10::optional<torch::Tensor> bias_b,
+                int64_t K, torch::Tensor qx, torch::Tensor ds, int64_t B, torch::Tensor part, torch::Tensor cnt,
+                c10::optional<torch::Tensor> err, c10::optional<torch::Tensor> prefetch, bool unit);
 void moe_tgemv(torch::Tensor w, int64_t qtype, int64_t rows_per_expert, int64_t K, torch::Tensor qx,
                torch::Tensor ds, int64_t topk, bool act_by_token, torch::Tensor chunk_expert, torch::Tensor chunk_pairs,
                torch::Tensor n_chunks, int64_t max_chunks, torch::Tensor y, int64_t epi, torch::Tensor err,
@@ -148,7 +154,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("counters"), pybind11::arg("err"), pybind11::arg("ctas"), pybind11::arg("spin_limit") = 0);
   m.def("p2p_argmax", &p2p_argmax, pybind11::arg("peers"), pybind11::arg("logits"), pybind11::arg("Vl"),
         pybind11::arg("v_off"), pybind11::arg("cand_off"), pybind11::arg("out"), pybind11::arg("B"),
-        pybind11::arg("flags_off"), pybind11::arg("site"), pybind11::arg("me"), pybind11::arg("counters"),
+        pybind11::arg("keys"), pybind11::arg("tickets"), pybind11::arg("epochs"), pybind11::arg("me"),
         pybind11::arg("err"), pybind11::arg("spin_limit") = 0);
   m.def("p2p_moe_combine_ar", &p2p_moe_combine_ar, "MoE combine fused with the expert-parallel all-reduce");
   m.def("moe_route", &moe_route, pybind11::arg("x"), pybind11::arg("gamma"), pybind11::arg("eps"),
@@ -168,11 +174,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("B"), pybind11::arg("y"), pybind11::arg("bias"),
         pybind11::arg("epi"), pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
         pybind11::arg("flags") = 0, pybind11::arg("ar_peers") = pybind11::none(), pybind11::arg("ar_me") = 0,
-        pybind11::arg("ar_parts_off") = 0, pybind11::arg("ar_flags_off") = 0, pybind11::arg("ar_epochs") = pybind11::none(),
+        pybind11::arg("ar_parts_off") = 0, pybind11::arg("ar_epochs") = pybind11::none(),
         pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("ar_spin_limit") = 0,
         pybind11::arg("unit") = false);
   m.def("tgemv_workspace", &tgemv_workspace);
   m.def("tgemv_unit_bytes", &tgemv_unit_bytes);
+  m.def("tgemv_pair_plan", &tgemv_pair_plan);
+  m.def("tgemv_pair", &tgemv_pair, pybind11::arg("wa"), pybind11::arg("qa"), pybind11::arg("Na"), pybind11::arg("ya"),
+        pybind11::arg("bias_a"), pybind11::arg("wb"), pybind11::arg("qb"), pybind11::arg("Nb"), pybind11::arg("yb"),
+        pybind11::arg("bias_b"), pybind11::arg("K"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("B"),
+        pybind11::arg("part"), pybind11::arg("cnt"), pybind11::arg("err") = pybind11::none(),
+        pybind11::arg("prefetch") = pybind11::none(), pybind11::arg("unit") = false);
   m.def("moe_tgemv", &moe_tgemv, pybind11::arg("w"), pybind11::arg("qtype"), pybind11::arg("rows_per_expert"),
         pybind11::arg("K"), pybind11::arg("qx"), pybind11::arg("ds"), pybind11::arg("topk"),
         pybind11::arg("act_by_token"), pybind11::arg("chunk_expert"), pybind11::arg("chunk_pairs"),

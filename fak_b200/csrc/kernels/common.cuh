@@ -117,6 +117,60 @@ FAK_DEV void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// First-index argmax as one 64-bit key: order-preserving float bits in the high word, the
+// complemented index in the low word, so the largest key is the largest value and, among equal
+// values, the lowest index.  Key 0 stands for "no element".
+FAK_DEV unsigned long long argmax_key(float v, uint32_t i) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - i);
+}
+FAK_DEV int argmax_key_index(unsigned long long k) { return k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0; }
+
+// The largest key of x[i0, i1) for the calling CTA (valid in thread 0); index i is reported as
+// i + id_off.  Every thread issues its PER loads (four floats each when VEC) before comparing, so
+// a chunk costs one memory latency rather than one per element.
+template <int PER, bool VEC>
+FAK_DEV unsigned long long cta_best_key(const float* __restrict__ x, int i0, int i1, uint32_t id_off) {
+  constexpr int E = VEC ? 4 : 1;
+  float v[PER][E];
+#pragma unroll
+  for (int j = 0; j < PER; j++) {
+    const int i = i0 + (j * (int)blockDim.x + (int)threadIdx.x) * E;
+    if (VEC && i + 4 <= i1) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(x + i));
+      v[j][0] = f.x;
+      if constexpr (E == 4) { v[j][1] = f.y; v[j][2] = f.z; v[j][3] = f.w; }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; e++) v[j][e] = i + e < i1 ? __ldg(x + i + e) : 0.f;
+    }
+  }
+  unsigned long long best = 0ull;
+#pragma unroll
+  for (int j = 0; j < PER; j++) {
+    const int i = i0 + (j * (int)blockDim.x + (int)threadIdx.x) * E;
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+      if (i + e < i1) {
+        const unsigned long long k = argmax_key(v[j][e], (uint32_t)(i + e) + id_off);
+        best = k > best ? k : best;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
+  }
+  __shared__ unsigned long long sk[32];
+  if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = sk[w] > best ? sk[w] : best;
+  return best;
+}
+
 }  // namespace fak
 
 #define FAK_CUDA_CHECK(expr)                                                                  \

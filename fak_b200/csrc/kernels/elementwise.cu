@@ -193,36 +193,19 @@ __global__ void k_argmax(const float* __restrict__ logits, int64_t ld, int V, in
 }
 
 // Multi-CTA first-index argmax: grid (rows, chunks).  Each CTA folds its chunk into one packed
-// 64-bit key per row -- order-preserving float bits in the high word, the complemented index in
-// the low word, so atomicMax keeps the largest value and, among equal values, the lowest index --
-// and the last CTA of a row (ticket) writes the index and resets the key and ticket to zero.
-FAK_DEV unsigned long long argmax_key(float v, int i) {
-  uint32_t u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
-}
+// 64-bit key per row (argmax_key: atomicMax keeps the largest value and, among equal values, the
+// lowest index), and the last CTA of a row (ticket) writes the index and resets the key and ticket
+// to zero.
+constexpr int kArgmaxThreads = 256, kArgmaxPer = 4;   // a CTA's chunk: 256 x 4 x 4 = 4096 floats
+template <bool VEC>
 __global__ void k_argmax_chunks(const float* __restrict__ logits, int64_t ld, int V, int chunk,
                                 unsigned long long* __restrict__ keys, int* __restrict__ tickets, int* __restrict__ out) {
   pdl_wait();
   const int r = blockIdx.x;
-  const float* x = logits + (int64_t)r * ld;
   const int i0 = blockIdx.y * chunk, i1 = min(V, i0 + chunk);
-  unsigned long long best = 0ull;
-  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    const unsigned long long k = argmax_key(x[i], i);
-    best = k > best ? k : best;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
-    best = k > best ? k : best;
-  }
-  __shared__ unsigned long long sk[32];
+  const unsigned long long best = cta_best_key<VEC ? kArgmaxPer : 4 * kArgmaxPer, VEC>(logits + (int64_t)r * ld, i0, i1, 0u);
   __shared__ int s_last;
-  if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
-  __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = sk[w] > best ? sk[w] : best;
     atomicMax(&keys[r], best);
     __threadfence();
     s_last = atomicAdd(&tickets[r], 1) == (int)gridDim.y - 1;
@@ -232,7 +215,7 @@ __global__ void k_argmax_chunks(const float* __restrict__ logits, int64_t ld, in
   if (threadIdx.x == 0 && s_last) {
     __threadfence();
     const unsigned long long k = atomicExch(&keys[r], 0ull);
-    out[r] = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+    out[r] = argmax_key_index(k);
     tickets[r] = 0;
   }
 }
@@ -360,10 +343,11 @@ void argmax_rows(torch::Tensor logits, int64_t V, torch::Tensor out, c10::option
     TORCH_CHECK(keys->scalar_type() == torch::kInt64 && keys->numel() >= R, "argmax: keys [R] int64");
     TORCH_CHECK(tickets.has_value() && tickets->scalar_type() == torch::kInt32 && tickets->numel() >= R,
                 "argmax: tickets [R] int32");
-    const int chunk = 8192;
-    auto cfg = make_cfg(dim3(R, (unsigned)((V + chunk - 1) / chunk)), dim3(256));
-    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_argmax_chunks, (const float*)logits.data_ptr<float>(),
-                                      (int64_t)logits.stride(0), (int)V, chunk,
+    const int chunk = kArgmaxThreads * kArgmaxPer * 4;
+    const bool vec = logits.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0;
+    auto cfg = make_cfg(dim3(R, (unsigned)((V + chunk - 1) / chunk)), dim3(kArgmaxThreads));
+    FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, vec ? k_argmax_chunks<true> : k_argmax_chunks<false>,
+                                      (const float*)logits.data_ptr<float>(), (int64_t)logits.stride(0), (int)V, chunk,
                                       reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>()),
                                       tickets->data_ptr<int>(), out.data_ptr<int>()));
     return;

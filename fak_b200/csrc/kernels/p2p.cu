@@ -269,53 +269,86 @@ __global__ void k_p2p_rs_push(Peers P, const float* __restrict__ part, int M, in
 }
 
 // ---- greedy sampling over vocab-sharded logits ---------------------------------------------
-// CTA b: first-index argmax of row b of the local logits slice, published as (value, global id)
-// to every rank; after the barrier every rank reduces the W candidates in rank order.
+// Grid (rows, chunks).  Each CTA folds its chunk of the local vocabulary shard into one argmax key
+// (global ids); the last CTA of a row (ticket) takes the row's key and exchanges it with the other
+// ranks as one 16-byte line {key low, epoch, key high, epoch} stored into slot [parity][row][me]
+// of every rank -- the epoch words travel in the same store as the key, so no fence or flag is
+// needed -- then polls its own W slots (bounded) and every rank takes the same largest key.
+// The epoch of a row counts launches in local memory (graph replays stay valid); slots alternate
+// halves by epoch parity, so a rank one step ahead cannot overwrite a key a slower rank has not read.
+constexpr int kArgmaxThreads = 256, kArgmaxPer = 4;   // a CTA's chunk: 256 x 4 float4 = 4096 floats
+
+FAK_DEV void ll_store16(uint4* p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+FAK_DEV uint4 ll_load16(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+template <bool VEC>
 __global__ void k_p2p_argmax(Peers P, const float* __restrict__ logits, int64_t ld, int Vl, int64_t v_off,
-                             int64_t cand_off, int* __restrict__ out, int64_t flags_off, int site, int me, int W,
-                             uint32_t* counters, int* err) {
+                             int64_t cand_off, int* __restrict__ out, unsigned long long* __restrict__ keys,
+                             int* __restrict__ tickets, uint32_t* __restrict__ epochs, int me, int W, int* err) {
   pdl_wait();
-  const int b = blockIdx.x;
-  const float* x = logits + (int64_t)b * ld;
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < Vl; i += blockDim.x) {
-    float v = x[i];
-    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  const int b = blockIdx.x, chunk = kArgmaxThreads * kArgmaxPer * 4;
+  const int i0 = blockIdx.y * chunk, i1 = min(Vl, i0 + chunk);
+  const unsigned long long best =
+      cta_best_key<VEC ? kArgmaxPer : 4 * kArgmaxPer, VEC>(logits + (int64_t)b * ld, i0, i1, (uint32_t)v_off);
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    atomicMax(&keys[b], best);
+    __threadfence();
+    s_last = atomicAdd(&tickets[b], 1) == (int)gridDim.y - 1;
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  if (!s_last || threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  unsigned long long k = 0ull;
+  uint32_t ep = 0;
+  if (lane == 0) {
+    __threadfence();
+    k = atomicExch(&keys[b], 0ull);
+    tickets[b] = 0;
+    ep = epochs[b] + 1;
+  }
+  k = __shfl_sync(0xffffffffu, k, 0);
+  ep = __shfl_sync(0xffffffffu, ep, 0);
+  const int64_t half = (int64_t)(ep & 1u) * MAX_CTAS * MAX_W;
+  if (lane < W) {   // lane r pushes to rank r, then reads rank r's key from its own buffer
+    const uint4 line = make_uint4((uint32_t)(k & 0xFFFFFFFFull), ep, (uint32_t)(k >> 32), ep);
+    ll_store16(reinterpret_cast<uint4*>(P.base[lane] + cand_off) + half + (int64_t)b * MAX_W + me, line);
+  }
+  unsigned long long kr = 0ull;
+  if (lane < W) {
+    const uint4* src = reinterpret_cast<const uint4*>(P.base[me] + cand_off) + half + (int64_t)b * MAX_W + lane;
+    uint4 v;
+    uint32_t it = 0;
+    while (true) {
+      v = ll_load16(src);
+      if (v.y == ep && v.w == ep) break;
+      if (++it > P.spin) {
+        report_error(err, 1);
+        break;
+      }
+    }
+    kr = ((unsigned long long)v.z << 32) | v.x;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, kr, o);
+    kr = t > kr ? t : kr;
   }
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int nw = blockDim.x >> 5;
-    for (int w = 1; w < nw; w++)
-      if (sv[w] > sv[0] || (sv[w] == sv[0] && si[w] < si[0])) { sv[0] = sv[w]; si[0] = si[w]; }
-    const int64_t gid = si[0] == 0x7fffffff ? 0x7fffffff : (int64_t)si[0] + v_off;
-    for (int r = 0; r < W; r++) {
-      float2* cand = reinterpret_cast<float2*>(P.base[r] + cand_off) + (int64_t)b * MAX_W + me;
-      *cand = make_float2(sv[0], __int_as_float((int)gid));
-    }
+  if (lane == 0) {
+    out[b] = argmax_key_index(kr);
+    epochs[b] = ep;
   }
-  rank_barrier(P, flags_off, site, b, me, W, counters, err);
-  if (threadIdx.x == 0) {
-    const float2* cand = reinterpret_cast<const float2*>(P.base[me] + cand_off) + (int64_t)b * MAX_W;
-    float bv = -INFINITY;
-    int bidx = 0x7fffffff;
-    for (int r = 0; r < W; r++) {
-      const float2 c = cand[r];
-      const int ci = __float_as_int(c.y);
-      if (c.x > bv || (c.x == bv && ci < bidx)) { bv = c.x; bidx = ci; }
-    }
-    out[b] = bidx == 0x7fffffff ? 0 : bidx;
-  }
-  pdl_launch_dependents();
 }
 
 // ---- MoE combine fused with the expert-parallel all-reduce -----------------------------------
@@ -481,19 +514,31 @@ void p2p_rs_push(torch::Tensor peers, torch::Tensor part, int64_t MR, int64_t pa
                                     parts_off, flags_off, (int)me, W, (uint32_t)epoch));
 }
 
+// logits [B, >= Vl] f32 (this rank's vocabulary shard, global ids v_off + i); cand_off: the
+// [2][MAX_CTAS][MAX_W] 16-byte line slots of the peer buffers; keys / tickets: local [B] scratch left
+// at zero; epochs: local [MAX_CTAS] launch counters.
 void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v_off, int64_t cand_off,
-                torch::Tensor out, int64_t B, int64_t flags_off, int64_t site, int64_t me, torch::Tensor counters,
-                torch::Tensor err, int64_t spin_limit) {
+                torch::Tensor out, int64_t B, torch::Tensor keys, torch::Tensor tickets, torch::Tensor epochs,
+                int64_t me, torch::Tensor err, int64_t spin_limit) {
   const int W = (int)peers.numel();
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.stride(1) == 1, "logits");
   TORCH_CHECK(B >= 1 && B <= MAX_CTAS, "argmax: batch 1..64");
+  TORCH_CHECK(cand_off % 16 == 0, "argmax: candidate slots 16-byte aligned");
+  TORCH_CHECK(keys.scalar_type() == torch::kInt64 && keys.numel() >= B && tickets.scalar_type() == torch::kInt32 &&
+                  tickets.numel() >= B, "argmax: keys [B] int64, tickets [B] int32");
+  TORCH_CHECK(epochs.scalar_type() == torch::kInt32 && epochs.numel() >= MAX_CTAS, "argmax: epochs [64] int32");
+  TORCH_CHECK(v_off >= 0 && v_off + Vl < 0xFFFFFFFFll, "argmax: ids fit 32 bits");
   Peers P = make_peers(peers, spin_limit);
+  const int chunk = kArgmaxThreads * kArgmaxPer * 4;
+  const bool vec = logits.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0;
   cudaLaunchAttribute attr[1];
-  auto cfg = pdl_cfg(dim3((unsigned)B), dim3(1024), attr);
-  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_argmax, P, (const float*)logits.data_ptr<float>(),
-                                    (int64_t)logits.stride(0), (int)Vl, v_off, cand_off, out.data_ptr<int>(),
-                                    flags_off, (int)site, (int)me, W, (uint32_t*)counters.data_ptr<int>(),
-                                    err.data_ptr<int>()));
+  auto cfg = pdl_cfg(dim3((unsigned)B, (unsigned)((Vl + chunk - 1) / chunk)), dim3(kArgmaxThreads), attr);
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, vec ? k_p2p_argmax<true> : k_p2p_argmax<false>, P,
+                                    (const float*)logits.data_ptr<float>(), (int64_t)logits.stride(0), (int)Vl, v_off,
+                                    cand_off, out.data_ptr<int>(),
+                                    reinterpret_cast<unsigned long long*>(keys.data_ptr<int64_t>()),
+                                    tickets.data_ptr<int>(), reinterpret_cast<uint32_t*>(epochs.data_ptr<int>()),
+                                    (int)me, W, err.data_ptr<int>()));
 }
 
 // out [B*k, d] f32 (expert outputs per (token, slot)); ids / wts [B, k]; x [B, d] f32 (residual, updated);

@@ -456,42 +456,63 @@ FAK_DEV void epilogue(int tile, const float (&v)[4], int tokb, int lane, int N, 
 }
 
 // Tensor-parallel all-reduce fused into the epilogue (K-split row-parallel layers: the attention
-// output projection and the down projection): the warp that finishes a tile pushes its partial into
-// slot [parity][me][tile] of every rank's symmetric buffer with plain stores, publishes a per-tile
-// epoch flag on every rank (release, system scope), waits (acquire, bounded) for all ranks' flags of
-// that tile, and sums the W slots of its own buffer in rank order -- every rank computes
-// bit-identical values -- before the residual add.  Epochs count launches per tile in local memory,
-// so the kernel replays inside CUDA graphs; the slots alternate between two halves by epoch parity,
-// so a fast rank's next launch (the next projection sharing the slots) cannot overwrite a partial a
-// slow rank has not summed yet: to reach epoch e + 2 it must pass epoch e + 1, which every rank
-// publishes only after its launch of epoch e finished.  The wait gives up after ``spin`` polls
-// (a launch argument) and records error code 4.  No multicast, no TMA from peer memory: peer memory
-// is touched by ordinary stores only.
+// output projection and the down projection).  The warp that finishes a tile pushes its partial into
+// slot [parity][me][tile] of every rank's symmetric buffer, sums the W slots of its own buffer in rank
+// order -- every rank computes bit-identical values -- and adds the sum to the residual.
+//
+// Flags travel inside the data (the low-latency line format NCCL calls LL): a lane's four partial
+// values go out as two 16-byte stores {v0, epoch, v1, epoch}, {v2, epoch, v3, epoch}, and a reader
+// polls its own copy of the line until both epoch words of both halves match.  An aligned 8-byte
+// half of a vector store arrives whole, so a matching epoch word vouches for the value beside it:
+// there is no separate flag, no system-scope fence and no acquire -- one NVLink write latency per
+// tile instead of a fence drain plus a flag round trip (the fence version cost 17 us per projection
+// at two ranks against 7 us for the GEMV alone).  The price is twice the bytes on the link, a few
+// KB per tile.
+//
+// Epochs count launches per tile in local memory, so the kernel replays inside CUDA graphs; the
+// slots alternate between two halves by epoch parity, so a fast rank's next launch (the next
+// projection sharing the slots) cannot overwrite a line a slow rank has not read yet: to write epoch
+// e + 2 it must have read every rank's epoch e + 1 lines, which a rank writes only after its launch
+// of epoch e (and so its reads of epoch e) finished.  A wait gives up after ``spin`` polls (a launch
+// argument) and records error code 4.  No multicast, no TMA from peer memory: peer memory is touched
+// by ordinary stores only.
 constexpr int AR_MAX_W = 8;
 constexpr uint32_t kArSpinLimit = 1u << 24;
 struct ArPeers {
   uint8_t* base[AR_MAX_W];  // symmetric buffer base of every rank (W = 0: no all-reduce)
   int W, me;
-  int64_t parts_off, flags_off;
+  int64_t parts_off;        // line slots: [2 parities][AR_MAX_W][T][4 n8 tiles][32 lanes][2] uint4
   uint32_t* epochs;         // local [T]
-  uint32_t spin;            // polls of a flag before the wait gives up
+  uint32_t spin;            // polls of a line before the wait gives up
 };
 
-FAK_DEV void ar_st_release(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// bytes of the line slots for T tiles
+__host__ __device__ constexpr int64_t ar_slot_bytes(int64_t T) { return 2LL * AR_MAX_W * T * 4 * 32 * 32; }
+
+FAK_DEV void ll_store(uint4* p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
-FAK_DEV uint32_t ar_ld_acquire(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+FAK_DEV uint4 ll_load(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
-// A warp's pushes are not fenced one tile at a time: it pushes the final partial of every tile it
-// completes (ar_push, plain stores into slot [parity][me][tile] of every rank), and after its last
-// tile (or after AR_PEND tiles) ar_finish issues ONE system-scope fence, releases the flags of all
-// those tiles on every rank, and only then waits for the other ranks' flags tile by tile, so the
-// NVLink round trips of a warp's tiles overlap instead of adding up.  Two pending tiles: a warp
-// rarely finalises more (there are more warps than output tiles), and a longer list costs the
+// lane's two lines of (source rank r, tile, n8 tile nt) in the half of epoch ep
+FAK_DEV uint4* ar_line(const ArPeers& ar, int owner, int T, uint32_t ep, int r, int tile, int nt, int lane) {
+  const int64_t half = (int64_t)(ep & 1u) * AR_MAX_W * T * 4 * 32 * 2;
+  return reinterpret_cast<uint4*>(ar.base[owner] + ar.parts_off) + half +
+         ((((int64_t)r * T + tile) * 4 + nt) * 32 + lane) * 2;
+}
+
+// A warp pushes the final partial of every tile it completes (ar_push) and reads the other ranks'
+// lines for those tiles only after AR_PEND of them (or its last tile), so the NVLink latencies of a
+// warp's tiles overlap each other and the GEMV of its next tile.  Two pending tiles: a warp rarely
+// finalises more (there are more warps than output tiles), and a longer list costs the
 // non-all-reduce launches registers they need.
 constexpr int AR_PEND = 2;
 
@@ -500,13 +521,15 @@ FAK_DEV uint32_t ar_push(const ArPeers& ar, int T, int tile, int lane, const flo
   uint32_t ep = 0;
   if (lane == 0) ep = ar.epochs[tile] + 1;
   ep = __shfl_sync(0xffffffffu, ep, 0);
-  // the half of the slots this epoch uses: [AR_MAX_W][T][<= 4 n8 tiles][32 lanes] float4 each
-  const int64_t half = (int64_t)(ep & 1u) * AR_MAX_W * T * 4 * 32;
 #pragma unroll
   for (int nt = 0; nt < NT; nt++) {
-    const float4 val = make_float4(v[nt][0], v[nt][1], v[nt][2], v[nt][3]);
-    const int64_t slot = half + (((int64_t)ar.me * T + tile) * NT + nt) * 32 + lane;
-    for (int r = 0; r < ar.W; r++) reinterpret_cast<float4*>(ar.base[r] + ar.parts_off)[slot] = val;
+    const uint4 l0 = make_uint4(__float_as_uint(v[nt][0]), ep, __float_as_uint(v[nt][1]), ep);
+    const uint4 l1 = make_uint4(__float_as_uint(v[nt][2]), ep, __float_as_uint(v[nt][3]), ep);
+    for (int r = 0; r < ar.W; r++) {
+      uint4* dst = ar_line(ar, r, T, ep, ar.me, tile, nt, lane);
+      ll_store(dst, l0);
+      ll_store(dst + 1, l1);
+    }
   }
   return ep;
 }
@@ -515,39 +538,29 @@ template <int NT>
 FAK_DEV void ar_finish(const ArPeers& ar, int T, const int (&pend)[AR_PEND], const uint32_t (&peps)[AR_PEND], int np,
                        int lane, int N, int B, float* __restrict__ y, int64_t ldy, const float* __restrict__ bias,
                        int epi, int* err) {
-  __syncwarp();
-  if (lane < ar.W) {
-    __threadfence_system();   // every lane's pushes (ordered by the warp barrier) before the flags
-    uint32_t* flags = reinterpret_cast<uint32_t*>(ar.base[lane] + ar.flags_off);
-#pragma unroll
-    for (int i = 0; i < AR_PEND; i++)
-      if (i < np) ar_st_release(flags + (int64_t)pend[i] * AR_MAX_W + ar.me, peps[i]);
-  }
 #pragma unroll
   for (int i = 0; i < AR_PEND; i++) {
     if (i >= np) break;
     const int tile = pend[i];
     const uint32_t ep = peps[i];
-    if (lane < ar.W) {
-      const uint32_t* mine = reinterpret_cast<const uint32_t*>(ar.base[ar.me] + ar.flags_off) +
-                             (int64_t)tile * AR_MAX_W + lane;
-      uint32_t it = 0;
-      while (ar_ld_acquire(mine) < ep) {
-        if (++it > ar.spin) {
-          report_error(err, 4);
-          break;
-        }
-      }
-    }
-    __syncwarp();
-    const int64_t half = (int64_t)(ep & 1u) * AR_MAX_W * T * 4 * 32;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
       float v[4] = {0.f, 0.f, 0.f, 0.f};
       for (int r = 0; r < ar.W; r++) {
-        const int64_t slot = half + (((int64_t)r * T + tile) * NT + nt) * 32 + lane;
-        const float4 p = __ldcg(reinterpret_cast<const float4*>(ar.base[ar.me] + ar.parts_off) + slot);
-        v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
+        const uint4* src = ar_line(ar, ar.me, T, ep, r, tile, nt, lane);
+        uint4 a, b;
+        uint32_t it = 0;
+        while (true) {
+          a = ll_load(src);
+          b = ll_load(src + 1);
+          if (a.y == ep && a.w == ep && b.y == ep && b.w == ep) break;
+          if (++it > ar.spin) {
+            report_error(err, 4);
+            break;
+          }
+        }
+        v[0] += __uint_as_float(a.x); v[1] += __uint_as_float(a.z);
+        v[2] += __uint_as_float(b.x); v[3] += __uint_as_float(b.z);
       }
       epilogue(tile, v, 8 * nt, lane, N, B, y, ldy, bias, epi);
     }
@@ -555,20 +568,58 @@ FAK_DEV void ar_finish(const ArPeers& ar, int T, const int (&pend)[AR_PEND], con
   }
 }
 
-template <int QT, int W, int R, int NT, bool US = false>
-__global__ void __launch_bounds__(W * 32, 1)
-k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__ qx, const float2* __restrict__ ds,
-        const float* __restrict__ xf, int64_t ldx, const float* __restrict__ gamma, float eps,
-        int B, float* __restrict__ y, int64_t ldy, const float* __restrict__ bias, int epi,
-        float* __restrict__ part, int* __restrict__ cnt, int* __restrict__ err, TGeo geo, ArPeers ar,
-        const uint8_t* __restrict__ pf, int64_t pf_bytes) {
+// One GEMV launch's arguments (a kernel parameter: read from the constant bank, never copied).
+struct TgArgs {
+  const uint8_t* Wt;     // tile-packed weights
+  int N, K;
+  const int8_t* qx;      // quantized activations [B, K] and their (scale, sum) pairs, or
+  const float2* ds;
+  const float* xf;       // fp32 activations [B, ldx] (normalised with gamma when given)
+  int64_t ldx;
+  const float* gamma;
+  float eps;
+  int B;
+  float* y;              // output [B, ldy]
+  int64_t ldy;
+  const float* bias;
+  int epi;
+  float* part;           // split-K partials and tickets
+  int* cnt;
+  int* err;
+  TGeo geo;
+  ArPeers ar;
+  const uint8_t* pf;     // L2 prefetch of the next kernel's weights
+  int64_t pf_bytes;
+};
+
+// The GEMV of one CTA (index bid among the geo.P * geo.S CTAs of this matrix).
+template <int QT, int W, int R, int NT, bool US>
+FAK_DEV void tgemv_cta(const int bid, const TgArgs& a) {
+  const uint8_t* __restrict__ Wt = a.Wt;
+  const int N = a.N, K = a.K;
+  const int8_t* __restrict__ qx = a.qx;
+  const float2* __restrict__ ds = a.ds;
+  const float* __restrict__ xf = a.xf;
+  const int64_t ldx = a.ldx;
+  const float* __restrict__ gamma = a.gamma;
+  const float eps = a.eps;
+  const int B = a.B;
+  float* __restrict__ y = a.y;
+  const int64_t ldy = a.ldy;
+  const float* __restrict__ bias = a.bias;
+  const int epi = a.epi;
+  float* __restrict__ part = a.part;
+  int* __restrict__ cnt = a.cnt;
+  int* __restrict__ err = a.err;
+  const TGeo& geo = a.geo;
+  const ArPeers& ar = a.ar;
   constexpr int UT = Tile<QT>::UT;
   constexpr int TABF = Tile<QT>::TABF;
   constexpr int MB = 8 * NT;  // token rows staged
   extern __shared__ __align__(128) uint8_t sm[];
   const TSmem L = tsmem(QT, W, R, NT, geo);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int slice = blockIdx.x % geo.S, cta = blockIdx.x / geo.S;
+  const int slice = bid % geo.S, cta = bid / geo.S;
   const int u0 = slice * geo.Us;
   const int nu = min(geo.Us, geo.U - u0);          // units of this slice
   const int k0 = u0 * 256;
@@ -612,7 +663,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
   // weights do not depend on the previous kernel: their first copies go out before the wait
   if (lane == 0)
     for (int i = 0; i < R - 1; i++) issue_next();
-  l2_prefetch(pf, pf_bytes);
+  l2_prefetch(a.pf, a.pf_bytes);
   pdl_wait();
   if (xf != nullptr) {
     // fp32 activations: optional RMSNorm (statistics over the whole row), then int8 per 32-block
@@ -801,7 +852,7 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
       }
     }
     if (have) {
-      if (ar.W > 0) {   // fused all-reduce: push now, fence / wait / sum / store in batches
+      if (ar.W > 0) {   // fused all-reduce: push now, read / sum / store in batches
         const uint32_t ep = ar_push<NT>(ar, geo.T, tile, lane, acc);
 #pragma unroll
         for (int i = 0; i < AR_PEND; i++)
@@ -820,6 +871,21 @@ k_tgemv(const uint8_t* __restrict__ Wt, int N, int K, const int8_t* __restrict__
     tile += wstride;
   }
   if (npend > 0) ar_finish<NT>(ar, geo.T, pend, peps, npend, lane, N, B, y, ldy, bias, epi, err);
+}
+
+template <int QT, int W, int R, int NT, bool US = false>
+__global__ void __launch_bounds__(W * 32, 1) k_tgemv(const TgArgs a) {
+  tgemv_cta<QT, W, R, NT, US>(blockIdx.x, a);
+  pdl_launch_dependents();
+}
+
+// Two GEMVs over the same activations in one launch (q|k in Q4_K and v in Q6_K, say): CTAs [0, nA)
+// run the first, the rest the second, so the two latency chains (activation staging, weight
+// copies, split-K tickets) overlap instead of following one another.
+template <int QA, int QB, int W, int R, int NT, bool US>
+__global__ void __launch_bounds__(W * 32, 1) k_tgemv_pair(const TgArgs a, const TgArgs b, const int nA) {
+  if ((int)blockIdx.x < nA) tgemv_cta<QA, W, R, NT, US>(blockIdx.x, a);
+  else tgemv_cta<QB, W, R, NT, US>(blockIdx.x - nA, b);
   pdl_launch_dependents();
 }
 
@@ -1045,7 +1111,7 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
            c10::optional<torch::Tensor> ds, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> gamma,
            double eps, int64_t B, torch::Tensor y, c10::optional<torch::Tensor> bias, int64_t epi, torch::Tensor part,
            torch::Tensor cnt, c10::optional<torch::Tensor> err, int64_t flags, c10::optional<torch::Tensor> ar_peers,
-           int64_t ar_me, int64_t ar_parts_off, int64_t ar_flags_off, c10::optional<torch::Tensor> ar_epochs,
+           int64_t ar_me, int64_t ar_parts_off, c10::optional<torch::Tensor> ar_epochs,
            c10::optional<torch::Tensor> prefetch, int64_t ar_spin_limit, bool unit) {
   TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8, "tgemv: w cuda uint8");
   const uint8_t* pfp = prefetch.has_value() ? reinterpret_cast<const uint8_t*>(prefetch->data_ptr()) : nullptr;
@@ -1056,12 +1122,11 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     TORCH_CHECK(h.scalar_type() == torch::kInt64 && h.numel() >= 1 && h.numel() <= AR_MAX_W, "tgemv: peers");
     TORCH_CHECK(ar_epochs.has_value() && ar_epochs->scalar_type() == torch::kInt32 &&
                     ar_epochs->numel() >= (N + 15) / 16, "tgemv: all-reduce epochs [tiles] int32");
-    TORCH_CHECK(epi == EPI_ADD && ar_parts_off % 16 == 0 && ar_flags_off % 4 == 0, "tgemv: all-reduce layout");
+    TORCH_CHECK(epi == EPI_ADD && ar_parts_off % 16 == 0, "tgemv: all-reduce layout");
     ar.W = (int)h.numel();
     ar.me = (int)ar_me;
     for (int r = 0; r < ar.W; r++) ar.base[r] = reinterpret_cast<uint8_t*>(h.data_ptr<int64_t>()[r]);
     ar.parts_off = ar_parts_off;
-    ar.flags_off = ar_flags_off;
     ar.epochs = reinterpret_cast<uint32_t*>(ar_epochs->data_ptr<int>());
     TORCH_CHECK(ar_spin_limit >= 0 && ar_spin_limit <= 0xffffffffll, "tgemv: spin limit");
     ar.spin = ar_spin_limit > 0 ? (uint32_t)ar_spin_limit : kArSpinLimit;
@@ -1138,13 +1203,29 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
     FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem));
     for (int64_t b0 = 0; b0 < B; b0 += chunk) {
       const int nb = (int)std::min<int64_t>(chunk, B - b0);
-      FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const uint8_t*)w.data_ptr<uint8_t>(), (int)N, (int)K,
-                                        qp ? qp + b0 * K : nullptr, dp ? dp + b0 * (K / 32) : nullptr,
-                                        xp ? xp + b0 * ldx : nullptr, ldx, gp, (float)eps, nb,
-                                        y.data_ptr<float>() + b0 * y.stride(0), (int64_t)y.stride(0), bp, (int)epi,
-                                        p.geo.S > 1 ? part.data_ptr<float>() : nullptr,
-                                        p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr, ep, p.geo, ar,
-                                        b0 == 0 ? pfp : nullptr, pfb));
+      TgArgs a{};
+      a.Wt = w.data_ptr<uint8_t>();
+      a.N = (int)N;
+      a.K = (int)K;
+      a.qx = qp ? qp + b0 * K : nullptr;
+      a.ds = dp ? dp + b0 * (K / 32) : nullptr;
+      a.xf = xp ? xp + b0 * ldx : nullptr;
+      a.ldx = ldx;
+      a.gamma = gp;
+      a.eps = (float)eps;
+      a.B = nb;
+      a.y = y.data_ptr<float>() + b0 * y.stride(0);
+      a.ldy = y.stride(0);
+      a.bias = bp;
+      a.epi = (int)epi;
+      a.part = p.geo.S > 1 ? part.data_ptr<float>() : nullptr;
+      a.cnt = p.geo.S > 1 ? cnt.data_ptr<int>() : nullptr;
+      a.err = ep;
+      a.geo = p.geo;
+      a.ar = ar;
+      a.pf = b0 == 0 ? pfp : nullptr;
+      a.pf_bytes = pfb;
+      FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
     }
   };
   // unit-scale activations (one scale per 256 columns, ActQ.unit) on Q4_K / Q6_K weights: integer
@@ -1176,6 +1257,151 @@ void tgemv(torch::Tensor w, int64_t qtype, int64_t N, int64_t K, c10::optional<t
 #undef FAK_TG
 #undef FAK_TG_NT
 #undef FAK_TG_W
+}
+
+namespace {
+// The CTA split and per-matrix plans of a pair launch: the SMs shared in proportion to the weight
+// bytes, both plans with 16 warps and a 3-deep ring (the one pair instantiation).  The K splits
+// depend on the shapes only, so a token reduces in the same order in every batch; the batch runs
+// as launches of the widest token tile whose staging fits for both matrices.
+struct PairPlan {
+  bool ok = false;
+  int nA = 0;
+  Plan a, b;
+  int64_t partA = 0, cntA = 0, partB = 0, cntB = 0;   // split-K scratch (floats, tickets) of each
+};
+
+PairPlan make_pair_plan(int qa, int64_t Na, int qb, int64_t Nb, int64_t K, int64_t B, int n_sm, int max_smem) {
+  PairPlan pp;
+  if (!(qa == QT_Q4_K && qb == QT_Q6_K) || K % 256 != 0 || B < 1 || B > 8 * MAXNT || n_sm < 2) return pp;
+  const int NT = B <= 8 ? 1 : (B <= 16 ? 2 : 4);
+  const int64_t U = K / 256;
+  const double ba = (double)((Na + 15) / 16) * U * tile_bytes(qa), bb = (double)((Nb + 15) / 16) * U * tile_bytes(qb);
+  pp.nA = std::min(n_sm - 1, std::max(1, (int)std::lround(n_sm * ba / (ba + bb))));
+  for (int nt = NT; nt >= 1; nt >>= 1) {
+    pp.a = make_plan(qa, Na, K, nt, pp.nA, max_smem, 16, 3, 0);
+    pp.b = make_plan(qb, Nb, K, nt, n_sm - pp.nA, max_smem, 16, 3, 0);
+    if (pp.a.NT == nt && pp.b.NT == nt) break;
+  }
+  if (pp.a.NT != pp.b.NT) return pp;
+  const int nt = pp.a.NT;
+  pp.partA = pp.a.geo.S > 1 ? (int64_t)pp.a.geo.S * pp.a.geo.T * 128 * nt : 0;
+  pp.cntA = pp.a.geo.S > 1 ? pp.a.geo.T : 0;
+  pp.partB = pp.b.geo.S > 1 ? (int64_t)pp.b.geo.S * pp.b.geo.T * 128 * nt : 0;
+  pp.cntB = pp.b.geo.S > 1 ? pp.b.geo.T : 0;
+  pp.ok = true;
+  return pp;
+}
+
+void dev_limits(int device, int& n_sm, int& max_smem) {
+  FAK_CUDA_CHECK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
+  FAK_CUDA_CHECK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+}
+}  // namespace
+
+// Whether two matrices over the same activations can run as one pair launch, and the split-K
+// scratch it needs: [] when not, else [CTAs of the first, floats, tickets].
+std::vector<int64_t> tgemv_pair_plan(int64_t qa, int64_t Na, int64_t qb, int64_t Nb, int64_t K, int64_t B,
+                                     int64_t device) {
+  int n_sm = 0, max_smem = 0;
+  dev_limits((int)device, n_sm, max_smem);
+  const PairPlan pp = make_pair_plan((int)qa, Na, (int)qb, Nb, K, B, n_sm, max_smem);
+  if (!pp.ok) return {};
+  return {pp.nA, pp.partA + pp.partB, pp.cntA + pp.cntB};
+}
+
+// ya[:B] = Wa . x (+ bias_a) and yb[:B] = Wb . x (+ bias_b), EPI_STORE, in one launch per chunk of
+// tokens; x quantized (qx, ds).  part / cnt hold both matrices' split-K scratch, the second's after
+// the first's.
+void tgemv_pair(torch::Tensor wa, int64_t qa, int64_t Na, torch::Tensor ya, c10::optional<torch::Tensor> bias_a,
+                torch::Tensor wb, int64_t qb, int64_t Nb, torch::Tensor yb, c10::optional<torch::Tensor> bias_b,
+                int64_t K, torch::Tensor qx, torch::Tensor ds, int64_t B, torch::Tensor part, torch::Tensor cnt,
+                c10::optional<torch::Tensor> err, c10::optional<torch::Tensor> prefetch, bool unit) {
+  static int n_sm = 0, max_smem = 0;
+  if (!n_sm) dev_limits(wa.get_device(), n_sm, max_smem);
+  const PairPlan pp = make_pair_plan((int)qa, Na, (int)qb, Nb, K, B, n_sm, max_smem);
+  TORCH_CHECK(pp.ok, "tgemv_pair: no pair launch for these shapes (check tgemv_pair_plan first)");
+  auto check_w = [&](const torch::Tensor& w, int64_t qt, int64_t N) {
+    TORCH_CHECK(w.is_cuda() && w.scalar_type() == torch::kUInt8 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+                "tgemv_pair: weights cuda uint8, 16-byte aligned");
+    TORCH_CHECK(w.numel() >= (N + 15) / 16 * (K / 256) * tile_bytes((int)qt), "tgemv_pair: weight buffer too small");
+  };
+  check_w(wa, qa, Na);
+  check_w(wb, qb, Nb);
+  auto check_y = [&](const torch::Tensor& y, int64_t N, const c10::optional<torch::Tensor>& bias) -> const float* {
+    TORCH_CHECK(y.scalar_type() == torch::kFloat32 && y.dim() == 2 && y.stride(1) == 1 && y.size(0) >= B &&
+                    y.size(1) >= N, "tgemv_pair: y [B, >=N] f32");
+    if (!bias.has_value()) return nullptr;
+    TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() >= N, "tgemv_pair: bias");
+    return bias->data_ptr<float>();
+  };
+  const float* bpa = check_y(ya, Na, bias_a);
+  const float* bpb = check_y(yb, Nb, bias_b);
+  TORCH_CHECK(qx.scalar_type() == torch::kInt8 && qx.is_contiguous() && qx.numel() >= B * K &&
+                  reinterpret_cast<uintptr_t>(qx.data_ptr()) % 16 == 0, "tgemv_pair: qx");
+  TORCH_CHECK(ds.scalar_type() == torch::kFloat32 && ds.is_contiguous() && ds.numel() >= B * K / 16 &&
+                  reinterpret_cast<uintptr_t>(ds.data_ptr()) % 16 == 0, "tgemv_pair: ds");
+  TORCH_CHECK(part.scalar_type() == torch::kFloat32 && part.numel() >= pp.partA + pp.partB &&
+                  cnt.scalar_type() == torch::kInt32 && cnt.numel() >= pp.cntA + pp.cntB, "tgemv_pair: scratch too small");
+  auto args = [&](const torch::Tensor& w, int64_t N, const torch::Tensor& y, const float* bp, const Plan& p,
+                  int64_t part_off, int64_t cnt_off) {
+    TgArgs a{};
+    a.Wt = w.data_ptr<uint8_t>();
+    a.N = (int)N;
+    a.K = (int)K;
+    a.qx = qx.data_ptr<int8_t>();
+    a.ds = reinterpret_cast<const float2*>(ds.data_ptr<float>());
+    a.y = y.data_ptr<float>();
+    a.ldy = y.stride(0);
+    a.bias = bp;
+    a.epi = EPI_STORE;
+    a.part = p.geo.S > 1 ? part.data_ptr<float>() + part_off : nullptr;
+    a.cnt = p.geo.S > 1 ? cnt.data_ptr<int>() + cnt_off : nullptr;
+    a.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+    a.geo = p.geo;
+    return a;
+  };
+  TgArgs A = args(wa, Na, ya, bpa, pp.a, 0, 0);
+  TgArgs Bv = args(wb, Nb, yb, bpb, pp.b, pp.partA, pp.cntA);
+  if (prefetch.has_value()) {
+    A.pf = reinterpret_cast<const uint8_t*>(prefetch->data_ptr());
+    A.pf_bytes = prefetch->numel() * prefetch->element_size();
+  }
+  const int nA = pp.a.geo.P * pp.a.geo.S, nB = pp.b.geo.P * pp.b.geo.S;
+  const int smem = std::max(pp.a.smem, pp.b.smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(16 * 32);
+  cfg.gridDim = dim3(nA + nB);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = fak::pdl_allowed();
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int chunk = 8 * pp.a.NT;
+  auto go = [&](auto kern) {
+    FAK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    for (int64_t b0 = 0; b0 < B; b0 += chunk) {
+      TgArgs a = A, b = Bv;
+      a.B = b.B = (int)std::min<int64_t>(chunk, B - b0);
+      a.qx = b.qx = A.qx + b0 * K;
+      a.ds = b.ds = A.ds + b0 * (K / 32);
+      a.y += b0 * a.ldy;
+      b.y += b0 * b.ldy;
+      if (b0 > 0) a.pf = nullptr;
+      FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, a, b, nA));
+    }
+  };
+#define FAK_TGP(NTV)                                                \
+  {                                                                 \
+    if (unit) go(k_tgemv_pair<QT_Q4_K, QT_Q6_K, 16, 3, NTV, true>); \
+    else go(k_tgemv_pair<QT_Q4_K, QT_Q6_K, 16, 3, NTV, false>);     \
+  }
+  if (pp.a.NT == 1) FAK_TGP(1)
+  else if (pp.a.NT == 2) FAK_TGP(2)
+  else FAK_TGP(4)
+#undef FAK_TGP
 }
 
 // Grouped expert GEMV over tile-packed experts (MoE decode).  w: tile-packed [E_local * rows_per_expert

@@ -150,6 +150,8 @@ class ModelRunner:
         # attention_merge merges the attention splits in the last split's CTA instead of a combine
         # kernel (one CTA then reads all the partials of its heads: a long tail, 0.7 ms/step slower).
         self.fused_act = fused_activations
+        # q|k and v in different block formats: one pair launch of the GEMV instead of two
+        self.qkv_pair = os.environ.get("FAK_QKV_PAIR", "1") != "0"
         self.attn_merge = attention_merge
         self.l2_prefetch = l2_prefetch
         self.ffn_in = K.FAct(self.h) if self.fused_act else self.act_ffn   # SwiGLU output -> down projection
@@ -240,6 +242,14 @@ class ModelRunner:
         """Tile-packed weights of ``w`` to warm L2 with during the current kernel (or None)."""
         return w.tp if self.l2_prefetch and w is not None and w.tp is not None else None
 
+    def _qkv_pair(self, L, xin, B: int) -> bool:
+        """The two q|k|v segments of different block formats as one pair launch (False: not possible)."""
+        (sa, oa), (sb, ob) = L.qkv
+        bias = L.qkv_bias
+        return K.gemv_pair(sa, sb, xin, B, self.qkv[:B, oa:oa + sa.rows], self.qkv[:B, ob:ob + sb.rows],
+                           bias[oa:oa + sa.rows] if bias is not None else None,
+                           bias[ob:ob + sb.rows] if bias is not None else None)
+
     def _layer_decode(self, i: int, B: int, pos, slot, bt, ctx, n_split: int) -> None:
         cfg, L, kv = self.cfg, self.w.layers[i], self.kv
         x = self.x[:B]
@@ -250,10 +260,11 @@ class ModelRunner:
         else:
             K.quant_act(x, self.act_d, L.attn_norm, cfg.rms_eps, prefetch=self._pf(segs[0][0]))
             xin = self.act_d
-        for j, (seg, off) in enumerate(segs):
-            bias = L.qkv_bias[off:off + seg.rows] if L.qkv_bias is not None else None
-            pf = segs[j + 1][0] if j + 1 < len(segs) else None
-            K.gemv(seg, xin, B, self.qkv[:B, off:off + seg.rows], bias, K.EPI_STORE, prefetch=self._pf(pf))
+        if not (self.qkv_pair and len(segs) == 2 and self._qkv_pair(L, xin, B)):
+            for j, (seg, off) in enumerate(segs):
+                bias = L.qkv_bias[off:off + seg.rows] if L.qkv_bias is not None else None
+                pf = segs[j + 1][0] if j + 1 < len(segs) else None
+                K.gemv(seg, xin, B, self.qkv[:B, off:off + seg.rows], bias, K.EPI_STORE, prefetch=self._pf(pf))
         K.rope_kv(self.qkv[:B], pos, slot, self.cos, self.sin, self.Hq, self.Hkv, L.q_norm, L.k_norm, cfg.rms_eps,
                   self.q[:B], None, kv.k[i], kv.v[i])
         if self.coll is None:

@@ -127,8 +127,8 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
     """y[:B] (op)= W . x for a decode batch (w: models.weights.QuantWeight); chunks of 8 tokens.
 
     Matrices with a tile-packed copy (``QuantWeight.pack``) run the tile-packed tensor-core GEMV;
-    others the row-major kernels.  ``ar`` = (peer bases, rank, parts offset, flags offset, epochs
-    [, spin limit]) fuses a tensor-parallel all-reduce of the result into the GEMV (EPI_ADD, one
+    others the row-major kernels.  ``ar`` = (peer bases, rank, line-slot offset, epochs [, spin
+    limit]) fuses a tensor-parallel all-reduce of the result into the GEMV (EPI_ADD, one
     launch, B <= 32); a peer that never arrives makes the wait give up after the spin limit (0: the
     kernel default) and report error 4 in the registered error word."""
     C = ext()
@@ -146,8 +146,8 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
             nb = min(TGEMV_MAX_B, B - b0)
             if ar is not None and B > TGEMV_MAX_B:
                 raise ValueError("the fused all-reduce GEMV takes at most 32 tokens")
-            arkw = {} if ar is None else dict(ar_peers=ar[0], ar_me=ar[1], ar_parts_off=ar[2], ar_flags_off=ar[3],
-                                              ar_epochs=ar[4], ar_spin_limit=ar[5] if len(ar) > 5 else 0)
+            arkw = {} if ar is None else dict(ar_peers=ar[0], ar_me=ar[1], ar_parts_off=ar[2], ar_epochs=ar[3],
+                                              ar_spin_limit=ar[4] if len(ar) > 4 else 0)
             if prefetch is not None and b0 == 0:
                 arkw["prefetch"] = prefetch
             ew = _err_word.get(w.tp.device)
@@ -170,6 +170,43 @@ def gemv(w, act: ActQ, B: int, y: torch.Tensor, bias: torch.Tensor | None = None
         else:
             C.qmmv(w.buf, w.qtype, w.rows, w.cols, w.pitch, q, d, nb, y[b0:b0 + nb], bias, epi)
         count()
+
+
+_pair_plans: dict = {}
+
+
+def gemv_pair(wa, wb, act: ActQ, B: int, ya: torch.Tensor, yb: torch.Tensor, bias_a: torch.Tensor | None = None,
+              bias_b: torch.Tensor | None = None, prefetch: torch.Tensor | None = None) -> bool:
+    """ya[:B] = Wa . x (+ bias_a) and yb[:B] = Wb . x (+ bias_b) in ONE launch of the tile-packed GEMV
+    (two matrices of different block formats over the same quantized activations, e.g. q|k in Q4_K
+    and v in Q6_K): the SMs are shared in proportion to the weight bytes, so the two launches' latency
+    chains overlap.  Returns False (nothing launched) when the pair has no such launch; the caller
+    then runs the two GEMVs one after the other."""
+    if wa.tp is None or wb.tp is None or isinstance(act, FAct) or wa.cols != wb.cols:
+        return False
+    if (wa.qtype, wb.qtype) == (14, 12):   # the launch takes the Q4_K matrix first
+        wa, wb, ya, yb, bias_a, bias_b = wb, wa, yb, ya, bias_b, bias_a
+    dev = wa.tp.device
+    chunks = [(b0, min(TGEMV_MAX_B, B - b0)) for b0 in range(0, B, TGEMV_MAX_B)]
+    for _, nb in chunks:
+        key = (wa.qtype, wa.rows, wb.qtype, wb.rows, wa.cols, nb, dev)
+        plan = _pair_plans.get(key)
+        if plan is None:
+            plan = _pair_plans[key] = tuple(ext().tgemv_pair_plan(wa.qtype, wa.rows, wb.qtype, wb.rows, wa.cols, nb,
+                                                                  dev.index or 0))
+        if not plan:
+            return False
+        part, cnt = tgemv_workspace(dev)
+        if part.numel() < plan[1] or cnt.numel() < plan[2]:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("tgemv scratch too small for a pair launch inside a graph capture")
+            return False
+    for b0, nb in chunks:
+        ext().tgemv_pair(wa.tp, wa.qtype, wa.rows, ya[b0:b0 + nb], bias_a, wb.tp, wb.qtype, wb.rows, yb[b0:b0 + nb],
+                         bias_b, wa.cols, act.q[b0:b0 + nb], act.ds[b0:b0 + nb], nb, part, cnt, _err_word.get(dev),
+                         prefetch if b0 == 0 else None, getattr(act, "unit", False))
+        count()
+    return True
 
 
 def decode_attention(q, k_cache, v_cache, block_table, ctx_len, n_split: int, out=None, act: ActQ | None = None,

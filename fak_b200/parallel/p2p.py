@@ -6,9 +6,11 @@ NVLink multicast object; ``FAK_P2P_MEM=symm`` uses torch symmetric memory instea
 
 * ``flags``   -- per-(site, CTA, source-rank) epoch flags of the cross-rank barriers;
 * ``parts``   -- fp32 [B, d] partial-sum slots per (layer, projection) for the unfused fallback;
-* ``cand``    -- (value, id) argmax candidates for greedy sampling over the vocab shards;
-* ``arparts`` -- per-tile partial slots of the all-reduce fused into the GEMV epilogue
-  ([epoch parity][source rank][tile][<= 32 tokens]), and ``arflags`` their per-tile epoch flags.
+* ``cand``    -- argmax key lines (key and launch epoch in one 16-byte store) for greedy sampling
+  over the vocab shards;
+* ``arparts`` -- per-tile line slots of the all-reduce fused into the GEMV epilogue
+  ([epoch parity][source rank][tile][<= 32 tokens]); each 16-byte line carries two values, each
+  beside the launch epoch that marks it valid (no separate flags).
 
 Both row-parallel projections of a decode layer -- the attention output projection (o_proj) and
 the down projection -- all-reduce in their own GEMV epilogue: the warp that finishes a 16-row output
@@ -42,6 +44,12 @@ from .tp import NcclTP
 
 MAX_CTAS = 64
 MAX_W = 8
+
+
+def ar_slot_bytes(tiles: int) -> int:
+    """Bytes of the fused all-reduce's line slots for ``tiles`` 16-row output tiles: two epoch
+    parities x MAX_W source ranks x 4 token tiles x 32 lanes x two 16-byte lines."""
+    return 2 * MAX_W * tiles * 4 * 32 * 32
 AR_CTAS = 16
 AG_CTAS = 16
 RS_CTAS = 64
@@ -103,14 +111,14 @@ class P2PTP(NcclTP):
         off = _align(off + self.n_sites * MAX_CTAS * MAX_W * 4)
         self.parts_off = off
         off = _align(off + 2 * L * B * d * 4)
+        # greedy argmax: per-row key lines [2 parities][MAX_CTAS rows][MAX_W sources] x 16 B
         self.cand_off = off
-        off = _align(off + B * MAX_W * 8)
-        # fused all-reduce: per-tile partial slots [parity][src][tile][<= 32 tokens] and flags
+        off = _align(off + 2 * MAX_CTAS * MAX_W * 16)
+        # fused all-reduce: per-tile line slots [parity][src][tile][<= 4 n8 tiles][32 lanes] x 2 x 16 B,
+        # each 16-byte line two (value, epoch) pairs
         self.ar_tiles = (d + 15) // 16
         self.arparts_off = off
-        off = _align(off + 2 * MAX_W * self.ar_tiles * 4 * 128 * 4)
-        self.arflags_off = off
-        off = _align(off + self.ar_tiles * MAX_W * 4)
+        off = _align(off + ar_slot_bytes(self.ar_tiles))
         # sampled steps: full-vocabulary logit rows [B, W * Vl], rank r's shard at columns [r Vl, (r+1) Vl)
         self.lg_ok = self.Vl % 4 == 0
         self.lg_off = off
@@ -158,6 +166,8 @@ class P2PTP(NcclTP):
             self.me = self.rank
         self.counters = torch.zeros(self.n_sites * MAX_CTAS, dtype=torch.int32, device=device)
         self.ar_epochs = torch.zeros(self.ar_tiles, dtype=torch.int32, device=device)
+        self.argmax_epochs = torch.zeros(MAX_CTAS, dtype=torch.int32, device=device)
+        self.argmax_ws = K.argmax_workspace(device, MAX_CTAS)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)   # replaced by the runner's status word
         if self.lg_ok:
             self._rows().fill_(float("-inf"))     # shard tails past the real vocabulary stay -inf
@@ -175,7 +185,7 @@ class P2PTP(NcclTP):
         return int(self.err.item())
 
     def _ar(self) -> tuple:
-        return (self.peers, self.me, self.arparts_off, self.arflags_off, self.ar_epochs, self.spin_limit)
+        return (self.peers, self.me, self.arparts_off, self.ar_epochs, self.spin_limit)
 
     def _part(self, i: int, which: int, B: int) -> tuple[int, torch.Tensor]:
         d = self.cfg.d_model
@@ -227,8 +237,8 @@ class P2PTP(NcclTP):
         """Local vocab-shard logits, then the distributed first-index argmax into rn.next_ids."""
         K.gemv(rn.w.lm_head, rn.lm_in, B, self.logits_local[:B, :self.Vl_real], None, K.EPI_STORE)
         ext().p2p_argmax(self.peers, self.logits_local[:B], self.Vl_real, self.v_off, self.cand_off,
-                         rn.next_ids[:B], B, self.flags_off, 3 * self.cfg.n_layers, self.me, self.counters, self.err,
-                         self.spin_limit)
+                         rn.next_ids[:B], B, self.argmax_ws[0], self.argmax_ws[1], self.argmax_epochs, self.me,
+                         self.err, self.spin_limit)
         K.count()
 
     def moe_combine(self, rn, i: int, B: int, st) -> None:

@@ -450,6 +450,36 @@ def test_tgemv_batch_invariant_and_repeatable(qt, blk):
     assert not K.tgemv_workspace("cuda")[1].any()
 
 
+@pytest.mark.parametrize("Na,Nb", [(4096, 512), (512, 64)])
+@pytest.mark.parametrize("B", [1, 5, 13, 32, 40])
+@pytest.mark.parametrize("unit", [False, True])
+def test_tgemv_pair(Na, Nb, B, unit):
+    """One launch of a Q4_K and a Q6_K matrix over the same activations (q|k and v of a Q4_K_M
+    layer) vs an fp32 reference of each; a token's outputs are bit-identical alone and in the batch,
+    and the split-K tickets of both halves are left at zero."""
+    from fak_b200.ops import kernels as K
+    Kd = 3584
+    wa, Wa, x, _ = _tg_case(GGMLType.Q4_K, Na, Kd, B, seed=21)
+    wb, Wb, _, _ = _tg_case(GGMLType.Q6_K, Nb, Kd, B, seed=22)
+    act = K.ActQ(max(8, B), Kd, "cuda", unit=unit)
+    K.quant_act(x, act)
+    ba, bb = torch.randn(Na, device="cuda") * 0.1, torch.randn(Nb, device="cuda") * 0.1
+    ya, yb = torch.zeros(B, Na, device="cuda"), torch.zeros(B, Nb, device="cuda")
+    assert K.gemv_pair(wb, wa, act, B, yb, ya, bb, ba)    # either order; the Q4_K matrix goes first
+    torch.cuda.synchronize()
+    for y, ref in ((ya, x @ Wa.T + ba), (yb, x @ Wb.T + bb)):
+        err = (y - ref).abs().max().item() / ref.abs().max().item()
+        cos = torch.nn.functional.cosine_similarity(y.flatten(), ref.flatten(), dim=0).item()
+        assert cos > 0.9995 and err < 0.03, (cos, err)
+    for b in sorted({0, B // 2, B - 1}):
+        solo = K.ActQ(8, Kd, "cuda", unit=unit)
+        K.quant_act(x[b:b + 1], solo)
+        y1a, y1b = torch.zeros(1, Na, device="cuda"), torch.zeros(1, Nb, device="cuda")
+        assert K.gemv_pair(wa, wb, solo, 1, y1a, y1b, ba, bb)
+        assert torch.equal(y1a[0], ya[b]) and torch.equal(y1b[0], yb[b]), b
+    assert not K.tgemv_workspace("cuda")[1].any()
+
+
 @pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.Q6_K])
 @pytest.mark.parametrize("B", [1, 5, 13, 32])
 @pytest.mark.parametrize("N,Kd", [(576, 4096), (16 * 2400, 1024)])
