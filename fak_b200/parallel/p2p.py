@@ -129,7 +129,9 @@ class P2PTP(NcclTP):
         # prefill all-reduce: the residual [T, d], partial slots [W][MR][d] (MR rows of owned
         # 128-row m-blocks per source rank) and tile flags [m-block][256-column block][MAX_W]
         Tp = max(0, int(max_prefill_tokens))
-        self.pf_fused = Tp > 0 and d % 4 == 0 and os.environ.get("FAK_PREFILL_P2P", "1") != "0"
+        # the fused prefill all-reduce is opt-in: at TP=2 on Qwen2.5-7B it measured TTFT p50 30.5-30.9 ms
+        # against 28.6 ms with NCCL's all-reduce for the same turns
+        self.pf_fused = Tp > 0 and d % 4 == 0 and os.environ.get("FAK_PREFILL_P2P", "0") == "1"
         Tp = Tp if self.pf_fused else 0
         n_m, n_n = -(-Tp // 128), -(-d // 256)
         self.pf_T, self.pf_MR = Tp, -(-n_m // self.world) * 128

@@ -29,6 +29,23 @@ def test_tp2_matches_tp1(model, fused):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["p2p", "sp"])
+def test_tp2_fused_prefill_matches_tp1(mode):
+    """The opt-in in-kernel prefill all-reduce (reduce-scatter in the GEMM epilogue, owner reduce and
+    broadcast) and the sequence-parallel prefill on top of it agree with TP=1."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT, FAK_PREFILL_P2P="1",
+               FAK_PREFILL_SP="1" if mode == "sp" else "0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29536", "-m", "fak_b200.benchmarks.tpcheck",
+           "--model", "tiny-qwen2", "--mix", "q4_k_m", "--fused", "1"]
+    p = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
+    assert p.returncode == 0, p.stderr[-3000:]
+    res = json.loads([l for l in p.stdout.splitlines() if l.startswith("{")][-1])
+    assert res["ok"], json.dumps({k: res.get(k) for k in ("teacher_forced", "greedy", "kernel_error",
+                                                         "collective_error")})
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep2_moe_matches_ep1():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
