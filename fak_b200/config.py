@@ -328,6 +328,7 @@ class EngineConfig:
     swap_space_gb: float = 16.0         # pinned host memory for swapped-out KV pages
     async_decode: bool = True           # device-resident lane state; tokens read back one step behind
     p2p_spin_limit: int = 0             # polls before a cross-rank wait gives up (0: kernel default, ~1 s)
+    cpu_offload_experts: bool = False   # MoE experts in host memory, their FFNs on the CPU (no CUDA graphs)
 
     ENV_KEYS = {
         "page_size": ("FAK_PAGED_KV_BLOCK_TOKENS", int),
@@ -356,6 +357,7 @@ class EngineConfig:
         "swap_space_gb": ("FAK_SWAP_SPACE_GB", float),
         "async_decode": ("FAK_ASYNC_DECODE", bool),
         "p2p_spin_limit": ("FAK_P2P_SPIN_LIMIT", int),
+        "cpu_offload_experts": ("FAK_CPU_OFFLOAD_EXPERTS", bool),
     }
 
     @classmethod

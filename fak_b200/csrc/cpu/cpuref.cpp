@@ -426,6 +426,178 @@ class CpuModel {
   int n_ctx = 0;
 };
 
+// ---- MoE experts resident in host memory (CPU offload) -----------------------------------------
+// The expert FFNs of a MoE layer run here while the dense projections, the router and attention
+// stay on the GPU (the llama.cpp --n-cpu-moe split; reference: internal/model/moe_offload.go,
+// splitKernel routing every expert weight to the host kernel).  A layer holds this rank's band of
+// experts [e0, e0 + n): gate/up rows interleaved in blocks of 8 (the device layout: rows
+// [16i, 16i+8) gate, [16i+8, 16i+16) up) and down rows, both in their GGML blocks.  ffn() adds
+// sum_slot w[b, slot] * expert_{ids[b, slot]}(x[b]) to out[b] for the slots whose expert is in
+// the band, the slots added in order so the result does not depend on the thread count.
+class CpuExperts {
+ public:
+  CpuExperts(int64_t n_layers, int64_t d, int64_t f, int64_t gate, bool act_quant)
+      : d_((int)d), f_((int)f), gate_((int)gate), act_quant_(act_quant), layers_(n_layers) {
+    if (gate < 2 || gate > 4) throw std::runtime_error("CpuExperts: gate code 2 (SwiGLU), 3 (GeGLU) or 4 (OAI)");
+  }
+
+  void set_layer(int64_t layer, int64_t e0, int64_t n, torch::Tensor gate_up, int64_t qt_gu, torch::Tensor down,
+                 int64_t qt_dn, c10::optional<torch::Tensor> bias_gu, c10::optional<torch::Tensor> bias_dn) {
+    if (!(layer >= 0 && layer < (int64_t)layers_.size()))
+      throw std::runtime_error("CpuExperts: layer");
+    L& l = layers_[layer];
+    l.e0 = (int)e0;
+    l.n = (int)n;
+    load(l.gu, gate_up, (int)qt_gu, (int)(n * 2 * f_), d_);
+    load(l.dn, down, (int)qt_dn, (int)(n * d_), f_);
+    l.bgu.clear();
+    l.bdn.clear();
+    if (bias_gu.has_value()) l.bgu = floats(*bias_gu, n * 2 * f_);
+    if (bias_dn.has_value()) l.bdn = floats(*bias_dn, n * d_);
+  }
+
+  void ffn(int64_t layer, torch::Tensor x, torch::Tensor ids, torch::Tensor wts, torch::Tensor out) {
+    if (!(layer >= 0 && layer < (int64_t)layers_.size() && layers_[layer].n > 0))
+      throw std::runtime_error("CpuExperts: layer not set");
+    const L& l = layers_[layer];
+    if (!(!x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.dim() == 2 &&
+                    x.size(1) == d_))
+      throw std::runtime_error("CpuExperts: x [B, d] f32 on the host");
+    const int B = (int)x.size(0);
+    if (!(ids.scalar_type() == torch::kInt32 && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == B))
+      throw std::runtime_error("CpuExperts: ids [B, k] int32");
+    if (!(wts.scalar_type() == torch::kFloat32 && wts.is_contiguous() && wts.sizes() == ids.sizes()))
+      throw std::runtime_error("CpuExperts: wts [B, k] f32");
+    if (!(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.sizes() == x.sizes()))
+      throw std::runtime_error("CpuExperts: out [B, d] f32");
+    const int k = (int)ids.size(1);
+    const int* id = ids.data_ptr<int>();
+    const float* w = wts.data_ptr<float>();
+    const float* xp = x.data_ptr<float>();
+    float* op = out.data_ptr<float>();
+    py::gil_scoped_release nogil;
+    std::vector<int> pb, pe;   // (token, local expert) of every slot routed into the band
+    std::vector<float> pw;
+    for (int b = 0; b < B; b++)
+      for (int j = 0; j < k; j++) {
+        const int e = id[b * k + j] - l.e0;
+        if (e >= 0 && e < l.n) {
+          pb.push_back(b);
+          pe.push_back(e);
+          pw.push_back(w[b * k + j]);
+        }
+      }
+    const int P = (int)pb.size();
+    if (P == 0) return;
+    std::vector<QAct> qx(act_quant_ ? B : 0);
+    for (int b = 0; b < (int)qx.size(); b++) qx[b].build(xp + (int64_t)b * d_, d_);
+    // gate/up rows of every routed pair, then the gated product
+    const int R = 2 * f_;
+    std::vector<float> gu((size_t)P * R), h((size_t)P * f_), y((size_t)P * d_);
+    pool().parallel_for((int64_t)P * R, [&](int64_t i0, int64_t i1) {
+      std::vector<float> tmp(d_);
+      for (int64_t i = i0; i < i1; i++) {
+        const int p = (int)(i / R), r = (int)(i % R);
+        const int64_t row = (int64_t)pe[p] * R + r;
+        float v = dot(l.gu, row, xp + (int64_t)pb[p] * d_, act_quant_ ? &qx[pb[p]] : nullptr, tmp.data());
+        if (!l.bgu.empty()) v += l.bgu[row];
+        gu[(size_t)i] = v;
+      }
+    });
+    for (int p = 0; p < P; p++)
+      for (int c = 0; c < f_; c++) {
+        const int blk = c / 8, off = c % 8;
+        const float g = gu[(size_t)p * R + blk * 16 + off], u = gu[(size_t)p * R + blk * 16 + 8 + off];
+        h[(size_t)p * f_ + c] = gated(g, u);
+      }
+    std::vector<QAct> qh(act_quant_ ? P : 0);
+    for (int p = 0; p < (int)qh.size(); p++) qh[p].build(h.data() + (size_t)p * f_, f_);
+    pool().parallel_for((int64_t)P * d_, [&](int64_t i0, int64_t i1) {
+      std::vector<float> tmp(f_);
+      for (int64_t i = i0; i < i1; i++) {
+        const int p = (int)(i / d_), r = (int)(i % d_);
+        const int64_t row = (int64_t)pe[p] * d_ + r;
+        float v = dot(l.dn, row, h.data() + (size_t)p * f_, act_quant_ ? &qh[p] : nullptr, tmp.data());
+        if (!l.bdn.empty()) v += l.bdn[row];
+        y[(size_t)i] = v;
+      }
+    });
+    for (int p = 0; p < P; p++) {   // slots in (token, slot) order
+      float* o = op + (int64_t)pb[p] * d_;
+      for (int c = 0; c < d_; c++) o[c] += pw[p] * y[(size_t)p * d_ + c];
+    }
+  }
+
+  int64_t bytes() const {
+    int64_t n = 0;
+    for (const L& l : layers_) n += (int64_t)l.gu.raw.size() + (int64_t)l.dn.raw.size();
+    return n;
+  }
+
+ private:
+  struct L {
+    int e0 = 0, n = 0;
+    Mat gu, dn;
+    std::vector<float> bgu, bdn;
+  };
+
+  static void load(Mat& m, const torch::Tensor& t, int qt, int rows, int cols) {
+    if (t.is_cuda() || t.scalar_type() != torch::kUInt8 || !t.is_contiguous())
+      throw std::runtime_error("CpuExperts: host uint8 rows");
+    const int64_t rb = row_bytes_of(qt, cols);
+    if (t.numel() != (int64_t)rows * rb)
+      throw std::runtime_error("CpuExperts: expected " + std::to_string(rows) + " rows of " + std::to_string(rb) +
+                               " bytes");
+    m.qt = qt;
+    m.rows = rows;
+    m.cols = cols;
+    m.row_bytes = rb;
+    m.raw.assign(t.data_ptr<uint8_t>(), t.data_ptr<uint8_t>() + t.numel());
+  }
+  static std::vector<float> floats(const torch::Tensor& t, int64_t n) {
+    if (t.is_cuda() || t.scalar_type() != torch::kFloat32 || !t.is_contiguous() || t.numel() != n)
+      throw std::runtime_error("CpuExperts: bias of " + std::to_string(n) + " host floats");
+    return std::vector<float>(t.data_ptr<float>(), t.data_ptr<float>() + n);
+  }
+  // one row of m dotted with x: int8 x int8 per 32-block for Q8_0 rows when the activations are
+  // quantized, else the row dequantized and dotted in double
+  static float dot(const Mat& m, int64_t r, const float* x, const QAct* qa, float* tmp) {
+    const uint8_t* row = m.raw.data() + r * m.row_bytes;
+    if (qa && m.qt == Q8_0) {
+      float acc = 0.f;
+      for (int b = 0; b < m.cols / 32; b++) {
+        const uint8_t* blk = row + b * 34;
+        const int8_t* wq = reinterpret_cast<const int8_t*>(blk + 2);
+        const int8_t* xq = qa->q.data() + b * 32;
+        int s = 0;
+        for (int i = 0; i < 32; i++) s += (int)wq[i] * (int)xq[i];
+        acc += h2f(rd16(blk)) * qa->d[b] * (float)s;
+      }
+      return acc;
+    }
+    dequant_row(m, (int)r, tmp);
+    double acc = 0.0;
+    for (int i = 0; i < m.cols; i++) acc += (double)tmp[i] * (double)x[i];
+    return (float)acc;
+  }
+  float gated(float g, float u) const {
+    if (gate_ == 4) {   // gpt-oss: alpha 1.702, limit 7
+      g = std::min(g, 7.f);
+      u = std::min(std::max(u, -7.f), 7.f);
+      return (u + 1.f) * g / (1.f + std::exp(-1.702f * g));
+    }
+    if (gate_ == 3) {   // GELU, tanh form
+      const float t = std::tanh(0.7978845608f * (g + 0.044715f * g * g * g));
+      return 0.5f * g * (1.f + t) * u;
+    }
+    return g / (1.f + std::exp(-g)) * u;
+  }
+
+  int d_, f_, gate_;
+  bool act_quant_;
+  std::vector<L> layers_;
+};
+
 void register_radix(py::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -438,5 +610,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("step", &CpuModel::step, py::call_guard<py::gil_scoped_release>())
       .def("generate", &CpuModel::generate, py::call_guard<py::gil_scoped_release>())
       .def("threads", &CpuModel::threads);
+  py::class_<CpuExperts>(m, "CpuExperts")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, bool>(), py::arg("n_layers"), py::arg("d"), py::arg("f"),
+           py::arg("gate"), py::arg("act_quant") = true)
+      .def("set_layer", &CpuExperts::set_layer, py::arg("layer"), py::arg("e0"), py::arg("n"), py::arg("gate_up"),
+           py::arg("qt_gu"), py::arg("down"), py::arg("qt_dn"), py::arg("bias_gu") = py::none(),
+           py::arg("bias_dn") = py::none())
+      .def("ffn", &CpuExperts::ffn)
+      .def("bytes", &CpuExperts::bytes);
   register_radix(m);
 }

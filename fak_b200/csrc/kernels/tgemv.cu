@@ -546,21 +546,44 @@ FAK_DEV void ar_finish(const ArPeers& ar, int T, const int (&pend)[AR_PEND], con
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
       float v[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int r = 0; r < ar.W; r++) {
-        const uint4* src = ar_line(ar, ar.me, T, ep, r, tile, nt, lane);
-        uint4 a, b;
+      // RP ranks' lines in flight at a time (two; one for wider token tiles: registers), each
+      // polled until both its lines carry this epoch, then added in rank order
+      constexpr int RP = NT == 1 ? 2 : 1;
+      for (int r0 = 0; r0 < ar.W; r0 += RP) {
+        const int nr = min(RP, ar.W - r0);
+        const uint4* src[RP];
+        uint4 l[RP][2];
+#pragma unroll
+        for (int j = 0; j < RP; j++) {
+          src[j] = ar_line(ar, ar.me, T, ep, j < nr ? r0 + j : r0, tile, nt, lane);
+          l[j][0] = ll_load(src[j]);
+          l[j][1] = ll_load(src[j] + 1);
+        }
+        auto ready = [&]() {
+          bool ok = true;
+#pragma unroll
+          for (int j = 0; j < RP; j++)
+            ok = ok && l[j][0].y == ep && l[j][0].w == ep && l[j][1].y == ep && l[j][1].w == ep;
+          return ok;
+        };
         uint32_t it = 0;
-        while (true) {
-          a = ll_load(src);
-          b = ll_load(src + 1);
-          if (a.y == ep && a.w == ep && b.y == ep && b.w == ep) break;
+        while (!ready()) {
           if (++it > ar.spin) {
             report_error(err, 4);
             break;
           }
+#pragma unroll
+          for (int j = 0; j < RP; j++) {
+            l[j][0] = ll_load(src[j]);
+            l[j][1] = ll_load(src[j] + 1);
+          }
         }
-        v[0] += __uint_as_float(a.x); v[1] += __uint_as_float(a.z);
-        v[2] += __uint_as_float(b.x); v[3] += __uint_as_float(b.z);
+#pragma unroll
+        for (int j = 0; j < RP; j++)
+          if (j < nr) {
+            v[0] += __uint_as_float(l[j][0].x); v[1] += __uint_as_float(l[j][0].z);
+            v[2] += __uint_as_float(l[j][1].x); v[3] += __uint_as_float(l[j][1].z);
+          }
       }
       epilogue(tile, v, 8 * nt, lane, N, B, y, ldy, bias, epi);
     }
@@ -831,20 +854,19 @@ FAK_DEV void tgemv_cta(const int bid, const TgArgs& a) {
           float v[4] = {0.f, 0.f, 0.f, 0.f};
           const float4* src = reinterpret_cast<const float4*>(part + (size_t)tile * 128 * NT) + 32 * nt + lane;
           const size_t sstride = (size_t)geo.T * 128 * NT / 4;   // float4s between slices
-          int s = 0;
-          // eight slices' partials in flight at once (one L2 round trip per eight), added in order
-          for (; s + 8 <= geo.S; s += 8) {
-            float4 p[8];
+          // up to SB slices' partials in flight at once (one L2 round trip per SB, a split of fewer
+          // slices included), added in slice order; wider token tiles keep fewer in flight (registers)
+          constexpr int SB = NT == 1 ? 8 : 4;
+          for (int s = 0; s < geo.S; s += SB) {
+            float4 p[SB];
 #pragma unroll
-            for (int u = 0; u < 8; u++) p[u] = __ldcg(src + (size_t)(s + u) * sstride);
+            for (int u = 0; u < SB; u++)
+              if (s + u < geo.S) p[u] = __ldcg(src + (size_t)(s + u) * sstride);
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-              v[0] += p[u].x; v[1] += p[u].y; v[2] += p[u].z; v[3] += p[u].w;
-            }
-          }
-          for (; s < geo.S; s++) {
-            const float4 p = __ldcg(src + (size_t)s * sstride);
-            v[0] += p.x; v[1] += p.y; v[2] += p.z; v[3] += p.w;
+            for (int u = 0; u < SB; u++)
+              if (s + u < geo.S) {
+                v[0] += p[u].x; v[1] += p[u].y; v[2] += p[u].z; v[3] += p[u].w;
+              }
           }
           acc[nt][0] = v[0]; acc[nt][1] = v[1]; acc[nt][2] = v[2]; acc[nt][3] = v[3];
         }

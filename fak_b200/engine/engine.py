@@ -102,11 +102,20 @@ class Engine:
                 from ..parallel.tp import NcclTP
                 collectives = NcclTP(tp_group, weights, self.ecfg.max_batch, self.device)
         self.tp_group = tp_group
+        offload = None
+        if any(L.experts_gate_up is not None and not L.experts_gate_up.buf.is_cuda for L in weights.layers):
+            # experts in host memory: their FFNs run on the CPU, which syncs the step with the host at
+            # every MoE layer, so no CUDA graphs and no device-resident decode loop
+            if weights.tp_size > 1:
+                raise NotImplementedError("MoE expert offload runs one GPU per replica (no TP / EP)")
+            from ..models.moe_offload import ExpertOffload
+            offload = ExpertOffload(weights)
+            self.ecfg = dataclasses.replace(self.ecfg, cuda_graph=False, async_decode=False)
         self.runner = ModelRunner(weights, self.kv, max_batch=self.ecfg.max_batch,
                                   max_prefill_tokens=self.ecfg.max_prefill_tokens, max_context=self.max_context,
                                   collectives=collectives, fused_activations=self.ecfg.fused_activations,
                                   attention_merge=self.ecfg.attention_merge, l2_prefetch=self.ecfg.l2_prefetch,
-                                  cascade_attention=self.ecfg.cascade_attention)
+                                  cascade_attention=self.ecfg.cascade_attention, expert_offload=offload)
         self.bt_width = math.ceil(self.max_context / ps)
         if self.ecfg.debug_poison:
             self._poison()
@@ -165,7 +174,8 @@ class Engine:
                   **kw) -> "Engine":
         r, n = cls._tp(tp_group)
         w = load_weights(cls._with_lora(gguf_source(path), lora), device, tp_rank=r, tp_size=n,
-                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
+                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights,
+                         offload_experts=(ecfg or EngineConfig()).cpu_offload_experts)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 
     @classmethod
@@ -178,7 +188,8 @@ class Engine:
         src = hf_source(model_dir)
         cls._check_device(src[0])
         w = load_weights(cls._with_lora(src, lora), device, tp_rank=r, tp_size=n,
-                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights)
+                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights,
+                         offload_experts=(ecfg or EngineConfig()).cpu_offload_experts)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 
     @classmethod
@@ -189,7 +200,8 @@ class Engine:
         cls._check_device(cfg)
         r, n = cls._tp(tp_group)
         w = load_weights(synthetic_source(cfg, mix, seed, std=std, device=str(device)), device, tp_rank=r, tp_size=n,
-                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights, repeat_layers=repeat_layers)
+                         prefill_dense=(ecfg or EngineConfig()).prefill_bf16_weights, repeat_layers=repeat_layers,
+                         offload_experts=(ecfg or EngineConfig()).cpu_offload_experts)
         return cls(w, ecfg, device, tp_group=tp_group, **kw)
 
     def shutdown(self) -> None:

@@ -91,6 +91,9 @@ def _grouped_ffn(rn, L, st: MoEState, n_tok: int, act) -> None:
 
 
 def moe_decode(rn, i: int, B: int) -> None:
+    if rn.expert_offload is not None:   # experts in host memory: their FFNs run on the CPU
+        rn.expert_offload.decode(rn, i, B)
+        return
     cfg, L, st = rn.cfg, rn.w.layers[i], _state(rn)
     C = ext()
     x = rn.x[:B]
@@ -109,6 +112,9 @@ def moe_decode(rn, i: int, B: int) -> None:
 
 def moe_prefill(rn, i: int, hb: torch.Tensor, x: torch.Tensor) -> None:
     """Per-expert dense GEMMs over the gathered tokens of each local expert (host-side grouping)."""
+    if rn.expert_offload is not None:
+        rn.expert_offload.prefill(rn, i, x)
+        return
     cfg, L = rn.cfg, rn.w.layers[i]
     C = ext()
     T = x.shape[0]

@@ -94,8 +94,11 @@ class PrefillMeta:
 class ModelRunner:
     def __init__(self, weights: ModelWeights, kv: KVCache, max_batch: int = 64, max_prefill_tokens: int = 4096,
                  max_context: int | None = None, collectives=None, fused_activations: bool = False,
-                 attention_merge: bool = False, l2_prefetch: bool = False, cascade_attention: bool = True):
+                 attention_merge: bool = False, l2_prefetch: bool = False, cascade_attention: bool = True,
+                 expert_offload=None):
         self.w = weights
+        # models.moe_offload.ExpertOffload when the MoE experts live in host memory (their FFNs on the CPU)
+        self.expert_offload = expert_offload
         self.cfg: ModelConfig = weights.cfg
         self.kv = kv
         self.coll = collectives

@@ -298,9 +298,13 @@ def _col_block_slice(raw: torch.Tensor, t: int, cols: int, c0: int, c1: int) -> 
 
 def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], device: str | torch.device = "cuda",
                  tp_rank: int = 0, tp_size: int = 1, expert_filter: tuple[int, int] | None = None,
-                 prefill_dense: bool = False, repeat_layers: bool = False) -> ModelWeights:
+                 prefill_dense: bool = False, repeat_layers: bool = False,
+                 offload_experts: bool = False) -> ModelWeights:
     """repeat_layers: load only block 0 and let every layer share it (smoke tests of a large
-    architecture: the same shapes and kernels, one layer's worth of weight synthesis and memory)."""
+    architecture: the same shapes and kernels, one layer's worth of weight synthesis and memory).
+    offload_experts: MoE expert matrices stay in host memory in their GGML blocks (their FFNs run
+    on the CPU, ``models.moe_offload``); a layer's experts pass through the device only while it
+    is converted."""
     import time
     cfg, get0, close = source
     device = torch.device(device)
@@ -391,7 +395,7 @@ def load_weights(source: tuple[ModelConfig, RawGetter, Callable[[], None]], devi
         if cfg.is_moe:
             # expert parallelism rides on the tensor-parallel group: rank r owns a band of experts
             band = expert_filter if expert_filter is not None else expert_slice(cfg.n_experts, tp_rank, tp_size)
-            _load_moe_layer(cfg, get, quant, p, L, device, band)
+            _load_moe_layer(cfg, get, quant, p, L, device, band, offload_experts)
         else:
             gs, gt, graw = quant(p + "ffn_gate.weight")
             us, ut, uraw = quant(p + "ffn_up.weight")
@@ -448,7 +452,7 @@ def expert_slice(E: int, rank: int, size: int) -> tuple[int, int]:
     return min(E, rank * per), min(E, (rank + 1) * per)
 
 
-def _load_moe_layer(cfg, get, quant, p, L: LayerWeights, device, expert_filter) -> None:
+def _load_moe_layer(cfg, get, quant, p, L: LayerWeights, device, expert_filter, offload: bool = False) -> None:
     E, f, d = cfg.n_experts, cfg.expert_ffn_dim, cfg.d_model
     L.router = _vec(get, p + "ffn_gate_inp.weight", device).view(E, d).contiguous()
     e0, e1 = expert_filter if expert_filter is not None else (0, E)
@@ -460,16 +464,20 @@ def _load_moe_layer(cfg, get, quant, p, L: LayerWeights, device, expert_filter) 
     draw = draw.view(E, d, -1)
     # experts stored back to back in one buffer (rows of expert e start at e * rows_per_expert)
     gu = torch.cat([interleave_gate_up(graw[e], uraw[e]) for e in range(e0, e1)])
-    L.experts_gate_up = QuantWeight.from_rows(gu, gt, d, device)
-    L.experts_down = QuantWeight.from_rows(draw[e0:e1].reshape((e1 - e0) * d, -1).contiguous(), dt, f, device)
+    wdev = torch.device("cpu") if offload else device   # where the expert matrices live
+    L.experts_gate_up = QuantWeight.from_rows(gu, gt, d, wdev)
+    L.experts_down = QuantWeight.from_rows(draw[e0:e1].reshape((e1 - e0) * d, -1).contiguous(), dt, f, wdev)
     L.expert_ids = list(range(e0, e1))
     if cfg.moe_bias:   # gpt-oss: router and expert biases
         L.router_bias = _vec(get, p + "ffn_gate_inp.bias", device)
         bg = _vec(get, p + "ffn_gate_exps.bias", device).view(E, f)
         bu = _vec(get, p + "ffn_up_exps.bias", device).view(E, f)
         L.experts_gate_up_bias = torch.cat([interleave_gate_up(bg[e][:, None], bu[e][:, None]).view(-1)
-                                            for e in range(e0, e1)]).contiguous()
-        L.experts_down_bias = _vec(get, p + "ffn_down_exps.bias", device).view(E, d)[e0:e1].reshape(-1).contiguous()
+                                            for e in range(e0, e1)]).contiguous().to(wdev)
+        L.experts_down_bias = _vec(get, p + "ffn_down_exps.bias", device).view(E, d)[e0:e1].reshape(-1) \
+            .contiguous().to(wdev)
+    if offload:
+        return
     if f % 256 == 0 and d % 256 == 0:  # tile-packed copies for the grouped expert GEMV
         L.experts_gate_up.pack()
         L.experts_down.pack()

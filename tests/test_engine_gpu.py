@@ -150,6 +150,29 @@ def test_moe_generation_matches_reference(tmp_path):
     assert min(agree) >= 3, (agree, outs)
 
 
+def test_moe_expert_offload_matches_device_experts(tmp_path):
+    """MoE experts kept in host memory (their FFNs on the CPU, the router / attention / dense layers
+    on the GPU): the same greedy continuations as the all-device engine, up to the int8 rounding
+    of the two expert paths."""
+    path = str(tmp_path / "moe.gguf")
+    write_synthetic_gguf(path, preset("tiny-qwen3moe"), "q8_0", seed=9, std=0.05)
+    dev_eng = _engine(path, graphs=True)
+    off = _engine(path, graphs=False, cpu_offload_experts=True)
+    assert off.runner.expert_offload is not None and off.runner.expert_offload.host_bytes > 0
+    assert all(not L.experts_gate_up.buf.is_cuda for L in off.runner.w.layers if L.experts_gate_up is not None)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, dev_eng.cfg.vocab_size, n).tolist() for n in (30, 12, 50)]
+    want = dev_eng.generate(prompts, max_new_tokens=8)
+    got = off.generate(prompts, max_new_tokens=8)
+    agree = []
+    for o, w in zip(got, want):
+        k = 0
+        while k < len(o) and o[k] == w[k]:
+            k += 1
+        agree.append(k)
+    assert min(agree) >= 3, (agree, got, want)
+
+
 def test_self_speculative_decode_matches_greedy(model_file):
     from fak_b200.engine import Engine
     base = _engine(model_file, graphs=True)
