@@ -83,6 +83,8 @@ def build_model_backend(args):
     from .engine import Engine
     from .serve import EngineBackend
     ecfg = EngineConfig.from_env(max_batch=args.max_batch)
+    if getattr(args, "cpu_offload_experts", False):
+        ecfg.cpu_offload_experts = True
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     if hf:
@@ -124,6 +126,8 @@ def _add_model_args(ap):
                     help="plan each chat prompt as a view of at most this many tokens (0: whole transcript)")
     ap.add_argument("--max-batch", type=int, default=32)
     ap.add_argument("--max-context", type=int, default=8192)
+    ap.add_argument("--cpu-offload-experts", action="store_true",
+                    help="keep MoE expert weights in host memory and run their FFNs on the CPU")
 
 
 def cmd_serve(args) -> int:
