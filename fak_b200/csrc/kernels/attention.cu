@@ -386,9 +386,11 @@ k_decode_attn(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
   // the last split CTA of this (sequence, KV group) merges all splits (same order and arithmetic
   // as k_decode_combine) and leaves its ticket at zero for the next launch
   __shared__ int s_ticket;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_ticket = atomicAdd(&tickets[b * Hkv + kvh], 1);
+  __syncthreads();   // every thread's partial, then one fence ahead of the ticket
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_ticket = atomicAdd(&tickets[b * Hkv + kvh], 1);
+  }
   __syncthreads();
   if (s_ticket != n_split - 1) return;
   __threadfence();

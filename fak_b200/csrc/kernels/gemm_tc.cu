@@ -383,10 +383,13 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.acc_empty[buf]);
       if (epi == G_RS) {
-        // every row of the tile is in the owner's memory before its flag is released
-        __threadfence_system();
+        // every row of the tile is in the owner's memory before its flag is released: the four
+        // epilogue warps meet at a barrier, then ONE thread fences at system scope (cumulative over
+        // the stores the barrier ordered before it) and releases the flag -- one system fence per
+        // tile instead of one per thread
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
+          __threadfence_system();
           const int mb = m0 / BM, nb = n0 / BN, n_n = (N + BN - 1) / BN;
           uint32_t* f = reinterpret_cast<uint32_t*>(rs.base[mb % rs.W] + rs.flags_off) +
                         ((int64_t)mb * n_n + nb) * RS_MAX_W + rs.me;

@@ -28,7 +28,7 @@ using namespace fak;
 namespace {
 
 constexpr int MAX_W = 8;
-constexpr int MAX_CTAS = 64;
+constexpr int MAX_CTAS = 128;
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 FAK_DEV void st_release_sys(uint32_t* p, uint32_t v) {
@@ -238,9 +238,12 @@ __global__ void k_sp_rmsnorm_shard(Peers P, const float* __restrict__ x_local, c
       *reinterpret_cast<uint2*>(shard + (int64_t)lr * N + c) = pk;
     }
   }
-  __threadfence_system();
+  // the CTA barrier orders every thread's rows before the releasing threads' system fences
   __syncthreads();
-  if (threadIdx.x < W) st_release_sys(reinterpret_cast<uint32_t*>(P.base[threadIdx.x] + flags_off) + mb, epoch);
+  if (threadIdx.x < W) {
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<uint32_t*>(P.base[threadIdx.x] + flags_off) + mb, epoch);
+  }
   pdl_launch_dependents();
 }
 
@@ -259,11 +262,12 @@ __global__ void k_p2p_rs_push(Peers P, const float* __restrict__ part, int M, in
       const float4 v = *reinterpret_cast<const float4*>(part + (int64_t)(mb * RS_BM + rr) * N + c);
       *reinterpret_cast<float4*>(dst + ((int64_t)me * MR + (mb / W) * RS_BM + rr) * N + c) = v;
     }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0)
+    __syncthreads();   // every thread's rows of the tile, then one system fence and the flag
+    if (threadIdx.x == 0) {
+      __threadfence_system();
       st_release_sys(reinterpret_cast<uint32_t*>(P.base[owner] + flags_off) + ((int64_t)mb * n_n + nb) * MAX_W + me,
                      epoch);
+    }
   }
   pdl_launch_dependents();
 }
@@ -427,7 +431,7 @@ void p2p_allgather_cols(torch::Tensor peers, torch::Tensor src, int64_t src_ld, 
                 "allgather: 16-byte granularity");
   };
   check(ncols, col0, src_ld, dst_ld, dst_off);
-  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allgather: 1..64 CTAs");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allgather: 1..128 CTAs");
   AgSeg s0{(const uint8_t*)src.data_ptr(), src_ld, dst_off, dst_ld, col0, ncols};
   AgSeg s1 = s0;
   int nseg = 1;
@@ -449,7 +453,7 @@ void p2p_allreduce_add(torch::Tensor peers, int64_t part_off, torch::Tensor x, i
   const int W = (int)peers.numel();
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.numel() >= n && n % 4 == 0, "x");
   TORCH_CHECK(part_off % 16 == 0, "partials must be 16-byte aligned");
-  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allreduce: 1..64 CTAs");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "allreduce: 1..128 CTAs");
   Peers P = make_peers(peers, spin_limit);
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_cfg(dim3((unsigned)ctas), dim3(256), attr);
@@ -464,7 +468,7 @@ void p2p_rs_reduce(torch::Tensor peers, int64_t parts_off, int64_t flags_off, in
                    torch::Tensor err, int64_t ctas, int64_t spin_limit, c10::optional<torch::Tensor> x_local) {
   const int W = (int)peers.numel();
   TORCH_CHECK(N % 4 == 0 && parts_off % 16 == 0 && x_off % 16 == 0 && flags_off % 4 == 0, "rs_reduce: alignment");
-  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "rs_reduce: 1..64 CTAs");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "rs_reduce: 1..128 CTAs");
   TORCH_CHECK(MR >= ((M + RS_BM - 1) / RS_BM + W - 1) / W * RS_BM, "rs_reduce: MR");
   if (M == 0) return;
   Peers P = make_peers(peers, spin_limit);
@@ -522,11 +526,11 @@ void p2p_argmax(torch::Tensor peers, torch::Tensor logits, int64_t Vl, int64_t v
                 int64_t me, torch::Tensor err, int64_t spin_limit) {
   const int W = (int)peers.numel();
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.stride(1) == 1, "logits");
-  TORCH_CHECK(B >= 1 && B <= MAX_CTAS, "argmax: batch 1..64");
+  TORCH_CHECK(B >= 1 && B <= MAX_CTAS, "argmax: batch 1..128");
   TORCH_CHECK(cand_off % 16 == 0, "argmax: candidate slots 16-byte aligned");
   TORCH_CHECK(keys.scalar_type() == torch::kInt64 && keys.numel() >= B && tickets.scalar_type() == torch::kInt32 &&
                   tickets.numel() >= B, "argmax: keys [B] int64, tickets [B] int32");
-  TORCH_CHECK(epochs.scalar_type() == torch::kInt32 && epochs.numel() >= MAX_CTAS, "argmax: epochs [64] int32");
+  TORCH_CHECK(epochs.scalar_type() == torch::kInt32 && epochs.numel() >= MAX_CTAS, "argmax: epochs [128] int32");
   TORCH_CHECK(v_off >= 0 && v_off + Vl < 0xFFFFFFFFll, "argmax: ids fit 32 bits");
   Peers P = make_peers(peers, spin_limit);
   const int chunk = kArgmaxThreads * kArgmaxPer * 4;
@@ -552,7 +556,7 @@ void p2p_moe_combine_ar(torch::Tensor peers, torch::Tensor out, torch::Tensor id
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.size(0) >= B, "moe_combine_ar: x");
   TORCH_CHECK(ids.scalar_type() == torch::kInt32 && wts.scalar_type() == torch::kFloat32, "moe_combine_ar: ids / wts");
   TORCH_CHECK(parts_off % 16 == 0 && (parity == 0 || parity == 1), "moe_combine_ar: parts layout");
-  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "moe_combine_ar: 1..64 CTAs");
+  TORCH_CHECK(ctas >= 1 && ctas <= MAX_CTAS, "moe_combine_ar: 1..128 CTAs");
   if (B <= 0) return;
   Peers P = make_peers(peers, spin_limit);
   cudaLaunchAttribute attr[1];

@@ -841,10 +841,14 @@ FAK_DEV void tgemv_cta(const int bid, const TgArgs& a) {
       float4* mine = reinterpret_cast<float4*>(part + ((size_t)slice * geo.T + tile) * 128 * NT) + lane;
 #pragma unroll
       for (int nt = 0; nt < NT; nt++) mine[32 * nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-      __threadfence();
+      // the warp barrier orders every lane's partial before lane 0's fence, which then covers them
+      // all (one fence per warp, not one per lane) ahead of the ticket
       __syncwarp();
       int old = 0;
-      if (lane == 0) old = atomicAdd(&cnt[tile], 1);
+      if (lane == 0) {
+        __threadfence();
+        old = atomicAdd(&cnt[tile], 1);
+      }
       old = __shfl_sync(0xffffffffu, old, 0);
       have = old == geo.S - 1;
       if (have) {  // last slice of this tile: reduce in slice order

@@ -42,7 +42,7 @@ from ..ops import kernels as K
 from ..ops._ext import ext
 from .tp import NcclTP
 
-MAX_CTAS = 64
+MAX_CTAS = 128
 MAX_W = 8
 
 
@@ -52,7 +52,7 @@ def ar_slot_bytes(tiles: int) -> int:
     return 2 * MAX_W * tiles * 4 * 32 * 32
 AR_CTAS = 16
 AG_CTAS = 16
-RS_CTAS = 64
+RS_CTAS = 128
 
 
 def _align(n: int, a: int = 256) -> int:
