@@ -536,7 +536,6 @@ void gemm_bf16_rs(torch::Tensor a, torch::Tensor b, torch::Tensor peers, int64_t
 // Sequence-parallel prefill GEMM: out (op)= A . B^T with A's m-blocks gathered from their owners'
 // normalised shards (see AgMaps).  peers: int64 [W] peer-buffer bases; shard_off: the [MR, K] bf16
 // shard in every buffer; flags_off: this rank's release flags [m-blocks]; M: rows of A and out.
-// With rs_parts_off >= 0 the epilogue is the reduce-scatter of G_RS instead (out unused).
 void gemm_bf16_ag(int64_t M, torch::Tensor b, torch::Tensor out, torch::Tensor peers, int64_t me, int64_t shard_off,
                   int64_t MR, int64_t flags_off, int64_t epoch, int64_t spin, c10::optional<torch::Tensor> bias,
                   int64_t epi, c10::optional<torch::Tensor> err) {
