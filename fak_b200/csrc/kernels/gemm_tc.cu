@@ -11,15 +11,12 @@
 // No TMA multicast is used, so the kernel is safe on multi-GPU runs.  The persistent variant
 // (default) keeps two TMEM accumulators so each CTA's epilogue overlaps its next tile's MMAs.
 //
-// G_RS (persistent variant, tensor-parallel prefill): the first half of an all-reduce in the
-// epilogue.  Output m-block mb belongs to rank mb % W; each fp32 tile is stored into this rank's
-// OWN peer buffer (partial [row][column]) and, once all 128 rows of the tile are written and
-// fenced system-wide, a tile flag on the owner is released with the call's epoch.  The owner's
-// k_p2p_rs_reduce then pulls the W partials of its tiles over NVLink (coalesced peer loads), sums
-// them into the residual and broadcasts it.  The tiles are stored locally rather than pushed to the
-// owner because the epilogue's row-per-thread stores crossed NVLink at about 150 GB/s (the GEMM
-// took 86 us instead of 25 us at 1280 x 3584 x 1792 over two ranks), while the reduce kernel's
-// float4-per-thread peer loads are coalesced.
+// G_RS (persistent variant, tensor-parallel prefill): the reduce-scatter half of an all-reduce in
+// the epilogue.  Output m-block mb belongs to rank mb % W; each fp32 tile is stored straight into
+// the owner's peer buffer (slot [this rank][owner-local row][column]) and, once all 128 rows of the
+// tile are written and fenced system-wide, a tile flag on the owner is released with the call's
+// epoch.  The owner's k_p2p_rs_reduce then sums the W partials into the residual and broadcasts
+// it, so the partials cross NVLink tile by tile while later tiles are still being computed.
 #include <torch/extension.h>
 #include <c10/cuda/CUDAStream.h>
 #include <cudaTypedefs.h>
@@ -47,7 +44,7 @@ __device__ __forceinline__ int gate_code(int epi) { return epi == G_OAI ? 4 : ep
 constexpr int RS_MAX_W = 8;
 struct RsPeers {
   uint8_t* base[RS_MAX_W];   // every rank's peer buffer
-  int64_t parts_off;         // this rank's partial [M][N] fp32 (in its own buffer)
+  int64_t parts_off;         // partial slots [W][MR][N] fp32
   int64_t flags_off;         // tile flags [m-block][n-block][RS_MAX_W] uint32
   int W, me, MR;             // ranks, this rank, owner-local rows per source slot
   uint32_t epoch;            // this call's flag value
@@ -372,8 +369,11 @@ k_gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmap_a, const __grid_
             for (int j = 0; j < 8; j++)
               if (col0 + j + 8 < N) store_val(p + j, o[j]);
           }
-        } else if (epi == G_RS) {   // this rank's partial, in its own peer buffer
-          float* dst = reinterpret_cast<float*>(rs.base[rs.me] + rs.parts_off) + (int64_t)row * N + col0;
+        } else if (epi == G_RS) {
+          const int mb = m0 / BM;
+          const int lr = (mb / rs.W) * BM + quarter * 32 + lane;   // row inside the owner's slot
+          float* dst = reinterpret_cast<float*>(rs.base[mb % rs.W] + rs.parts_off) +
+                       ((int64_t)rs.me * rs.MR + lr) * N + col0;
           store16<float>(dst, v, false, min(16, N - col0));
         } else {
           store16<OutT>(out + (int64_t)row * ldo + col0, v, epi == G_ADD, min(16, N - col0));
@@ -500,10 +500,10 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optiona
     TORCH_CHECK(false, "out must be float32 or bfloat16");
 }
 
-// Tensor-parallel prefill: C = A . B^T with the first half of the all-reduce in the epilogue (G_RS
-// above).  peers: int64 [W] base addresses of every rank's peer buffer; the owner rank of m-block
-// mb is mb % W; the partial region at parts_off holds W * MR rows (MR >= ceil(m-blocks / W) * 128,
-// so at least M).  N must be a multiple of 4.  k_p2p_rs_reduce (p2p.cu) completes the all-reduce.
+// Tensor-parallel prefill: C = A . B^T with the reduce-scatter half of the all-reduce in the
+// epilogue (G_RS above).  peers: int64 [W] base addresses of every rank's peer buffer; the owner
+// rank of m-block mb is mb % W and holds MR rows per source slot (MR >= ceil(m-blocks / W) * 128).
+// N must be a multiple of 4.  k_p2p_rs_reduce (p2p.cu) completes the all-reduce.
 void gemm_bf16_rs(torch::Tensor a, torch::Tensor b, torch::Tensor peers, int64_t me, int64_t parts_off,
                   int64_t flags_off, int64_t MR, int64_t epoch, c10::optional<torch::Tensor> err) {
   TORCH_CHECK(a.is_cuda() && a.scalar_type() == torch::kBFloat16 && a.dim() == 2 && a.stride(1) == 1, "a: [M,K] bf16");

@@ -126,14 +126,13 @@ __global__ void k_p2p_allreduce_add(Peers P, int64_t part_off, float* __restrict
 
 // ---- prefill all-reduce: reduce + broadcast of owned tiles ----------------------------------
 // The [M, N] fp32 output is cut into 128-row m-blocks and 256-column n-blocks; rank mb % W owns
-// m-block mb.  Every rank has stored its partial [M, N] into its OWN peer buffer at parts_off and
-// released the tile flag flags[mb][nb][src] on the owner with this call's epoch (the G_RS epilogue
-// of gemm_tc.cu, or k_p2p_rs_push below).  For each owned tile, in the order the tiles are
-// produced, a CTA waits (bounded) for the W flags, pulls the W partials (coalesced peer loads),
-// adds them in rank order to the residual x (a [M, N] fp32 array in every rank's peer buffer at
-// x_off) and stores the sum into x on every rank; a cross-rank barrier per CTA then orders all
-// broadcasts before the kernel ends, so every rank's x holds the full reduced rows -- and no rank
-// overwrites its partial (the next call's GEMM) while another still reads it.
+// m-block mb.  Every rank has stored its partial of each tile into the owner's slot
+// parts[src][owner-local row][N] and released the tile flag flags[mb][nb][src] with this call's
+// epoch (the G_RS epilogue of gemm_tc.cu, or k_p2p_rs_push below).  For each owned tile, in the
+// order the tiles are produced, a CTA waits (bounded) for the W flags, adds the partials in rank
+// order to the residual x (a [M, N] fp32 array in every rank's peer buffer at x_off) and stores the
+// sum into x on every rank; a cross-rank barrier per CTA then orders all broadcasts before the
+// kernel ends, so every rank's x holds the full reduced rows.
 constexpr int RS_BM = 128, RS_BN = 256;
 
 FAK_DEV bool wait_flag_ge(const uint32_t* f, uint32_t v, uint32_t spin, int* err) {
@@ -156,6 +155,7 @@ __global__ void __launch_bounds__(1024) k_p2p_rs_reduce(Peers P, int64_t parts_o
   const int n_m = (M + RS_BM - 1) / RS_BM, n_n = (N + RS_BN - 1) / RS_BN;
   const int own = me < n_m ? (n_m - 1 - me) / W + 1 : 0;   // owned m-blocks me, me + W, ...
   const uint8_t* mine = P.base[me];
+  const float* parts = reinterpret_cast<const float*>(mine + parts_off);
   const float* xl = reinterpret_cast<const float*>(mine + x_off);
   for (int it = blockIdx.x; it < own * n_n; it += gridDim.x) {
     const int k = it % own, nb = it / own, mb = me + k * W;
@@ -175,14 +175,14 @@ __global__ void __launch_bounds__(1024) k_p2p_rs_reduce(Peers P, int64_t parts_o
         const int e = min(e0 + u * (int)blockDim.x, n4 - 1);   // tail lanes repeat the last element
         const int rr = e / cols4, c = nb * RS_BN + 4 * (e - rr * cols4);
         xi[u] = x_local ? (int64_t)(k * RS_BM + rr) * N + c : (int64_t)(mb * RS_BM + rr) * N + c;
-        pi[u] = (int64_t)(mb * RS_BM + rr) * N + c;   // the partials' row: the global row
+        pi[u] = (int64_t)(k * RS_BM + rr) * N + c;
         acc[u] = *reinterpret_cast<const float4*>((x_local ? x_local : xl) + xi[u]);
       }
       for (int r = 0; r < W; r++) {
         float4 v[4];
 #pragma unroll
         for (int u = 0; u < 4; u++)
-          v[u] = __ldcg(reinterpret_cast<const float4*>(P.base[r] + parts_off) + pi[u] / 4);
+          v[u] = __ldcg(reinterpret_cast<const float4*>(parts + (int64_t)r * MR * N + pi[u]));
 #pragma unroll
         for (int u = 0; u < 4; u++) {
           acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
@@ -247,21 +247,20 @@ __global__ void k_sp_rmsnorm_shard(Peers P, const float* __restrict__ x_local, c
   pdl_launch_dependents();
 }
 
-// The first half for a partial that is not produced by a GEMM epilogue: part [M, N] fp32 (local) is
-// copied tile by tile into this rank's partial region, each tile's flag released on its owner after
-// its rows.
-__global__ void k_p2p_rs_push(Peers P, const float* __restrict__ part, int M, int N, int64_t parts_off,
+// The reduce-scatter half for a partial that is not produced by a GEMM epilogue: part [M, N] fp32
+// (local) is copied tile by tile into the owners' slots, each tile's flag released after its rows.
+__global__ void k_p2p_rs_push(Peers P, const float* __restrict__ part, int M, int N, int MR, int64_t parts_off,
                               int64_t flags_off, int me, int W, uint32_t epoch) {
   pdl_wait();
   const int n_m = (M + RS_BM - 1) / RS_BM, n_n = (N + RS_BN - 1) / RS_BN;
   for (int t = blockIdx.x; t < n_m * n_n; t += gridDim.x) {
     const int mb = t % n_m, nb = t / n_m, owner = mb % W;
-    float* dst = reinterpret_cast<float*>(P.base[me] + parts_off);
+    float* dst = reinterpret_cast<float*>(P.base[owner] + parts_off);
     const int rows = min(RS_BM, M - mb * RS_BM), cols4 = min(RS_BN, N - nb * RS_BN) >> 2;
     for (int e = threadIdx.x; e < rows * cols4; e += blockDim.x) {
       const int rr = e / cols4, c = nb * RS_BN + 4 * (e - rr * cols4);
-      const int64_t i = (int64_t)(mb * RS_BM + rr) * N + c;
-      *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(part + i);
+      const float4 v = *reinterpret_cast<const float4*>(part + (int64_t)(mb * RS_BM + rr) * N + c);
+      *reinterpret_cast<float4*>(dst + ((int64_t)me * MR + (mb / W) * RS_BM + rr) * N + c) = v;
     }
     __syncthreads();   // every thread's rows of the tile, then one system fence and the flag
     if (threadIdx.x == 0) {
@@ -515,7 +514,7 @@ void p2p_rs_push(torch::Tensor peers, torch::Tensor part, int64_t MR, int64_t pa
   const int tiles = ((M + RS_BM - 1) / RS_BM) * ((N + RS_BN - 1) / RS_BN);
   cudaLaunchAttribute attr[1];
   auto cfg = pdl_cfg(dim3((unsigned)std::min(tiles, 148)), dim3(256), attr);
-  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_rs_push, P, (const float*)part.data_ptr<float>(), M, N,
+  FAK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, k_p2p_rs_push, P, (const float*)part.data_ptr<float>(), M, N, (int)MR,
                                     parts_off, flags_off, (int)me, W, (uint32_t)epoch));
 }
 

@@ -21,12 +21,12 @@ all-gather of the attention output (each rank streams only its slice of o_proj).
 tokens fall back to the GEMV + one-shot all-reduce kernel pair.  Greedy decoding ends with a
 distributed argmax instead of gathering 152k logits.
 
-Prefill can all-reduce both row-parallel projections (and the MoE expert sum) without NCCL
-(``FAK_PREFILL_P2P=1``): the tcgen05 GEMM's epilogue stores each 128 x 256 fp32 output tile into
-this rank's partial region and releases a tile flag on the tile's owner (owner = m-block mod W;
-``gemm_tc.cu`` ``G_RS``), and the owner's ``k_p2p_rs_reduce`` pulls the W partials of its tiles,
-adds them to the residual and stores the rows into every rank's residual (the all-gather half),
-which for that reason lives in the peer buffer (``prefill_x``).
+Prefill all-reduces both row-parallel projections (and the MoE expert sum) without NCCL: the
+tcgen05 GEMM's epilogue stores each 128 x 256 fp32 output tile into the owner rank's slot (owner =
+m-block mod W, the reduce-scatter half; ``gemm_tc.cu`` ``G_RS``) and releases a tile flag, and the
+owner's ``k_p2p_rs_reduce`` adds the W partials to the residual and stores the rows into every
+rank's residual (the all-gather half), which for that reason lives in the peer buffer
+(``prefill_x``) -- the partials cross NVLink tile by tile while the GEMM computes later tiles.
 
 Every wait is bounded (``spin_limit`` polls; 0 = the kernels' default of about a second) and writes
 an error word the engine reads back with each step's tokens (``engine.Engine._collect``).
@@ -126,8 +126,8 @@ class P2PTP(NcclTP):
         # MoE combine fused with the expert-parallel all-reduce: [2 layer parities][W][B * d] partials
         self.moe_off = off
         off = _align(off + (2 * self.world * B * d * 4 if cfg.is_moe else 0))
-        # prefill all-reduce: the residual [T, d], this rank's partial [W * MR >= T rows][d] (MR rows
-        # of owned 128-row m-blocks per rank) and tile flags [m-block][256-column block][MAX_W]
+        # prefill all-reduce: the residual [T, d], partial slots [W][MR][d] (MR rows of owned
+        # 128-row m-blocks per source rank) and tile flags [m-block][256-column block][MAX_W]
         Tp = max(0, int(max_prefill_tokens))
         # the fused prefill all-reduce is opt-in: at TP=2 on Qwen2.5-7B it measured TTFT p50 30.5-30.9 ms
         # against 28.6 ms with NCCL's all-reduce for the same turns
