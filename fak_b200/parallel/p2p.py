@@ -21,12 +21,12 @@ all-gather of the attention output (each rank streams only its slice of o_proj).
 tokens fall back to the GEMV + one-shot all-reduce kernel pair.  Greedy decoding ends with a
 distributed argmax instead of gathering 152k logits.
 
-Prefill all-reduces both row-parallel projections (and the MoE expert sum) without NCCL: the
-tcgen05 GEMM's epilogue stores each 128 x 256 fp32 output tile into the owner rank's slot (owner =
-m-block mod W, the reduce-scatter half; ``gemm_tc.cu`` ``G_RS``) and releases a tile flag, and the
-owner's ``k_p2p_rs_reduce`` adds the W partials to the residual and stores the rows into every
-rank's residual (the all-gather half), which for that reason lives in the peer buffer
-(``prefill_x``) -- the partials cross NVLink tile by tile while the GEMM computes later tiles.
+Prefill can all-reduce both row-parallel projections (and the MoE expert sum) without NCCL
+(``FAK_PREFILL_P2P=1``; NCCL's all-reduce is the default for prefill, measured faster): the tcgen05
+GEMM's epilogue stores each 128 x 256 fp32 output tile into the owner rank's slot (owner = m-block
+mod W, the reduce-scatter half; ``gemm_tc.cu`` ``G_RS``) and releases a tile flag, and the owner's
+``k_p2p_rs_reduce`` adds the W partials to the residual and stores the rows into every rank's
+residual (the all-gather half), which for that reason lives in the peer buffer (``prefill_x``).
 
 Every wait is bounded (``spin_limit`` polls; 0 = the kernels' default of about a second) and writes
 an error word the engine reads back with each step's tokens (``engine.Engine._collect``).
